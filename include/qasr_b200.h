@@ -1,0 +1,187 @@
+/*
+ * qasr_b200.h — C ABI of the B200 (sm_100a) Qwen3-ASR text-decoder backend.
+ *
+ * This is the drop-in boundary for the reference crate's text-decoder hot path
+ * (eclipse005/qwen3-asr-wgpu v0.3.0).  The reference binds that path through the
+ * `TextBackend` enum (src/inference.rs:213-269) and, for batched decode, through
+ * `WgpuTextDecoder::{fork_capped, set_input_token, pos}` (src/decoder.rs:2453, 1670,
+ * 929), `prefill_batch` (src/decoder.rs:3599) and `BatchProjections::{new, step}`
+ * (src/decoder.rs:2945, 3339).  Every entry point below names the reference call it
+ * replaces.  A Rust `TextBackend::B200` variant binds these through `extern "C"`.
+ *
+ * Conventions
+ *  - Plain C types only.  Host buffers are borrowed for the duration of the call and
+ *    copied; the library owns all device memory.
+ *  - f16 values travel as IEEE binary16 bit patterns in uint16_t (little endian), the
+ *    same bytes the reference hands its kernels ("hidden_words", src/inference.rs:219).
+ *  - Every call returns a qasr_status.  A failing call never aborts or traps; the
+ *    message is available from qasr_last_error() until the next call on the context.
+ *  - A context is bound to one CUDA device and must be used from one host thread at a
+ *    time (the reference's decoder is likewise single-threaded behind a Mutex,
+ *    src/inference.rs:303-316).  Eight GPUs = eight contexts.
+ */
+#ifndef QASR_B200_H
+#define QASR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  The reference maps failures to anyhow::Result / AsrError
+ * (src/error.rs:1-25, src/decoder.rs:4458-4486); these are their C equivalents. */
+typedef enum {
+  QASR_OK = 0,
+  QASR_ERR_INVALID_ARG = 1,    /* bad pointer, size, slot id or token (ensure!/bail!) */
+  QASR_ERR_OOM = 2,            /* device or host allocation failed                  */
+  QASR_ERR_CAPACITY = 3,       /* KV or slot capacity exceeded (max_seq, pages)     */
+  QASR_ERR_DEVICE = 4,         /* CUDA runtime/driver error                          */
+  QASR_ERR_DEVICE_TIMEOUT = 5, /* a bounded device-side wait gave up                 */
+  QASR_ERR_CANCELLED = 6,      /* the caller asked to stop (BatchEvents::should_stop) */
+  QASR_ERR_STATE = 7           /* call order violated (e.g. step before load)        */
+} qasr_status;
+
+/* Weight storage formats of the decoder linears. */
+enum {
+  QASR_WEIGHTS_F16 = 0,  /* f16 [out, in] row-major, as the reference's f16 kernels read */
+  QASR_WEIGHTS_INT8 = 1  /* int8 [out, in] + f16 per-row scale: value = f16(f32(q) * s)  */
+};
+
+/* Text decoder hyper-parameters; mirrors `TextConfig` (src/decoder.rs:166-175) with
+ * the defaults of `TextDecoderConfig` (src/config.rs:102-110). */
+typedef struct {
+  int32_t vocab_size;          /* 151936 */
+  int32_t hidden_size;         /* 1024 (0.6B) / 2048 (1.7B) */
+  int32_t intermediate_size;   /* 3072 / 6144 */
+  int32_t num_hidden_layers;   /* 28 */
+  int32_t num_attention_heads; /* 16 */
+  int32_t num_key_value_heads; /* 8 */
+  int32_t head_dim;            /* 128 */
+  float rms_norm_eps;          /* 1e-6, narrowed f64 -> f32 as src/decoder.rs:191 does */
+} qasr_text_config;
+
+/* Capacity plan of a context (replaces the reference's per-fork buffers,
+ * src/decoder.rs:2457-2778, with one paged pool). */
+typedef struct {
+  int32_t weight_format;     /* QASR_WEIGHTS_F16 or QASR_WEIGHTS_INT8 */
+  int32_t max_slots;         /* slot table size (reference MAX_BATCH = 32 is lifted) */
+  int32_t max_seq;           /* per-slot position ceiling (rope table rows needed)   */
+  int32_t kv_pages;          /* pool pages of QASR_PAGE_POSITIONS positions; 0 = max_slots*ceil(max_seq/page) */
+  int32_t max_prefill_rows;  /* rows per prefill launch chunk; 0 = 4096             */
+  int32_t flags;             /* QASR_FLAG_* */
+} qasr_options;
+
+#define QASR_PAGE_POSITIONS 64
+/* Keep the f32 logits of the last prefill/step rows so qasr_read_logits can return
+ * them (the reference's CPU decoder exposes f32 logits, src/cpu_decoder.rs:458-472). */
+#define QASR_FLAG_KEEP_LOGITS 1u
+/* Replay batched decode steps through a CUDA graph (default on). */
+#define QASR_FLAG_NO_GRAPH 2u
+
+/* Weights of one decoder layer (HF names, src/cpu_decoder.rs:126-138).  Linear
+ * weights are [out, in] row-major: q [nqh*hd, hs], k/v [nkv*hd, hs], o [hs, nqh*hd],
+ * gate/up [I, hs], down [hs, I].  With QASR_WEIGHTS_INT8 each linear points at int8
+ * data and its *_scale at `out` f16 scales; with QASR_WEIGHTS_F16 the *_scale fields
+ * are ignored.  Norm gains are f16 vectors. */
+typedef struct {
+  const void *q_proj, *k_proj, *v_proj, *o_proj, *gate_proj, *up_proj, *down_proj;
+  const uint16_t *q_scale, *k_scale, *v_scale, *o_scale, *gate_scale, *up_scale, *down_scale;
+  const uint16_t *input_layernorm, *post_attention_layernorm, *q_norm, *k_norm;
+} qasr_layer_weights;
+
+typedef struct qasr_ctx qasr_ctx;
+
+/* --- lifetime (WgpuTextDecoder::load, src/decoder.rs:977-1573) ------------------ */
+qasr_status qasr_create(const qasr_text_config* cfg, const qasr_options* opts, int device,
+                        qasr_ctx** out);
+void qasr_destroy(qasr_ctx* ctx);
+const char* qasr_last_error(const qasr_ctx* ctx);
+/* Version string of the library build. */
+const char* qasr_version(void);
+
+/* Run all device work of this context on `stream` (a cudaStream_t); NULL restores
+ * the context's own stream.  Lets a caller time the hot path with its own events. */
+qasr_status qasr_set_stream(qasr_ctx* ctx, void* stream);
+qasr_status qasr_synchronize(qasr_ctx* ctx);
+
+/* Tied embedding / lm_head table f16 [vocab, hidden] and the final norm gain f16
+ * [hidden] (src/cpu_decoder.rs:182-192, 458-472). */
+qasr_status qasr_load_embed(qasr_ctx* ctx, const uint16_t* embed, const uint16_t* final_norm);
+/* One layer's weights (Layer::load src/cpu_decoder.rs:118-139; fused layout of
+ * convert_layer src/decoder.rs:4366-4417).  The library fuses q|k|v and gate|up. */
+qasr_status qasr_load_layer(qasr_ctx* ctx, int layer, const qasr_layer_weights* w);
+
+/* TextBackend::set_rope_tables (src/inference.rs:263-268): f16 cos/sin, each
+ * [positions, head_dim] row-major, as computed by qasr_build_rope_tables. */
+qasr_status qasr_set_rope_tables(qasr_ctx* ctx, const uint16_t* cos, const uint16_t* sin,
+                                 int positions);
+/* TextBackend::max_seq (src/inference.rs:233-238). */
+int32_t qasr_max_seq(const qasr_ctx* ctx);
+
+/* --- slots (WgpuTextDecoder::fork_capped / pos / set_input_token) -------------- */
+/* fork_capped (src/decoder.rs:2453): a new decode slot sharing the weights, with a
+ * private KV of `cap` positions (rounded up to whole pages). */
+qasr_status qasr_fork_capped(qasr_ctx* ctx, int cap, int* slot);
+qasr_status qasr_slot_free(qasr_ctx* ctx, int slot);
+/* TextBackend::ensure_capacity (src/inference.rs:242-247): grow-only; keeps the KV
+ * contents (the GPU decoder's contract, src/decoder.rs:1604-1661).  Returns the new
+ * capacity in *cap. */
+qasr_status qasr_ensure_capacity(qasr_ctx* ctx, int slot, int need, int* cap);
+/* WgpuTextDecoder::pos (src/decoder.rs:929): positions already in the slot's KV. */
+qasr_status qasr_slot_pos(qasr_ctx* ctx, int slot, int* pos);
+/* Set a slot's position (fill_slots sets d.pos = len, src/inference.rs:745). */
+qasr_status qasr_set_slot_pos(qasr_ctx* ctx, int slot, int pos);
+/* WgpuTextDecoder::set_input_token (src/decoder.rs:1670-1672): the token the next
+ * step embeds.  Without it the next step embeds the slot's own last argmax. */
+qasr_status qasr_set_input_token(qasr_ctx* ctx, int slot, int32_t token);
+
+/* set_input_token for several slots at once, without a host sync: the tokens are
+ * staged in pinned memory and scattered on the device ahead of the next step (the
+ * per-step host->device input of a caller that feeds tokens itself). */
+qasr_status qasr_set_input_tokens(qasr_ctx* ctx, const int* slots, int n, const int32_t* tokens);
+
+/* --- the hot path ---------------------------------------------------------------- */
+/* TextBackend::prefill (src/inference.rs:219-224): run `s` f16 hidden rows
+ * ([s, hidden]) at positions kv_start.. through every layer into the slot's KV, then
+ * return the argmax of the last row in *token. */
+qasr_status qasr_prefill(qasr_ctx* ctx, int slot, const uint16_t* hidden, int s, int kv_start,
+                         int32_t* token);
+/* TextBackend::step (src/inference.rs:226-231): embed the slot's input token, run
+ * one position, return the argmax. */
+qasr_status qasr_step(qasr_ctx* ctx, int slot, int32_t* token);
+/* prefill_batch (src/decoder.rs:3599-3637): several slots in one launch sequence.
+ * `hidden` holds the segments' rows back to back (Σ lens rows); kv_starts may be
+ * NULL (all zero).  first_tokens[i] receives segment i's argmax. */
+qasr_status qasr_prefill_batch(qasr_ctx* ctx, const int* slots, int n, const uint16_t* hidden,
+                               const int* lens, const int* kv_starts, int32_t* first_tokens);
+/* BatchProjections::step (src/decoder.rs:3339-3510): one decode position for each
+ * listed slot.  Input tokens come from qasr_set_input_token or, by default, from the
+ * slot's previous argmax, read on the device (on-device feedback, src/decoder.rs:
+ * 2125-2126).  If out_tokens is non-NULL the step's argmax ids are copied to it (a
+ * host sync); with NULL the step is enqueued and returns at once. */
+qasr_status qasr_step_batch(qasr_ctx* ctx, const int* slots, int n, int32_t* out_tokens);
+/* Copy the f32 logits [rows, vocab] of the last prefill (one row per segment) or step
+ * (one row per slot) — only with QASR_FLAG_KEEP_LOGITS. */
+qasr_status qasr_read_logits(qasr_ctx* ctx, float* out, int rows);
+
+/* --- host helpers of the reference's loader ------------------------------------ */
+/* compute_mrope_cos_sin + text_positions (src/mrope.rs:46-80) rounded to f16 the
+ * way src/inference.rs:1037-1047 does: angles in f64, cos/sin -> f32 -> f16.
+ * `section`/`nsection` is the mrope quota ([24,20,20]); interleaved != 0 picks the
+ * Qwen2-VL interleaved map (build_dim_map, src/mrope.rs:5-41). */
+qasr_status qasr_build_rope_tables(uint16_t* cos, uint16_t* sin, int positions, int head_dim,
+                                   double rope_theta, const int* section, int nsection,
+                                   int interleaved);
+/* build_dim_map (src/mrope.rs:5-41): writes `half` axis indices into out. */
+qasr_status qasr_build_dim_map(const int* section, int nsection, int half, int interleaved,
+                               int* out);
+/* dequant_i8 (src/weights.rs:372-385): out[r, c] = f16(f32(q[r, c]) * scale_f32[r]). */
+qasr_status qasr_dequant_i8(const int8_t* q, const float* scale_f32, int rows, int cols,
+                            uint16_t* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QASR_B200_H */

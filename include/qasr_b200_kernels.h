@@ -1,0 +1,57 @@
+/*
+ * qasr_b200_kernels.h — device-pointer entry points of the individual B200 kernels.
+ *
+ * The reference checks and measures its kernels one by one with dedicated probes:
+ * src/bin/w8_probe.rs (W8 GEMV/GEMM vs an f64 reference), src/bin/batch_gemv_bench.rs
+ * (batched GEMV bandwidth), src/bin/attn_bench.rs and src/bin/attn_slots_probe.rs
+ * (decode attention).  These calls are the same seams for the B200 kernels: all
+ * pointers are device pointers, `stream` is a cudaStream_t (NULL = legacy default
+ * stream), nothing is synchronised.  Workspaces are cached per device inside the
+ * library and only grow.  Errors are written to `err` (if non-NULL, `errlen` bytes).
+ */
+#ifndef QASR_B200_KERNELS_H
+#define QASR_B200_KERNELS_H
+
+#include <stdint.h>
+
+#include "qasr_b200.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* out[r, m] = f16(sum_k W[m, k] x[r, k])            (accumulate == 0)
+ * out[r, m] = f16(f32(out[r, m]) + sum_k ...)         (accumulate != 0)
+ * W: [n_out, k] f16 (weight_format QASR_WEIGHTS_F16) or int8 + f16 per-row scale
+ * (QASR_WEIGHTS_INT8, value f16(f32(q) * s)).  n_out % 128 == 0; k % 128 == 0.
+ * Replaces gemv / gemv_w8 / gemv_batch_slots / prefill_gemm(_w8)
+ * (src/shaders.rs:273-889, 2995-3082). */
+qasr_status qasr_kernel_gemm(int device, void* stream, int weight_format, const void* w,
+                             const uint16_t* scale, int n_out, int k, const uint16_t* x, int ldx,
+                             int rows, uint16_t* out, int ldo, int accumulate, char* err,
+                             int errlen);
+
+/* GQA attention of `rows` query rows over their slot's paged KV (gqa_decode_* /
+ * gqa_split_merge, src/shaders.rs:1881-2905).  q/out: [rows, q_ld] f16 (q heads 2g and
+ * 2g+1 read kv head g); kv_pool: [pages][layers][2][nkv][64][128] f16; page_table:
+ * [slots][max_pages] int32; row r attends positions 0..row_pos[r] of slot row_slot[r]. */
+qasr_status qasr_kernel_attention(int device, void* stream, const uint16_t* q, int q_ld,
+                                  uint16_t* out, const uint16_t* kv_pool, const int* page_table,
+                                  int max_pages, int layers, int nkv, int layer,
+                                  const int* row_slot, const int* row_pos, int rows, char* err,
+                                  int errlen);
+
+/* Append K and V rows ([rows, nkv*128] f16 each) at (row_slot[r], row_pos[r]) of
+ * layer `layer` — the cache writes of qkv_extract(_slots) (src/shaders.rs:1376-1635). */
+qasr_status qasr_kernel_kv_append(int device, void* stream, const uint16_t* k, const uint16_t* v,
+                                  uint16_t* kv_pool, const int* page_table, int max_pages,
+                                  int layers, int nkv, int layer, const int* row_slot,
+                                  const int* row_pos, int rows, char* err, int errlen);
+
+/* Number of kernels this library launched since load (all contexts and probes). */
+uint64_t qasr_kernel_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QASR_B200_KERNELS_H */

@@ -1,0 +1,357 @@
+"""qasr_b200 — B200 (sm_100a) backend for the Qwen3-ASR text-decoder hot path.
+
+Python mirror of the reference crate's decoder interface, over the C ABI in
+include/qasr_b200.h (libqasr_b200.so, built in-tree by build.py):
+
+* ``TextDecoder`` follows ``TextBackend`` (src/inference.rs:213-269): ``prefill``,
+  ``step``, ``max_seq``, ``ensure_capacity``, ``set_rope_tables``; and the batched API of
+  ``WgpuTextDecoder`` (``fork_capped``, ``pos``, ``set_input_token``;
+  src/decoder.rs:2453, 929, 1670), ``prefill_batch`` (src/decoder.rs:3599) and
+  ``BatchProjections::step`` (src/decoder.rs:3339) as ``step_batch``.
+* Failures raise ``DecoderError`` carrying the library's status code and message —
+  the reference's ``anyhow`` errors (src/decoder.rs:4458-4486).
+
+There is no CPU fallback: if the shared library cannot be loaded, importing this
+package raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import numpy as np
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = _PKG / "libqasr_b200.so"
+
+QASR_OK = 0
+STATUS_NAMES = {
+    0: "QASR_OK", 1: "QASR_ERR_INVALID_ARG", 2: "QASR_ERR_OOM", 3: "QASR_ERR_CAPACITY",
+    4: "QASR_ERR_DEVICE", 5: "QASR_ERR_DEVICE_TIMEOUT", 6: "QASR_ERR_CANCELLED", 7: "QASR_ERR_STATE",
+}
+WEIGHTS_F16 = 0
+WEIGHTS_INT8 = 1
+FLAG_KEEP_LOGITS = 1
+FLAG_NO_GRAPH = 2
+PAGE_POSITIONS = 64
+
+# Every symbol include/*.h declares (checked by the CPU test suite).
+EXPORTED_SYMBOLS = (
+    "qasr_create", "qasr_destroy", "qasr_last_error", "qasr_version", "qasr_set_stream",
+    "qasr_synchronize", "qasr_load_embed", "qasr_load_layer", "qasr_set_rope_tables",
+    "qasr_max_seq", "qasr_fork_capped", "qasr_slot_free", "qasr_ensure_capacity",
+    "qasr_slot_pos", "qasr_set_slot_pos", "qasr_set_input_token", "qasr_set_input_tokens",
+    "qasr_prefill", "qasr_step", "qasr_prefill_batch", "qasr_step_batch", "qasr_read_logits",
+    "qasr_build_rope_tables", "qasr_build_dim_map", "qasr_dequant_i8",
+    "qasr_kernel_gemm", "qasr_kernel_attention", "qasr_kernel_kv_append",
+    "qasr_kernel_launch_count",
+    "qasr_synth_key", "qasr_synth_normal_f16", "qasr_synth_uniform_ids",
+    "qasr_synth_quantize_rows", "qasr_f32_to_f16", "qasr_f16_to_f32", "qasr_f32_to_f16_array",
+    "qasr_f16_to_f32_array",
+)
+
+
+class DecoderError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+        self.status = status
+
+
+class TextConfig(ctypes.Structure):
+    """qasr_text_config — TextConfig (src/decoder.rs:166-175)."""
+    _fields_ = [("vocab_size", ctypes.c_int32), ("hidden_size", ctypes.c_int32),
+                ("intermediate_size", ctypes.c_int32), ("num_hidden_layers", ctypes.c_int32),
+                ("num_attention_heads", ctypes.c_int32), ("num_key_value_heads", ctypes.c_int32),
+                ("head_dim", ctypes.c_int32), ("rms_norm_eps", ctypes.c_float)]
+
+
+class Options(ctypes.Structure):
+    _fields_ = [("weight_format", ctypes.c_int32), ("max_slots", ctypes.c_int32),
+                ("max_seq", ctypes.c_int32), ("kv_pages", ctypes.c_int32),
+                ("max_prefill_rows", ctypes.c_int32), ("flags", ctypes.c_int32)]
+
+
+class LayerWeights(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in (
+        "q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj",
+        "q_scale", "k_scale", "v_scale", "o_scale", "gate_scale", "up_scale", "down_scale",
+        "input_layernorm", "post_attention_layernorm", "q_norm", "k_norm")]
+
+
+def _load() -> ctypes.CDLL:
+    if not LIB_PATH.exists():
+        raise ImportError(f"{LIB_PATH} is missing: run `python {_PKG / 'build.py'}` first")
+    lib = ctypes.CDLL(str(LIB_PATH))
+    P = ctypes.c_void_p
+    I = ctypes.c_int
+    lib.qasr_create.argtypes = [ctypes.POINTER(TextConfig), ctypes.POINTER(Options), I, ctypes.POINTER(P)]
+    lib.qasr_destroy.argtypes = [P]
+    lib.qasr_destroy.restype = None
+    lib.qasr_last_error.argtypes = [P]
+    lib.qasr_last_error.restype = ctypes.c_char_p
+    lib.qasr_version.restype = ctypes.c_char_p
+    lib.qasr_set_stream.argtypes = [P, P]
+    lib.qasr_synchronize.argtypes = [P]
+    lib.qasr_load_embed.argtypes = [P, P, P]
+    lib.qasr_load_layer.argtypes = [P, I, ctypes.POINTER(LayerWeights)]
+    lib.qasr_set_rope_tables.argtypes = [P, P, P, I]
+    lib.qasr_max_seq.argtypes = [P]
+    lib.qasr_fork_capped.argtypes = [P, I, ctypes.POINTER(I)]
+    lib.qasr_slot_free.argtypes = [P, I]
+    lib.qasr_ensure_capacity.argtypes = [P, I, I, ctypes.POINTER(I)]
+    lib.qasr_slot_pos.argtypes = [P, I, ctypes.POINTER(I)]
+    lib.qasr_set_slot_pos.argtypes = [P, I, I]
+    lib.qasr_set_input_token.argtypes = [P, I, ctypes.c_int32]
+    lib.qasr_set_input_tokens.argtypes = [P, P, I, P]
+    lib.qasr_prefill.argtypes = [P, I, P, I, I, P]
+    lib.qasr_step.argtypes = [P, I, P]
+    lib.qasr_prefill_batch.argtypes = [P, P, I, P, P, P, P]
+    lib.qasr_step_batch.argtypes = [P, P, I, P]
+    lib.qasr_read_logits.argtypes = [P, P, I]
+    lib.qasr_build_rope_tables.argtypes = [P, P, I, I, ctypes.c_double, P, I, I]
+    lib.qasr_build_dim_map.argtypes = [P, I, I, I, P]
+    lib.qasr_dequant_i8.argtypes = [P, P, I, I, P]
+    lib.qasr_kernel_gemm.argtypes = [I, P, I, P, P, I, I, P, I, I, P, I, I, ctypes.c_char_p, I]
+    lib.qasr_kernel_attention.argtypes = [I, P, P, I, P, P, P, I, I, I, I, P, P, I, ctypes.c_char_p, I]
+    lib.qasr_kernel_kv_append.argtypes = [I, P, P, P, P, P, I, I, I, I, P, P, I, ctypes.c_char_p, I]
+    lib.qasr_kernel_launch_count.restype = ctypes.c_uint64
+    lib.qasr_synth_key.argtypes = [ctypes.c_uint64, ctypes.c_uint64]
+    lib.qasr_synth_key.restype = ctypes.c_uint64
+    lib.qasr_synth_normal_f16.argtypes = [P, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_uint64,
+                                          ctypes.c_float, ctypes.c_float]
+    lib.qasr_synth_normal_f16.restype = None
+    lib.qasr_synth_uniform_ids.argtypes = [P, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_uint64,
+                                           ctypes.c_int32, ctypes.c_int32]
+    lib.qasr_synth_uniform_ids.restype = None
+    lib.qasr_synth_quantize_rows.argtypes = [P, I, I, P, P]
+    lib.qasr_synth_quantize_rows.restype = None
+    lib.qasr_f32_to_f16.argtypes = [ctypes.c_float]
+    lib.qasr_f32_to_f16.restype = ctypes.c_uint16
+    lib.qasr_f16_to_f32.argtypes = [ctypes.c_uint16]
+    lib.qasr_f16_to_f32.restype = ctypes.c_float
+    lib.qasr_f32_to_f16_array.argtypes = [P, P, ctypes.c_size_t]
+    lib.qasr_f32_to_f16_array.restype = None
+    lib.qasr_f16_to_f32_array.argtypes = [P, P, ctypes.c_size_t]
+    lib.qasr_f16_to_f32_array.restype = None
+    return lib
+
+
+lib = _load()
+
+from .synth import (MODEL_PRESETS, SyntheticModel, build_rope_tables, dim_map,  # noqa: E402,F401
+                    f16_bits_to_f32, f32_to_f16_bits, text_config)
+
+
+def _ptr(a: np.ndarray | None):
+    if a is None:
+        return None
+    assert a.flags["C_CONTIGUOUS"], "arrays handed to the library must be C-contiguous"
+    return ctypes.c_void_p(a.ctypes.data)
+
+
+def launch_count() -> int:
+    """Kernels this library launched (graph replays included) since it was loaded."""
+    return int(lib.qasr_kernel_launch_count())
+
+
+class TextDecoder:
+    """One B200 decoder context: weights, paged KV pool, slot table (one device)."""
+
+    def __init__(self, cfg: dict, *, weight_format: int = WEIGHTS_F16, max_slots: int = 1,
+                 max_seq: int = 4096, kv_pages: int = 0, max_prefill_rows: int = 0,
+                 keep_logits: bool = False, use_graph: bool = True, device: int = 0):
+        self.cfg = dict(cfg)
+        self._tc = TextConfig(cfg["vocab_size"], cfg["hidden_size"], cfg["intermediate_size"],
+                              cfg["num_hidden_layers"], cfg["num_attention_heads"],
+                              cfg["num_key_value_heads"], cfg["head_dim"], cfg["rms_norm_eps"])
+        flags = (FLAG_KEEP_LOGITS if keep_logits else 0) | (0 if use_graph else FLAG_NO_GRAPH)
+        self._opts = Options(weight_format, max_slots, max_seq, kv_pages, max_prefill_rows, flags)
+        self.weight_format = weight_format
+        self.max_slots = max_slots
+        self._ctx = ctypes.c_void_p()
+        st = lib.qasr_create(ctypes.byref(self._tc), ctypes.byref(self._opts), device,
+                             ctypes.byref(self._ctx))
+        if st != QASR_OK:
+            msg = self._err()
+            self.close()
+            raise DecoderError(st, msg)
+
+    # ---------------------------------------------------------------- plumbing
+    def _err(self) -> str:
+        if not self._ctx:
+            return "no context"
+        return lib.qasr_last_error(self._ctx).decode()
+
+    def _check(self, st: int):
+        if st != QASR_OK:
+            raise DecoderError(st, self._err())
+
+    def close(self):
+        if getattr(self, "_ctx", None):
+            lib.qasr_destroy(self._ctx)
+            self._ctx = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def set_stream(self, stream_handle: int | None):
+        self._check(lib.qasr_set_stream(self._ctx, ctypes.c_void_p(stream_handle or 0)))
+
+    def synchronize(self):
+        self._check(lib.qasr_synchronize(self._ctx))
+
+    # ---------------------------------------------------------------- loading
+    def load_embed(self, embed: np.ndarray, final_norm: np.ndarray):
+        self._check(lib.qasr_load_embed(self._ctx, _ptr(embed), _ptr(final_norm)))
+
+    def load_layer(self, layer: int, w: dict):
+        """w: HF-named arrays (q_proj ... down_proj, *_scale for INT8, norms)."""
+        lw = LayerWeights()
+        keep = []
+        for name, _ in LayerWeights._fields_:
+            a = w.get(name)
+            if a is not None:
+                a = np.ascontiguousarray(a)
+                keep.append(a)
+                setattr(lw, name, a.ctypes.data)
+        self._check(lib.qasr_load_layer(self._ctx, layer, ctypes.byref(lw)))
+
+    def load_model(self, model: "SyntheticModel"):
+        self.load_embed(model.embed, model.final_norm)
+        for layer in range(self.cfg["num_hidden_layers"]):
+            self.load_layer(layer, model.layer(layer, int8=self.weight_format == WEIGHTS_INT8))
+
+    def set_rope_tables(self, cos: np.ndarray, sin: np.ndarray):
+        positions = cos.shape[0]
+        self._check(lib.qasr_set_rope_tables(self._ctx, _ptr(cos), _ptr(sin), positions))
+
+    @property
+    def max_seq(self) -> int:
+        return int(lib.qasr_max_seq(self._ctx))
+
+    # ---------------------------------------------------------------- slots
+    def fork_capped(self, cap: int) -> int:
+        s = ctypes.c_int()
+        self._check(lib.qasr_fork_capped(self._ctx, cap, ctypes.byref(s)))
+        return s.value
+
+    def slot_free(self, slot: int):
+        self._check(lib.qasr_slot_free(self._ctx, slot))
+
+    def ensure_capacity(self, slot: int, need: int) -> int:
+        c = ctypes.c_int()
+        self._check(lib.qasr_ensure_capacity(self._ctx, slot, need, ctypes.byref(c)))
+        return c.value
+
+    def pos(self, slot: int) -> int:
+        p = ctypes.c_int()
+        self._check(lib.qasr_slot_pos(self._ctx, slot, ctypes.byref(p)))
+        return p.value
+
+    def set_pos(self, slot: int, pos: int):
+        self._check(lib.qasr_set_slot_pos(self._ctx, slot, pos))
+
+    def set_input_token(self, slot: int, token: int):
+        self._check(lib.qasr_set_input_token(self._ctx, slot, int(token)))
+
+    def set_input_tokens(self, slots, tokens):
+        s = np.ascontiguousarray(slots, dtype=np.int32)
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        self._check(lib.qasr_set_input_tokens(self._ctx, _ptr(s), len(s), _ptr(t)))
+
+    # ---------------------------------------------------------------- hot path
+    def prefill(self, slot: int, hidden: np.ndarray, kv_start: int = 0) -> int:
+        """TextBackend::prefill: hidden is [s, hidden] f16 bits (uint16)."""
+        h = np.ascontiguousarray(hidden, dtype=np.uint16)
+        tok = ctypes.c_int32()
+        self._check(lib.qasr_prefill(self._ctx, slot, _ptr(h), h.shape[0], kv_start, ctypes.byref(tok)))
+        return tok.value
+
+    def step(self, slot: int) -> int:
+        tok = ctypes.c_int32()
+        self._check(lib.qasr_step(self._ctx, slot, ctypes.byref(tok)))
+        return tok.value
+
+    def prefill_batch(self, slots, hiddens, kv_starts=None) -> np.ndarray:
+        slots_a = np.ascontiguousarray(slots, dtype=np.int32)
+        lens = np.array([h.shape[0] for h in hiddens], dtype=np.int32)
+        hid = np.ascontiguousarray(np.concatenate(hiddens, axis=0), dtype=np.uint16)
+        ks = None if kv_starts is None else np.ascontiguousarray(kv_starts, dtype=np.int32)
+        out = np.zeros(len(slots_a), dtype=np.int32)
+        self._check(lib.qasr_prefill_batch(self._ctx, _ptr(slots_a), len(slots_a), _ptr(hid), _ptr(lens),
+                                           _ptr(ks), _ptr(out)))
+        return out
+
+    def step_batch(self, slots, read_tokens: bool = True):
+        s = np.ascontiguousarray(slots, dtype=np.int32)
+        if read_tokens:
+            out = np.zeros(len(s), dtype=np.int32)
+            self._check(lib.qasr_step_batch(self._ctx, _ptr(s), len(s), _ptr(out)))
+            return out
+        self._check(lib.qasr_step_batch(self._ctx, _ptr(s), len(s), None))
+        return None
+
+    def read_logits(self, rows: int) -> np.ndarray:
+        out = np.zeros((rows, self.cfg["vocab_size"]), dtype=np.float32)
+        self._check(lib.qasr_read_logits(self._ctx, _ptr(out), rows))
+        return out
+
+
+def kernel_gemm(device: int, stream: int, weight_format: int, w_ptr: int, scale_ptr: int | None,
+                n_out: int, k: int, x_ptr: int, ldx: int, rows: int, out_ptr: int, ldo: int,
+                accumulate: bool = False):
+    err = ctypes.create_string_buffer(512)
+    st = lib.qasr_kernel_gemm(device, ctypes.c_void_p(stream), weight_format, ctypes.c_void_p(w_ptr),
+                              ctypes.c_void_p(scale_ptr or 0), n_out, k, ctypes.c_void_p(x_ptr), ldx,
+                              rows, ctypes.c_void_p(out_ptr), ldo, int(accumulate), err, 512)
+    if st != QASR_OK:
+        raise DecoderError(st, err.value.decode())
+
+
+def kernel_attention(device: int, stream: int, q_ptr: int, q_ld: int, out_ptr: int, pool_ptr: int,
+                     page_table_ptr: int, max_pages: int, layers: int, nkv: int, layer: int,
+                     row_slot_ptr: int, row_pos_ptr: int, rows: int):
+    err = ctypes.create_string_buffer(512)
+    V = ctypes.c_void_p
+    st = lib.qasr_kernel_attention(device, V(stream), V(q_ptr), q_ld, V(out_ptr), V(pool_ptr),
+                                   V(page_table_ptr), max_pages, layers, nkv, layer, V(row_slot_ptr),
+                                   V(row_pos_ptr), rows, err, 512)
+    if st != QASR_OK:
+        raise DecoderError(st, err.value.decode())
+
+
+def kernel_kv_append(device: int, stream: int, k_ptr: int, v_ptr: int, pool_ptr: int,
+                     page_table_ptr: int, max_pages: int, layers: int, nkv: int, layer: int,
+                     row_slot_ptr: int, row_pos_ptr: int, rows: int):
+    err = ctypes.create_string_buffer(512)
+    V = ctypes.c_void_p
+    st = lib.qasr_kernel_kv_append(device, V(stream), V(k_ptr), V(v_ptr), V(pool_ptr), V(page_table_ptr),
+                                   max_pages, layers, nkv, layer, V(row_slot_ptr), V(row_pos_ptr), rows,
+                                   err, 512)
+    if st != QASR_OK:
+        raise DecoderError(st, err.value.decode())
+
+
+def version() -> str:
+    return lib.qasr_version().decode()
+
+
+__all__ = [
+    "TextDecoder", "DecoderError", "SyntheticModel", "MODEL_PRESETS", "text_config",
+    "build_rope_tables", "dim_map", "kernel_gemm", "kernel_attention", "kernel_kv_append",
+    "launch_count", "version", "WEIGHTS_F16", "WEIGHTS_INT8", "EXPORTED_SYMBOLS", "lib",
+    "f16_bits_to_f32", "f32_to_f16_bits", "PAGE_POSITIONS",
+]
+
+if os.environ.get("QASR_B200_VERBOSE"):
+    print(f"[qasr_b200] loaded {LIB_PATH} ({version()})")

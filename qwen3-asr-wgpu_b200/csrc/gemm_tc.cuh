@@ -1,0 +1,511 @@
+// Weight-streaming GEMM on the sm_100a tensor cores (tcgen05 + TMEM + TMA).
+//
+//   out[r, m] = epilogue( sum_k  W[m, k] * X[r, k] )      W: [n_out, K] f16 or int8
+//                                                          X: [rows, K] f16 (activations)
+//
+// This replaces the reference's decoder GEMVs/GEMMs: gemv / gemv_w8 / gemv_norm /
+// gemv_batch_slots / prefill_gemm(_w8) (src/shaders.rs:273-1132, 2995-3082).  It is
+// "swap-AB": the weight rows are the UMMA M dimension (tiles of 128 rows) and the
+// activation rows (decode slots or prefill rows) are N (16..128 per tile), so a decode
+// step with B slots reads every weight byte once, whatever B is.
+//
+// Roles of the 384-thread CTA (one persistent CTA per SM):
+//   warp 0      TMA producer: W tile (128 rows x 128 B) + X tile(s) per k-block
+//   warp 1      UMMA issuer:  tcgen05.mma kind::f16, A from TMEM, B from smem
+//   warp 2      TMEM allocator (512 columns)
+//   warps 4-7   "A" builders: read one W row each from the swizzled smem tile,
+//               dequantise int8 -> f16 as f16(f32(q) * scale) with one correctly rounded
+//               f16 multiply (the exact value dequant_i8 produces, src/weights.rs:372-385),
+//               store the row into TMEM as the MMA's A operand
+//   warps 8-11  epilogue: TMEM accumulators -> fused epilogue (see EpiKind)
+//
+// Work split: the (tile, k-block) units are cut into equal contiguous ranges, one per
+// CTA ("stream-K").  A tile split across CTAs is finished by the CTA that arrives last
+// on the tile's counter; it adds the f32 partials in segment order, so results do not
+// depend on arrival order.  No CTA ever waits on another.
+#pragma once
+#include "device_common.cuh"
+
+namespace qasr {
+
+enum EpiKind : int {
+  EPI_STORE = 0,   // out[r, m] = f16(acc)
+  EPI_RESID = 1,   // h[r, m] = f16(f32(h[r, m]) + acc)  (batch_dot_acc, src/cpu_decoder.rs:45-62)
+  EPI_SILU = 2,    // interleaved gate|up tiles -> f16(silu(f16 g) * f16 u) (src/cpu_decoder.rs:442-448)
+  EPI_QKV = 3,     // per-head q/k RMSNorm + rotate-half RoPE; Q -> q_out, K and raw V -> paged KV
+  EPI_LOGITS = 4,  // f32 logits (optional) + per-row argmax via 64-bit atomicMax keys
+};
+
+constexpr int GEMM_THREADS = 384;
+constexpr int GEMM_MAX_STAGES = 8;
+constexpr int GEMM_A_STAGES = 4;
+constexpr int GEMM_MAX_NTILE = 128;
+constexpr uint32_t GEMM_TMEM_COLS = 512;
+
+struct KvLayout {
+  __half* pool;             // [pages][layers][2][nkv][64][head_dim]
+  const int* page_table;    // [slots][max_pages]
+  int max_pages;
+  int layers;
+  int nkv;
+};
+
+__device__ __forceinline__ size_t kv_elem_offset(const KvLayout& kv, int slot, int pos, int layer,
+                                                 int which, int kvh) {
+  const int page = kv.page_table[static_cast<size_t>(slot) * kv.max_pages + (pos >> 6)];
+  return ((((static_cast<size_t>(page) * kv.layers + layer) * 2 + which) * kv.nkv + kvh) * 64 +
+          (pos & 63)) *
+         128;
+}
+
+struct GemmArgs {
+  int n_out, k, rows, n_tile, n_tiles, kblocks, units, grid, stages, max_seg;
+  const __half* scale;  // int8: f16 per-row scale
+  // epilogue
+  int epi;
+  __half* out;
+  int ldo;
+  // EPI_QKV
+  const float* qn_w;
+  const float* kn_w;
+  const __half* rope_cos;
+  const __half* rope_sin;
+  const int* row_slot;
+  const int* row_pos;
+  KvLayout kv;
+  int layer;
+  __half* q_out;
+  int q_ld;
+  float eps;
+  // EPI_LOGITS
+  float* logits;
+  int ld_logits;
+  unsigned long long* best;
+  // split tiles
+  float* ws;
+  int* counters;
+  uint32_t* status;
+};
+
+__device__ __forceinline__ int cta_of_unit(long long x, long long units, long long grid) {
+  // CTA c owns units [c*U/G, (c+1)*U/G); the owner of x is the largest c with c*U/G <= x.
+  return static_cast<int>(((x + 1) * grid + units - 1) / units - 1);
+}
+
+// ------------------------------------------------------------------ epilogues
+struct EpiSmem {
+  float red[4][16];
+  float xs[16][128];
+  int last_flag;
+};
+
+__device__ __forceinline__ void warp_sum16(float (&s)[16]) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s[j] += __shfl_xor_sync(0xffffffffu, s[j], o);
+  }
+}
+
+template <int EPI>
+__device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, EpiSmem& es, int mt, int nt,
+                                               int c0, int e, const float (&v)[16]) {
+  const int warp_e = e >> 5;
+  const int lane = e & 31;
+  const int nbase = nt * a.n_tile + c0;
+  if constexpr (EPI == EPI_STORE) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int n = nbase + j;
+      if (n < a.rows) a.out[static_cast<size_t>(n) * a.ldo + mt * 128 + e] = __float2half_rn(v[j]);
+    }
+  } else if constexpr (EPI == EPI_RESID) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int n = nbase + j;
+      if (n < a.rows) {
+        __half* p = a.out + static_cast<size_t>(n) * a.ldo + mt * 128 + e;
+        *p = __float2half_rn(__fadd_rn(__half2float(*p), v[j]));
+      }
+    }
+  } else if constexpr (EPI == EPI_SILU) {
+    // tile mt: rows [0,64) = gate[mt*64 + i], rows [64,128) = up[mt*64 + i]
+    if (e >= 64) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) es.xs[j][e - 64] = f16_round(v[j]);
+    }
+    named_bar_sync(1, 128);
+    if (e < 64) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int n = nbase + j;
+        if (n < a.rows) {
+          const float g = f16_round(v[j]);
+          const float u = es.xs[j][e];
+          const float silu = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+          a.out[static_cast<size_t>(n) * a.ldo + mt * 64 + e] = __float2half_rn(__fmul_rn(silu, u));
+        }
+      }
+    }
+    named_bar_sync(1, 128);
+  } else if constexpr (EPI == EPI_QKV) {
+    // tile mt = one head: 0..15 q, 16..23 k, 24..31 v (fused [q|k|v] rows)
+    const int nq = a.q_ld / 128;
+    if (mt >= nq + a.kv.nkv) {  // V: raw f16 projection into the cache
+      const int kvh = mt - nq - a.kv.nkv;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int n = nbase + j;
+        if (n < a.rows) {
+          const size_t off = kv_elem_offset(a.kv, a.row_slot[n], a.row_pos[n], a.layer, 1, kvh);
+          a.kv.pool[off + e] = __float2half_rn(v[j]);
+        }
+      }
+      return;
+    }
+    float x[16], s[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      x[j] = f16_round(v[j]);
+      s[j] = __fmul_rn(x[j], x[j]);
+    }
+    warp_sum16(s);
+    if (lane == 0) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) es.red[warp_e][j] = s[j];
+    }
+    named_bar_sync(1, 128);
+    const float w = (mt < nq ? a.qn_w : a.kn_w)[e];
+    float xn[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float sum2 = (es.red[0][j] + es.red[1][j]) + (es.red[2][j] + es.red[3][j]);
+      const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum2, 128.0f), a.eps)));
+      xn[j] = __fmul_rn(__fmul_rn(x[j], inv), w);
+      es.xs[j][e] = xn[j];
+    }
+    named_bar_sync(1, 128);
+    const float sign = e < 64 ? -1.0f : 1.0f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int n = nbase + j;
+      if (n < a.rows) {
+        const int pos = a.row_pos[n];
+        const float c = __half2float(a.rope_cos[static_cast<size_t>(pos) * 128 + e]);
+        const float sn = __half2float(a.rope_sin[static_cast<size_t>(pos) * 128 + e]);
+        const float xp = es.xs[j][e ^ 64];
+        const float o = __fadd_rn(__fmul_rn(xn[j], c), __fmul_rn(__fmul_rn(sign, xp), sn));
+        const __half oh = __float2half_rn(o);
+        if (mt < nq) {
+          a.q_out[static_cast<size_t>(n) * a.q_ld + mt * 128 + e] = oh;
+        } else {
+          const size_t off = kv_elem_offset(a.kv, a.row_slot[n], pos, a.layer, 0, mt - nq);
+          a.kv.pool[off + e] = oh;
+        }
+      }
+    }
+    named_bar_sync(1, 128);
+  } else if constexpr (EPI == EPI_LOGITS) {
+    const uint32_t vocab_row = static_cast<uint32_t>(mt * 128 + e);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int n = nbase + j;  // warp-uniform
+      if (n < a.rows) {
+        if (a.logits != nullptr) a.logits[static_cast<size_t>(n) * a.ld_logits + vocab_row] = v[j];
+        unsigned long long key = argmax_key(v[j], vocab_row);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+          key = other > key ? other : key;
+        }
+        if (lane == 0) atomicMax(a.best + n, key);
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ kernel
+template <bool INT8, int EPI>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
+                   const __grid_constant__ GemmArgs a) {
+  constexpr int KE = INT8 ? 128 : 64;        // k elements per k-block (128 bytes of W row)
+  constexpr int ATOMS = INT8 ? 2 : 1;        // 64-element (128-byte) X atoms per k-block
+  constexpr int ACOLS = KE / 2;              // TMEM columns of one A stage (2 f16 / column)
+  constexpr int KSTEPS = KE / 16;            // UMMA K = 16 per instruction
+  constexpr uint32_t D_COLS0 = 0;            // two accumulator buffers at columns 0 and 128
+  constexpr uint32_t A_COLS0 = 256;
+
+  extern __shared__ __align__(1024) uint8_t dsmem[];
+  __shared__ __align__(8) uint64_t full_bar[GEMM_MAX_STAGES], sfree_bar[GEMM_MAX_STAGES];
+  __shared__ __align__(8) uint64_t afull_bar[GEMM_A_STAGES], afree_bar[GEMM_A_STAGES];
+  __shared__ __align__(8) uint64_t dfull_bar[2], dfree_bar[2], done_bar;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ volatile int abort_flag;
+  __shared__ EpiSmem es;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~uintptr_t(1023));
+  const int S = a.stages;
+  const uint32_t x_tile_bytes = static_cast<uint32_t>(a.n_tile) * 128u;
+  const uint32_t stage_bytes = 16384u + ATOMS * x_tile_bytes;
+  const uint32_t tx_bytes = stage_bytes;
+
+  const long long U = a.units, G = a.grid;
+  const long long ub = static_cast<long long>(blockIdx.x) * U / G;
+  const long long ue = static_cast<long long>(blockIdx.x + 1) * U / G;
+  const int KB = a.kblocks;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&sfree_bar[i], 1);
+    }
+    for (int i = 0; i < GEMM_A_STAGES; ++i) {
+      mbar_init(&afull_bar[i], 4);
+      mbar_init(&afree_bar[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&dfull_bar[i], 1);
+      mbar_init(&dfree_bar[i], 4);
+    }
+    mbar_init(&done_bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(&tmem_base_sh, GEMM_TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_w);
+    tma_prefetch_desc(&tm_x);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_sh;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      long long i = 0;
+      for (long long u = ub; u < ue; ++u, ++i) {
+        const int s = static_cast<int>(i % S);
+        const uint32_t ph = static_cast<uint32_t>((i / S) & 1);
+        if (!mbar_wait(&sfree_bar[s], ph ^ 1u, &abort_flag, a.status, 0x101)) break;
+        const int T = static_cast<int>(u / KB), kb = static_cast<int>(u % KB);
+        const int mt = T / a.n_tiles, nt = T % a.n_tiles;
+        uint8_t* st = smem + static_cast<size_t>(s) * stage_bytes;
+        mbar_arrive_expect_tx(&full_bar[s], tx_bytes);
+        tma_load_2d(st, &tm_w, &full_bar[s], kb * KE, mt * 128);
+#pragma unroll
+        for (int at = 0; at < ATOMS; ++at)
+          tma_load_2d(st + 16384 + at * x_tile_bytes, &tm_x, &full_bar[s], kb * KE + at * 64,
+                      nt * a.n_tile);
+      }
+      // Drain: wait until every issued copy has landed before the CTA may exit.
+      const long long issued = i;
+      for (long long j = issued > S ? issued - S : 0; j < issued; ++j) {
+        const int s = static_cast<int>(j % S);
+        mbar_wait(&full_bar[s], static_cast<uint32_t>((j / S) & 1), nullptr, a.status, 0x102);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ UMMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_f16_m128(static_cast<uint32_t>(a.n_tile));
+      long long i = 0, seg = -1;
+      int d = 0;
+      bool issued_any = false;
+      for (long long u = ub; u < ue; ++u, ++i) {
+        const int kb = static_cast<int>(u % KB);
+        const bool first = (u == ub) || (kb == 0);
+        const bool last = (u == ue - 1) || (kb == KB - 1);
+        const int s = static_cast<int>(i % S);
+        const int ast = static_cast<int>(i % GEMM_A_STAGES);
+        if (first) {
+          ++seg;
+          d = static_cast<int>(seg & 1);
+          if (!mbar_wait(&dfree_bar[d], static_cast<uint32_t>(((seg >> 1) & 1) ^ 1), &abort_flag,
+                         a.status, 0x201))
+            break;
+          tc_fence_after();
+        }
+        if (!mbar_wait(&afull_bar[ast], static_cast<uint32_t>((i / GEMM_A_STAGES) & 1), &abort_flag,
+                       a.status, 0x202))
+          break;
+        if (!mbar_wait(&full_bar[s], static_cast<uint32_t>((i / S) & 1), &abort_flag, a.status,
+                       0x203))
+          break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + D_COLS0 + static_cast<uint32_t>(d) * 128u;
+        const uint32_t a_tmem = tmem_base + A_COLS0 + static_cast<uint32_t>(ast) * ACOLS;
+        const uint32_t x_base = smem_u32(smem + static_cast<size_t>(s) * stage_bytes + 16384);
+#pragma unroll
+        for (int kk = 0; kk < KSTEPS; ++kk) {
+          const uint32_t b_addr = x_base + static_cast<uint32_t>(kk >> 2) * x_tile_bytes +
+                                  static_cast<uint32_t>(kk & 3) * 32u;
+          umma_f16_ts(d_tmem, a_tmem + static_cast<uint32_t>(kk) * 8u, smem_desc_sw128(b_addr),
+                      idesc, (first && kk == 0) ? 0u : 1u);
+        }
+        umma_commit(&sfree_bar[s]);
+        umma_commit(&afree_bar[ast]);
+        if (last) umma_commit(&dfull_bar[d]);
+        issued_any = true;
+      }
+      if (issued_any) {  // all MMAs must retire before the TMEM is released
+        umma_commit(&done_bar);
+        mbar_wait(&done_bar, 0, nullptr, a.status, 0x204);
+      }
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ------------------------------------------------------------ A builders
+    const int t = threadIdx.x - 128;  // row of the 128-row tile == TMEM lane
+    const uint32_t lane_base = static_cast<uint32_t>((warp - 4) * 32) << 16;
+    long long i = 0;
+    int cur_mt = -1;
+    __half2 sc2 = __floats2half2_rn(1.0f, 1.0f);
+    for (long long u = ub; u < ue; ++u, ++i) {
+      const int s = static_cast<int>(i % S);
+      const int ast = static_cast<int>(i % GEMM_A_STAGES);
+      if (!mbar_wait_warp(&full_bar[s], static_cast<uint32_t>((i / S) & 1), &abort_flag, a.status,
+                          0x301))
+        break;
+      if (!mbar_wait_warp(&afree_bar[ast], static_cast<uint32_t>(((i / GEMM_A_STAGES) & 1) ^ 1),
+                          &abort_flag, a.status, 0x302))
+        break;
+      tc_fence_after();
+      const int T = static_cast<int>(u / KB);
+      const int mt = T / a.n_tiles;
+      if (INT8 && mt != cur_mt) {
+        const __half sc = a.scale[mt * 128 + t];
+        sc2 = __halves2half2(sc, sc);
+        cur_mt = mt;
+      }
+      const uint8_t* row = smem + static_cast<size_t>(s) * stage_bytes + t * 128;
+      const uint32_t taddr = tmem_base + lane_base + A_COLS0 + static_cast<uint32_t>(ast) * ACOLS;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 chunk = *reinterpret_cast<const uint4*>(row + ((c ^ (t & 7)) << 4));
+        if constexpr (INT8) {
+          const uint32_t w4[4] = {chunk.x, chunk.y, chunk.z, chunk.w};
+          uint32_t outw[8];
+          const __half2 bias = __floats2half2_rn(1152.0f, 1152.0f);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t ub8 = w4[q] ^ 0x80808080u;  // q + 128 as unsigned bytes
+            uint32_t lo = __byte_perm(ub8, 0x64646464u, 0x4140);
+            uint32_t hi = __byte_perm(ub8, 0x64646464u, 0x4342);
+            __half2 hl = __hsub2(*reinterpret_cast<__half2*>(&lo), bias);  // exact q
+            __half2 hh = __hsub2(*reinterpret_cast<__half2*>(&hi), bias);
+            hl = __hmul2_rn(hl, sc2);  // f16(q * s), one IEEE rounding
+            hh = __hmul2_rn(hh, sc2);
+            outw[2 * q] = *reinterpret_cast<uint32_t*>(&hl);
+            outw[2 * q + 1] = *reinterpret_cast<uint32_t*>(&hh);
+          }
+          tmem_st_x8(taddr + static_cast<uint32_t>(c) * 8u, reinterpret_cast<const uint32_t(&)[8]>(outw));
+        } else {
+          const uint32_t w4[4] = {chunk.x, chunk.y, chunk.z, chunk.w};
+          tmem_st_x4(taddr + static_cast<uint32_t>(c) * 4u, w4);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&afull_bar[ast]);
+    }
+  } else if (warp >= 8) {
+    // ------------------------------------------------------------ epilogue
+    const int e = threadIdx.x - 256;
+    const uint32_t lane_base = static_cast<uint32_t>((warp - 8) * 32) << 16;
+    long long seg = -1;
+    long long u = ub;
+    while (u < ue) {
+      const int T = static_cast<int>(u / KB);
+      const long long tile_end = static_cast<long long>(T + 1) * KB;
+      const long long seg_end = ue < tile_end ? ue : tile_end;
+      const int kb0 = static_cast<int>(u - static_cast<long long>(T) * KB);
+      const int kb1 = static_cast<int>(seg_end - static_cast<long long>(T) * KB);
+      ++seg;
+      const int d = static_cast<int>(seg & 1);
+      if (e == 0)
+        es.last_flag = mbar_wait(&dfull_bar[d], static_cast<uint32_t>((seg >> 1) & 1), &abort_flag,
+                                 a.status, 0x401)
+                           ? 1
+                           : 0;
+      named_bar_sync(1, 128);
+      const int got = es.last_flag;
+      named_bar_sync(1, 128);
+      if (!got) break;
+      mbar_try_wait(&dfull_bar[d], static_cast<uint32_t>((seg >> 1) & 1));
+      tc_fence_after();
+      const int mt = T / a.n_tiles, nt = T % a.n_tiles;
+      const uint32_t dt = tmem_base + lane_base + D_COLS0 + static_cast<uint32_t>(d) * 128u;
+      if (kb0 == 0 && kb1 == KB) {
+        for (int c0 = 0; c0 < a.n_tile; c0 += 16) {
+          uint32_t r[16];
+          tmem_ld_x16(dt + static_cast<uint32_t>(c0), r);
+          tmem_wait_ld();
+          float v[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+          epilogue_chunk<EPI>(a, es, mt, nt, c0, e, v);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&dfree_bar[d]);
+      } else {
+        const int first_cta = cta_of_unit(static_cast<long long>(T) * KB, U, G);
+        const int last_cta = cta_of_unit(static_cast<long long>(T) * KB + KB - 1, U, G);
+        const int nseg = last_cta - first_cta + 1;
+        const int segidx = static_cast<int>(blockIdx.x) - first_cta;
+        const size_t tile_elems = static_cast<size_t>(a.n_tile) * 128;
+        float* wsT = a.ws + static_cast<size_t>(T) * a.max_seg * tile_elems;
+        for (int c0 = 0; c0 < a.n_tile; c0 += 16) {
+          uint32_t r[16];
+          tmem_ld_x16(dt + static_cast<uint32_t>(c0), r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            wsT[segidx * tile_elems + static_cast<size_t>(c0 + j) * 128 + e] = __uint_as_float(r[j]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&dfree_bar[d]);
+        __threadfence();
+        named_bar_sync(1, 128);
+        if (e == 0) {
+          const int old = atomicAdd(a.counters + T, 1);
+          es.last_flag = (old == nseg - 1) ? 1 : 0;
+        }
+        named_bar_sync(1, 128);
+        if (es.last_flag) {
+          __threadfence();
+          for (int c0 = 0; c0 < a.n_tile; c0 += 16) {
+            float v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              float acc = 0.0f;
+              for (int sg = 0; sg < nseg; ++sg)
+                acc += __ldcg(wsT + sg * tile_elems + static_cast<size_t>(c0 + j) * 128 + e);
+              v[j] = acc;
+            }
+            epilogue_chunk<EPI>(a, es, mt, nt, c0, e, v);
+          }
+          if (e == 0) a.counters[T] = 0;
+        }
+        named_bar_sync(1, 128);
+      }
+      u = seg_end;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 2) tmem_dealloc(tmem_base, GEMM_TMEM_COLS);
+}
+
+}  // namespace qasr

@@ -1,0 +1,1209 @@
+// Host runtime of the B200 text-decoder backend: the C ABI of include/qasr_b200.h.
+//
+// One context = one device, one stream, one replica of the weights, one paged KV pool
+// and a slot table.  The batched decode step (BatchProjections::step,
+// src/decoder.rs:3339-3510) is recorded once per slot list into a CUDA graph and
+// replayed; per-step state (input tokens, positions) lives in device memory, so a
+// step needs no host->device traffic (on-device token feedback,
+// src/decoder.rs:2125-2126).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "attention.cuh"
+#include "f16_host.h"
+#include "gemm_tc.cuh"
+#include "qasr_b200.h"
+#include "qasr_b200_kernels.h"
+#include "rows.cuh"
+
+namespace qasr {
+
+std::atomic<uint64_t> g_launches{0};
+
+// ----------------------------------------------------------------------------- TMA maps
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn(std::string* err) {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  if (!fn && err) *err = "cuTensorMapEncodeTiled is not available from the driver";
+  return fn;
+}
+
+// 2-D row-major tensor [outer, inner] with 128-byte swizzled boxes {box_inner, box_outer}.
+static bool make_tmap(CUtensorMap* m, const void* base, bool bytes1, uint64_t inner,
+                      uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                      std::string* err) {
+  EncodeTiledFn fn = encode_fn(err);
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(m, bytes1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                        2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    if (err) *err = "cuTensorMapEncodeTiled failed (code " + std::to_string(static_cast<int>(r)) + ")";
+    return false;
+  }
+  return true;
+}
+
+// ----------------------------------------------------------------------------- GEMM plan
+struct Linear {
+  void* w = nullptr;        // device [n_out, k]
+  __half* scale = nullptr;  // device [n_out] (int8)
+  int n_out = 0, k = 0;
+  bool int8 = false;
+  CUtensorMap tm{};
+};
+
+struct GemmLaunch {
+  const CUtensorMap* tmw = nullptr;
+  CUtensorMap tmx{};
+  GemmArgs args{};
+  int grid = 0;
+  size_t smem = 0;
+  bool int8 = false;
+  int epi = 0;
+};
+
+static int g_dyn_smem_max = 0;
+
+template <bool I8, int EPI>
+static cudaError_t gemm_set_attr(int dyn) {
+  return cudaFuncSetAttribute(gemm_tc_kernel<I8, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              dyn);
+}
+
+static cudaError_t init_kernel_attrs(std::string* err) {
+  static std::once_flag once;
+  static cudaError_t result = cudaSuccess;
+  std::call_once(once, [] {
+    cudaFuncAttributes fa{};
+    result = cudaFuncGetAttributes(&fa, gemm_tc_kernel<true, EPI_QKV>);
+    if (result != cudaSuccess) return;
+    int optin = 0, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    g_dyn_smem_max = optin - static_cast<int>(fa.sharedSizeBytes) - 256;
+    const int d = g_dyn_smem_max;
+    cudaError_t e = cudaSuccess;
+    e = e ? e : gemm_set_attr<false, EPI_STORE>(d);
+    e = e ? e : gemm_set_attr<false, EPI_RESID>(d);
+    e = e ? e : gemm_set_attr<false, EPI_SILU>(d);
+    e = e ? e : gemm_set_attr<false, EPI_QKV>(d);
+    e = e ? e : gemm_set_attr<false, EPI_LOGITS>(d);
+    e = e ? e : gemm_set_attr<true, EPI_STORE>(d);
+    e = e ? e : gemm_set_attr<true, EPI_RESID>(d);
+    e = e ? e : gemm_set_attr<true, EPI_SILU>(d);
+    e = e ? e : gemm_set_attr<true, EPI_QKV>(d);
+    result = e;
+  });
+  if (result != cudaSuccess && err) *err = std::string("kernel attribute setup: ") + cudaGetErrorString(result);
+  return result;
+}
+
+static int cta_of_unit_host(long long x, long long units, long long grid) {
+  return static_cast<int>(((x + 1) * grid + units - 1) / units - 1);
+}
+
+struct GemmShape {
+  int n_tile, n_tiles, kblocks, tiles, units, grid, stages, max_seg;
+  size_t smem, ws_floats;
+};
+
+static GemmShape gemm_shape(int n_out, int k, bool int8, int rows, int num_sms) {
+  GemmShape s{};
+  s.n_tile = rows <= GEMM_MAX_NTILE ? std::max(16, (rows + 15) / 16 * 16) : GEMM_MAX_NTILE;
+  s.n_tiles = (rows + s.n_tile - 1) / s.n_tile;
+  const int ke = int8 ? 128 : 64;
+  s.kblocks = k / ke;
+  s.tiles = (n_out / 128) * s.n_tiles;
+  s.units = s.tiles * s.kblocks;
+  s.grid = std::min(num_sms, s.units);
+  const int atoms = int8 ? 2 : 1;
+  const int stage = 16384 + atoms * s.n_tile * 128;
+  const int dyn = g_dyn_smem_max > 0 ? g_dyn_smem_max : 200 * 1024;
+  s.stages = std::max(2, std::min(GEMM_MAX_STAGES, (dyn - 1024) / stage));
+  s.smem = static_cast<size_t>(s.stages) * stage + 1024;
+  int max_seg = 1;
+  for (int t = 0; t < s.tiles; ++t) {
+    const long long a = static_cast<long long>(t) * s.kblocks;
+    const int f = cta_of_unit_host(a, s.units, s.grid);
+    const int l = cta_of_unit_host(a + s.kblocks - 1, s.units, s.grid);
+    max_seg = std::max(max_seg, l - f + 1);
+  }
+  s.max_seg = max_seg;
+  s.ws_floats = max_seg > 1 ? static_cast<size_t>(s.tiles) * max_seg * s.n_tile * 128 : 0;
+  return s;
+}
+
+static cudaError_t launch_gemm(const GemmLaunch& L, cudaStream_t st) {
+  dim3 grid(L.grid), block(GEMM_THREADS);
+#define QASR_GEMM_CASE(I8, EPI)                                                          \
+  if (L.int8 == I8 && L.epi == EPI) {                                                    \
+    gemm_tc_kernel<I8, EPI><<<grid, block, L.smem, st>>>(*L.tmw, L.tmx, L.args);          \
+    g_launches.fetch_add(1, std::memory_order_relaxed);                                  \
+    return cudaGetLastError();                                                           \
+  }
+  QASR_GEMM_CASE(false, EPI_STORE)
+  QASR_GEMM_CASE(false, EPI_RESID)
+  QASR_GEMM_CASE(false, EPI_SILU)
+  QASR_GEMM_CASE(false, EPI_QKV)
+  QASR_GEMM_CASE(false, EPI_LOGITS)
+  QASR_GEMM_CASE(true, EPI_STORE)
+  QASR_GEMM_CASE(true, EPI_RESID)
+  QASR_GEMM_CASE(true, EPI_SILU)
+  QASR_GEMM_CASE(true, EPI_QKV)
+#undef QASR_GEMM_CASE
+  return cudaErrorInvalidValue;
+}
+
+// Per-device workspaces shared by the probe entry points (grow-only).
+struct ProbeWs {
+  float* ws = nullptr;
+  size_t ws_floats = 0;
+  int* cnt = nullptr;
+  size_t cnt_n = 0;
+};
+
+}  // namespace qasr
+
+using namespace qasr;
+
+// ============================================================================ context
+struct LayerDev {
+  Linear qkv, o, gu, down;
+  float *iln = nullptr, *pln = nullptr, *qn = nullptr, *kn = nullptr;
+  bool loaded = false;
+};
+
+struct SlotState {
+  bool used = false;
+  int cap = 0;
+  int pos = 0;
+  std::vector<int> pages;
+};
+
+struct qasr_ctx {
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t stream = nullptr;
+  qasr_text_config cfg{};
+  qasr_options opts{};
+  std::string err;
+  std::vector<void*> allocs;
+
+  std::vector<LayerDev> layers;
+  Linear lm;  // tied embedding as an f16 [vocab, hs] weight
+  float* final_norm = nullptr;
+  bool embed_loaded = false;
+  __half *rope_cos = nullptr, *rope_sin = nullptr;
+  int rope_positions = 0;
+
+  __half* kv_pool = nullptr;
+  int kv_pages = 0, max_pages = 0;
+  int* page_table = nullptr;
+  std::vector<int> free_pages;
+  std::vector<SlotState> slots;
+  int* pos_dev = nullptr;
+  int* next_tok_dev = nullptr;
+
+  int rows_max = 0;
+  __half *h = nullptr, *x = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr, *xf = nullptr;
+  int *drow_slot = nullptr, *drow_pos = nullptr;  // decode rows (read by the step graph)
+  int *prow_slot = nullptr, *prow_pos = nullptr;  // prefill rows
+  int *fin_slot = nullptr, *fin_pos = nullptr, *fin_src = nullptr, *out_tok = nullptr;
+  int* tok_in = nullptr;
+  unsigned long long* best = nullptr;
+  float* logits = nullptr;
+  int logits_rows = 0;
+  int last_logit_rows = 0;
+  float* gemm_ws = nullptr;
+  size_t gemm_ws_floats = 0;
+  int* gemm_cnt = nullptr;
+  size_t gemm_cnt_n = 0;
+  float* attn_ws = nullptr;
+  int* attn_cnt = nullptr;
+  int attn_max_chunks = ATTN_ROW_CHUNKS;
+  uint32_t* status = nullptr;
+  int* pinned_tok = nullptr;  // synchronous staging
+  int* pinned_in = nullptr;   // input-token staging, reusable once ev_in completed
+  cudaEvent_t ev_in = nullptr;
+
+  cudaGraphExec_t graph = nullptr;
+  std::vector<int> graph_slots;
+  uint64_t graph_kernels = 0;
+};
+
+namespace {
+
+qasr_status fail(qasr_ctx* c, qasr_status s, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  if (c) c->err = buf;
+  return s;
+}
+
+qasr_status cuda_fail(qasr_ctx* c, cudaError_t e, const char* what) {
+  return fail(c, e == cudaErrorMemoryAllocation ? QASR_ERR_OOM : QASR_ERR_DEVICE, "%s: %s", what,
+              cudaGetErrorString(e));
+}
+
+#define CK(call, what)                                 \
+  do {                                                 \
+    cudaError_t _e = (call);                           \
+    if (_e != cudaSuccess) return cuda_fail(c, _e, what); \
+  } while (0)
+
+template <class T>
+qasr_status dalloc(qasr_ctx* c, T** p, size_t count, const char* what) {
+  void* v = nullptr;
+  const size_t bytes = std::max<size_t>(count * sizeof(T), 256);
+  cudaError_t e = cudaMalloc(&v, bytes);
+  if (e != cudaSuccess) return cuda_fail(c, e, what);
+  e = cudaMemset(v, 0, bytes);
+  if (e != cudaSuccess) return cuda_fail(c, e, what);
+  c->allocs.push_back(v);
+  *p = static_cast<T*>(v);
+  return QASR_OK;
+}
+
+void drop_graph(qasr_ctx* c) {
+  if (c->graph) cudaGraphExecDestroy(c->graph);
+  c->graph = nullptr;
+  c->graph_slots.clear();
+}
+
+qasr_status check_device_status(qasr_ctx* c) {
+  uint32_t st[2] = {0, 0};
+  CK(cudaMemcpyAsync(st, c->status, sizeof st, cudaMemcpyDeviceToHost, c->stream), "status read");
+  CK(cudaStreamSynchronize(c->stream), "stream sync");
+  if (st[0] != 0) {
+    const uint32_t zero[2] = {0, 0};
+    cudaMemcpy(c->status, zero, sizeof zero, cudaMemcpyHostToDevice);
+    if (st[0] == DEVERR_TIMEOUT)
+      return fail(c, QASR_ERR_DEVICE_TIMEOUT, "a device-side wait timed out (site 0x%x)", st[1]);
+    return fail(c, QASR_ERR_INVALID_ARG, "device-side bounds check failed (code %u, site 0x%x)",
+                st[0], st[1]);
+  }
+  return QASR_OK;
+}
+
+// Build a launch of `lin` over activations X [rows, lin.k] (row stride ldx elements).
+qasr_status plan_gemm(qasr_ctx* c, const Linear& lin, const __half* X, int ldx, int rows, int epi,
+                      GemmLaunch* L) {
+  const GemmShape s = gemm_shape(lin.n_out, lin.k, lin.int8, rows, c->num_sms);
+  if (s.ws_floats > c->gemm_ws_floats || static_cast<size_t>(s.tiles) > c->gemm_cnt_n)
+    return fail(c, QASR_ERR_CAPACITY, "GEMM workspace too small for %d x %d over %d rows",
+                lin.n_out, lin.k, rows);
+  if (!make_tmap(&L->tmx, X, false, static_cast<uint64_t>(lin.k), static_cast<uint64_t>(rows),
+                 static_cast<uint64_t>(ldx) * 2, 64, static_cast<uint32_t>(s.n_tile), &c->err))
+    return QASR_ERR_DEVICE;
+  L->tmw = &lin.tm;
+  L->int8 = lin.int8;
+  L->epi = epi;
+  L->grid = s.grid;
+  L->smem = s.smem;
+  GemmArgs& a = L->args;
+  a = GemmArgs{};
+  a.n_out = lin.n_out;
+  a.k = lin.k;
+  a.rows = rows;
+  a.n_tile = s.n_tile;
+  a.n_tiles = s.n_tiles;
+  a.kblocks = s.kblocks;
+  a.units = s.units;
+  a.grid = s.grid;
+  a.stages = s.stages;
+  a.max_seg = s.max_seg;
+  a.scale = lin.scale;
+  a.epi = epi;
+  a.ws = c->gemm_ws;
+  a.counters = c->gemm_cnt;
+  a.status = c->status;
+  a.eps = c->cfg.rms_norm_eps;
+  a.kv.pool = c->kv_pool;
+  a.kv.page_table = c->page_table;
+  a.kv.max_pages = c->max_pages;
+  a.kv.layers = c->cfg.num_hidden_layers;
+  a.kv.nkv = c->cfg.num_key_value_heads;
+  a.q_ld = c->cfg.num_attention_heads * c->cfg.head_dim;
+  a.rope_cos = c->rope_cos;
+  a.rope_sin = c->rope_sin;
+  return QASR_OK;
+}
+
+qasr_status run_gemm(qasr_ctx* c, const GemmLaunch& L) {
+  CK(launch_gemm(L, c->stream), "GEMM launch");
+  return QASR_OK;
+}
+
+qasr_status launch_attention(qasr_ctx* c, int layer, int rows, const int* rs, const int* rp) {
+  AttnArgs a{};
+  a.q = c->q;
+  a.q_ld = c->cfg.num_attention_heads * c->cfg.head_dim;
+  a.out = c->attn;
+  a.row_slot = rs;
+  a.row_pos = rp;
+  a.kv.pool = c->kv_pool;
+  a.kv.page_table = c->page_table;
+  a.kv.max_pages = c->max_pages;
+  a.kv.layers = c->cfg.num_hidden_layers;
+  a.kv.nkv = c->cfg.num_key_value_heads;
+  a.layer = layer;
+  a.rows = rows;
+  a.scale = 1.0f / std::sqrt(static_cast<float>(c->cfg.head_dim));
+  a.ws = c->attn_ws;
+  a.counters = c->attn_cnt;
+  a.max_chunks = c->attn_max_chunks;
+  a.status = c->status;
+  const int grid = c->num_sms * 4;
+  attention_kernel<<<grid, ATTN_THREADS, (rows + 1) * sizeof(int), c->stream>>>(a);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  CK(cudaGetLastError(), "attention launch");
+  return QASR_OK;
+}
+
+// All layers over `rows` rows already in c->h with row_slot/row_pos set.
+qasr_status enqueue_layers(qasr_ctx* c, int rows, const int* rs, const int* rp, uint64_t* nk) {
+  const int hs = c->cfg.hidden_size;
+  const int qd = c->cfg.num_attention_heads * c->cfg.head_dim;
+  const int I = c->cfg.intermediate_size;
+  for (int l = 0; l < c->cfg.num_hidden_layers; ++l) {
+    LayerDev& L = c->layers[l];
+    rmsnorm_rows_kernel<<<rows, 256, 0, c->stream>>>(c->x, c->h, nullptr, L.iln, hs, c->cfg.rms_norm_eps);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    CK(cudaGetLastError(), "rmsnorm launch");
+    GemmLaunch g;
+    qasr_status s = plan_gemm(c, L.qkv, c->x, hs, rows, EPI_QKV, &g);
+    if (s) return s;
+    g.args.qn_w = L.qn;
+    g.args.kn_w = L.kn;
+    g.args.q_out = c->q;
+    g.args.layer = l;
+    g.args.row_slot = rs;
+    g.args.row_pos = rp;
+    if ((s = run_gemm(c, g))) return s;
+    if ((s = launch_attention(c, l, rows, rs, rp))) return s;
+    if ((s = plan_gemm(c, L.o, c->attn, qd, rows, EPI_RESID, &g))) return s;
+    g.args.out = c->h;
+    g.args.ldo = hs;
+    if ((s = run_gemm(c, g))) return s;
+    rmsnorm_rows_kernel<<<rows, 256, 0, c->stream>>>(c->x, c->h, nullptr, L.pln, hs, c->cfg.rms_norm_eps);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    CK(cudaGetLastError(), "rmsnorm launch");
+    if ((s = plan_gemm(c, L.gu, c->x, hs, rows, EPI_SILU, &g))) return s;
+    g.args.out = c->act;
+    g.args.ldo = I;
+    if ((s = run_gemm(c, g))) return s;
+    if ((s = plan_gemm(c, L.down, c->act, I, rows, EPI_RESID, &g))) return s;
+    g.args.out = c->h;
+    g.args.ldo = hs;
+    if ((s = run_gemm(c, g))) return s;
+    *nk += 7;
+  }
+  return QASR_OK;
+}
+
+// final norm + lm_head + argmax for `n` rows: xf[i] = norm(h[src_rows[i]]).
+qasr_status enqueue_head(qasr_ctx* c, int n, const int* src_rows, const int* slot_of,
+                         const int* pos_of, int* out_tok, uint64_t* nk) {
+  const int hs = c->cfg.hidden_size;
+  rmsnorm_rows_kernel<<<n, 256, 0, c->stream>>>(c->xf, c->h, src_rows, c->final_norm, hs,
+                                                c->cfg.rms_norm_eps);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  CK(cudaGetLastError(), "final norm launch");
+  GemmLaunch g;
+  qasr_status s = plan_gemm(c, c->lm, c->xf, hs, n, EPI_LOGITS, &g);
+  if (s) return s;
+  g.args.logits = (c->opts.flags & QASR_FLAG_KEEP_LOGITS) ? c->logits : nullptr;
+  g.args.ld_logits = c->cfg.vocab_size;
+  g.args.best = c->best;
+  if ((s = run_gemm(c, g))) return s;
+  finalize_rows_kernel<<<(n + 127) / 128, 128, 0, c->stream>>>(c->best, n, slot_of, pos_of,
+                                                               out_tok, c->next_tok_dev, c->pos_dev);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  CK(cudaGetLastError(), "finalize launch");
+  *nk += 3;
+  return QASR_OK;
+}
+
+qasr_status enqueue_decode(qasr_ctx* c, int n, uint64_t* nk) {
+  embed_rows_kernel<<<n, 128, 0, c->stream>>>(c->h, static_cast<const __half*>(c->lm.w),
+                                              c->cfg.hidden_size, c->cfg.vocab_size, c->drow_slot,
+                                              c->next_tok_dev, c->pos_dev, c->drow_pos, c->status);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  CK(cudaGetLastError(), "embed launch");
+  *nk += 1;
+  qasr_status s = enqueue_layers(c, n, c->drow_slot, c->drow_pos, nk);
+  if (s) return s;
+  return enqueue_head(c, n, nullptr, c->drow_slot, c->drow_pos, c->out_tok, nk);
+}
+
+qasr_status ready(qasr_ctx* c) {
+  if (!c->embed_loaded) return fail(c, QASR_ERR_STATE, "embedding not loaded");
+  for (size_t l = 0; l < c->layers.size(); ++l)
+    if (!c->layers[l].loaded) return fail(c, QASR_ERR_STATE, "layer %zu not loaded", l);
+  if (c->rope_positions <= 0) return fail(c, QASR_ERR_STATE, "rope tables not set");
+  return QASR_OK;
+}
+
+qasr_status check_slot(qasr_ctx* c, int slot) {
+  if (slot < 0 || slot >= static_cast<int>(c->slots.size()) || !c->slots[slot].used)
+    return fail(c, QASR_ERR_INVALID_ARG, "slot %d is not allocated", slot);
+  return QASR_OK;
+}
+
+qasr_status grow_slot(qasr_ctx* c, int slot, int need) {
+  SlotState& S = c->slots[slot];
+  if (need <= S.cap) return QASR_OK;
+  if (need > c->opts.max_seq)
+    return fail(c, QASR_ERR_CAPACITY, "slot %d needs %d positions, max_seq is %d", slot, need,
+                c->opts.max_seq);
+  const int want_pages = (need + QASR_PAGE_POSITIONS - 1) / QASR_PAGE_POSITIONS;
+  const int add = want_pages - static_cast<int>(S.pages.size());
+  if (add > static_cast<int>(c->free_pages.size()))
+    return fail(c, QASR_ERR_CAPACITY, "KV pool exhausted: slot %d needs %d more pages, %zu free",
+                slot, add, c->free_pages.size());
+  for (int i = 0; i < add; ++i) {
+    S.pages.push_back(c->free_pages.back());
+    c->free_pages.pop_back();
+  }
+  S.cap = static_cast<int>(S.pages.size()) * QASR_PAGE_POSITIONS;
+  CK(cudaMemcpyAsync(c->page_table + static_cast<size_t>(slot) * c->max_pages, S.pages.data(),
+                     S.pages.size() * sizeof(int), cudaMemcpyHostToDevice, c->stream),
+     "page table upload");
+  CK(cudaStreamSynchronize(c->stream), "page table sync");
+  return QASR_OK;
+}
+
+qasr_status upload_linear(qasr_ctx* c, Linear* lin, int n_out, int k, bool int8,
+                          const std::vector<const void*>& parts, const std::vector<int>& part_rows,
+                          const std::vector<const uint16_t*>& scales,
+                          const std::vector<int>& row_order /* fused row -> (part,row) flat */) {
+  // Fuse the parts along the output dim in `row_order` and upload.
+  const size_t elem = int8 ? 1 : 2;
+  std::vector<uint8_t> host(static_cast<size_t>(n_out) * k * elem);
+  std::vector<uint16_t> host_s(int8 ? n_out : 0);
+  std::vector<int> part_base(parts.size(), 0);
+  for (size_t p = 1; p < parts.size(); ++p) part_base[p] = part_base[p - 1] + part_rows[p - 1];
+  for (int r = 0; r < n_out; ++r) {
+    const int src = row_order.empty() ? r : row_order[r];
+    size_t p = 0;
+    while (p + 1 < parts.size() && src >= part_base[p + 1]) ++p;
+    const int pr = src - part_base[p];
+    std::memcpy(&host[static_cast<size_t>(r) * k * elem],
+                static_cast<const uint8_t*>(parts[p]) + static_cast<size_t>(pr) * k * elem, k * elem);
+    if (int8) host_s[r] = scales[p][pr];
+  }
+  if (!lin->w) {
+    qasr_status s = dalloc(c, reinterpret_cast<uint8_t**>(&lin->w), host.size(), "weight alloc");
+    if (s) return s;
+    if (int8 && (s = dalloc(c, &lin->scale, n_out, "scale alloc"))) return s;
+  }
+  CK(cudaMemcpy(lin->w, host.data(), host.size(), cudaMemcpyHostToDevice), "weight upload");
+  if (int8) CK(cudaMemcpy(lin->scale, host_s.data(), n_out * 2, cudaMemcpyHostToDevice), "scale upload");
+  lin->n_out = n_out;
+  lin->k = k;
+  lin->int8 = int8;
+  if (!make_tmap(&lin->tm, lin->w, int8, static_cast<uint64_t>(k), static_cast<uint64_t>(n_out),
+                 static_cast<uint64_t>(k) * elem, int8 ? 128 : 64, 128, &c->err))
+    return QASR_ERR_DEVICE;
+  return QASR_OK;
+}
+
+qasr_status upload_f32_vec(qasr_ctx* c, float** dst, const uint16_t* src, int n) {
+  if (!src) return fail(c, QASR_ERR_INVALID_ARG, "missing norm vector");
+  std::vector<float> f(n);
+  for (int i = 0; i < n; ++i) f[i] = f16_bits_to_f32(src[i]);
+  if (!*dst) {
+    qasr_status s = dalloc(c, dst, n, "norm alloc");
+    if (s) return s;
+  }
+  CK(cudaMemcpy(*dst, f.data(), n * sizeof(float), cudaMemcpyHostToDevice), "norm upload");
+  return QASR_OK;
+}
+
+}  // namespace
+
+// ============================================================================ C ABI
+extern "C" {
+
+const char* qasr_version(void) { return "qasr_b200 0.1.0 (sm_100a, tcgen05)"; }
+
+const char* qasr_last_error(const qasr_ctx* ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+uint64_t qasr_kernel_launch_count(void) { return g_launches.load(); }
+
+qasr_status qasr_create(const qasr_text_config* cfg, const qasr_options* opts, int device,
+                        qasr_ctx** out) {
+  if (!cfg || !opts || !out) return QASR_ERR_INVALID_ARG;
+  *out = nullptr;
+  auto* c = new qasr_ctx();
+  c->cfg = *cfg;
+  c->opts = *opts;
+  c->device = device;
+  const qasr_text_config& t = *cfg;
+  auto bad = [&](const char* m) {
+    fail(c, QASR_ERR_INVALID_ARG, "%s", m);
+    *out = c;  // the caller reads the message, then destroys
+    return QASR_ERR_INVALID_ARG;
+  };
+  if (t.head_dim != 128) return bad("head_dim must be 128");
+  if (t.num_key_value_heads <= 0 || t.num_attention_heads != 2 * t.num_key_value_heads)
+    return bad("the B200 kernels need 2 query heads per kv head (GQA rep 2)");
+  if (t.hidden_size % 128 || t.intermediate_size % 128 || t.vocab_size % 128 ||
+      t.hidden_size < 128 || t.vocab_size <= 0 || t.num_hidden_layers <= 0)
+    return bad("hidden, intermediate and vocab sizes must be positive multiples of 128");
+  if (opts->weight_format != QASR_WEIGHTS_F16 && opts->weight_format != QASR_WEIGHTS_INT8)
+    return bad("weight_format must be QASR_WEIGHTS_F16 or QASR_WEIGHTS_INT8");
+  if (opts->max_slots <= 0 || opts->max_slots > 4096 || opts->max_seq <= 0)
+    return bad("max_slots must be 1..4096 and max_seq positive");
+  if (c->opts.max_prefill_rows <= 0) c->opts.max_prefill_rows = 2048;
+  c->opts.max_prefill_rows = std::min(c->opts.max_prefill_rows, 4096);
+  *out = c;
+
+  CK(cudaSetDevice(device), "cudaSetDevice");
+  CK(cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device), "SM count");
+  int major = 0;
+  CK(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device), "cc");
+  if (major != 10) return fail(c, QASR_ERR_DEVICE, "device %d is not an sm_100 (B200) GPU", device);
+  if (init_kernel_attrs(&c->err) != cudaSuccess) return QASR_ERR_DEVICE;
+  CK(cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking), "stream create");
+  c->stream = c->own_stream;
+
+  const int L = t.num_hidden_layers, hs = t.hidden_size, I = t.intermediate_size;
+  const int qd = t.num_attention_heads * t.head_dim;
+  c->layers.resize(L);
+  c->max_pages = (opts->max_seq + QASR_PAGE_POSITIONS - 1) / QASR_PAGE_POSITIONS;
+  c->kv_pages = opts->kv_pages > 0 ? opts->kv_pages : opts->max_slots * c->max_pages;
+  const size_t page_elems = static_cast<size_t>(L) * 2 * t.num_key_value_heads * 64 * 128;
+  qasr_status s;
+  if ((s = dalloc(c, &c->kv_pool, page_elems * c->kv_pages, "KV pool"))) return s;
+  if ((s = dalloc(c, &c->page_table, static_cast<size_t>(opts->max_slots) * c->max_pages, "page table")))
+    return s;
+  c->free_pages.resize(c->kv_pages);
+  for (int i = 0; i < c->kv_pages; ++i) c->free_pages[i] = c->kv_pages - 1 - i;
+  c->slots.resize(opts->max_slots);
+  if ((s = dalloc(c, &c->pos_dev, opts->max_slots, "pos"))) return s;
+  if ((s = dalloc(c, &c->next_tok_dev, opts->max_slots, "tokens"))) return s;
+
+  c->rows_max = std::max(opts->max_slots, c->opts.max_prefill_rows);
+  const size_t R = c->rows_max;
+  if ((s = dalloc(c, &c->h, R * hs, "h")) || (s = dalloc(c, &c->x, R * hs, "x")) ||
+      (s = dalloc(c, &c->q, R * qd, "q")) || (s = dalloc(c, &c->attn, R * qd, "attn")) ||
+      (s = dalloc(c, &c->act, R * I, "act")) ||
+      (s = dalloc(c, &c->xf, static_cast<size_t>(opts->max_slots) * hs, "xf")) ||
+      (s = dalloc(c, &c->drow_slot, opts->max_slots, "drow_slot")) ||
+      (s = dalloc(c, &c->drow_pos, opts->max_slots, "drow_pos")) ||
+      (s = dalloc(c, &c->prow_slot, R, "prow_slot")) || (s = dalloc(c, &c->prow_pos, R, "prow_pos")) ||
+      (s = dalloc(c, &c->fin_slot, opts->max_slots, "fin_slot")) ||
+      (s = dalloc(c, &c->fin_pos, opts->max_slots, "fin_pos")) ||
+      (s = dalloc(c, &c->fin_src, opts->max_slots, "fin_src")) ||
+      (s = dalloc(c, &c->out_tok, opts->max_slots, "out_tok")) ||
+      (s = dalloc(c, &c->tok_in, 2 * static_cast<size_t>(opts->max_slots), "tok_in")) ||
+      (s = dalloc(c, &c->best, opts->max_slots, "argmax keys")) ||
+      (s = dalloc(c, &c->status, 4, "status")))
+    return s;
+  if (opts->flags & QASR_FLAG_KEEP_LOGITS) {
+    c->logits_rows = opts->max_slots;
+    if ((s = dalloc(c, &c->logits, static_cast<size_t>(opts->max_slots) * t.vocab_size, "logits")))
+      return s;
+  }
+  // GEMM split workspace: worst case over every GEMM shape and row count used.
+  const bool i8 = opts->weight_format == QASR_WEIGHTS_INT8;
+  size_t wsf = 0, cnt = 0;
+  const int shapes[4][2] = {{qd + 2 * t.num_key_value_heads * 128, hs}, {hs, qd}, {2 * I, hs}, {hs, I}};
+  for (int rows = 1; rows <= c->rows_max; rows = rows < 128 ? rows + 1 : rows + 128) {
+    for (auto& sh : shapes) {
+      const GemmShape g = gemm_shape(sh[0], sh[1], i8, rows, c->num_sms);
+      wsf = std::max(wsf, g.ws_floats);
+      cnt = std::max(cnt, static_cast<size_t>(g.tiles));
+    }
+    if (rows <= opts->max_slots) {
+      const GemmShape g = gemm_shape(t.vocab_size, hs, false, rows, c->num_sms);
+      wsf = std::max(wsf, g.ws_floats);
+      cnt = std::max(cnt, static_cast<size_t>(g.tiles));
+    }
+  }
+  c->gemm_ws_floats = wsf;
+  c->gemm_cnt_n = cnt;
+  if ((s = dalloc(c, &c->gemm_ws, std::max<size_t>(wsf, 64), "GEMM workspace")) ||
+      (s = dalloc(c, &c->gemm_cnt, cnt, "GEMM counters")))
+    return s;
+  const size_t apart = R * t.num_key_value_heads * c->attn_max_chunks * ATTN_PART_FLOATS;
+  if ((s = dalloc(c, &c->attn_ws, apart, "attention workspace")) ||
+      (s = dalloc(c, &c->attn_cnt, R * t.num_key_value_heads, "attention counters")))
+    return s;
+  CK(cudaMallocHost(&c->pinned_tok, sizeof(int) * opts->max_slots * 2), "pinned alloc");
+  CK(cudaMallocHost(&c->pinned_in, sizeof(int) * opts->max_slots * 2), "pinned alloc");
+  CK(cudaEventCreateWithFlags(&c->ev_in, cudaEventDisableTiming), "event create");
+  return QASR_OK;
+}
+
+void qasr_destroy(qasr_ctx* c) {
+  if (!c) return;
+  cudaSetDevice(c->device);
+  if (c->stream) cudaStreamSynchronize(c->stream);
+  drop_graph(c);
+  for (void* p : c->allocs) cudaFree(p);
+  if (c->pinned_tok) cudaFreeHost(c->pinned_tok);
+  if (c->pinned_in) cudaFreeHost(c->pinned_in);
+  if (c->ev_in) cudaEventDestroy(c->ev_in);
+  if (c->own_stream) cudaStreamDestroy(c->own_stream);
+  delete c;
+}
+
+qasr_status qasr_set_stream(qasr_ctx* c, void* stream) {
+  if (!c) return QASR_ERR_INVALID_ARG;
+  drop_graph(c);
+  c->stream = stream ? static_cast<cudaStream_t>(stream) : c->own_stream;
+  return QASR_OK;
+}
+
+qasr_status qasr_synchronize(qasr_ctx* c) {
+  if (!c) return QASR_ERR_INVALID_ARG;
+  cudaSetDevice(c->device);
+  return check_device_status(c);
+}
+
+qasr_status qasr_load_embed(qasr_ctx* c, const uint16_t* embed, const uint16_t* final_norm) {
+  if (!c || !embed || !final_norm) return fail(c, QASR_ERR_INVALID_ARG, "null embed/final_norm");
+  CK(cudaSetDevice(c->device), "cudaSetDevice");
+  drop_graph(c);
+  const int V = c->cfg.vocab_size, hs = c->cfg.hidden_size;
+  qasr_status s = upload_linear(c, &c->lm, V, hs, false, {embed}, {V}, {}, {});
+  if (s) return s;
+  if ((s = upload_f32_vec(c, &c->final_norm, final_norm, hs))) return s;
+  c->embed_loaded = true;
+  return QASR_OK;
+}
+
+qasr_status qasr_load_layer(qasr_ctx* c, int layer, const qasr_layer_weights* w) {
+  if (!c || !w) return fail(c, QASR_ERR_INVALID_ARG, "null layer weights");
+  if (layer < 0 || layer >= c->cfg.num_hidden_layers)
+    return fail(c, QASR_ERR_INVALID_ARG, "layer %d out of range", layer);
+  CK(cudaSetDevice(c->device), "cudaSetDevice");
+  drop_graph(c);
+  const bool i8 = c->opts.weight_format == QASR_WEIGHTS_INT8;
+  const int hs = c->cfg.hidden_size, I = c->cfg.intermediate_size;
+  const int qd = c->cfg.num_attention_heads * c->cfg.head_dim;
+  const int kvd = c->cfg.num_key_value_heads * c->cfg.head_dim;
+  const void* lin[7] = {w->q_proj, w->k_proj, w->v_proj, w->o_proj, w->gate_proj, w->up_proj, w->down_proj};
+  const uint16_t* sc[7] = {w->q_scale, w->k_scale, w->v_scale, w->o_scale, w->gate_scale, w->up_scale, w->down_scale};
+  for (int i = 0; i < 7; ++i) {
+    if (!lin[i]) return fail(c, QASR_ERR_INVALID_ARG, "layer %d: missing linear %d", layer, i);
+    if (i8 && !sc[i]) return fail(c, QASR_ERR_INVALID_ARG, "layer %d: missing int8 scale %d", layer, i);
+  }
+  LayerDev& L = c->layers[layer];
+  qasr_status s;
+  // fused [q|k|v] rows (fused_pieces / fused_i8_pieces, src/decoder.rs:4243-4314)
+  if ((s = upload_linear(c, &L.qkv, qd + 2 * kvd, hs, i8, {lin[0], lin[1], lin[2]}, {qd, kvd, kvd},
+                         {sc[0], sc[1], sc[2]}, {})))
+    return s;
+  if ((s = upload_linear(c, &L.o, hs, qd, i8, {lin[3]}, {hs}, {sc[3]}, {}))) return s;
+  // gate|up interleaved in 64-row blocks so one 128-row tile holds gate[j..j+64) and
+  // up[j..j+64): the SiLU product is formed in the GEMM epilogue.
+  std::vector<int> order(2 * I);
+  for (int r = 0; r < 2 * I; ++r) {
+    const int blk = r / 128, within = r % 128;
+    order[r] = within < 64 ? blk * 64 + within : I + blk * 64 + (within - 64);
+  }
+  if ((s = upload_linear(c, &L.gu, 2 * I, hs, i8, {lin[4], lin[5]}, {I, I}, {sc[4], sc[5]}, order)))
+    return s;
+  if ((s = upload_linear(c, &L.down, hs, I, i8, {lin[6]}, {hs}, {sc[6]}, {}))) return s;
+  if ((s = upload_f32_vec(c, &L.iln, w->input_layernorm, hs)) ||
+      (s = upload_f32_vec(c, &L.pln, w->post_attention_layernorm, hs)) ||
+      (s = upload_f32_vec(c, &L.qn, w->q_norm, c->cfg.head_dim)) ||
+      (s = upload_f32_vec(c, &L.kn, w->k_norm, c->cfg.head_dim)))
+    return s;
+  L.loaded = true;
+  return QASR_OK;
+}
+
+qasr_status qasr_set_rope_tables(qasr_ctx* c, const uint16_t* cos, const uint16_t* sin, int positions) {
+  if (!c || !cos || !sin || positions <= 0) return fail(c, QASR_ERR_INVALID_ARG, "bad rope tables");
+  CK(cudaSetDevice(c->device), "cudaSetDevice");
+  drop_graph(c);
+  const size_t n = static_cast<size_t>(positions) * c->cfg.head_dim;
+  if (positions > c->rope_positions) {
+    qasr_status s;
+    if ((s = dalloc(c, &c->rope_cos, n, "rope cos")) || (s = dalloc(c, &c->rope_sin, n, "rope sin")))
+      return s;
+  }
+  CK(cudaMemcpy(c->rope_cos, cos, n * 2, cudaMemcpyHostToDevice), "rope upload");
+  CK(cudaMemcpy(c->rope_sin, sin, n * 2, cudaMemcpyHostToDevice), "rope upload");
+  c->rope_positions = positions;
+  return QASR_OK;
+}
+
+int32_t qasr_max_seq(const qasr_ctx* c) { return c ? c->opts.max_seq : 0; }
+
+qasr_status qasr_fork_capped(qasr_ctx* c, int cap, int* slot) {
+  if (!c || !slot || cap <= 0) return fail(c, QASR_ERR_INVALID_ARG, "bad fork_capped arguments");
+  CK(cudaSetDevice(c->device), "cudaSetDevice");
+  int id = -1;
+  for (size_t i = 0; i < c->slots.size(); ++i)
+    if (!c->slots[i].used) {
+      id = static_cast<int>(i);
+      break;
+    }
+  if (id < 0) return fail(c, QASR_ERR_CAPACITY, "all %zu slots are in use", c->slots.size());
+  c->slots[id] = SlotState{};
+  c->slots[id].used = true;
+  qasr_status s = grow_slot(c, id, std::min(cap, c->opts.max_seq));
+  if (s) {
+    c->slots[id].used = false;
+    return s;
+  }
+  CK(cudaMemsetAsync(c->pos_dev + id, 0, 4, c->stream), "pos reset");
+  CK(cudaMemsetAsync(c->next_tok_dev + id, 0, 4, c->stream), "token reset");
+  CK(cudaStreamSynchronize(c->stream), "sync");
+  *slot = id;
+  return QASR_OK;
+}
+
+qasr_status qasr_slot_free(qasr_ctx* c, int slot) {
+  if (!c) return QASR_ERR_INVALID_ARG;
+  qasr_status s = check_slot(c, slot);
+  if (s) return s;
+  cudaSetDevice(c->device);
+  cudaStreamSynchronize(c->stream);
+  SlotState& S = c->slots[slot];
+  for (int p : S.pages) c->free_pages.push_back(p);
+  S = SlotState{};
+  return QASR_OK;
+}
+
+qasr_status qasr_ensure_capacity(qasr_ctx* c, int slot, int need, int* cap) {
+  if (!c) return QASR_ERR_INVALID_ARG;
+  qasr_status s = check_slot(c, slot);
+  if (s) return s;
+  CK(cudaSetDevice(c->device), "cudaSetDevice");
+  // grow-only and stepped like KV_STEP (src/decoder.rs:1604-1661); contents are kept
+  const int target = std::min(c->opts.max_seq, (need + 255) / 256 * 256);
+  if ((s = grow_slot(c, slot, std::max(target, need)))) return s;
+  if (cap) *cap = c->slots[slot].cap;
+  return QASR_OK;
+}
+
+qasr_status qasr_slot_pos(qasr_ctx* c, int slot, int* pos) {
+  if (!c || !pos) return QASR_ERR_INVALID_ARG;
+  qasr_status s = check_slot(c, slot);
+  if (s) return s;
+  *pos = c->slots[slot].pos;
+  return QASR_OK;
+}
+
+qasr_status qasr_set_slot_pos(qasr_ctx* c, int slot, int pos) {
+  if (!c) return QASR_ERR_INVALID_ARG;
+  qasr_status s = check_slot(c, slot);
+  if (s) return s;
+  if (pos < 0 || pos > c->slots[slot].cap)
+    return fail(c, QASR_ERR_INVALID_ARG, "position %d outside slot capacity %d", pos, c->slots[slot].cap);
+  CK(cudaSetDevice(c->device), "cudaSetDevice");
+  c->pinned_tok[0] = pos;
+  CK(cudaMemcpyAsync(c->pos_dev + slot, c->pinned_tok, 4, cudaMemcpyHostToDevice, c->stream), "pos upload");
+  CK(cudaStreamSynchronize(c->stream), "sync");
+  c->slots[slot].pos = pos;
+  return QASR_OK;
+}
+
+qasr_status qasr_set_input_token(qasr_ctx* c, int slot, int32_t token) {
+  if (!c) return QASR_ERR_INVALID_ARG;
+  qasr_status s = check_slot(c, slot);
+  if (s) return s;
+  if (token < 0 || token >= c->cfg.vocab_size)
+    return fail(c, QASR_ERR_INVALID_ARG, "token %d outside the vocabulary", token);
+  CK(cudaSetDevice(c->device), "cudaSetDevice");
+  c->pinned_tok[0] = token;
+  CK(cudaMemcpyAsync(c->next_tok_dev + slot, c->pinned_tok, 4, cudaMemcpyHostToDevice, c->stream),
+     "token upload");
+  CK(cudaStreamSynchronize(c->stream), "sync");
+  return QASR_OK;
+}
+
+qasr_status qasr_set_input_tokens(qasr_ctx* c, const int* slots, int n, const int32_t* tokens) {
+  if (!c || n < 0 || (n > 0 && (!slots || !tokens))) return fail(c, QASR_ERR_INVALID_ARG, "bad arguments");
+  if (n == 0) return QASR_OK;
+  if (n > static_cast<int>(c->slots.size())) return fail(c, QASR_ERR_INVALID_ARG, "too many slots");
+  for (int i = 0; i < n; ++i) {
+    qasr_status s = check_slot(c, slots[i]);
+    if (s) return s;
+    if (tokens[i] < 0 || tokens[i] >= c->cfg.vocab_size)
+      return fail(c, QASR_ERR_INVALID_ARG, "token %d outside the vocabulary", tokens[i]);
+  }
+  CK(cudaSetDevice(c->device), "cudaSetDevice");
+  CK(cudaEventSynchronize(c->ev_in), "staging reuse");
+  std::memcpy(c->pinned_in, slots, n * sizeof(int));
+  std::memcpy(c->pinned_in + c->slots.size(), tokens, n * sizeof(int));
+  CK(cudaMemcpyAsync(c->tok_in, c->pinned_in + c->slots.size(), n * sizeof(int), cudaMemcpyHostToDevice,
+                     c->stream),
+     "token upload");
+  int* slots_dev = c->tok_in + c->slots.size();
+  CK(cudaMemcpyAsync(slots_dev, c->pinned_in, n * sizeof(int), cudaMemcpyHostToDevice, c->stream),
+     "slot upload");
+  CK(cudaEventRecord(c->ev_in, c->stream), "event record");
+  scatter_tokens_kernel<<<(n + 127) / 128, 128, 0, c->stream>>>(c->next_tok_dev, slots_dev, c->tok_in, n);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  CK(cudaGetLastError(), "scatter launch");
+  return QASR_OK;
+}
+
+qasr_status qasr_step_batch(qasr_ctx* c, const int* slots, int n, int32_t* out_tokens) {
+  if (!c || (!slots && n > 0) || n < 0) return fail(c, QASR_ERR_INVALID_ARG, "bad step arguments");
+  if (n == 0) return QASR_OK;
+  qasr_status s = ready(c);
+  if (s) return s;
+  if (n > static_cast<int>(c->slots.size()))
+    return fail(c, QASR_ERR_INVALID_ARG, "%d rows exceed max_slots", n);
+  CK(cudaSetDevice(c->device), "cudaSetDevice");
+  std::vector<int> list(slots, slots + n);
+  {
+    std::vector<int> sorted = list;
+    std::sort(sorted.begin(), sorted.end());
+    if (std::adjacent_find(sorted.begin(), sorted.end()) != sorted.end())
+      return fail(c, QASR_ERR_INVALID_ARG, "a slot is listed twice");
+  }
+  for (int sl : list) {
+    if ((s = check_slot(c, sl))) return s;
+    const SlotState& S = c->slots[sl];
+    if (S.pos >= S.cap)
+      return fail(c, QASR_ERR_CAPACITY, "slot %d is full (%d positions); ensure_capacity first", sl, S.cap);
+    if (S.pos >= c->rope_positions)
+      return fail(c, QASR_ERR_CAPACITY, "slot %d position %d beyond the rope tables", sl, S.pos);
+  }
+  const bool use_graph = !(c->opts.flags & QASR_FLAG_NO_GRAPH);
+  if (!use_graph || !c->graph || c->graph_slots != list) {
+    drop_graph(c);
+    CK(cudaMemcpyAsync(c->drow_slot, list.data(), n * sizeof(int), cudaMemcpyHostToDevice, c->stream),
+       "row upload");
+    if (use_graph) {
+      uint64_t nk = 0;
+      const uint64_t before = g_launches.load();
+      CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "graph capture");
+      s = enqueue_decode(c, n, &nk);
+      cudaGraph_t g = nullptr;
+      const cudaError_t e = cudaStreamEndCapture(c->stream, &g);
+      g_launches.store(before);  // recorded, not launched
+      if (s) {
+        if (g) cudaGraphDestroy(g);
+        return s;
+      }
+      if (e != cudaSuccess) return cuda_fail(c, e, "graph capture");
+      const cudaError_t ie = cudaGraphInstantiate(&c->graph, g, 0);
+      cudaGraphDestroy(g);
+      if (ie != cudaSuccess) return cuda_fail(c, ie, "graph instantiate");
+      c->graph_slots = list;
+      c->graph_kernels = nk;
+    }
+  }
+  if (use_graph) {
+    CK(cudaGraphLaunch(c->graph, c->stream), "graph launch");
+    g_launches.fetch_add(c->graph_kernels, std::memory_order_relaxed);
+  } else {
+    uint64_t nk = 0;
+    if ((s = enqueue_decode(c, n, &nk))) return s;
+  }
+  for (int sl : list) c->slots[sl].pos += 1;
+  c->last_logit_rows = n;
+  if (out_tokens) {
+    CK(cudaMemcpyAsync(c->pinned_tok, c->out_tok, n * sizeof(int), cudaMemcpyDeviceToHost, c->stream),
+       "token readback");
+    if ((s = check_device_status(c))) return s;
+    std::memcpy(out_tokens, c->pinned_tok, n * sizeof(int));
+  }
+  return QASR_OK;
+}
+
+qasr_status qasr_step(qasr_ctx* c, int slot, int32_t* token) {
+  return qasr_step_batch(c, &slot, 1, token);
+}
+
+qasr_status qasr_prefill_batch(qasr_ctx* c, const int* slots, int n, const uint16_t* hidden,
+                               const int* lens, const int* kv_starts, int32_t* first_tokens) {
+  if (!c || !slots || !hidden || !lens || n <= 0 || !first_tokens)
+    return fail(c, QASR_ERR_INVALID_ARG, "bad prefill arguments");
+  qasr_status s = ready(c);
+  if (s) return s;
+  if (n > static_cast<int>(c->slots.size())) return fail(c, QASR_ERR_INVALID_ARG, "too many segments");
+  CK(cudaSetDevice(c->device), "cudaSetDevice");
+  std::vector<int> seen;
+  long long total = 0;
+  for (int i = 0; i < n; ++i) {
+    if ((s = check_slot(c, slots[i]))) return s;
+    const int ks = kv_starts ? kv_starts[i] : 0;
+    if (lens[i] <= 0 || ks < 0) return fail(c, QASR_ERR_INVALID_ARG, "segment %d: bad length/start", i);
+    if (ks + lens[i] > c->opts.max_seq)
+      return fail(c, QASR_ERR_CAPACITY, "prefill needs %d positions, max_seq is %d", ks + lens[i],
+                  c->opts.max_seq);
+    if (ks + lens[i] > c->rope_positions)
+      return fail(c, QASR_ERR_CAPACITY, "prefill beyond the rope tables");
+    if ((s = grow_slot(c, slots[i], ks + lens[i]))) return s;
+    seen.push_back(slots[i]);
+    total += lens[i];
+  }
+  std::sort(seen.begin(), seen.end());
+  if (std::adjacent_find(seen.begin(), seen.end()) != seen.end())
+    return fail(c, QASR_ERR_INVALID_ARG, "a slot is listed twice");
+  const int hs = c->cfg.hidden_size;
+  const int chunk = c->rows_max;
+  std::vector<int> rs, rp;
+  std::vector<int> seg_end;  // global row index of each segment's last row
+  rs.reserve(total);
+  rp.reserve(total);
+  for (int i = 0; i < n; ++i) {
+    const int ks = kv_starts ? kv_starts[i] : 0;
+    for (int j = 0; j < lens[i]; ++j) {
+      rs.push_back(slots[i]);
+      rp.push_back(ks + j);
+    }
+    seg_end.push_back(static_cast<int>(rs.size()) - 1);
+  }
+  int next_seg = 0;
+  for (long long r0 = 0; r0 < total; r0 += chunk) {
+    const int rows = static_cast<int>(std::min<long long>(chunk, total - r0));
+    CK(cudaMemcpyAsync(c->h, hidden + static_cast<size_t>(r0) * hs, static_cast<size_t>(rows) * hs * 2,
+                       cudaMemcpyHostToDevice, c->stream),
+       "hidden upload");
+    CK(cudaMemcpyAsync(c->prow_slot, rs.data() + r0, rows * sizeof(int), cudaMemcpyHostToDevice, c->stream),
+       "row upload");
+    CK(cudaMemcpyAsync(c->prow_pos, rp.data() + r0, rows * sizeof(int), cudaMemcpyHostToDevice, c->stream),
+       "row upload");
+    uint64_t nk = 0;
+    if ((s = enqueue_layers(c, rows, c->prow_slot, c->prow_pos, &nk))) return s;
+    std::vector<int> fsrc, fslot, fpos;
+    const int seg0 = next_seg;
+    while (next_seg < n && seg_end[next_seg] < r0 + rows) {
+      fsrc.push_back(static_cast<int>(seg_end[next_seg] - r0));
+      fslot.push_back(slots[next_seg]);
+      fpos.push_back(rp[seg_end[next_seg]]);
+      ++next_seg;
+    }
+    if (!fsrc.empty()) {
+      const int nf = static_cast<int>(fsrc.size());
+      CK(cudaMemcpyAsync(c->fin_src, fsrc.data(), nf * sizeof(int), cudaMemcpyHostToDevice, c->stream), "fin upload");
+      CK(cudaMemcpyAsync(c->fin_slot, fslot.data(), nf * sizeof(int), cudaMemcpyHostToDevice, c->stream), "fin upload");
+      CK(cudaMemcpyAsync(c->fin_pos, fpos.data(), nf * sizeof(int), cudaMemcpyHostToDevice, c->stream), "fin upload");
+      if ((s = enqueue_head(c, nf, c->fin_src, c->fin_slot, c->fin_pos, c->out_tok + seg0, &nk))) return s;
+    }
+    // the next chunk overwrites the row buffers: finish this one first
+    CK(cudaStreamSynchronize(c->stream), "prefill chunk sync");
+  }
+  CK(cudaMemcpyAsync(c->pinned_tok, c->out_tok, n * sizeof(int), cudaMemcpyDeviceToHost, c->stream),
+     "token readback");
+  if ((s = check_device_status(c))) return s;
+  std::memcpy(first_tokens, c->pinned_tok, n * sizeof(int));
+  for (int i = 0; i < n; ++i) c->slots[slots[i]].pos = (kv_starts ? kv_starts[i] : 0) + lens[i];
+  c->last_logit_rows = n;
+  return QASR_OK;
+}
+
+qasr_status qasr_prefill(qasr_ctx* c, int slot, const uint16_t* hidden, int s, int kv_start,
+                         int32_t* token) {
+  return qasr_prefill_batch(c, &slot, 1, hidden, &s, &kv_start, token);
+}
+
+qasr_status qasr_read_logits(qasr_ctx* c, float* out, int rows) {
+  if (!c || !out) return QASR_ERR_INVALID_ARG;
+  if (!(c->opts.flags & QASR_FLAG_KEEP_LOGITS) || !c->logits)
+    return fail(c, QASR_ERR_STATE, "context created without QASR_FLAG_KEEP_LOGITS");
+  if (rows <= 0 || rows > c->last_logit_rows)
+    return fail(c, QASR_ERR_INVALID_ARG, "asked for %d logit rows, last call produced %d", rows,
+                c->last_logit_rows);
+  CK(cudaSetDevice(c->device), "cudaSetDevice");
+  CK(cudaMemcpyAsync(out, c->logits, static_cast<size_t>(rows) * c->cfg.vocab_size * sizeof(float),
+                     cudaMemcpyDeviceToHost, c->stream),
+     "logits readback");
+  return check_device_status(c);
+}
+
+// ============================================================================ probes
+static qasr_status probe_err(char* err, int errlen, qasr_status s, const std::string& m) {
+  if (err && errlen > 0) {
+    std::snprintf(err, errlen, "%s", m.c_str());
+  }
+  return s;
+}
+
+qasr_status qasr_kernel_gemm(int device, void* stream, int weight_format, const void* w,
+                             const uint16_t* scale, int n_out, int k, const uint16_t* x, int ldx,
+                             int rows, uint16_t* out, int ldo, int accumulate, char* err, int errlen) {
+  static std::mutex mu;
+  static ProbeWs pws[16];
+  std::lock_guard<std::mutex> lock(mu);
+  std::string e;
+  if (device < 0 || device >= 16 || !w || !x || !out || rows <= 0 || n_out % 128 || k % 128 ||
+      (weight_format == QASR_WEIGHTS_INT8 && !scale))
+    return probe_err(err, errlen, QASR_ERR_INVALID_ARG, "bad gemm probe arguments");
+  if (cudaSetDevice(device) != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, "cudaSetDevice");
+  if (init_kernel_attrs(&e) != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, e);
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  const bool i8 = weight_format == QASR_WEIGHTS_INT8;
+  const GemmShape s = gemm_shape(n_out, k, i8, rows, sms);
+  ProbeWs& P = pws[device];
+  if (s.ws_floats > P.ws_floats) {
+    if (P.ws) cudaFree(P.ws);
+    P.ws = nullptr;
+    if (cudaMalloc(&P.ws, s.ws_floats * sizeof(float)) != cudaSuccess)
+      return probe_err(err, errlen, QASR_ERR_OOM, "workspace");
+    P.ws_floats = s.ws_floats;
+  }
+  if (static_cast<size_t>(s.tiles) > P.cnt_n) {
+    if (P.cnt) cudaFree(P.cnt);
+    P.cnt = nullptr;
+    if (cudaMalloc(&P.cnt, s.tiles * sizeof(int)) != cudaSuccess ||
+        cudaMemset(P.cnt, 0, s.tiles * sizeof(int)) != cudaSuccess)
+      return probe_err(err, errlen, QASR_ERR_OOM, "counters");
+    P.cnt_n = s.tiles;
+  }
+  CUtensorMap tmw;
+  GemmLaunch L;
+  if (!make_tmap(&tmw, w, i8, k, n_out, static_cast<uint64_t>(k) * (i8 ? 1 : 2), i8 ? 128 : 64, 128, &e) ||
+      !make_tmap(&L.tmx, x, false, k, rows, static_cast<uint64_t>(ldx) * 2, 64, s.n_tile, &e))
+    return probe_err(err, errlen, QASR_ERR_DEVICE, e);
+  L.tmw = &tmw;
+  L.int8 = i8;
+  L.epi = accumulate ? EPI_RESID : EPI_STORE;
+  L.grid = s.grid;
+  L.smem = s.smem;
+  GemmArgs& a = L.args;
+  a.n_out = n_out;
+  a.k = k;
+  a.rows = rows;
+  a.n_tile = s.n_tile;
+  a.n_tiles = s.n_tiles;
+  a.kblocks = s.kblocks;
+  a.units = s.units;
+  a.grid = s.grid;
+  a.stages = s.stages;
+  a.max_seg = s.max_seg;
+  a.scale = reinterpret_cast<const __half*>(scale);
+  a.epi = L.epi;
+  a.out = reinterpret_cast<__half*>(out);
+  a.ldo = ldo;
+  a.ws = P.ws;
+  a.counters = P.cnt;
+  const cudaError_t ce = launch_gemm(L, static_cast<cudaStream_t>(stream));
+  if (ce != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, cudaGetErrorString(ce));
+  return QASR_OK;
+}
+
+qasr_status qasr_kernel_attention(int device, void* stream, const uint16_t* q, int q_ld,
+                                  uint16_t* out, const uint16_t* kv_pool, const int* page_table,
+                                  int max_pages, int layers, int nkv, int layer,
+                                  const int* row_slot, const int* row_pos, int rows, char* err,
+                                  int errlen) {
+  static std::mutex mu;
+  static ProbeWs pws[16];
+  std::lock_guard<std::mutex> lock(mu);
+  if (device < 0 || device >= 16 || !q || !out || !kv_pool || !page_table || !row_slot || !row_pos ||
+      rows <= 0 || rows > 16384 || nkv <= 0 || q_ld != 2 * nkv * 128 || layer < 0 || layer >= layers)
+    return probe_err(err, errlen, QASR_ERR_INVALID_ARG, "bad attention probe arguments");
+  if (cudaSetDevice(device) != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, "cudaSetDevice");
+  const int max_chunks = ATTN_ROW_CHUNKS;
+  ProbeWs& P = pws[device];
+  const size_t need = static_cast<size_t>(rows) * nkv * max_chunks * ATTN_PART_FLOATS;
+  if (need > P.ws_floats) {
+    if (P.ws) cudaFree(P.ws);
+    P.ws = nullptr;
+    if (cudaMalloc(&P.ws, need * sizeof(float)) != cudaSuccess)
+      return probe_err(err, errlen, QASR_ERR_OOM, "attention workspace");
+    P.ws_floats = need;
+  }
+  if (static_cast<size_t>(rows) * nkv > P.cnt_n) {
+    if (P.cnt) cudaFree(P.cnt);
+    P.cnt = nullptr;
+    if (cudaMalloc(&P.cnt, rows * nkv * sizeof(int)) != cudaSuccess ||
+        cudaMemset(P.cnt, 0, rows * nkv * sizeof(int)) != cudaSuccess)
+      return probe_err(err, errlen, QASR_ERR_OOM, "attention counters");
+    P.cnt_n = static_cast<size_t>(rows) * nkv;
+  }
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  AttnArgs a{};
+  a.q = reinterpret_cast<const __half*>(q);
+  a.q_ld = q_ld;
+  a.out = reinterpret_cast<__half*>(out);
+  a.row_slot = row_slot;
+  a.row_pos = row_pos;
+  a.kv.pool = const_cast<__half*>(reinterpret_cast<const __half*>(kv_pool));
+  a.kv.page_table = page_table;
+  a.kv.max_pages = max_pages;
+  a.kv.layers = layers;
+  a.kv.nkv = nkv;
+  a.layer = layer;
+  a.rows = rows;
+  a.scale = 1.0f / std::sqrt(128.0f);
+  a.ws = P.ws;
+  a.counters = P.cnt;
+  a.max_chunks = max_chunks;
+  attention_kernel<<<sms * 4, ATTN_THREADS, (rows + 1) * sizeof(int), static_cast<cudaStream_t>(stream)>>>(a);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  const cudaError_t ce = cudaGetLastError();
+  if (ce != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, cudaGetErrorString(ce));
+  return QASR_OK;
+}
+
+}  // extern "C"
+
+namespace qasr {
+__global__ void kv_append_kernel(const __half* __restrict__ k, const __half* __restrict__ v,
+                                 KvLayout kv, int layer, const int* __restrict__ row_slot,
+                                 const int* __restrict__ row_pos) {
+  const int r = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+  const int ld = kv.nkv * 128;
+  const size_t ko = kv_elem_offset(kv, row_slot[r], row_pos[r], layer, 0, h);
+  const size_t vo = kv_elem_offset(kv, row_slot[r], row_pos[r], layer, 1, h);
+  kv.pool[ko + d] = k[static_cast<size_t>(r) * ld + h * 128 + d];
+  kv.pool[vo + d] = v[static_cast<size_t>(r) * ld + h * 128 + d];
+}
+}  // namespace qasr
+
+extern "C" qasr_status qasr_kernel_kv_append(int device, void* stream, const uint16_t* k,
+                                             const uint16_t* v, uint16_t* kv_pool,
+                                             const int* page_table, int max_pages, int layers,
+                                             int nkv, int layer, const int* row_slot,
+                                             const int* row_pos, int rows, char* err, int errlen) {
+  if (!k || !v || !kv_pool || !page_table || !row_slot || !row_pos || rows <= 0 || nkv <= 0 ||
+      layer < 0 || layer >= layers)
+    return probe_err(err, errlen, QASR_ERR_INVALID_ARG, "bad kv append arguments");
+  if (cudaSetDevice(device) != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, "cudaSetDevice");
+  KvLayout kv{reinterpret_cast<__half*>(kv_pool), page_table, max_pages, layers, nkv};
+  kv_append_kernel<<<dim3(rows, nkv), 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const __half*>(k), reinterpret_cast<const __half*>(v), kv, layer, row_slot, row_pos);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  const cudaError_t ce = cudaGetLastError();
+  if (ce != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, cudaGetErrorString(ce));
+  return QASR_OK;
+}

@@ -1,0 +1,161 @@
+"""Decoder-level parity on the B200 against the CPU oracle (restated CpuTextDecoder).
+
+Same seeded weights and prefixes into both.  Checked per case:
+* greedy ids identical (free-running) — the reference's own gate for batching modes
+  (src/bin/batch_step_bench.rs:60-170 requires identical token streams);
+* teacher-forced logits: both sides fed the oracle's token history, max |Δlogit|
+  <= 2e-2 (f16 weights) / 5e-2 (INT8 weights), the tolerances the north star states.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+F16_TOL = 2e-2
+INT8_TOL = 5e-2
+
+
+def _setup(qasr, oracle, cfg, int8, slots, max_seq=2048, seed=1234):
+    from oracle.oracle import OracleModel
+    model = qasr.SyntheticModel(cfg, seed=seed)
+    dec = qasr.TextDecoder(cfg, weight_format=qasr.WEIGHTS_INT8 if int8 else qasr.WEIGHTS_F16,
+                           max_slots=slots, max_seq=max_seq, keep_logits=True)
+    om = OracleModel(cfg)
+    dec.load_embed(model.embed, model.final_norm)
+    om.load_embed(model.embed, model.final_norm)
+    for l in range(cfg["num_hidden_layers"]):
+        w = model.layer(l, int8=int8)
+        dec.load_layer(l, w)
+        om.load_layer(l, w)
+    cos, sin = qasr.build_rope_tables(max_seq)
+    dec.set_rope_tables(cos, sin)
+    om.set_rope_tables(cos, sin)
+    return model, dec, om
+
+
+def _run_parity(qasr, oracle, cfg, int8, n_audio, steps, n_slots=1, check_slots=None):
+    from oracle.oracle import OracleSeq
+    tol = INT8_TOL if int8 else F16_TOL
+    model, dec, om = _setup(qasr, oracle, cfg, int8, n_slots)
+    check_slots = list(range(n_slots)) if check_slots is None else check_slots
+    prefixes = [model.prefix(s, n_audio[s % len(n_audio)])[0] for s in range(n_slots)]
+    slots = [dec.fork_capped(p.shape[0] + steps + 8) for p in prefixes]
+    first = dec.prefill_batch(slots, prefixes)
+    g_logits0 = dec.read_logits(n_slots)
+    seqs = {}
+    o_tok = {}
+    worst = 0.0
+    for i in check_slots:
+        seqs[i] = OracleSeq(om, 2048)
+        tok, lg = seqs[i].prefill(prefixes[i], want_logits=True)
+        o_tok[i] = [tok]
+        worst = max(worst, float(np.max(np.abs(g_logits0[i] - lg))))
+        assert first[i] == tok, f"slot {i}: prefill argmax {first[i]} vs oracle {tok}"
+    g_tok = {i: [int(first[i])] for i in range(n_slots)}
+    for _ in range(steps):
+        # teacher forcing: both sides embed the oracle's previous token
+        feed = [o_tok[i][-1] if i in o_tok else g_tok[i][-1] for i in range(n_slots)]
+        dec.set_input_tokens(slots, feed)
+        out = dec.step_batch(slots)
+        lg_all = dec.read_logits(n_slots)
+        for i in range(n_slots):
+            g_tok[i].append(int(out[i]))
+        for i in check_slots:
+            tok, lg = seqs[i].step(want_logits=True)
+            o_tok[i].append(tok)
+            worst = max(worst, float(np.max(np.abs(lg_all[i] - lg))))
+    mismatch = {i: (g_tok[i], o_tok[i]) for i in check_slots if g_tok[i] != o_tok[i]}
+    dec.close()
+    om.close()
+    return worst, mismatch, tol
+
+
+@pytest.mark.parametrize("int8", [False, True], ids=["f16", "int8"])
+def test_two_layer_decoder_matches_oracle(qasr, cuda_device, oracle, int8):
+    cfg = qasr.text_config("0.6b", num_hidden_layers=2)
+    worst, mismatch, tol = _run_parity(qasr, oracle, cfg, int8, n_audio=[40, 7, 120], steps=12, n_slots=3)
+    assert worst <= tol, f"teacher-forced max |dlogit| {worst:.4g} > {tol}"
+    assert not mismatch, f"greedy ids differ: {mismatch}"
+
+
+def test_batched_equals_serial(qasr, cuda_device, oracle):
+    """BatchProjections::step vs one slot at a time: identical ids
+    (src/bin/batch_step_bench.rs requires serial == fused)."""
+    cfg = qasr.text_config("0.6b", num_hidden_layers=2)
+    model = qasr.SyntheticModel(cfg, seed=77)
+    cos, sin = qasr.build_rope_tables(1024)
+    streams = []
+    for batched in (False, True):
+        dec = qasr.TextDecoder(cfg, max_slots=4, max_seq=1024)
+        dec.load_model(model)
+        dec.set_rope_tables(cos, sin)
+        pre = [model.prefix(s, 30 + 11 * s)[0] for s in range(4)]
+        slots = [dec.fork_capped(256) for _ in range(4)]
+        toks = [list(map(int, dec.prefill_batch(slots, pre)))] if batched else \
+            [[dec.prefill(slots[i], pre[i]) for i in range(4)]]
+        for _ in range(10):
+            if batched:
+                toks.append(list(map(int, dec.step_batch(slots))))
+            else:
+                toks.append([dec.step(s) for s in slots])
+        streams.append(np.array(toks))
+        dec.close()
+    # prefill_batch concatenates segments into one GEMM (prefill_multi); decode steps
+    # of one slot must not depend on the other slots in the batch.
+    np.testing.assert_array_equal(streams[0][1:], streams[1][1:])
+
+
+def test_graph_replay_equals_eager(qasr, cuda_device):
+    cfg = qasr.text_config("0.6b", num_hidden_layers=2)
+    model = qasr.SyntheticModel(cfg, seed=5)
+    cos, sin = qasr.build_rope_tables(512)
+    runs = []
+    for graph in (True, False):
+        dec = qasr.TextDecoder(cfg, max_slots=2, max_seq=512, use_graph=graph)
+        dec.load_model(model)
+        dec.set_rope_tables(cos, sin)
+        slots = [dec.fork_capped(128), dec.fork_capped(128)]
+        dec.prefill_batch(slots, [model.prefix(0, 20)[0], model.prefix(1, 33)[0]])
+        runs.append([list(dec.step_batch(slots)) for _ in range(8)])
+        dec.close()
+    assert runs[0] == runs[1]
+
+
+def test_errors_are_status_codes(qasr, cuda_device):
+    cfg = qasr.text_config("0.6b", num_hidden_layers=1)
+    dec = qasr.TextDecoder(cfg, max_slots=1, max_seq=128)
+    with pytest.raises(qasr.DecoderError) as e:
+        dec.step_batch([0])
+    assert e.value.status in (1, 7)
+    model = qasr.SyntheticModel(cfg)
+    dec.load_model(model)
+    cos, sin = qasr.build_rope_tables(128)
+    dec.set_rope_tables(cos, sin)
+    s = dec.fork_capped(64)
+    with pytest.raises(qasr.DecoderError) as e:
+        dec.prefill(s, model.prefix(0, 200)[0])  # 224 rows > max_seq 128
+    assert e.value.status == 3
+    with pytest.raises(qasr.DecoderError):
+        dec.fork_capped(64)  # only one slot
+    with pytest.raises(qasr.DecoderError):
+        dec.set_input_token(s, 151936)  # outside the vocabulary
+    dec.close()
+
+
+@pytest.mark.slow
+def test_config1_shape_matches_oracle(qasr, cuda_device, oracle):
+    """Config 1 shape: 0.6B f16, 28 layers, prefix 9 + 200 audio + 15 ids, greedy decode."""
+    cfg = qasr.text_config("0.6b")
+    worst, mismatch, tol = _run_parity(qasr, oracle, cfg, False, n_audio=[200], steps=32)
+    assert worst <= tol, f"teacher-forced max |dlogit| {worst:.4g} > {tol}"
+    assert not mismatch, f"greedy ids differ: {mismatch}"
+
+
+@pytest.mark.slow
+def test_config2_shape_matches_oracle(qasr, cuda_device, oracle):
+    """Config 2 shape: 0.6B INT8, 16 slots; two slots checked against the oracle."""
+    cfg = qasr.text_config("0.6b")
+    worst, mismatch, tol = _run_parity(qasr, oracle, cfg, True, n_audio=[390, 250], steps=12,
+                                       n_slots=16, check_slots=[0, 9])
+    assert worst <= tol, f"teacher-forced max |dlogit| {worst:.4g} > {tol}"
+    assert not mismatch, f"greedy ids differ: {mismatch}"
