@@ -1,0 +1,388 @@
+"""Decode throughput of the B200 Qwen3-ASR text-decoder step (BASELINE.json metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...   (one process per GPU)
+
+Workload (per GPU): Qwen3-ASR-1.7B text decoder, INT8 weights
+(per-row symmetric, f16 scales, seeded N(0, 0.02)), 32 decode slots, KV lengths drawn
+uniform in [100, 1500]; a slot that reaches 1500 positions is refilled with a fresh
+seeded prefix (prefill time is excluded from the decode metric and reported apart).
+Slots shard across GPUs: every rank holds a weight replica and its own 32 slots, no
+collective on the hot path ("scaling": "weak").
+
+A step = one decode position for all 32 slots of the rank (BatchProjections::step).
+The weights (2.03 GB) and the KV cache (~3 GB) exceed the 126 MB L2 by far, so no L2
+flush is needed between steps.  Times are CUDA events on the context's stream; the
+whole-job value uses the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+SLOTS_PER_GPU = 32
+LEN_LO, LEN_HI = 100, 1500
+MAX_SEQ = 1536
+SEED = 20260101
+PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
+FALLBACK_HBM_GBS = 6650.0
+METRIC = "decode tokens/sec (box) 1.7B INT8 @1/2/4/8 B200; % HBM roofline"
+
+
+def load_pkg():
+    sys.path.insert(0, str(ROOT / "tests"))
+    from conftest import load_package  # the package dir name has dashes
+    return load_package()
+
+
+def peaks():
+    if PEAKS_FILE.exists():
+        p = json.loads(PEAKS_FILE.read_text())
+        return float(p["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def algorithmic_bytes(cfg, kv_lens_before):
+    """HBM bytes one decode step must move: every weight byte once (int8 linears +
+    f16 scales + f16 tied lm_head + f32 norms) + each slot's K/V rows (all layers) +
+    the appended row."""
+    hs, I, L, V = cfg["hidden_size"], cfg["intermediate_size"], cfg["num_hidden_layers"], cfg["vocab_size"]
+    qd = cfg["num_attention_heads"] * cfg["head_dim"]
+    kvd = cfg["num_key_value_heads"] * cfg["head_dim"]
+    lin = (qd + 2 * kvd) * hs + hs * qd + 2 * I * hs + hs * I
+    rows = (qd + 2 * kvd) + hs + 2 * I + hs
+    weights = L * (lin + 2 * rows) + V * hs * 2 + L * (2 * hs + 2 * cfg["head_dim"]) * 4 + hs * 4
+    kv_row = L * 2 * kvd * 2  # bytes of one position, all layers, K and V
+    kv = sum(int(n) for n in kv_lens_before) * kv_row + len(kv_lens_before) * kv_row
+    return weights, kv
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled while the timed region runs."""
+
+    def __init__(self, gpu_index: int):
+        self.path = tempfile.mktemp(suffix=".csv")
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={gpu_index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 9:
+                rows.append(f)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for n, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def cpu_baseline(cfg, sample_tokens=12, prefix_rows=16):
+    """The reference's CPU decoder (restated in oracle/) on this host's cores: one slot,
+    `prefix_rows` prefill, then `sample_tokens` timed decode steps (tokens/s)."""
+    from oracle.oracle import OracleModel, OracleSeq
+    pkg = load_pkg()
+    model = pkg.SyntheticModel(cfg, seed=SEED)
+    om = OracleModel(cfg)
+    om.load_model(model, int8=True)
+    cos, sin = pkg.build_rope_tables(MAX_SEQ)
+    om.set_rope_tables(cos, sin)
+    seq = OracleSeq(om, MAX_SEQ)
+    hidden, _ = model.prefix(0, 0, n_text=prefix_rows, n_before=9)
+    seq.prefill(hidden)
+    seq.step()  # warm-up
+    t0 = time.perf_counter()
+    for _ in range(sample_tokens):
+        seq.step()
+    dt = time.perf_counter() - t0
+    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    seq.close()
+    om.close()
+    return {"value": sample_tokens / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"1 slot, {prefix_rows}-row prefix, {sample_tokens} timed greedy steps after 1 "
+                      f"warm-up (1.7B INT8 weights dequantised to f32 as the reference CPU decoder keeps "
+                      f"them); attention is <3% of a CPU step at these lengths"}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference CPU decoder path (restated, oracle/) on all host cores."""
+    if rank != 0:
+        return
+    pkg = load_pkg()
+    cfg = pkg.text_config("1.7b")
+    sample = max(3, min(args.steps, 12))
+    cb = cpu_baseline(cfg, sample_tokens=sample)
+    line = {"metric": METRIC, "impl": "reference", "value": cb["value"], "unit": "tokens/s",
+            "n_gpus": world, "steps": sample, "warmup": 1, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32 (int8 weights dequantised to f16)",
+            "data": "synthetic", "config": {"workload": "cfg4: Qwen3-ASR-1.7B INT8 decode, 1 slot on CPU",
+                                            "model": "qwen3-asr-1.7b-text-decoder"},
+            "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def time_kernels(pkg, torch, dec, cfg, slots, stream, kv_lens):
+    """CUDA-event timing of the two dominant kernels at the bench's shapes, through the
+    probe entry points: paged attention over the slots' current KV and the INT8
+    gate|up GEMM (the largest weight stream)."""
+    from qasr_b200 import synth
+    res = {}
+    hs, I = cfg["hidden_size"], cfg["intermediate_size"]
+    # ---- gate|up GEMM, 32 rows, int8 [2I, hs]
+    w = torch.randint(-127, 128, (2 * I, hs), dtype=torch.int8, device="cuda")
+    s = torch.full((2 * I,), 0.001, dtype=torch.float16, device="cuda")
+    x = torch.randn((len(slots), hs), dtype=torch.float16, device="cuda")
+    o = torch.empty((len(slots), 2 * I), dtype=torch.float16, device="cuda")
+    def gemm():
+        pkg.kernel_gemm(0, stream.cuda_stream, pkg.WEIGHTS_INT8, w.data_ptr(), s.data_ptr(), 2 * I, hs,
+                        x.data_ptr(), hs, len(slots), o.data_ptr(), 2 * I)
+    # ---- attention: one layer of the 1.7B shape over the slots' lengths
+    nkv = cfg["num_key_value_heads"]
+    lens = [int(n) for n in kv_lens]
+    max_pages = max((n + 63) // 64 for n in lens)
+    pool = torch.randn((len(lens) * max_pages, 1, 2, nkv, 64, 128), dtype=torch.float16, device="cuda")
+    pt = torch.arange(len(lens) * max_pages, dtype=torch.int32, device="cuda").view(len(lens), max_pages)
+    q = torch.randn((len(lens), 2 * nkv * 128), dtype=torch.float16, device="cuda")
+    ao = torch.empty_like(q)
+    rs = torch.arange(len(lens), dtype=torch.int32, device="cuda")
+    rp = torch.tensor([n - 1 for n in lens], dtype=torch.int32, device="cuda")
+    def attn():
+        pkg.kernel_attention(0, stream.cuda_stream, q.data_ptr(), 2 * nkv * 128, ao.data_ptr(), pool.data_ptr(),
+                             pt.data_ptr(), max_pages, 1, nkv, 0, rs.data_ptr(), rp.data_ptr(), len(lens))
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+    for name, fn, nbytes in (("gemm_gate_up_int8", gemm, 2 * I * hs + 2 * I * 2 + len(slots) * hs * 2 * 3),
+                             ("attention_decode", attn, sum(lens) * nkv * 512 + len(lens) * 4096 * 2)):
+        times = []
+        with torch.cuda.stream(stream):
+            for it in range(13):
+                flush.zero_()  # evict the operands from L2 between launches
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                fn()
+                b.record(stream)
+                b.synchronize()
+                if it >= 3:
+                    times.append(a.elapsed_time(b) * 1e-3)
+        t = statistics.median(times)
+        res[name] = {"seconds": t, "bytes": nbytes, "gbs": nbytes / t / 1e9}
+    del w, pool, flush
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=768)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=128)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+
+    pkg = load_pkg()
+    cfg = pkg.text_config("1.7b")
+    model = pkg.SyntheticModel(cfg, seed=SEED)
+    rng = np.random.default_rng(SEED + 7919 * rank)
+    dec = pkg.TextDecoder(cfg, weight_format=pkg.WEIGHTS_INT8, max_slots=SLOTS_PER_GPU, max_seq=MAX_SEQ,
+                          device=local)
+    t_load = time.perf_counter()
+    dec.load_model(model)
+    cos, sin = pkg.build_rope_tables(MAX_SEQ)
+    dec.set_rope_tables(cos, sin)
+    t_load = time.perf_counter() - t_load
+    stream = torch.cuda.Stream()
+    dec.set_stream(stream.cuda_stream)
+
+    refill_count = [0] * SLOTS_PER_GPU
+
+    def make_prefix(s, length):
+        stream_id = (rank * SLOTS_PER_GPU + s) * 65536 + refill_count[s]
+        refill_count[s] += 1
+        n_text = min(24, length)
+        hidden, _ = model.prefix(stream_id, length - n_text, n_text=n_text, n_before=min(9, n_text))
+        return hidden
+
+    slots = [dec.fork_capped(MAX_SEQ) for _ in range(SLOTS_PER_GPU)]
+    lens0 = rng.integers(LEN_LO, LEN_HI + 1, size=SLOTS_PER_GPU)
+    t_pf = time.perf_counter()
+    dec.prefill_batch(slots, [make_prefix(s, int(n)) for s, n in enumerate(lens0)])
+    t_pf = time.perf_counter() - t_pf
+    kv_len = [int(n) for n in lens0]
+    prefill_time = [0.0]
+
+    def refill_if_full():
+        full = [i for i in range(SLOTS_PER_GPU) if kv_len[i] >= LEN_HI]
+        if not full:
+            return
+        new = [int(rng.integers(LEN_LO, LEN_HI)) for _ in full]
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        dec.prefill_batch([slots[i] for i in full], [make_prefix(i, n) for i, n in zip(full, new)])
+        b.record(stream)
+        b.synchronize()
+        prefill_time[0] += a.elapsed_time(b) * 1e-3
+        for i, n in zip(full, new):
+            kv_len[i] = n
+
+    # ---- warm-up (graph capture happens on the first step)
+    for _ in range(args.warmup):
+        refill_if_full()
+        dec.step_batch(slots, read_tokens=False)
+        for i in range(SLOTS_PER_GPU):
+            kv_len[i] += 1
+    dec.synchronize()
+
+    # ---- timed region: exactly K steps; refills (prefill) are timed apart and excluded
+    bytes_w, _ = algorithmic_bytes(cfg, [])
+    kv_bytes = 0
+    step_events = []
+    prefill_time[0] = 0.0
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    launches0 = pkg.launch_count()
+    t_wall = time.perf_counter()
+    for _ in range(args.steps):
+        refill_if_full()
+        _, kvb = algorithmic_bytes(cfg, kv_len)
+        kv_bytes += kvb
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push("decode_step")
+        a.record(stream)
+        dec.step_batch(slots, read_tokens=False)
+        b.record(stream)
+        torch.cuda.nvtx.range_pop()
+        step_events.append((a, b))
+        for i in range(SLOTS_PER_GPU):
+            kv_len[i] += 1
+    torch.cuda.synchronize()
+    t_wall = time.perf_counter() - t_wall
+    launches = pkg.launch_count() - launches0
+    clk = clocks.stop()
+    if dist is not None:
+        dist.barrier()
+    decode_s = sum(a.elapsed_time(b) for a, b in step_events) * 1e-3
+    dec.synchronize()
+
+    # ---- end to end through the C ABI with host buffers: H2D input tokens, D2H argmax
+    e2e_steps = min(args.e2e_steps, args.steps)
+    host_tokens = np.zeros(SLOTS_PER_GPU, np.int32)
+    e2e_pf0 = prefill_time[0]
+    torch.cuda.synchronize()
+    t_e2e = time.perf_counter()
+    for _ in range(e2e_steps):
+        refill_if_full()
+        dec.set_input_tokens(slots, host_tokens)
+        host_tokens = dec.step_batch(slots, read_tokens=True)
+        for i in range(SLOTS_PER_GPU):
+            kv_len[i] += 1
+    t_e2e = time.perf_counter() - t_e2e - (prefill_time[0] - e2e_pf0)
+
+    # ---- dominant kernels, timed alone at the bench shapes
+    kernels = time_kernels(pkg, torch, dec, cfg, slots, stream, kv_len)
+
+    local_vals = torch.tensor([decode_s, t_e2e, prefill_time[0]], dtype=torch.float64, device="cuda")
+    if dist is not None:
+        dist.all_reduce(local_vals, op=dist.ReduceOp.MAX)
+    decode_max, e2e_max, _ = local_vals.tolist()
+
+    if rank == 0:
+        hbm, peak_kind = peaks()
+        tokens = args.steps * SLOTS_PER_GPU * world
+        value = tokens / decode_max
+        ms_step = decode_max / args.steps * 1e3
+        step_bytes = bytes_w + kv_bytes / args.steps
+        step_gbs = step_bytes / (decode_max / args.steps) / 1e9
+        dom_name = max(kernels, key=lambda k: kernels[k]["seconds"])
+        dom = kernels[dom_name]
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8 weights x f16 activations, f32 accumulate", "data": "synthetic",
+            "config": {"workload": "cfg4: Qwen3-ASR-1.7B text decoder, INT8 per-row weights, 32 slots/GPU, "
+                                   "KV U(100,1500), refill at 1500",
+                       "model": "qwen3-asr-1.7b-text-decoder (random init N(0,0.02), norm gains 1)",
+                       "global_batch": SLOTS_PER_GPU * world, "seq_len": f"{LEN_LO}-{LEN_HI}",
+                       "parallelism": f"slot-replica dp{world}",
+                       "l2": "operands (2.0 GB weights + ~3 GB KV per step) far exceed the 126 MB L2"},
+            "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": dom["gbs"], "peak": hbm,
+                         "unit": "GB/s", "frac": dom["gbs"] / hbm, "traffic": None,
+                         "peak_kind": peak_kind, "kernels": kernels},
+            "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_gbs, "frac": step_gbs / hbm,
+                              "weights_bytes": bytes_w, "kv_bytes_per_step": kv_bytes / args.steps},
+            "e2e": {"value": e2e_steps * SLOTS_PER_GPU * world / e2e_max, "unit": "tokens/s",
+                    "h2d_bytes_per_step": SLOTS_PER_GPU * 8, "d2h_bytes_per_step": SLOTS_PER_GPU * 4,
+                    "steps": e2e_steps},
+            "gpu_launches": launches,
+            "clocks": clk,
+            "prefill": {"initial_rows": int(sum(lens0)), "initial_seconds": t_pf,
+                        "refill_seconds_in_timed_region": prefill_time[0]},
+            "wall_seconds_timed_region": t_wall,
+            "load_seconds": t_load,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            try:
+                line["cpu_baseline"] = cpu_baseline(cfg)
+            except Exception as e:  # keep the GPU line even if the host is too small
+                line["cpu_baseline"] = {"value": None, "error": str(e)}
+        print(json.dumps(line), flush=True)
+    dec.close()
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -157,9 +157,11 @@ def test_kv_append_then_attention(qasr, cuda_device):
     k = synth.normal_f16((rows, nkv * 128), 1, 1, 0.0, 1.0)
     v = synth.normal_f16((rows, nkv * 128), 1, 2, 0.0, 1.0)
     pos = np.array([0, 63, 64, 100], np.int32)
-    qasr.kernel_kv_append(0, 0, _dev(k, torch).data_ptr(), _dev(v, torch).data_ptr(), pool.data_ptr(),
-                          pt.data_ptr(), 2, layers, nkv, 0, _dev(np.arange(rows, dtype=np.int32), torch).data_ptr(),
-                          _dev(pos, torch).data_ptr(), rows)
+    # keep every device tensor referenced until the kernel has run
+    dk, dv = _dev(k, torch), _dev(v, torch)
+    drs, drp = _dev(np.arange(rows, dtype=np.int32), torch), _dev(pos, torch)
+    qasr.kernel_kv_append(0, 0, dk.data_ptr(), dv.data_ptr(), pool.data_ptr(), pt.data_ptr(), 2, layers, nkv,
+                          0, drs.data_ptr(), drp.data_ptr(), rows)
     torch.cuda.synchronize()
     P = pool.cpu().numpy().view(np.uint16)
     table = [[3, 5], [0, 7], [1, 2], [4, 6]]
