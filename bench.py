@@ -169,6 +169,9 @@ def time_kernels(pkg, torch, dec, cfg, slots, stream, kv_lens):
     s = torch.full((2 * I,), 0.001, dtype=torch.float16, device="cuda")
     x = torch.randn((len(slots), hs), dtype=torch.float16, device="cuda")
     o = torch.empty((len(slots), 2 * I), dtype=torch.float16, device="cuda")
+    wt = torch.empty_like(w)
+    pkg.kernel_pack_weights(0, stream.cuda_stream, pkg.WEIGHTS_INT8, w.data_ptr(), 2 * I, hs, wt.data_ptr())
+    w = wt
     def gemm():
         pkg.kernel_gemm(0, stream.cuda_stream, pkg.WEIGHTS_INT8, w.data_ptr(), s.data_ptr(), 2 * I, hs,
                         x.data_ptr(), hs, len(slots), o.data_ptr(), 2 * I)

@@ -20,10 +20,20 @@
 extern "C" {
 #endif
 
+/* Re-lay a row-major weight [n_out, k] (f16 or int8) into the tiled HBM layout the
+ * GEMM streams: 16 KB blocks of 128 rows x 128 bytes, one per (row tile, k block),
+ * 128-byte swizzle applied.  w_tiled must hold n_out * k * element-size bytes.
+ * (The reference uploads the file bytes verbatim, src/weights.rs:300-308; the B200
+ * loader re-lays them once at load.) */
+qasr_status qasr_kernel_pack_weights(int device, void* stream, int weight_format,
+                                     const void* w_rowmajor, int n_out, int k, void* w_tiled,
+                                     char* err, int errlen);
+
 /* out[r, m] = f16(sum_k W[m, k] x[r, k])            (accumulate == 0)
  * out[r, m] = f16(f32(out[r, m]) + sum_k ...)         (accumulate != 0)
  * W: [n_out, k] f16 (weight_format QASR_WEIGHTS_F16) or int8 + f16 per-row scale
- * (QASR_WEIGHTS_INT8, value f16(f32(q) * s)).  n_out % 128 == 0; k % 128 == 0.
+ * (QASR_WEIGHTS_INT8, value f16(f32(q) * s)), in the layout qasr_kernel_pack_weights
+ * produces.  n_out % 128 == 0; k % 128 == 0.
  * Replaces gemv / gemv_w8 / gemv_batch_slots / prefill_gemm(_w8)
  * (src/shaders.rs:273-889, 2995-3082). */
 qasr_status qasr_kernel_gemm(int device, void* stream, int weight_format, const void* w,

@@ -44,7 +44,7 @@ EXPORTED_SYMBOLS = (
     "qasr_slot_pos", "qasr_set_slot_pos", "qasr_set_input_token", "qasr_set_input_tokens",
     "qasr_prefill", "qasr_step", "qasr_prefill_batch", "qasr_step_batch", "qasr_read_logits",
     "qasr_build_rope_tables", "qasr_build_dim_map", "qasr_dequant_i8",
-    "qasr_kernel_gemm", "qasr_kernel_attention", "qasr_kernel_kv_append",
+    "qasr_kernel_pack_weights", "qasr_kernel_gemm", "qasr_kernel_attention", "qasr_kernel_kv_append",
     "qasr_kernel_launch_count",
     "qasr_synth_key", "qasr_synth_normal_f16", "qasr_synth_uniform_ids",
     "qasr_synth_quantize_rows", "qasr_f32_to_f16", "qasr_f16_to_f32", "qasr_f32_to_f16_array",
@@ -112,6 +112,7 @@ def _load() -> ctypes.CDLL:
     lib.qasr_build_rope_tables.argtypes = [P, P, I, I, ctypes.c_double, P, I, I]
     lib.qasr_build_dim_map.argtypes = [P, I, I, I, P]
     lib.qasr_dequant_i8.argtypes = [P, P, I, I, P]
+    lib.qasr_kernel_pack_weights.argtypes = [I, P, I, P, I, I, P, ctypes.c_char_p, I]
     lib.qasr_kernel_gemm.argtypes = [I, P, I, P, P, I, I, P, I, I, P, I, I, ctypes.c_char_p, I]
     lib.qasr_kernel_attention.argtypes = [I, P, P, I, P, P, P, I, I, I, I, P, P, I, ctypes.c_char_p, I]
     lib.qasr_kernel_kv_append.argtypes = [I, P, P, P, P, P, I, I, I, I, P, P, I, ctypes.c_char_p, I]
@@ -307,6 +308,17 @@ class TextDecoder:
         return out
 
 
+def kernel_pack_weights(device: int, stream: int, weight_format: int, w_rowmajor_ptr: int, n_out: int,
+                        k: int, w_tiled_ptr: int):
+    """Row-major [n_out, k] weight -> the tiled layout kernel_gemm streams."""
+    err = ctypes.create_string_buffer(512)
+    st = lib.qasr_kernel_pack_weights(device, ctypes.c_void_p(stream), weight_format,
+                                      ctypes.c_void_p(w_rowmajor_ptr), n_out, k, ctypes.c_void_p(w_tiled_ptr),
+                                      err, 512)
+    if st != QASR_OK:
+        raise DecoderError(st, err.value.decode())
+
+
 def kernel_gemm(device: int, stream: int, weight_format: int, w_ptr: int, scale_ptr: int | None,
                 n_out: int, k: int, x_ptr: int, ldx: int, rows: int, out_ptr: int, ldo: int,
                 accumulate: bool = False):
@@ -348,7 +360,7 @@ def version() -> str:
 
 __all__ = [
     "TextDecoder", "DecoderError", "SyntheticModel", "MODEL_PRESETS", "text_config",
-    "build_rope_tables", "dim_map", "kernel_gemm", "kernel_attention", "kernel_kv_append",
+    "build_rope_tables", "dim_map", "kernel_pack_weights", "kernel_gemm", "kernel_attention", "kernel_kv_append",
     "launch_count", "version", "WEIGHTS_F16", "WEIGHTS_INT8", "EXPORTED_SYMBOLS", "lib",
     "f16_bits_to_f32", "f32_to_f16_bits", "PAGE_POSITIONS",
 ]

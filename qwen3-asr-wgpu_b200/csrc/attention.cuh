@@ -73,6 +73,8 @@ __global__ void __launch_bounds__(ATTN_THREADS)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nkv = a.kv.nkv;
+  griddep_wait();
+  griddep_launch_dependents();
 
   // ---- unit decomposition (identical in every CTA) ----
   if (tid == 0) {

@@ -38,7 +38,7 @@ enum EpiKind : int {
 
 constexpr int GEMM_THREADS = 384;
 constexpr int GEMM_MAX_STAGES = 8;
-constexpr int GEMM_A_STAGES = 4;
+constexpr int GEMM_A_STAGES = 8;  // upper bound; the kernel fits what TMEM allows
 constexpr int GEMM_MAX_NTILE = 128;
 constexpr uint32_t GEMM_TMEM_COLS = 512;
 
@@ -60,7 +60,8 @@ __device__ __forceinline__ size_t kv_elem_offset(const KvLayout& kv, int slot, i
 
 struct GemmArgs {
   int n_out, k, rows, n_tile, n_tiles, kblocks, units, grid, stages, max_seg;
-  const __half* scale;  // int8: f16 per-row scale
+  const uint8_t* w_tiles;  // weights in the tiled layout (weight_tile_offset)
+  const __half* scale;     // int8: f16 per-row scale
   // epilogue
   int epi;
   __half* out;
@@ -224,20 +225,52 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, EpiSmem& es, i
   }
 }
 
+// ------------------------------------------------------------------ weight tiles
+// HBM layout of a weight matrix [n_out, K] (1-byte int8 or 2-byte f16): unit (mt, kb) =
+// rows [128 mt, +128) x bytes [128 kb, +128) of each row, stored as one contiguous
+// 16 KB block at ((mt * KB + kb) * 16384), row r at r * 128, and 16-byte chunk c of the
+// row at chunk position c ^ (r & 7) — the 128-byte swizzle the shared-memory tile uses,
+// so one cp.async.bulk lands it ready for the A builders (no strided 128-row gather).
+__device__ __forceinline__ size_t weight_tile_offset(int row, int chunk16, int kb_per_row) {
+  const int mt = row >> 7, r = row & 127;
+  const int kb = chunk16 >> 3, c = chunk16 & 7;
+  return (static_cast<size_t>(mt) * kb_per_row + kb) * 16384 + static_cast<size_t>(r) * 128 +
+         static_cast<size_t>((c ^ (r & 7)) << 4);
+}
+
+__global__ void pack_weight_tiles_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst,
+                                         int n_out, int row_bytes) {
+  const int chunks = row_bytes >> 4;
+  const long long total = static_cast<long long>(n_out) * chunks;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int row = static_cast<int>(i / chunks), ch = static_cast<int>(i % chunks);
+    dst[weight_tile_offset(row, ch, row_bytes >> 7) >> 4] = src[i];
+  }
+}
+
+// ------------------------------------------------------------------ PDL
+// Programmatic dependent launch: a kernel may start while its predecessor drains; it
+// must execute griddep_wait() before touching anything the predecessor produces or
+// consumes.  Weights, scales and tables are constant during a step and may be read
+// before it.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ------------------------------------------------------------------ kernel
 template <bool INT8, int EPI>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
-                   const __grid_constant__ GemmArgs a) {
-  constexpr int KE = INT8 ? 128 : 64;        // k elements per k-block (128 bytes of W row)
-  constexpr int ATOMS = INT8 ? 2 : 1;        // 64-element (128-byte) X atoms per k-block
-  constexpr int ACOLS = KE / 2;              // TMEM columns of one A stage (2 f16 / column)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ GemmArgs a) {
+  constexpr int KE = INT8 ? 128 : 64;        // k elements per unit (128 bytes of W row)
+  constexpr int ATOMS = INT8 ? 2 : 1;        // 64-element (128-byte) X atoms per unit
+  constexpr uint32_t ACOLS = KE / 2;         // TMEM columns of one A stage (2 f16 / column)
   constexpr int KSTEPS = KE / 16;            // UMMA K = 16 per instruction
-  constexpr uint32_t D_COLS0 = 0;            // two accumulator buffers at columns 0 and 128
-  constexpr uint32_t A_COLS0 = 256;
 
   extern __shared__ __align__(1024) uint8_t dsmem[];
-  __shared__ __align__(8) uint64_t full_bar[GEMM_MAX_STAGES], sfree_bar[GEMM_MAX_STAGES];
+  __shared__ __align__(8) uint64_t wfull_bar[GEMM_MAX_STAGES], xfull_bar[GEMM_MAX_STAGES],
+      sfree_bar[GEMM_MAX_STAGES];
   __shared__ __align__(8) uint64_t afull_bar[GEMM_A_STAGES], afree_bar[GEMM_A_STAGES];
   __shared__ __align__(8) uint64_t dfull_bar[2], dfree_bar[2], done_bar;
   __shared__ uint32_t tmem_base_sh;
@@ -250,7 +283,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const int S = a.stages;
   const uint32_t x_tile_bytes = static_cast<uint32_t>(a.n_tile) * 128u;
   const uint32_t stage_bytes = 16384u + ATOMS * x_tile_bytes;
-  const uint32_t tx_bytes = stage_bytes;
+  // TMEM: two accumulator buffers of DCOLS columns, then SA dequantised A stages
+  const uint32_t DCOLS = (static_cast<uint32_t>(a.n_tile) + 31u) & ~31u;
+  const uint32_t A_COLS0 = 2u * DCOLS;
+  int SA = static_cast<int>((GEMM_TMEM_COLS - A_COLS0) / ACOLS);
+  SA = SA > GEMM_A_STAGES ? GEMM_A_STAGES : SA;
 
   const long long U = a.units, G = a.grid;
   const long long ub = static_cast<long long>(blockIdx.x) * U / G;
@@ -259,10 +296,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
-      mbar_init(&full_bar[i], 1);
+      mbar_init(&wfull_bar[i], 1);
+      mbar_init(&xfull_bar[i], 1);
       mbar_init(&sfree_bar[i], 1);
     }
-    for (int i = 0; i < GEMM_A_STAGES; ++i) {
+    for (int i = 0; i < SA; ++i) {
       mbar_init(&afull_bar[i], 4);
       mbar_init(&afree_bar[i], 1);
     }
@@ -278,38 +316,56 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     tmem_alloc(&tmem_base_sh, GEMM_TMEM_COLS);
     tmem_relinquish();
   }
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tm_w);
-    tma_prefetch_desc(&tm_x);
-  }
+  if (warp == 0 && lane == 0) tma_prefetch_desc(&tm_x);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  griddep_launch_dependents();
   const uint32_t tmem_base = tmem_base_sh;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------ producer
     if (lane == 0) {
-      long long i = 0;
-      for (long long u = ub; u < ue; ++u, ++i) {
-        const int s = static_cast<int>(i % S);
-        const uint32_t ph = static_cast<uint32_t>((i / S) & 1);
-        if (!mbar_wait(&sfree_bar[s], ph ^ 1u, &abort_flag, a.status, 0x101)) break;
+      const long long n = ue - ub;
+      const long long pre = n < S ? n : S;
+      auto issue_w = [&](long long i) {
+        const long long u = ub + i;
         const int T = static_cast<int>(u / KB), kb = static_cast<int>(u % KB);
-        const int mt = T / a.n_tiles, nt = T % a.n_tiles;
-        uint8_t* st = smem + static_cast<size_t>(s) * stage_bytes;
-        mbar_arrive_expect_tx(&full_bar[s], tx_bytes);
-        tma_load_2d(st, &tm_w, &full_bar[s], kb * KE, mt * 128);
+        const int mt = T / a.n_tiles;
+        uint8_t* st = smem + static_cast<size_t>(i % S) * stage_bytes;
+        uint64_t* bar = &wfull_bar[i % S];
+        mbar_arrive_expect_tx(bar, 16384u);
+        bulk_load(st, a.w_tiles + (static_cast<size_t>(mt) * KB + kb) * 16384, 16384u, bar);
+      };
+      auto issue_x = [&](long long i) {
+        const long long u = ub + i;
+        const int T = static_cast<int>(u / KB), kb = static_cast<int>(u % KB);
+        const int nt = T % a.n_tiles;
+        uint8_t* st = smem + static_cast<size_t>(i % S) * stage_bytes + 16384;
+        uint64_t* bar = &xfull_bar[i % S];
+        mbar_arrive_expect_tx(bar, ATOMS * x_tile_bytes);
 #pragma unroll
         for (int at = 0; at < ATOMS; ++at)
-          tma_load_2d(st + 16384 + at * x_tile_bytes, &tm_x, &full_bar[s], kb * KE + at * 64,
-                      nt * a.n_tile);
+          tma_load_2d(st + at * x_tile_bytes, &tm_x, bar, kb * KE + at * 64, nt * a.n_tile);
+      };
+      // weights do not depend on the previous kernel: stream the first stages at once
+      for (long long i = 0; i < pre; ++i) issue_w(i);
+      griddep_wait();
+      for (long long i = 0; i < pre; ++i) issue_x(i);
+      long long i = pre;
+      for (; i < n; ++i) {
+        const int s = static_cast<int>(i % S);
+        if (!mbar_wait(&sfree_bar[s], static_cast<uint32_t>(((i / S) & 1) ^ 1), &abort_flag, a.status,
+                       0x101))
+          break;
+        issue_w(i);
+        issue_x(i);
       }
-      // Drain: wait until every issued copy has landed before the CTA may exit.
-      const long long issued = i;
-      for (long long j = issued > S ? issued - S : 0; j < issued; ++j) {
-        const int s = static_cast<int>(j % S);
-        mbar_wait(&full_bar[s], static_cast<uint32_t>((j / S) & 1), nullptr, a.status, 0x102);
+      // drain: every issued copy lands before the CTA may exit
+      for (long long j = i > S ? i - S : 0; j < i; ++j) {
+        const uint32_t ph = static_cast<uint32_t>((j / S) & 1);
+        mbar_wait(&wfull_bar[j % S], ph, nullptr, a.status, 0x102);
+        mbar_wait(&xfull_bar[j % S], ph, nullptr, a.status, 0x103);
       }
     }
   } else if (warp == 1) {
@@ -324,7 +380,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         const bool first = (u == ub) || (kb == 0);
         const bool last = (u == ue - 1) || (kb == KB - 1);
         const int s = static_cast<int>(i % S);
-        const int ast = static_cast<int>(i % GEMM_A_STAGES);
+        const int ast = static_cast<int>(i % SA);
         if (first) {
           ++seg;
           d = static_cast<int>(seg & 1);
@@ -333,14 +389,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             break;
           tc_fence_after();
         }
-        if (!mbar_wait(&afull_bar[ast], static_cast<uint32_t>((i / GEMM_A_STAGES) & 1), &abort_flag,
-                       a.status, 0x202))
+        if (!mbar_wait(&afull_bar[ast], static_cast<uint32_t>((i / SA) & 1), &abort_flag, a.status,
+                       0x202))
           break;
-        if (!mbar_wait(&full_bar[s], static_cast<uint32_t>((i / S) & 1), &abort_flag, a.status,
+        if (!mbar_wait(&xfull_bar[s], static_cast<uint32_t>((i / S) & 1), &abort_flag, a.status,
                        0x203))
           break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + D_COLS0 + static_cast<uint32_t>(d) * 128u;
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(d) * DCOLS;
         const uint32_t a_tmem = tmem_base + A_COLS0 + static_cast<uint32_t>(ast) * ACOLS;
         const uint32_t x_base = smem_u32(smem + static_cast<size_t>(s) * stage_bytes + 16384);
 #pragma unroll
@@ -369,12 +425,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     __half2 sc2 = __floats2half2_rn(1.0f, 1.0f);
     for (long long u = ub; u < ue; ++u, ++i) {
       const int s = static_cast<int>(i % S);
-      const int ast = static_cast<int>(i % GEMM_A_STAGES);
-      if (!mbar_wait_warp(&full_bar[s], static_cast<uint32_t>((i / S) & 1), &abort_flag, a.status,
+      const int ast = static_cast<int>(i % SA);
+      if (!mbar_wait_warp(&wfull_bar[s], static_cast<uint32_t>((i / S) & 1), &abort_flag, a.status,
                           0x301))
         break;
-      if (!mbar_wait_warp(&afree_bar[ast], static_cast<uint32_t>(((i / GEMM_A_STAGES) & 1) ^ 1),
-                          &abort_flag, a.status, 0x302))
+      if (!mbar_wait_warp(&afree_bar[ast], static_cast<uint32_t>(((i / SA) & 1) ^ 1), &abort_flag,
+                          a.status, 0x302))
         break;
       tc_fence_after();
       const int T = static_cast<int>(u / KB);
@@ -418,6 +474,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
   } else if (warp >= 8) {
     // ------------------------------------------------------------ epilogue
+    griddep_wait();  // outputs, residual inputs and split workspaces belong to the stream order
     const int e = threadIdx.x - 256;
     const uint32_t lane_base = static_cast<uint32_t>((warp - 8) * 32) << 16;
     long long seg = -1;
@@ -442,7 +499,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       mbar_try_wait(&dfull_bar[d], static_cast<uint32_t>((seg >> 1) & 1));
       tc_fence_after();
       const int mt = T / a.n_tiles, nt = T % a.n_tiles;
-      const uint32_t dt = tmem_base + lane_base + D_COLS0 + static_cast<uint32_t>(d) * 128u;
+      const uint32_t dt = tmem_base + lane_base + static_cast<uint32_t>(d) * DCOLS;
       if (kb0 == 0 && kb1 == KB) {
         for (int c0 = 0; c0 < a.n_tile; c0 += 16) {
           uint32_t r[16];
@@ -457,19 +514,23 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&dfree_bar[d]);
       } else {
+        // split tile: partial [seg][row][n_tile] f32; the last CTA adds them in seg order
         const int first_cta = cta_of_unit(static_cast<long long>(T) * KB, U, G);
         const int last_cta = cta_of_unit(static_cast<long long>(T) * KB + KB - 1, U, G);
         const int nseg = last_cta - first_cta + 1;
         const int segidx = static_cast<int>(blockIdx.x) - first_cta;
         const size_t tile_elems = static_cast<size_t>(a.n_tile) * 128;
         float* wsT = a.ws + static_cast<size_t>(T) * a.max_seg * tile_elems;
+        float* mine = wsT + segidx * tile_elems + static_cast<size_t>(e) * a.n_tile;
         for (int c0 = 0; c0 < a.n_tile; c0 += 16) {
           uint32_t r[16];
           tmem_ld_x16(dt + static_cast<uint32_t>(c0), r);
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            wsT[segidx * tile_elems + static_cast<size_t>(c0 + j) * 128 + e] = __uint_as_float(r[j]);
+          for (int j = 0; j < 16; j += 4)
+            __stcg(reinterpret_cast<float4*>(mine + c0 + j),
+                   make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                               __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3])));
         }
         tc_fence_before();
         __syncwarp();
@@ -483,14 +544,46 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         named_bar_sync(1, 128);
         if (es.last_flag) {
           __threadfence();
+          const float* rowp = wsT + static_cast<size_t>(e) * a.n_tile;
           for (int c0 = 0; c0 < a.n_tile; c0 += 16) {
+            float4 acc[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+            int sg = 0;
+            for (; sg + 4 <= nseg; sg += 4) {  // 16 independent 16-byte loads in flight
+              float4 p[4][4];
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                  p[q][j] = __ldcg(reinterpret_cast<const float4*>(rowp + (sg + q) * tile_elems + c0 + 4 * j));
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  acc[j].x += p[q][j].x;
+                  acc[j].y += p[q][j].y;
+                  acc[j].z += p[q][j].z;
+                  acc[j].w += p[q][j].w;
+                }
+            }
+            for (; sg < nseg; ++sg) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float4 p = __ldcg(reinterpret_cast<const float4*>(rowp + sg * tile_elems + c0 + 4 * j));
+                acc[j].x += p.x;
+                acc[j].y += p.y;
+                acc[j].z += p.z;
+                acc[j].w += p.w;
+              }
+            }
             float v[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              float acc = 0.0f;
-              for (int sg = 0; sg < nseg; ++sg)
-                acc += __ldcg(wsT + sg * tile_elems + static_cast<size_t>(c0 + j) * 128 + e);
-              v[j] = acc;
+            for (int j = 0; j < 4; ++j) {
+              v[4 * j] = acc[j].x;
+              v[4 * j + 1] = acc[j].y;
+              v[4 * j + 2] = acc[j].z;
+              v[4 * j + 3] = acc[j].w;
             }
             epilogue_chunk<EPI>(a, es, mt, nt, c0, e, v);
           }

@@ -2,6 +2,7 @@
 // argmax finalisation with on-device token feedback, token scatter.
 #pragma once
 #include "device_common.cuh"
+#include "gemm_tc.cuh"  // griddep_wait / griddep_launch_dependents
 
 namespace qasr {
 
@@ -11,6 +12,8 @@ __global__ void embed_rows_kernel(__half* __restrict__ h, const __half* __restri
                                   int vocab, const int* __restrict__ row_slot,
                                   const int* __restrict__ next_tok, const int* __restrict__ pos,
                                   int* __restrict__ row_pos, uint32_t* status) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int r = blockIdx.x;
   const int slot = row_slot[r];
   int tok = next_tok[slot];
@@ -30,6 +33,8 @@ __global__ void rmsnorm_rows_kernel(__half* __restrict__ out, const __half* __re
                                     const int* __restrict__ src_rows, const float* __restrict__ w,
                                     int hs, float eps) {
   __shared__ float red[32];
+  griddep_wait();
+  griddep_launch_dependents();
   const int r = blockIdx.x;
   const int src = src_rows ? src_rows[r] : r;
   const __half* x = in + static_cast<size_t>(src) * hs;
@@ -68,6 +73,8 @@ __global__ void finalize_rows_kernel(unsigned long long* __restrict__ best, int 
                                      const int* __restrict__ row_slot,
                                      const int* __restrict__ row_pos, int* __restrict__ out_tok,
                                      int* __restrict__ next_tok, int* __restrict__ pos) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= rows) return;
   const unsigned long long key = best[r];
@@ -81,6 +88,8 @@ __global__ void finalize_rows_kernel(unsigned long long* __restrict__ best, int 
 
 __global__ void scatter_tokens_kernel(int* __restrict__ next_tok, const int* __restrict__ slots,
                                       const int* __restrict__ toks, int n) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) next_tok[slots[i]] = toks[i];
 }

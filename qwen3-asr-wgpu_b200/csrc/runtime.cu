@@ -14,6 +14,7 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -74,15 +75,41 @@ static bool make_tmap(CUtensorMap* m, const void* base, bool bytes1, uint64_t in
 
 // ----------------------------------------------------------------------------- GEMM plan
 struct Linear {
-  void* w = nullptr;        // device [n_out, k]
+  void* w = nullptr;        // device, tiled layout (weight_tile_offset)
   __half* scale = nullptr;  // device [n_out] (int8)
   int n_out = 0, k = 0;
   bool int8 = false;
-  CUtensorMap tm{};
 };
 
+// Launch with programmatic stream serialization (PDL) unless disabled by
+// QASR_B200_NO_PDL=1: the kernel may start while its predecessor drains and orders
+// itself with griddepcontrol.wait.
+static bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("QASR_B200_NO_PDL");
+    return !(e && e[0] == '1');
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                            cudaStream_t st, bool pdl, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (pdl && pdl_enabled()) ? 1 : 0;
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 struct GemmLaunch {
-  const CUtensorMap* tmw = nullptr;
   CUtensorMap tmx{};
   GemmArgs args{};
   int grid = 0;
@@ -144,7 +171,9 @@ static GemmShape gemm_shape(int n_out, int k, bool int8, int rows, int num_sms) 
   s.kblocks = k / ke;
   s.tiles = (n_out / 128) * s.n_tiles;
   s.units = s.tiles * s.kblocks;
-  s.grid = std::min(num_sms, s.units);
+  // at least 4 units per CTA: a CTA that streams less than ~64 KB of weights spends
+  // more on its pipeline fill and split fixup than on the bytes
+  s.grid = std::max(1, std::min(num_sms, s.units / 4));
   const int atoms = int8 ? 2 : 1;
   const int stage = 16384 + atoms * s.n_tile * 128;
   const int dyn = g_dyn_smem_max > 0 ? g_dyn_smem_max : 200 * 1024;
@@ -162,14 +191,11 @@ static GemmShape gemm_shape(int n_out, int k, bool int8, int rows, int num_sms) 
   return s;
 }
 
-static cudaError_t launch_gemm(const GemmLaunch& L, cudaStream_t st) {
+static cudaError_t launch_gemm(const GemmLaunch& L, cudaStream_t st, bool pdl) {
   dim3 grid(L.grid), block(GEMM_THREADS);
 #define QASR_GEMM_CASE(I8, EPI)                                                          \
-  if (L.int8 == I8 && L.epi == EPI) {                                                    \
-    gemm_tc_kernel<I8, EPI><<<grid, block, L.smem, st>>>(*L.tmw, L.tmx, L.args);          \
-    g_launches.fetch_add(1, std::memory_order_relaxed);                                  \
-    return cudaGetLastError();                                                           \
-  }
+  if (L.int8 == I8 && L.epi == EPI)                                                      \
+    return launch_k(gemm_tc_kernel<I8, EPI>, grid, block, L.smem, st, pdl, L.tmx, L.args);
   QASR_GEMM_CASE(false, EPI_STORE)
   QASR_GEMM_CASE(false, EPI_RESID)
   QASR_GEMM_CASE(false, EPI_SILU)
@@ -220,7 +246,8 @@ struct qasr_ctx {
   std::vector<void*> allocs;
 
   std::vector<LayerDev> layers;
-  Linear lm;  // tied embedding as an f16 [vocab, hs] weight
+  Linear lm;  // tied embedding as an f16 [vocab, hs] weight (tiled, for the lm_head GEMM)
+  __half* embed = nullptr;  // the same table row-major, for the token embedding gather
   float* final_norm = nullptr;
   bool embed_loaded = false;
   __half *rope_cos = nullptr, *rope_sin = nullptr;
@@ -328,7 +355,6 @@ qasr_status plan_gemm(qasr_ctx* c, const Linear& lin, const __half* X, int ldx, 
   if (!make_tmap(&L->tmx, X, false, static_cast<uint64_t>(lin.k), static_cast<uint64_t>(rows),
                  static_cast<uint64_t>(ldx) * 2, 64, static_cast<uint32_t>(s.n_tile), &c->err))
     return QASR_ERR_DEVICE;
-  L->tmw = &lin.tm;
   L->int8 = lin.int8;
   L->epi = epi;
   L->grid = s.grid;
@@ -345,6 +371,7 @@ qasr_status plan_gemm(qasr_ctx* c, const Linear& lin, const __half* X, int ldx, 
   a.grid = s.grid;
   a.stages = s.stages;
   a.max_seg = s.max_seg;
+  a.w_tiles = static_cast<const uint8_t*>(lin.w);
   a.scale = lin.scale;
   a.epi = epi;
   a.ws = c->gemm_ws;
@@ -363,7 +390,7 @@ qasr_status plan_gemm(qasr_ctx* c, const Linear& lin, const __half* X, int ldx, 
 }
 
 qasr_status run_gemm(qasr_ctx* c, const GemmLaunch& L) {
-  CK(launch_gemm(L, c->stream), "GEMM launch");
+  CK(launch_gemm(L, c->stream, true), "GEMM launch");
   return QASR_OK;
 }
 
@@ -387,9 +414,8 @@ qasr_status launch_attention(qasr_ctx* c, int layer, int rows, const int* rs, co
   a.max_chunks = c->attn_max_chunks;
   a.status = c->status;
   const int grid = c->num_sms * 4;
-  attention_kernel<<<grid, ATTN_THREADS, (rows + 1) * sizeof(int), c->stream>>>(a);
-  g_launches.fetch_add(1, std::memory_order_relaxed);
-  CK(cudaGetLastError(), "attention launch");
+  CK(launch_k(attention_kernel, dim3(grid), dim3(ATTN_THREADS), (rows + 1) * sizeof(int), c->stream, true, a),
+     "attention launch");
   return QASR_OK;
 }
 
@@ -400,9 +426,9 @@ qasr_status enqueue_layers(qasr_ctx* c, int rows, const int* rs, const int* rp, 
   const int I = c->cfg.intermediate_size;
   for (int l = 0; l < c->cfg.num_hidden_layers; ++l) {
     LayerDev& L = c->layers[l];
-    rmsnorm_rows_kernel<<<rows, 256, 0, c->stream>>>(c->x, c->h, nullptr, L.iln, hs, c->cfg.rms_norm_eps);
-    g_launches.fetch_add(1, std::memory_order_relaxed);
-    CK(cudaGetLastError(), "rmsnorm launch");
+    CK(launch_k(rmsnorm_rows_kernel, dim3(rows), dim3(256), 0, c->stream, true, c->x,
+                (const __half*)c->h, (const int*)nullptr, (const float*)L.iln, hs, c->cfg.rms_norm_eps),
+       "rmsnorm launch");
     GemmLaunch g;
     qasr_status s = plan_gemm(c, L.qkv, c->x, hs, rows, EPI_QKV, &g);
     if (s) return s;
@@ -418,9 +444,9 @@ qasr_status enqueue_layers(qasr_ctx* c, int rows, const int* rs, const int* rp, 
     g.args.out = c->h;
     g.args.ldo = hs;
     if ((s = run_gemm(c, g))) return s;
-    rmsnorm_rows_kernel<<<rows, 256, 0, c->stream>>>(c->x, c->h, nullptr, L.pln, hs, c->cfg.rms_norm_eps);
-    g_launches.fetch_add(1, std::memory_order_relaxed);
-    CK(cudaGetLastError(), "rmsnorm launch");
+    CK(launch_k(rmsnorm_rows_kernel, dim3(rows), dim3(256), 0, c->stream, true, c->x,
+                (const __half*)c->h, (const int*)nullptr, (const float*)L.pln, hs, c->cfg.rms_norm_eps),
+       "rmsnorm launch");
     if ((s = plan_gemm(c, L.gu, c->x, hs, rows, EPI_SILU, &g))) return s;
     g.args.out = c->act;
     g.args.ldo = I;
@@ -438,10 +464,9 @@ qasr_status enqueue_layers(qasr_ctx* c, int rows, const int* rs, const int* rp, 
 qasr_status enqueue_head(qasr_ctx* c, int n, const int* src_rows, const int* slot_of,
                          const int* pos_of, int* out_tok, uint64_t* nk) {
   const int hs = c->cfg.hidden_size;
-  rmsnorm_rows_kernel<<<n, 256, 0, c->stream>>>(c->xf, c->h, src_rows, c->final_norm, hs,
-                                                c->cfg.rms_norm_eps);
-  g_launches.fetch_add(1, std::memory_order_relaxed);
-  CK(cudaGetLastError(), "final norm launch");
+  CK(launch_k(rmsnorm_rows_kernel, dim3(n), dim3(256), 0, c->stream, true, c->xf, (const __half*)c->h,
+              src_rows, (const float*)c->final_norm, hs, c->cfg.rms_norm_eps),
+     "final norm launch");
   GemmLaunch g;
   qasr_status s = plan_gemm(c, c->lm, c->xf, hs, n, EPI_LOGITS, &g);
   if (s) return s;
@@ -449,20 +474,18 @@ qasr_status enqueue_head(qasr_ctx* c, int n, const int* src_rows, const int* slo
   g.args.ld_logits = c->cfg.vocab_size;
   g.args.best = c->best;
   if ((s = run_gemm(c, g))) return s;
-  finalize_rows_kernel<<<(n + 127) / 128, 128, 0, c->stream>>>(c->best, n, slot_of, pos_of,
-                                                               out_tok, c->next_tok_dev, c->pos_dev);
-  g_launches.fetch_add(1, std::memory_order_relaxed);
-  CK(cudaGetLastError(), "finalize launch");
+  CK(launch_k(finalize_rows_kernel, dim3((n + 127) / 128), dim3(128), 0, c->stream, true, c->best, n,
+              slot_of, pos_of, out_tok, c->next_tok_dev, c->pos_dev),
+     "finalize launch");
   *nk += 3;
   return QASR_OK;
 }
 
 qasr_status enqueue_decode(qasr_ctx* c, int n, uint64_t* nk) {
-  embed_rows_kernel<<<n, 128, 0, c->stream>>>(c->h, static_cast<const __half*>(c->lm.w),
-                                              c->cfg.hidden_size, c->cfg.vocab_size, c->drow_slot,
-                                              c->next_tok_dev, c->pos_dev, c->drow_pos, c->status);
-  g_launches.fetch_add(1, std::memory_order_relaxed);
-  CK(cudaGetLastError(), "embed launch");
+  CK(launch_k(embed_rows_kernel, dim3(n), dim3(128), 0, c->stream, true, c->h, (const __half*)c->embed,
+              c->cfg.hidden_size, c->cfg.vocab_size, (const int*)c->drow_slot, (const int*)c->next_tok_dev,
+              (const int*)c->pos_dev, c->drow_pos, c->status),
+     "embed launch");
   *nk += 1;
   qasr_status s = enqueue_layers(c, n, c->drow_slot, c->drow_pos, nk);
   if (s) return s;
@@ -530,14 +553,23 @@ qasr_status upload_linear(qasr_ctx* c, Linear* lin, int n_out, int k, bool int8,
     if (s) return s;
     if (int8 && (s = dalloc(c, &lin->scale, n_out, "scale alloc"))) return s;
   }
-  CK(cudaMemcpy(lin->w, host.data(), host.size(), cudaMemcpyHostToDevice), "weight upload");
+  // row-major staging copy, then the tiled HBM layout the GEMM streams
+  void* staging = nullptr;
+  CK(cudaMalloc(&staging, host.size()), "weight staging");
+  cudaError_t e = cudaMemcpy(staging, host.data(), host.size(), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) {
+    pack_weight_tiles_kernel<<<1024, 256>>>(static_cast<const uint4*>(staging), static_cast<uint4*>(lin->w),
+                                           n_out, static_cast<int>(k * elem));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaFree(staging);
+  if (e != cudaSuccess) return cuda_fail(c, e, "weight upload");
   if (int8) CK(cudaMemcpy(lin->scale, host_s.data(), n_out * 2, cudaMemcpyHostToDevice), "scale upload");
   lin->n_out = n_out;
   lin->k = k;
   lin->int8 = int8;
-  if (!make_tmap(&lin->tm, lin->w, int8, static_cast<uint64_t>(k), static_cast<uint64_t>(n_out),
-                 static_cast<uint64_t>(k) * elem, int8 ? 128 : 64, 128, &c->err))
-    return QASR_ERR_DEVICE;
   return QASR_OK;
 }
 
@@ -703,6 +735,8 @@ qasr_status qasr_load_embed(qasr_ctx* c, const uint16_t* embed, const uint16_t* 
   const int V = c->cfg.vocab_size, hs = c->cfg.hidden_size;
   qasr_status s = upload_linear(c, &c->lm, V, hs, false, {embed}, {V}, {}, {});
   if (s) return s;
+  if (!c->embed && (s = dalloc(c, &c->embed, static_cast<size_t>(V) * hs, "embed alloc"))) return s;
+  CK(cudaMemcpy(c->embed, embed, static_cast<size_t>(V) * hs * 2, cudaMemcpyHostToDevice), "embed upload");
   if ((s = upload_f32_vec(c, &c->final_norm, final_norm, hs))) return s;
   c->embed_loaded = true;
   return QASR_OK;
@@ -1087,12 +1121,9 @@ qasr_status qasr_kernel_gemm(int device, void* stream, int weight_format, const 
       return probe_err(err, errlen, QASR_ERR_OOM, "counters");
     P.cnt_n = s.tiles;
   }
-  CUtensorMap tmw;
   GemmLaunch L;
-  if (!make_tmap(&tmw, w, i8, k, n_out, static_cast<uint64_t>(k) * (i8 ? 1 : 2), i8 ? 128 : 64, 128, &e) ||
-      !make_tmap(&L.tmx, x, false, k, rows, static_cast<uint64_t>(ldx) * 2, 64, s.n_tile, &e))
+  if (!make_tmap(&L.tmx, x, false, k, rows, static_cast<uint64_t>(ldx) * 2, 64, s.n_tile, &e))
     return probe_err(err, errlen, QASR_ERR_DEVICE, e);
-  L.tmw = &tmw;
   L.int8 = i8;
   L.epi = accumulate ? EPI_RESID : EPI_STORE;
   L.grid = s.grid;
@@ -1108,13 +1139,14 @@ qasr_status qasr_kernel_gemm(int device, void* stream, int weight_format, const 
   a.grid = s.grid;
   a.stages = s.stages;
   a.max_seg = s.max_seg;
+  a.w_tiles = static_cast<const uint8_t*>(w);
   a.scale = reinterpret_cast<const __half*>(scale);
   a.epi = L.epi;
   a.out = reinterpret_cast<__half*>(out);
   a.ldo = ldo;
   a.ws = P.ws;
   a.counters = P.cnt;
-  const cudaError_t ce = launch_gemm(L, static_cast<cudaStream_t>(stream));
+  const cudaError_t ce = launch_gemm(L, static_cast<cudaStream_t>(stream), false);
   if (ce != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, cudaGetErrorString(ce));
   return QASR_OK;
 }
@@ -1168,9 +1200,8 @@ qasr_status qasr_kernel_attention(int device, void* stream, const uint16_t* q, i
   a.ws = P.ws;
   a.counters = P.cnt;
   a.max_chunks = max_chunks;
-  attention_kernel<<<sms * 4, ATTN_THREADS, (rows + 1) * sizeof(int), static_cast<cudaStream_t>(stream)>>>(a);
-  g_launches.fetch_add(1, std::memory_order_relaxed);
-  const cudaError_t ce = cudaGetLastError();
+  const cudaError_t ce = launch_k(attention_kernel, dim3(sms * 4), dim3(ATTN_THREADS), (rows + 1) * sizeof(int),
+                                  static_cast<cudaStream_t>(stream), false, a);
   if (ce != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, cudaGetErrorString(ce));
   return QASR_OK;
 }
@@ -1189,6 +1220,21 @@ __global__ void kv_append_kernel(const __half* __restrict__ k, const __half* __r
   kv.pool[vo + d] = v[static_cast<size_t>(r) * ld + h * 128 + d];
 }
 }  // namespace qasr
+
+extern "C" qasr_status qasr_kernel_pack_weights(int device, void* stream, int weight_format,
+                                                const void* w_rowmajor, int n_out, int k, void* w_tiled,
+                                                char* err, int errlen) {
+  if (!w_rowmajor || !w_tiled || n_out <= 0 || n_out % 128 || k <= 0 || k % 128)
+    return probe_err(err, errlen, QASR_ERR_INVALID_ARG, "bad pack arguments");
+  if (cudaSetDevice(device) != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, "cudaSetDevice");
+  const int row_bytes = k * (weight_format == QASR_WEIGHTS_INT8 ? 1 : 2);
+  pack_weight_tiles_kernel<<<1024, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(w_rowmajor), static_cast<uint4*>(w_tiled), n_out, row_bytes);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  const cudaError_t ce = cudaGetLastError();
+  if (ce != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, cudaGetErrorString(ce));
+  return QASR_OK;
+}
 
 extern "C" qasr_status qasr_kernel_kv_append(int device, void* stream, const uint16_t* k,
                                              const uint16_t* v, uint16_t* kv_pool,

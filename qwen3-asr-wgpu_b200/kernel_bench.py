@@ -60,6 +60,9 @@ def bench_gemm(args, pkg, torch):
     x = torch.randn((r, k), dtype=torch.float16, device="cuda")
     o = torch.zeros((r, n), dtype=torch.float16, device="cuda")
     st = torch.cuda.current_stream().cuda_stream
+    tiled = torch.empty_like(w)
+    pkg.kernel_pack_weights(0, st, fmt, w.data_ptr(), n, k, tiled.data_ptr())
+    w = tiled
 
     def run():
         pkg.kernel_gemm(0, st, fmt, w.data_ptr(), sc.data_ptr() if sc is not None else None, n, k,

@@ -20,6 +20,13 @@ def _dev(a, torch, dtype=None):
     return t.cuda()
 
 
+def _pack(qasr, torch, fmt, w_dev, n_out, k):
+    """Row-major device weight -> the tiled layout the GEMM streams."""
+    tiled = torch.empty_like(w_dev)
+    qasr.kernel_pack_weights(0, 0, fmt, w_dev.data_ptr(), n_out, k, tiled.data_ptr())
+    return tiled
+
+
 def _gemm_case(qasr, torch, fmt, n_out, k, rows, seed, accumulate=False):
     from qasr_b200 import synth
     w16 = synth.normal_f16((n_out, k), seed, 1, 0.0, 0.02)
@@ -34,6 +41,7 @@ def _gemm_case(qasr, torch, fmt, n_out, k, rows, seed, accumulate=False):
         wd = w16
         w_dev = _dev(w16, torch)
         s_dev = None
+    w_dev = _pack(qasr, torch, fmt, w_dev, n_out, k)
     x_dev = _dev(x16, torch)
     h0 = synth.normal_f16((rows, n_out), seed, 3, 0.0, 1.0)
     out = _dev(h0 if accumulate else np.zeros((rows, n_out), np.uint16), torch)
@@ -87,6 +95,7 @@ def test_int8_dequant_bit_exact(qasr, cuda_device, oracle):
     x[np.arange(rows), cols] = 1.0
     out = torch.zeros((rows, n_out), dtype=torch.int16, device="cuda")
     qd, sd, xd = _dev(q, torch), _dev(s, torch), _dev(x.view(np.uint16), torch)
+    qd = _pack(qasr, torch, qasr.WEIGHTS_INT8, qd, n_out, k)
     qasr.kernel_gemm(0, 0, qasr.WEIGHTS_INT8, qd.data_ptr(), sd.data_ptr(), n_out, k, xd.data_ptr(), k,
                      rows, out.data_ptr(), n_out, False)
     torch.cuda.synchronize()
