@@ -41,6 +41,16 @@ qasr_status qasr_kernel_gemm(int device, void* stream, int weight_format, const 
                              int rows, uint16_t* out, int ldo, int accumulate, char* err,
                              int errlen);
 
+/* qasr_kernel_gemm with a latency trace: if `trace` (device, grid * 12 uint64) is
+ * non-NULL each CTA records %globaltimer stamps of its pipeline milestones (entry, setup,
+ * first weight/activation copies issued, first stage seen/built, first/last MMA, first
+ * accumulator, last store, split fixup, exit); *grid_out receives the CTA count. */
+qasr_status qasr_kernel_gemm_traced(int device, void* stream, int weight_format, const void* w,
+                                    const uint16_t* scale, int n_out, int k, const uint16_t* x,
+                                    int ldx, int rows, uint16_t* out, int ldo, int accumulate,
+                                    unsigned long long* trace, int* grid_out, char* err,
+                                    int errlen);
+
 /* GQA attention of `rows` query rows over their slot's paged KV (gqa_decode_* /
  * gqa_split_merge, src/shaders.rs:1881-2905).  q/out: [rows, q_ld] f16 (q heads 2g and
  * 2g+1 read kv head g); kv_pool: [pages][layers][2][nkv][64][128] f16; page_table:

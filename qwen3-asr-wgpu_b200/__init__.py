@@ -44,7 +44,8 @@ EXPORTED_SYMBOLS = (
     "qasr_slot_pos", "qasr_set_slot_pos", "qasr_set_input_token", "qasr_set_input_tokens",
     "qasr_prefill", "qasr_step", "qasr_prefill_batch", "qasr_step_batch", "qasr_read_logits",
     "qasr_build_rope_tables", "qasr_build_dim_map", "qasr_dequant_i8",
-    "qasr_kernel_pack_weights", "qasr_kernel_gemm", "qasr_kernel_attention", "qasr_kernel_kv_append",
+    "qasr_kernel_pack_weights", "qasr_kernel_gemm", "qasr_kernel_gemm_traced", "qasr_kernel_attention",
+    "qasr_kernel_kv_append",
     "qasr_kernel_launch_count",
     "qasr_synth_key", "qasr_synth_normal_f16", "qasr_synth_uniform_ids",
     "qasr_synth_quantize_rows", "qasr_f32_to_f16", "qasr_f16_to_f32", "qasr_f32_to_f16_array",
@@ -114,6 +115,8 @@ def _load() -> ctypes.CDLL:
     lib.qasr_dequant_i8.argtypes = [P, P, I, I, P]
     lib.qasr_kernel_pack_weights.argtypes = [I, P, I, P, I, I, P, ctypes.c_char_p, I]
     lib.qasr_kernel_gemm.argtypes = [I, P, I, P, P, I, I, P, I, I, P, I, I, ctypes.c_char_p, I]
+    lib.qasr_kernel_gemm_traced.argtypes = [I, P, I, P, P, I, I, P, I, I, P, I, I, P, ctypes.POINTER(I),
+                                            ctypes.c_char_p, I]
     lib.qasr_kernel_attention.argtypes = [I, P, P, I, P, P, P, I, I, I, I, P, P, I, ctypes.c_char_p, I]
     lib.qasr_kernel_kv_append.argtypes = [I, P, P, P, P, P, I, I, I, I, P, P, I, ctypes.c_char_p, I]
     lib.qasr_kernel_launch_count.restype = ctypes.c_uint64
@@ -328,6 +331,22 @@ def kernel_gemm(device: int, stream: int, weight_format: int, w_ptr: int, scale_
                               rows, ctypes.c_void_p(out_ptr), ldo, int(accumulate), err, 512)
     if st != QASR_OK:
         raise DecoderError(st, err.value.decode())
+
+
+def kernel_gemm_traced(device: int, stream: int, weight_format: int, w_ptr: int, scale_ptr: int | None,
+                       n_out: int, k: int, x_ptr: int, ldx: int, rows: int, out_ptr: int, ldo: int,
+                       trace_ptr: int, accumulate: bool = False) -> int:
+    """kernel_gemm that records per-CTA %globaltimer milestones into trace (grid x 12 u64);
+    returns the CTA count."""
+    err = ctypes.create_string_buffer(512)
+    grid = ctypes.c_int()
+    st = lib.qasr_kernel_gemm_traced(device, ctypes.c_void_p(stream), weight_format, ctypes.c_void_p(w_ptr),
+                                     ctypes.c_void_p(scale_ptr or 0), n_out, k, ctypes.c_void_p(x_ptr), ldx,
+                                     rows, ctypes.c_void_p(out_ptr), ldo, int(accumulate),
+                                     ctypes.c_void_p(trace_ptr), ctypes.byref(grid), err, 512)
+    if st != QASR_OK:
+        raise DecoderError(st, err.value.decode())
+    return grid.value
 
 
 def kernel_attention(device: int, stream: int, q_ptr: int, q_ld: int, out_ptr: int, pool_ptr: int,

@@ -6,35 +6,51 @@
 // o = f16(sum_t p_t v_t / sum_t p_t).
 //
 // Each query row r (slot s_r, position p_r) attends to positions [0, p_r] of its slot,
-// which makes one kernel serve a decode step (one row per slot) and a prefill chunk
+// so one kernel serves a decode step (one row per slot) and a prefill chunk
 // (consecutive positions of a slot; causal by construction).
 //
-// Work unit = (row, kv head, chunk); both q heads of the kv head are done together so
-// K/V are read once (the reference's "pair" kernel idea).  A row of length len is cut
-// into chunks of CH = max(64, roundup64(len / ATTN_ROW_CHUNKS)) positions — a function
-// of the row alone, so a slot's result does not depend on the other slots of the
-// batch.  A row with several chunks is merged by the CTA that finishes its last chunk
-// (atomic counter, no waiting), chunks in index order.
+// Layout: a KV page holds 64 positions; the K (or V) rows of one (page, layer, kv head)
+// are one contiguous 16 KB block.  Work unit = (row, kv head, chunk of stages); a
+// stage is two pages (128 positions).  Both q heads of the kv head are done together
+// so K/V are read once (the reference's "pair" kernel idea).  A row is cut into at
+// most ATTN_ROW_CHUNKS chunks as a function of its own length, so a slot's result does
+// not depend on the other rows of the launch.
 //
-// Inside a unit each warp takes 32-position batches: lane L covers dims
-// [8*(L%16), +8) of the positions p0 + 2*i + L/16 (i < 16), i.e. 16-byte loads that
-// read a whole 256-byte K or V row per half-warp; the dot products are finished by a
-// 4-round transposing butterfly, the softmax is online per warp, the warps merge in
-// shared memory.
+// Persistent CTA per SM: warp 8 streams the pages of the CTA's units, stage after stage,
+// into a 3-deep shared-memory ring with cp.async.bulk (completion counted on mbarriers,
+// no multicast); warps 0-7 each take 16 positions of a stage, lane l holding dims
+// [4l, 4l+4): 32 partial dot products (16 positions x 2 heads) are finished by one
+// 5-round transposing butterfly, the softmax is online per head and warp, the warps
+// merge in shared memory, and a row split into several chunks is merged by the CTA
+// that finishes its last chunk (atomic counter, no waiting), chunks in index order.
 #pragma once
 #include "device_common.cuh"
-#include "gemm_tc.cuh"  // KvLayout, kv_elem_offset
+#include "gemm_tc.cuh"  // KvLayout, kv_elem_offset, griddep_*
 
 namespace qasr {
 
-constexpr int ATTN_THREADS = 128;
-constexpr int ATTN_PART_FLOATS = 4 + 2 * 128;  // m_a, m_b, l_a, l_b, o_a[128], o_b[128]
-constexpr int ATTN_ROW_CHUNKS = 8;             // chunks per row (upper bound)
+constexpr int ATTN_CONSUMER_WARPS = 8;
+constexpr int ATTN_THREADS = (ATTN_CONSUMER_WARPS + 1) * 32;
+constexpr int ATTN_STAGES = 3;
+constexpr int ATTN_PAGE_BYTES = 64 * 128 * 2;            // K or V rows of one page / head
+constexpr int ATTN_STAGE_BYTES = 4 * ATTN_PAGE_BYTES;    // 2 pages x (K + V)
+constexpr int ATTN_PART_FLOATS = 4 + 2 * 128;            // m0, m1, l0, l1, o0[128], o1[128]
+constexpr int ATTN_ROW_CHUNKS = 4;                       // chunks per row (upper bound)
+constexpr int ATTN_MAX_ROWS = 4096;
 
-__host__ __device__ __forceinline__ int attn_chunk_len(int len) {
-  const int c = (len + ATTN_ROW_CHUNKS - 1) / ATTN_ROW_CHUNKS;
-  const int r = (c + 63) / 64 * 64;
-  return r < 64 ? 64 : r;
+__host__ __device__ __forceinline__ int attn_row_stages(int len) { return (len + 127) / 128; }
+__host__ __device__ __forceinline__ int attn_chunk_stages(int len) {
+  const int st = attn_row_stages(len);
+  return (st + ATTN_ROW_CHUNKS - 1) / ATTN_ROW_CHUNKS;
+}
+__host__ __device__ __forceinline__ int attn_row_chunks(int len) {
+  const int cs = attn_chunk_stages(len);
+  return (attn_row_stages(len) + cs - 1) / cs;
+}
+// dynamic shared memory of one CTA for `rows` query rows
+__host__ __device__ __forceinline__ size_t attn_smem_bytes(int rows) {
+  return 1024 + static_cast<size_t>(ATTN_STAGES) * ATTN_STAGE_BYTES +
+         static_cast<size_t>(rows + 1) * sizeof(int);
 }
 
 struct AttnArgs {
@@ -47,238 +63,302 @@ struct AttnArgs {
   int layer;
   int rows;
   float scale;
-  float* ws;        // [rows * nkv * max_chunks][ATTN_PART_FLOATS]
+  float* ws;        // [rows * nkv * ATTN_ROW_CHUNKS][ATTN_PART_FLOATS]
   int* counters;    // [rows * nkv], zero between launches
   int max_chunks;
   uint32_t* status;
 };
 
-__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
-  const __half2* h = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 t = __half22float2(h[i]);
-    f[2 * i] = t.x;
-    f[2 * i + 1] = t.y;
+struct AttnUnit {
+  int r, g, c, nch, len, s0, s1;  // row, kv head, chunk, chunks of the row, row length, stages [s0, s1)
+};
+
+__device__ __forceinline__ AttnUnit attn_unit(const AttnArgs& a, const int* prefix, int u) {
+  int lo = 0, hi = a.rows - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (prefix[mid] <= u) lo = mid; else hi = mid - 1;
   }
+  AttnUnit t;
+  t.r = lo;
+  t.len = a.row_pos[lo] + 1;
+  t.nch = attn_row_chunks(t.len);
+  const int rem = u - prefix[lo];
+  t.g = rem / t.nch;
+  t.c = rem % t.nch;
+  const int cs = attn_chunk_stages(t.len);
+  t.s0 = t.c * cs;
+  const int st = attn_row_stages(t.len);
+  t.s1 = min(t.s0 + cs, st);
+  return t;
 }
 
-__global__ void __launch_bounds__(ATTN_THREADS)
+__global__ void __launch_bounds__(ATTN_THREADS, 1)
     attention_kernel(const __grid_constant__ AttnArgs a) {
-  extern __shared__ int prefix[];  // rows + 1 entries
-  __shared__ int sh_units;
-  __shared__ float sm_m[4][2], sm_l[4][2];
-  __shared__ float sm_acc[4][2][128];
-  __shared__ int sh_last;
+  extern __shared__ __align__(1024) uint8_t attn_dsmem[];
+  __shared__ __align__(8) uint64_t full_bar[ATTN_STAGES], empty_bar[ATTN_STAGES];
+  __shared__ float sm_m[ATTN_CONSUMER_WARPS][2], sm_l[ATTN_CONSUMER_WARPS][2];
+  __shared__ __align__(16) float sm_acc[ATTN_CONSUMER_WARPS][2][128];
+  __shared__ __align__(16) float sm_p[ATTN_CONSUMER_WARPS][32];
+  __shared__ int sh_units, sh_last, sh_scan[ATTN_THREADS / 32];
+  __shared__ volatile int abort_flag;
 
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(attn_dsmem) + 1023) & ~uintptr_t(1023));
+  int* prefix = reinterpret_cast<int*>(smem + ATTN_STAGES * ATTN_STAGE_BYTES);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nkv = a.kv.nkv;
+
+  if (tid == 0) {
+    for (int i = 0; i < ATTN_STAGES; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], ATTN_CONSUMER_WARPS);
+    }
+    abort_flag = 0;
+    fence_mbar_init();
+  }
   griddep_wait();
   griddep_launch_dependents();
 
-  // ---- unit decomposition (identical in every CTA) ----
-  if (tid == 0) {
-    int acc = 0;
-    for (int r = 0; r < a.rows; ++r) {
-      prefix[r] = acc;
-      const int len = a.row_pos[r] + 1;
-      const int ch = attn_chunk_len(len);
-      acc += ((len + ch - 1) / ch) * nkv;
+  // ---- unit table: prefix[r] = first unit of row r (block-wide scan)
+  {
+    const int per = (a.rows + ATTN_THREADS - 1) / ATTN_THREADS;
+    const int r0 = tid * per, r1 = min(r0 + per, a.rows);
+    int local = 0;
+    for (int r = r0; r < r1; ++r) local += attn_row_chunks(a.row_pos[r] + 1) * nkv;
+    int incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
     }
-    prefix[a.rows] = acc;
-    sh_units = acc;
+    if (lane == 31) sh_scan[warp] = incl;
+    __syncthreads();
+    if (tid == 0) {
+      int acc = 0;
+      for (int w = 0; w < ATTN_THREADS / 32; ++w) {
+        const int v = sh_scan[w];
+        sh_scan[w] = acc;
+        acc += v;
+      }
+      sh_units = acc;
+    }
+    __syncthreads();
+    int run = sh_scan[warp] + incl - local;
+    for (int r = r0; r < r1; ++r) {
+      prefix[r] = run;
+      run += attn_row_chunks(a.row_pos[r] + 1) * nkv;
+    }
+    if (tid == 0) prefix[a.rows] = sh_units;
+    __syncthreads();
   }
-  __syncthreads();
   const int U = sh_units;
 
-  for (int u = blockIdx.x; u < U; u += gridDim.x) {
-    // find row r with prefix[r] <= u < prefix[r+1]
-    int lo = 0, hi = a.rows - 1;
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (prefix[mid] <= u) lo = mid; else hi = mid - 1;
-    }
-    const int r = lo;
-    const int len = a.row_pos[r] + 1;
-    const int CH = attn_chunk_len(len);
-    const int nch = (len + CH - 1) / CH;
-    const int rem = u - prefix[r];
-    const int g = rem / nch, c = rem % nch;
-    const int slot = a.row_slot[r];
-    const int t0 = c * CH;
-    const int t1 = min(t0 + CH, len);
-
-    // q of heads 2g, 2g+1 for this lane's 8 dims
-    const int d0 = 8 * (lane & 15);
-    const int hw = lane >> 4;
-    float qa[8], qb[8];
-    unpack8(*reinterpret_cast<const uint4*>(a.q + static_cast<size_t>(r) * a.q_ld + (2 * g) * 128 + d0), qa);
-    unpack8(*reinterpret_cast<const uint4*>(a.q + static_cast<size_t>(r) * a.q_ld + (2 * g + 1) * 128 + d0), qb);
-
-    float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
-    float acc_a[8], acc_b[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) acc_a[i] = acc_b[i] = 0.f;
-
-    for (int p0 = t0 + warp * 32; p0 < t1; p0 += 4 * 32) {
-      const size_t kbase = kv_elem_offset(a.kv, slot, p0, a.layer, 0, g);
-      const size_t vbase = kv_elem_offset(a.kv, slot, p0, a.layer, 1, g);
-      const __half* kp = a.kv.pool + kbase + d0;
-      const __half* vp = a.kv.pool + vbase + d0;
-      float da[16], db[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const uint4 kr = __ldg(reinterpret_cast<const uint4*>(kp + (2 * i + hw) * 128));
-        float kf[8];
-        unpack8(kr, kf);
-        float sa = 0.f, sb = 0.f;
-#pragma unroll
-        for (int d = 0; d < 8; ++d) {
-          sa = fmaf(qa[d], kf[d], sa);
-          sb = fmaf(qb[d], kf[d], sb);
-        }
-        da[i] = sa;
-        db[i] = sb;
-      }
-      // transposing butterfly over the 16 lanes of each half-warp: lane j ends up with
-      // the full dot product of position index j
-#pragma unroll
-      for (int o = 8; o >= 1; o >>= 1) {
-        const bool upper = (lane & o) != 0;
-#pragma unroll
-        for (int j = 0; j < o; ++j) {
-          const float send_a = upper ? da[j] : da[j + o];
-          const float keep_a = upper ? da[j + o] : da[j];
-          const float send_b = upper ? db[j] : db[j + o];
-          const float keep_b = upper ? db[j + o] : db[j];
-          da[j] = keep_a + __shfl_xor_sync(0xffffffffu, send_a, o);
-          db[j] = keep_b + __shfl_xor_sync(0xffffffffu, send_b, o);
-        }
-      }
-      const int my_pos = p0 + 2 * (lane & 15) + hw;
-      const bool valid = my_pos < t1;
-      const float s_a = valid ? da[0] * a.scale : -INFINITY;
-      const float s_b = valid ? db[0] * a.scale : -INFINITY;
-      float bm_a = s_a, bm_b = s_b;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        bm_a = fmaxf(bm_a, __shfl_xor_sync(0xffffffffu, bm_a, o));
-        bm_b = fmaxf(bm_b, __shfl_xor_sync(0xffffffffu, bm_b, o));
-      }
-      const float mn_a = fmaxf(m_a, bm_a), mn_b = fmaxf(m_b, bm_b);
-      const float corr_a = expf(m_a - mn_a), corr_b = expf(m_b - mn_b);
-      const float p_a = valid ? expf(s_a - mn_a) : 0.f;
-      const float p_b = valid ? expf(s_b - mn_b) : 0.f;
-      l_a = l_a * corr_a + p_a;
-      l_b = l_b * corr_b + p_b;
-#pragma unroll
-      for (int d = 0; d < 8; ++d) {
-        acc_a[d] *= corr_a;
-        acc_b[d] *= corr_b;
-      }
-      m_a = mn_a;
-      m_b = mn_b;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float pa = __shfl_sync(0xffffffffu, p_a, (lane & 16) | i);
-        const float pb = __shfl_sync(0xffffffffu, p_b, (lane & 16) | i);
-        if (p0 + 2 * i + hw < t1) {
-          const uint4 vr = __ldg(reinterpret_cast<const uint4*>(vp + (2 * i + hw) * 128));
-          float vf[8];
-          unpack8(vr, vf);
-#pragma unroll
-          for (int d = 0; d < 8; ++d) {
-            acc_a[d] = fmaf(pa, vf[d], acc_a[d]);
-            acc_b[d] = fmaf(pb, vf[d], acc_b[d]);
-          }
-        }
-      }
-    }
-    // combine the two half-warps (same running max) and the lanes' partial sums
-#pragma unroll
-    for (int d = 0; d < 8; ++d) {
-      acc_a[d] += __shfl_xor_sync(0xffffffffu, acc_a[d], 16);
-      acc_b[d] += __shfl_xor_sync(0xffffffffu, acc_b[d], 16);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      l_a += __shfl_xor_sync(0xffffffffu, l_a, o);
-      l_b += __shfl_xor_sync(0xffffffffu, l_b, o);
-    }
+  if (warp == ATTN_CONSUMER_WARPS) {
+    // ------------------------------------------------------------ page producer
     if (lane == 0) {
-      sm_m[warp][0] = m_a;
-      sm_m[warp][1] = m_b;
-      sm_l[warp][0] = l_a;
-      sm_l[warp][1] = l_b;
-    }
-    if (lane < 16) {
-#pragma unroll
-      for (int d = 0; d < 8; ++d) {
-        sm_acc[warp][0][d0 + d] = acc_a[d];
-        sm_acc[warp][1][d0 + d] = acc_b[d];
-      }
-    }
-    __syncthreads();
-    // merge the 4 warps: thread tid owns dim tid of both heads
-    float M[2], L[2], O[2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      float mx = -INFINITY;
-      for (int w = 0; w < 4; ++w) mx = fmaxf(mx, sm_m[w][h]);
-      float ls = 0.f, os = 0.f;
-      for (int w = 0; w < 4; ++w) {
-        if (sm_m[w][h] == -INFINITY) continue;
-        const float f = expf(sm_m[w][h] - mx);
-        ls += sm_l[w][h] * f;
-        os += sm_acc[w][h][tid] * f;
-      }
-      M[h] = mx;
-      L[h] = ls;
-      O[h] = os;
-    }
-    const size_t obase = static_cast<size_t>(r) * a.q_ld + (2 * g) * 128 + tid;
-    if (nch == 1) {
-      a.out[obase] = __float2half_rn(O[0] / L[0]);
-      a.out[obase + 128] = __float2half_rn(O[1] / L[1]);
-    } else {
-      const size_t pidx = (static_cast<size_t>(r) * nkv + g) * a.max_chunks;
-      float* part = a.ws + (pidx + c) * ATTN_PART_FLOATS;
-      if (tid == 0) {
-        part[0] = M[0];
-        part[1] = M[1];
-        part[2] = L[0];
-        part[3] = L[1];
-      }
-      part[4 + tid] = O[0];
-      part[4 + 128 + tid] = O[1];
-      __threadfence();
-      __syncthreads();
-      if (tid == 0) {
-        const int old = atomicAdd(a.counters + r * nkv + g, 1);
-        sh_last = (old == nch - 1) ? 1 : 0;
-      }
-      __syncthreads();
-      if (sh_last) {
-        __threadfence();
-        const float* parts = a.ws + pidx * ATTN_PART_FLOATS;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          float mx = -INFINITY;
-          for (int cc = 0; cc < nch; ++cc) mx = fmaxf(mx, __ldcg(parts + cc * ATTN_PART_FLOATS + h));
-          float ls = 0.f, os = 0.f;
-          for (int cc = 0; cc < nch; ++cc) {
-            const float mc = __ldcg(parts + cc * ATTN_PART_FLOATS + h);
-            if (mc == -INFINITY) continue;
-            const float f = expf(mc - mx);
-            ls += __ldcg(parts + cc * ATTN_PART_FLOATS + 2 + h) * f;
-            os += __ldcg(parts + cc * ATTN_PART_FLOATS + 4 + h * 128 + tid) * f;
+      long long gs = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < U && ok; u += gridDim.x) {
+        const AttnUnit t = attn_unit(a, prefix, u);
+        const int slot = a.row_slot[t.r];
+        const int pages = (t.len + 63) >> 6;
+        for (int st = t.s0; st < t.s1; ++st, ++gs) {
+          const int sl = static_cast<int>(gs % ATTN_STAGES);
+          if (!mbar_wait(&empty_bar[sl], static_cast<uint32_t>(((gs / ATTN_STAGES) & 1) ^ 1), &abort_flag,
+                         a.status, 0x601)) {
+            ok = false;
+            break;
           }
-          a.out[obase + h * 128] = __float2half_rn(os / ls);
+          const int p0 = st * 2;
+          const int np = min(2, pages - p0);
+          uint8_t* buf = smem + static_cast<size_t>(sl) * ATTN_STAGE_BYTES;
+          mbar_arrive_expect_tx(&full_bar[sl], static_cast<uint32_t>(np) * 2u * ATTN_PAGE_BYTES);
+          for (int pp = 0; pp < np; ++pp) {
+            const size_t ko = kv_elem_offset(a.kv, slot, (p0 + pp) * 64, a.layer, 0, t.g);
+            const size_t vo = kv_elem_offset(a.kv, slot, (p0 + pp) * 64, a.layer, 1, t.g);
+            bulk_load(buf + pp * ATTN_PAGE_BYTES, a.kv.pool + ko, ATTN_PAGE_BYTES, &full_bar[sl]);
+            bulk_load(buf + (2 + pp) * ATTN_PAGE_BYTES, a.kv.pool + vo, ATTN_PAGE_BYTES, &full_bar[sl]);
+          }
         }
-        if (tid == 0) a.counters[r * nkv + g] = 0;
       }
+      for (long long j = gs > ATTN_STAGES ? gs - ATTN_STAGES : 0; j < gs; ++j)  // drain
+        mbar_wait(&full_bar[j % ATTN_STAGES], static_cast<uint32_t>((j / ATTN_STAGES) & 1), nullptr,
+                  a.status, 0x602);
     }
-    __syncthreads();
+  } else {
+    // ------------------------------------------------------------ consumers
+    long long gs = 0;
+    for (int u = blockIdx.x; u < U; u += gridDim.x) {
+      const AttnUnit t = attn_unit(a, prefix, u);
+      const __half* qr = a.q + static_cast<size_t>(t.r) * a.q_ld;
+      float qa[4], qb[4];
+      {
+        const float2 a01 = __half22float2(*reinterpret_cast<const __half2*>(qr + (2 * t.g) * 128 + 4 * lane));
+        const float2 a23 = __half22float2(*reinterpret_cast<const __half2*>(qr + (2 * t.g) * 128 + 4 * lane + 2));
+        const float2 b01 = __half22float2(*reinterpret_cast<const __half2*>(qr + (2 * t.g + 1) * 128 + 4 * lane));
+        const float2 b23 = __half22float2(*reinterpret_cast<const __half2*>(qr + (2 * t.g + 1) * 128 + 4 * lane + 2));
+        qa[0] = a01.x; qa[1] = a01.y; qa[2] = a23.x; qa[3] = a23.y;
+        qb[0] = b01.x; qb[1] = b01.y; qb[2] = b23.x; qb[3] = b23.y;
+      }
+      // lanes 0-15 carry head 2g's running max / partial sum, lanes 16-31 head 2g+1's
+      float m = -INFINITY, l = 0.f;
+      float acc_a[4] = {0.f, 0.f, 0.f, 0.f}, acc_b[4] = {0.f, 0.f, 0.f, 0.f};
+      bool ok = true;
+      for (int st = t.s0; st < t.s1; ++st, ++gs) {
+        const int sl = static_cast<int>(gs % ATTN_STAGES);
+        if (!mbar_wait_warp(&full_bar[sl], static_cast<uint32_t>((gs / ATTN_STAGES) & 1), &abort_flag,
+                            a.status, 0x603)) {
+          ok = false;
+          break;
+        }
+        const int tw = st * 128 + warp * 16;  // first position of this warp's 16
+        if (tw < t.len) {
+          const uint8_t* buf = smem + static_cast<size_t>(sl) * ATTN_STAGE_BYTES;
+          const __half* kbuf = reinterpret_cast<const __half*>(buf) + warp * 16 * 128;
+          const __half* vbuf = reinterpret_cast<const __half*>(buf + 2 * ATTN_PAGE_BYTES) + warp * 16 * 128;
+          float v[32];
+#pragma unroll
+          for (int p = 0; p < 16; ++p) {
+            const uint2 kr = *reinterpret_cast<const uint2*>(kbuf + p * 128 + 4 * lane);
+            const float2 k01 = __half22float2(*reinterpret_cast<const __half2*>(&kr.x));
+            const float2 k23 = __half22float2(*reinterpret_cast<const __half2*>(&kr.y));
+            v[p] = fmaf(qa[3], k23.y, fmaf(qa[2], k23.x, fmaf(qa[1], k01.y, qa[0] * k01.x)));
+            v[16 + p] = fmaf(qb[3], k23.y, fmaf(qb[2], k23.x, fmaf(qb[1], k01.y, qb[0] * k01.x)));
+          }
+          // transposing butterfly: lane j ends with the full dot product of value j
+#pragma unroll
+          for (int o = 16; o >= 1; o >>= 1) {
+            const bool upper = (lane & o) != 0;
+#pragma unroll
+            for (int j = 0; j < o; ++j) {
+              const float send = upper ? v[j] : v[j + o];
+              const float keep = upper ? v[j + o] : v[j];
+              v[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+            }
+          }
+          const bool valid = tw + (lane & 15) < t.len;
+          const float s = valid ? v[0] * a.scale : -INFINITY;
+          float bm = s;
+#pragma unroll
+          for (int o = 8; o >= 1; o >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
+          const float mn = fmaxf(m, bm);
+          const float corr = (m == mn) ? 1.0f : expf(m - mn);
+          const float p = valid ? expf(s - mn) : 0.0f;
+          l = l * corr + p;
+          m = mn;
+          sm_p[warp][lane] = p;
+          const float ca = __shfl_sync(0xffffffffu, corr, 0);
+          const float cb = __shfl_sync(0xffffffffu, corr, 16);
+#pragma unroll
+          for (int d = 0; d < 4; ++d) {
+            acc_a[d] *= ca;
+            acc_b[d] *= cb;
+          }
+          __syncwarp();
+          const int nvalid = min(16, t.len - tw);
+#pragma unroll
+          for (int p4 = 0; p4 < 4; ++p4) {
+            const float4 pa4 = *reinterpret_cast<const float4*>(&sm_p[warp][4 * p4]);
+            const float4 pb4 = *reinterpret_cast<const float4*>(&sm_p[warp][16 + 4 * p4]);
+            const float pa[4] = {pa4.x, pa4.y, pa4.z, pa4.w};
+            const float pb[4] = {pb4.x, pb4.y, pb4.z, pb4.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int pp = 4 * p4 + q;
+              if (pp < nvalid) {
+                const uint2 vr = *reinterpret_cast<const uint2*>(vbuf + pp * 128 + 4 * lane);
+                const float2 v01 = __half22float2(*reinterpret_cast<const __half2*>(&vr.x));
+                const float2 v23 = __half22float2(*reinterpret_cast<const __half2*>(&vr.y));
+                acc_a[0] = fmaf(pa[q], v01.x, acc_a[0]);
+                acc_a[1] = fmaf(pa[q], v01.y, acc_a[1]);
+                acc_a[2] = fmaf(pa[q], v23.x, acc_a[2]);
+                acc_a[3] = fmaf(pa[q], v23.y, acc_a[3]);
+                acc_b[0] = fmaf(pb[q], v01.x, acc_b[0]);
+                acc_b[1] = fmaf(pb[q], v01.y, acc_b[1]);
+                acc_b[2] = fmaf(pb[q], v23.x, acc_b[2]);
+                acc_b[3] = fmaf(pb[q], v23.y, acc_b[3]);
+              }
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty_bar[sl]);
+      }
+      if (!ok) break;
+      // ---- merge the 8 warps (sum over the 16 lanes of each head group first)
+#pragma unroll
+      for (int o = 8; o >= 1; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+      if (lane == 0 || lane == 16) {
+        sm_m[warp][lane >> 4] = m;
+        sm_l[warp][lane >> 4] = l;
+      }
+      *reinterpret_cast<float4*>(&sm_acc[warp][0][4 * lane]) = make_float4(acc_a[0], acc_a[1], acc_a[2], acc_a[3]);
+      *reinterpret_cast<float4*>(&sm_acc[warp][1][4 * lane]) = make_float4(acc_b[0], acc_b[1], acc_b[2], acc_b[3]);
+      named_bar_sync(1, ATTN_CONSUMER_WARPS * 32);
+      const int h = tid >> 7, dd = tid & 127;
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < ATTN_CONSUMER_WARPS; ++w) M = fmaxf(M, sm_m[w][h]);
+      float Ls = 0.f, Os = 0.f;
+#pragma unroll
+      for (int w = 0; w < ATTN_CONSUMER_WARPS; ++w) {
+        const float mw = sm_m[w][h];
+        if (mw == -INFINITY) continue;
+        const float f = expf(mw - M);
+        Ls += sm_l[w][h] * f;
+        Os += sm_acc[w][h][dd] * f;
+      }
+      const size_t obase = static_cast<size_t>(t.r) * a.q_ld + (2 * t.g + h) * 128 + dd;
+      if (t.nch == 1) {
+        a.out[obase] = __float2half_rn(Os / Ls);
+      } else {
+        const size_t pidx = (static_cast<size_t>(t.r) * nkv + t.g) * ATTN_ROW_CHUNKS;
+        float* part = a.ws + (pidx + t.c) * ATTN_PART_FLOATS;
+        if (dd == 0) {
+          part[h] = M;
+          part[2 + h] = Ls;
+        }
+        part[4 + h * 128 + dd] = Os;
+        __threadfence();
+        named_bar_sync(1, ATTN_CONSUMER_WARPS * 32);
+        if (tid == 0) {
+          const int old = atomicAdd(a.counters + t.r * nkv + t.g, 1);
+          sh_last = (old == t.nch - 1) ? 1 : 0;
+        }
+        named_bar_sync(1, ATTN_CONSUMER_WARPS * 32);
+        if (sh_last) {
+          __threadfence();
+          const float* parts = a.ws + pidx * ATTN_PART_FLOATS;
+          float mc[ATTN_ROW_CHUNKS], lc[ATTN_ROW_CHUNKS], oc[ATTN_ROW_CHUNKS];
+#pragma unroll
+          for (int cc = 0; cc < ATTN_ROW_CHUNKS; ++cc) {  // independent loads, all in flight
+            if (cc < t.nch) {
+              mc[cc] = __ldcg(parts + cc * ATTN_PART_FLOATS + h);
+              lc[cc] = __ldcg(parts + cc * ATTN_PART_FLOATS + 2 + h);
+              oc[cc] = __ldcg(parts + cc * ATTN_PART_FLOATS + 4 + h * 128 + dd);
+            } else {
+              mc[cc] = -INFINITY;
+              lc[cc] = 0.f;
+              oc[cc] = 0.f;
+            }
+          }
+          float mx = -INFINITY;
+#pragma unroll
+          for (int cc = 0; cc < ATTN_ROW_CHUNKS; ++cc) mx = fmaxf(mx, mc[cc]);
+          float ls = 0.f, os = 0.f;
+#pragma unroll
+          for (int cc = 0; cc < ATTN_ROW_CHUNKS; ++cc) {
+            if (mc[cc] == -INFINITY) continue;
+            const float f = expf(mc[cc] - mx);
+            ls += lc[cc] * f;
+            os += oc[cc] * f;
+          }
+          a.out[obase] = __float2half_rn(os / ls);
+          if (tid == 0) a.counters[t.r * nkv + t.g] = 0;
+        }
+      }
+      named_bar_sync(1, ATTN_CONSUMER_WARPS * 32);  // smem merge buffers are reused
+    }
   }
 }
 

@@ -86,7 +86,18 @@ struct GemmArgs {
   float* ws;
   int* counters;
   uint32_t* status;
+  // optional latency trace: per CTA GEMM_TRACE_SLOTS %globaltimer stamps (diagnostics)
+  unsigned long long* trace;
 };
+
+constexpr int GEMM_TRACE_SLOTS = 12;
+// trace slots: 0 entry, 1 setup done, 2 first W issued, 3 first X issued, 4 first W seen by
+// the A builders, 5 first A stage built, 6 first MMA issued, 7 last MMA issued, 8 first
+// accumulator seen by the epilogue, 9 last tile stored / partial written, 10 split fixup done,
+// 11 exit
+__device__ __forceinline__ void trace_stamp(const GemmArgs& a, int slot) {
+  if (a.trace != nullptr) a.trace[blockIdx.x * GEMM_TRACE_SLOTS + slot] = globaltimer();
+}
 
 __device__ __forceinline__ int cta_of_unit(long long x, long long units, long long grid) {
   // CTA c owns units [c*U/G, (c+1)*U/G); the owner of x is the largest c with c*U/G <= x.
@@ -295,6 +306,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const int KB = a.kblocks;
 
   if (threadIdx.x == 0) {
+    trace_stamp(a, 0);
     for (int i = 0; i < S; ++i) {
       mbar_init(&wfull_bar[i], 1);
       mbar_init(&xfull_bar[i], 1);
@@ -322,6 +334,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   tc_fence_after();
   griddep_launch_dependents();
   const uint32_t tmem_base = tmem_base_sh;
+  if (threadIdx.x == 0) trace_stamp(a, 1);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -350,8 +363,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       };
       // weights do not depend on the previous kernel: stream the first stages at once
       for (long long i = 0; i < pre; ++i) issue_w(i);
+      trace_stamp(a, 2);
       griddep_wait();
       for (long long i = 0; i < pre; ++i) issue_x(i);
+      trace_stamp(a, 3);
       long long i = pre;
       for (; i < n; ++i) {
         const int s = static_cast<int>(i % S);
@@ -396,6 +411,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                        0x203))
           break;
         tc_fence_after();
+        if (i == 0) trace_stamp(a, 6);
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(d) * DCOLS;
         const uint32_t a_tmem = tmem_base + A_COLS0 + static_cast<uint32_t>(ast) * ACOLS;
         const uint32_t x_base = smem_u32(smem + static_cast<size_t>(s) * stage_bytes + 16384);
@@ -412,6 +428,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         issued_any = true;
       }
       if (issued_any) {  // all MMAs must retire before the TMEM is released
+        trace_stamp(a, 7);
         umma_commit(&done_bar);
         mbar_wait(&done_bar, 0, nullptr, a.status, 0x204);
       }
@@ -433,6 +450,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                           a.status, 0x302))
         break;
       tc_fence_after();
+      if (i == 0 && threadIdx.x == 128) trace_stamp(a, 4);
       const int T = static_cast<int>(u / KB);
       const int mt = T / a.n_tiles;
       if (INT8 && mt != cur_mt) {
@@ -471,6 +489,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&afull_bar[ast]);
+      if (i == 0 && threadIdx.x == 128) trace_stamp(a, 5);
     }
   } else if (warp >= 8) {
     // ------------------------------------------------------------ epilogue
@@ -498,6 +517,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       if (!got) break;
       mbar_try_wait(&dfull_bar[d], static_cast<uint32_t>((seg >> 1) & 1));
       tc_fence_after();
+      if (seg == 0 && e == 0) trace_stamp(a, 8);
       const int mt = T / a.n_tiles, nt = T % a.n_tiles;
       const uint32_t dt = tmem_base + lane_base + static_cast<uint32_t>(d) * DCOLS;
       if (kb0 == 0 && kb1 == KB) {
@@ -513,6 +533,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&dfree_bar[d]);
+        if (e == 0) trace_stamp(a, 9);
       } else {
         // split tile: partial [seg][row][n_tile] f32; the last CTA adds them in seg order
         const int first_cta = cta_of_unit(static_cast<long long>(T) * KB, U, G);
@@ -535,6 +556,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&dfree_bar[d]);
+        if (e == 0) trace_stamp(a, 9);
         __threadfence();
         named_bar_sync(1, 128);
         if (e == 0) {
@@ -587,7 +609,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             }
             epilogue_chunk<EPI>(a, es, mt, nt, c0, e, v);
           }
-          if (e == 0) a.counters[T] = 0;
+          if (e == 0) {
+            a.counters[T] = 0;
+            trace_stamp(a, 10);
+          }
         }
         named_bar_sync(1, 128);
       }
@@ -599,6 +624,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 2) tmem_dealloc(tmem_base, GEMM_TMEM_COLS);
+  if (threadIdx.x == 0) trace_stamp(a, 11);
 }
 
 }  // namespace qasr

@@ -148,6 +148,8 @@ static cudaError_t init_kernel_attrs(std::string* err) {
     e = e ? e : gemm_set_attr<true, EPI_RESID>(d);
     e = e ? e : gemm_set_attr<true, EPI_SILU>(d);
     e = e ? e : gemm_set_attr<true, EPI_QKV>(d);
+    e = e ? e : cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(attn_smem_bytes(ATTN_MAX_ROWS)));
     result = e;
   });
   if (result != cudaSuccess && err) *err = std::string("kernel attribute setup: ") + cudaGetErrorString(result);
@@ -413,8 +415,8 @@ qasr_status launch_attention(qasr_ctx* c, int layer, int rows, const int* rs, co
   a.counters = c->attn_cnt;
   a.max_chunks = c->attn_max_chunks;
   a.status = c->status;
-  const int grid = c->num_sms * 4;
-  CK(launch_k(attention_kernel, dim3(grid), dim3(ATTN_THREADS), (rows + 1) * sizeof(int), c->stream, true, a),
+  CK(launch_k(attention_kernel, dim3(c->num_sms), dim3(ATTN_THREADS), attn_smem_bytes(rows), c->stream, true,
+              a),
      "attention launch");
   return QASR_OK;
 }
@@ -1092,6 +1094,14 @@ static qasr_status probe_err(char* err, int errlen, qasr_status s, const std::st
 qasr_status qasr_kernel_gemm(int device, void* stream, int weight_format, const void* w,
                              const uint16_t* scale, int n_out, int k, const uint16_t* x, int ldx,
                              int rows, uint16_t* out, int ldo, int accumulate, char* err, int errlen) {
+  return qasr_kernel_gemm_traced(device, stream, weight_format, w, scale, n_out, k, x, ldx, rows, out, ldo,
+                                 accumulate, nullptr, nullptr, err, errlen);
+}
+
+qasr_status qasr_kernel_gemm_traced(int device, void* stream, int weight_format, const void* w,
+                                    const uint16_t* scale, int n_out, int k, const uint16_t* x, int ldx,
+                                    int rows, uint16_t* out, int ldo, int accumulate,
+                                    unsigned long long* trace, int* grid_out, char* err, int errlen) {
   static std::mutex mu;
   static ProbeWs pws[16];
   std::lock_guard<std::mutex> lock(mu);
@@ -1146,6 +1156,8 @@ qasr_status qasr_kernel_gemm(int device, void* stream, int weight_format, const 
   a.ldo = ldo;
   a.ws = P.ws;
   a.counters = P.cnt;
+  a.trace = trace;
+  if (grid_out) *grid_out = s.grid;
   const cudaError_t ce = launch_gemm(L, static_cast<cudaStream_t>(stream), false);
   if (ce != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, cudaGetErrorString(ce));
   return QASR_OK;
@@ -1160,7 +1172,7 @@ qasr_status qasr_kernel_attention(int device, void* stream, const uint16_t* q, i
   static ProbeWs pws[16];
   std::lock_guard<std::mutex> lock(mu);
   if (device < 0 || device >= 16 || !q || !out || !kv_pool || !page_table || !row_slot || !row_pos ||
-      rows <= 0 || rows > 16384 || nkv <= 0 || q_ld != 2 * nkv * 128 || layer < 0 || layer >= layers)
+      rows <= 0 || rows > ATTN_MAX_ROWS || nkv <= 0 || q_ld != 2 * nkv * 128 || layer < 0 || layer >= layers)
     return probe_err(err, errlen, QASR_ERR_INVALID_ARG, "bad attention probe arguments");
   if (cudaSetDevice(device) != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, "cudaSetDevice");
   const int max_chunks = ATTN_ROW_CHUNKS;
@@ -1200,7 +1212,9 @@ qasr_status qasr_kernel_attention(int device, void* stream, const uint16_t* q, i
   a.ws = P.ws;
   a.counters = P.cnt;
   a.max_chunks = max_chunks;
-  const cudaError_t ce = launch_k(attention_kernel, dim3(sms * 4), dim3(ATTN_THREADS), (rows + 1) * sizeof(int),
+  std::string e;
+  if (init_kernel_attrs(&e) != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, e);
+  const cudaError_t ce = launch_k(attention_kernel, dim3(sms), dim3(ATTN_THREADS), attn_smem_bytes(rows),
                                   static_cast<cudaStream_t>(stream), false, a);
   if (ce != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, cudaGetErrorString(ce));
   return QASR_OK;

@@ -70,9 +70,30 @@ def bench_gemm(args, pkg, torch):
 
     med, best = _time(torch, run, args.iters)
     nbytes = wbytes + r * k * 2 + r * n * 2 * (2 if args.accumulate else 1)
-    return {"kernel": "gemm_tc", "fmt": args.fmt, "n_out": n, "k": k, "rows": r, "median_us": med * 1e6,
-            "best_us": best * 1e6, "bytes": nbytes, "gbs": nbytes / med / 1e9,
-            "tflops": 2.0 * n * k * r / med / 1e12}
+    res = {"kernel": "gemm_tc", "fmt": args.fmt, "n_out": n, "k": k, "rows": r, "median_us": med * 1e6,
+           "best_us": best * 1e6, "bytes": nbytes, "gbs": nbytes / med / 1e9,
+           "tflops": 2.0 * n * k * r / med / 1e12}
+    if args.trace:
+        # per-CTA milestones (see GEMM_TRACE_SLOTS): median / max over CTAs, in microseconds
+        # after the earliest CTA entry of the launch
+        trace = torch.zeros((1024, 12), dtype=torch.int64, device="cuda")
+        torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda").zero_()
+        grid = pkg.kernel_gemm_traced(0, st, fmt, w.data_ptr(), sc.data_ptr() if sc is not None else None, n, k,
+                                      x.data_ptr(), k, r, o.data_ptr(), n, trace.data_ptr(), args.accumulate)
+        torch.cuda.synchronize()
+        t = trace[:grid].cpu().numpy().astype(np.float64)
+        t0 = t[:, 0].min()
+        names = ["entry", "setup", "w_issued", "x_issued", "w_seen", "a_built", "mma_first", "mma_last",
+                 "acc_seen", "stored", "fixup_done", "exit"]
+        res["trace_us"] = {}
+        for i, nm in enumerate(names):
+            col = t[:, i]
+            col = col[col > 0]
+            if col.size:
+                res["trace_us"][nm] = [round(float(np.median(col - t0)) / 1e3, 2),
+                                       round(float(np.max(col - t0)) / 1e3, 2)]
+        res["grid"] = grid
+    return res
 
 
 def _kv_setup(pkg, torch, args, rng):
@@ -145,6 +166,7 @@ def main(argv=None):
     g.add_argument("--k", type=int, default=2048)
     g.add_argument("--rows", type=int, default=32)
     g.add_argument("--accumulate", action="store_true")
+    g.add_argument("--trace", action="store_true")
     for name in ("attention", "append"):
         a = sub.add_parser(name)
         a.add_argument("--slots", type=int, default=512)
