@@ -9,15 +9,19 @@
 // activation rows (decode slots or prefill rows) are N (16..128 per tile), so a decode
 // step with B slots reads every weight byte once, whatever B is.
 //
-// Roles of the 384-thread CTA (one persistent CTA per SM):
-//   warp 0      TMA producer: W tile (128 rows x 128 B) + X tile(s) per k-block
-//   warp 1      UMMA issuer:  tcgen05.mma kind::f16, A from TMEM, B from smem
+// Roles of the CTA (one persistent CTA per SM):
+//   warp 0      producer: one 16 KB bulk copy per weight unit (128 rows x 128 B, stored
+//               pre-tiled and pre-swizzled in HBM) + TMA of the activation tile(s)
+//   warp 1      UMMA issuer: tcgen05.mma kind::f16, f32 accumulators in TMEM
 //   warp 2      TMEM allocator (512 columns)
-//   warps 4-7   "A" builders: read one W row each from the swizzled smem tile,
-//               dequantise int8 -> f16 as f16(f32(q) * scale) with one correctly rounded
-//               f16 multiply (the exact value dequant_i8 produces, src/weights.rs:372-385),
-//               store the row into TMEM as the MMA's A operand
-//   warps 8-11  epilogue: TMEM accumulators -> fused epilogue (see EpiKind)
+//   f16 weights: the weight tile in shared memory already is the canonical K-major
+//               128-byte-swizzled operand, so A is read straight from shared memory.
+//   int8 weights: two warpgroups of "A builders" (warps 4-11) take alternate units:
+//               each thread reads one W row from the swizzled tile, dequantises it as
+//               f16(f32(q) * scale) with one correctly rounded f16 multiply (the exact
+//               value dequant_i8 produces, src/weights.rs:372-385) and stores the row into
+//               TMEM, which the MMA then reads as its A operand.
+//   last 4 warps  epilogue: TMEM accumulators -> fused epilogue (see EpiKind)
 //
 // Work split: the (tile, k-block) units are cut into equal contiguous ranges, one per
 // CTA ("stream-K").  A tile split across CTAs is finished by the CTA that arrives last
@@ -36,7 +40,10 @@ enum EpiKind : int {
   EPI_LOGITS = 4,  // f32 logits (optional) + per-row argmax via 64-bit atomicMax keys
 };
 
-constexpr int GEMM_THREADS = 384;
+constexpr int GEMM_BUILD_GROUPS = 2;  // int8 A-builder warpgroups
+__host__ __device__ constexpr int gemm_threads(bool int8) {
+  return 128 + (int8 ? GEMM_BUILD_GROUPS * 128 : 0) + 128;
+}
 constexpr int GEMM_MAX_STAGES = 8;
 constexpr int GEMM_A_STAGES = 8;  // upper bound; the kernel fits what TMEM allows
 constexpr int GEMM_MAX_NTILE = 128;
@@ -272,8 +279,10 @@ __device__ __forceinline__ void griddep_launch_dependents() {
 
 // ------------------------------------------------------------------ kernel
 template <bool INT8, int EPI>
-__global__ void __launch_bounds__(GEMM_THREADS, 1)
+__global__ void __launch_bounds__(gemm_threads(INT8), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ GemmArgs a) {
+  constexpr int NBG = INT8 ? GEMM_BUILD_GROUPS : 0;  // builder warpgroups
+  constexpr int EPI_WARP0 = 4 + 4 * NBG;
   constexpr int KE = INT8 ? 128 : 64;        // k elements per unit (128 bytes of W row)
   constexpr int ATOMS = INT8 ? 2 : 1;        // 64-element (128-byte) X atoms per unit
   constexpr uint32_t ACOLS = KE / 2;         // TMEM columns of one A stage (2 f16 / column)
@@ -299,6 +308,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const uint32_t A_COLS0 = 2u * DCOLS;
   int SA = static_cast<int>((GEMM_TMEM_COLS - A_COLS0) / ACOLS);
   SA = SA > GEMM_A_STAGES ? GEMM_A_STAGES : SA;
+  if (!INT8) SA = 1;  // unused: A comes from shared memory
 
   const long long U = a.units, G = a.grid;
   const long long ub = static_cast<long long>(blockIdx.x) * U / G;
@@ -404,26 +414,38 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             break;
           tc_fence_after();
         }
-        if (!mbar_wait(&afull_bar[ast], static_cast<uint32_t>((i / SA) & 1), &abort_flag, a.status,
-                       0x202))
-          break;
+        if (INT8) {
+          if (!mbar_wait(&afull_bar[ast], static_cast<uint32_t>((i / SA) & 1), &abort_flag, a.status,
+                         0x202))
+            break;
+        } else {
+          if (!mbar_wait(&wfull_bar[s], static_cast<uint32_t>((i / S) & 1), &abort_flag, a.status,
+                         0x205))
+            break;
+        }
         if (!mbar_wait(&xfull_bar[s], static_cast<uint32_t>((i / S) & 1), &abort_flag, a.status,
                        0x203))
           break;
         tc_fence_after();
         if (i == 0) trace_stamp(a, 6);
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(d) * DCOLS;
-        const uint32_t a_tmem = tmem_base + A_COLS0 + static_cast<uint32_t>(ast) * ACOLS;
-        const uint32_t x_base = smem_u32(smem + static_cast<size_t>(s) * stage_bytes + 16384);
+        const uint32_t w_base = smem_u32(smem + static_cast<size_t>(s) * stage_bytes);
+        const uint32_t x_base = w_base + 16384u;
 #pragma unroll
         for (int kk = 0; kk < KSTEPS; ++kk) {
           const uint32_t b_addr = x_base + static_cast<uint32_t>(kk >> 2) * x_tile_bytes +
                                   static_cast<uint32_t>(kk & 3) * 32u;
-          umma_f16_ts(d_tmem, a_tmem + static_cast<uint32_t>(kk) * 8u, smem_desc_sw128(b_addr),
-                      idesc, (first && kk == 0) ? 0u : 1u);
+          const uint32_t acc = (first && kk == 0) ? 0u : 1u;
+          if constexpr (INT8) {
+            const uint32_t a_tmem = tmem_base + A_COLS0 + static_cast<uint32_t>(ast) * ACOLS;
+            umma_f16_ts(d_tmem, a_tmem + static_cast<uint32_t>(kk) * 8u, smem_desc_sw128(b_addr), idesc, acc);
+          } else {
+            umma_f16_ss(d_tmem, smem_desc_sw128(w_base + static_cast<uint32_t>(kk) * 32u),
+                        smem_desc_sw128(b_addr), idesc, acc);
+          }
         }
         umma_commit(&sfree_bar[s]);
-        umma_commit(&afree_bar[ast]);
+        if (INT8) umma_commit(&afree_bar[ast]);
         if (last) umma_commit(&dfull_bar[d]);
         issued_any = true;
       }
@@ -433,14 +455,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         mbar_wait(&done_bar, 0, nullptr, a.status, 0x204);
       }
     }
-  } else if (warp >= 4 && warp < 8) {
+  } else if (INT8 && warp >= 4 && warp < EPI_WARP0) {
     // ------------------------------------------------------------ A builders
-    const int t = threadIdx.x - 128;  // row of the 128-row tile == TMEM lane
-    const uint32_t lane_base = static_cast<uint32_t>((warp - 4) * 32) << 16;
-    long long i = 0;
+    const int grp = (warp - 4) >> 2;                // this warpgroup builds units grp, grp+NBG, ...
+    const int t = (threadIdx.x - 128) & 127;        // row of the 128-row tile == TMEM lane
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    long long i = grp;
     int cur_mt = -1;
     __half2 sc2 = __floats2half2_rn(1.0f, 1.0f);
-    for (long long u = ub; u < ue; ++u, ++i) {
+    for (long long u = ub + grp; u < ue; u += NBG, i += NBG) {
       const int s = static_cast<int>(i % S);
       const int ast = static_cast<int>(i % SA);
       if (!mbar_wait_warp(&wfull_bar[s], static_cast<uint32_t>((i / S) & 1), &abort_flag, a.status,
@@ -450,7 +473,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                           a.status, 0x302))
         break;
       tc_fence_after();
-      if (i == 0 && threadIdx.x == 128) trace_stamp(a, 4);
+      if (i == 0 && t == 0) trace_stamp(a, 4);
       const int T = static_cast<int>(u / KB);
       const int mt = T / a.n_tiles;
       if (INT8 && mt != cur_mt) {
@@ -489,13 +512,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&afull_bar[ast]);
-      if (i == 0 && threadIdx.x == 128) trace_stamp(a, 5);
+      if (i == 0 && t == 0) trace_stamp(a, 5);
     }
-  } else if (warp >= 8) {
+  } else if (warp >= EPI_WARP0) {
     // ------------------------------------------------------------ epilogue
     griddep_wait();  // outputs, residual inputs and split workspaces belong to the stream order
-    const int e = threadIdx.x - 256;
-    const uint32_t lane_base = static_cast<uint32_t>((warp - 8) * 32) << 16;
+    const int e = threadIdx.x - EPI_WARP0 * 32;
+    const uint32_t lane_base = static_cast<uint32_t>((warp - EPI_WARP0) * 32) << 16;
     long long seg = -1;
     long long u = ub;
     while (u < ue) {
@@ -571,16 +594,18 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             float4 acc[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+            // SEGU segments per round: SEGU * 4 independent 16-byte loads in flight
+            constexpr int SEGU = INT8 ? 2 : 4;  // the int8 CTA has more threads: fewer registers
             int sg = 0;
-            for (; sg + 4 <= nseg; sg += 4) {  // 16 independent 16-byte loads in flight
-              float4 p[4][4];
+            for (; sg + SEGU <= nseg; sg += SEGU) {
+              float4 p[SEGU][4];
 #pragma unroll
-              for (int q = 0; q < 4; ++q)
+              for (int q = 0; q < SEGU; ++q)
 #pragma unroll
                 for (int j = 0; j < 4; ++j)
                   p[q][j] = __ldcg(reinterpret_cast<const float4*>(rowp + (sg + q) * tile_elems + c0 + 4 * j));
 #pragma unroll
-              for (int q = 0; q < 4; ++q)
+              for (int q = 0; q < SEGU; ++q)
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                   acc[j].x += p[q][j].x;

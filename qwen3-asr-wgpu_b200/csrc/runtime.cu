@@ -194,7 +194,7 @@ static GemmShape gemm_shape(int n_out, int k, bool int8, int rows, int num_sms) 
 }
 
 static cudaError_t launch_gemm(const GemmLaunch& L, cudaStream_t st, bool pdl) {
-  dim3 grid(L.grid), block(GEMM_THREADS);
+  dim3 grid(L.grid), block(gemm_threads(L.int8));
 #define QASR_GEMM_CASE(I8, EPI)                                                          \
   if (L.int8 == I8 && L.epi == EPI)                                                      \
     return launch_k(gemm_tc_kernel<I8, EPI>, grid, block, L.smem, st, pdl, L.tmx, L.args);
