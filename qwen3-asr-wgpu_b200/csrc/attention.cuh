@@ -156,16 +156,15 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
   if (warp == ATTN_CONSUMER_WARPS) {
     // ------------------------------------------------------------ page producer
     if (lane == 0) {
-      long long gs = 0;
+      int gs = 0, sl = 0;
+      uint32_t ph = 0;  // (gs / ATTN_STAGES) & 1, kept incrementally
       bool ok = true;
       for (int u = blockIdx.x; u < U && ok; u += gridDim.x) {
         const AttnUnit t = attn_unit(a, prefix, u);
         const int slot = a.row_slot[t.r];
         const int pages = (t.len + 63) >> 6;
-        for (int st = t.s0; st < t.s1; ++st, ++gs) {
-          const int sl = static_cast<int>(gs % ATTN_STAGES);
-          if (!mbar_wait(&empty_bar[sl], static_cast<uint32_t>(((gs / ATTN_STAGES) & 1) ^ 1), &abort_flag,
-                         a.status, 0x601)) {
+        for (int st = t.s0; st < t.s1; ++st) {
+          if (!mbar_wait(&empty_bar[sl], ph ^ 1u, &abort_flag, a.status, 0x601)) {
             ok = false;
             break;
           }
@@ -179,15 +178,21 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
             bulk_load(buf + pp * ATTN_PAGE_BYTES, a.kv.pool + ko, ATTN_PAGE_BYTES, &full_bar[sl]);
             bulk_load(buf + (2 + pp) * ATTN_PAGE_BYTES, a.kv.pool + vo, ATTN_PAGE_BYTES, &full_bar[sl]);
           }
+          ++gs;
+          if (++sl == ATTN_STAGES) {
+            sl = 0;
+            ph ^= 1u;
+          }
         }
       }
-      for (long long j = gs > ATTN_STAGES ? gs - ATTN_STAGES : 0; j < gs; ++j)  // drain
+      for (int j = gs > ATTN_STAGES ? gs - ATTN_STAGES : 0; j < gs; ++j)  // drain
         mbar_wait(&full_bar[j % ATTN_STAGES], static_cast<uint32_t>((j / ATTN_STAGES) & 1), nullptr,
                   a.status, 0x602);
     }
   } else {
     // ------------------------------------------------------------ consumers
-    long long gs = 0;
+    int sl = 0;
+    uint32_t ph = 0;
     for (int u = blockIdx.x; u < U; u += gridDim.x) {
       const AttnUnit t = attn_unit(a, prefix, u);
       const __half* qr = a.q + static_cast<size_t>(t.r) * a.q_ld;
@@ -204,10 +209,8 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
       float m = -INFINITY, l = 0.f;
       float acc_a[4] = {0.f, 0.f, 0.f, 0.f}, acc_b[4] = {0.f, 0.f, 0.f, 0.f};
       bool ok = true;
-      for (int st = t.s0; st < t.s1; ++st, ++gs) {
-        const int sl = static_cast<int>(gs % ATTN_STAGES);
-        if (!mbar_wait_warp(&full_bar[sl], static_cast<uint32_t>((gs / ATTN_STAGES) & 1), &abort_flag,
-                            a.status, 0x603)) {
+      for (int st = t.s0; st < t.s1; ++st) {
+        if (!mbar_wait_warp(&full_bar[sl], ph, &abort_flag, a.status, 0x603)) {
           ok = false;
           break;
         }
@@ -283,6 +286,10 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty_bar[sl]);
+        if (++sl == ATTN_STAGES) {
+          sl = 0;
+          ph ^= 1u;
+        }
       }
       if (!ok) break;
       // ---- merge the 8 warps (sum over the 16 lanes of each head group first)

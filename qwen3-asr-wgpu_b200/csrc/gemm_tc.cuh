@@ -278,6 +278,27 @@ __device__ __forceinline__ void griddep_launch_dependents() {
 }
 
 // ------------------------------------------------------------------ kernel
+// Position in the (tile, k-block) unit order, advanced without divisions (the
+// single-thread producer / MMA loops must not spend hundreds of cycles per unit).
+struct UnitCursor {
+  int kb, mt, nt, KB, NT;
+  __device__ __forceinline__ UnitCursor(int u, int KB_, int NT_) : KB(KB_), NT(NT_) {
+    const int T = u / KB_;
+    kb = u - T * KB_;
+    mt = T / NT_;
+    nt = T - mt * NT_;
+  }
+  __device__ __forceinline__ void advance() {
+    if (++kb == KB) {
+      kb = 0;
+      if (++nt == NT) {
+        nt = 0;
+        ++mt;
+      }
+    }
+  }
+};
+
 template <bool INT8, int EPI>
 __global__ void __launch_bounds__(gemm_threads(INT8), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ GemmArgs a) {
@@ -349,87 +370,89 @@ __global__ void __launch_bounds__(gemm_threads(INT8), 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      const long long n = ue - ub;
-      const long long pre = n < S ? n : S;
-      auto issue_w = [&](long long i) {
-        const long long u = ub + i;
-        const int T = static_cast<int>(u / KB), kb = static_cast<int>(u % KB);
-        const int mt = T / a.n_tiles;
-        uint8_t* st = smem + static_cast<size_t>(i % S) * stage_bytes;
-        uint64_t* bar = &wfull_bar[i % S];
+      const int n = static_cast<int>(ue - ub);
+      const int pre = n < S ? n : S;
+      UnitCursor cw(static_cast<int>(ub), KB, a.n_tiles), cx = cw;
+      auto issue_w = [&](int st, const UnitCursor& c) {
+        uint64_t* bar = &wfull_bar[st];
         mbar_arrive_expect_tx(bar, 16384u);
-        bulk_load(st, a.w_tiles + (static_cast<size_t>(mt) * KB + kb) * 16384, 16384u, bar);
+        bulk_load(smem + static_cast<size_t>(st) * stage_bytes,
+                  a.w_tiles + (static_cast<size_t>(c.mt) * KB + c.kb) * 16384, 16384u, bar);
       };
-      auto issue_x = [&](long long i) {
-        const long long u = ub + i;
-        const int T = static_cast<int>(u / KB), kb = static_cast<int>(u % KB);
-        const int nt = T % a.n_tiles;
-        uint8_t* st = smem + static_cast<size_t>(i % S) * stage_bytes + 16384;
-        uint64_t* bar = &xfull_bar[i % S];
+      auto issue_x = [&](int st, const UnitCursor& c) {
+        uint64_t* bar = &xfull_bar[st];
+        uint8_t* dst = smem + static_cast<size_t>(st) * stage_bytes + 16384;
         mbar_arrive_expect_tx(bar, ATOMS * x_tile_bytes);
 #pragma unroll
         for (int at = 0; at < ATOMS; ++at)
-          tma_load_2d(st + at * x_tile_bytes, &tm_x, bar, kb * KE + at * 64, nt * a.n_tile);
+          tma_load_2d(dst + at * x_tile_bytes, &tm_x, bar, c.kb * KE + at * 64, c.nt * a.n_tile);
       };
       // weights do not depend on the previous kernel: stream the first stages at once
-      for (long long i = 0; i < pre; ++i) issue_w(i);
+      for (int i = 0; i < pre; ++i) {
+        issue_w(i, cw);
+        cw.advance();
+      }
       trace_stamp(a, 2);
       griddep_wait();
-      for (long long i = 0; i < pre; ++i) issue_x(i);
-      trace_stamp(a, 3);
-      long long i = pre;
-      for (; i < n; ++i) {
-        const int s = static_cast<int>(i % S);
-        if (!mbar_wait(&sfree_bar[s], static_cast<uint32_t>(((i / S) & 1) ^ 1), &abort_flag, a.status,
-                       0x101))
-          break;
-        issue_w(i);
-        issue_x(i);
+      for (int i = 0; i < pre; ++i) {
+        issue_x(i, cx);
+        cx.advance();
       }
-      // drain: every issued copy lands before the CTA may exit
-      for (long long j = i > S ? i - S : 0; j < i; ++j) {
-        const uint32_t ph = static_cast<uint32_t>((j / S) & 1);
-        mbar_wait(&wfull_bar[j % S], ph, nullptr, a.status, 0x102);
-        mbar_wait(&xfull_bar[j % S], ph, nullptr, a.status, 0x103);
+      trace_stamp(a, 3);
+      int st = pre == S ? 0 : pre;
+      uint32_t ph = pre == S ? 1u : 0u;  // phase index parity of unit i = i / S
+      int i = pre;
+      for (; i < n; ++i) {
+        if (!mbar_wait(&sfree_bar[st], ph ^ 1u, &abort_flag, a.status, 0x101)) break;
+        issue_w(st, cw);
+        issue_x(st, cx);
+        cw.advance();
+        cx.advance();
+        if (++st == S) {
+          st = 0;
+          ph ^= 1u;
+        }
+      }
+      // drain: every issued copy lands before the CTA may exit (slot j last held unit
+      // i_j = the largest issued unit index congruent to j)
+      const int issued = i;
+      for (int j = 0; j < S && j < issued; ++j) {
+        const int il = issued - 1 - ((issued - 1 - j) % S);
+        const uint32_t pj = static_cast<uint32_t>((il / S) & 1);
+        mbar_wait(&wfull_bar[j], pj, nullptr, a.status, 0x102);
+        mbar_wait(&xfull_bar[j], pj, nullptr, a.status, 0x103);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ UMMA issuer
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_f16_m128(static_cast<uint32_t>(a.n_tile));
-      long long i = 0, seg = -1;
-      int d = 0;
+      const int n = static_cast<int>(ue - ub);
+      UnitCursor c(static_cast<int>(ub), KB, a.n_tiles);
+      int st = 0, ast = 0, seg = -1, d = 0;
+      uint32_t ph = 0, aph = 0;
       bool issued_any = false;
-      for (long long u = ub; u < ue; ++u, ++i) {
-        const int kb = static_cast<int>(u % KB);
-        const bool first = (u == ub) || (kb == 0);
-        const bool last = (u == ue - 1) || (kb == KB - 1);
-        const int s = static_cast<int>(i % S);
-        const int ast = static_cast<int>(i % SA);
+      for (int i = 0; i < n; ++i) {
+        const bool first = (i == 0) || (c.kb == 0);
+        const bool last = (i == n - 1) || (c.kb == KB - 1);
         if (first) {
           ++seg;
-          d = static_cast<int>(seg & 1);
+          d = seg & 1;
           if (!mbar_wait(&dfree_bar[d], static_cast<uint32_t>(((seg >> 1) & 1) ^ 1), &abort_flag,
                          a.status, 0x201))
             break;
           tc_fence_after();
         }
         if (INT8) {
-          if (!mbar_wait(&afull_bar[ast], static_cast<uint32_t>((i / SA) & 1), &abort_flag, a.status,
-                         0x202))
-            break;
+          if (!mbar_wait(&afull_bar[ast], aph, &abort_flag, a.status, 0x202)) break;
         } else {
-          if (!mbar_wait(&wfull_bar[s], static_cast<uint32_t>((i / S) & 1), &abort_flag, a.status,
-                         0x205))
-            break;
+          if (!mbar_wait(&wfull_bar[st], ph, &abort_flag, a.status, 0x205)) break;
         }
-        if (!mbar_wait(&xfull_bar[s], static_cast<uint32_t>((i / S) & 1), &abort_flag, a.status,
-                       0x203))
-          break;
+        if (!mbar_wait(&xfull_bar[st], ph, &abort_flag, a.status, 0x203)) break;
         tc_fence_after();
         if (i == 0) trace_stamp(a, 6);
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(d) * DCOLS;
-        const uint32_t w_base = smem_u32(smem + static_cast<size_t>(s) * stage_bytes);
+        const uint32_t w_base = smem_u32(smem + static_cast<size_t>(st) * stage_bytes);
         const uint32_t x_base = w_base + 16384u;
 #pragma unroll
         for (int kk = 0; kk < KSTEPS; ++kk) {
@@ -444,10 +467,19 @@ __global__ void __launch_bounds__(gemm_threads(INT8), 1)
                         smem_desc_sw128(b_addr), idesc, acc);
           }
         }
-        umma_commit(&sfree_bar[s]);
+        umma_commit(&sfree_bar[st]);
         if (INT8) umma_commit(&afree_bar[ast]);
         if (last) umma_commit(&dfull_bar[d]);
         issued_any = true;
+        c.advance();
+        if (++st == S) {
+          st = 0;
+          ph ^= 1u;
+        }
+        if (++ast == SA) {
+          ast = 0;
+          aph ^= 1u;
+        }
       }
       if (issued_any) {  // all MMAs must retire before the TMEM is released
         trace_stamp(a, 7);
@@ -460,28 +492,24 @@ __global__ void __launch_bounds__(gemm_threads(INT8), 1)
     const int grp = (warp - 4) >> 2;                // this warpgroup builds units grp, grp+NBG, ...
     const int t = (threadIdx.x - 128) & 127;        // row of the 128-row tile == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    long long i = grp;
+    const int n = static_cast<int>(ue - ub);
+    UnitCursor cur(static_cast<int>(ub) + grp, KB, a.n_tiles);
+    int st = grp % S, ast = grp % SA;
+    uint32_t ph = static_cast<uint32_t>((grp / S) & 1), aph = static_cast<uint32_t>((grp / SA) & 1);
     int cur_mt = -1;
     __half2 sc2 = __floats2half2_rn(1.0f, 1.0f);
-    for (long long u = ub + grp; u < ue; u += NBG, i += NBG) {
-      const int s = static_cast<int>(i % S);
-      const int ast = static_cast<int>(i % SA);
-      if (!mbar_wait_warp(&wfull_bar[s], static_cast<uint32_t>((i / S) & 1), &abort_flag, a.status,
-                          0x301))
-        break;
-      if (!mbar_wait_warp(&afree_bar[ast], static_cast<uint32_t>(((i / SA) & 1) ^ 1), &abort_flag,
-                          a.status, 0x302))
-        break;
+    for (int i = grp; i < n; i += NBG) {
+      if (!mbar_wait_warp(&wfull_bar[st], ph, &abort_flag, a.status, 0x301)) break;
+      if (!mbar_wait_warp(&afree_bar[ast], aph ^ 1u, &abort_flag, a.status, 0x302)) break;
       tc_fence_after();
       if (i == 0 && t == 0) trace_stamp(a, 4);
-      const int T = static_cast<int>(u / KB);
-      const int mt = T / a.n_tiles;
+      const int mt = cur.mt;
       if (INT8 && mt != cur_mt) {
         const __half sc = a.scale[mt * 128 + t];
         sc2 = __halves2half2(sc, sc);
         cur_mt = mt;
       }
-      const uint8_t* row = smem + static_cast<size_t>(s) * stage_bytes + t * 128;
+      const uint8_t* row = smem + static_cast<size_t>(st) * stage_bytes + t * 128;
       const uint32_t taddr = tmem_base + lane_base + A_COLS0 + static_cast<uint32_t>(ast) * ACOLS;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
@@ -513,22 +541,35 @@ __global__ void __launch_bounds__(gemm_threads(INT8), 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&afull_bar[ast]);
       if (i == 0 && t == 0) trace_stamp(a, 5);
+#pragma unroll
+      for (int q = 0; q < NBG; ++q) cur.advance();
+      st += NBG;
+      if (st >= S) {
+        st -= S;
+        ph ^= 1u;
+      }
+      ast += NBG;
+      if (ast >= SA) {
+        ast -= SA;
+        aph ^= 1u;
+      }
     }
   } else if (warp >= EPI_WARP0) {
     // ------------------------------------------------------------ epilogue
     griddep_wait();  // outputs, residual inputs and split workspaces belong to the stream order
     const int e = threadIdx.x - EPI_WARP0 * 32;
     const uint32_t lane_base = static_cast<uint32_t>((warp - EPI_WARP0) * 32) << 16;
-    long long seg = -1;
-    long long u = ub;
-    while (u < ue) {
-      const int T = static_cast<int>(u / KB);
-      const long long tile_end = static_cast<long long>(T + 1) * KB;
-      const long long seg_end = ue < tile_end ? ue : tile_end;
-      const int kb0 = static_cast<int>(u - static_cast<long long>(T) * KB);
-      const int kb1 = static_cast<int>(seg_end - static_cast<long long>(T) * KB);
+    int seg = -1;
+    int u = static_cast<int>(ub);
+    const int uend = static_cast<int>(ue);
+    while (u < uend) {
+      const int T = u / KB;
+      const int tile_end = (T + 1) * KB;
+      const int seg_end = uend < tile_end ? uend : tile_end;
+      const int kb0 = u - T * KB;
+      const int kb1 = seg_end - T * KB;
       ++seg;
-      const int d = static_cast<int>(seg & 1);
+      const int d = seg & 1;
       if (e == 0)
         es.last_flag = mbar_wait(&dfull_bar[d], static_cast<uint32_t>((seg >> 1) & 1), &abort_flag,
                                  a.status, 0x401)
