@@ -16,13 +16,15 @@
 // most ATTN_ROW_CHUNKS chunks as a function of its own length, so a slot's result does
 // not depend on the other rows of the launch.
 //
-// Persistent CTA per SM: warp 8 streams the pages of the CTA's units, stage after stage,
-// into a 3-deep shared-memory ring with cp.async.bulk (completion counted on mbarriers,
-// no multicast); warps 0-7 each take 16 positions of a stage, lane l holding dims
-// [4l, 4l+4): 32 partial dot products (16 positions x 2 heads) are finished by one
-// 5-round transposing butterfly, the softmax is online per head and warp, the warps
-// merge in shared memory, and a row split into several chunks is merged by the CTA
-// that finishes its last chunk (atomic counter, no waiting), chunks in index order.
+// Persistent CTA per SM: warp 8 streams the pages of the CTA's units (and each unit's q
+// rows, with its first stage), stage after stage, into a 3-deep shared-memory ring with
+// cp.async.bulk (completion counted on mbarriers, no multicast); warps 0-7 each take 16
+// positions of a stage, lane l holding dims [4l, 4l+4): 32 partial dot products
+// (16 positions x 2 heads) are finished by one 5-round transposing butterfly and the
+// softmax is online per head and warp.  At a unit's end the consumer warps drop their
+// state into a double-buffered shared slot and move on; warp 9 merges the 8 warps,
+// stores the output (or the chunk's partial), and the CTA that finishes a row's last
+// chunk merges the chunks in index order (atomic counter, no waiting).
 #pragma once
 #include "device_common.cuh"
 #include "gemm_tc.cuh"  // KvLayout, kv_elem_offset, griddep_*
@@ -30,13 +32,13 @@
 namespace qasr {
 
 constexpr int ATTN_CONSUMER_WARPS = 8;
-constexpr int ATTN_THREADS = (ATTN_CONSUMER_WARPS + 1) * 32;
+constexpr int ATTN_THREADS = (ATTN_CONSUMER_WARPS + 2) * 32;  // + page producer + merger
 constexpr int ATTN_STAGES = 3;
 constexpr int ATTN_PAGE_BYTES = 64 * 128 * 2;            // K or V rows of one page / head
 constexpr int ATTN_STAGE_BYTES = 4 * ATTN_PAGE_BYTES;    // 2 pages x (K + V)
 constexpr int ATTN_PART_FLOATS = 4 + 2 * 128;            // m0, m1, l0, l1, o0[128], o1[128]
 constexpr int ATTN_ROW_CHUNKS = 4;                       // chunks per row (upper bound)
-constexpr int ATTN_MAX_ROWS = 4096;
+constexpr int ATTN_MAX_ROWS = 2048;
 
 __host__ __device__ __forceinline__ int attn_row_stages(int len) { return (len + 127) / 128; }
 __host__ __device__ __forceinline__ int attn_chunk_stages(int len) {
@@ -97,10 +99,12 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
     attention_kernel(const __grid_constant__ AttnArgs a) {
   extern __shared__ __align__(1024) uint8_t attn_dsmem[];
   __shared__ __align__(8) uint64_t full_bar[ATTN_STAGES], empty_bar[ATTN_STAGES];
-  __shared__ float sm_m[ATTN_CONSUMER_WARPS][2], sm_l[ATTN_CONSUMER_WARPS][2];
-  __shared__ __align__(16) float sm_acc[ATTN_CONSUMER_WARPS][2][128];
+  __shared__ __align__(8) uint64_t mfull_bar[2], mfree_bar[2];
+  __shared__ __align__(16) __half sm_q[ATTN_STAGES][256];             // q of heads 2g, 2g+1
+  __shared__ float sm_m[2][ATTN_CONSUMER_WARPS][2], sm_l[2][ATTN_CONSUMER_WARPS][2];
+  __shared__ __align__(16) float sm_acc[2][ATTN_CONSUMER_WARPS][2][128];
   __shared__ __align__(16) float sm_p[ATTN_CONSUMER_WARPS][32];
-  __shared__ int sh_units, sh_last, sh_scan[ATTN_THREADS / 32];
+  __shared__ int sh_units, sh_scan[ATTN_THREADS / 32];
   __shared__ volatile int abort_flag;
 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(attn_dsmem) + 1023) & ~uintptr_t(1023));
@@ -112,6 +116,10 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
     for (int i = 0; i < ATTN_STAGES; ++i) {
       mbar_init(&full_bar[i], 1);
       mbar_init(&empty_bar[i], ATTN_CONSUMER_WARPS);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&mfull_bar[i], ATTN_CONSUMER_WARPS);
+      mbar_init(&mfree_bar[i], 1);
     }
     abort_flag = 0;
     fence_mbar_init();
@@ -171,7 +179,10 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
           const int p0 = st * 2;
           const int np = min(2, pages - p0);
           uint8_t* buf = smem + static_cast<size_t>(sl) * ATTN_STAGE_BYTES;
-          mbar_arrive_expect_tx(&full_bar[sl], static_cast<uint32_t>(np) * 2u * ATTN_PAGE_BYTES);
+          const bool first = st == t.s0;
+          mbar_arrive_expect_tx(&full_bar[sl], static_cast<uint32_t>(np) * 2u * ATTN_PAGE_BYTES + (first ? 512u : 0u));
+          if (first)  // the unit's q rows (heads 2g, 2g+1: 512 contiguous bytes) ride along
+            bulk_load(&sm_q[sl][0], a.q + static_cast<size_t>(t.r) * a.q_ld + 2 * t.g * 128, 512u, &full_bar[sl]);
           for (int pp = 0; pp < np; ++pp) {
             const size_t ko = kv_elem_offset(a.kv, slot, (p0 + pp) * 64, a.layer, 0, t.g);
             const size_t vo = kv_elem_offset(a.kv, slot, (p0 + pp) * 64, a.layer, 1, t.g);
@@ -189,30 +200,146 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
         mbar_wait(&full_bar[j % ATTN_STAGES], static_cast<uint32_t>((j / ATTN_STAGES) & 1), nullptr,
                   a.status, 0x602);
     }
+  } else if (warp == ATTN_CONSUMER_WARPS + 1) {
+    // ------------------------------------------------------------ merger
+    int k = 0;
+    for (int u = blockIdx.x; u < U; u += gridDim.x, ++k) {
+      const AttnUnit t = attn_unit(a, prefix, u);
+      const int b = k & 1;
+      if (!mbar_wait_warp(&mfull_bar[b], static_cast<uint32_t>((k >> 1) & 1), &abort_flag, a.status, 0x604))
+        break;
+      // lane covers dims [4 lane, +4) of both heads; combine the 8 warps
+      float M[2], Ls[2], O[2][4];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float mx = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < ATTN_CONSUMER_WARPS; ++w) mx = fmaxf(mx, sm_m[b][w][h]);
+        float ls = 0.f;
+        float o[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int w = 0; w < ATTN_CONSUMER_WARPS; ++w) {
+          const float mw = sm_m[b][w][h];
+          if (mw == -INFINITY) continue;
+          const float f = expf(mw - mx);
+          ls += sm_l[b][w][h] * f;
+          const float4 v = *reinterpret_cast<const float4*>(&sm_acc[b][w][h][4 * lane]);
+          o[0] += v.x * f;
+          o[1] += v.y * f;
+          o[2] += v.z * f;
+          o[3] += v.w * f;
+        }
+        M[h] = mx;
+        Ls[h] = ls;
+#pragma unroll
+        for (int d = 0; d < 4; ++d) O[h][d] = o[d];
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&mfree_bar[b]);  // state read: the consumers may reuse the buffer
+      __half* outp = a.out + static_cast<size_t>(t.r) * a.q_ld + (2 * t.g) * 128 + 4 * lane;
+      if (t.nch == 1) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float inv = 1.0f / Ls[h];
+          __half2 v01 = __floats2half2_rn(O[h][0] / Ls[h], O[h][1] / Ls[h]);
+          __half2 v23 = __floats2half2_rn(O[h][2] / Ls[h], O[h][3] / Ls[h]);
+          (void)inv;
+          uint2 pk;
+          pk.x = *reinterpret_cast<uint32_t*>(&v01);
+          pk.y = *reinterpret_cast<uint32_t*>(&v23);
+          *reinterpret_cast<uint2*>(outp + h * 128) = pk;
+        }
+      } else {
+        const size_t pidx = (static_cast<size_t>(t.r) * nkv + t.g) * ATTN_ROW_CHUNKS;
+        float* part = a.ws + (pidx + t.c) * ATTN_PART_FLOATS;
+        if (lane == 0) {
+          part[0] = M[0];
+          part[1] = M[1];
+          part[2] = Ls[0];
+          part[3] = Ls[1];
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          __stcg(reinterpret_cast<float4*>(part + 4 + h * 128 + 4 * lane),
+                 make_float4(O[h][0], O[h][1], O[h][2], O[h][3]));
+        __threadfence();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) last = (atomicAdd(a.counters + t.r * nkv + t.g, 1) == t.nch - 1) ? 1 : 0;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+          __threadfence();
+          const float* parts = a.ws + pidx * ATTN_PART_FLOATS;
+          float mc[ATTN_ROW_CHUNKS][2], lc[ATTN_ROW_CHUNKS][2];
+          float4 oc[ATTN_ROW_CHUNKS][2];
+#pragma unroll
+          for (int cc = 0; cc < ATTN_ROW_CHUNKS; ++cc) {  // independent loads, all in flight
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              if (cc < t.nch) {
+                mc[cc][h] = __ldcg(parts + cc * ATTN_PART_FLOATS + h);
+                lc[cc][h] = __ldcg(parts + cc * ATTN_PART_FLOATS + 2 + h);
+                oc[cc][h] = __ldcg(reinterpret_cast<const float4*>(parts + cc * ATTN_PART_FLOATS + 4 + h * 128 + 4 * lane));
+              } else {
+                mc[cc][h] = -INFINITY;
+                lc[cc][h] = 0.f;
+                oc[cc][h] = make_float4(0.f, 0.f, 0.f, 0.f);
+              }
+            }
+          }
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float mx = -INFINITY;
+#pragma unroll
+            for (int cc = 0; cc < ATTN_ROW_CHUNKS; ++cc) mx = fmaxf(mx, mc[cc][h]);
+            float ls = 0.f;
+            float o[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int cc = 0; cc < ATTN_ROW_CHUNKS; ++cc) {
+              if (mc[cc][h] == -INFINITY) continue;
+              const float f = expf(mc[cc][h] - mx);
+              ls += lc[cc][h] * f;
+              o[0] += oc[cc][h].x * f;
+              o[1] += oc[cc][h].y * f;
+              o[2] += oc[cc][h].z * f;
+              o[3] += oc[cc][h].w * f;
+            }
+            __half2 v01 = __floats2half2_rn(o[0] / ls, o[1] / ls);
+            __half2 v23 = __floats2half2_rn(o[2] / ls, o[3] / ls);
+            uint2 pk;
+            pk.x = *reinterpret_cast<uint32_t*>(&v01);
+            pk.y = *reinterpret_cast<uint32_t*>(&v23);
+            *reinterpret_cast<uint2*>(outp + h * 128) = pk;
+          }
+          if (lane == 0) a.counters[t.r * nkv + t.g] = 0;
+        }
+      }
+    }
   } else {
     // ------------------------------------------------------------ consumers
-    int sl = 0;
+    int sl = 0, k = 0;
     uint32_t ph = 0;
-    for (int u = blockIdx.x; u < U; u += gridDim.x) {
+    bool ok = true;
+    for (int u = blockIdx.x; u < U && ok; u += gridDim.x, ++k) {
       const AttnUnit t = attn_unit(a, prefix, u);
-      const __half* qr = a.q + static_cast<size_t>(t.r) * a.q_ld;
       float qa[4], qb[4];
-      {
-        const float2 a01 = __half22float2(*reinterpret_cast<const __half2*>(qr + (2 * t.g) * 128 + 4 * lane));
-        const float2 a23 = __half22float2(*reinterpret_cast<const __half2*>(qr + (2 * t.g) * 128 + 4 * lane + 2));
-        const float2 b01 = __half22float2(*reinterpret_cast<const __half2*>(qr + (2 * t.g + 1) * 128 + 4 * lane));
-        const float2 b23 = __half22float2(*reinterpret_cast<const __half2*>(qr + (2 * t.g + 1) * 128 + 4 * lane + 2));
-        qa[0] = a01.x; qa[1] = a01.y; qa[2] = a23.x; qa[3] = a23.y;
-        qb[0] = b01.x; qb[1] = b01.y; qb[2] = b23.x; qb[3] = b23.y;
-      }
       // lanes 0-15 carry head 2g's running max / partial sum, lanes 16-31 head 2g+1's
       float m = -INFINITY, l = 0.f;
       float acc_a[4] = {0.f, 0.f, 0.f, 0.f}, acc_b[4] = {0.f, 0.f, 0.f, 0.f};
-      bool ok = true;
       for (int st = t.s0; st < t.s1; ++st) {
         if (!mbar_wait_warp(&full_bar[sl], ph, &abort_flag, a.status, 0x603)) {
           ok = false;
           break;
+        }
+        if (st == t.s0) {
+          const uint2 qa2 = *reinterpret_cast<const uint2*>(&sm_q[sl][4 * lane]);
+          const uint2 qb2 = *reinterpret_cast<const uint2*>(&sm_q[sl][128 + 4 * lane]);
+          const float2 a01 = __half22float2(*reinterpret_cast<const __half2*>(&qa2.x));
+          const float2 a23 = __half22float2(*reinterpret_cast<const __half2*>(&qa2.y));
+          const float2 b01 = __half22float2(*reinterpret_cast<const __half2*>(&qb2.x));
+          const float2 b23 = __half22float2(*reinterpret_cast<const __half2*>(&qb2.y));
+          qa[0] = a01.x; qa[1] = a01.y; qa[2] = a23.x; qa[3] = a23.y;
+          qb[0] = b01.x; qb[1] = b01.y; qb[2] = b23.x; qb[3] = b23.y;
         }
         const int tw = st * 128 + warp * 16;  // first position of this warp's 16
         if (tw < t.len) {
@@ -292,79 +419,21 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
         }
       }
       if (!ok) break;
-      // ---- merge the 8 warps (sum over the 16 lanes of each head group first)
+      // ---- hand this warp's state to the merger (double-buffered by unit parity)
 #pragma unroll
       for (int o = 8; o >= 1; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+      const int b = k & 1;
+      if (!mbar_wait_warp(&mfree_bar[b], static_cast<uint32_t>(((k >> 1) & 1) ^ 1), &abort_flag, a.status,
+                          0x605))
+        break;
       if (lane == 0 || lane == 16) {
-        sm_m[warp][lane >> 4] = m;
-        sm_l[warp][lane >> 4] = l;
+        sm_m[b][warp][lane >> 4] = m;
+        sm_l[b][warp][lane >> 4] = l;
       }
-      *reinterpret_cast<float4*>(&sm_acc[warp][0][4 * lane]) = make_float4(acc_a[0], acc_a[1], acc_a[2], acc_a[3]);
-      *reinterpret_cast<float4*>(&sm_acc[warp][1][4 * lane]) = make_float4(acc_b[0], acc_b[1], acc_b[2], acc_b[3]);
-      named_bar_sync(1, ATTN_CONSUMER_WARPS * 32);
-      const int h = tid >> 7, dd = tid & 127;
-      float M = -INFINITY;
-#pragma unroll
-      for (int w = 0; w < ATTN_CONSUMER_WARPS; ++w) M = fmaxf(M, sm_m[w][h]);
-      float Ls = 0.f, Os = 0.f;
-#pragma unroll
-      for (int w = 0; w < ATTN_CONSUMER_WARPS; ++w) {
-        const float mw = sm_m[w][h];
-        if (mw == -INFINITY) continue;
-        const float f = expf(mw - M);
-        Ls += sm_l[w][h] * f;
-        Os += sm_acc[w][h][dd] * f;
-      }
-      const size_t obase = static_cast<size_t>(t.r) * a.q_ld + (2 * t.g + h) * 128 + dd;
-      if (t.nch == 1) {
-        a.out[obase] = __float2half_rn(Os / Ls);
-      } else {
-        const size_t pidx = (static_cast<size_t>(t.r) * nkv + t.g) * ATTN_ROW_CHUNKS;
-        float* part = a.ws + (pidx + t.c) * ATTN_PART_FLOATS;
-        if (dd == 0) {
-          part[h] = M;
-          part[2 + h] = Ls;
-        }
-        part[4 + h * 128 + dd] = Os;
-        __threadfence();
-        named_bar_sync(1, ATTN_CONSUMER_WARPS * 32);
-        if (tid == 0) {
-          const int old = atomicAdd(a.counters + t.r * nkv + t.g, 1);
-          sh_last = (old == t.nch - 1) ? 1 : 0;
-        }
-        named_bar_sync(1, ATTN_CONSUMER_WARPS * 32);
-        if (sh_last) {
-          __threadfence();
-          const float* parts = a.ws + pidx * ATTN_PART_FLOATS;
-          float mc[ATTN_ROW_CHUNKS], lc[ATTN_ROW_CHUNKS], oc[ATTN_ROW_CHUNKS];
-#pragma unroll
-          for (int cc = 0; cc < ATTN_ROW_CHUNKS; ++cc) {  // independent loads, all in flight
-            if (cc < t.nch) {
-              mc[cc] = __ldcg(parts + cc * ATTN_PART_FLOATS + h);
-              lc[cc] = __ldcg(parts + cc * ATTN_PART_FLOATS + 2 + h);
-              oc[cc] = __ldcg(parts + cc * ATTN_PART_FLOATS + 4 + h * 128 + dd);
-            } else {
-              mc[cc] = -INFINITY;
-              lc[cc] = 0.f;
-              oc[cc] = 0.f;
-            }
-          }
-          float mx = -INFINITY;
-#pragma unroll
-          for (int cc = 0; cc < ATTN_ROW_CHUNKS; ++cc) mx = fmaxf(mx, mc[cc]);
-          float ls = 0.f, os = 0.f;
-#pragma unroll
-          for (int cc = 0; cc < ATTN_ROW_CHUNKS; ++cc) {
-            if (mc[cc] == -INFINITY) continue;
-            const float f = expf(mc[cc] - mx);
-            ls += lc[cc] * f;
-            os += oc[cc] * f;
-          }
-          a.out[obase] = __float2half_rn(os / ls);
-          if (tid == 0) a.counters[t.r * nkv + t.g] = 0;
-        }
-      }
-      named_bar_sync(1, ATTN_CONSUMER_WARPS * 32);  // smem merge buffers are reused
+      *reinterpret_cast<float4*>(&sm_acc[b][warp][0][4 * lane]) = make_float4(acc_a[0], acc_a[1], acc_a[2], acc_a[3]);
+      *reinterpret_cast<float4*>(&sm_acc[b][warp][1][4 * lane]) = make_float4(acc_b[0], acc_b[1], acc_b[2], acc_b[3]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&mfull_bar[b]);
     }
   }
 }

@@ -44,7 +44,7 @@ constexpr int GEMM_BUILD_GROUPS = 2;  // int8 A-builder warpgroups
 __host__ __device__ constexpr int gemm_threads(bool int8) {
   return 128 + (int8 ? GEMM_BUILD_GROUPS * 128 : 0) + 128;
 }
-constexpr int GEMM_MAX_STAGES = 8;
+constexpr int GEMM_MAX_STAGES = 12;
 constexpr int GEMM_A_STAGES = 8;  // upper bound; the kernel fits what TMEM allows
 constexpr int GEMM_MAX_NTILE = 128;
 constexpr uint32_t GEMM_TMEM_COLS = 512;
@@ -496,7 +496,7 @@ __global__ void __launch_bounds__(gemm_threads(INT8), 1)
     UnitCursor cur(static_cast<int>(ub) + grp, KB, a.n_tiles);
     int st = grp % S, ast = grp % SA;
     uint32_t ph = static_cast<uint32_t>((grp / S) & 1), aph = static_cast<uint32_t>((grp / SA) & 1);
-    int cur_mt = -1;
+    int cur_mt = -1, pend_ast = -1;
     __half2 sc2 = __floats2half2_rn(1.0f, 1.0f);
     for (int i = grp; i < n; i += NBG) {
       if (!mbar_wait_warp(&wfull_bar[st], ph, &abort_flag, a.status, 0x301)) break;
@@ -536,10 +536,21 @@ __global__ void __launch_bounds__(gemm_threads(INT8), 1)
           tmem_st_x4(taddr + static_cast<uint32_t>(c) * 4u, w4);
         }
       }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&afull_bar[ast]);
+      // Publish two built units per wait: the TMEM store round trip is paid once for both.
+      // (Needs S >= NBG + 1 and SA >= NBG + 1 so the unit built next never waits on the
+      // pending one; the host guarantees both.)
+      if (pend_ast >= 0 || i + NBG >= n) {
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (pend_ast >= 0) mbar_arrive(&afull_bar[pend_ast]);
+          mbar_arrive(&afull_bar[ast]);
+        }
+        pend_ast = -1;
+      } else {
+        pend_ast = ast;
+      }
       if (i == 0 && t == 0) trace_stamp(a, 5);
 #pragma unroll
       for (int q = 0; q < NBG; ++q) cur.advance();

@@ -179,7 +179,8 @@ static GemmShape gemm_shape(int n_out, int k, bool int8, int rows, int num_sms) 
   const int atoms = int8 ? 2 : 1;
   const int stage = 16384 + atoms * s.n_tile * 128;
   const int dyn = g_dyn_smem_max > 0 ? g_dyn_smem_max : 200 * 1024;
-  s.stages = std::max(2, std::min(GEMM_MAX_STAGES, (dyn - 1024) / stage));
+  // >= 3 stages: the int8 A builders publish units in pairs (see the kernel)
+  s.stages = std::max(3, std::min(GEMM_MAX_STAGES, (dyn - 1024) / stage));
   s.smem = static_cast<size_t>(s.stages) * stage + 1024;
   int max_seg = 1;
   for (int t = 0; t < s.tiles; ++t) {
@@ -623,7 +624,7 @@ qasr_status qasr_create(const qasr_text_config* cfg, const qasr_options* opts, i
   if (opts->max_slots <= 0 || opts->max_slots > 4096 || opts->max_seq <= 0)
     return bad("max_slots must be 1..4096 and max_seq positive");
   if (c->opts.max_prefill_rows <= 0) c->opts.max_prefill_rows = 2048;
-  c->opts.max_prefill_rows = std::min(c->opts.max_prefill_rows, 4096);
+  c->opts.max_prefill_rows = std::min(c->opts.max_prefill_rows, ATTN_MAX_ROWS);
   *out = c;
 
   CK(cudaSetDevice(device), "cudaSetDevice");
@@ -1172,12 +1173,12 @@ qasr_status qasr_kernel_attention(int device, void* stream, const uint16_t* q, i
   static ProbeWs pws[16];
   std::lock_guard<std::mutex> lock(mu);
   if (device < 0 || device >= 16 || !q || !out || !kv_pool || !page_table || !row_slot || !row_pos ||
-      rows <= 0 || rows > ATTN_MAX_ROWS || nkv <= 0 || q_ld != 2 * nkv * 128 || layer < 0 || layer >= layers)
+      rows <= 0 || nkv <= 0 || q_ld != 2 * nkv * 128 || layer < 0 || layer >= layers)
     return probe_err(err, errlen, QASR_ERR_INVALID_ARG, "bad attention probe arguments");
   if (cudaSetDevice(device) != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, "cudaSetDevice");
   const int max_chunks = ATTN_ROW_CHUNKS;
   ProbeWs& P = pws[device];
-  const size_t need = static_cast<size_t>(rows) * nkv * max_chunks * ATTN_PART_FLOATS;
+  const size_t need = static_cast<size_t>(std::min(rows, ATTN_MAX_ROWS)) * nkv * max_chunks * ATTN_PART_FLOATS;
   if (need > P.ws_floats) {
     if (P.ws) cudaFree(P.ws);
     P.ws = nullptr;
@@ -1214,9 +1215,18 @@ qasr_status qasr_kernel_attention(int device, void* stream, const uint16_t* q, i
   a.max_chunks = max_chunks;
   std::string e;
   if (init_kernel_attrs(&e) != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, e);
-  const cudaError_t ce = launch_k(attention_kernel, dim3(sms), dim3(ATTN_THREADS), attn_smem_bytes(rows),
-                                  static_cast<cudaStream_t>(stream), false, a);
-  if (ce != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, cudaGetErrorString(ce));
+  // one launch per ATTN_MAX_ROWS rows (the unit table of a launch lives in shared memory)
+  for (int r0 = 0; r0 < rows; r0 += ATTN_MAX_ROWS) {
+    AttnArgs b = a;
+    b.rows = std::min(ATTN_MAX_ROWS, rows - r0);
+    b.q = a.q + static_cast<size_t>(r0) * q_ld;
+    b.out = a.out + static_cast<size_t>(r0) * q_ld;
+    b.row_slot = row_slot + r0;
+    b.row_pos = row_pos + r0;
+    const cudaError_t ce = launch_k(attention_kernel, dim3(sms), dim3(ATTN_THREADS), attn_smem_bytes(b.rows),
+                                    static_cast<cudaStream_t>(stream), false, b);
+    if (ce != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, cudaGetErrorString(ce));
+  }
   return QASR_OK;
 }
 
