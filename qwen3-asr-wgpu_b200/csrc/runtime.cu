@@ -465,7 +465,7 @@ qasr_status enqueue_layers(qasr_ctx* c, int rows, const int* rs, const int* rp, 
 
 // final norm + lm_head + argmax for `n` rows: xf[i] = norm(h[src_rows[i]]).
 qasr_status enqueue_head(qasr_ctx* c, int n, const int* src_rows, const int* slot_of,
-                         const int* pos_of, int* out_tok, uint64_t* nk) {
+                         const int* pos_of, int* out_tok, int logit_row0, uint64_t* nk) {
   const int hs = c->cfg.hidden_size;
   CK(launch_k(rmsnorm_rows_kernel, dim3(n), dim3(256), 0, c->stream, true, c->xf, (const __half*)c->h,
               src_rows, (const float*)c->final_norm, hs, c->cfg.rms_norm_eps),
@@ -473,7 +473,9 @@ qasr_status enqueue_head(qasr_ctx* c, int n, const int* src_rows, const int* slo
   GemmLaunch g;
   qasr_status s = plan_gemm(c, c->lm, c->xf, hs, n, EPI_LOGITS, &g);
   if (s) return s;
-  g.args.logits = (c->opts.flags & QASR_FLAG_KEEP_LOGITS) ? c->logits : nullptr;
+  g.args.logits = (c->opts.flags & QASR_FLAG_KEEP_LOGITS)
+                      ? c->logits + static_cast<size_t>(logit_row0) * c->cfg.vocab_size
+                      : nullptr;
   g.args.ld_logits = c->cfg.vocab_size;
   g.args.best = c->best;
   if ((s = run_gemm(c, g))) return s;
@@ -492,7 +494,7 @@ qasr_status enqueue_decode(qasr_ctx* c, int n, uint64_t* nk) {
   *nk += 1;
   qasr_status s = enqueue_layers(c, n, c->drow_slot, c->drow_pos, nk);
   if (s) return s;
-  return enqueue_head(c, n, nullptr, c->drow_slot, c->drow_pos, c->out_tok, nk);
+  return enqueue_head(c, n, nullptr, c->drow_slot, c->drow_pos, c->out_tok, 0, nk);
 }
 
 qasr_status ready(qasr_ctx* c) {
@@ -1051,7 +1053,8 @@ qasr_status qasr_prefill_batch(qasr_ctx* c, const int* slots, int n, const uint1
       CK(cudaMemcpyAsync(c->fin_src, fsrc.data(), nf * sizeof(int), cudaMemcpyHostToDevice, c->stream), "fin upload");
       CK(cudaMemcpyAsync(c->fin_slot, fslot.data(), nf * sizeof(int), cudaMemcpyHostToDevice, c->stream), "fin upload");
       CK(cudaMemcpyAsync(c->fin_pos, fpos.data(), nf * sizeof(int), cudaMemcpyHostToDevice, c->stream), "fin upload");
-      if ((s = enqueue_head(c, nf, c->fin_src, c->fin_slot, c->fin_pos, c->out_tok + seg0, &nk))) return s;
+      // segment i's token and logits land at row i (prefill chunks append segments)
+      if ((s = enqueue_head(c, nf, c->fin_src, c->fin_slot, c->fin_pos, c->out_tok + seg0, seg0, &nk))) return s;
     }
     // the next chunk overwrites the row buffers: finish this one first
     CK(cudaStreamSynchronize(c->stream), "prefill chunk sync");
