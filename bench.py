@@ -250,8 +250,11 @@ def main():
 
     refill_count = [0] * SLOTS_PER_GPU
 
+    from qasr_b200 import sharding
+    global_slots = sharding.slot_range(rank, world, SLOTS_PER_GPU)
+
     def make_prefix(s, length):
-        stream_id = (rank * SLOTS_PER_GPU + s) * 65536 + refill_count[s]
+        stream_id = sharding.prefix_stream(global_slots[s], refill_count[s])
         refill_count[s] += 1
         n_text = min(24, length)
         hidden, _ = model.prefix(stream_id, length - n_text, n_text=n_text, n_before=min(9, n_text))
@@ -337,10 +340,8 @@ def main():
     # ---- dominant kernels, timed alone at the bench shapes
     kernels = time_kernels(pkg, torch, dec, cfg, slots, stream, kv_len)
 
-    local_vals = torch.tensor([decode_s, t_e2e, prefill_time[0]], dtype=torch.float64, device="cuda")
-    if dist is not None:
-        dist.all_reduce(local_vals, op=dist.ReduceOp.MAX)
-    decode_max, e2e_max, _ = local_vals.tolist()
+    decode_max, e2e_max, _ = sharding.max_over_ranks([decode_s, t_e2e, prefill_time[0]], dist,
+                                                     device=torch.device("cuda", local))
 
     if rank == 0:
         hbm, peak_kind = peaks()
