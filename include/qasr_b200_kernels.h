@@ -61,6 +61,25 @@ qasr_status qasr_kernel_attention(int device, void* stream, const uint16_t* q, i
                                   const int* row_slot, const int* row_pos, int rows, char* err,
                                   int errlen);
 
+/* qasr_kernel_attention without any device allocation — for callers that may not call
+ * cudaMalloc: code running while a CUDA graph is being captured, hosts that hand the
+ * library a fixed memory budget up front, and real-time audio paths that must not touch
+ * the allocator between frames.  No counterpart in the reference (its wgpu decoder owns
+ * all buffers).  The scratch is one static device array inside the library (about
+ * 2 MiB, held by every GPU that loads the library until the process exits), so:
+ *   - at most 64 query rows and 8 kv heads per call; larger calls fail with
+ *     QASR_ERR_CAPACITY (use qasr_kernel_attention);
+ *   - the first call on a device looks the array's address up
+ *     (cudaGetSymbolAddress): make that first call before any stream capture;
+ *   - all calls share the array: calls that overlap on the GPU (other streams, other
+ *     threads) race and must be serialised by the caller.
+ * Same inputs, outputs and results as qasr_kernel_attention. */
+qasr_status qasr_kernel_attention_noalloc(int device, void* stream, const uint16_t* q, int q_ld,
+                                          uint16_t* out, const uint16_t* kv_pool,
+                                          const int* page_table, int max_pages, int layers,
+                                          int nkv, int layer, const int* row_slot,
+                                          const int* row_pos, int rows, char* err, int errlen);
+
 /* Append K and V rows ([rows, nkv*128] f16 each) at (row_slot[r], row_pos[r]) of
  * layer `layer` — the cache writes of qkv_extract(_slots) (src/shaders.rs:1376-1635). */
 qasr_status qasr_kernel_kv_append(int device, void* stream, const uint16_t* k, const uint16_t* v,

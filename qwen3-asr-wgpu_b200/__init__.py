@@ -45,7 +45,7 @@ EXPORTED_SYMBOLS = (
     "qasr_prefill", "qasr_step", "qasr_prefill_batch", "qasr_step_batch", "qasr_read_logits",
     "qasr_build_rope_tables", "qasr_build_dim_map", "qasr_dequant_i8",
     "qasr_kernel_pack_weights", "qasr_kernel_gemm", "qasr_kernel_gemm_traced", "qasr_kernel_attention",
-    "qasr_kernel_kv_append",
+    "qasr_kernel_attention_noalloc", "qasr_kernel_kv_append",
     "qasr_kernel_launch_count",
     "qasr_synth_key", "qasr_synth_normal_f16", "qasr_synth_uniform_ids",
     "qasr_synth_quantize_rows", "qasr_f32_to_f16", "qasr_f16_to_f32", "qasr_f32_to_f16_array",
@@ -118,6 +118,7 @@ def _load() -> ctypes.CDLL:
     lib.qasr_kernel_gemm_traced.argtypes = [I, P, I, P, P, I, I, P, I, I, P, I, I, P, ctypes.POINTER(I),
                                             ctypes.c_char_p, I]
     lib.qasr_kernel_attention.argtypes = [I, P, P, I, P, P, P, I, I, I, I, P, P, I, ctypes.c_char_p, I]
+    lib.qasr_kernel_attention_noalloc.argtypes = [I, P, P, I, P, P, P, I, I, I, I, P, P, I, ctypes.c_char_p, I]
     lib.qasr_kernel_kv_append.argtypes = [I, P, P, P, P, P, I, I, I, I, P, P, I, ctypes.c_char_p, I]
     lib.qasr_kernel_launch_count.restype = ctypes.c_uint64
     lib.qasr_synth_key.argtypes = [ctypes.c_uint64, ctypes.c_uint64]
@@ -361,6 +362,20 @@ def kernel_attention(device: int, stream: int, q_ptr: int, q_ld: int, out_ptr: i
         raise DecoderError(st, err.value.decode())
 
 
+def kernel_attention_noalloc(device: int, stream: int, q_ptr: int, q_ld: int, out_ptr: int, pool_ptr: int,
+                             page_table_ptr: int, max_pages: int, layers: int, nkv: int, layer: int,
+                             row_slot_ptr: int, row_pos_ptr: int, rows: int):
+    """kernel_attention with its scratch in a static device array: no allocation, at most
+    64 rows x 8 kv heads per call, one call at a time per device."""
+    err = ctypes.create_string_buffer(512)
+    V = ctypes.c_void_p
+    st = lib.qasr_kernel_attention_noalloc(device, V(stream), V(q_ptr), q_ld, V(out_ptr), V(pool_ptr),
+                                           V(page_table_ptr), max_pages, layers, nkv, layer, V(row_slot_ptr),
+                                           V(row_pos_ptr), rows, err, 512)
+    if st != QASR_OK:
+        raise DecoderError(st, err.value.decode())
+
+
 def kernel_kv_append(device: int, stream: int, k_ptr: int, v_ptr: int, pool_ptr: int,
                      page_table_ptr: int, max_pages: int, layers: int, nkv: int, layer: int,
                      row_slot_ptr: int, row_pos_ptr: int, rows: int):
@@ -379,7 +394,7 @@ def version() -> str:
 
 __all__ = [
     "TextDecoder", "DecoderError", "SyntheticModel", "MODEL_PRESETS", "text_config",
-    "build_rope_tables", "dim_map", "kernel_pack_weights", "kernel_gemm", "kernel_attention", "kernel_kv_append",
+    "build_rope_tables", "dim_map", "kernel_pack_weights", "kernel_gemm", "kernel_attention_noalloc", "kernel_attention", "kernel_kv_append",
     "launch_count", "version", "WEIGHTS_F16", "WEIGHTS_INT8", "EXPORTED_SYMBOLS", "lib",
     "f16_bits_to_f32", "f32_to_f16_bits", "PAGE_POSITIONS",
 ]

@@ -1235,6 +1235,89 @@ qasr_status qasr_kernel_attention(int device, void* stream, const uint16_t* q, i
 
 }  // extern "C"
 
+// ============================================================================ no-alloc variant
+// Attention for callers that must not allocate device memory (see
+// qasr_kernel_attention_noalloc in include/qasr_b200_kernels.h).  Its scratch — the
+// per-(row, kv head) arrival counters and the chunk partials of the split-row merge —
+// is this file-scope array, sized for QASR_NOALLOC_MAX_ROWS rows x QASR_NOALLOC_MAX_KV
+// kv heads.  Every GPU that loads the library holds it until the process exits.  In host
+// code `g_attn_noalloc_scratch` only names the symbol; the device address comes from
+// cudaGetSymbolAddress, once per device.
+namespace qasr {
+constexpr int NOALLOC_MAX_ROWS = 64;
+constexpr int NOALLOC_MAX_KV = 8;
+constexpr size_t NOALLOC_COUNTER_BYTES = static_cast<size_t>(NOALLOC_MAX_ROWS) * NOALLOC_MAX_KV * sizeof(int);
+constexpr size_t NOALLOC_PARTIAL_BYTES = static_cast<size_t>(NOALLOC_MAX_ROWS) * NOALLOC_MAX_KV *
+                                         ATTN_ROW_CHUNKS * ATTN_PART_FLOATS * sizeof(float);
+constexpr size_t NOALLOC_SCRATCH_BYTES = NOALLOC_COUNTER_BYTES + NOALLOC_PARTIAL_BYTES;  // ~2 MiB
+static_assert(NOALLOC_COUNTER_BYTES % 256 == 0, "partials must stay 256-byte aligned");
+}  // namespace qasr
+
+static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[qasr::NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 16;
+std::once_flag g_noalloc_once[kMaxDevices];
+void* g_noalloc_addr[kMaxDevices] = {};
+cudaError_t g_noalloc_setup[kMaxDevices] = {};
+}  // namespace
+
+extern "C" qasr_status qasr_kernel_attention_noalloc(int device, void* stream, const uint16_t* q,
+                                                     int q_ld, uint16_t* out, const uint16_t* kv_pool,
+                                                     const int* page_table, int max_pages, int layers,
+                                                     int nkv, int layer, const int* row_slot,
+                                                     const int* row_pos, int rows, char* err,
+                                                     int errlen) {
+  if (device < 0 || device >= kMaxDevices || !q || !out || !kv_pool || !page_table || !row_slot ||
+      !row_pos || rows <= 0 || nkv <= 0 || q_ld != 2 * nkv * 128 || layer < 0 || layer >= layers)
+    return probe_err(err, errlen, QASR_ERR_INVALID_ARG, "bad attention arguments");
+  if (rows > NOALLOC_MAX_ROWS || nkv > NOALLOC_MAX_KV)
+    return probe_err(err, errlen, QASR_ERR_CAPACITY,
+                     "qasr_kernel_attention_noalloc handles at most 64 query rows and 8 kv heads per "
+                     "call (its scratch is a fixed static array); split the rows or use "
+                     "qasr_kernel_attention");
+  if (cudaSetDevice(device) != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, "cudaSetDevice");
+  // set-up, once per device, with that device current: the array's device address
+  std::call_once(g_noalloc_once[device], [device] {
+    g_noalloc_setup[device] = cudaGetSymbolAddress(&g_noalloc_addr[device], g_attn_noalloc_scratch);
+  });
+  if (g_noalloc_setup[device] != cudaSuccess || g_noalloc_addr[device] == nullptr)
+    return probe_err(err, errlen, QASR_ERR_DEVICE,
+                     std::string("cudaGetSymbolAddress of the static attention scratch failed: ") +
+                         cudaGetErrorString(g_noalloc_setup[device]));
+  std::string e;
+  if (init_kernel_attrs(&e) != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, e);
+  unsigned char* scratch = static_cast<unsigned char*>(g_noalloc_addr[device]);
+  int* counters = reinterpret_cast<int*>(scratch);
+  float* partials = reinterpret_cast<float*>(scratch + NOALLOC_COUNTER_BYTES);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // the counters must start at zero; the array keeps whatever the last call left
+  cudaError_t ce = cudaMemsetAsync(counters, 0, static_cast<size_t>(rows) * nkv * sizeof(int), st);
+  if (ce != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, cudaGetErrorString(ce));
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  AttnArgs a{};
+  a.q = reinterpret_cast<const __half*>(q);
+  a.q_ld = q_ld;
+  a.out = reinterpret_cast<__half*>(out);
+  a.row_slot = row_slot;
+  a.row_pos = row_pos;
+  a.kv.pool = const_cast<__half*>(reinterpret_cast<const __half*>(kv_pool));
+  a.kv.page_table = page_table;
+  a.kv.max_pages = max_pages;
+  a.kv.layers = layers;
+  a.kv.nkv = nkv;
+  a.layer = layer;
+  a.rows = rows;
+  a.scale = 1.0f / std::sqrt(128.0f);
+  a.ws = partials;
+  a.counters = counters;
+  a.max_chunks = ATTN_ROW_CHUNKS;
+  ce = launch_k(attention_kernel, dim3(sms), dim3(ATTN_THREADS), attn_smem_bytes(rows), st, false, a);
+  if (ce != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, cudaGetErrorString(ce));
+  return QASR_OK;
+}
+
 namespace qasr {
 __global__ void kv_append_kernel(const __half* __restrict__ k, const __half* __restrict__ v,
                                  KvLayout kv, int layer, const int* __restrict__ row_slot,
