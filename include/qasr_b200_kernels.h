@@ -61,6 +61,17 @@ qasr_status qasr_kernel_attention(int device, void* stream, const uint16_t* q, i
                                   const int* row_slot, const int* row_pos, int rows, char* err,
                                   int errlen);
 
+/* qasr_kernel_attention with a latency trace: if `trace` (device, SM count x 8 uint64) is
+ * non-NULL each CTA records %globaltimer stamps (entry, unit table ready, first stage
+ * landed, first unit merged, last stage consumed, last unit merged, producer done) and
+ * the number of units it processed. */
+qasr_status qasr_kernel_attention_traced(int device, void* stream, const uint16_t* q, int q_ld,
+                                         uint16_t* out, const uint16_t* kv_pool,
+                                         const int* page_table, int max_pages, int layers,
+                                         int nkv, int layer, const int* row_slot,
+                                         const int* row_pos, int rows, unsigned long long* trace,
+                                         char* err, int errlen);
+
 /* qasr_kernel_attention without any device allocation — for callers that may not call
  * cudaMalloc: code running while a CUDA graph is being captured, hosts that hand the
  * library a fixed memory budget up front, and real-time audio paths that must not touch

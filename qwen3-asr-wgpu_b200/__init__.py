@@ -45,7 +45,7 @@ EXPORTED_SYMBOLS = (
     "qasr_prefill", "qasr_step", "qasr_prefill_batch", "qasr_step_batch", "qasr_read_logits",
     "qasr_build_rope_tables", "qasr_build_dim_map", "qasr_dequant_i8",
     "qasr_kernel_pack_weights", "qasr_kernel_gemm", "qasr_kernel_gemm_traced", "qasr_kernel_attention",
-    "qasr_kernel_attention_noalloc", "qasr_kernel_kv_append",
+    "qasr_kernel_attention_noalloc", "qasr_kernel_attention_traced", "qasr_kernel_kv_append",
     "qasr_kernel_launch_count",
     "qasr_synth_key", "qasr_synth_normal_f16", "qasr_synth_uniform_ids",
     "qasr_synth_quantize_rows", "qasr_f32_to_f16", "qasr_f16_to_f32", "qasr_f32_to_f16_array",
@@ -118,6 +118,7 @@ def _load() -> ctypes.CDLL:
     lib.qasr_kernel_gemm_traced.argtypes = [I, P, I, P, P, I, I, P, I, I, P, I, I, P, ctypes.POINTER(I),
                                             ctypes.c_char_p, I]
     lib.qasr_kernel_attention.argtypes = [I, P, P, I, P, P, P, I, I, I, I, P, P, I, ctypes.c_char_p, I]
+    lib.qasr_kernel_attention_traced.argtypes = [I, P, P, I, P, P, P, I, I, I, I, P, P, I, P, ctypes.c_char_p, I]
     lib.qasr_kernel_attention_noalloc.argtypes = [I, P, P, I, P, P, P, I, I, I, I, P, P, I, ctypes.c_char_p, I]
     lib.qasr_kernel_kv_append.argtypes = [I, P, P, P, P, P, I, I, I, I, P, P, I, ctypes.c_char_p, I]
     lib.qasr_kernel_launch_count.restype = ctypes.c_uint64
@@ -358,6 +359,18 @@ def kernel_attention(device: int, stream: int, q_ptr: int, q_ld: int, out_ptr: i
     st = lib.qasr_kernel_attention(device, V(stream), V(q_ptr), q_ld, V(out_ptr), V(pool_ptr),
                                    V(page_table_ptr), max_pages, layers, nkv, layer, V(row_slot_ptr),
                                    V(row_pos_ptr), rows, err, 512)
+    if st != QASR_OK:
+        raise DecoderError(st, err.value.decode())
+
+
+def kernel_attention_traced(device: int, stream: int, q_ptr: int, q_ld: int, out_ptr: int, pool_ptr: int,
+                            page_table_ptr: int, max_pages: int, layers: int, nkv: int, layer: int,
+                            row_slot_ptr: int, row_pos_ptr: int, rows: int, trace_ptr: int):
+    err = ctypes.create_string_buffer(512)
+    V = ctypes.c_void_p
+    st = lib.qasr_kernel_attention_traced(device, V(stream), V(q_ptr), q_ld, V(out_ptr), V(pool_ptr),
+                                          V(page_table_ptr), max_pages, layers, nkv, layer, V(row_slot_ptr),
+                                          V(row_pos_ptr), rows, V(trace_ptr), err, 512)
     if st != QASR_OK:
         raise DecoderError(st, err.value.decode())
 

@@ -69,7 +69,16 @@ struct AttnArgs {
   int* counters;    // [rows * nkv], zero between launches
   int max_chunks;
   uint32_t* status;
+  unsigned long long* trace;  // optional: per CTA ATTN_TRACE_SLOTS %globaltimer stamps
 };
+
+constexpr int ATTN_TRACE_SLOTS = 8;
+// slots: 0 entry, 1 unit table ready, 2 first stage landed (consumer warp 0), 3 first
+// unit handed to the merger, 4 last stage consumed, 5 last unit merged, 6 producer done,
+// 7 units processed by this CTA
+__device__ __forceinline__ void attn_stamp(const AttnArgs& a, int slot) {
+  if (a.trace != nullptr) a.trace[blockIdx.x * ATTN_TRACE_SLOTS + slot] = globaltimer();
+}
 
 struct AttnUnit {
   int r, g, c, nch, len, s0, s1;  // row, kv head, chunk, chunks of the row, row length, stages [s0, s1)
@@ -113,6 +122,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
   const int nkv = a.kv.nkv;
 
   if (tid == 0) {
+    attn_stamp(a, 0);
     for (int i = 0; i < ATTN_STAGES; ++i) {
       mbar_init(&full_bar[i], 1);
       mbar_init(&empty_bar[i], ATTN_CONSUMER_WARPS);
@@ -160,6 +170,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
     __syncthreads();
   }
   const int U = sh_units;
+  if (tid == 0) attn_stamp(a, 1);
 
   if (warp == ATTN_CONSUMER_WARPS) {
     // ------------------------------------------------------------ page producer
@@ -196,6 +207,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
           }
         }
       }
+      attn_stamp(a, 6);
       for (int j = gs > ATTN_STAGES ? gs - ATTN_STAGES : 0; j < gs; ++j)  // drain
         mbar_wait(&full_bar[j % ATTN_STAGES], static_cast<uint32_t>((j / ATTN_STAGES) & 1), nullptr,
                   a.status, 0x602);
@@ -236,6 +248,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&mfree_bar[b]);  // state read: the consumers may reuse the buffer
+      if (lane == 0 && k == 0) attn_stamp(a, 3);
       __half* outp = a.out + static_cast<size_t>(t.r) * a.q_ld + (2 * t.g) * 128 + 4 * lane;
       if (t.nch == 1) {
 #pragma unroll
@@ -315,6 +328,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
         }
       }
     }
+    if (lane == 0) attn_stamp(a, 5);
   } else {
     // ------------------------------------------------------------ consumers
     int sl = 0, k = 0;
@@ -331,6 +345,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
           ok = false;
           break;
         }
+        if (k == 0 && st == t.s0 && tid == 0) attn_stamp(a, 2);
         if (st == t.s0) {
           const uint2 qa2 = *reinterpret_cast<const uint2*>(&sm_q[sl][4 * lane]);
           const uint2 qb2 = *reinterpret_cast<const uint2*>(&sm_q[sl][128 + 4 * lane]);
@@ -434,6 +449,10 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
       *reinterpret_cast<float4*>(&sm_acc[b][warp][1][4 * lane]) = make_float4(acc_b[0], acc_b[1], acc_b[2], acc_b[3]);
       __syncwarp();
       if (lane == 0) mbar_arrive(&mfull_bar[b]);
+    }
+    if (tid == 0) {
+      attn_stamp(a, 4);
+      if (a.trace != nullptr) a.trace[blockIdx.x * ATTN_TRACE_SLOTS + 7] = static_cast<unsigned long long>(k);
     }
   }
 }

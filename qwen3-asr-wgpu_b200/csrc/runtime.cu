@@ -1172,6 +1172,15 @@ qasr_status qasr_kernel_attention(int device, void* stream, const uint16_t* q, i
                                   int max_pages, int layers, int nkv, int layer,
                                   const int* row_slot, const int* row_pos, int rows, char* err,
                                   int errlen) {
+  return qasr_kernel_attention_traced(device, stream, q, q_ld, out, kv_pool, page_table, max_pages, layers,
+                                      nkv, layer, row_slot, row_pos, rows, nullptr, err, errlen);
+}
+
+qasr_status qasr_kernel_attention_traced(int device, void* stream, const uint16_t* q, int q_ld,
+                                         uint16_t* out, const uint16_t* kv_pool, const int* page_table,
+                                         int max_pages, int layers, int nkv, int layer,
+                                         const int* row_slot, const int* row_pos, int rows,
+                                         unsigned long long* trace, char* err, int errlen) {
   static std::mutex mu;
   static ProbeWs pws[16];
   std::lock_guard<std::mutex> lock(mu);
@@ -1216,6 +1225,7 @@ qasr_status qasr_kernel_attention(int device, void* stream, const uint16_t* q, i
   a.ws = P.ws;
   a.counters = P.cnt;
   a.max_chunks = max_chunks;
+  a.trace = trace;
   std::string e;
   if (init_kernel_attrs(&e) != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, e);
   // one launch per ATTN_MAX_ROWS rows (the unit table of a launch lives in shared memory)

@@ -122,9 +122,24 @@ def bench_attention(args, pkg, torch):
 
     med, best = _time(torch, run, args.iters)
     nbytes = int(lens.sum()) * nkv * 512 + rows * 2 * nkv * 128 * 2 * 2
-    return {"kernel": "attention", "slots": rows, "len_lo": args.lo, "len_hi": args.hi,
-            "mean_len": float(lens.mean()), "median_us": med * 1e6, "best_us": best * 1e6, "bytes": nbytes,
-            "gbs": nbytes / med / 1e9}
+    res = {"kernel": "attention", "slots": rows, "len_lo": args.lo, "len_hi": args.hi,
+           "mean_len": float(lens.mean()), "median_us": med * 1e6, "best_us": best * 1e6, "bytes": nbytes,
+           "gbs": nbytes / med / 1e9}
+    if args.trace:
+        sms = torch.cuda.get_device_properties(0).multi_processor_count
+        trace = torch.zeros((sms, 8), dtype=torch.int64, device="cuda")
+        torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda").zero_()
+        pkg.kernel_attention_traced(0, st, q.data_ptr(), 2 * nkv * 128, out.data_ptr(), pool.data_ptr(),
+                                    pt.data_ptr(), max_pages, 1, nkv, 0, rs.data_ptr(), rp.data_ptr(), rows,
+                                    trace.data_ptr())
+        torch.cuda.synchronize()
+        t = trace.cpu().numpy().astype(np.float64)
+        t0 = t[:, 0].min()
+        names = ["entry", "table", "first_stage", "first_merge", "consumers_done", "merger_done", "producer_done"]
+        res["trace_us"] = {nm: [round(float(np.median(t[:, i] - t0)) / 1e3, 2), round(float(np.max(t[:, i] - t0)) / 1e3, 2)]
+                           for i, nm in enumerate(names)}
+        res["units_per_cta"] = [int(t[:, 7].min()), int(np.median(t[:, 7])), int(t[:, 7].max())]
+    return res
 
 
 def bench_append(args, pkg, torch):
@@ -174,6 +189,7 @@ def main(argv=None):
         a.add_argument("--hi", type=int, default=4096)
         a.add_argument("--chunk", type=int, default=1 if name == "attention" else 13)
         a.add_argument("--seed", type=int, default=5)
+        a.add_argument("--trace", action="store_true")
     for p in sub.choices.values():
         p.add_argument("--iters", type=int, default=20)
     args = ap.parse_args(argv)
