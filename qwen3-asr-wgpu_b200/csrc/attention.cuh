@@ -174,39 +174,78 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
 
   if (warp == ATTN_CONSUMER_WARPS) {
     // ------------------------------------------------------------ page producer
-    if (lane == 0) {
-      int gs = 0, sl = 0;
-      uint32_t ph = 0;  // (gs / ATTN_STAGES) & 1, kept incrementally
-      bool ok = true;
-      for (int u = blockIdx.x; u < U && ok; u += gridDim.x) {
-        const AttnUnit t = attn_unit(a, prefix, u);
-        const int slot = a.row_slot[t.r];
-        const int pages = (t.len + 63) >> 6;
-        for (int st = t.s0; st < t.s1; ++st) {
-          if (!mbar_wait(&empty_bar[sl], ph ^ 1u, &abort_flag, a.status, 0x601)) {
-            ok = false;
-            break;
-          }
-          const int p0 = st * 2;
-          const int np = min(2, pages - p0);
+    // The whole warp fetches a unit's page ids at once (lane i: pages i and 32 + i of
+    // the unit) and prefetches the next unit's while the current one streams, so issuing a
+    // stage never waits on a row_slot -> page_table pointer chase.
+    int sl = 0, gs = 0;
+    uint32_t ph = 0;  // (gs / ATTN_STAGES) & 1, kept incrementally
+    bool ok = true;
+    const size_t head_stride = static_cast<size_t>(64) * 128;  // elements per (page, layer, which, head)
+    auto page_base = [&](int page, int which, int g) {
+      return a.kv.pool + ((((static_cast<size_t>(page) * a.kv.layers + a.layer) * 2 + which) * a.kv.nkv + g) *
+                          head_stride);
+    };
+    auto fetch = [&](int u, AttnUnit& t, int& slot, int& pg0, int& pg1) {
+      t = attn_unit(a, prefix, u);
+      slot = a.row_slot[t.r];
+      const int pages = (t.len + 63) >> 6;
+      const int p0 = t.s0 * 2;
+      const int* row = a.kv.page_table + static_cast<size_t>(slot) * a.kv.max_pages;
+      pg0 = (p0 + lane < pages) ? row[p0 + lane] : 0;
+      pg1 = (p0 + 32 + lane < pages) ? row[p0 + 32 + lane] : 0;
+    };
+    AttnUnit t{}, tn{};
+    int slot = 0, pg0 = 0, pg1 = 0, slotn = 0, pn0 = 0, pn1 = 0;
+    int u = blockIdx.x;
+    if (u < U) fetch(u, t, slot, pg0, pg1);
+    for (; u < U && ok; u += gridDim.x) {
+      const int un = u + gridDim.x;
+      if (un < U) fetch(un, tn, slotn, pn0, pn1);  // in flight while this unit streams
+      const int pages = (t.len + 63) >> 6;
+      const int* row = a.kv.page_table + static_cast<size_t>(slot) * a.kv.max_pages;
+      for (int st = t.s0; st < t.s1; ++st) {
+        int w = 1;
+        if (lane == 0) w = mbar_wait(&empty_bar[sl], ph ^ 1u, &abort_flag, a.status, 0x601) ? 1 : 0;
+        if (!__shfl_sync(0xffffffffu, w, 0)) {
+          ok = false;
+          break;
+        }
+        const int p0 = st * 2;
+        const int np = min(2, pages - p0);
+        int pid[2];
+#pragma unroll
+        for (int pp = 0; pp < 2; ++pp) {
+          const int ui = p0 + pp - t.s0 * 2;  // page index within the unit
+          const int v0 = __shfl_sync(0xffffffffu, pg0, ui & 31);
+          const int v1 = __shfl_sync(0xffffffffu, pg1, ui & 31);
+          pid[pp] = ui < 32 ? v0 : v1;
+        }
+        if (lane == 0) {
           uint8_t* buf = smem + static_cast<size_t>(sl) * ATTN_STAGE_BYTES;
           const bool first = st == t.s0;
-          mbar_arrive_expect_tx(&full_bar[sl], static_cast<uint32_t>(np) * 2u * ATTN_PAGE_BYTES + (first ? 512u : 0u));
+          mbar_arrive_expect_tx(&full_bar[sl],
+                                static_cast<uint32_t>(np) * 2u * ATTN_PAGE_BYTES + (first ? 512u : 0u));
           if (first)  // the unit's q rows (heads 2g, 2g+1: 512 contiguous bytes) ride along
             bulk_load(&sm_q[sl][0], a.q + static_cast<size_t>(t.r) * a.q_ld + 2 * t.g * 128, 512u, &full_bar[sl]);
           for (int pp = 0; pp < np; ++pp) {
-            const size_t ko = kv_elem_offset(a.kv, slot, (p0 + pp) * 64, a.layer, 0, t.g);
-            const size_t vo = kv_elem_offset(a.kv, slot, (p0 + pp) * 64, a.layer, 1, t.g);
-            bulk_load(buf + pp * ATTN_PAGE_BYTES, a.kv.pool + ko, ATTN_PAGE_BYTES, &full_bar[sl]);
-            bulk_load(buf + (2 + pp) * ATTN_PAGE_BYTES, a.kv.pool + vo, ATTN_PAGE_BYTES, &full_bar[sl]);
-          }
-          ++gs;
-          if (++sl == ATTN_STAGES) {
-            sl = 0;
-            ph ^= 1u;
+            const int ui = p0 + pp - t.s0 * 2;
+            const int page = ui < 64 ? pid[pp] : row[p0 + pp];  // units longer than 64 pages: direct
+            bulk_load(buf + pp * ATTN_PAGE_BYTES, page_base(page, 0, t.g), ATTN_PAGE_BYTES, &full_bar[sl]);
+            bulk_load(buf + (2 + pp) * ATTN_PAGE_BYTES, page_base(page, 1, t.g), ATTN_PAGE_BYTES, &full_bar[sl]);
           }
         }
+        ++gs;
+        if (++sl == ATTN_STAGES) {
+          sl = 0;
+          ph ^= 1u;
+        }
       }
+      t = tn;
+      slot = slotn;
+      pg0 = pn0;
+      pg1 = pn1;
+    }
+    if (lane == 0) {
       attn_stamp(a, 6);
       for (int j = gs > ATTN_STAGES ? gs - ATTN_STAGES : 0; j < gs; ++j)  // drain
         mbar_wait(&full_bar[j % ATTN_STAGES], static_cast<uint32_t>((j / ATTN_STAGES) & 1), nullptr,
