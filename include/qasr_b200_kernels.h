@@ -53,7 +53,10 @@ qasr_status qasr_kernel_gemm_traced(int device, void* stream, int weight_format,
 
 /* GQA attention of `rows` query rows over their slot's paged KV (gqa_decode_* /
  * gqa_split_merge, src/shaders.rs:1881-2905).  q/out: [rows, q_ld] f16 (q heads 2g and
- * 2g+1 read kv head g); kv_pool: [pages][layers][2][nkv][64][128] f16; page_table:
+ * 2g+1 read kv head g); kv_pool: [pages][layers][2][nkv][64][128] f16 with each
+ * 128-dim row stored swizzled: dim d of position p sits at column
+ * ((d/8) ^ (p%8))*8 + d%8 (16-byte chunks permuted by the position's low 3 bits, so
+ * tensor-core fragment loads from shared memory are bank-conflict free); page_table:
  * [slots][max_pages] int32; row r attends positions 0..row_pos[r] of slot row_slot[r]. */
 qasr_status qasr_kernel_attention(int device, void* stream, const uint16_t* q, int q_ld,
                                   uint16_t* out, const uint16_t* kv_pool, const int* page_table,
@@ -92,7 +95,8 @@ qasr_status qasr_kernel_attention_noalloc(int device, void* stream, const uint16
                                           const int* row_pos, int rows, char* err, int errlen);
 
 /* Append K and V rows ([rows, nkv*128] f16 each) at (row_slot[r], row_pos[r]) of
- * layer `layer` — the cache writes of qkv_extract(_slots) (src/shaders.rs:1376-1635). */
+ * layer `layer`, in the swizzled row layout qasr_kernel_attention reads — the cache
+ * writes of qkv_extract(_slots) (src/shaders.rs:1376-1635). */
 qasr_status qasr_kernel_kv_append(int device, void* stream, const uint16_t* k, const uint16_t* v,
                                   uint16_t* kv_pool, const int* page_table, int max_pages,
                                   int layers, int nkv, int layer, const int* row_slot,

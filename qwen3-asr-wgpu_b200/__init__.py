@@ -401,6 +401,16 @@ def kernel_kv_append(device: int, stream: int, k_ptr: int, v_ptr: int, pool_ptr:
         raise DecoderError(st, err.value.decode())
 
 
+def kv_page_swizzle(pool: np.ndarray) -> np.ndarray:
+    """Convert KV pool pages [..., 64, 128] between the logical row layout and the
+    swizzled one the kernels use (dim d of position p at column ((d // 8) ^ (p % 8)) * 8
+    + d % 8).  The map is its own inverse, so the same call converts both ways."""
+    p = np.arange(PAGE_POSITIONS)[:, None]
+    d = np.arange(128)[None, :]
+    col = (((d >> 3) ^ (p & 7)) << 3) | (d & 7)
+    return np.take_along_axis(pool, np.broadcast_to(col, pool.shape), axis=-1)
+
+
 def version() -> str:
     return lib.qasr_version().decode()
 
@@ -409,7 +419,7 @@ __all__ = [
     "TextDecoder", "DecoderError", "SyntheticModel", "MODEL_PRESETS", "text_config",
     "build_rope_tables", "dim_map", "kernel_pack_weights", "kernel_gemm", "kernel_attention_noalloc", "kernel_attention", "kernel_kv_append",
     "launch_count", "version", "WEIGHTS_F16", "WEIGHTS_INT8", "EXPORTED_SYMBOLS", "lib",
-    "f16_bits_to_f32", "f32_to_f16_bits", "PAGE_POSITIONS",
+    "f16_bits_to_f32", "f32_to_f16_bits", "PAGE_POSITIONS", "kv_page_swizzle",
 ]
 
 if os.environ.get("QASR_B200_VERBOSE"):

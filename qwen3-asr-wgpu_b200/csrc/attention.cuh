@@ -19,12 +19,12 @@
 // Persistent CTA per SM: warp 8 streams the pages of the CTA's units (and each unit's q
 // rows, with its first stage), stage after stage, into a 3-deep shared-memory ring with
 // cp.async.bulk (completion counted on mbarriers, no multicast); warps 0-7 each take 16
-// positions of a stage, lane l holding dims [4l, 4l+4): 32 partial dot products
-// (16 positions x 2 heads) are finished by one 5-round transposing butterfly and the
-// softmax is online per head and warp.  At a unit's end the consumer warps drop their
-// state into a double-buffered shared slot and move on; warp 9 merges the 8 warps,
-// stores the output (or the chunk's partial), and the CTA that finishes a row's last
-// chunk merges the chunks in index order (atomic counter, no waiting).
+// positions of a stage and compute S = Q K^T and O += P V on the tensor cores
+// (mma.sync: with two real query rows per kv head the work is too thin for tcgen05) with
+// an online softmax per head and warp.  At a unit's end the consumer warps drop their
+// state into a double-buffered shared slot and move on; warp 9 merges the 8 warps and
+// stores the output or, for a row cut into several chunks, the chunk's partial, which
+// attention_merge_kernel combines in chunk order.
 #pragma once
 #include "device_common.cuh"
 #include "gemm_tc.cuh"  // KvLayout, kv_elem_offset, griddep_*
@@ -65,9 +65,7 @@ struct AttnArgs {
   int layer;
   int rows;
   float scale;
-  float* ws;        // [rows * nkv * ATTN_ROW_CHUNKS][ATTN_PART_FLOATS]
-  int* counters;    // [rows * nkv], zero between launches
-  int max_chunks;
+  float* ws;        // [rows * nkv * ATTN_ROW_CHUNKS][ATTN_PART_FLOATS]: chunk partials
   uint32_t* status;
   unsigned long long* trace;  // optional: per CTA ATTN_TRACE_SLOTS %globaltimer stamps
 };
@@ -78,6 +76,28 @@ constexpr int ATTN_TRACE_SLOTS = 8;
 // 7 units processed by this CTA
 __device__ __forceinline__ void attn_stamp(const AttnArgs& a, int slot) {
   if (a.trace != nullptr) a.trace[blockIdx.x * ATTN_TRACE_SLOTS + slot] = globaltimer();
+}
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                            uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                                  uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+// D += A B, m16n8k16, f16 operands, f32 accumulators
+__device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 struct AttnUnit {
@@ -112,7 +132,6 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
   __shared__ __align__(16) __half sm_q[ATTN_STAGES][256];             // q of heads 2g, 2g+1
   __shared__ float sm_m[2][ATTN_CONSUMER_WARPS][2], sm_l[2][ATTN_CONSUMER_WARPS][2];
   __shared__ __align__(16) float sm_acc[2][ATTN_CONSUMER_WARPS][2][128];
-  __shared__ __align__(16) float sm_p[ATTN_CONSUMER_WARPS][32];
   __shared__ int sh_units, sh_scan[ATTN_THREADS / 32];
   __shared__ volatile int abort_flag;
 
@@ -253,13 +272,15 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
     }
   } else if (warp == ATTN_CONSUMER_WARPS + 1) {
     // ------------------------------------------------------------ merger
+    // Combines the 8 warps of a unit; stores the output (one-chunk rows) or the chunk's
+    // partial (m, l, o) for attention_merge_kernel.  No fence or atomic on this path.
     int k = 0;
     for (int u = blockIdx.x; u < U; u += gridDim.x, ++k) {
       const AttnUnit t = attn_unit(a, prefix, u);
       const int b = k & 1;
       if (!mbar_wait_warp(&mfull_bar[b], static_cast<uint32_t>((k >> 1) & 1), &abort_flag, a.status, 0x604))
         break;
-      // lane covers dims [4 lane, +4) of both heads; combine the 8 warps
+      // lane covers dims [4 lane, +4) of both heads
       float M[2], Ls[2], O[2][4];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
@@ -288,97 +309,46 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&mfree_bar[b]);  // state read: the consumers may reuse the buffer
       if (lane == 0 && k == 0) attn_stamp(a, 3);
-      __half* outp = a.out + static_cast<size_t>(t.r) * a.q_ld + (2 * t.g) * 128 + 4 * lane;
       if (t.nch == 1) {
+        __half* outp = a.out + static_cast<size_t>(t.r) * a.q_ld + (2 * t.g) * 128 + 4 * lane;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const float inv = 1.0f / Ls[h];
           __half2 v01 = __floats2half2_rn(O[h][0] / Ls[h], O[h][1] / Ls[h]);
           __half2 v23 = __floats2half2_rn(O[h][2] / Ls[h], O[h][3] / Ls[h]);
-          (void)inv;
           uint2 pk;
           pk.x = *reinterpret_cast<uint32_t*>(&v01);
           pk.y = *reinterpret_cast<uint32_t*>(&v23);
           *reinterpret_cast<uint2*>(outp + h * 128) = pk;
         }
       } else {
-        const size_t pidx = (static_cast<size_t>(t.r) * nkv + t.g) * ATTN_ROW_CHUNKS;
-        float* part = a.ws + (pidx + t.c) * ATTN_PART_FLOATS;
-        if (lane == 0) {
-          part[0] = M[0];
-          part[1] = M[1];
-          part[2] = Ls[0];
-          part[3] = Ls[1];
-        }
+        float* part = a.ws + ((static_cast<size_t>(t.r) * nkv + t.g) * ATTN_ROW_CHUNKS + t.c) * ATTN_PART_FLOATS;
+        if (lane == 0) *reinterpret_cast<float4*>(part) = make_float4(M[0], M[1], Ls[0], Ls[1]);
 #pragma unroll
         for (int h = 0; h < 2; ++h)
-          __stcg(reinterpret_cast<float4*>(part + 4 + h * 128 + 4 * lane),
-                 make_float4(O[h][0], O[h][1], O[h][2], O[h][3]));
-        __threadfence();
-        __syncwarp();
-        int last = 0;
-        if (lane == 0) last = (atomicAdd(a.counters + t.r * nkv + t.g, 1) == t.nch - 1) ? 1 : 0;
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (last) {
-          __threadfence();
-          const float* parts = a.ws + pidx * ATTN_PART_FLOATS;
-          float mc[ATTN_ROW_CHUNKS][2], lc[ATTN_ROW_CHUNKS][2];
-          float4 oc[ATTN_ROW_CHUNKS][2];
-#pragma unroll
-          for (int cc = 0; cc < ATTN_ROW_CHUNKS; ++cc) {  // independent loads, all in flight
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              if (cc < t.nch) {
-                mc[cc][h] = __ldcg(parts + cc * ATTN_PART_FLOATS + h);
-                lc[cc][h] = __ldcg(parts + cc * ATTN_PART_FLOATS + 2 + h);
-                oc[cc][h] = __ldcg(reinterpret_cast<const float4*>(parts + cc * ATTN_PART_FLOATS + 4 + h * 128 + 4 * lane));
-              } else {
-                mc[cc][h] = -INFINITY;
-                lc[cc][h] = 0.f;
-                oc[cc][h] = make_float4(0.f, 0.f, 0.f, 0.f);
-              }
-            }
-          }
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            float mx = -INFINITY;
-#pragma unroll
-            for (int cc = 0; cc < ATTN_ROW_CHUNKS; ++cc) mx = fmaxf(mx, mc[cc][h]);
-            float ls = 0.f;
-            float o[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int cc = 0; cc < ATTN_ROW_CHUNKS; ++cc) {
-              if (mc[cc][h] == -INFINITY) continue;
-              const float f = expf(mc[cc][h] - mx);
-              ls += lc[cc][h] * f;
-              o[0] += oc[cc][h].x * f;
-              o[1] += oc[cc][h].y * f;
-              o[2] += oc[cc][h].z * f;
-              o[3] += oc[cc][h].w * f;
-            }
-            __half2 v01 = __floats2half2_rn(o[0] / ls, o[1] / ls);
-            __half2 v23 = __floats2half2_rn(o[2] / ls, o[3] / ls);
-            uint2 pk;
-            pk.x = *reinterpret_cast<uint32_t*>(&v01);
-            pk.y = *reinterpret_cast<uint32_t*>(&v23);
-            *reinterpret_cast<uint2*>(outp + h * 128) = pk;
-          }
-          if (lane == 0) a.counters[t.r * nkv + t.g] = 0;
-        }
+          *reinterpret_cast<float4*>(part + 4 + h * 128 + 4 * lane) = make_float4(O[h][0], O[h][1], O[h][2], O[h][3]);
       }
     }
     if (lane == 0) attn_stamp(a, 5);
   } else {
-    // ------------------------------------------------------------ consumers
+    // ------------------------------------------------------------ consumers (tensor cores)
+    // Per stage a warp owns 16 positions.  S = Q K^T with mma.sync m16n8k16: A = the two q
+    // heads as rows 0 and 1 of a 16-row tile (the rest zero), B = K rows fetched with
+    // ldmatrix; O += P V with P (f32) split into two f16 terms p_hi + p_lo so the weights
+    // keep ~22 bits.  Lane (g4 = lane / 4, tig = lane % 4) holds for g4 < 2 the scores of
+    // head g4 at positions {2 tig, 2 tig + 1, 8 + 2 tig, 9 + 2 tig} and O[head g4][8 nt +
+    // 2 tig, +1] for the 16 n-tiles nt.
+    const int g4 = lane >> 2, tig = lane & 3;
+    const int lrow = lane & 7, lmat = lane >> 3;
     int sl = 0, k = 0;
     uint32_t ph = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < U && ok; u += gridDim.x, ++k) {
       const AttnUnit t = attn_unit(a, prefix, u);
-      float qa[4], qb[4];
-      // lanes 0-15 carry head 2g's running max / partial sum, lanes 16-31 head 2g+1's
+      uint32_t qf[8][2];
+      float o[16][4];
+#pragma unroll
+      for (int nt = 0; nt < 16; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
       float m = -INFINITY, l = 0.f;
-      float acc_a[4] = {0.f, 0.f, 0.f, 0.f}, acc_b[4] = {0.f, 0.f, 0.f, 0.f};
       for (int st = t.s0; st < t.s1; ++st) {
         if (!mbar_wait_warp(&full_bar[sl], ph, &abort_flag, a.status, 0x603)) {
           ok = false;
@@ -386,82 +356,67 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
         }
         if (k == 0 && st == t.s0 && tid == 0) attn_stamp(a, 2);
         if (st == t.s0) {
-          const uint2 qa2 = *reinterpret_cast<const uint2*>(&sm_q[sl][4 * lane]);
-          const uint2 qb2 = *reinterpret_cast<const uint2*>(&sm_q[sl][128 + 4 * lane]);
-          const float2 a01 = __half22float2(*reinterpret_cast<const __half2*>(&qa2.x));
-          const float2 a23 = __half22float2(*reinterpret_cast<const __half2*>(&qa2.y));
-          const float2 b01 = __half22float2(*reinterpret_cast<const __half2*>(&qb2.x));
-          const float2 b23 = __half22float2(*reinterpret_cast<const __half2*>(&qb2.y));
-          qa[0] = a01.x; qa[1] = a01.y; qa[2] = a23.x; qa[3] = a23.y;
-          qb[0] = b01.x; qb[1] = b01.y; qb[2] = b23.x; qb[3] = b23.y;
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            qf[ks][0] = g4 < 2 ? *reinterpret_cast<const uint32_t*>(&sm_q[sl][g4 * 128 + 16 * ks + 2 * tig]) : 0u;
+            qf[ks][1] = g4 < 2 ? *reinterpret_cast<const uint32_t*>(&sm_q[sl][g4 * 128 + 16 * ks + 8 + 2 * tig]) : 0u;
+          }
         }
         const int tw = st * 128 + warp * 16;  // first position of this warp's 16
         if (tw < t.len) {
           const uint8_t* buf = smem + static_cast<size_t>(sl) * ATTN_STAGE_BYTES;
-          const __half* kbuf = reinterpret_cast<const __half*>(buf) + warp * 16 * 128;
-          const __half* vbuf = reinterpret_cast<const __half*>(buf + 2 * ATTN_PAGE_BYTES) + warp * 16 * 128;
-          float v[32];
+          const uint32_t kb = smem_u32(buf) + warp * 16 * 256;
+          const uint32_t vb = smem_u32(buf + 2 * ATTN_PAGE_BYTES) + warp * 16 * 256;
+          float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+          {
+            const int pl = (lmat >> 1) * 8 + lrow;  // position this lane addresses
 #pragma unroll
-          for (int p = 0; p < 16; ++p) {
-            const uint2 kr = *reinterpret_cast<const uint2*>(kbuf + p * 128 + 4 * lane);
-            const float2 k01 = __half22float2(*reinterpret_cast<const __half2*>(&kr.x));
-            const float2 k23 = __half22float2(*reinterpret_cast<const __half2*>(&kr.y));
-            v[p] = fmaf(qa[3], k23.y, fmaf(qa[2], k23.x, fmaf(qa[1], k01.y, qa[0] * k01.x)));
-            v[16 + p] = fmaf(qb[3], k23.y, fmaf(qb[2], k23.x, fmaf(qb[1], k01.y, qb[0] * k01.x)));
-          }
-          // transposing butterfly: lane j ends with the full dot product of value j
-#pragma unroll
-          for (int o = 16; o >= 1; o >>= 1) {
-            const bool upper = (lane & o) != 0;
-#pragma unroll
-            for (int j = 0; j < o; ++j) {
-              const float send = upper ? v[j] : v[j + o];
-              const float keep = upper ? v[j + o] : v[j];
-              v[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+            for (int ks = 0; ks < 8; ++ks) {
+              const int chunk = 2 * ks + (lmat & 1);
+              uint32_t b0, b1, b2, b3;
+              ldmatrix_x4(kb + pl * 256 + ((chunk ^ lrow) << 4), b0, b1, b2, b3);
+              mma_16816(s0, qf[ks][0], 0u, qf[ks][1], 0u, b0, b1);
+              mma_16816(s1, qf[ks][0], 0u, qf[ks][1], 0u, b2, b3);
             }
           }
-          const bool valid = tw + (lane & 15) < t.len;
-          const float s = valid ? v[0] * a.scale : -INFINITY;
-          float bm = s;
-#pragma unroll
-          for (int o = 8; o >= 1; o >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
-          const float mn = fmaxf(m, bm);
+          float sc[4] = {s0[0] * a.scale, s0[1] * a.scale, s1[0] * a.scale, s1[1] * a.scale};
+          const int pos0 = tw + 2 * tig;
+          const bool v0 = pos0 < t.len, v1 = pos0 + 1 < t.len, v2 = pos0 + 8 < t.len, v3 = pos0 + 9 < t.len;
+          if (!v0) sc[0] = -INFINITY;
+          if (!v1) sc[1] = -INFINITY;
+          if (!v2) sc[2] = -INFINITY;
+          if (!v3) sc[3] = -INFINITY;
+          float mx = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+          const float mn = fmaxf(m, mx);
           const float corr = (m == mn) ? 1.0f : expf(m - mn);
-          const float p = valid ? expf(s - mn) : 0.0f;
-          l = l * corr + p;
+          const float p0 = v0 ? expf(sc[0] - mn) : 0.f, p1 = v1 ? expf(sc[1] - mn) : 0.f;
+          const float p2 = v2 ? expf(sc[2] - mn) : 0.f, p3 = v3 ? expf(sc[3] - mn) : 0.f;
+          l = l * corr + ((p0 + p1) + (p2 + p3));
           m = mn;
-          sm_p[warp][lane] = p;
-          const float ca = __shfl_sync(0xffffffffu, corr, 0);
-          const float cb = __shfl_sync(0xffffffffu, corr, 16);
 #pragma unroll
-          for (int d = 0; d < 4; ++d) {
-            acc_a[d] *= ca;
-            acc_b[d] *= cb;
+          for (int nt = 0; nt < 16; ++nt) {
+            o[nt][0] *= corr;
+            o[nt][1] *= corr;
           }
-          __syncwarp();
-          const int nvalid = min(16, t.len - tw);
+          const __half2 h01 = __floats2half2_rn(p0, p1), h23 = __floats2half2_rn(p2, p3);
+          const float2 r01 = __half22float2(h01), r23 = __half22float2(h23);
+          const __half2 l01 = __floats2half2_rn(p0 - r01.x, p1 - r01.y);
+          const __half2 l23 = __floats2half2_rn(p2 - r23.x, p3 - r23.y);
+          const uint32_t ah0 = *reinterpret_cast<const uint32_t*>(&h01), ah2 = *reinterpret_cast<const uint32_t*>(&h23);
+          const uint32_t al0 = *reinterpret_cast<const uint32_t*>(&l01), al2 = *reinterpret_cast<const uint32_t*>(&l23);
+          {
+            const int pl = (lmat & 1) * 8 + lrow;
 #pragma unroll
-          for (int p4 = 0; p4 < 4; ++p4) {
-            const float4 pa4 = *reinterpret_cast<const float4*>(&sm_p[warp][4 * p4]);
-            const float4 pb4 = *reinterpret_cast<const float4*>(&sm_p[warp][16 + 4 * p4]);
-            const float pa[4] = {pa4.x, pa4.y, pa4.z, pa4.w};
-            const float pb[4] = {pb4.x, pb4.y, pb4.z, pb4.w};
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const int pp = 4 * p4 + q;
-              if (pp < nvalid) {
-                const uint2 vr = *reinterpret_cast<const uint2*>(vbuf + pp * 128 + 4 * lane);
-                const float2 v01 = __half22float2(*reinterpret_cast<const __half2*>(&vr.x));
-                const float2 v23 = __half22float2(*reinterpret_cast<const __half2*>(&vr.y));
-                acc_a[0] = fmaf(pa[q], v01.x, acc_a[0]);
-                acc_a[1] = fmaf(pa[q], v01.y, acc_a[1]);
-                acc_a[2] = fmaf(pa[q], v23.x, acc_a[2]);
-                acc_a[3] = fmaf(pa[q], v23.y, acc_a[3]);
-                acc_b[0] = fmaf(pb[q], v01.x, acc_b[0]);
-                acc_b[1] = fmaf(pb[q], v01.y, acc_b[1]);
-                acc_b[2] = fmaf(pb[q], v23.x, acc_b[2]);
-                acc_b[3] = fmaf(pb[q], v23.y, acc_b[3]);
-              }
+            for (int n2 = 0; n2 < 8; ++n2) {
+              const int chunk = 2 * n2 + (lmat >> 1);
+              uint32_t b0, b1, b2, b3;
+              ldmatrix_x4_trans(vb + pl * 256 + ((chunk ^ lrow) << 4), b0, b1, b2, b3);
+              mma_16816(o[2 * n2], ah0, 0u, ah2, 0u, b0, b1);
+              mma_16816(o[2 * n2], al0, 0u, al2, 0u, b0, b1);
+              mma_16816(o[2 * n2 + 1], ah0, 0u, ah2, 0u, b2, b3);
+              mma_16816(o[2 * n2 + 1], al0, 0u, al2, 0u, b2, b3);
             }
           }
         }
@@ -474,18 +429,21 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
       }
       if (!ok) break;
       // ---- hand this warp's state to the merger (double-buffered by unit parity)
-#pragma unroll
-      for (int o = 8; o >= 1; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+      l += __shfl_xor_sync(0xffffffffu, l, 1);
+      l += __shfl_xor_sync(0xffffffffu, l, 2);
       const int b = k & 1;
       if (!mbar_wait_warp(&mfree_bar[b], static_cast<uint32_t>(((k >> 1) & 1) ^ 1), &abort_flag, a.status,
                           0x605))
         break;
-      if (lane == 0 || lane == 16) {
-        sm_m[b][warp][lane >> 4] = m;
-        sm_l[b][warp][lane >> 4] = l;
+      if (g4 < 2) {
+        if (tig == 0) {
+          sm_m[b][warp][g4] = m;
+          sm_l[b][warp][g4] = l;
+        }
+#pragma unroll
+        for (int nt = 0; nt < 16; ++nt)
+          *reinterpret_cast<float2*>(&sm_acc[b][warp][g4][8 * nt + 2 * tig]) = make_float2(o[nt][0], o[nt][1]);
       }
-      *reinterpret_cast<float4*>(&sm_acc[b][warp][0][4 * lane]) = make_float4(acc_a[0], acc_a[1], acc_a[2], acc_a[3]);
-      *reinterpret_cast<float4*>(&sm_acc[b][warp][1][4 * lane]) = make_float4(acc_b[0], acc_b[1], acc_b[2], acc_b[3]);
       __syncwarp();
       if (lane == 0) mbar_arrive(&mfull_bar[b]);
     }
@@ -494,6 +452,41 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
       if (a.trace != nullptr) a.trace[blockIdx.x * ATTN_TRACE_SLOTS + 7] = static_cast<unsigned long long>(k);
     }
   }
+}
+
+// Rows cut into several chunks: merge the chunks' (m, l, o) in index order and store
+// the f16 output.  One CTA of 256 threads per (row, kv head); one-chunk rows exit.
+__global__ void __launch_bounds__(256) attention_merge_kernel(const __grid_constant__ AttnArgs a) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int nkv = a.kv.nkv;
+  const int r = blockIdx.x / nkv, g = blockIdx.x % nkv;
+  if (r >= a.rows) return;
+  const int len = a.row_pos[r] + 1;
+  const int nch = attn_row_chunks(len);
+  if (nch == 1) return;
+  const int h = threadIdx.x >> 7, d = threadIdx.x & 127;
+  const float* parts = a.ws + (static_cast<size_t>(r) * nkv + g) * ATTN_ROW_CHUNKS * ATTN_PART_FLOATS;
+  float mc[ATTN_ROW_CHUNKS], lc[ATTN_ROW_CHUNKS], oc[ATTN_ROW_CHUNKS];
+#pragma unroll
+  for (int c = 0; c < ATTN_ROW_CHUNKS; ++c) {  // independent loads, all in flight
+    const bool have = c < nch;
+    mc[c] = have ? parts[c * ATTN_PART_FLOATS + h] : -INFINITY;
+    lc[c] = have ? parts[c * ATTN_PART_FLOATS + 2 + h] : 0.f;
+    oc[c] = have ? parts[c * ATTN_PART_FLOATS + 4 + h * 128 + d] : 0.f;
+  }
+  float mx = -INFINITY;
+#pragma unroll
+  for (int c = 0; c < ATTN_ROW_CHUNKS; ++c) mx = fmaxf(mx, mc[c]);
+  float ls = 0.f, os = 0.f;
+#pragma unroll
+  for (int c = 0; c < ATTN_ROW_CHUNKS; ++c) {
+    if (mc[c] == -INFINITY) continue;
+    const float f = expf(mc[c] - mx);
+    ls += lc[c] * f;
+    os += oc[c] * f;
+  }
+  a.out[static_cast<size_t>(r) * a.q_ld + (2 * g + h) * 128 + d] = __float2half_rn(os / ls);
 }
 
 }  // namespace qasr

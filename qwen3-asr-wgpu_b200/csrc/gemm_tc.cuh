@@ -57,6 +57,14 @@ struct KvLayout {
   int nkv;
 };
 
+// Within a page, position p's 128 dims are one 256-byte row whose 16-byte chunk c is
+// stored at chunk c ^ (p & 7): eight consecutive positions of one chunk then sit in eight
+// different bank groups, which makes the attention kernel's ldmatrix reads conflict-free.
+__host__ __device__ __forceinline__ int kv_dim_swizzle(int pos, int d) {
+  return ((((d >> 3) ^ (pos & 7)) << 3) | (d & 7));
+}
+
+// Offset of the 128-dim row of (slot, pos) in the pool; add kv_dim_swizzle(pos, d).
 __device__ __forceinline__ size_t kv_elem_offset(const KvLayout& kv, int slot, int pos, int layer,
                                                  int which, int kvh) {
   const int page = kv.page_table[static_cast<size_t>(slot) * kv.max_pages + (pos >> 6)];
@@ -177,7 +185,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, EpiSmem& es, i
         const int n = nbase + j;
         if (n < a.rows) {
           const size_t off = kv_elem_offset(a.kv, a.row_slot[n], a.row_pos[n], a.layer, 1, kvh);
-          a.kv.pool[off + e] = __float2half_rn(v[j]);
+          a.kv.pool[off + kv_dim_swizzle(a.row_pos[n], e)] = __float2half_rn(v[j]);
         }
       }
       return;
@@ -219,7 +227,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, EpiSmem& es, i
           a.q_out[static_cast<size_t>(n) * a.q_ld + mt * 128 + e] = oh;
         } else {
           const size_t off = kv_elem_offset(a.kv, a.row_slot[n], pos, a.layer, 0, mt - nq);
-          a.kv.pool[off + e] = oh;
+          a.kv.pool[off + kv_dim_swizzle(pos, e)] = oh;
         }
       }
     }

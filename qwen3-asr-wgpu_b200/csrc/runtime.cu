@@ -279,8 +279,6 @@ struct qasr_ctx {
   int* gemm_cnt = nullptr;
   size_t gemm_cnt_n = 0;
   float* attn_ws = nullptr;
-  int* attn_cnt = nullptr;
-  int attn_max_chunks = ATTN_ROW_CHUNKS;
   uint32_t* status = nullptr;
   int* pinned_tok = nullptr;  // synchronous staging
   int* pinned_in = nullptr;   // input-token staging, reusable once ev_in completed
@@ -397,6 +395,13 @@ qasr_status run_gemm(qasr_ctx* c, const GemmLaunch& L) {
   return QASR_OK;
 }
 
+// attention_kernel and, behind it, attention_merge_kernel (rows cut into several chunks)
+cudaError_t launch_attention_pair(const AttnArgs& a, int sms, cudaStream_t st, bool pdl) {
+  cudaError_t e = launch_k(attention_kernel, dim3(sms), dim3(ATTN_THREADS), attn_smem_bytes(a.rows), st, pdl, a);
+  if (e != cudaSuccess) return e;
+  return launch_k(attention_merge_kernel, dim3(a.rows * a.kv.nkv), dim3(256), 0, st, pdl, a);
+}
+
 qasr_status launch_attention(qasr_ctx* c, int layer, int rows, const int* rs, const int* rp) {
   AttnArgs a{};
   a.q = c->q;
@@ -413,12 +418,8 @@ qasr_status launch_attention(qasr_ctx* c, int layer, int rows, const int* rs, co
   a.rows = rows;
   a.scale = 1.0f / std::sqrt(static_cast<float>(c->cfg.head_dim));
   a.ws = c->attn_ws;
-  a.counters = c->attn_cnt;
-  a.max_chunks = c->attn_max_chunks;
   a.status = c->status;
-  CK(launch_k(attention_kernel, dim3(c->num_sms), dim3(ATTN_THREADS), attn_smem_bytes(rows), c->stream, true,
-              a),
-     "attention launch");
+  CK(launch_attention_pair(a, c->num_sms, c->stream, true), "attention launch");
   return QASR_OK;
 }
 
@@ -697,9 +698,8 @@ qasr_status qasr_create(const qasr_text_config* cfg, const qasr_options* opts, i
   if ((s = dalloc(c, &c->gemm_ws, std::max<size_t>(wsf, 64), "GEMM workspace")) ||
       (s = dalloc(c, &c->gemm_cnt, cnt, "GEMM counters")))
     return s;
-  const size_t apart = R * t.num_key_value_heads * c->attn_max_chunks * ATTN_PART_FLOATS;
-  if ((s = dalloc(c, &c->attn_ws, apart, "attention workspace")) ||
-      (s = dalloc(c, &c->attn_cnt, R * t.num_key_value_heads, "attention counters")))
+  const size_t apart = R * t.num_key_value_heads * ATTN_ROW_CHUNKS * ATTN_PART_FLOATS;
+  if ((s = dalloc(c, &c->attn_ws, apart, "attention workspace")))
     return s;
   CK(cudaMallocHost(&c->pinned_tok, sizeof(int) * opts->max_slots * 2), "pinned alloc");
   CK(cudaMallocHost(&c->pinned_in, sizeof(int) * opts->max_slots * 2), "pinned alloc");
@@ -1198,14 +1198,6 @@ qasr_status qasr_kernel_attention_traced(int device, void* stream, const uint16_
       return probe_err(err, errlen, QASR_ERR_OOM, "attention workspace");
     P.ws_floats = need;
   }
-  if (static_cast<size_t>(rows) * nkv > P.cnt_n) {
-    if (P.cnt) cudaFree(P.cnt);
-    P.cnt = nullptr;
-    if (cudaMalloc(&P.cnt, rows * nkv * sizeof(int)) != cudaSuccess ||
-        cudaMemset(P.cnt, 0, rows * nkv * sizeof(int)) != cudaSuccess)
-      return probe_err(err, errlen, QASR_ERR_OOM, "attention counters");
-    P.cnt_n = static_cast<size_t>(rows) * nkv;
-  }
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
   AttnArgs a{};
@@ -1223,8 +1215,6 @@ qasr_status qasr_kernel_attention_traced(int device, void* stream, const uint16_
   a.rows = rows;
   a.scale = 1.0f / std::sqrt(128.0f);
   a.ws = P.ws;
-  a.counters = P.cnt;
-  a.max_chunks = max_chunks;
   a.trace = trace;
   std::string e;
   if (init_kernel_attrs(&e) != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, e);
@@ -1236,8 +1226,7 @@ qasr_status qasr_kernel_attention_traced(int device, void* stream, const uint16_
     b.out = a.out + static_cast<size_t>(r0) * q_ld;
     b.row_slot = row_slot + r0;
     b.row_pos = row_pos + r0;
-    const cudaError_t ce = launch_k(attention_kernel, dim3(sms), dim3(ATTN_THREADS), attn_smem_bytes(b.rows),
-                                    static_cast<cudaStream_t>(stream), false, b);
+    const cudaError_t ce = launch_attention_pair(b, sms, static_cast<cudaStream_t>(stream), false);
     if (ce != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, cudaGetErrorString(ce));
   }
   return QASR_OK;
@@ -1248,19 +1237,16 @@ qasr_status qasr_kernel_attention_traced(int device, void* stream, const uint16_
 // ============================================================================ no-alloc variant
 // Attention for callers that must not allocate device memory (see
 // qasr_kernel_attention_noalloc in include/qasr_b200_kernels.h).  Its scratch — the
-// per-(row, kv head) arrival counters and the chunk partials of the split-row merge —
-// is this file-scope array, sized for QASR_NOALLOC_MAX_ROWS rows x QASR_NOALLOC_MAX_KV
-// kv heads.  Every GPU that loads the library holds it until the process exits.  In host
+// chunk partials of the split-row merge — is this file-scope array, sized for
+// NOALLOC_MAX_ROWS rows x NOALLOC_MAX_KV kv heads; nothing in it needs clearing
+// between calls (every partial a merge reads is written by the same call).  Every GPU that loads the library holds it until the process exits.  In host
 // code `g_attn_noalloc_scratch` only names the symbol; the device address comes from
 // cudaGetSymbolAddress, once per device.
 namespace qasr {
 constexpr int NOALLOC_MAX_ROWS = 64;
 constexpr int NOALLOC_MAX_KV = 8;
-constexpr size_t NOALLOC_COUNTER_BYTES = static_cast<size_t>(NOALLOC_MAX_ROWS) * NOALLOC_MAX_KV * sizeof(int);
-constexpr size_t NOALLOC_PARTIAL_BYTES = static_cast<size_t>(NOALLOC_MAX_ROWS) * NOALLOC_MAX_KV *
-                                         ATTN_ROW_CHUNKS * ATTN_PART_FLOATS * sizeof(float);
-constexpr size_t NOALLOC_SCRATCH_BYTES = NOALLOC_COUNTER_BYTES + NOALLOC_PARTIAL_BYTES;  // ~2 MiB
-static_assert(NOALLOC_COUNTER_BYTES % 256 == 0, "partials must stay 256-byte aligned");
+constexpr size_t NOALLOC_SCRATCH_BYTES = static_cast<size_t>(NOALLOC_MAX_ROWS) * NOALLOC_MAX_KV *
+                                         ATTN_ROW_CHUNKS * ATTN_PART_FLOATS * sizeof(float);  // ~2 MiB
 }  // namespace qasr
 
 static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[qasr::NOALLOC_SCRATCH_BYTES];
@@ -1297,13 +1283,8 @@ extern "C" qasr_status qasr_kernel_attention_noalloc(int device, void* stream, c
                          cudaGetErrorString(g_noalloc_setup[device]));
   std::string e;
   if (init_kernel_attrs(&e) != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, e);
-  unsigned char* scratch = static_cast<unsigned char*>(g_noalloc_addr[device]);
-  int* counters = reinterpret_cast<int*>(scratch);
-  float* partials = reinterpret_cast<float*>(scratch + NOALLOC_COUNTER_BYTES);
+  float* partials = static_cast<float*>(g_noalloc_addr[device]);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // the counters must start at zero; the array keeps whatever the last call left
-  cudaError_t ce = cudaMemsetAsync(counters, 0, static_cast<size_t>(rows) * nkv * sizeof(int), st);
-  if (ce != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, cudaGetErrorString(ce));
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
   AttnArgs a{};
@@ -1321,9 +1302,7 @@ extern "C" qasr_status qasr_kernel_attention_noalloc(int device, void* stream, c
   a.rows = rows;
   a.scale = 1.0f / std::sqrt(128.0f);
   a.ws = partials;
-  a.counters = counters;
-  a.max_chunks = ATTN_ROW_CHUNKS;
-  ce = launch_k(attention_kernel, dim3(sms), dim3(ATTN_THREADS), attn_smem_bytes(rows), st, false, a);
+  const cudaError_t ce = launch_attention_pair(a, sms, st, false);
   if (ce != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, cudaGetErrorString(ce));
   return QASR_OK;
 }
@@ -1336,8 +1315,9 @@ __global__ void kv_append_kernel(const __half* __restrict__ k, const __half* __r
   const int ld = kv.nkv * 128;
   const size_t ko = kv_elem_offset(kv, row_slot[r], row_pos[r], layer, 0, h);
   const size_t vo = kv_elem_offset(kv, row_slot[r], row_pos[r], layer, 1, h);
-  kv.pool[ko + d] = k[static_cast<size_t>(r) * ld + h * 128 + d];
-  kv.pool[vo + d] = v[static_cast<size_t>(r) * ld + h * 128 + d];
+  const int sd = kv_dim_swizzle(row_pos[r], d);
+  kv.pool[ko + sd] = k[static_cast<size_t>(r) * ld + h * 128 + d];
+  kv.pool[vo + sd] = v[static_cast<size_t>(r) * ld + h * 128 + d];
 }
 }  // namespace qasr
 

@@ -163,7 +163,8 @@ class SyntheticModel:
         Layout: n_before text rows, n_audio audio rows, n_text - n_before text rows.
         `stream` keys the draw (slot * 65536 + refill index)."""
         hs = self.cfg["hidden_size"]
-        ids = uniform_ids(n_text, self.seed, T_PREFIX_IDS + stream)
+        ids = uniform_ids(n_text, self.seed, T_PREFIX_IDS + stream,
+                          hi=min(TEXT_ID_HIGH, self.cfg["vocab_size"]))
         audio = normal_f16((n_audio, hs), self.seed, T_PREFIX_AUDIO + stream, 0.0, 0.05)
         emb = self.embed
         rows = [emb[ids[:n_before]], audio, emb[ids[n_before:]]]

@@ -116,7 +116,7 @@ def _attention_case(qasr, torch, oracle, lens, seed, nkv=8, layers=2, layer=1):
     q = synth.normal_f16((rows, 2 * nkv * 128), seed, 8, 0.0, 1.0)
     row_slot = np.arange(rows, dtype=np.int32)
     row_pos = np.array([l - 1 for l in lens], np.int32)
-    d_pool, d_pt, d_q = _dev(pool, torch), _dev(page_table, torch), _dev(q, torch)
+    d_pool, d_pt, d_q = _dev(qasr.kv_page_swizzle(pool), torch), _dev(page_table, torch), _dev(q, torch)
     d_rs, d_rp = _dev(row_slot, torch), _dev(row_pos, torch)
     out = torch.zeros((rows, 2 * nkv * 128), dtype=torch.int16, device="cuda")
     qasr.kernel_attention(0, 0, d_q.data_ptr(), 2 * nkv * 128, out.data_ptr(), d_pool.data_ptr(),
@@ -172,7 +172,7 @@ def test_kv_append_then_attention(qasr, cuda_device):
     qasr.kernel_kv_append(0, 0, dk.data_ptr(), dv.data_ptr(), pool.data_ptr(), pt.data_ptr(), 2, layers, nkv,
                           0, drs.data_ptr(), drp.data_ptr(), rows)
     torch.cuda.synchronize()
-    P = pool.cpu().numpy().view(np.uint16)
+    P = qasr.kv_page_swizzle(pool.cpu().numpy().view(np.uint16))
     table = [[3, 5], [0, 7], [1, 2], [4, 6]]
     for r in range(rows):
         page = table[r][pos[r] // 64]
