@@ -21,6 +21,7 @@
 #include <vector>
 
 #include "attention.cuh"
+#include "decode_chain.cuh"
 #include "f16_host.h"
 #include "gemm_tc.cuh"
 #include "qasr_b200.h"
@@ -119,6 +120,7 @@ struct GemmLaunch {
 };
 
 static int g_dyn_smem_max = 0;
+static int g_chain_dyn_max = 0;
 
 template <bool I8, int EPI>
 static cudaError_t gemm_set_attr(int dyn) {
@@ -150,6 +152,13 @@ static cudaError_t init_kernel_attrs(std::string* err) {
     e = e ? e : gemm_set_attr<true, EPI_QKV>(d);
     e = e ? e : cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(attn_smem_bytes(ATTN_MAX_ROWS)));
+    cudaFuncAttributes fc{};
+    e = e ? e : cudaFuncGetAttributes(&fc, decode_chain_kernel);
+    if (e == cudaSuccess) {
+      g_chain_dyn_max = optin - static_cast<int>(fc.sharedSizeBytes) - 256;
+      e = cudaFuncSetAttribute(decode_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               g_chain_dyn_max);
+    }
     result = e;
   });
   if (result != cudaSuccess && err) *err = std::string("kernel attribute setup: ") + cudaGetErrorString(result);
@@ -192,6 +201,42 @@ static GemmShape gemm_shape(int n_out, int k, bool int8, int rows, int num_sms) 
   s.max_seg = max_seg;
   s.ws_floats = max_seg > 1 ? static_cast<size_t>(s.tiles) * max_seg * s.n_tile * 128 : 0;
   return s;
+}
+
+// ----------------------------------------------------------------------------- decode chain
+struct ChainShape {
+  int n_tile, w_stages, a_stages;
+  size_t smem;
+};
+
+static ChainShape chain_shape(int rows) {
+  ChainShape s{};
+  s.n_tile = std::max(16, (rows + 15) / 16 * 16);
+  const int dcols = (s.n_tile + 31) / 32 * 32;
+  s.a_stages = std::min(CHAIN_MAX_A_STAGES, (static_cast<int>(GEMM_TMEM_COLS) - 2 * dcols) / 64);
+  const int xstage = 2 * s.n_tile * 128;
+  const int dyn = g_chain_dyn_max > 0 ? g_chain_dyn_max : 200 * 1024;
+  s.w_stages = std::min(CHAIN_MAX_W_STAGES, (dyn - 1024 - CHAIN_X_STAGES * xstage) / 16384);
+  s.smem = 1024 + static_cast<size_t>(s.w_stages) * 16384 + static_cast<size_t>(CHAIN_X_STAGES) * xstage;
+  return s;
+}
+
+// int8 GEMM of the chain: at least two units (32 KB of weights) per taking-part CTA
+static ChainGemm chain_gemm_plan(const uint8_t* w, const __half* scale, int n_out, int k, int xmap, int sms) {
+  ChainGemm g{};
+  g.w = w;
+  g.scale = scale;
+  g.kblocks = k / 128;
+  g.units = (n_out / 128) * g.kblocks;
+  g.grid = std::max(1, std::min(sms, g.units / 2));
+  int ms = 1;
+  for (int t = 0; t < n_out / 128; ++t) {
+    const long long a = static_cast<long long>(t) * g.kblocks;
+    ms = std::max(ms, cta_of_unit_host(a + g.kblocks - 1, g.units, g.grid) - cta_of_unit_host(a, g.units, g.grid) + 1);
+  }
+  g.max_seg = ms;
+  g.xmap = xmap;
+  return g;
 }
 
 static cudaError_t launch_gemm(const GemmLaunch& L, cudaStream_t st, bool pdl) {
@@ -279,6 +324,11 @@ struct qasr_ctx {
   int* gemm_cnt = nullptr;
   size_t gemm_cnt_n = 0;
   float* attn_ws = nullptr;
+  // decode chain (int8 weights, <= CHAIN_MAX_ROWS rows): partial sums and barrier counters
+  bool chain_ok = false;
+  float* chain_ws = nullptr;
+  size_t chain_ws_floats = 0;
+  unsigned int* chain_bar = nullptr;
   uint32_t* status = nullptr;
   int* pinned_tok = nullptr;  // synchronous staging
   int* pinned_in = nullptr;   // input-token staging, reusable once ev_in completed
@@ -459,18 +509,22 @@ qasr_status enqueue_layers(qasr_ctx* c, int rows, const int* rs, const int* rp, 
     g.args.out = c->h;
     g.args.ldo = hs;
     if ((s = run_gemm(c, g))) return s;
-    *nk += 7;
+    *nk += 8;
   }
   return QASR_OK;
 }
 
 // final norm + lm_head + argmax for `n` rows: xf[i] = norm(h[src_rows[i]]).
 qasr_status enqueue_head(qasr_ctx* c, int n, const int* src_rows, const int* slot_of,
-                         const int* pos_of, int* out_tok, int logit_row0, uint64_t* nk) {
+                         const int* pos_of, int* out_tok, int logit_row0, uint64_t* nk,
+                         bool norm = true) {
   const int hs = c->cfg.hidden_size;
-  CK(launch_k(rmsnorm_rows_kernel, dim3(n), dim3(256), 0, c->stream, true, c->xf, (const __half*)c->h,
-              src_rows, (const float*)c->final_norm, hs, c->cfg.rms_norm_eps),
-     "final norm launch");
+  if (norm) {
+    CK(launch_k(rmsnorm_rows_kernel, dim3(n), dim3(256), 0, c->stream, true, c->xf, (const __half*)c->h,
+                src_rows, (const float*)c->final_norm, hs, c->cfg.rms_norm_eps),
+       "final norm launch");
+    *nk += 1;
+  }
   GemmLaunch g;
   qasr_status s = plan_gemm(c, c->lm, c->xf, hs, n, EPI_LOGITS, &g);
   if (s) return s;
@@ -483,11 +537,14 @@ qasr_status enqueue_head(qasr_ctx* c, int n, const int* src_rows, const int* slo
   CK(launch_k(finalize_rows_kernel, dim3((n + 127) / 128), dim3(128), 0, c->stream, true, c->best, n,
               slot_of, pos_of, out_tok, c->next_tok_dev, c->pos_dev),
      "finalize launch");
-  *nk += 3;
+  *nk += 2;
   return QASR_OK;
 }
 
+qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk);
+
 qasr_status enqueue_decode(qasr_ctx* c, int n, uint64_t* nk) {
+  if (c->chain_ok && n <= CHAIN_MAX_ROWS) return enqueue_decode_chain(c, n, nk);
   CK(launch_k(embed_rows_kernel, dim3(n), dim3(128), 0, c->stream, true, c->h, (const __half*)c->embed,
               c->cfg.hidden_size, c->cfg.vocab_size, (const int*)c->drow_slot, (const int*)c->next_tok_dev,
               (const int*)c->pos_dev, c->drow_pos, c->status),
@@ -496,6 +553,148 @@ qasr_status enqueue_decode(qasr_ctx* c, int n, uint64_t* nk) {
   qasr_status s = enqueue_layers(c, n, c->drow_slot, c->drow_pos, nk);
   if (s) return s;
   return enqueue_head(c, n, nullptr, c->drow_slot, c->drow_pos, c->out_tok, 0, nk);
+}
+
+// One cooperative launch of decode_chain_kernel (one CTA per SM).
+qasr_status launch_chain(qasr_ctx* c, const ChainArgs& a, const ChainShape& sh, int n) {
+  const int hs = c->cfg.hidden_size, qd = c->cfg.num_attention_heads * c->cfg.head_dim;
+  const int I = c->cfg.intermediate_size;
+  CUtensorMap tx, ta, tact;
+  const uint32_t box = static_cast<uint32_t>(sh.n_tile);
+  if (!make_tmap(&tx, c->x, false, hs, n, static_cast<uint64_t>(hs) * 2, 64, box, &c->err) ||
+      !make_tmap(&ta, c->attn, false, qd, n, static_cast<uint64_t>(qd) * 2, 64, box, &c->err) ||
+      !make_tmap(&tact, c->act, false, I, n, static_cast<uint64_t>(I) * 2, 64, box, &c->err))
+    return QASR_ERR_DEVICE;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(c->num_sms);
+  cfg.blockDim = dim3(CHAIN_THREADS);
+  cfg.dynamicSmemBytes = sh.smem;
+  cfg.stream = c->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  CK(cudaLaunchKernelEx(&cfg, decode_chain_kernel, tx, ta, tact, a), "decode chain launch");
+  return QASR_OK;
+}
+
+// The int8 decode step as 1 + 3 L + 2 launches: chain (embed, norm, QKV 0), then per
+// layer attention + merge + chain (o_proj ... next layer's QKV, or the final norm),
+// then lm_head + argmax.
+qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
+  const ChainShape sh = chain_shape(n);
+  const int L = c->cfg.num_hidden_layers, hs = c->cfg.hidden_size, I = c->cfg.intermediate_size;
+  const int nq = c->cfg.num_attention_heads, nkv = c->cfg.num_key_value_heads;
+  const int qd = nq * c->cfg.head_dim, qkv_out = qd + 2 * nkv * 128;
+  const int sms = c->num_sms;
+  CK(cudaMemsetAsync(c->chain_bar, 0, static_cast<size_t>(L + 1) * sizeof(unsigned int), c->stream),
+     "chain barrier reset");
+  ChainArgs base{};
+  base.rows = n;
+  base.n_tile = sh.n_tile;
+  base.w_stages = sh.w_stages;
+  base.a_stages = sh.a_stages;
+  base.hs = hs;
+  base.inter = I;
+  base.nq = nq;
+  base.nkv = nkv;
+  base.eps = c->cfg.rms_norm_eps;
+  base.h = c->h;
+  base.q = c->q;
+  base.act = c->act;
+  base.embed = c->embed;
+  base.vocab = c->cfg.vocab_size;
+  base.row_slot = c->drow_slot;
+  base.row_pos = c->drow_pos;
+  base.next_tok = c->next_tok_dev;
+  base.pos = c->pos_dev;
+  base.rope_cos = c->rope_cos;
+  base.rope_sin = c->rope_sin;
+  base.kv.pool = c->kv_pool;
+  base.kv.page_table = c->page_table;
+  base.kv.max_pages = c->max_pages;
+  base.kv.layers = L;
+  base.kv.nkv = nkv;
+  base.ws = c->chain_ws;
+  base.status = c->status;
+  auto gemm = [&](const Linear& lin, int xmap) {
+    return chain_gemm_plan(static_cast<const uint8_t*>(lin.w), lin.scale, lin.n_out, lin.k, xmap, sms);
+  };
+  auto op = [](int kind, int g) {
+    ChainOp o{};
+    o.kind = kind;
+    o.gemm = g;
+    return o;
+  };
+  auto fits = [&](const ChainArgs& a) {
+    for (int i = 0; i < a.n_ops; ++i) {
+      if (a.ops[i].kind == CH_GEMM) continue;
+      const ChainGemm& g = a.gemms[a.ops[i].gemm];
+      const int tiles = g.units / g.kblocks;
+      if (static_cast<size_t>(tiles) * g.max_seg * sh.n_tile * 128 > c->chain_ws_floats) return false;
+    }
+    return true;
+  };
+  // chain 0: embed + input norm of layer 0, QKV GEMM, q/k norm + RoPE + K/V append
+  {
+    ChainArgs a = base;
+    a.barrier = c->chain_bar;
+    const LayerDev& L0 = c->layers[0];
+    a.gemms[0] = gemm(L0.qkv, 0);
+    a.ops[0] = op(CH_EMBED_NORM, 0);
+    a.ops[0].norm_w = L0.iln;
+    a.ops[0].norm_out = c->x;
+    a.ops[1] = op(CH_GEMM, 0);
+    a.ops[2] = op(CH_QKV, 0);
+    a.ops[2].qn_w = L0.qn;
+    a.ops[2].kn_w = L0.kn;
+    a.ops[2].layer = 0;
+    a.n_ops = 3;
+    if (!fits(a)) return fail(c, QASR_ERR_CAPACITY, "chain workspace too small");
+    qasr_status s = launch_chain(c, a, sh, n);
+    if (s) return s;
+  }
+  for (int l = 0; l < L; ++l) {
+    qasr_status s = launch_attention(c, l, n, c->drow_slot, c->drow_pos);
+    if (s) return s;
+    const LayerDev& Ld = c->layers[l];
+    ChainArgs a = base;
+    a.barrier = c->chain_bar + l + 1;
+    a.gemms[0] = gemm(Ld.o, 1);
+    a.gemms[1] = gemm(Ld.gu, 0);
+    a.gemms[2] = gemm(Ld.down, 2);
+    int k = 0;
+    a.ops[k++] = op(CH_GEMM, 0);
+    a.ops[k] = op(CH_RESID_NORM, 0);
+    a.ops[k].norm_w = Ld.pln;
+    a.ops[k++].norm_out = c->x;
+    a.ops[k++] = op(CH_GEMM, 1);
+    a.ops[k++] = op(CH_SILU, 1);
+    a.ops[k++] = op(CH_GEMM, 2);
+    a.ops[k] = op(CH_RESID_NORM, 2);
+    if (l + 1 < L) {
+      const LayerDev& Ln = c->layers[l + 1];
+      a.ops[k].norm_w = Ln.iln;
+      a.ops[k++].norm_out = c->x;
+      a.gemms[3] = gemm(Ln.qkv, 0);
+      a.ops[k++] = op(CH_GEMM, 3);
+      a.ops[k] = op(CH_QKV, 3);
+      a.ops[k].qn_w = Ln.qn;
+      a.ops[k].kn_w = Ln.kn;
+      a.ops[k++].layer = l + 1;
+    } else {
+      a.ops[k].norm_w = c->final_norm;
+      a.ops[k++].norm_out = c->xf;
+    }
+    a.n_ops = k;
+    if (!fits(a)) return fail(c, QASR_ERR_CAPACITY, "chain workspace too small");
+    if ((s = launch_chain(c, a, sh, n))) return s;
+  }
+  (void)qkv_out;
+  *nk += 1 + 3 * static_cast<uint64_t>(L);
+  return enqueue_head(c, n, nullptr, c->drow_slot, c->drow_pos, c->out_tok, 0, nk, false);
 }
 
 qasr_status ready(qasr_ctx* c) {
@@ -701,6 +900,22 @@ qasr_status qasr_create(const qasr_text_config* cfg, const qasr_options* opts, i
   const size_t apart = R * t.num_key_value_heads * ATTN_ROW_CHUNKS * ATTN_PART_FLOATS;
   if ((s = dalloc(c, &c->attn_ws, apart, "attention workspace")))
     return s;
+  // The int8 decode step runs as persistent chain launches when its shapes fit them.
+  const char* no_chain = std::getenv("QASR_B200_NO_CHAIN");
+  c->chain_ok = i8 && hs <= CHAIN_MAX_HS && hs % 256 == 0 && I % 64 == 0 &&
+                !(no_chain && no_chain[0] == '1');
+  if (c->chain_ok) {
+    const int n_tile = chain_shape(std::min(opts->max_slots, CHAIN_MAX_ROWS)).n_tile;
+    size_t cw = 0;
+    for (auto& sh : shapes) {
+      const ChainGemm g = chain_gemm_plan(nullptr, nullptr, sh[0], sh[1], 0, c->num_sms);
+      cw = std::max(cw, static_cast<size_t>(sh[0] / 128) * g.max_seg * n_tile * 128);
+    }
+    c->chain_ws_floats = cw;
+    if ((s = dalloc(c, &c->chain_ws, cw, "chain workspace")) ||
+        (s = dalloc(c, &c->chain_bar, static_cast<size_t>(L + 1), "chain barriers")))
+      return s;
+  }
   CK(cudaMallocHost(&c->pinned_tok, sizeof(int) * opts->max_slots * 2), "pinned alloc");
   CK(cudaMallocHost(&c->pinned_in, sizeof(int) * opts->max_slots * 2), "pinned alloc");
   CK(cudaEventCreateWithFlags(&c->ev_in, cudaEventDisableTiming), "event create");

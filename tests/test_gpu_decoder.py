@@ -97,15 +97,18 @@ def test_two_layer_decoder_matches_oracle(qasr, cuda_device, oracle, int8):
     _check(*_run_parity(qasr, oracle, cfg, int8, n_audio=[40, 7, 120], steps=12, n_slots=3))
 
 
-def test_batched_equals_serial(qasr, cuda_device, oracle):
+@pytest.mark.parametrize("int8", [False, True], ids=["f16", "int8-chain"])
+def test_batched_equals_serial(qasr, cuda_device, oracle, int8):
     """BatchProjections::step vs one slot at a time: identical ids
-    (src/bin/batch_step_bench.rs requires serial == fused)."""
+    (src/bin/batch_step_bench.rs requires serial == fused).  INT8 decode runs through
+    the persistent decode-chain kernel."""
     cfg = qasr.text_config("0.6b", num_hidden_layers=2)
     model = qasr.SyntheticModel(cfg, seed=77)
     cos, sin = qasr.build_rope_tables(1024)
     streams = []
+    fmt = qasr.WEIGHTS_INT8 if int8 else qasr.WEIGHTS_F16
     for batched in (False, True):
-        dec = qasr.TextDecoder(cfg, max_slots=4, max_seq=1024)
+        dec = qasr.TextDecoder(cfg, weight_format=fmt, max_slots=4, max_seq=1024)
         dec.load_model(model)
         dec.set_rope_tables(cos, sin)
         pre = [model.prefix(s, 30 + 11 * s)[0] for s in range(4)]
@@ -124,13 +127,15 @@ def test_batched_equals_serial(qasr, cuda_device, oracle):
     np.testing.assert_array_equal(streams[0][1:], streams[1][1:])
 
 
-def test_graph_replay_equals_eager(qasr, cuda_device):
+@pytest.mark.parametrize("int8", [False, True], ids=["f16", "int8-chain"])
+def test_graph_replay_equals_eager(qasr, cuda_device, int8):
     cfg = qasr.text_config("0.6b", num_hidden_layers=2)
     model = qasr.SyntheticModel(cfg, seed=5)
     cos, sin = qasr.build_rope_tables(512)
     runs = []
+    fmt = qasr.WEIGHTS_INT8 if int8 else qasr.WEIGHTS_F16
     for graph in (True, False):
-        dec = qasr.TextDecoder(cfg, max_slots=2, max_seq=512, use_graph=graph)
+        dec = qasr.TextDecoder(cfg, weight_format=fmt, max_slots=2, max_seq=512, use_graph=graph)
         dec.load_model(model)
         dec.set_rope_tables(cos, sin)
         slots = [dec.fork_capped(128), dec.fork_capped(128)]
@@ -138,6 +143,36 @@ def test_graph_replay_equals_eager(qasr, cuda_device):
         runs.append([list(dec.step_batch(slots)) for _ in range(8)])
         dec.close()
     assert runs[0] == runs[1]
+
+
+def test_decode_chain_matches_per_kernel_path(qasr, cuda_device, monkeypatch):
+    """The persistent decode-chain launches and the per-kernel launches compute the same
+    step (they differ only in f32 summation order): logits within the INT8 tolerance of
+    each other over 1.7B-shaped layers with 20 slots."""
+    cfg = qasr.text_config("1.7b", num_hidden_layers=3)
+    model = qasr.SyntheticModel(cfg, seed=31)
+    cos, sin = qasr.build_rope_tables(512)
+    logits, toks = [], []
+    for no_chain in ("0", "1"):
+        monkeypatch.setenv("QASR_B200_NO_CHAIN", no_chain)
+        dec = qasr.TextDecoder(cfg, weight_format=qasr.WEIGHTS_INT8, max_slots=20, max_seq=512,
+                               keep_logits=True)
+        dec.load_model(model)
+        dec.set_rope_tables(cos, sin)
+        slots = [dec.fork_capped(400) for _ in range(20)]
+        dec.prefill_batch(slots, [model.prefix(s, 17 + 13 * s)[0] for s in range(20)])
+        lg, tk = [], []
+        for step in range(4):
+            dec.set_input_tokens(slots, [(7919 * (step + 1) + 104729 * s) % 151000 for s in range(20)])
+            tk.append(list(map(int, dec.step_batch(slots))))
+            lg.append(dec.read_logits(20))
+        logits.append(np.stack(lg))
+        toks.append(np.array(tk))
+        dec.close()
+    err = float(np.max(np.abs(logits[0] - logits[1])))
+    print(f"chain vs per-kernel: max |dlogit| {err:.3g}, ids equal {np.mean(toks[0] == toks[1]):.3f}")
+    assert err <= INT8_TOL
+    assert np.mean(toks[0] == toks[1]) >= 0.9
 
 
 def test_errors_are_status_codes(qasr, cuda_device):
