@@ -79,6 +79,11 @@ typedef struct {
 #define QASR_FLAG_KEEP_LOGITS 1u
 /* Replay batched decode steps through a CUDA graph (default on). */
 #define QASR_FLAG_NO_GRAPH 2u
+/* Record per-CTA %globaltimer stamps inside the int8 decode-chain launches of each step
+ * (read with qasr_read_trace; a diagnostic like the reference's QWEN3_ASR_PROFILE
+ * timings, src/decoder.rs:84-96). */
+#define QASR_FLAG_TRACE 4u
+#define QASR_TRACE_SLOTS 128
 
 /* Weights of one decoder layer (HF names, src/cpu_decoder.rs:126-138).  Linear
  * weights are [out, in] row-major: q [nqh*hd, hs], k/v [nkv*hd, hs], o [hs, nqh*hd],
@@ -165,6 +170,15 @@ qasr_status qasr_step_batch(qasr_ctx* ctx, const int* slots, int n, int32_t* out
 /* Copy the f32 logits [rows, vocab] of the last prefill (one row per segment) or step
  * (one row per slot) — only with QASR_FLAG_KEEP_LOGITS. */
 qasr_status qasr_read_logits(qasr_ctx* ctx, float* out, int rows);
+/* Copy the stamps of the last decode step (QASR_FLAG_TRACE): [launch][cta][slot] uint64
+ * nanoseconds, launch = chain launch index of the step (layers + 1 of them), slot 0 =
+ * CTA entry, 1 + 2 i = operation i done by this CTA, 2 + 2 i = the barrier after it
+ * passed (i < 12), 25 + g = GEMM g's input seen ready, 29 + g = its first MMA issued,
+ * 33 + g = its last MMA issued, 40 + j / 104 + j = the CTA's j-th unit of the launch
+ * seen complete (A built, X landed) / its MMAs issued (j < 24),
+ * QASR_TRACE_SLOTS - 1 = exit; 0 where nothing happened.
+ * *count receives launches * ctas * slots; at most `cap` values are written. */
+qasr_status qasr_read_trace(qasr_ctx* ctx, uint64_t* out, int cap, int* count);
 
 /* --- host helpers of the reference's loader ------------------------------------ */
 /* compute_mrope_cos_sin + text_positions (src/mrope.rs:46-80) rounded to f16 the

@@ -34,6 +34,8 @@ WEIGHTS_F16 = 0
 WEIGHTS_INT8 = 1
 FLAG_KEEP_LOGITS = 1
 FLAG_NO_GRAPH = 2
+FLAG_TRACE = 4
+TRACE_SLOTS = 128
 PAGE_POSITIONS = 64
 
 # Every symbol include/*.h declares (checked by the CPU test suite).
@@ -43,6 +45,7 @@ EXPORTED_SYMBOLS = (
     "qasr_max_seq", "qasr_fork_capped", "qasr_slot_free", "qasr_ensure_capacity",
     "qasr_slot_pos", "qasr_set_slot_pos", "qasr_set_input_token", "qasr_set_input_tokens",
     "qasr_prefill", "qasr_step", "qasr_prefill_batch", "qasr_step_batch", "qasr_read_logits",
+    "qasr_read_trace",
     "qasr_build_rope_tables", "qasr_build_dim_map", "qasr_dequant_i8",
     "qasr_kernel_pack_weights", "qasr_kernel_gemm", "qasr_kernel_gemm_traced", "qasr_kernel_attention",
     "qasr_kernel_attention_noalloc", "qasr_kernel_attention_traced", "qasr_kernel_kv_append",
@@ -110,6 +113,7 @@ def _load() -> ctypes.CDLL:
     lib.qasr_prefill_batch.argtypes = [P, P, I, P, P, P, P]
     lib.qasr_step_batch.argtypes = [P, P, I, P]
     lib.qasr_read_logits.argtypes = [P, P, I]
+    lib.qasr_read_trace.argtypes = [P, P, I, ctypes.POINTER(I)]
     lib.qasr_build_rope_tables.argtypes = [P, P, I, I, ctypes.c_double, P, I, I]
     lib.qasr_build_dim_map.argtypes = [P, I, I, I, P]
     lib.qasr_dequant_i8.argtypes = [P, P, I, I, P]
@@ -166,12 +170,14 @@ class TextDecoder:
 
     def __init__(self, cfg: dict, *, weight_format: int = WEIGHTS_F16, max_slots: int = 1,
                  max_seq: int = 4096, kv_pages: int = 0, max_prefill_rows: int = 0,
-                 keep_logits: bool = False, use_graph: bool = True, device: int = 0):
+                 keep_logits: bool = False, use_graph: bool = True, trace: bool = False,
+                 device: int = 0):
         self.cfg = dict(cfg)
         self._tc = TextConfig(cfg["vocab_size"], cfg["hidden_size"], cfg["intermediate_size"],
                               cfg["num_hidden_layers"], cfg["num_attention_heads"],
                               cfg["num_key_value_heads"], cfg["head_dim"], cfg["rms_norm_eps"])
-        flags = (FLAG_KEEP_LOGITS if keep_logits else 0) | (0 if use_graph else FLAG_NO_GRAPH)
+        flags = ((FLAG_KEEP_LOGITS if keep_logits else 0) | (0 if use_graph else FLAG_NO_GRAPH) |
+                 (FLAG_TRACE if trace else 0))
         self._opts = Options(weight_format, max_slots, max_seq, kv_pages, max_prefill_rows, flags)
         self.weight_format = weight_format
         self.max_slots = max_slots
@@ -307,6 +313,16 @@ class TextDecoder:
         self._check(lib.qasr_step_batch(self._ctx, _ptr(s), len(s), None))
         return None
 
+    def read_trace(self) -> np.ndarray:
+        """%globaltimer stamps of the last decode step's chain launches (trace=True):
+        uint64 [launch, cta, TRACE_SLOTS] (see qasr_read_trace)."""
+        n = ctypes.c_int(0)
+        probe = np.zeros(1, dtype=np.uint64)
+        self._check(lib.qasr_read_trace(self._ctx, _ptr(probe), 0, ctypes.byref(n)))
+        out = np.zeros(n.value, dtype=np.uint64)
+        self._check(lib.qasr_read_trace(self._ctx, _ptr(out), n.value, ctypes.byref(n)))
+        return out.reshape(self.cfg["num_hidden_layers"] + 1, -1, TRACE_SLOTS)
+
     def read_logits(self, rows: int) -> np.ndarray:
         out = np.zeros((rows, self.cfg["vocab_size"]), dtype=np.float32)
         self._check(lib.qasr_read_logits(self._ctx, _ptr(out), rows))
@@ -419,7 +435,8 @@ __all__ = [
     "TextDecoder", "DecoderError", "SyntheticModel", "MODEL_PRESETS", "text_config",
     "build_rope_tables", "dim_map", "kernel_pack_weights", "kernel_gemm", "kernel_attention_noalloc", "kernel_attention", "kernel_kv_append",
     "launch_count", "version", "WEIGHTS_F16", "WEIGHTS_INT8", "EXPORTED_SYMBOLS", "lib",
-    "f16_bits_to_f32", "f32_to_f16_bits", "PAGE_POSITIONS", "kv_page_swizzle",
+    "f16_bits_to_f32", "f32_to_f16_bits", "PAGE_POSITIONS", "kv_page_swizzle", "FLAG_TRACE",
+    "TRACE_SLOTS",
 ]
 
 if os.environ.get("QASR_B200_VERBOSE"):

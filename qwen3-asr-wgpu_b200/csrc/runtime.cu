@@ -204,37 +204,54 @@ static GemmShape gemm_shape(int n_out, int k, bool int8, int rows, int num_sms) 
 }
 
 // ----------------------------------------------------------------------------- decode chain
+static_assert(CHAIN_TRACE_SLOTS == QASR_TRACE_SLOTS, "trace layout of the C ABI");
 struct ChainShape {
-  int n_tile, w_stages, a_stages;
+  int n_tile, w_stages, a_stages, n_acc;
   size_t smem;
 };
 
 static ChainShape chain_shape(int rows) {
   ChainShape s{};
   s.n_tile = std::max(16, (rows + 15) / 16 * 16);
-  const int dcols = (s.n_tile + 31) / 32 * 32;
+  const int dstr = (s.n_tile + 31) / 32 * 32;  // TMEM columns of one accumulator
+  // MMA issuer warps (one accumulator each): a thread issues a tcgen05 instruction only
+  // every ~120-230 cycles, so small-N units need several issuers
+  s.n_acc = dstr <= 32 ? 3 : (dstr <= 64 ? 2 : 1);
+  const int dcols = dstr * s.n_acc;
+  // unit slots: one 64-column A stage in TMEM and one X tile in shared memory each
   s.a_stages = std::min(CHAIN_MAX_A_STAGES, (static_cast<int>(GEMM_TMEM_COLS) - 2 * dcols) / 64);
   const int xstage = 2 * s.n_tile * 128;
   const int dyn = g_chain_dyn_max > 0 ? g_chain_dyn_max : 200 * 1024;
-  s.w_stages = std::min(CHAIN_MAX_W_STAGES, (dyn - 1024 - CHAIN_X_STAGES * xstage) / 16384);
-  s.smem = 1024 + static_cast<size_t>(s.w_stages) * 16384 + static_cast<size_t>(CHAIN_X_STAGES) * xstage;
+  s.w_stages = std::min(CHAIN_MAX_W_STAGES, (dyn - 1024 - s.a_stages * xstage) / 16384);
+  s.smem = 1024 + static_cast<size_t>(s.w_stages) * 16384 + static_cast<size_t>(s.a_stages) * xstage;
   return s;
 }
 
-// int8 GEMM of the chain: at least two units (32 KB of weights) per taking-part CTA
-static ChainGemm chain_gemm_plan(const uint8_t* w, const __half* scale, int n_out, int k, int xmap, int sms) {
+// bound on segments per tile for the chain GEMM kinds (QKV, o_proj, gate|up, down): the
+// reader of each adds that many partial slots with all loads in flight
+static int chain_seg_cap(int kind) {
+  return kind == 0 ? CHAIN_QKV_SEG : (kind == 2 ? CHAIN_SILU_SEG : CHAIN_MAX_SEG);
+}
+
+// int8 GEMM of the chain: at least two units (32 KB of weights) per taking-part CTA, and
+// few enough taking-part CTAs that no tile is cut into more than `max_seg_cap` segments
+// (the bound of the operation that adds the partials).
+static ChainGemm chain_gemm_plan(const uint8_t* w, const __half* scale, int n_out, int k, int xmap, int sms,
+                                 int max_seg_cap) {
   ChainGemm g{};
   g.w = w;
   g.scale = scale;
   g.kblocks = k / 128;
   g.units = (n_out / 128) * g.kblocks;
-  g.grid = std::max(1, std::min(sms, g.units / 2));
-  int ms = 1;
-  for (int t = 0; t < n_out / 128; ++t) {
-    const long long a = static_cast<long long>(t) * g.kblocks;
-    ms = std::max(ms, cta_of_unit_host(a + g.kblocks - 1, g.units, g.grid) - cta_of_unit_host(a, g.units, g.grid) + 1);
+  for (g.grid = std::max(1, std::min(sms, g.units / 2));; --g.grid) {
+    int ms = 1;
+    for (int t = 0; t < n_out / 128; ++t) {
+      const long long a = static_cast<long long>(t) * g.kblocks;
+      ms = std::max(ms, cta_of_unit_host(a + g.kblocks - 1, g.units, g.grid) - cta_of_unit_host(a, g.units, g.grid) + 1);
+    }
+    g.max_seg = ms;
+    if (ms <= max_seg_cap || g.grid == 1) break;
   }
-  g.max_seg = ms;
   g.xmap = xmap;
   return g;
 }
@@ -326,9 +343,13 @@ struct qasr_ctx {
   float* attn_ws = nullptr;
   // decode chain (int8 weights, <= CHAIN_MAX_ROWS rows): partial sums and barrier counters
   bool chain_ok = false;
-  float* chain_ws = nullptr;
-  size_t chain_ws_floats = 0;
+  float* chain_ws[4] = {};  // partial sums of the chain's QKV, o_proj, gate|up, down GEMMs
+  int chain_ws_rows = 0;
   unsigned int* chain_bar = nullptr;
+  float* chain_ss = nullptr;  // [CHAIN_MAX_ROWS][CHAIN_MAX_HS / 128]
+  int* chain_row_page = nullptr;        // [CHAIN_MAX_ROWS]
+  __half* chain_row_rope = nullptr;     // [CHAIN_MAX_ROWS][256]
+  unsigned long long* chain_trace = nullptr;  // QASR_FLAG_TRACE: [L + 1][sms][slots]
   uint32_t* status = nullptr;
   int* pinned_tok = nullptr;  // synchronous staging
   int* pinned_in = nullptr;   // input-token staging, reusable once ev_in completed
@@ -595,6 +616,7 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
   base.rows = n;
   base.n_tile = sh.n_tile;
   base.w_stages = sh.w_stages;
+  base.n_acc = sh.n_acc;
   base.a_stages = sh.a_stages;
   base.hs = hs;
   base.inter = I;
@@ -612,15 +634,21 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
   base.pos = c->pos_dev;
   base.rope_cos = c->rope_cos;
   base.rope_sin = c->rope_sin;
+  base.row_page = c->chain_row_page;
+  base.row_rope = c->chain_row_rope;
   base.kv.pool = c->kv_pool;
   base.kv.page_table = c->page_table;
   base.kv.max_pages = c->max_pages;
   base.kv.layers = L;
   base.kv.nkv = nkv;
-  base.ws = c->chain_ws;
+  base.ws_rows = c->chain_ws_rows;
+  base.ss = c->chain_ss;
   base.status = c->status;
-  auto gemm = [&](const Linear& lin, int xmap) {
-    return chain_gemm_plan(static_cast<const uint8_t*>(lin.w), lin.scale, lin.n_out, lin.k, xmap, sms);
+  auto gemm = [&](const Linear& lin, int xmap, int kind) {
+    ChainGemm g = chain_gemm_plan(static_cast<const uint8_t*>(lin.w), lin.scale, lin.n_out, lin.k, xmap, sms,
+                                  chain_seg_cap(kind));
+    g.ws = c->chain_ws[kind];
+    return g;
   };
   auto op = [](int kind, int g) {
     ChainOp o{};
@@ -628,21 +656,13 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
     o.gemm = g;
     return o;
   };
-  auto fits = [&](const ChainArgs& a) {
-    for (int i = 0; i < a.n_ops; ++i) {
-      if (a.ops[i].kind == CH_GEMM) continue;
-      const ChainGemm& g = a.gemms[a.ops[i].gemm];
-      const int tiles = g.units / g.kblocks;
-      if (static_cast<size_t>(tiles) * g.max_seg * sh.n_tile * 128 > c->chain_ws_floats) return false;
-    }
-    return true;
-  };
   // chain 0: embed + input norm of layer 0, QKV GEMM, q/k norm + RoPE + K/V append
   {
     ChainArgs a = base;
     a.barrier = c->chain_bar;
+    a.trace = c->chain_trace;
     const LayerDev& L0 = c->layers[0];
-    a.gemms[0] = gemm(L0.qkv, 0);
+    a.gemms[0] = gemm(L0.qkv, 0, 0);
     a.ops[0] = op(CH_EMBED_NORM, 0);
     a.ops[0].norm_w = L0.iln;
     a.ops[0].norm_out = c->x;
@@ -652,7 +672,6 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
     a.ops[2].kn_w = L0.kn;
     a.ops[2].layer = 0;
     a.n_ops = 3;
-    if (!fits(a)) return fail(c, QASR_ERR_CAPACITY, "chain workspace too small");
     qasr_status s = launch_chain(c, a, sh, n);
     if (s) return s;
   }
@@ -662,23 +681,26 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
     const LayerDev& Ld = c->layers[l];
     ChainArgs a = base;
     a.barrier = c->chain_bar + l + 1;
-    a.gemms[0] = gemm(Ld.o, 1);
-    a.gemms[1] = gemm(Ld.gu, 0);
-    a.gemms[2] = gemm(Ld.down, 2);
+    if (c->chain_trace) a.trace = c->chain_trace + static_cast<size_t>(l + 1) * sms * CHAIN_TRACE_SLOTS;
+    a.gemms[0] = gemm(Ld.o, 1, 1);
+    a.gemms[1] = gemm(Ld.gu, 0, 2);
+    a.gemms[2] = gemm(Ld.down, 2, 3);
     int k = 0;
     a.ops[k++] = op(CH_GEMM, 0);
-    a.ops[k] = op(CH_RESID_NORM, 0);
+    a.ops[k++] = op(CH_RESID, 0);
+    a.ops[k] = op(CH_NORM, 0);
     a.ops[k].norm_w = Ld.pln;
     a.ops[k++].norm_out = c->x;
     a.ops[k++] = op(CH_GEMM, 1);
     a.ops[k++] = op(CH_SILU, 1);
     a.ops[k++] = op(CH_GEMM, 2);
-    a.ops[k] = op(CH_RESID_NORM, 2);
+    a.ops[k++] = op(CH_RESID, 2);
+    a.ops[k] = op(CH_NORM, 2);
     if (l + 1 < L) {
       const LayerDev& Ln = c->layers[l + 1];
       a.ops[k].norm_w = Ln.iln;
       a.ops[k++].norm_out = c->x;
-      a.gemms[3] = gemm(Ln.qkv, 0);
+      a.gemms[3] = gemm(Ln.qkv, 0, 0);
       a.ops[k++] = op(CH_GEMM, 3);
       a.ops[k] = op(CH_QKV, 3);
       a.ops[k].qn_w = Ln.qn;
@@ -689,7 +711,6 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
       a.ops[k++].norm_out = c->xf;
     }
     a.n_ops = k;
-    if (!fits(a)) return fail(c, QASR_ERR_CAPACITY, "chain workspace too small");
     if ((s = launch_chain(c, a, sh, n))) return s;
   }
   (void)qkv_out;
@@ -905,15 +926,22 @@ qasr_status qasr_create(const qasr_text_config* cfg, const qasr_options* opts, i
   c->chain_ok = i8 && hs <= CHAIN_MAX_HS && hs % 256 == 0 && I % 64 == 0 &&
                 !(no_chain && no_chain[0] == '1');
   if (c->chain_ok) {
-    const int n_tile = chain_shape(std::min(opts->max_slots, CHAIN_MAX_ROWS)).n_tile;
-    size_t cw = 0;
-    for (auto& sh : shapes) {
-      const ChainGemm g = chain_gemm_plan(nullptr, nullptr, sh[0], sh[1], 0, c->num_sms);
-      cw = std::max(cw, static_cast<size_t>(sh[0] / 128) * g.max_seg * n_tile * 128);
+    c->chain_ws_rows = chain_shape(std::min(opts->max_slots, CHAIN_MAX_ROWS)).n_tile;
+    for (int i = 0; i < 4; ++i) {  // shapes[] order: QKV, o_proj, gate|up, down
+      const ChainGemm g = chain_gemm_plan(nullptr, nullptr, shapes[i][0], shapes[i][1], 0, c->num_sms,
+                                          chain_seg_cap(i));
+      if ((s = dalloc(c, &c->chain_ws[i],
+                      static_cast<size_t>(shapes[i][0] / 128) * g.max_seg * c->chain_ws_rows * 128, "chain workspace")))
+        return s;
     }
-    c->chain_ws_floats = cw;
-    if ((s = dalloc(c, &c->chain_ws, cw, "chain workspace")) ||
-        (s = dalloc(c, &c->chain_bar, static_cast<size_t>(L + 1), "chain barriers")))
+    if ((s = dalloc(c, &c->chain_bar, static_cast<size_t>(L + 1), "chain barriers")) ||
+        (s = dalloc(c, &c->chain_ss, static_cast<size_t>(CHAIN_MAX_ROWS) * CHAIN_MAX_HS / 128, "chain norms")) ||
+        (s = dalloc(c, &c->chain_row_page, static_cast<size_t>(CHAIN_MAX_ROWS), "chain row pages")) ||
+        (s = dalloc(c, &c->chain_row_rope, static_cast<size_t>(CHAIN_MAX_ROWS) * 256, "chain row rope")))
+      return s;
+    if ((opts->flags & QASR_FLAG_TRACE) &&
+        (s = dalloc(c, &c->chain_trace, static_cast<size_t>(L + 1) * c->num_sms * CHAIN_TRACE_SLOTS,
+                    "chain trace")))
       return s;
   }
   CK(cudaMallocHost(&c->pinned_tok, sizeof(int) * opts->max_slots * 2), "pinned alloc");
@@ -1299,6 +1327,18 @@ qasr_status qasr_read_logits(qasr_ctx* c, float* out, int rows) {
   CK(cudaMemcpyAsync(out, c->logits, static_cast<size_t>(rows) * c->cfg.vocab_size * sizeof(float),
                      cudaMemcpyDeviceToHost, c->stream),
      "logits readback");
+  return check_device_status(c);
+}
+
+qasr_status qasr_read_trace(qasr_ctx* c, uint64_t* out, int cap, int* count) {
+  if (!c || !out || !count || cap < 0) return QASR_ERR_INVALID_ARG;
+  if (!c->chain_trace) return fail(c, QASR_ERR_STATE, "no trace: create the context with QASR_FLAG_TRACE (int8 weights)");
+  const size_t n = static_cast<size_t>(c->cfg.num_hidden_layers + 1) * c->num_sms * CHAIN_TRACE_SLOTS;
+  *count = static_cast<int>(n);
+  CK(cudaSetDevice(c->device), "cudaSetDevice");
+  CK(cudaMemcpyAsync(out, c->chain_trace, std::min(n, static_cast<size_t>(cap)) * sizeof(uint64_t),
+                     cudaMemcpyDeviceToHost, c->stream),
+     "trace readback");
   return check_device_status(c);
 }
 

@@ -4,6 +4,7 @@ the same way: src/bin/batch_gemv_bench.rs, src/bin/gemv_bench.rs, src/bin/attn_b
     python qwen3-asr-wgpu_b200/kernel_bench.py gemm --fmt int8 --n-out 12288 --k 2048 --rows 32
     python qwen3-asr-wgpu_b200/kernel_bench.py attention --slots 512 --lo 256 --hi 4096
     python qwen3-asr-wgpu_b200/kernel_bench.py append --slots 512 --chunk 13
+    python qwen3-asr-wgpu_b200/kernel_bench.py step --slots 32 --lo 100 --hi 1500
 
 Each prints one JSON line: median CUDA-event time per launch (operands evicted from L2
 by a 256 MB write between launches), algorithmic bytes and GB/s.  `attention` is
@@ -172,6 +173,70 @@ def bench_append(args, pkg, torch):
             "gbs": nbytes / med / 1e9}
 
 
+def bench_step(args, pkg, torch):
+    """Timeline of one int8 decode step (cfg4 shape) from the decode-chain trace: per
+    chain launch its duration, per operation the time (after the launch's first CTA
+    entry) at which the last CTA finished it and at which the barrier after it opened,
+    and the gap between launches (attention + merge + launch overhead)."""
+    cfg = pkg.text_config(args.model, num_hidden_layers=args.layers)
+    model = pkg.SyntheticModel(cfg, seed=args.seed)
+    dec = pkg.TextDecoder(cfg, weight_format=pkg.WEIGHTS_INT8, max_slots=args.slots, max_seq=args.hi + 64,
+                          trace=True)
+    dec.load_model(model)
+    cos, sin = pkg.build_rope_tables(args.hi + 64)
+    dec.set_rope_tables(cos, sin)
+    rng = np.random.default_rng(args.seed)
+    lens = rng.integers(args.lo, args.hi + 1, size=args.slots)
+    slots = [dec.fork_capped(args.hi + 32) for _ in range(args.slots)]
+    dec.prefill_batch(slots, [model.prefix(s, int(n) - 24)[0] for s, n in enumerate(lens)])
+    stream = torch.cuda.Stream()
+    dec.set_stream(stream.cuda_stream)
+    st = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    times = []
+    for _ in range(args.iters):
+        st[0].record(stream)
+        dec.step_batch(slots, read_tokens=False)
+        st[1].record(stream)
+        st[1].synchronize()
+        times.append(st[0].elapsed_time(st[1]) * 1e3)
+    tr = dec.read_trace().astype(np.float64)  # [launch, cta, slot]
+    dec.close()
+    t0 = tr[0, :, 0].min()
+    launches = []
+    for k in range(tr.shape[0]):
+        ent = tr[k, :, 0].min()
+        ext = tr[k, :, -1].max()
+        ops = []
+        for i in range(12):
+            done, passed = tr[k, :, 1 + 2 * i], tr[k, :, 2 + 2 * i]
+            if not done.any():
+                break
+            ops.append([round((np.median(done) - ent) / 1e3, 2), round((done.max() - ent) / 1e3, 2),
+                        round((passed.max() - ent) / 1e3, 2) if passed.any() else None])
+        gemms = []
+        for g in range(4):
+            xr, m0, m1 = tr[k, :, 25 + g], tr[k, :, 29 + g], tr[k, :, 33 + g]
+            if not xr.any():
+                break
+            rel = lambda col: [round((np.median(col[col > 0]) - ent) / 1e3, 2), round((col[col > 0].max() - ent) / 1e3, 2)] \
+                if (col > 0).any() else None
+            gemms.append({"x_ready": rel(xr), "first_mma": rel(m0), "last_mma": rel(m1)})
+        units = {}
+        for cta in (0, 100):
+            row = tr[k, cta]
+            units[cta] = [[round((row[b + j] - ent) / 1e3, 2) if row[b + j] > 0 else None for j in range(24)]
+                          for b in (40, 72, 104)]
+        launches.append({"start_us": round((ent - t0) / 1e3, 2), "dur_us": round((ext - ent) / 1e3, 2),
+                         "ops_done_passed_us": ops, "gemms_median_max_us": gemms,
+                         "units_w_a_mma_cta0_cta100": units})
+    gaps = [round((launches[k + 1]["start_us"] - launches[k]["start_us"] - launches[k]["dur_us"]), 2)
+            for k in range(len(launches) - 1)]
+    return {"kernel": "decode_step", "slots": args.slots, "layers": args.layers, "median_step_us": statistics.median(times),
+            "chain_dur_us_median": statistics.median(l["dur_us"] for l in launches[1:]),
+            "gap_us_median": statistics.median(gaps), "launches": launches[:3], "last": launches[-1],
+            "gaps_us": gaps[:6]}
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="what", required=True)
@@ -190,16 +255,23 @@ def main(argv=None):
         a.add_argument("--chunk", type=int, default=1 if name == "attention" else 13)
         a.add_argument("--seed", type=int, default=5)
         a.add_argument("--trace", action="store_true")
+    sp = sub.add_parser("step")
+    sp.add_argument("--model", default="1.7b")
+    sp.add_argument("--layers", type=int, default=28)
+    sp.add_argument("--slots", type=int, default=32)
+    sp.add_argument("--lo", type=int, default=100)
+    sp.add_argument("--hi", type=int, default=1500)
+    sp.add_argument("--seed", type=int, default=5)
     for p in sub.choices.values():
         p.add_argument("--iters", type=int, default=20)
     args = ap.parse_args(argv)
     import torch
     pkg = _pkg()
-    fn = {"gemm": bench_gemm, "attention": bench_attention, "append": bench_append}[args.what]
+    fn = {"gemm": bench_gemm, "attention": bench_attention, "append": bench_append, "step": bench_step}[args.what]
     res = fn(args, pkg, torch)
     hbm = None
     peaks = ROOT / "MEASURED_PEAKS.json"
-    if peaks.exists():
+    if peaks.exists() and "gbs" in res:
         hbm = json.loads(peaks.read_text())["hbm_gbs"]
         res["hbm_frac_of_measured"] = res["gbs"] / hbm
     print(json.dumps(res), flush=True)
