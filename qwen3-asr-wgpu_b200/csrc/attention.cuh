@@ -19,7 +19,7 @@
 // Persistent CTA per SM: warp 8 streams the pages of the CTA's units (and each unit's q
 // rows, with its first stage), stage after stage, into a 3-deep shared-memory ring with
 // cp.async.bulk (completion counted on mbarriers, no multicast); warps 0-7 each take 16
-// positions of a stage and compute S = Q K^T and O += P V on the tensor cores
+// positions of a stage and compute S^T = K Q^T and O^T += V^T P^T on the tensor cores
 // (mma.sync: with two real query rows per kv head the work is too thin for tcgen05) with
 // an online softmax per head and warp.  At a unit's end the consumer warps drop their
 // state into a double-buffered shared slot and move on; warp 9 merges the 8 warps and
@@ -331,12 +331,14 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
     if (lane == 0) attn_stamp(a, 5);
   } else {
     // ------------------------------------------------------------ consumers (tensor cores)
-    // Per stage a warp owns 16 positions.  S = Q K^T with mma.sync m16n8k16: A = the two q
-    // heads as rows 0 and 1 of a 16-row tile (the rest zero), B = K rows fetched with
-    // ldmatrix; O += P V with P (f32) split into two f16 terms p_hi + p_lo so the weights
-    // keep ~22 bits.  Lane (g4 = lane / 4, tig = lane % 4) holds for g4 < 2 the scores of
-    // head g4 at positions {2 tig, 2 tig + 1, 8 + 2 tig, 9 + 2 tig} and O[head g4][8 nt +
-    // 2 tig, +1] for the 16 n-tiles nt.
+    // Per stage a warp owns 16 positions and computes, transposed so that positions and
+    // dims take the 16-wide M side of mma.sync m16n8k16 and the two GQA heads the N side:
+    //   S^T [16 pos x 8] = K [16 pos x 128] . Q^T [128 x 8]      (8 MMAs, K via ldmatrix)
+    //   O^T [128 x 8]   += V^T [128 x 16 pos] . P^T [16 pos x 8] (8 m-tiles x hi/lo = 16 MMAs)
+    // Q columns 2..7 are zero.  Lane (g4 = lane / 4, tig = lane % 4) holds S^T / O^T
+    // columns 2 tig, 2 tig + 1, so the real heads 0 and 1 live in the tig == 0 lanes: scores
+    // of positions g4 and g4 + 8, and O^T rows 16 mt + g4 and 16 mt + g4 + 8.  P (f32) is
+    // split into f16 hi + lo terms so the softmax weights keep ~22 bits.
     const int g4 = lane >> 2, tig = lane & 3;
     const int lrow = lane & 7, lmat = lane >> 3;
     int sl = 0, k = 0;
@@ -344,22 +346,22 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
     bool ok = true;
     for (int u = blockIdx.x; u < U && ok; u += gridDim.x, ++k) {
       const AttnUnit t = attn_unit(a, prefix, u);
-      uint32_t qf[8][2];
-      float o[16][4];
+      uint32_t qb[8][2];
+      float o[8][4];
 #pragma unroll
-      for (int nt = 0; nt < 16; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
-      float m = -INFINITY, l = 0.f;
+      for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+      float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
       for (int st = t.s0; st < t.s1; ++st) {
         if (!mbar_wait_warp(&full_bar[sl], ph, &abort_flag, a.status, 0x603)) {
           ok = false;
           break;
         }
         if (k == 0 && st == t.s0 && tid == 0) attn_stamp(a, 2);
-        if (st == t.s0) {
+        if (st == t.s0) {  // Q^T B fragments: head g4 (g4 < 2), dims 16 ks + 2 tig (+8)
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks) {
-            qf[ks][0] = g4 < 2 ? *reinterpret_cast<const uint32_t*>(&sm_q[sl][g4 * 128 + 16 * ks + 2 * tig]) : 0u;
-            qf[ks][1] = g4 < 2 ? *reinterpret_cast<const uint32_t*>(&sm_q[sl][g4 * 128 + 16 * ks + 8 + 2 * tig]) : 0u;
+            qb[ks][0] = g4 < 2 ? *reinterpret_cast<const uint32_t*>(&sm_q[sl][g4 * 128 + 16 * ks + 2 * tig]) : 0u;
+            qb[ks][1] = g4 < 2 ? *reinterpret_cast<const uint32_t*>(&sm_q[sl][g4 * 128 + 16 * ks + 8 + 2 * tig]) : 0u;
           }
         }
         const int tw = st * 128 + warp * 16;  // first position of this warp's 16
@@ -367,56 +369,66 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
           const uint8_t* buf = smem + static_cast<size_t>(sl) * ATTN_STAGE_BYTES;
           const uint32_t kb = smem_u32(buf) + warp * 16 * 256;
           const uint32_t vb = smem_u32(buf + 2 * ATTN_PAGE_BYTES) + warp * 16 * 256;
-          float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+          float sacc[4] = {0.f, 0.f, 0.f, 0.f};
           {
-            const int pl = (lmat >> 1) * 8 + lrow;  // position this lane addresses
+            const int pl = (lmat & 1) * 8 + lrow;  // position this lane addresses
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
-              const int chunk = 2 * ks + (lmat & 1);
-              uint32_t b0, b1, b2, b3;
-              ldmatrix_x4(kb + pl * 256 + ((chunk ^ lrow) << 4), b0, b1, b2, b3);
-              mma_16816(s0, qf[ks][0], 0u, qf[ks][1], 0u, b0, b1);
-              mma_16816(s1, qf[ks][0], 0u, qf[ks][1], 0u, b2, b3);
+              const int chunk = 2 * ks + (lmat >> 1);
+              uint32_t a0, a1, a2, a3;
+              ldmatrix_x4(kb + pl * 256 + ((chunk ^ lrow) << 4), a0, a1, a2, a3);
+              mma_16816(sacc, a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
             }
           }
-          float sc[4] = {s0[0] * a.scale, s0[1] * a.scale, s1[0] * a.scale, s1[1] * a.scale};
-          const int pos0 = tw + 2 * tig;
-          const bool v0 = pos0 < t.len, v1 = pos0 + 1 < t.len, v2 = pos0 + 8 < t.len, v3 = pos0 + 9 < t.len;
-          if (!v0) sc[0] = -INFINITY;
-          if (!v1) sc[1] = -INFINITY;
-          if (!v2) sc[2] = -INFINITY;
-          if (!v3) sc[3] = -INFINITY;
-          float mx = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-          const float mn = fmaxf(m, mx);
-          const float corr = (m == mn) ? 1.0f : expf(m - mn);
-          const float p0 = v0 ? expf(sc[0] - mn) : 0.f, p1 = v1 ? expf(sc[1] - mn) : 0.f;
-          const float p2 = v2 ? expf(sc[2] - mn) : 0.f, p3 = v3 ? expf(sc[3] - mn) : 0.f;
-          l = l * corr + ((p0 + p1) + (p2 + p3));
-          m = mn;
+          // sacc: [pos g4][head 2tig], [pos g4][2tig+1], [pos g4+8][2tig], [pos g4+8][2tig+1]
+          const bool v0 = tw + g4 < t.len, v1 = tw + g4 + 8 < t.len;
+          float sc[4] = {v0 ? sacc[0] * a.scale : -INFINITY, v0 ? sacc[1] * a.scale : -INFINITY,
+                         v1 ? sacc[2] * a.scale : -INFINITY, v1 ? sacc[3] * a.scale : -INFINITY};
+          float p[4], corr[2];
 #pragma unroll
-          for (int nt = 0; nt < 16; ++nt) {
-            o[nt][0] *= corr;
-            o[nt][1] *= corr;
+          for (int h = 0; h < 2; ++h) {
+            float mx = fmaxf(sc[h], sc[2 + h]);
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+            const float mn = fmaxf(m[h], mx);  // finite: position tw is always valid
+            corr[h] = (m[h] == mn) ? 1.0f : expf(m[h] - mn);
+            p[h] = v0 ? expf(sc[h] - mn) : 0.f;
+            p[2 + h] = v1 ? expf(sc[2 + h] - mn) : 0.f;
+            l[h] = l[h] * corr[h] + (p[h] + p[2 + h]);
+            m[h] = mn;
           }
-          const __half2 h01 = __floats2half2_rn(p0, p1), h23 = __floats2half2_rn(p2, p3);
-          const float2 r01 = __half22float2(h01), r23 = __half22float2(h23);
-          const __half2 l01 = __floats2half2_rn(p0 - r01.x, p1 - r01.y);
-          const __half2 l23 = __floats2half2_rn(p2 - r23.x, p3 - r23.y);
-          const uint32_t ah0 = *reinterpret_cast<const uint32_t*>(&h01), ah2 = *reinterpret_cast<const uint32_t*>(&h23);
-          const uint32_t al0 = *reinterpret_cast<const uint32_t*>(&l01), al2 = *reinterpret_cast<const uint32_t*>(&l23);
-          {
-            const int pl = (lmat & 1) * 8 + lrow;
 #pragma unroll
-            for (int n2 = 0; n2 < 8; ++n2) {
-              const int chunk = 2 * n2 + (lmat >> 1);
-              uint32_t b0, b1, b2, b3;
-              ldmatrix_x4_trans(vb + pl * 256 + ((chunk ^ lrow) << 4), b0, b1, b2, b3);
-              mma_16816(o[2 * n2], ah0, 0u, ah2, 0u, b0, b1);
-              mma_16816(o[2 * n2], al0, 0u, al2, 0u, b0, b1);
-              mma_16816(o[2 * n2 + 1], ah0, 0u, ah2, 0u, b2, b3);
-              mma_16816(o[2 * n2 + 1], al0, 0u, al2, 0u, b2, b3);
+          for (int mt = 0; mt < 8; ++mt) {
+            o[mt][0] *= corr[0];
+            o[mt][1] *= corr[1];
+            o[mt][2] *= corr[0];
+            o[mt][3] *= corr[1];
+          }
+          // P^T B fragments for column (head) g4: positions 2 tig, 2 tig + 1 (b0) and
+          // 8 + 2 tig, 9 + 2 tig (b1), held by lanes 8 tig and 8 tig + 4 (tig == 0 there)
+          const int s0l = 8 * tig, s1l = 8 * tig + 4;
+          const float x00 = __shfl_sync(0xffffffffu, p[0], s0l), x01 = __shfl_sync(0xffffffffu, p[1], s0l);
+          const float y00 = __shfl_sync(0xffffffffu, p[0], s1l), y01 = __shfl_sync(0xffffffffu, p[1], s1l);
+          const float x20 = __shfl_sync(0xffffffffu, p[2], s0l), x21 = __shfl_sync(0xffffffffu, p[3], s0l);
+          const float y20 = __shfl_sync(0xffffffffu, p[2], s1l), y21 = __shfl_sync(0xffffffffu, p[3], s1l);
+          const bool real = g4 < 2;
+          const float pa = real ? (g4 == 0 ? x00 : x01) : 0.f, pb = real ? (g4 == 0 ? y00 : y01) : 0.f;
+          const float pc = real ? (g4 == 0 ? x20 : x21) : 0.f, pd = real ? (g4 == 0 ? y20 : y21) : 0.f;
+          const __half2 h0 = __floats2half2_rn(pa, pb), h1 = __floats2half2_rn(pc, pd);
+          const float2 r0 = __half22float2(h0), r1 = __half22float2(h1);
+          const __half2 l0 = __floats2half2_rn(pa - r0.x, pb - r0.y), l1 = __floats2half2_rn(pc - r1.x, pd - r1.y);
+          const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(&h0), bh1 = *reinterpret_cast<const uint32_t*>(&h1);
+          const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(&l0), bl1 = *reinterpret_cast<const uint32_t*>(&l1);
+          {
+            const int pl = (lmat >> 1) * 8 + lrow;
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt) {
+              const int chunk = 2 * mt + (lmat & 1);
+              uint32_t a0, a1, a2, a3;
+              ldmatrix_x4_trans(vb + pl * 256 + ((chunk ^ lrow) << 4), a0, a1, a2, a3);
+              mma_16816(o[mt], a0, a1, a2, a3, bh0, bh1);
+              mma_16816(o[mt], a0, a1, a2, a3, bl0, bl1);
             }
           }
         }
@@ -429,20 +441,30 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
       }
       if (!ok) break;
       // ---- hand this warp's state to the merger (double-buffered by unit parity)
-      l += __shfl_xor_sync(0xffffffffu, l, 1);
-      l += __shfl_xor_sync(0xffffffffu, l, 2);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        l[h] += __shfl_xor_sync(0xffffffffu, l[h], 4);
+        l[h] += __shfl_xor_sync(0xffffffffu, l[h], 8);
+        l[h] += __shfl_xor_sync(0xffffffffu, l[h], 16);
+      }
       const int b = k & 1;
       if (!mbar_wait_warp(&mfree_bar[b], static_cast<uint32_t>(((k >> 1) & 1) ^ 1), &abort_flag, a.status,
                           0x605))
         break;
-      if (g4 < 2) {
-        if (tig == 0) {
-          sm_m[b][warp][g4] = m;
-          sm_l[b][warp][g4] = l;
+      if (tig == 0) {
+        if (g4 == 0) {
+          sm_m[b][warp][0] = m[0];
+          sm_m[b][warp][1] = m[1];
+          sm_l[b][warp][0] = l[0];
+          sm_l[b][warp][1] = l[1];
         }
 #pragma unroll
-        for (int nt = 0; nt < 16; ++nt)
-          *reinterpret_cast<float2*>(&sm_acc[b][warp][g4][8 * nt + 2 * tig]) = make_float2(o[nt][0], o[nt][1]);
+        for (int mt = 0; mt < 8; ++mt) {
+          sm_acc[b][warp][0][16 * mt + g4] = o[mt][0];
+          sm_acc[b][warp][1][16 * mt + g4] = o[mt][1];
+          sm_acc[b][warp][0][16 * mt + g4 + 8] = o[mt][2];
+          sm_acc[b][warp][1][16 * mt + g4 + 8] = o[mt][3];
+        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&mfull_bar[b]);
