@@ -23,8 +23,9 @@
 //               each unit's X tile once its GEMM's input is ready
 //   warps 1-3   UMMA issuers (A from TMEM, B = X from shared memory), k-steps split
 //               round-robin over them; warp 2 also allocates the TMEM
-//   warps 4-11  int8 A builders (two warpgroups, alternate units): f16(q * s) into TMEM
-//   warps 12-15 epilogue and row operations; they also run the grid barriers
+//   warps 4-7   int8 A builders: f16(q * s) into TMEM
+//   warps 8-15  epilogue (two warps per TMEM lane quadrant, splitting the accumulator
+//               columns) and row operations; they also run the grid barriers
 #pragma once
 #include "device_common.cuh"
 #include "gemm_tc.cuh"
@@ -39,6 +40,10 @@ constexpr int CHAIN_MAX_A_STAGES = 8;
 constexpr int CHAIN_MAX_ROWS = 128;  // one N tile
 constexpr int CHAIN_TRACE_SLOTS = 128;  // == QASR_TRACE_SLOTS
 constexpr int CHAIN_MAX_HS = 2048;   // hidden size the row operations hold in registers
+// warps 8-15 run the epilogue and the row operations (two per TMEM lane quadrant), warps
+// 4-7 dequantise: one builder warpgroup keeps pace with the MMA issuers
+constexpr int CHAIN_EPI_WARPS = 8;
+constexpr int CHAIN_EPI_THREADS = CHAIN_EPI_WARPS * 32;
 // most segments a tile of a chain GEMM may be cut into, per reader (all loads of a read are
 // issued at once): residual adds (o_proj, down), SiLU (gate|up), q/k/v (QKV)
 constexpr int CHAIN_MAX_SEG = 12;
@@ -177,21 +182,24 @@ __device__ __forceinline__ float4 chain_sum_slots4(const float* p, size_t stride
   return acc;
 }
 
-// Block-of-128 sum (the four epilogue warps), the same value in every thread.
-__device__ __forceinline__ float chain_sum128(float v, float* red, int e) {
+// Sum over the epilogue group (CHAIN_EPI_WARPS warps), the same value in every thread.
+__device__ __forceinline__ float chain_group_sum(float v, float* red, int e) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  named_bar_sync(1, 128);
+  named_bar_sync(1, CHAIN_EPI_THREADS);
   if ((e & 31) == 0) red[e >> 5] = v;
-  named_bar_sync(1, 128);
-  return (red[0] + red[1]) + (red[2] + red[3]);
+  named_bar_sync(1, CHAIN_EPI_THREADS);
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < CHAIN_EPI_WARPS; ++w) t += red[w];
+  return t;
 }
 
 __global__ void __launch_bounds__(CHAIN_THREADS, 1)
     decode_chain_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_attn,
                         const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ ChainArgs a) {
   constexpr int KSTEPS = 8;  // 128 k elements per unit, UMMA K = 16
-  constexpr int EPI_WARP0 = 12;
+  constexpr int EPI_WARP0 = 16 - CHAIN_EPI_WARPS;
   extern __shared__ __align__(1024) uint8_t chain_dsmem[];
   __shared__ __align__(8) uint64_t wfull_bar[CHAIN_MAX_W_STAGES], wfree_bar[CHAIN_MAX_W_STAGES];
   // unit slots: A stage (TMEM) + X tile (shared memory) of one unit.  ufull completes when
@@ -202,7 +210,7 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
   __shared__ volatile int abort_flag;
   __shared__ int xready;  // GEMMs whose X input is complete (written by the epilogue leader)
   __shared__ int seg_ok, bar_ok;
-  __shared__ float red[4];
+  __shared__ float red[CHAIN_EPI_WARPS];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(chain_dsmem) + 1023) & ~uintptr_t(1023));
@@ -232,7 +240,7 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&dfull_bar[i], NACC);
-      mbar_init(&dfree_bar[i], 4);
+      mbar_init(&dfree_bar[i], CHAIN_EPI_WARPS);
     }
     mbar_init(&done_bar, NACC);
     abort_flag = 0;
@@ -419,12 +427,11 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
       umma_commit(&done_bar);
       mbar_wait(&done_bar, 0, nullptr, a.status, 0x724);
     }
-  } else if (warp >= 4 && warp < EPI_WARP0) {
+  } else if (warp >= 4 && warp < 8) {
     // ------------------------------------------------------------ int8 A builders
     // Each unit is published as soon as its TMEM stores land (tcgen05.wait::st is cheap);
     // the row scale of the unit's tile is loaded before the unit's barrier waits so its
     // latency overlaps them.
-    const int grp = (warp - 4) >> 2;
     const int t = (threadIdx.x - 128) & 127;  // row of the tile == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     int st = 0, ast = 0, i = 0;  // W stage, unit slot
@@ -446,7 +453,6 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
           ast = 0;
           aph ^= 1u;
         }
-        if ((i & 1) != grp) continue;
         const __half sc = g.scale[(u / g.kblocks) * 128 + t];
         if (!mbar_wait_warp(&wfull_bar[my_st], my_ph, &abort_flag, a.status, 0x731) ||
             !mbar_wait_warp(&ufree_bar[my_ast], my_aph ^ 1u, &abort_flag, a.status, 0x732)) {
@@ -488,9 +494,11 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
     }
   } else if (warp >= EPI_WARP0) {
     // ------------------------------------------------------------ epilogue + row operations
-    const int e = threadIdx.x - EPI_WARP0 * 32;
+    const int e = threadIdx.x - EPI_WARP0 * 32;  // 0 .. CHAIN_EPI_THREADS - 1
     const int we = warp - EPI_WARP0;
-    const uint32_t lane_base = static_cast<uint32_t>(we * 32) << 16;
+    const int row = (warp & 3) * 32 + lane;       // TMEM lane quadrant of this warp = tile row
+    const int half = we >> 2;                     // two warps per quadrant split the columns
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const size_t slot_floats = static_cast<size_t>(a.ws_rows) * 128;
     int seg = -1, nbar = 0, gi = 0;
     bool ok = true;
@@ -510,9 +518,9 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
             seg_ok = mbar_wait(&dfull_bar[d], static_cast<uint32_t>((seg >> 1) & 1), &abort_flag, a.status, 0x741)
                          ? 1
                          : 0;
-          named_bar_sync(1, 128);
+          named_bar_sync(1, CHAIN_EPI_THREADS);
           const int got = seg_ok;
-          named_bar_sync(1, 128);
+          named_bar_sync(1, CHAIN_EPI_THREADS);
           if (!got) {
             ok = false;
             break;
@@ -521,10 +529,10 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
           tc_fence_after();
           const int segidx = static_cast<int>(blockIdx.x) - cta_of_unit(static_cast<long long>(T) * g.kblocks,
                                                                          g.units, g.grid);
-          float* dst = g.ws + (static_cast<size_t>(T) * g.max_seg + segidx) * slot_floats + e;
+          float* dst = g.ws + (static_cast<size_t>(T) * g.max_seg + segidx) * slot_floats + row;
           const uint32_t dt = tmem_base + lane_base + static_cast<uint32_t>(d) * DCOLS;
           const int n_used = min(NACC, seg_end - u);  // issuers that had units in the segment
-          for (int c0 = 0; c0 < a.n_tile; c0 += 16) {
+          for (int c0 = 16 * half; c0 < a.n_tile; c0 += 32) {
             float v[16];
             for (int q = 0; q < n_used; ++q) {
               uint32_t r[16];
@@ -545,7 +553,7 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
       } else if (op.kind == CH_EMBED_NORM) {
         // h[r] = embed row of the slot's input token, x[r] = rmsnorm(h[r]); one row per CTA,
         // thread e holds the column pairs 2e + 256 j
-        const int np = a.hs / 256;
+        const int np = a.hs / (2 * CHAIN_EPI_THREADS);
         for (int r = blockIdx.x; r < a.rows; r += gridDim.x) {
           __half* hr = a.h + static_cast<size_t>(r) * a.hs;
           const int slot = a.row_slot[r];
@@ -565,37 +573,38 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
             __stcg(reinterpret_cast<uint4*>(a.row_rope + static_cast<size_t>(r) * 256 + e * 8),
                    *reinterpret_cast<const uint4*>(rs));
           }
-          float2 v[CHAIN_MAX_HS / 256];
+          float2 v[CHAIN_MAX_HS / (2 * CHAIN_EPI_THREADS)];
           float sq = 0.f;
 #pragma unroll
-          for (int j = 0; j < CHAIN_MAX_HS / 256; ++j) {
+          for (int j = 0; j < CHAIN_MAX_HS / (2 * CHAIN_EPI_THREADS); ++j) {
             if (j < np) {
-              v[j] = __half22float2(*reinterpret_cast<const __half2*>(src + 2 * e + 256 * j));
-              __stcg(reinterpret_cast<__half2*>(hr + 2 * e + 256 * j), __floats2half2_rn(v[j].x, v[j].y));
+              const int i = 2 * e + 2 * CHAIN_EPI_THREADS * j;
+              v[j] = __half22float2(*reinterpret_cast<const __half2*>(src + i));
+              __stcg(reinterpret_cast<__half2*>(hr + i), __floats2half2_rn(v[j].x, v[j].y));
               sq = __fadd_rn(sq, __fmul_rn(v[j].x, v[j].x));
               sq = __fadd_rn(sq, __fmul_rn(v[j].y, v[j].y));
             }
           }
-          const float tot = chain_sum128(sq, red, e);
+          const float tot = chain_group_sum(sq, red, e);
           const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(a.hs)), a.eps)));
           __half* y = op.norm_out + static_cast<size_t>(r) * a.hs;
 #pragma unroll
-          for (int j = 0; j < CHAIN_MAX_HS / 256; ++j) {
+          for (int j = 0; j < CHAIN_MAX_HS / (2 * CHAIN_EPI_THREADS); ++j) {
             if (j < np) {
-              const int i = 2 * e + 256 * j;
+              const int i = 2 * e + 2 * CHAIN_EPI_THREADS * j;
               const float x0 = __fmul_rn(__fmul_rn(v[j].x, inv), op.norm_w[i]);
               const float x1 = __fmul_rn(__fmul_rn(v[j].y, inv), op.norm_w[i + 1]);
               __stcg(reinterpret_cast<__half2*>(y + i), __floats2half2_rn(x0, x1));
             }
           }
-          named_bar_sync(1, 128);  // `red` is reused by the next row
+          named_bar_sync(1, CHAIN_EPI_THREADS);  // `red` is reused by the next row
         }
       } else if (op.kind == CH_RESID) {
         // h[r, 128 T + c] = f16(h + sum of partials), and the tile's sum of squares of the
         // new f16 values into ss[r][T]; one warp per (row, tile), lane = 4 columns
         const ChainGemm& g = a.gemms[op.gemm];
         const int tiles = a.hs / 128;
-        for (int it = blockIdx.x * 4 + we; it < a.rows * tiles; it += gridDim.x * 4) {
+        for (int it = blockIdx.x * CHAIN_EPI_WARPS + we; it < a.rows * tiles; it += gridDim.x * CHAIN_EPI_WARPS) {
           const int r = it / tiles, T = it - r * tiles;
           const float4 acc = chain_sum_slots4<CHAIN_MAX_SEG>(chain_partial(a, g, T, r, 4 * lane), slot_floats,
                                                              g.max_seg);
@@ -622,7 +631,7 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
         // x[r] = f16(h * inv * w), inv = 1 / sqrt(sum_T ss[r][T] / hs + eps) (rms_norm_row,
         // src/cpu_decoder.rs:261-272); one warp per (row, tile)
         const int tiles = a.hs / 128;
-        for (int it = blockIdx.x * 4 + we; it < a.rows * tiles; it += gridDim.x * 4) {
+        for (int it = blockIdx.x * CHAIN_EPI_WARPS + we; it < a.rows * tiles; it += gridDim.x * CHAIN_EPI_WARPS) {
           const int r = it / tiles, T = it - r * tiles;
           float t = lane < tiles ? __ldcg(a.ss + r * CHAIN_MAX_HS / 128 + lane) : 0.f;
 #pragma unroll
@@ -648,8 +657,8 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
         const ChainGemm& g = a.gemms[op.gemm];
         const int tiles = g.units / g.kblocks;
         const int total = a.rows * tiles * 16;
-        const int stride = gridDim.x * 128;
-        for (int q0 = blockIdx.x * 128 + e; q0 < total; q0 += 2 * stride) {
+        const int stride = gridDim.x * CHAIN_EPI_THREADS;
+        for (int q0 = blockIdx.x * CHAIN_EPI_THREADS + e; q0 < total; q0 += 2 * stride) {
           float4 gs[2], us[2];
 #pragma unroll
           for (int k = 0; k < 2; ++k) {
@@ -688,7 +697,7 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
         // dim d (d ^ 64) sits in lane ^ 16
         const ChainGemm& g = a.gemms[op.gemm];
         const int heads = a.nq + 2 * a.nkv;
-        for (int it = blockIdx.x * 4 + we; it < a.rows * heads; it += gridDim.x * 4) {
+        for (int it = blockIdx.x * CHAIN_EPI_WARPS + we; it < a.rows * heads; it += gridDim.x * CHAIN_EPI_WARPS) {
           const int r = it / heads, t = it - r * heads;
           const int d0 = 4 * lane;
           const int pos = __ldcg(a.row_pos + r);
@@ -751,7 +760,7 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
       }
       // ---- grid barrier between dependent operations
       if (oi + 1 < a.n_ops) {
-        named_bar_sync(1, 128);
+        named_bar_sync(1, CHAIN_EPI_THREADS);
         if (e == 0) {
           if (a.trace != nullptr && oi < 12) a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 1 + 2 * oi] = globaltimer();
           ++nbar;
@@ -774,7 +783,7 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
           if (a.trace != nullptr && oi < 12) a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 2 + 2 * oi] = globaltimer();
           if (a.ops[oi + 1].kind == CH_GEMM) st_release_cta_shared(&xready, gi + 1);
         }
-        named_bar_sync(1, 128);
+        named_bar_sync(1, CHAIN_EPI_THREADS);
         if (!bar_ok) ok = false;
       } else if (e == 0 && a.trace != nullptr && oi < 12) {
         a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 1 + 2 * oi] = globaltimer();

@@ -923,7 +923,7 @@ qasr_status qasr_create(const qasr_text_config* cfg, const qasr_options* opts, i
     return s;
   // The int8 decode step runs as persistent chain launches when its shapes fit them.
   const char* no_chain = std::getenv("QASR_B200_NO_CHAIN");
-  c->chain_ok = i8 && hs <= CHAIN_MAX_HS && hs % 256 == 0 && I % 64 == 0 &&
+  c->chain_ok = i8 && hs <= CHAIN_MAX_HS && hs % (2 * CHAIN_EPI_THREADS) == 0 && I % 64 == 0 &&
                 !(no_chain && no_chain[0] == '1');
   if (c->chain_ok) {
     c->chain_ws_rows = chain_shape(std::min(opts->max_slots, CHAIN_MAX_ROWS)).n_tile;

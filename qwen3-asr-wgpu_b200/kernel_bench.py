@@ -212,6 +212,7 @@ def bench_step(args, pkg, torch):
             if not done.any():
                 break
             ops.append([round((np.median(done) - ent) / 1e3, 2), round((done.max() - ent) / 1e3, 2),
+                        round((passed[passed > 0].min() - ent) / 1e3, 2) if passed.any() else None,
                         round((passed.max() - ent) / 1e3, 2) if passed.any() else None])
         gemms = []
         for g in range(4):
@@ -227,6 +228,7 @@ def bench_step(args, pkg, torch):
             units[cta] = [[round((row[b + j] - ent) / 1e3, 2) if row[b + j] > 0 else None for j in range(24)]
                           for b in (40, 72, 104)]
         launches.append({"start_us": round((ent - t0) / 1e3, 2), "dur_us": round((ext - ent) / 1e3, 2),
+                         "entry_skew_us": round((tr[k, :, 0].max() - ent) / 1e3, 2),
                          "ops_done_passed_us": ops, "gemms_median_max_us": gemms,
                          "units_w_a_mma_cta0_cta100": units})
     gaps = [round((launches[k + 1]["start_us"] - launches[k]["start_us"] - launches[k]["dur_us"]), 2)
