@@ -179,6 +179,13 @@ qasr_status qasr_read_logits(qasr_ctx* ctx, float* out, int rows);
  * QASR_TRACE_SLOTS - 1 = exit; 0 where nothing happened.
  * *count receives launches * ctas * slots; at most `cap` values are written. */
 qasr_status qasr_read_trace(qasr_ctx* ctx, uint64_t* out, int cap, int* count);
+/* Copy the attention launches' stamps of the last decode step (QASR_FLAG_TRACE):
+ * [layer][cta][QASR_ATTN_TRACE_SLOTS] uint64 nanoseconds, slot 0 = CTA entry, 1 = unit
+ * table ready, 2 = first stage landed, 3 = first unit merged, 4 = last stage consumed,
+ * 5 = last unit merged, 6 = last page copy issued, 7 = units processed (a count).
+ * *count receives layers * ctas * slots; at most `cap` values are written. */
+#define QASR_ATTN_TRACE_SLOTS 8
+qasr_status qasr_read_attn_trace(qasr_ctx* ctx, uint64_t* out, int cap, int* count);
 
 /* --- host helpers of the reference's loader ------------------------------------ */
 /* compute_mrope_cos_sin + text_positions (src/mrope.rs:46-80) rounded to f16 the

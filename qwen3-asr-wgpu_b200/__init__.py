@@ -36,6 +36,7 @@ FLAG_KEEP_LOGITS = 1
 FLAG_NO_GRAPH = 2
 FLAG_TRACE = 4
 TRACE_SLOTS = 128
+ATTN_TRACE_SLOTS = 8
 PAGE_POSITIONS = 64
 
 # Every symbol include/*.h declares (checked by the CPU test suite).
@@ -46,6 +47,7 @@ EXPORTED_SYMBOLS = (
     "qasr_slot_pos", "qasr_set_slot_pos", "qasr_set_input_token", "qasr_set_input_tokens",
     "qasr_prefill", "qasr_step", "qasr_prefill_batch", "qasr_step_batch", "qasr_read_logits",
     "qasr_read_trace",
+    "qasr_read_attn_trace",
     "qasr_build_rope_tables", "qasr_build_dim_map", "qasr_dequant_i8",
     "qasr_kernel_pack_weights", "qasr_kernel_gemm", "qasr_kernel_gemm_traced", "qasr_kernel_attention",
     "qasr_kernel_attention_noalloc", "qasr_kernel_attention_traced", "qasr_kernel_kv_append",
@@ -114,6 +116,7 @@ def _load() -> ctypes.CDLL:
     lib.qasr_step_batch.argtypes = [P, P, I, P]
     lib.qasr_read_logits.argtypes = [P, P, I]
     lib.qasr_read_trace.argtypes = [P, P, I, ctypes.POINTER(I)]
+    lib.qasr_read_attn_trace.argtypes = [P, P, I, ctypes.POINTER(I)]
     lib.qasr_build_rope_tables.argtypes = [P, P, I, I, ctypes.c_double, P, I, I]
     lib.qasr_build_dim_map.argtypes = [P, I, I, I, P]
     lib.qasr_dequant_i8.argtypes = [P, P, I, I, P]
@@ -322,6 +325,16 @@ class TextDecoder:
         out = np.zeros(n.value, dtype=np.uint64)
         self._check(lib.qasr_read_trace(self._ctx, _ptr(out), n.value, ctypes.byref(n)))
         return out.reshape(self.cfg["num_hidden_layers"] + 1, -1, TRACE_SLOTS)
+
+    def read_attn_trace(self) -> np.ndarray:
+        """%globaltimer stamps of the last decode step's attention launches (trace=True):
+        uint64 [layer, cta, ATTN_TRACE_SLOTS] (see qasr_read_attn_trace)."""
+        n = ctypes.c_int(0)
+        probe = np.zeros(1, dtype=np.uint64)
+        self._check(lib.qasr_read_attn_trace(self._ctx, _ptr(probe), 0, ctypes.byref(n)))
+        out = np.zeros(n.value, dtype=np.uint64)
+        self._check(lib.qasr_read_attn_trace(self._ctx, _ptr(out), n.value, ctypes.byref(n)))
+        return out.reshape(self.cfg["num_hidden_layers"], -1, ATTN_TRACE_SLOTS)
 
     def read_logits(self, rows: int) -> np.ndarray:
         out = np.zeros((rows, self.cfg["vocab_size"]), dtype=np.float32)

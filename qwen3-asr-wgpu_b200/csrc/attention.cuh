@@ -25,6 +25,12 @@
 // state into a double-buffered shared slot and move on; warp 9 merges the 8 warps and
 // stores the output or, for a row cut into several chunks, the chunk's partial, which
 // attention_merge_kernel combines in chunk order.
+//
+// Programmatic dependent launch: with `early` > 0 (the decode step, where the launch
+// before this one appended exactly `early` new positions per row and wrote q), the page
+// producer streams stages made only of older positions before griddepcontrol.wait, so
+// the first KV bytes are in flight while the previous kernel drains; q and the stages
+// holding new positions are fetched after the wait.
 #pragma once
 #include "device_common.cuh"
 #include "gemm_tc.cuh"  // KvLayout, kv_elem_offset, griddep_*
@@ -66,6 +72,7 @@ struct AttnArgs {
   int rows;
   float scale;
   float* ws;        // [rows * nkv * ATTN_ROW_CHUNKS][ATTN_PART_FLOATS]: chunk partials
+  int early;        // > 0: positions >= len - early are new (see above); 0: wait first
   uint32_t* status;
   unsigned long long* trace;  // optional: per CTA ATTN_TRACE_SLOTS %globaltimer stamps
 };
@@ -153,7 +160,9 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
     abort_flag = 0;
     fence_mbar_init();
   }
-  griddep_wait();
+  // row_slot / row_pos / page tables and the older KV positions predate the previous
+  // launch; q, the new positions and the outputs' readers belong to it.
+  if (a.early <= 0) griddep_wait();
   griddep_launch_dependents();
 
   // ---- unit table: prefix[r] = first unit of row r (block-wide scan)
@@ -215,6 +224,17 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
     };
     AttnUnit t{}, tn{};
     int slot = 0, pg0 = 0, pg1 = 0, slotn = 0, pn0 = 0, pn1 = 0;
+    // Stages issued before griddepcontrol.wait (at most the ring's depth) that start a
+    // unit still owe their q rows: the pending q source per ring slot, loaded after the wait.
+    bool waited = a.early <= 0;
+    const __half* q_owed[ATTN_STAGES] = {};
+    auto wait_prev = [&]() {
+      griddep_wait();
+      waited = true;
+      if (lane == 0)
+        for (int j = 0; j < ATTN_STAGES; ++j)
+          if (q_owed[j] != nullptr) bulk_load(&sm_q[j][0], q_owed[j], 512u, &full_bar[j]);
+    };
     int u = blockIdx.x;
     if (u < U) fetch(u, t, slot, pg0, pg1);
     for (; u < U && ok; u += gridDim.x) {
@@ -223,6 +243,8 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
       const int pages = (t.len + 63) >> 6;
       const int* row = a.kv.page_table + static_cast<size_t>(slot) * a.kv.max_pages;
       for (int st = t.s0; st < t.s1; ++st) {
+        // before the wait: only the first ring pass, and only stages of older positions
+        if (!waited && (gs >= ATTN_STAGES || (st + 1) * 128 > t.len - a.early)) wait_prev();
         int w = 1;
         if (lane == 0) w = mbar_wait(&empty_bar[sl], ph ^ 1u, &abort_flag, a.status, 0x601) ? 1 : 0;
         if (!__shfl_sync(0xffffffffu, w, 0)) {
@@ -244,8 +266,11 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
           const bool first = st == t.s0;
           mbar_arrive_expect_tx(&full_bar[sl],
                                 static_cast<uint32_t>(np) * 2u * ATTN_PAGE_BYTES + (first ? 512u : 0u));
-          if (first)  // the unit's q rows (heads 2g, 2g+1: 512 contiguous bytes) ride along
-            bulk_load(&sm_q[sl][0], a.q + static_cast<size_t>(t.r) * a.q_ld + 2 * t.g * 128, 512u, &full_bar[sl]);
+          if (first) {  // the unit's q rows (heads 2g, 2g+1: 512 contiguous bytes) ride along
+            const __half* qs = a.q + static_cast<size_t>(t.r) * a.q_ld + 2 * t.g * 128;
+            if (waited) bulk_load(&sm_q[sl][0], qs, 512u, &full_bar[sl]);
+            else q_owed[sl] = qs;
+          }
           for (int pp = 0; pp < np; ++pp) {
             const int ui = p0 + pp - t.s0 * 2;
             const int page = ui < 64 ? pid[pp] : row[p0 + pp];  // units longer than 64 pages: direct
@@ -264,6 +289,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
       pg0 = pn0;
       pg1 = pn1;
     }
+    if (!waited) wait_prev();
     if (lane == 0) {
       attn_stamp(a, 6);
       for (int j = gs > ATTN_STAGES ? gs - ATTN_STAGES : 0; j < gs; ++j)  // drain
@@ -273,7 +299,9 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
   } else if (warp == ATTN_CONSUMER_WARPS + 1) {
     // ------------------------------------------------------------ merger
     // Combines the 8 warps of a unit; stores the output (one-chunk rows) or the chunk's
-    // partial (m, l, o) for attention_merge_kernel.  No fence or atomic on this path.
+    // partial (m, l, o) for attention_merge_kernel.  No fence or atomic on this path: a
+    // gpu-scope fence here would also wait for the CTA's page copies in flight.
+    if (a.early > 0) griddep_wait();
     int k = 0;
     for (int u = blockIdx.x; u < U; u += gridDim.x, ++k) {
       const AttnUnit t = attn_unit(a, prefix, u);
@@ -341,6 +369,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
     // split into f16 hi + lo terms so the softmax weights keep ~22 bits.
     const int g4 = lane >> 2, tig = lane & 3;
     const int lrow = lane & 7, lmat = lane >> 3;
+    if (a.early > 0) griddep_wait();
     int sl = 0, k = 0;
     uint32_t ph = 0;
     bool ok = true;

@@ -205,6 +205,7 @@ static GemmShape gemm_shape(int n_out, int k, bool int8, int rows, int num_sms) 
 
 // ----------------------------------------------------------------------------- decode chain
 static_assert(CHAIN_TRACE_SLOTS == QASR_TRACE_SLOTS, "trace layout of the C ABI");
+static_assert(ATTN_TRACE_SLOTS == QASR_ATTN_TRACE_SLOTS, "attention trace layout of the C ABI");
 struct ChainShape {
   int n_tile, w_stages, a_stages, n_acc;
   size_t smem;
@@ -341,6 +342,7 @@ struct qasr_ctx {
   int* gemm_cnt = nullptr;
   size_t gemm_cnt_n = 0;
   float* attn_ws = nullptr;
+  unsigned long long* attn_trace = nullptr;  // QASR_FLAG_TRACE: [L][sms][ATTN_TRACE_SLOTS]
   // decode chain (int8 weights, <= CHAIN_MAX_ROWS rows): partial sums and barrier counters
   bool chain_ok = false;
   float* chain_ws[4] = {};  // partial sums of the chain's QKV, o_proj, gate|up, down GEMMs
@@ -473,7 +475,9 @@ cudaError_t launch_attention_pair(const AttnArgs& a, int sms, cudaStream_t st, b
   return launch_k(attention_merge_kernel, dim3(a.rows * a.kv.nkv), dim3(256), 0, st, pdl, a);
 }
 
-qasr_status launch_attention(qasr_ctx* c, int layer, int rows, const int* rs, const int* rp) {
+// `early` > 0 only where the previous launch appended exactly that many positions per
+// row and wrote q, and everything else the attention reads predates it.
+qasr_status launch_attention(qasr_ctx* c, int layer, int rows, const int* rs, const int* rp, int early = 0) {
   AttnArgs a{};
   a.q = c->q;
   a.q_ld = c->cfg.num_attention_heads * c->cfg.head_dim;
@@ -489,7 +493,9 @@ qasr_status launch_attention(qasr_ctx* c, int layer, int rows, const int* rs, co
   a.rows = rows;
   a.scale = 1.0f / std::sqrt(static_cast<float>(c->cfg.head_dim));
   a.ws = c->attn_ws;
+  a.early = early;
   a.status = c->status;
+  if (c->attn_trace) a.trace = c->attn_trace + static_cast<size_t>(layer) * c->num_sms * ATTN_TRACE_SLOTS;
   CK(launch_attention_pair(a, c->num_sms, c->stream, true), "attention launch");
   return QASR_OK;
 }
@@ -676,7 +682,8 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
     if (s) return s;
   }
   for (int l = 0; l < L; ++l) {
-    qasr_status s = launch_attention(c, l, n, c->drow_slot, c->drow_pos);
+    // layer 0's row_pos comes from chain 0 (the launch just before it): no early start
+    qasr_status s = launch_attention(c, l, n, c->drow_slot, c->drow_pos, l > 0 ? 1 : 0);
     if (s) return s;
     const LayerDev& Ld = c->layers[l];
     ChainArgs a = base;
@@ -940,8 +947,10 @@ qasr_status qasr_create(const qasr_text_config* cfg, const qasr_options* opts, i
         (s = dalloc(c, &c->chain_row_rope, static_cast<size_t>(CHAIN_MAX_ROWS) * 256, "chain row rope")))
       return s;
     if ((opts->flags & QASR_FLAG_TRACE) &&
-        (s = dalloc(c, &c->chain_trace, static_cast<size_t>(L + 1) * c->num_sms * CHAIN_TRACE_SLOTS,
-                    "chain trace")))
+        ((s = dalloc(c, &c->chain_trace, static_cast<size_t>(L + 1) * c->num_sms * CHAIN_TRACE_SLOTS,
+                     "chain trace")) ||
+         (s = dalloc(c, &c->attn_trace, static_cast<size_t>(L) * c->num_sms * ATTN_TRACE_SLOTS,
+                     "attention trace"))))
       return s;
   }
   CK(cudaMallocHost(&c->pinned_tok, sizeof(int) * opts->max_slots * 2), "pinned alloc");
@@ -1342,6 +1351,18 @@ qasr_status qasr_read_trace(qasr_ctx* c, uint64_t* out, int cap, int* count) {
   return check_device_status(c);
 }
 
+qasr_status qasr_read_attn_trace(qasr_ctx* c, uint64_t* out, int cap, int* count) {
+  if (!c || !out || !count || cap < 0) return QASR_ERR_INVALID_ARG;
+  if (!c->attn_trace) return fail(c, QASR_ERR_STATE, "no trace: create the context with QASR_FLAG_TRACE (int8 weights)");
+  const size_t n = static_cast<size_t>(c->cfg.num_hidden_layers) * c->num_sms * ATTN_TRACE_SLOTS;
+  *count = static_cast<int>(n);
+  CK(cudaSetDevice(c->device), "cudaSetDevice");
+  CK(cudaMemcpyAsync(out, c->attn_trace, std::min(n, static_cast<size_t>(cap)) * sizeof(uint64_t),
+                     cudaMemcpyDeviceToHost, c->stream),
+     "trace readback");
+  return check_device_status(c);
+}
+
 // ============================================================================ probes
 static qasr_status probe_err(char* err, int errlen, qasr_status s, const std::string& m) {
   if (err && errlen > 0) {
@@ -1453,6 +1474,7 @@ qasr_status qasr_kernel_attention_traced(int device, void* stream, const uint16_
       return probe_err(err, errlen, QASR_ERR_OOM, "attention workspace");
     P.ws_floats = need;
   }
+
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
   AttnArgs a{};
@@ -1494,8 +1516,9 @@ qasr_status qasr_kernel_attention_traced(int device, void* stream, const uint16_
 // qasr_kernel_attention_noalloc in include/qasr_b200_kernels.h).  Its scratch — the
 // chunk partials of the split-row merge — is this file-scope array, sized for
 // NOALLOC_MAX_ROWS rows x NOALLOC_MAX_KV kv heads; nothing in it needs clearing
-// between calls (every partial a merge reads is written by the same call).  Every GPU that loads the library holds it until the process exits.  In host
-// code `g_attn_noalloc_scratch` only names the symbol; the device address comes from
+// between calls (every partial a merge reads is written by the same call).  Every GPU
+// that loads the library holds it until the process exits.  In host code
+// `g_attn_noalloc_scratch` only names the symbol; the device address comes from
 // cudaGetSymbolAddress, once per device.
 namespace qasr {
 constexpr int NOALLOC_MAX_ROWS = 64;

@@ -200,7 +200,23 @@ def bench_step(args, pkg, torch):
         st[1].synchronize()
         times.append(st[0].elapsed_time(st[1]) * 1e3)
     tr = dec.read_trace().astype(np.float64)  # [launch, cta, slot]
+    at = dec.read_attn_trace().astype(np.float64)  # [layer, cta, slot]
     dec.close()
+    # attention launch l sits between chain launches l and l + 1: its stamps relative to
+    # the last CTA exit of chain l (median / last CTA)
+    attn = []
+    for l in range(at.shape[0]):
+        x0 = tr[l, :, -1].max()
+        rel = lambda col: [round((np.median(col[col > 0]) - x0) / 1e3, 2), round((col[col > 0].max() - x0) / 1e3, 2)] \
+            if (col > 0).any() else None
+        e = at[l]
+        attn.append({"entry": rel(e[:, 0]), "unit_table": rel(e[:, 1]), "first_stage": rel(e[:, 2]),
+                     "first_merged": rel(e[:, 3]), "last_consumed": rel(e[:, 4]), "last_merged": rel(e[:, 5]),
+                     "next_chain_entry": round((tr[l + 1, :, 0].min() - x0) / 1e3, 2)})
+    attn_median = {k: ([round(statistics.median(a[k][i] for a in attn[1:]), 2) for i in range(2)]
+                       if isinstance(attn[1][k], list) else
+                       (round(statistics.median(a[k] for a in attn[1:]), 2) if attn[1][k] is not None else None))
+                   for k in attn[1]} if len(attn) > 1 else None
     t0 = tr[0, :, 0].min()
     launches = []
     for k in range(tr.shape[0]):
@@ -236,7 +252,7 @@ def bench_step(args, pkg, torch):
     return {"kernel": "decode_step", "slots": args.slots, "layers": args.layers, "median_step_us": statistics.median(times),
             "chain_dur_us_median": statistics.median(l["dur_us"] for l in launches[1:]),
             "gap_us_median": statistics.median(gaps), "launches": launches[:3], "last": launches[-1],
-            "gaps_us": gaps[:6]}
+            "gaps_us": gaps[:6], "attention_layers_1plus_median": attn_median, "attention_first": attn[:2]}
 
 
 def main(argv=None):
