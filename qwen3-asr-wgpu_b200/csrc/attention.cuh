@@ -207,6 +207,9 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
     // stage never waits on a row_slot -> page_table pointer chase.
     int sl = 0, gs = 0;
     uint32_t ph = 0;  // (gs / ATTN_STAGES) & 1, kept incrementally
+    // Each KV byte is read once per launch: evict-first, so the stream leaves L2's other
+    // contents (weights prefetched for the next launch, activations) in place.
+    const uint64_t kv_pol = l2_policy_evict_first();
     bool ok = true;
     const size_t head_stride = static_cast<size_t>(64) * 128;  // elements per (page, layer, which, head)
     auto page_base = [&](int page, int which, int g) {
@@ -274,8 +277,9 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
           for (int pp = 0; pp < np; ++pp) {
             const int ui = p0 + pp - t.s0 * 2;
             const int page = ui < 64 ? pid[pp] : row[p0 + pp];  // units longer than 64 pages: direct
-            bulk_load(buf + pp * ATTN_PAGE_BYTES, page_base(page, 0, t.g), ATTN_PAGE_BYTES, &full_bar[sl]);
-            bulk_load(buf + (2 + pp) * ATTN_PAGE_BYTES, page_base(page, 1, t.g), ATTN_PAGE_BYTES, &full_bar[sl]);
+            bulk_load_hint(buf + pp * ATTN_PAGE_BYTES, page_base(page, 0, t.g), ATTN_PAGE_BYTES, &full_bar[sl], kv_pol);
+            bulk_load_hint(buf + (2 + pp) * ATTN_PAGE_BYTES, page_base(page, 1, t.g), ATTN_PAGE_BYTES, &full_bar[sl],
+                           kv_pol);
           }
         }
         ++gs;

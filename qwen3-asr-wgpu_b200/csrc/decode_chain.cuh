@@ -89,6 +89,9 @@ struct ChainArgs {
   int rows, n_tile;
   int w_stages, a_stages;  // weight stages; unit slots (A stage in TMEM + X tile in smem)
   int n_acc;  // MMA issuer warps = accumulators per segment buffer (1 to 3)
+  ChainGemm next_first;  // the next chain launch's first GEMM (w == nullptr: none): its
+                         // units of this CTA are prefetched into L2 once this launch's
+                         // weights are all issued, so they are resident when it starts
   int hs, inter, nq, nkv;
   float eps;
   __half* h;    // [rows][hs] residual stream
@@ -337,6 +340,18 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
           break;
         } else {
           __nanosleep(32);  // leave the issue slots to this SM sub-partition's other warps
+        }
+      }
+      // the next launch's first weights and their row scales: into L2 while this launch
+      // and the attention run
+      if (a.next_first.w != nullptr && !abort_flag) {
+        const ChainGemm& nf = a.next_first;
+        int nu, nue;
+        chain_unit_range(nf, blockIdx.x, nu, nue);
+        for (int u = nu; u < nue; ++u) {
+          bulk_prefetch_l2(nf.w + static_cast<size_t>(u) * 16384, 16384u);
+          if (u == nu || u % nf.kblocks == 0)  // a new 128-row tile: its 128 f16 scales
+            bulk_prefetch_l2(nf.scale + static_cast<size_t>(u / nf.kblocks) * 128, 256u);
         }
       }
       // every issued copy lands before exit

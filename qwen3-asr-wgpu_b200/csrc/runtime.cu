@@ -669,6 +669,7 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
     a.trace = c->chain_trace;
     const LayerDev& L0 = c->layers[0];
     a.gemms[0] = gemm(L0.qkv, 0, 0);
+    a.next_first = gemm(L0.o, 1, 1);
     a.ops[0] = op(CH_EMBED_NORM, 0);
     a.ops[0].norm_w = L0.iln;
     a.ops[0].norm_out = c->x;
@@ -690,6 +691,7 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
     a.barrier = c->chain_bar + l + 1;
     if (c->chain_trace) a.trace = c->chain_trace + static_cast<size_t>(l + 1) * sms * CHAIN_TRACE_SLOTS;
     a.gemms[0] = gemm(Ld.o, 1, 1);
+    if (l + 1 < L) a.next_first = gemm(c->layers[l + 1].o, 1, 1);
     a.gemms[1] = gemm(Ld.gu, 0, 2);
     a.gemms[2] = gemm(Ld.down, 2, 3);
     int k = 0;
