@@ -174,7 +174,9 @@ qasr_status qasr_read_logits(qasr_ctx* ctx, float* out, int rows);
  * nanoseconds, launch = chain launch index of the step (layers + 1 of them), slot 0 =
  * CTA entry, 1 + 2 i = operation i done by this CTA, 2 + 2 i = the barrier after it
  * passed (i < 12), 25 + g = GEMM g's input seen ready, 29 + g = its first MMA issued,
- * 33 + g = its last MMA issued, 40 + j / 104 + j = the CTA's j-th unit of the launch
+ * 33 + g = its last MMA issued, 37 / 38 / 39 = barriers initialised / set-up done /
+ * producer ready, 64 / 65 = the first unit's weights seen / A slot free by the builders,
+ * 72 + j = unit j's A operand published, 40 + j / 104 + j = the CTA's j-th unit of the launch
  * seen complete (A built, X landed) / its MMAs issued (j < 24),
  * QASR_TRACE_SLOTS - 1 = exit; 0 where nothing happened.
  * *count receives launches * ctas * slots; at most `cap` values are written. */

@@ -117,7 +117,10 @@ struct ChainArgs {
   unsigned long long* trace;  // optional: per CTA CHAIN_TRACE_SLOTS %globaltimer stamps: 0 entry,
                               // 1 + 2 i op i done, 2 + 2 i barrier after op i passed (i < 12),
                               // 25 + g GEMM g's input seen ready, 29 + g its first MMA issued,
-                              // 33 + g its last MMA issued, 40 + j / 104 + j the CTA's j-th
+                              // 33 + g its last MMA issued, 37 / 38 / 39 barriers initialised /
+                              // set-up done / producer ready, 64 / 65 the first unit's W seen /
+                              // A slot free (builder warp 4), 72 + j unit j's A published,
+                              // 40 + j / 104 + j the CTA's j-th
                               // unit of the launch seen complete / its MMAs issued (j < 24),
                               // 127 exit
 };
@@ -127,8 +130,11 @@ __device__ __forceinline__ void chain_unit_range(const ChainGemm& g, int cta, in
     ub = ue = 0;
     return;
   }
-  ub = static_cast<int>(static_cast<long long>(cta) * g.units / g.grid);
-  ue = static_cast<int>(static_cast<long long>(cta + 1) * g.units / g.grid);
+  // 32-bit unsigned arithmetic (cta * units < 2^32: chain_gemm_plan bounds units); a
+  // 64-bit division here is a software routine that delayed every CTA's first copy
+  const unsigned int u = static_cast<unsigned int>(g.units), gr = static_cast<unsigned int>(g.grid);
+  ub = static_cast<int>(static_cast<unsigned int>(cta) * u / gr);
+  ue = static_cast<int>(static_cast<unsigned int>(cta + 1) * u / gr);
 }
 
 // non-blocking test of an mbarrier phase
@@ -249,6 +255,7 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
     abort_flag = 0;
     xready = (a.n_ops > 0 && a.ops[0].kind == CH_GEMM) ? 1 : 0;
     fence_mbar_init();
+    if (a.trace != nullptr) a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 37] = globaltimer();
   }
   if (warp == 2) {
     tmem_alloc(&tmem_base_sh, GEMM_TMEM_COLS);
@@ -264,6 +271,7 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_sh;
   griddep_wait();
+  if (threadIdx.x == 0 && a.trace != nullptr) a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 38] = globaltimer();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -290,6 +298,7 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
       };
       w_advance();
       x_advance();
+      if (a.trace != nullptr) a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 39] = globaltimer();
       uint64_t t_idle = globaltimer();
       while (wu < wue || xu < xue) {
         bool prog = false;
@@ -469,13 +478,20 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
           aph ^= 1u;
         }
         const __half sc = g.scale[(u / g.kblocks) * 128 + t];
-        if (!mbar_wait_warp(&wfull_bar[my_st], my_ph, &abort_flag, a.status, 0x731) ||
-            !mbar_wait_warp(&ufree_bar[my_ast], my_aph ^ 1u, &abort_flag, a.status, 0x732)) {
+        if (!mbar_wait_warp(&wfull_bar[my_st], my_ph, &abort_flag, a.status, 0x731)) {
+          ok = false;
+          break;
+        }
+        if (i == 0 && warp == 4 && lane == 0 && a.trace != nullptr)
+          a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 64] = globaltimer();
+        if (!mbar_wait_warp(&ufree_bar[my_ast], my_aph ^ 1u, &abort_flag, a.status, 0x732)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const __half2 sc2 = __halves2half2(sc, sc);
+        if (i == 0 && warp == 4 && lane == 0 && a.trace != nullptr)
+          a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 65] = globaltimer();
         const uint8_t* row = smem + static_cast<size_t>(my_st) * 16384 + t * 128;
         uint4 chunk[8];
 #pragma unroll
@@ -505,6 +521,8 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&ufull_bar[my_ast]);
+        if (i < 24 && warp == 4 && lane == 0 && a.trace != nullptr)
+          a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 72 + i] = globaltimer();
       }
     }
   } else if (warp >= EPI_WARP0) {

@@ -116,7 +116,11 @@ __device__ __forceinline__ void trace_stamp(const GemmArgs& a, int slot) {
 
 __device__ __forceinline__ int cta_of_unit(long long x, long long units, long long grid) {
   // CTA c owns units [c*U/G, (c+1)*U/G); the owner of x is the largest c with c*U/G <= x.
-  return static_cast<int>(((x + 1) * grid + units - 1) / units - 1);
+  // Unsigned 32-bit arithmetic ((x + 1) * G + U <= 2 U G < 2^32 for every GEMM of these
+  // models: U <= 19K units, G <= the SM count); a 64-bit division is a slow software routine.
+  const unsigned int xu = static_cast<unsigned int>(x), U = static_cast<unsigned int>(units),
+                     G = static_cast<unsigned int>(grid);
+  return static_cast<int>(((xu + 1u) * G + U - 1u) / U) - 1;
 }
 
 // ------------------------------------------------------------------ epilogues

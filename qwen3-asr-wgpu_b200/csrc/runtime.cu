@@ -423,6 +423,9 @@ qasr_status check_device_status(qasr_ctx* c) {
 qasr_status plan_gemm(qasr_ctx* c, const Linear& lin, const __half* X, int ldx, int rows, int epi,
                       GemmLaunch* L) {
   const GemmShape s = gemm_shape(lin.n_out, lin.k, lin.int8, rows, c->num_sms);
+  if (2ull * static_cast<unsigned long long>(s.units) * static_cast<unsigned long long>(s.grid) >= (1ull << 32))
+    return fail(c, QASR_ERR_CAPACITY, "GEMM %d x %d over %d rows: too many units for 32-bit unit maps",
+                lin.n_out, lin.k, rows);
   if (s.ws_floats > c->gemm_ws_floats || static_cast<size_t>(s.tiles) > c->gemm_cnt_n)
     return fail(c, QASR_ERR_CAPACITY, "GEMM workspace too small for %d x %d over %d rows",
                 lin.n_out, lin.k, rows);
@@ -939,6 +942,8 @@ qasr_status qasr_create(const qasr_text_config* cfg, const qasr_options* opts, i
     for (int i = 0; i < 4; ++i) {  // shapes[] order: QKV, o_proj, gate|up, down
       const ChainGemm g = chain_gemm_plan(nullptr, nullptr, shapes[i][0], shapes[i][1], 0, c->num_sms,
                                           chain_seg_cap(i));
+      if (2ull * static_cast<unsigned long long>(g.units) * static_cast<unsigned long long>(g.grid) >= (1ull << 32))
+        return fail(c, QASR_ERR_CAPACITY, "decode chain GEMM: too many units for 32-bit unit maps");
       if ((s = dalloc(c, &c->chain_ws[i],
                       static_cast<size_t>(shapes[i][0] / 128) * g.max_seg * c->chain_ws_rows * 128, "chain workspace")))
         return s;

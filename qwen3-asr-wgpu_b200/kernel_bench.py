@@ -245,6 +245,9 @@ def bench_step(args, pkg, torch):
                           for b in (40, 72, 104)]
         launches.append({"start_us": round((ent - t0) / 1e3, 2), "dur_us": round((ext - ent) / 1e3, 2),
                          "entry_skew_us": round((tr[k, :, 0].max() - ent) / 1e3, 2),
+                         "prologue_median_us": [round((np.median(tr[k, :, j]) - ent) / 1e3, 2) for j in (37, 38, 39)],
+                         "first_unit_w_slot_a_seen_issued_us": [round((np.median(tr[k, :, j]) - ent) / 1e3, 2)
+                                                                for j in (64, 65, 72, 40, 104)],
                          "ops_done_passed_us": ops, "gemms_median_max_us": gemms,
                          "units_w_a_mma_cta0_cta100": units})
     gaps = [round((launches[k + 1]["start_us"] - launches[k]["start_us"] - launches[k]["dur_us"]), 2)
