@@ -45,8 +45,11 @@ typedef enum {
 
 /* Weight storage formats of the decoder linears. */
 enum {
-  QASR_WEIGHTS_F16 = 0,  /* f16 [out, in] row-major, as the reference's f16 kernels read */
-  QASR_WEIGHTS_INT8 = 1  /* int8 [out, in] + f16 per-row scale: value = f16(f32(q) * s)  */
+  QASR_WEIGHTS_F16 = 0,     /* f16 [out, in] row-major, as the reference's f16 kernels read */
+  QASR_WEIGHTS_INT8 = 1,    /* int8 [out, in] + f16 per-row scale: value = f16(f32(q) * s)  */
+  QASR_WEIGHTS_INT8_F32 = 2 /* int8 [out, in] + f32 per-row scale, the INT8 export's own
+                               `.weight_scale` (PackedInt8, src/weights.rs:309-356):
+                               value = f16(f32(q) * s), the f32 product rounded to f16 */
 };
 
 /* Text decoder hyper-parameters; mirrors `TextConfig` (src/decoder.rs:166-175) with
@@ -88,11 +91,12 @@ typedef struct {
 /* Weights of one decoder layer (HF names, src/cpu_decoder.rs:126-138).  Linear
  * weights are [out, in] row-major: q [nqh*hd, hs], k/v [nkv*hd, hs], o [hs, nqh*hd],
  * gate/up [I, hs], down [hs, I].  With QASR_WEIGHTS_INT8 each linear points at int8
- * data and its *_scale at `out` f16 scales; with QASR_WEIGHTS_F16 the *_scale fields
- * are ignored.  Norm gains are f16 vectors. */
+ * data and its *_scale at `out` f16 scales, with QASR_WEIGHTS_INT8_F32 at `out` f32
+ * scales; with QASR_WEIGHTS_F16 the *_scale fields are ignored.  Norm gains are f16
+ * vectors. */
 typedef struct {
   const void *q_proj, *k_proj, *v_proj, *o_proj, *gate_proj, *up_proj, *down_proj;
-  const uint16_t *q_scale, *k_scale, *v_scale, *o_scale, *gate_scale, *up_scale, *down_scale;
+  const void *q_scale, *k_scale, *v_scale, *o_scale, *gate_scale, *up_scale, *down_scale;
   const uint16_t *input_layernorm, *post_attention_layernorm, *q_norm, *k_norm;
 } qasr_layer_weights;
 

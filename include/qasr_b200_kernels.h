@@ -31,13 +31,13 @@ qasr_status qasr_kernel_pack_weights(int device, void* stream, int weight_format
 
 /* out[r, m] = f16(sum_k W[m, k] x[r, k])            (accumulate == 0)
  * out[r, m] = f16(f32(out[r, m]) + sum_k ...)         (accumulate != 0)
- * W: [n_out, k] f16 (weight_format QASR_WEIGHTS_F16) or int8 + f16 per-row scale
- * (QASR_WEIGHTS_INT8, value f16(f32(q) * s)), in the layout qasr_kernel_pack_weights
- * produces.  n_out % 128 == 0; k % 128 == 0.
+ * W: [n_out, k] f16 (weight_format QASR_WEIGHTS_F16) or int8 + a per-row scale, f16
+ * (QASR_WEIGHTS_INT8) or f32 (QASR_WEIGHTS_INT8_F32), value f16(f32(q) * s), in the
+ * layout qasr_kernel_pack_weights produces.  n_out % 128 == 0; k % 128 == 0.
  * Replaces gemv / gemv_w8 / gemv_batch_slots / prefill_gemm(_w8)
  * (src/shaders.rs:273-889, 2995-3082). */
 qasr_status qasr_kernel_gemm(int device, void* stream, int weight_format, const void* w,
-                             const uint16_t* scale, int n_out, int k, const uint16_t* x, int ldx,
+                             const void* scale, int n_out, int k, const uint16_t* x, int ldx,
                              int rows, uint16_t* out, int ldo, int accumulate, char* err,
                              int errlen);
 
@@ -46,7 +46,7 @@ qasr_status qasr_kernel_gemm(int device, void* stream, int weight_format, const 
  * first weight/activation copies issued, first stage seen/built, first/last MMA, first
  * accumulator, last store, split fixup, exit); *grid_out receives the CTA count. */
 qasr_status qasr_kernel_gemm_traced(int device, void* stream, int weight_format, const void* w,
-                                    const uint16_t* scale, int n_out, int k, const uint16_t* x,
+                                    const void* scale, int n_out, int k, const uint16_t* x,
                                     int ldx, int rows, uint16_t* out, int ldo, int accumulate,
                                     unsigned long long* trace, int* grid_out, char* err,
                                     int errlen);

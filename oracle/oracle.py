@@ -128,15 +128,19 @@ class OracleModel:
         lib.oracle_load_embed(self._m, _p(np.ascontiguousarray(embed)), _p(np.ascontiguousarray(final_norm)))
 
     def load_layer(self, layer: int, w: dict):
-        """w: the same dict the B200 library gets; int8 scales (f16 bits) are widened to
-        F32 exactly, the reference's PackedInt8 scale format."""
+        """w: the same dict the B200 library gets; int8 scales are the reference's
+        PackedInt8 F32 format: float32 arrays as given, f16 bits widened exactly."""
         int8 = w["q_proj"].dtype == np.int8
         lins = [np.ascontiguousarray(w[n]) for n in LINEARS]
         lin_arr = (ctypes.c_void_p * 7)(*[a.ctypes.data for a in lins])
         scales = []
         if int8:
-            scales = [np.ascontiguousarray(np.asarray(w[n.replace("_proj", "_scale")], dtype=np.uint16)
-                                           .view(np.float16).astype(np.float32)) for n in LINEARS]
+            def f32_scale(a):
+                a = np.asarray(a)
+                if a.dtype == np.float32:
+                    return np.ascontiguousarray(a)
+                return np.ascontiguousarray(a.astype(np.uint16).view(np.float16).astype(np.float32))
+            scales = [f32_scale(w[n.replace("_proj", "_scale")]) for n in LINEARS]
         sc_arr = (ctypes.c_void_p * 7)(*[a.ctypes.data for a in scales]) if int8 else (ctypes.c_void_p * 7)()
         norms = [np.ascontiguousarray(w[n]) for n in ("input_layernorm", "post_attention_layernorm",
                                                        "q_norm", "k_norm")]
@@ -144,10 +148,10 @@ class OracleModel:
         if st != 0:
             raise ValueError(f"oracle_load_layer({layer}) failed")
 
-    def load_model(self, model, int8: bool):
+    def load_model(self, model, int8: bool, scale_f32: bool = False):
         self.load_embed(model.embed, model.final_norm)
         for l in range(self.cfg["num_hidden_layers"]):
-            self.load_layer(l, model.layer(l, int8=int8))
+            self.load_layer(l, model.layer(l, int8=int8, scale_f32=scale_f32))
 
     def set_rope_tables(self, cos, sin):
         lib.oracle_set_rope_tables(self._m, _p(np.ascontiguousarray(cos)), _p(np.ascontiguousarray(sin)),

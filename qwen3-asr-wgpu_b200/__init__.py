@@ -32,6 +32,7 @@ STATUS_NAMES = {
 }
 WEIGHTS_F16 = 0
 WEIGHTS_INT8 = 1
+WEIGHTS_INT8_F32 = 2  # int8 + f32 per-row scales (the INT8 export's own `.weight_scale`)
 FLAG_KEEP_LOGITS = 1
 FLAG_NO_GRAPH = 2
 FLAG_TRACE = 4
@@ -230,12 +231,17 @@ class TextDecoder:
         self._check(lib.qasr_load_embed(self._ctx, _ptr(embed), _ptr(final_norm)))
 
     def load_layer(self, layer: int, w: dict):
-        """w: HF-named arrays (q_proj ... down_proj, *_scale for INT8, norms)."""
+        """w: HF-named arrays (q_proj ... down_proj, *_scale for INT8, norms).  Scales are
+        f16 bits (uint16) for WEIGHTS_INT8 and float32 for WEIGHTS_INT8_F32."""
         lw = LayerWeights()
         keep = []
+        want = {WEIGHTS_INT8: np.uint16, WEIGHTS_INT8_F32: np.float32}.get(self.weight_format)
         for name, _ in LayerWeights._fields_:
             a = w.get(name)
             if a is not None:
+                if name.endswith("_scale") and want is not None and np.asarray(a).dtype != want:
+                    raise ValueError(f"{name}: {np.asarray(a).dtype} scales for weight format "
+                                     f"{self.weight_format} (needs {np.dtype(want).name})")
                 a = np.ascontiguousarray(a)
                 keep.append(a)
                 setattr(lw, name, a.ctypes.data)
@@ -244,7 +250,8 @@ class TextDecoder:
     def load_model(self, model: "SyntheticModel"):
         self.load_embed(model.embed, model.final_norm)
         for layer in range(self.cfg["num_hidden_layers"]):
-            self.load_layer(layer, model.layer(layer, int8=self.weight_format == WEIGHTS_INT8))
+            self.load_layer(layer, model.layer(layer, int8=self.weight_format != WEIGHTS_F16,
+                                               scale_f32=self.weight_format == WEIGHTS_INT8_F32))
 
     def set_rope_tables(self, cos: np.ndarray, sin: np.ndarray):
         positions = cos.shape[0]
@@ -447,7 +454,7 @@ def version() -> str:
 __all__ = [
     "TextDecoder", "DecoderError", "SyntheticModel", "MODEL_PRESETS", "text_config",
     "build_rope_tables", "dim_map", "kernel_pack_weights", "kernel_gemm", "kernel_attention_noalloc", "kernel_attention", "kernel_kv_append",
-    "launch_count", "version", "WEIGHTS_F16", "WEIGHTS_INT8", "EXPORTED_SYMBOLS", "lib",
+    "launch_count", "version", "WEIGHTS_F16", "WEIGHTS_INT8", "WEIGHTS_INT8_F32", "EXPORTED_SYMBOLS", "lib",
     "f16_bits_to_f32", "f32_to_f16_bits", "PAGE_POSITIONS", "kv_page_swizzle", "FLAG_TRACE",
     "TRACE_SLOTS",
 ]

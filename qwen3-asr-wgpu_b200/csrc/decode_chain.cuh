@@ -61,7 +61,8 @@ enum ChainOpKind : int {
 
 struct ChainGemm {
   const uint8_t* w;     // int8 weights in the tiled layout (weight_tile_offset)
-  const __half* scale;  // f16 per-row scales
+  const void* scale;    // per-row scales: f16, or f32 when scale32
+  int scale32;
   int kblocks;          // K / 128
   int units;            // (n_out / 128) * kblocks
   int grid;             // CTAs that take part: the first `grid` of the launch
@@ -359,8 +360,11 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
         chain_unit_range(nf, blockIdx.x, nu, nue);
         for (int u = nu; u < nue; ++u) {
           bulk_prefetch_l2(nf.w + static_cast<size_t>(u) * 16384, 16384u);
-          if (u == nu || u % nf.kblocks == 0)  // a new 128-row tile: its 128 f16 scales
-            bulk_prefetch_l2(nf.scale + static_cast<size_t>(u / nf.kblocks) * 128, 256u);
+          if (u == nu || u % nf.kblocks == 0) {  // a new 128-row tile: its 128 scales
+            const uint32_t sb = nf.scale32 ? 4u : 2u;
+            bulk_prefetch_l2(static_cast<const uint8_t*>(nf.scale) + static_cast<size_t>(u / nf.kblocks) * 128 * sb,
+                             128u * sb);
+          }
         }
       }
       // every issued copy lands before exit
@@ -461,7 +465,6 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
     int st = 0, ast = 0, i = 0;  // W stage, unit slot
     uint32_t ph = 0, aph = 0;
     bool ok = true;
-    const __half2 bias = __floats2half2_rn(1152.0f, 1152.0f);
     for (int gi = 0; gi < n_gemm_ops && ok; ++gi) {
       const ChainGemm& g = a.gemms[gi];
       int ub, ue;
@@ -477,7 +480,10 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
           ast = 0;
           aph ^= 1u;
         }
-        const __half sc = g.scale[(u / g.kblocks) * 128 + t];
+        const bool f32s = g.scale32 != 0;
+        const int srow = (u / g.kblocks) * 128 + t;
+        const float sc32 = f32s ? static_cast<const float*>(g.scale)[srow] : 1.0f;
+        const __half sc = f32s ? __float2half_rn(1.0f) : static_cast<const __half*>(g.scale)[srow];
         if (!mbar_wait_warp(&wfull_bar[my_st], my_ph, &abort_flag, a.status, 0x731)) {
           ok = false;
           break;
@@ -499,24 +505,20 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&wfree_bar[my_st]);  // the W stage is read: refill it
         const uint32_t taddr = tmem_base + lane_base + A_COLS0 + static_cast<uint32_t>(my_ast) * 64u;
+        // one body per scale width: the choice is made once per unit, not per word
+        auto build_row = [&](auto f32tag) {
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint32_t w4[4] = {chunk[c].x, chunk[c].y, chunk[c].z, chunk[c].w};
-          uint32_t outw[8];
+          for (int c = 0; c < 8; ++c) {
+            const uint32_t w4[4] = {chunk[c].x, chunk[c].y, chunk[c].z, chunk[c].w};
+            uint32_t outw[8];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint32_t ub8 = w4[q] ^ 0x80808080u;  // q + 128 as unsigned bytes
-            uint32_t lo = __byte_perm(ub8, 0x64646464u, 0x4140);
-            uint32_t hi = __byte_perm(ub8, 0x64646464u, 0x4342);
-            __half2 hl = __hsub2(*reinterpret_cast<__half2*>(&lo), bias);  // exact q
-            __half2 hh = __hsub2(*reinterpret_cast<__half2*>(&hi), bias);
-            hl = __hmul2_rn(hl, sc2);  // f16(q * s), one IEEE rounding
-            hh = __hmul2_rn(hh, sc2);
-            outw[2 * q] = *reinterpret_cast<uint32_t*>(&hl);
-            outw[2 * q + 1] = *reinterpret_cast<uint32_t*>(&hh);
+            for (int q = 0; q < 4; ++q)
+              dequant_i8x4<decltype(f32tag)::value>(w4[q], sc2, sc32, outw[2 * q], outw[2 * q + 1]);
+            tmem_st_x8(taddr + static_cast<uint32_t>(c) * 8u, reinterpret_cast<const uint32_t(&)[8]>(outw));
           }
-          tmem_st_x8(taddr + static_cast<uint32_t>(c) * 8u, reinterpret_cast<const uint32_t(&)[8]>(outw));
-        }
+        };
+        if (f32s) build_row(std::true_type{});
+        else build_row(std::false_type{});
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();

@@ -17,10 +17,10 @@
 //   f16 weights: the weight tile in shared memory already is the canonical K-major
 //               128-byte-swizzled operand, so A is read straight from shared memory.
 //   int8 weights: two warpgroups of "A builders" (warps 4-11) take alternate units:
-//               each thread reads one W row from the swizzled tile, dequantises it as
-//               f16(f32(q) * scale) with one correctly rounded f16 multiply (the exact
-//               value dequant_i8 produces, src/weights.rs:372-385) and stores the row into
-//               TMEM, which the MMA then reads as its A operand.
+//               each thread reads one W row from the swizzled tile, dequantises it to
+//               f16(f32(q) * scale) (the value dequant_i8 produces, src/weights.rs:372-385;
+//               see dequant_i8x4) and stores the row into TMEM, which the MMA then reads as
+//               its A operand.
 //   last 4 warps  epilogue: TMEM accumulators -> fused epilogue (see EpiKind)
 //
 // Work split: the (tile, k-block) units are cut into equal contiguous ranges, one per
@@ -28,6 +28,7 @@
 // on the tile's counter; it adds the f32 partials in segment order, so results do not
 // depend on arrival order.  No CTA ever waits on another.
 #pragma once
+#include <type_traits>
 #include "device_common.cuh"
 
 namespace qasr {
@@ -76,7 +77,8 @@ __device__ __forceinline__ size_t kv_elem_offset(const KvLayout& kv, int slot, i
 struct GemmArgs {
   int n_out, k, rows, n_tile, n_tiles, kblocks, units, grid, stages, max_seg;
   const uint8_t* w_tiles;  // weights in the tiled layout (weight_tile_offset)
-  const __half* scale;     // int8: f16 per-row scale
+  const void* scale;       // int8: per-row scale, f16 or (scale32) f32
+  int scale32;
   // epilogue
   int epi;
   __half* out;
@@ -121,6 +123,32 @@ __device__ __forceinline__ int cta_of_unit(long long x, long long units, long lo
   const unsigned int xu = static_cast<unsigned int>(x), U = static_cast<unsigned int>(units),
                      G = static_cast<unsigned int>(grid);
   return static_cast<int>(((xu + 1u) * G + U - 1u) / U) - 1;
+}
+
+// Four int8 weights (one little-endian word, byte j = value j) -> f16(f32(q) * s) as two
+// packed f16 pairs (values 0,1 and 2,3).  q + 1152 is built exactly as an f16 by byte
+// placement and the bias subtracted exactly.  An f16 scale: q * s is exact in f32
+// (8 x 11 significant bits), so one f16 multiply rounds it once, as f16(f32(q) * s).  An
+// f32 scale (the INT8 export's `.weight_scale`, PackedInt8 src/weights.rs:309-356): the
+// f32 product, then the f16 rounding — both of the reference's roundings.
+template <bool F32S>
+__device__ __forceinline__ void dequant_i8x4(uint32_t w, __half2 s16, float s32, uint32_t& o01, uint32_t& o23) {
+  const __half2 bias = __floats2half2_rn(1152.0f, 1152.0f);
+  const uint32_t ub8 = w ^ 0x80808080u;  // q + 128 as unsigned bytes
+  uint32_t lo = __byte_perm(ub8, 0x64646464u, 0x4140);
+  uint32_t hi = __byte_perm(ub8, 0x64646464u, 0x4342);
+  __half2 hl = __hsub2(*reinterpret_cast<__half2*>(&lo), bias);  // exact q
+  __half2 hh = __hsub2(*reinterpret_cast<__half2*>(&hi), bias);
+  if constexpr (F32S) {
+    const float2 fl = __half22float2(hl), fh = __half22float2(hh);
+    hl = __floats2half2_rn(__fmul_rn(fl.x, s32), __fmul_rn(fl.y, s32));
+    hh = __floats2half2_rn(__fmul_rn(fh.x, s32), __fmul_rn(fh.y, s32));
+  } else {
+    hl = __hmul2_rn(hl, s16);
+    hh = __hmul2_rn(hh, s16);
+  }
+  o01 = *reinterpret_cast<uint32_t*>(&hl);
+  o23 = *reinterpret_cast<uint32_t*>(&hh);
 }
 
 // ------------------------------------------------------------------ epilogues
@@ -510,6 +538,8 @@ __global__ void __launch_bounds__(gemm_threads(INT8), 1)
     uint32_t ph = static_cast<uint32_t>((grp / S) & 1), aph = static_cast<uint32_t>((grp / SA) & 1);
     int cur_mt = -1, pend_ast = -1;
     __half2 sc2 = __floats2half2_rn(1.0f, 1.0f);
+    float sc32 = 1.0f;
+    const bool f32s = a.scale32 != 0;
     for (int i = grp; i < n; i += NBG) {
       if (!mbar_wait_warp(&wfull_bar[st], ph, &abort_flag, a.status, 0x301)) break;
       if (!mbar_wait_warp(&afree_bar[ast], aph ^ 1u, &abort_flag, a.status, 0x302)) break;
@@ -517,37 +547,36 @@ __global__ void __launch_bounds__(gemm_threads(INT8), 1)
       if (i == 0 && t == 0) trace_stamp(a, 4);
       const int mt = cur.mt;
       if (INT8 && mt != cur_mt) {
-        const __half sc = a.scale[mt * 128 + t];
-        sc2 = __halves2half2(sc, sc);
+        if (f32s) {
+          sc32 = static_cast<const float*>(a.scale)[mt * 128 + t];
+        } else {
+          const __half sc = static_cast<const __half*>(a.scale)[mt * 128 + t];
+          sc2 = __halves2half2(sc, sc);
+        }
         cur_mt = mt;
       }
       const uint8_t* row = smem + static_cast<size_t>(st) * stage_bytes + t * 128;
       const uint32_t taddr = tmem_base + lane_base + A_COLS0 + static_cast<uint32_t>(ast) * ACOLS;
+      // one body per scale width: the choice is made once per unit, not per word
+      auto build_row = [&](auto f32tag) {
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint4 chunk = *reinterpret_cast<const uint4*>(row + ((c ^ (t & 7)) << 4));
-        if constexpr (INT8) {
-          const uint32_t w4[4] = {chunk.x, chunk.y, chunk.z, chunk.w};
-          uint32_t outw[8];
-          const __half2 bias = __floats2half2_rn(1152.0f, 1152.0f);
+        for (int c = 0; c < 8; ++c) {
+          const uint4 chunk = *reinterpret_cast<const uint4*>(row + ((c ^ (t & 7)) << 4));
+          if constexpr (INT8) {
+            const uint32_t w4[4] = {chunk.x, chunk.y, chunk.z, chunk.w};
+            uint32_t outw[8];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint32_t ub8 = w4[q] ^ 0x80808080u;  // q + 128 as unsigned bytes
-            uint32_t lo = __byte_perm(ub8, 0x64646464u, 0x4140);
-            uint32_t hi = __byte_perm(ub8, 0x64646464u, 0x4342);
-            __half2 hl = __hsub2(*reinterpret_cast<__half2*>(&lo), bias);  // exact q
-            __half2 hh = __hsub2(*reinterpret_cast<__half2*>(&hi), bias);
-            hl = __hmul2_rn(hl, sc2);  // f16(q * s), one IEEE rounding
-            hh = __hmul2_rn(hh, sc2);
-            outw[2 * q] = *reinterpret_cast<uint32_t*>(&hl);
-            outw[2 * q + 1] = *reinterpret_cast<uint32_t*>(&hh);
+            for (int q = 0; q < 4; ++q)
+              dequant_i8x4<decltype(f32tag)::value>(w4[q], sc2, sc32, outw[2 * q], outw[2 * q + 1]);
+            tmem_st_x8(taddr + static_cast<uint32_t>(c) * 8u, reinterpret_cast<const uint32_t(&)[8]>(outw));
+          } else {
+            const uint32_t w4[4] = {chunk.x, chunk.y, chunk.z, chunk.w};
+            tmem_st_x4(taddr + static_cast<uint32_t>(c) * 4u, w4);
           }
-          tmem_st_x8(taddr + static_cast<uint32_t>(c) * 8u, reinterpret_cast<const uint32_t(&)[8]>(outw));
-        } else {
-          const uint32_t w4[4] = {chunk.x, chunk.y, chunk.z, chunk.w};
-          tmem_st_x4(taddr + static_cast<uint32_t>(c) * 4u, w4);
         }
-      }
+      };
+      if (INT8 && f32s) build_row(std::true_type{});
+      else build_row(std::false_type{});
       // Publish two built units per wait: the TMEM store round trip is paid once for both.
       // (Needs S >= NBG + 1 and SA >= NBG + 1 so the unit built next never waits on the
       // pending one; the host guarantees both.)

@@ -77,9 +77,10 @@ static bool make_tmap(CUtensorMap* m, const void* base, bool bytes1, uint64_t in
 // ----------------------------------------------------------------------------- GEMM plan
 struct Linear {
   void* w = nullptr;        // device, tiled layout (weight_tile_offset)
-  __half* scale = nullptr;  // device [n_out] (int8)
+  void* scale = nullptr;    // device [n_out] (int8): f16, or f32 when scale32
   int n_out = 0, k = 0;
   bool int8 = false;
+  bool scale32 = false;
 };
 
 // Launch with programmatic stream serialization (PDL) unless disabled by
@@ -237,11 +238,12 @@ static int chain_seg_cap(int kind) {
 // int8 GEMM of the chain: at least two units (32 KB of weights) per taking-part CTA, and
 // few enough taking-part CTAs that no tile is cut into more than `max_seg_cap` segments
 // (the bound of the operation that adds the partials).
-static ChainGemm chain_gemm_plan(const uint8_t* w, const __half* scale, int n_out, int k, int xmap, int sms,
-                                 int max_seg_cap) {
+static ChainGemm chain_gemm_plan(const uint8_t* w, const void* scale, bool scale32, int n_out, int k, int xmap,
+                                 int sms, int max_seg_cap) {
   ChainGemm g{};
   g.w = w;
   g.scale = scale;
+  g.scale32 = scale32 ? 1 : 0;
   g.kblocks = k / 128;
   g.units = (n_out / 128) * g.kblocks;
   for (g.grid = std::max(1, std::min(sms, g.units / 2));; --g.grid) {
@@ -450,6 +452,7 @@ qasr_status plan_gemm(qasr_ctx* c, const Linear& lin, const __half* X, int ldx, 
   a.max_seg = s.max_seg;
   a.w_tiles = static_cast<const uint8_t*>(lin.w);
   a.scale = lin.scale;
+  a.scale32 = lin.scale32 ? 1 : 0;
   a.epi = epi;
   a.ws = c->gemm_ws;
   a.counters = c->gemm_cnt;
@@ -654,7 +657,7 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
   base.ss = c->chain_ss;
   base.status = c->status;
   auto gemm = [&](const Linear& lin, int xmap, int kind) {
-    ChainGemm g = chain_gemm_plan(static_cast<const uint8_t*>(lin.w), lin.scale, lin.n_out, lin.k, xmap, sms,
+    ChainGemm g = chain_gemm_plan(static_cast<const uint8_t*>(lin.w), lin.scale, lin.scale32, lin.n_out, lin.k, xmap, sms,
                                   chain_seg_cap(kind));
     g.ws = c->chain_ws[kind];
     return g;
@@ -767,14 +770,15 @@ qasr_status grow_slot(qasr_ctx* c, int slot, int need) {
   return QASR_OK;
 }
 
-qasr_status upload_linear(qasr_ctx* c, Linear* lin, int n_out, int k, bool int8,
+qasr_status upload_linear(qasr_ctx* c, Linear* lin, int n_out, int k, bool int8, bool scale32,
                           const std::vector<const void*>& parts, const std::vector<int>& part_rows,
-                          const std::vector<const uint16_t*>& scales,
+                          const std::vector<const void*>& scales,
                           const std::vector<int>& row_order /* fused row -> (part,row) flat */) {
-  // Fuse the parts along the output dim in `row_order` and upload.
+  // Fuse the parts along the output dim in `row_order` (scales in the same order) and upload.
   const size_t elem = int8 ? 1 : 2;
+  const size_t selem = scale32 ? 4 : 2;
   std::vector<uint8_t> host(static_cast<size_t>(n_out) * k * elem);
-  std::vector<uint16_t> host_s(int8 ? n_out : 0);
+  std::vector<uint8_t> host_s(int8 ? static_cast<size_t>(n_out) * selem : 0);
   std::vector<int> part_base(parts.size(), 0);
   for (size_t p = 1; p < parts.size(); ++p) part_base[p] = part_base[p - 1] + part_rows[p - 1];
   for (int r = 0; r < n_out; ++r) {
@@ -784,12 +788,14 @@ qasr_status upload_linear(qasr_ctx* c, Linear* lin, int n_out, int k, bool int8,
     const int pr = src - part_base[p];
     std::memcpy(&host[static_cast<size_t>(r) * k * elem],
                 static_cast<const uint8_t*>(parts[p]) + static_cast<size_t>(pr) * k * elem, k * elem);
-    if (int8) host_s[r] = scales[p][pr];
+    if (int8) std::memcpy(&host_s[static_cast<size_t>(r) * selem], static_cast<const uint8_t*>(scales[p]) + pr * selem, selem);
   }
   if (!lin->w) {
     qasr_status s = dalloc(c, reinterpret_cast<uint8_t**>(&lin->w), host.size(), "weight alloc");
     if (s) return s;
-    if (int8 && (s = dalloc(c, &lin->scale, n_out, "scale alloc"))) return s;
+    if (int8 && (s = dalloc(c, reinterpret_cast<uint8_t**>(&lin->scale), host_s.size(), "scale alloc"))) return s;
+  } else if (int8 && lin->scale32 != scale32) {
+    return fail(c, QASR_ERR_INVALID_ARG, "scale width differs from the first load of this linear");
   }
   // row-major staging copy, then the tiled HBM layout the GEMM streams
   void* staging = nullptr;
@@ -804,10 +810,11 @@ qasr_status upload_linear(qasr_ctx* c, Linear* lin, int n_out, int k, bool int8,
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   cudaFree(staging);
   if (e != cudaSuccess) return cuda_fail(c, e, "weight upload");
-  if (int8) CK(cudaMemcpy(lin->scale, host_s.data(), n_out * 2, cudaMemcpyHostToDevice), "scale upload");
+  if (int8) CK(cudaMemcpy(lin->scale, host_s.data(), host_s.size(), cudaMemcpyHostToDevice), "scale upload");
   lin->n_out = n_out;
   lin->k = k;
   lin->int8 = int8;
+  lin->scale32 = scale32;
   return QASR_OK;
 }
 
@@ -854,8 +861,9 @@ qasr_status qasr_create(const qasr_text_config* cfg, const qasr_options* opts, i
   if (t.hidden_size % 128 || t.intermediate_size % 128 || t.vocab_size % 128 ||
       t.hidden_size < 128 || t.vocab_size <= 0 || t.num_hidden_layers <= 0)
     return bad("hidden, intermediate and vocab sizes must be positive multiples of 128");
-  if (opts->weight_format != QASR_WEIGHTS_F16 && opts->weight_format != QASR_WEIGHTS_INT8)
-    return bad("weight_format must be QASR_WEIGHTS_F16 or QASR_WEIGHTS_INT8");
+  if (opts->weight_format != QASR_WEIGHTS_F16 && opts->weight_format != QASR_WEIGHTS_INT8 &&
+      opts->weight_format != QASR_WEIGHTS_INT8_F32)
+    return bad("weight_format must be QASR_WEIGHTS_F16, QASR_WEIGHTS_INT8 or QASR_WEIGHTS_INT8_F32");
   if (opts->max_slots <= 0 || opts->max_slots > 4096 || opts->max_seq <= 0)
     return bad("max_slots must be 1..4096 and max_seq positive");
   if (c->opts.max_prefill_rows <= 0) c->opts.max_prefill_rows = 2048;
@@ -910,7 +918,7 @@ qasr_status qasr_create(const qasr_text_config* cfg, const qasr_options* opts, i
       return s;
   }
   // GEMM split workspace: worst case over every GEMM shape and row count used.
-  const bool i8 = opts->weight_format == QASR_WEIGHTS_INT8;
+  const bool i8 = opts->weight_format != QASR_WEIGHTS_F16;
   size_t wsf = 0, cnt = 0;
   const int shapes[4][2] = {{qd + 2 * t.num_key_value_heads * 128, hs}, {hs, qd}, {2 * I, hs}, {hs, I}};
   for (int rows = 1; rows <= c->rows_max; rows = rows < 128 ? rows + 1 : rows + 128) {
@@ -940,7 +948,7 @@ qasr_status qasr_create(const qasr_text_config* cfg, const qasr_options* opts, i
   if (c->chain_ok) {
     c->chain_ws_rows = chain_shape(std::min(opts->max_slots, CHAIN_MAX_ROWS)).n_tile;
     for (int i = 0; i < 4; ++i) {  // shapes[] order: QKV, o_proj, gate|up, down
-      const ChainGemm g = chain_gemm_plan(nullptr, nullptr, shapes[i][0], shapes[i][1], 0, c->num_sms,
+      const ChainGemm g = chain_gemm_plan(nullptr, nullptr, false, shapes[i][0], shapes[i][1], 0, c->num_sms,
                                           chain_seg_cap(i));
       if (2ull * static_cast<unsigned long long>(g.units) * static_cast<unsigned long long>(g.grid) >= (1ull << 32))
         return fail(c, QASR_ERR_CAPACITY, "decode chain GEMM: too many units for 32-bit unit maps");
@@ -997,7 +1005,7 @@ qasr_status qasr_load_embed(qasr_ctx* c, const uint16_t* embed, const uint16_t* 
   CK(cudaSetDevice(c->device), "cudaSetDevice");
   drop_graph(c);
   const int V = c->cfg.vocab_size, hs = c->cfg.hidden_size;
-  qasr_status s = upload_linear(c, &c->lm, V, hs, false, {embed}, {V}, {}, {});
+  qasr_status s = upload_linear(c, &c->lm, V, hs, false, false, {embed}, {V}, {}, {});
   if (s) return s;
   if (!c->embed && (s = dalloc(c, &c->embed, static_cast<size_t>(V) * hs, "embed alloc"))) return s;
   CK(cudaMemcpy(c->embed, embed, static_cast<size_t>(V) * hs * 2, cudaMemcpyHostToDevice), "embed upload");
@@ -1012,12 +1020,13 @@ qasr_status qasr_load_layer(qasr_ctx* c, int layer, const qasr_layer_weights* w)
     return fail(c, QASR_ERR_INVALID_ARG, "layer %d out of range", layer);
   CK(cudaSetDevice(c->device), "cudaSetDevice");
   drop_graph(c);
-  const bool i8 = c->opts.weight_format == QASR_WEIGHTS_INT8;
+  const bool i8 = c->opts.weight_format != QASR_WEIGHTS_F16;
+  const bool s32 = c->opts.weight_format == QASR_WEIGHTS_INT8_F32;
   const int hs = c->cfg.hidden_size, I = c->cfg.intermediate_size;
   const int qd = c->cfg.num_attention_heads * c->cfg.head_dim;
   const int kvd = c->cfg.num_key_value_heads * c->cfg.head_dim;
   const void* lin[7] = {w->q_proj, w->k_proj, w->v_proj, w->o_proj, w->gate_proj, w->up_proj, w->down_proj};
-  const uint16_t* sc[7] = {w->q_scale, w->k_scale, w->v_scale, w->o_scale, w->gate_scale, w->up_scale, w->down_scale};
+  const void* sc[7] = {w->q_scale, w->k_scale, w->v_scale, w->o_scale, w->gate_scale, w->up_scale, w->down_scale};
   for (int i = 0; i < 7; ++i) {
     if (!lin[i]) return fail(c, QASR_ERR_INVALID_ARG, "layer %d: missing linear %d", layer, i);
     if (i8 && !sc[i]) return fail(c, QASR_ERR_INVALID_ARG, "layer %d: missing int8 scale %d", layer, i);
@@ -1025,10 +1034,10 @@ qasr_status qasr_load_layer(qasr_ctx* c, int layer, const qasr_layer_weights* w)
   LayerDev& L = c->layers[layer];
   qasr_status s;
   // fused [q|k|v] rows (fused_pieces / fused_i8_pieces, src/decoder.rs:4243-4314)
-  if ((s = upload_linear(c, &L.qkv, qd + 2 * kvd, hs, i8, {lin[0], lin[1], lin[2]}, {qd, kvd, kvd},
+  if ((s = upload_linear(c, &L.qkv, qd + 2 * kvd, hs, i8, s32, {lin[0], lin[1], lin[2]}, {qd, kvd, kvd},
                          {sc[0], sc[1], sc[2]}, {})))
     return s;
-  if ((s = upload_linear(c, &L.o, hs, qd, i8, {lin[3]}, {hs}, {sc[3]}, {}))) return s;
+  if ((s = upload_linear(c, &L.o, hs, qd, i8, s32, {lin[3]}, {hs}, {sc[3]}, {}))) return s;
   // gate|up interleaved in 64-row blocks so one 128-row tile holds gate[j..j+64) and
   // up[j..j+64): the SiLU product is formed in the GEMM epilogue.
   std::vector<int> order(2 * I);
@@ -1036,9 +1045,9 @@ qasr_status qasr_load_layer(qasr_ctx* c, int layer, const qasr_layer_weights* w)
     const int blk = r / 128, within = r % 128;
     order[r] = within < 64 ? blk * 64 + within : I + blk * 64 + (within - 64);
   }
-  if ((s = upload_linear(c, &L.gu, 2 * I, hs, i8, {lin[4], lin[5]}, {I, I}, {sc[4], sc[5]}, order)))
+  if ((s = upload_linear(c, &L.gu, 2 * I, hs, i8, s32, {lin[4], lin[5]}, {I, I}, {sc[4], sc[5]}, order)))
     return s;
-  if ((s = upload_linear(c, &L.down, hs, I, i8, {lin[6]}, {hs}, {sc[6]}, {}))) return s;
+  if ((s = upload_linear(c, &L.down, hs, I, i8, s32, {lin[6]}, {hs}, {sc[6]}, {}))) return s;
   if ((s = upload_f32_vec(c, &L.iln, w->input_layernorm, hs)) ||
       (s = upload_f32_vec(c, &L.pln, w->post_attention_layernorm, hs)) ||
       (s = upload_f32_vec(c, &L.qn, w->q_norm, c->cfg.head_dim)) ||
@@ -1379,14 +1388,14 @@ static qasr_status probe_err(char* err, int errlen, qasr_status s, const std::st
 }
 
 qasr_status qasr_kernel_gemm(int device, void* stream, int weight_format, const void* w,
-                             const uint16_t* scale, int n_out, int k, const uint16_t* x, int ldx,
+                             const void* scale, int n_out, int k, const uint16_t* x, int ldx,
                              int rows, uint16_t* out, int ldo, int accumulate, char* err, int errlen) {
   return qasr_kernel_gemm_traced(device, stream, weight_format, w, scale, n_out, k, x, ldx, rows, out, ldo,
                                  accumulate, nullptr, nullptr, err, errlen);
 }
 
 qasr_status qasr_kernel_gemm_traced(int device, void* stream, int weight_format, const void* w,
-                                    const uint16_t* scale, int n_out, int k, const uint16_t* x, int ldx,
+                                    const void* scale, int n_out, int k, const uint16_t* x, int ldx,
                                     int rows, uint16_t* out, int ldo, int accumulate,
                                     unsigned long long* trace, int* grid_out, char* err, int errlen) {
   static std::mutex mu;
@@ -1394,13 +1403,15 @@ qasr_status qasr_kernel_gemm_traced(int device, void* stream, int weight_format,
   std::lock_guard<std::mutex> lock(mu);
   std::string e;
   if (device < 0 || device >= 16 || !w || !x || !out || rows <= 0 || n_out % 128 || k % 128 ||
-      (weight_format == QASR_WEIGHTS_INT8 && !scale))
+      (weight_format != QASR_WEIGHTS_F16 && weight_format != QASR_WEIGHTS_INT8 &&
+       weight_format != QASR_WEIGHTS_INT8_F32) ||
+      (weight_format != QASR_WEIGHTS_F16 && !scale))
     return probe_err(err, errlen, QASR_ERR_INVALID_ARG, "bad gemm probe arguments");
   if (cudaSetDevice(device) != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, "cudaSetDevice");
   if (init_kernel_attrs(&e) != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, e);
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-  const bool i8 = weight_format == QASR_WEIGHTS_INT8;
+  const bool i8 = weight_format != QASR_WEIGHTS_F16;
   const GemmShape s = gemm_shape(n_out, k, i8, rows, sms);
   ProbeWs& P = pws[device];
   if (s.ws_floats > P.ws_floats) {
@@ -1437,7 +1448,8 @@ qasr_status qasr_kernel_gemm_traced(int device, void* stream, int weight_format,
   a.stages = s.stages;
   a.max_seg = s.max_seg;
   a.w_tiles = static_cast<const uint8_t*>(w);
-  a.scale = reinterpret_cast<const __half*>(scale);
+  a.scale = scale;
+  a.scale32 = weight_format == QASR_WEIGHTS_INT8_F32 ? 1 : 0;
   a.epi = L.epi;
   a.out = reinterpret_cast<__half*>(out);
   a.ldo = ldo;
@@ -1612,7 +1624,7 @@ extern "C" qasr_status qasr_kernel_pack_weights(int device, void* stream, int we
   if (!w_rowmajor || !w_tiled || n_out <= 0 || n_out % 128 || k <= 0 || k % 128)
     return probe_err(err, errlen, QASR_ERR_INVALID_ARG, "bad pack arguments");
   if (cudaSetDevice(device) != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, "cudaSetDevice");
-  const int row_bytes = k * (weight_format == QASR_WEIGHTS_INT8 ? 1 : 2);
+  const int row_bytes = k * (weight_format != QASR_WEIGHTS_F16 ? 1 : 2);
   pack_weight_tiles_kernel<<<1024, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint4*>(w_rowmajor), static_cast<uint4*>(w_tiled), n_out, row_bytes);
   g_launches.fetch_add(1, std::memory_order_relaxed);

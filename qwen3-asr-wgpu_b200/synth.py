@@ -70,6 +70,17 @@ def quantize_rows(w: np.ndarray):
     return q, s
 
 
+def quantize_rows_f32(w: np.ndarray):
+    """Per-row symmetric int8 of an f16-bits matrix with f32 scales, the way an INT8
+    export stores them (`I8 [out, in]` + `F32 [out]` `.weight_scale`):
+    s = max|w_r| / 127 in f32, q = clamp(rne(w / s), -127, 127)."""
+    wf = f16_bits_to_f32(w)
+    amax = np.abs(wf).max(axis=1).astype(np.float32)
+    s = np.where(amax > 0, amax / np.float32(127.0), np.float32(1.0)).astype(np.float32)
+    q = np.clip(np.rint(wf / s[:, None]), -127, 127).astype(np.int8)
+    return q, s
+
+
 def f16_bits_to_f32(a: np.ndarray) -> np.ndarray:
     return np.ascontiguousarray(a, dtype=np.uint16).view(np.float16).astype(np.float32)
 
@@ -139,13 +150,14 @@ class SyntheticModel:
     def _gain(self, n: int, tid: int) -> np.ndarray:
         return np.full(n, np.float16(self.norm_gain).view(np.uint16), dtype=np.uint16)
 
-    def layer(self, l: int, int8: bool = False) -> dict:
-        """HF-named host arrays of layer l: f16 bits, or int8 + f16-bits scales."""
+    def layer(self, l: int, int8: bool = False, scale_f32: bool = False) -> dict:
+        """HF-named host arrays of layer l: f16 bits, or int8 + scales (f16 bits, or
+        float32 with scale_f32)."""
         out = {}
         for name, (kind, shape) in self._shapes().items():
             w = normal_f16(shape, self.seed, l * 32 + kind, 0.0, self.std)
             if int8:
-                q, s = quantize_rows(w)
+                q, s = quantize_rows_f32(w) if scale_f32 else quantize_rows(w)
                 out[name] = q
                 out[name.replace("_proj", "_scale")] = s
             else:

@@ -19,15 +19,16 @@ INT8_TOL = 5e-2
 
 
 def _setup(qasr, oracle, cfg, int8, slots, max_seq=2048, seed=1234):
+    """int8: False (f16 weights), True (int8 + f16 scales) or "f32" (int8 + f32 scales)."""
     from oracle.oracle import OracleModel
     model = qasr.SyntheticModel(cfg, seed=seed)
-    dec = qasr.TextDecoder(cfg, weight_format=qasr.WEIGHTS_INT8 if int8 else qasr.WEIGHTS_F16,
-                           max_slots=slots, max_seq=max_seq, keep_logits=True)
+    fmt = qasr.WEIGHTS_F16 if not int8 else (qasr.WEIGHTS_INT8_F32 if int8 == "f32" else qasr.WEIGHTS_INT8)
+    dec = qasr.TextDecoder(cfg, weight_format=fmt, max_slots=slots, max_seq=max_seq, keep_logits=True)
     om = OracleModel(cfg)
     dec.load_embed(model.embed, model.final_norm)
     om.load_embed(model.embed, model.final_norm)
     for l in range(cfg["num_hidden_layers"]):
-        w = model.layer(l, int8=int8)
+        w = model.layer(l, int8=bool(int8), scale_f32=int8 == "f32")
         dec.load_layer(l, w)
         om.load_layer(l, w)
     cos, sin = qasr.build_rope_tables(max_seq)
@@ -91,7 +92,7 @@ def _check(worst, report, tol):
     assert len(flips) <= max(1, len(report) // 10), f"too many near-tie flips: {flips}"
 
 
-@pytest.mark.parametrize("int8", [False, True], ids=["f16", "int8"])
+@pytest.mark.parametrize("int8", [False, True, "f32"], ids=["f16", "int8", "int8-f32scale"])
 def test_two_layer_decoder_matches_oracle(qasr, cuda_device, oracle, int8):
     cfg = qasr.text_config("0.6b", num_hidden_layers=2)
     _check(*_run_parity(qasr, oracle, cfg, int8, n_audio=[40, 7, 120], steps=12, n_slots=3))

@@ -31,10 +31,11 @@ def _gemm_case(qasr, torch, fmt, n_out, k, rows, seed, accumulate=False):
     from qasr_b200 import synth
     w16 = synth.normal_f16((n_out, k), seed, 1, 0.0, 0.02)
     x16 = synth.normal_f16((rows, k), seed, 2, 0.0, 1.0)
-    if fmt == qasr.WEIGHTS_INT8:
-        q, s = synth.quantize_rows(w16)
+    if fmt in (qasr.WEIGHTS_INT8, qasr.WEIGHTS_INT8_F32):
+        f32s = fmt == qasr.WEIGHTS_INT8_F32
+        q, s = synth.quantize_rows_f32(w16) if f32s else synth.quantize_rows(w16)
         from oracle import oracle
-        wd = oracle.dequant_i8(q, s.view(np.float16).astype(np.float32))
+        wd = oracle.dequant_i8(q, s if f32s else s.view(np.float16).astype(np.float32))
         w_dev = _dev(q, torch)
         s_dev = _dev(s, torch)
     else:
@@ -61,7 +62,7 @@ SHAPES = [
 ]
 
 
-@pytest.mark.parametrize("fmt", [0, 1], ids=["f16", "int8"])
+@pytest.mark.parametrize("fmt", [0, 1, 2], ids=["f16", "int8", "int8-f32scale"])
 @pytest.mark.parametrize("n_out,k,rows", SHAPES)
 def test_gemm_matches_dequantised_reference(qasr, cuda_device, fmt, n_out, k, rows):
     import torch
@@ -101,6 +102,35 @@ def test_int8_dequant_bit_exact(qasr, cuda_device, oracle):
     torch.cuda.synchronize()
     got = out.cpu().numpy().view(np.uint16)
     deq = oracle.dequant_i8(q, s.view(np.float16).astype(np.float32))
+    np.testing.assert_array_equal(got, deq[:, cols].T)
+
+
+def test_int8_f32_scale_dequant_bit_exact(qasr, cuda_device, oracle):
+    """As above with the INT8 export's own f32 scales (QASR_WEIGHTS_INT8_F32): the
+    value is the f32 product rounded to f16, f16(f32(q) * s) (PackedInt8,
+    src/weights.rs:309-356; dequant_i8 :372-385), bit for bit."""
+    import torch
+    from qasr_b200 import synth
+    n_out, k, rows = 512, 256, 64
+    w16 = synth.normal_f16((n_out, k), 98, 1, 0.0, 0.02)
+    q, s = synth.quantize_rows_f32(w16)
+    q[0, :8] = [-127, 127, -1, 1, 0, 64, -64, 100]
+    # scales with full f32 mantissas and products near f16 rounding boundaries
+    s[1] = np.float32(1.0 + 2.0 ** -12 + 2.0 ** -23)
+    s[2] = np.float32(3.0517578e-05)  # products in the f16 subnormal range
+    q[1, :8] = [1, 3, 5, 7, -9, 11, 13, -127]
+    q[2, :8] = [1, -1, 2, 3, 127, -127, 64, 65]
+    cols = (np.arange(rows) * 37) % k
+    x = np.zeros((rows, k), np.float16)
+    x[np.arange(rows), cols] = 1.0
+    out = torch.zeros((rows, n_out), dtype=torch.int16, device="cuda")
+    qd, sd, xd = _dev(q, torch), _dev(s, torch), _dev(x.view(np.uint16), torch)
+    qd = _pack(qasr, torch, qasr.WEIGHTS_INT8_F32, qd, n_out, k)
+    qasr.kernel_gemm(0, 0, qasr.WEIGHTS_INT8_F32, qd.data_ptr(), sd.data_ptr(), n_out, k, xd.data_ptr(), k,
+                     rows, out.data_ptr(), n_out, False)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().view(np.uint16)
+    deq = oracle.dequant_i8(q, s)
     np.testing.assert_array_equal(got, deq[:, cols].T)
 
 

@@ -20,6 +20,21 @@ def test_dequant_matches_python_shim(oracle, qasr):
     np.testing.assert_array_equal(host, want)
 
 
+def test_f32_scale_quantizer_and_dequant(oracle, qasr):
+    """The INT8 export's format (`I8` + F32 `.weight_scale`, src/weights.rs:300-308,
+    309-356): scales carry full f32 mantissas (most are not f16 values), q stays in
+    [-127, 127], and dequant is the f32 product rounded to f16 (src/weights.rs:372-385)."""
+    from qasr_b200 import synth
+    w = synth.normal_f16((64, 256), 5, 1, 0.0, 0.02)
+    q, s = synth.quantize_rows_f32(w)
+    assert q.dtype == np.int8 and s.dtype == np.float32
+    assert q.min() >= -127 and q.max() <= 127 and np.abs(q).max(axis=1).min() == 127
+    assert np.mean(s.astype(np.float16).astype(np.float32) != s) > 0.9
+    got = oracle.dequant_i8(q, s)
+    want = (q.astype(np.float32) * s[:, None]).astype(np.float16).view(np.uint16)
+    np.testing.assert_array_equal(got, want)
+
+
 def test_dequant_extremes(oracle):
     # src/weights.rs:560-569
     q = np.frombuffer(bytes([128, 127, 0, 1]), dtype=np.int8).reshape(1, 4)
