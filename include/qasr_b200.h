@@ -193,6 +193,60 @@ qasr_status qasr_read_trace(qasr_ctx* ctx, uint64_t* out, int cap, int* count);
 #define QASR_ATTN_TRACE_SLOTS 8
 qasr_status qasr_read_attn_trace(qasr_ctx* ctx, uint64_t* out, int cap, int* count);
 
+/* --- checkpoints (src/weights.rs, src/config.rs) -------------------------------- */
+/* The decode path's part of a model directory's config.json (AsrConfig::from_file,
+ * src/config.rs:142-173): `thinker_config.text_config`, or the HF-native top-level
+ * `text_config`; absent fields take the reference's defaults (src/config.rs:102-124,
+ * 137); `rope_parameters.rope_theta` overrides `rope_theta`; rms_norm_eps is narrowed
+ * f64 -> f32 (src/decoder.rs:191).  mrope_section / mrope_interleaved follow
+ * TextDecoderConfig::mrope_section / mrope_interleaved (src/config.rs:175-189). */
+typedef struct {
+  qasr_text_config text;
+  double rope_theta;
+  int32_t mrope_section[4];  /* the first n_mrope_section entries are set */
+  int32_t n_mrope_section;
+  int32_t mrope_interleaved;
+} qasr_model_config;
+qasr_status qasr_read_model_config(const char* model_dir, qasr_model_config* out, char* err, int errlen);
+
+/* An opened checkpoint: every safetensors shard of `model_dir` memory-mapped
+ * (load_tensors, src/weights.rs:150-171: model.safetensors.index.json's shards, else
+ * model.safetensors), HF-native names remapped (src/weights.rs:173-201:
+ * model.language_model.* -> thinker.model.*, model.audio_tower.* ->
+ * thinker.audio_tower.*, model.multi_modal_projector.linear_{1,2}* ->
+ * thinker.audio_tower.proj{1,2}*).  Host-only: needs no GPU. */
+typedef struct qasr_checkpoint qasr_checkpoint;
+qasr_status qasr_checkpoint_open(const char* model_dir, qasr_checkpoint** out, char* err, int errlen);
+void qasr_checkpoint_close(qasr_checkpoint* ck);
+const char* qasr_checkpoint_last_error(const qasr_checkpoint* ck);
+/* Tensors in the checkpoint (after remapping). */
+int64_t qasr_checkpoint_tensor_count(const qasr_checkpoint* ck);
+/* dtype (safetensors name, e.g. "BF16", "I8") and shape of `name`; ndim receives the
+ * rank, at most `cap` dims are written.  QASR_ERR_INVALID_ARG if absent. */
+qasr_status qasr_checkpoint_tensor_info(qasr_checkpoint* ck, const char* name, char* dtype, int dtype_cap,
+                                        int64_t* shape, int cap, int* ndim);
+/* The weight format a context needs for `{prefix}.layers.0.self_attn.q_proj.weight`
+ * (prefix NULL = "thinker.model"): QASR_WEIGHTS_INT8_F32 when it is I8 (the INT8
+ * export, src/weights.rs:300-308), else QASR_WEIGHTS_F16. */
+qasr_status qasr_checkpoint_weight_format(qasr_checkpoint* ck, const char* prefix, int* weight_format);
+/* get_f16 (src/weights.rs:394-417): `name` as f16 (bf16 / f32 narrowed with
+ * round-to-nearest-even, src/weights.rs:55-80; I8 dequantised with its
+ * `<name without .weight>.weight_scale`, f16(f32(q) * s)); `count` = elements. */
+qasr_status qasr_checkpoint_read_f16(qasr_checkpoint* ck, const char* name, uint16_t* out, int64_t count);
+/* append_f16_row_le (src/weights.rs:121-146): rows `rows[0..n)` of a 2-D `name` as f16
+ * into out [n][cols] (the token-embedding lookup that builds a prefill's hidden rows). */
+qasr_status qasr_checkpoint_rows_f16(qasr_checkpoint* ck, const char* name, const int32_t* rows, int n,
+                                     uint16_t* out, int64_t count);
+/* WgpuTextDecoder::load's weight intake (src/decoder.rs:1253-1262, 4366-4417;
+ * get_matrix / get_int8 src/weights.rs:459-489): `{prefix}.embed_tokens.weight`,
+ * `{prefix}.norm.weight` and every layer's norms and linears into `ctx` (prefix NULL
+ * = "thinker.model").  A QASR_WEIGHTS_F16 context takes float linears narrowed to f16
+ * and I8 linears dequantised; a QASR_WEIGHTS_INT8_F32 context takes I8 + F32
+ * `.weight_scale` verbatim (PackedInt8 src/weights.rs:309-356: cols % 4 == 0, scale F32
+ * [rows]); a QASR_WEIGHTS_INT8 context takes I8 whose scales are all f16 values.
+ * Shapes are checked against the context's config. */
+qasr_status qasr_load_checkpoint(qasr_ctx* ctx, qasr_checkpoint* ck, const char* prefix);
+
 /* --- host helpers of the reference's loader ------------------------------------ */
 /* compute_mrope_cos_sin + text_positions (src/mrope.rs:46-80) rounded to f16 the
  * way src/inference.rs:1037-1047 does: angles in f64, cos/sin -> f32 -> f16.

@@ -56,6 +56,10 @@ EXPORTED_SYMBOLS = (
     "qasr_synth_key", "qasr_synth_normal_f16", "qasr_synth_uniform_ids",
     "qasr_synth_quantize_rows", "qasr_f32_to_f16", "qasr_f16_to_f32", "qasr_f32_to_f16_array",
     "qasr_f16_to_f32_array",
+    "qasr_read_model_config", "qasr_checkpoint_open", "qasr_checkpoint_close",
+    "qasr_checkpoint_last_error", "qasr_checkpoint_tensor_count", "qasr_checkpoint_tensor_info",
+    "qasr_checkpoint_weight_format", "qasr_checkpoint_read_f16", "qasr_checkpoint_rows_f16",
+    "qasr_load_checkpoint",
 )
 
 
@@ -84,6 +88,13 @@ class LayerWeights(ctypes.Structure):
         "q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj",
         "q_scale", "k_scale", "v_scale", "o_scale", "gate_scale", "up_scale", "down_scale",
         "input_layernorm", "post_attention_layernorm", "q_norm", "k_norm")]
+
+
+class ModelConfig(ctypes.Structure):
+    """qasr_model_config: the decode path's part of a model directory's config.json."""
+    _fields_ = [("text", TextConfig), ("rope_theta", ctypes.c_double),
+                ("mrope_section", ctypes.c_int32 * 4), ("n_mrope_section", ctypes.c_int32),
+                ("mrope_interleaved", ctypes.c_int32)]
 
 
 def _load() -> ctypes.CDLL:
@@ -148,6 +159,21 @@ def _load() -> ctypes.CDLL:
     lib.qasr_f32_to_f16_array.restype = None
     lib.qasr_f16_to_f32_array.argtypes = [P, P, ctypes.c_size_t]
     lib.qasr_f16_to_f32_array.restype = None
+    C = ctypes.c_char_p
+    I64 = ctypes.c_int64
+    lib.qasr_read_model_config.argtypes = [C, ctypes.POINTER(ModelConfig), C, I]
+    lib.qasr_checkpoint_open.argtypes = [C, ctypes.POINTER(P), C, I]
+    lib.qasr_checkpoint_close.argtypes = [P]
+    lib.qasr_checkpoint_close.restype = None
+    lib.qasr_checkpoint_last_error.argtypes = [P]
+    lib.qasr_checkpoint_last_error.restype = ctypes.c_char_p
+    lib.qasr_checkpoint_tensor_count.argtypes = [P]
+    lib.qasr_checkpoint_tensor_count.restype = I64
+    lib.qasr_checkpoint_tensor_info.argtypes = [P, C, C, I, P, I, ctypes.POINTER(I)]
+    lib.qasr_checkpoint_weight_format.argtypes = [P, C, ctypes.POINTER(I)]
+    lib.qasr_checkpoint_read_f16.argtypes = [P, C, P, I64]
+    lib.qasr_checkpoint_rows_f16.argtypes = [P, C, P, I, P, I64]
+    lib.qasr_load_checkpoint.argtypes = [P, P, C]
     return lib
 
 
@@ -246,6 +272,10 @@ class TextDecoder:
                 keep.append(a)
                 setattr(lw, name, a.ctypes.data)
         self._check(lib.qasr_load_layer(self._ctx, layer, ctypes.byref(lw)))
+
+    def load_checkpoint(self, ck: "Checkpoint", prefix: str | None = None):
+        """Every decoder weight of an opened checkpoint (qasr_load_checkpoint)."""
+        self._check(lib.qasr_load_checkpoint(self._ctx, ck._h, prefix.encode() if prefix else None))
 
     def load_model(self, model: "SyntheticModel"):
         self.load_embed(model.embed, model.final_norm)
@@ -346,6 +376,87 @@ class TextDecoder:
     def read_logits(self, rows: int) -> np.ndarray:
         out = np.zeros((rows, self.cfg["vocab_size"]), dtype=np.float32)
         self._check(lib.qasr_read_logits(self._ctx, _ptr(out), rows))
+        return out
+
+
+def read_model_config(model_dir: str) -> dict:
+    """qasr_read_model_config: text config (a dict qasr.TextDecoder takes), rope_theta,
+    mrope_section, mrope_interleaved."""
+    mc = ModelConfig()
+    err = ctypes.create_string_buffer(512)
+    st = lib.qasr_read_model_config(str(model_dir).encode(), ctypes.byref(mc), err, 512)
+    if st != QASR_OK:
+        raise DecoderError(st, err.value.decode())
+    t = mc.text
+    cfg = {f: getattr(t, f) for f, _ in TextConfig._fields_}
+    return {"text_config": cfg, "rope_theta": mc.rope_theta,
+            "mrope_section": [mc.mrope_section[k] for k in range(mc.n_mrope_section)],
+            "mrope_interleaved": bool(mc.mrope_interleaved)}
+
+
+class Checkpoint:
+    """A model directory's safetensors shards, memory-mapped (qasr_checkpoint_*)."""
+
+    def __init__(self, model_dir: str):
+        h = ctypes.c_void_p()
+        err = ctypes.create_string_buffer(512)
+        st = lib.qasr_checkpoint_open(str(model_dir).encode(), ctypes.byref(h), err, 512)
+        if st != QASR_OK:
+            raise DecoderError(st, err.value.decode())
+        self._h = h
+
+    def close(self):
+        if self._h:
+            lib.qasr_checkpoint_close(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, st: int):
+        if st != QASR_OK:
+            raise DecoderError(st, lib.qasr_checkpoint_last_error(self._h).decode())
+
+    def __len__(self) -> int:
+        return int(lib.qasr_checkpoint_tensor_count(self._h))
+
+    def info(self, name: str):
+        """(dtype, shape) of a tensor."""
+        dt = ctypes.create_string_buffer(16)
+        shape = np.zeros(8, np.int64)
+        nd = ctypes.c_int(0)
+        self._check(lib.qasr_checkpoint_tensor_info(self._h, name.encode(), dt, 16, _ptr(shape), 8,
+                                                    ctypes.byref(nd)))
+        return dt.value.decode(), tuple(int(x) for x in shape[:nd.value])
+
+    def weight_format(self, prefix: str | None = None) -> int:
+        f = ctypes.c_int(0)
+        self._check(lib.qasr_checkpoint_weight_format(self._h, prefix.encode() if prefix else None,
+                                                      ctypes.byref(f)))
+        return f.value
+
+    def read_f16(self, name: str) -> np.ndarray:
+        """get_f16: f16 bits (uint16) in the tensor's shape."""
+        _, shape = self.info(name)
+        out = np.zeros(shape, np.uint16)
+        self._check(lib.qasr_checkpoint_read_f16(self._h, name.encode(), _ptr(out), out.size))
+        return out
+
+    def rows_f16(self, name: str, rows) -> np.ndarray:
+        """append_f16_row_le for each row id: f16 bits [n, cols]."""
+        _, shape = self.info(name)
+        ids = np.ascontiguousarray(rows, dtype=np.int32)
+        out = np.zeros((ids.size, shape[1]), np.uint16)
+        self._check(lib.qasr_checkpoint_rows_f16(self._h, name.encode(), _ptr(ids), ids.size, _ptr(out), out.size))
         return out
 
 
@@ -455,6 +566,7 @@ __all__ = [
     "TextDecoder", "DecoderError", "SyntheticModel", "MODEL_PRESETS", "text_config",
     "build_rope_tables", "dim_map", "kernel_pack_weights", "kernel_gemm", "kernel_attention_noalloc", "kernel_attention", "kernel_kv_append",
     "launch_count", "version", "WEIGHTS_F16", "WEIGHTS_INT8", "WEIGHTS_INT8_F32", "EXPORTED_SYMBOLS", "lib",
+    "Checkpoint", "read_model_config", "ModelConfig",
     "f16_bits_to_f32", "f32_to_f16_bits", "PAGE_POSITIONS", "kv_page_swizzle", "FLAG_TRACE",
     "TRACE_SLOTS",
 ]

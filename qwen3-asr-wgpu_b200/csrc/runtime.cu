@@ -25,6 +25,7 @@
 #include "f16_host.h"
 #include "gemm_tc.cuh"
 #include "qasr_b200.h"
+#include "ctx_internal.h"
 #include "qasr_b200_kernels.h"
 #include "rows.cuh"
 
@@ -831,6 +832,19 @@ qasr_status upload_f32_vec(qasr_ctx* c, float** dst, const uint16_t* src, int n)
 }
 
 }  // namespace
+
+namespace qasr {
+bool ctx_shape(const qasr_ctx* c, qasr_text_config* cfg, int* weight_format) {
+  if (!c) return false;
+  if (cfg) *cfg = c->cfg;
+  if (weight_format) *weight_format = c->opts.weight_format;
+  return true;
+}
+qasr_status ctx_fail(qasr_ctx* c, qasr_status s, const std::string& msg) {
+  if (c) c->err = msg;
+  return s;
+}
+}  // namespace qasr
 
 // ============================================================================ C ABI
 extern "C" {
