@@ -98,6 +98,64 @@ def test_two_layer_decoder_matches_oracle(qasr, cuda_device, oracle, int8):
     _check(*_run_parity(qasr, oracle, cfg, int8, n_audio=[40, 7, 120], steps=12, n_slots=3))
 
 
+@pytest.mark.parametrize("int8", [False, True], ids=["f16", "int8"])
+def test_prefix_reuse_prefill_matches_oracle(qasr, cuda_device, oracle, int8):
+    """Streaming rounds (src/stream.rs:366-395): prefill with kv_start > 0 keeps KV
+    positions [0, kv_start) and writes the new rows from kv_start (CpuTextDecoder::prefill
+    src/cpu_decoder.rs:487-515; prefill_impl q_off src/decoder.rs:4489-4499, 4664-4714).
+    Two slots: prefill, decode, then a second prefill that reuses part of the cache
+    (slot 0 rolls back 10 positions, slot 1 continues at its position), then decode;
+    teacher-forced against the oracle doing the same."""
+    from oracle.oracle import OracleSeq
+    cfg = qasr.text_config("0.6b", num_hidden_layers=2)
+    tol = INT8_TOL if int8 else F16_TOL
+    model, dec, om = _setup(qasr, oracle, cfg, int8, 2)
+    seqs = [OracleSeq(om, 2048) for _ in range(2)]
+    slots = [dec.fork_capped(256) for _ in range(2)]
+    worst = 0.0
+    flips = []
+
+    def compare(g_tok, g_lg, o):
+        nonlocal worst
+        for i in range(2):
+            worst = max(worst, float(np.max(np.abs(g_lg[i] - o[i][1]))))
+            if int(g_tok[i]) != o[i][0]:
+                flips.append((i, int(g_tok[i]), o[i][0], float(o[i][1][o[i][0]] - o[i][1][int(g_tok[i])])))
+
+    last = [0, 0]  # the oracle's latest token: both sides embed it next (teacher forcing)
+
+    def decode(n):
+        for _ in range(n):
+            dec.set_input_tokens(slots, last)
+            g = dec.step_batch(slots)
+            lg = dec.read_logits(2)
+            o = [s.step(want_logits=True) for s in seqs]
+            compare(g, lg, o)
+            last[:] = [t for t, _ in o]
+
+    pre = [model.prefix(s, 30 + 17 * s)[0] for s in range(2)]
+    g = dec.prefill_batch(slots, pre)
+    o = [seqs[i].prefill(pre[i], want_logits=True) for i in range(2)]
+    compare(g, dec.read_logits(2), o)
+    last[:] = [t for t, _ in o]
+    decode(5)
+    pos = [dec.pos(s) for s in slots]
+    assert pos == [p.shape[0] + 5 for p in pre]
+    new = [model.prefix(100 + s, 7 + 6 * s, n_text=13, n_before=4)[0] for s in range(2)]
+    starts = [pos[0] - 10, pos[1]]
+    g = dec.prefill_batch(slots, new, kv_starts=starts)
+    o = [seqs[i].prefill(new[i], kv_start=starts[i], want_logits=True) for i in range(2)]
+    compare(g, dec.read_logits(2), o)
+    assert [dec.pos(s) for s in slots] == [starts[i] + new[i].shape[0] for i in range(2)]
+    last[:] = [t for t, _ in o]
+    decode(5)
+    dec.close()
+    om.close()
+    print(f"prefix reuse: max |dlogit| {worst:.3g}; flips {flips}")
+    assert worst <= tol
+    assert not [f for f in flips if f[3] > 2.0 * worst], flips
+
+
 @pytest.mark.parametrize("int8", [False, True], ids=["f16", "int8-chain"])
 def test_batched_equals_serial(qasr, cuda_device, oracle, int8):
     """BatchProjections::step vs one slot at a time: identical ids
