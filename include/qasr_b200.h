@@ -40,7 +40,9 @@ typedef enum {
   QASR_ERR_DEVICE = 4,         /* CUDA runtime/driver error                          */
   QASR_ERR_DEVICE_TIMEOUT = 5, /* a bounded device-side wait gave up                 */
   QASR_ERR_CANCELLED = 6,      /* the caller asked to stop (BatchEvents::should_stop) */
-  QASR_ERR_STATE = 7           /* call order violated (e.g. step before load)        */
+  QASR_ERR_STATE = 7,          /* call order violated (e.g. step before load)        */
+  QASR_ERR_NOT_DECODED = 8     /* a batch ended without a result for the item
+                                  (Outcomes::finish / not_decoded, src/inference.rs:894-915) */
 } qasr_status;
 
 /* Weight storage formats of the decoder linears. */
@@ -246,6 +248,70 @@ qasr_status qasr_checkpoint_rows_f16(qasr_checkpoint* ck, const char* name, cons
  * [rows]); a QASR_WEIGHTS_INT8 context takes I8 whose scales are all f16 values.
  * Shapes are checked against the context's config. */
 qasr_status qasr_load_checkpoint(qasr_ctx* ctx, qasr_checkpoint* ck, const char* prefix);
+
+/* --- many segments through a few slots (decode_batch_embeds / run_batch_attempt,
+ *     src/inference.rs:1944-2227; fill_slots :699-756; BatchEvents :823-836) -------- */
+enum { QASR_STOP_EOS = 0, QASR_STOP_MAX_TOKENS = 1 }; /* StopReason, src/prompt.rs:6-12 */
+#define QASR_ENDOFTEXT_TOKEN_ID 151643 /* src/prompt.rs:25 */
+#define QASR_IM_END_TOKEN_ID 151645    /* src/prompt.rs:24 */
+
+/* One segment: its prompt rows (f16 [len][hidden], e.g. built with
+ * qasr_checkpoint_rows_f16 around the audio rows) and its max_new_tokens. */
+typedef struct {
+  const uint16_t* hidden;
+  int32_t len;
+  int32_t max_new_tokens;
+} qasr_segment;
+/* A segment's outcome.  tokens (caller-allocated, max_new_tokens entries) receives the
+ * generated ids; status is QASR_OK or the error that belongs to this segment alone. */
+typedef struct {
+  int32_t status;
+  int32_t stop_reason; /* QASR_STOP_* (status QASR_OK) */
+  int32_t n_tokens;
+  int32_t* tokens;
+} qasr_item_result;
+/* BatchEvents: on_item once per segment in completion order (longest prompt first, so
+ * not input order); should_stop polled between decode steps (true: unfinished
+ * segments end QASR_ERR_CANCELLED).  Either may be NULL. */
+typedef struct {
+  void* user;
+  void (*on_item)(void* user, int index, const qasr_item_result* result);
+  int (*should_stop)(void* user);
+} qasr_batch_events;
+typedef struct {
+  int32_t width;         /* slots per attempt (--batch); halved after a failed attempt */
+  int32_t eos[2];        /* {QASR_ENDOFTEXT_TOKEN_ID, QASR_IM_END_TOKEN_ID} */
+  int32_t kv_step;       /* KV capacity granule (KV_STEP = 256, src/decoder.rs:725) */
+  int32_t batch_seq_cap; /* segments needing more positions take the single-sequence
+                            path (BATCH_SEQ_CAP = 4096, src/decoder.rs:684) */
+} qasr_batch_options;
+/* The decoder operations the scheduler drives (a qasr_ctx supplies them; tests supply
+ * fakes).  step_batch embeds each slot's previous argmax (on-device feedback); every
+ * function returns a qasr_status. */
+typedef struct {
+  void* user;
+  int32_t hidden_size;
+  int (*fork_capped)(void* user, int cap, int* slot);
+  int (*slot_free)(void* user, int slot);
+  int (*prefill_batch)(void* user, const int* slots, int n, const uint16_t* hidden, const int* lens,
+                       int32_t* first_tokens);
+  int (*step_batch)(void* user, const int* slots, int n, int32_t* out_tokens);
+} qasr_decode_backend;
+/* Decode every segment the way decode_batch_embeds does: segments whose
+ * round_up(len + max_new + 8, kv_step) exceeds batch_seq_cap first, one at a time on
+ * the single-sequence path (generate_from_embeds, src/inference.rs:2229-2376); the rest
+ * in attempts of `width` slots — longest prompt first, free slots refilled from the
+ * frontier in one batched prefill, a slot finishing at an eos id or when max_new_tokens
+ * are generated — and, when an attempt fails, again at half the width for the segments
+ * not yet finished (width < 2: the single-sequence path).  As in the reference, a
+ * batched segment whose first token is an eos id ends without a result
+ * (QASR_ERR_NOT_DECODED).  Returns QASR_OK once every segment has its result, or an
+ * argument error. */
+qasr_status qasr_batch_decode(qasr_ctx* ctx, const qasr_segment* segs, int n, const qasr_batch_options* opts,
+                              const qasr_batch_events* events, qasr_item_result* results);
+qasr_status qasr_batch_decode_backend(const qasr_decode_backend* backend, const qasr_segment* segs, int n,
+                                      const qasr_batch_options* opts, const qasr_batch_events* events,
+                                      qasr_item_result* results);
 
 /* --- host helpers of the reference's loader ------------------------------------ */
 /* compute_mrope_cos_sin + text_positions (src/mrope.rs:46-80) rounded to f16 the

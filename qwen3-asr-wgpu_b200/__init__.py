@@ -29,7 +29,10 @@ QASR_OK = 0
 STATUS_NAMES = {
     0: "QASR_OK", 1: "QASR_ERR_INVALID_ARG", 2: "QASR_ERR_OOM", 3: "QASR_ERR_CAPACITY",
     4: "QASR_ERR_DEVICE", 5: "QASR_ERR_DEVICE_TIMEOUT", 6: "QASR_ERR_CANCELLED", 7: "QASR_ERR_STATE",
+    8: "QASR_ERR_NOT_DECODED",
 }
+STOP_EOS, STOP_MAX_TOKENS = 0, 1
+ENDOFTEXT_TOKEN_ID, IM_END_TOKEN_ID = 151643, 151645
 WEIGHTS_F16 = 0
 WEIGHTS_INT8 = 1
 WEIGHTS_INT8_F32 = 2  # int8 + f32 per-row scales (the INT8 export's own `.weight_scale`)
@@ -59,7 +62,7 @@ EXPORTED_SYMBOLS = (
     "qasr_read_model_config", "qasr_checkpoint_open", "qasr_checkpoint_close",
     "qasr_checkpoint_last_error", "qasr_checkpoint_tensor_count", "qasr_checkpoint_tensor_info",
     "qasr_checkpoint_weight_format", "qasr_checkpoint_read_f16", "qasr_checkpoint_rows_f16",
-    "qasr_load_checkpoint",
+    "qasr_load_checkpoint", "qasr_batch_decode", "qasr_batch_decode_backend",
 )
 
 
@@ -95,6 +98,42 @@ class ModelConfig(ctypes.Structure):
     _fields_ = [("text", TextConfig), ("rope_theta", ctypes.c_double),
                 ("mrope_section", ctypes.c_int32 * 4), ("n_mrope_section", ctypes.c_int32),
                 ("mrope_interleaved", ctypes.c_int32)]
+
+
+class Segment(ctypes.Structure):
+    _fields_ = [("hidden", ctypes.c_void_p), ("len", ctypes.c_int32), ("max_new_tokens", ctypes.c_int32)]
+
+
+class ItemResult(ctypes.Structure):
+    _fields_ = [("status", ctypes.c_int32), ("stop_reason", ctypes.c_int32), ("n_tokens", ctypes.c_int32),
+                ("tokens", ctypes.POINTER(ctypes.c_int32))]
+
+
+ON_ITEM = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ItemResult))
+SHOULD_STOP = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p)
+
+
+class BatchEvents(ctypes.Structure):
+    _fields_ = [("user", ctypes.c_void_p), ("on_item", ON_ITEM), ("should_stop", SHOULD_STOP)]
+
+
+class BatchOptions(ctypes.Structure):
+    _fields_ = [("width", ctypes.c_int32), ("eos", ctypes.c_int32 * 2), ("kv_step", ctypes.c_int32),
+                ("batch_seq_cap", ctypes.c_int32)]
+
+
+BE_FORK = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_int))
+BE_FREE = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_int)
+BE_PREFILL = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int), ctypes.c_int,
+                              ctypes.POINTER(ctypes.c_uint16), ctypes.POINTER(ctypes.c_int),
+                              ctypes.POINTER(ctypes.c_int32))
+BE_STEP = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int), ctypes.c_int,
+                           ctypes.POINTER(ctypes.c_int32))
+
+
+class DecodeBackend(ctypes.Structure):
+    _fields_ = [("user", ctypes.c_void_p), ("hidden_size", ctypes.c_int32), ("fork_capped", BE_FORK),
+                ("slot_free", BE_FREE), ("prefill_batch", BE_PREFILL), ("step_batch", BE_STEP)]
 
 
 def _load() -> ctypes.CDLL:
@@ -174,6 +213,11 @@ def _load() -> ctypes.CDLL:
     lib.qasr_checkpoint_read_f16.argtypes = [P, C, P, I64]
     lib.qasr_checkpoint_rows_f16.argtypes = [P, C, P, I, P, I64]
     lib.qasr_load_checkpoint.argtypes = [P, P, C]
+    lib.qasr_batch_decode.argtypes = [P, ctypes.POINTER(Segment), I, ctypes.POINTER(BatchOptions),
+                                      ctypes.POINTER(BatchEvents), ctypes.POINTER(ItemResult)]
+    lib.qasr_batch_decode_backend.argtypes = [ctypes.POINTER(DecodeBackend), ctypes.POINTER(Segment), I,
+                                              ctypes.POINTER(BatchOptions), ctypes.POINTER(BatchEvents),
+                                              ctypes.POINTER(ItemResult)]
     return lib
 
 
@@ -272,6 +316,12 @@ class TextDecoder:
                 keep.append(a)
                 setattr(lw, name, a.ctypes.data)
         self._check(lib.qasr_load_layer(self._ctx, layer, ctypes.byref(lw)))
+
+    def batch_decode(self, segments, *, width: int, eos=(ENDOFTEXT_TOKEN_ID, IM_END_TOKEN_ID),
+                     kv_step: int = 256, batch_seq_cap: int = 4096, on_item=None, should_stop=None):
+        """qasr_batch_decode: [(hidden, max_new_tokens)] -> [{status, stop, tokens}]."""
+        return _batch_call(lib.qasr_batch_decode, self._ctx, segments, width, eos, kv_step, batch_seq_cap,
+                           on_item, should_stop)
 
     def load_checkpoint(self, ck: "Checkpoint", prefix: str | None = None):
         """Every decoder weight of an opened checkpoint (qasr_load_checkpoint)."""
@@ -377,6 +427,82 @@ class TextDecoder:
         out = np.zeros((rows, self.cfg["vocab_size"]), dtype=np.float32)
         self._check(lib.qasr_read_logits(self._ctx, _ptr(out), rows))
         return out
+
+
+def _batch_call(fn, first_arg, segments, width, eos, kv_step, batch_seq_cap, on_item, should_stop):
+    """Shared driver of qasr_batch_decode(_backend): segments = [(hidden f16 bits
+    [len, hidden], max_new_tokens)]; returns per segment {status, stop, tokens} and calls
+    on_item(index, result) in completion order."""
+    n = len(segments)
+    keep = [np.ascontiguousarray(h, dtype=np.uint16) for h, _ in segments]
+    segs = (Segment * max(n, 1))()
+    res = (ItemResult * max(n, 1))()
+    bufs = []
+    for i, (h, m) in enumerate(segments):
+        segs[i].hidden = keep[i].ctypes.data
+        segs[i].len = keep[i].shape[0]
+        segs[i].max_new_tokens = int(m)
+        b = (ctypes.c_int32 * int(m))()
+        bufs.append(b)
+        res[i].tokens = b
+    out = [None] * n
+
+    def convert(r):
+        return {"status": r.status, "stop": r.stop_reason, "tokens": [r.tokens[k] for k in range(r.n_tokens)]}
+
+    def _on(user, idx, rp):
+        out[idx] = convert(rp.contents)
+        if on_item is not None:
+            on_item(idx, out[idx])
+
+    ev = BatchEvents(None, ON_ITEM(_on), SHOULD_STOP(lambda user: 1 if (should_stop and should_stop()) else 0))
+    opts = BatchOptions(width, (ctypes.c_int32 * 2)(*eos), kv_step, batch_seq_cap)
+    st = fn(first_arg, segs, n, ctypes.byref(opts), ctypes.byref(ev), res)
+    if st != QASR_OK:
+        raise DecoderError(st, "batch decode arguments")
+    return [out[i] if out[i] is not None else convert(res[i]) for i in range(n)]
+
+
+def batch_decode_backend(backend, segments, *, width: int, eos=(ENDOFTEXT_TOKEN_ID, IM_END_TOKEN_ID),
+                         kv_step: int = 256, batch_seq_cap: int = 4096, on_item=None, should_stop=None):
+    """qasr_batch_decode_backend over a Python object with hidden_size and
+    fork_capped(cap) -> slot, slot_free(slot), prefill_batch(slots, hiddens) -> firsts,
+    step_batch(slots) -> tokens; raising DecoderError(status, ...) reports a status."""
+    def wrap(f):
+        def g(*a):
+            try:
+                return f(*a) or 0
+            except DecoderError as e:
+                return e.status
+        return g
+
+    def fork(user, cap, slot_p):
+        slot_p[0] = backend.fork_capped(cap)
+
+    def free(user, slot):
+        backend.slot_free(slot)
+
+    def prefill(user, slots_p, n, hidden_p, lens_p, first_p):
+        hs = backend.hidden_size
+        lens = [lens_p[k] for k in range(n)]
+        flat = np.ctypeslib.as_array(hidden_p, shape=(sum(lens) * hs,)).copy()
+        hiddens, off = [], 0
+        for L in lens:
+            hiddens.append(flat[off * hs:(off + L) * hs].reshape(L, hs))
+            off += L
+        firsts = backend.prefill_batch([slots_p[k] for k in range(n)], hiddens)
+        for k in range(n):
+            first_p[k] = int(firsts[k])
+
+    def step(user, slots_p, n, out_p):
+        toks = backend.step_batch([slots_p[k] for k in range(n)])
+        for k in range(n):
+            out_p[k] = int(toks[k])
+
+    be = DecodeBackend(None, backend.hidden_size, BE_FORK(wrap(fork)), BE_FREE(wrap(free)),
+                       BE_PREFILL(wrap(prefill)), BE_STEP(wrap(step)))
+    return _batch_call(lib.qasr_batch_decode_backend, ctypes.byref(be), segments, width, eos, kv_step,
+                       batch_seq_cap, on_item, should_stop)
 
 
 def read_model_config(model_dir: str) -> dict:
@@ -566,7 +692,8 @@ __all__ = [
     "TextDecoder", "DecoderError", "SyntheticModel", "MODEL_PRESETS", "text_config",
     "build_rope_tables", "dim_map", "kernel_pack_weights", "kernel_gemm", "kernel_attention_noalloc", "kernel_attention", "kernel_kv_append",
     "launch_count", "version", "WEIGHTS_F16", "WEIGHTS_INT8", "WEIGHTS_INT8_F32", "EXPORTED_SYMBOLS", "lib",
-    "Checkpoint", "read_model_config", "ModelConfig",
+    "Checkpoint", "read_model_config", "ModelConfig", "batch_decode_backend", "STOP_EOS", "STOP_MAX_TOKENS",
+    "ENDOFTEXT_TOKEN_ID", "IM_END_TOKEN_ID",
     "f16_bits_to_f32", "f32_to_f16_bits", "PAGE_POSITIONS", "kv_page_swizzle", "FLAG_TRACE",
     "TRACE_SLOTS",
 ]

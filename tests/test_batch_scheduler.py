@@ -1,0 +1,194 @@
+"""The batch driver (qasr_batch_decode_backend) on the CPU, over a scripted fake decoder.
+
+Mirrors decode_batch_embeds / run_batch_attempt / fill_slots (src/inference.rs:1944-2227,
+699-756) and the single-sequence loop of generate_from_embeds (:2300-2376): longest
+prompt first, refill from the frontier, eos / max_new_tokens, width halving after a
+failed attempt with finished items kept, should_stop, per-item results, and the
+reference's own quirks (a batched segment whose first token is an eos id is reported
+as not decoded; the batched path reads one token past max_new)."""
+import numpy as np
+import pytest
+
+HS = 4
+EOS = (151643, 151645)
+
+
+class Fake:
+    """Segment i's hidden rows carry i in element [0, 0]; its decoder emits script[i]."""
+
+    def __init__(self, scripts, max_live=64, fail_step_at=None, filler=7):
+        self.scripts, self.max_live, self.fail_step_at, self.filler = scripts, max_live, fail_step_at, filler
+        self.hidden_size = HS
+        self.live = {}        # slot -> [segment, position in script]
+        self.next_slot = 0
+        self.forks, self.admissions, self.steps = [], [], 0
+
+    def fork_capped(self, cap):
+        from qasr_b200 import DecoderError
+        self.forks.append(cap)
+        if len(self.live) >= self.max_live:
+            raise DecoderError(3, "no slot")
+        s = self.next_slot
+        self.next_slot += 1
+        self.live[s] = None
+        return s
+
+    def slot_free(self, slot):
+        self.live.pop(slot, None)
+
+    def tok(self, seg, k):
+        sc = self.scripts[seg]
+        return sc[k] if k < len(sc) else self.filler
+
+    def prefill_batch(self, slots, hiddens):
+        segs = [int(h[0, 0]) for h in hiddens]
+        self.admissions.append(segs)
+        out = []
+        for s, g in zip(slots, segs):
+            self.live[s] = [g, 0]
+            out.append(self.tok(g, 0))
+        return out
+
+    def step_batch(self, slots):
+        from qasr_b200 import DecoderError
+        self.steps += 1
+        if self.fail_step_at is not None and self.steps == self.fail_step_at:
+            raise DecoderError(4, "device lost")
+        out = []
+        for s in slots:
+            st = self.live[s]
+            st[1] += 1
+            out.append(self.tok(st[0], st[1]))
+        return out
+
+
+def segs(lens, max_new):
+    out = []
+    for i, (L, m) in enumerate(zip(lens, max_new)):
+        h = np.zeros((L, HS), np.uint16)
+        h[0, 0] = i
+        out.append((h, m))
+    return out
+
+
+def batched_expect(script, max_new):
+    """run_batch_attempt for one segment: (status, stop, tokens)."""
+    if script[0] in EOS:
+        return 8, 1, []  # QASR_ERR_NOT_DECODED
+    gen, k = [script[0]], 1
+    while True:
+        t = script[k] if k < len(script) else 7
+        if t in EOS:
+            return 0, 0, gen
+        if len(gen) >= max_new:
+            return 0, 1, gen
+        gen.append(t)
+        k += 1
+
+
+def single_expect(script, max_new):
+    """generate_from_embeds' loop."""
+    if script[0] in EOS:
+        return 0, 0, []
+    gen = [script[0]]
+    for k in range(1, max_new):
+        t = script[k] if k < len(script) else 7
+        if t in EOS:
+            return 0, 0, gen
+        gen.append(t)
+    return 0, 1, gen
+
+
+def check(res, want):
+    got = [(r["status"], r["stop"], r["tokens"]) for r in res]
+    assert got == want
+
+
+def test_longest_first_admission_refill_and_completion_order(qasr):
+    scripts = [[10, 11, EOS[0]], [20, 21, 22, 23, 24, 25], [30, EOS[1]], [40, 41, 42, 43], [50, 51, 52, EOS[0]]]
+    lens = [5, 9, 3, 7, 8]
+    max_new = [8, 4, 8, 8, 8]
+    fake = Fake(scripts)
+    order = []
+    res = qasr.batch_decode_backend(fake, segs(lens, max_new), width=2, on_item=lambda i, r: order.append(i))
+    check(res, [batched_expect(s, m) for s, m in zip(scripts, max_new)])
+    # lengths 9, 8 first; every refill goes to the slot that just freed
+    assert fake.admissions[0] == [1, 4]
+    assert sorted(sum(fake.admissions, [])) == [0, 1, 2, 3, 4]
+    assert fake.admissions[1:] == [[3], [0], [2]]
+    # the step that reaches max_new still runs: segment 1 (max_new 4) ends after 4 steps
+    assert res[1]["tokens"] == [20, 21, 22, 23] and res[1]["stop"] == qasr.STOP_MAX_TOKENS
+    assert order[0] == 4 and sorted(order) == [0, 1, 2, 3, 4]
+    # one fork per slot, each with the attempt's largest round_up(len + max_new + 8, 256)
+    assert fake.forks == [256, 256] and not fake.live
+
+
+def test_eos_first_token(qasr):
+    # batched: never reported, so not decoded; single-sequence: an empty transcript
+    scripts = [[EOS[0]], [EOS[1], 5], [60, 61]]
+    res = qasr.batch_decode_backend(Fake(scripts), segs([4, 4, 4], [3, 3, 3]), width=4)
+    check(res, [batched_expect(s, 3) for s in scripts])
+    assert [r["status"] for r in res] == [8, 8, 0]
+    res = qasr.batch_decode_backend(Fake(scripts), segs([4, 4, 4], [3, 3, 3]), width=1)
+    check(res, [single_expect(s, 3) for s in scripts])
+    assert res[0] == {"status": 0, "stop": qasr.STOP_EOS, "tokens": []}
+
+
+def test_eos_as_the_token_past_max_new(qasr):
+    # the batched path reads token max_new and reports Eos; the single path stops first
+    scripts = [[1, 2, 3, EOS[0]]]
+    b = qasr.batch_decode_backend(Fake(scripts), segs([4], [3]), width=2)
+    s = qasr.batch_decode_backend(Fake(scripts), segs([4], [3]), width=1)
+    assert b[0] == {"status": 0, "stop": qasr.STOP_EOS, "tokens": [1, 2, 3]}
+    assert s[0] == {"status": 0, "stop": qasr.STOP_MAX_TOKENS, "tokens": [1, 2, 3]}
+
+
+def test_width_halves_until_the_slots_fit(qasr):
+    scripts = [[i * 10 + k for k in range(6)] for i in range(6)]
+    fake = Fake(scripts, max_live=2)
+    res = qasr.batch_decode_backend(fake, segs([10, 9, 8, 7, 6, 5], [4] * 6), width=8)
+    check(res, [batched_expect(s, 4) for s in scripts])
+    # width 8 -> 3rd fork refused; 4 -> 3rd refused; 2 fits
+    assert len(fake.forks) == 3 + 3 + 2
+
+
+def test_failed_attempt_keeps_finished_items(qasr):
+    scripts = [[1, EOS[0]], [2, 3, 4, 5, 6, 7, 8], [9, 10, 11, 12, 13, 14], [15, EOS[1]]]
+    fake = Fake(scripts, fail_step_at=3)
+    seen = []
+    res = qasr.batch_decode_backend(fake, segs([8, 7, 6, 5], [6] * 4), width=4,
+                                    on_item=lambda i, r: seen.append(i))
+    check(res, [batched_expect(s, 6) for s in scripts])
+    # 0 and 3 finished before the failing step; the rest reran at width 2
+    assert seen[:2] == [0, 3] and sorted(seen) == [0, 1, 2, 3]
+    assert fake.admissions[-1] == [1, 2]
+
+
+def test_should_stop_cancels_the_unfinished(qasr):
+    scripts = [[1, EOS[0]], [2] * 20, [3] * 20]
+    polls = {"n": 0}
+
+    def stop():
+        polls["n"] += 1
+        return polls["n"] > 4
+
+    res = qasr.batch_decode_backend(Fake(scripts), segs([3, 9, 8], [10] * 3), width=3, should_stop=stop)
+    assert res[0]["status"] == 0 and res[0]["stop"] == qasr.STOP_EOS
+    assert [r["status"] for r in res[1:]] == [6, 6]  # QASR_ERR_CANCELLED
+
+
+def test_long_segments_take_the_single_path_first(qasr):
+    scripts = [[1, 2, 3], [4, 5, 6], [7, 8, 9]]
+    fake = Fake(scripts)
+    order = []
+    res = qasr.batch_decode_backend(fake, segs([100, 300, 50], [3] * 3), width=4, batch_seq_cap=256,
+                                    on_item=lambda i, r: order.append(i))
+    assert order[0] == 1 and fake.admissions[0] == [1]      # alone, before the batch
+    assert fake.forks[0] == 512                            # round_up(300 + 3 + 8, 256)
+    check([res[1]], [single_expect(scripts[1], 3)])
+    check([res[0], res[2]], [batched_expect(scripts[0], 3), batched_expect(scripts[2], 3)])
+
+
+def test_arguments_are_checked(qasr):
+    with pytest.raises(qasr.DecoderError):
+        qasr.batch_decode_backend(Fake([[1]]), segs([3], [0]), width=2)
