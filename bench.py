@@ -165,8 +165,8 @@ def time_kernels(pkg, torch, dec, cfg, slots, stream, kv_lens):
     """CUDA-event timing of the two dominant kernels at the bench's shapes, through the
     probe entry points: paged attention over the slots' current KV and the INT8
     gate|up GEMM (the largest weight stream)."""
-    from qasr_b200 import synth
     res = {}
+    dev = torch.cuda.current_device()  # this rank's GPU (the probes take an explicit device)
     hs, I = cfg["hidden_size"], cfg["intermediate_size"]
     # ---- gate|up GEMM, 32 rows, int8 [2I, hs]
     w = torch.randint(-127, 128, (2 * I, hs), dtype=torch.int8, device="cuda")
@@ -174,10 +174,10 @@ def time_kernels(pkg, torch, dec, cfg, slots, stream, kv_lens):
     x = torch.randn((len(slots), hs), dtype=torch.float16, device="cuda")
     o = torch.empty((len(slots), 2 * I), dtype=torch.float16, device="cuda")
     wt = torch.empty_like(w)
-    pkg.kernel_pack_weights(0, stream.cuda_stream, pkg.WEIGHTS_INT8, w.data_ptr(), 2 * I, hs, wt.data_ptr())
+    pkg.kernel_pack_weights(dev, stream.cuda_stream, pkg.WEIGHTS_INT8, w.data_ptr(), 2 * I, hs, wt.data_ptr())
     w = wt
     def gemm():
-        pkg.kernel_gemm(0, stream.cuda_stream, pkg.WEIGHTS_INT8, w.data_ptr(), s.data_ptr(), 2 * I, hs,
+        pkg.kernel_gemm(dev, stream.cuda_stream, pkg.WEIGHTS_INT8, w.data_ptr(), s.data_ptr(), 2 * I, hs,
                         x.data_ptr(), hs, len(slots), o.data_ptr(), 2 * I)
     # ---- attention: one layer of the 1.7B shape over the slots' lengths
     nkv = cfg["num_key_value_heads"]
@@ -190,7 +190,7 @@ def time_kernels(pkg, torch, dec, cfg, slots, stream, kv_lens):
     rs = torch.arange(len(lens), dtype=torch.int32, device="cuda")
     rp = torch.tensor([n - 1 for n in lens], dtype=torch.int32, device="cuda")
     def attn():
-        pkg.kernel_attention(0, stream.cuda_stream, q.data_ptr(), 2 * nkv * 128, ao.data_ptr(), pool.data_ptr(),
+        pkg.kernel_attention(dev, stream.cuda_stream, q.data_ptr(), 2 * nkv * 128, ao.data_ptr(), pool.data_ptr(),
                              pt.data_ptr(), max_pages, 1, nkv, 0, rs.data_ptr(), rp.data_ptr(), len(lens))
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
     for name, fn, nbytes in (("gemm_gate_up_int8", gemm, 2 * I * hs + 2 * I * 2 + len(slots) * hs * 2 * 3),
@@ -251,16 +251,27 @@ def main():
         run_reference(args, rank, world)
         return
 
+    if world > 1:
+        # torchrun starts every rank with OMP_NUM_THREADS=1; the host-side work (synthetic
+        # weights, quantisation) gets this rank's share of the cores instead
+        share = max(1, (os.cpu_count() or 1) // int(os.environ.get("LOCAL_WORLD_SIZE", world)))
+        os.environ["OMP_NUM_THREADS"] = str(share)
     import torch
     torch.cuda.set_device(local)
     dist = None
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
 
     pkg = load_pkg()
+    if world > 1:
+        try:  # the library's OpenMP runtime, should torch have initialised it with one thread
+            import ctypes
+            ctypes.CDLL("libgomp.so.1").omp_set_num_threads(int(os.environ["OMP_NUM_THREADS"]))
+        except OSError:
+            pass
     cfg = pkg.text_config("1.7b")
     model = pkg.SyntheticModel(cfg, seed=SEED)
     rng = np.random.default_rng(SEED + 7919 * rank)
