@@ -182,6 +182,7 @@ qasr_status qasr_read_logits(qasr_ctx* ctx, float* out, int rows);
  * passed (i < 12), 25 + g = GEMM g's input seen ready, 29 + g = its first MMA issued,
  * 33 + g = its last MMA issued, 37 / 38 / 39 = barriers initialised / set-up done /
  * producer ready, 64 / 65 = the first unit's weights seen / A slot free by the builders,
+ * 66 = the epilogue's wait for the previous launch returned,
  * 72 + j = unit j's A operand published, 40 + j / 104 + j = the CTA's j-th unit of the launch
  * seen complete (A built, X landed) / its MMAs issued (j < 24),
  * QASR_TRACE_SLOTS - 1 = exit; 0 where nothing happened.

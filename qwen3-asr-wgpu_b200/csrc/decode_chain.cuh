@@ -120,7 +120,8 @@ struct ChainArgs {
                               // 25 + g GEMM g's input seen ready, 29 + g its first MMA issued,
                               // 33 + g its last MMA issued, 37 / 38 / 39 barriers initialised /
                               // set-up done / producer ready, 64 / 65 the first unit's W seen /
-                              // A slot free (builder warp 4), 72 + j unit j's A published,
+                              // A slot free (builder warp 4), 66 the epilogue's wait for the
+                              // previous launch returned, 72 + j unit j's A published,
                               // 40 + j / 104 + j the CTA's j-th
                               // unit of the launch seen complete / its MMAs issued (j < 24),
                               // 127 exit
@@ -219,6 +220,7 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_flag;
   __shared__ int xready;  // GEMMs whose X input is complete (written by the epilogue leader)
+  __shared__ int prev_done;  // the previous launch is complete (epilogue leader, after its wait)
   __shared__ int seg_ok, bar_ok;
   __shared__ float red[CHAIN_EPI_WARPS];
 
@@ -255,6 +257,7 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
     mbar_init(&done_bar, NACC);
     abort_flag = 0;
     xready = (a.n_ops > 0 && a.ops[0].kind == CH_GEMM) ? 1 : 0;
+    prev_done = 0;
     fence_mbar_init();
     if (a.trace != nullptr) a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 37] = globaltimer();
   }
@@ -271,7 +274,11 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_sh;
-  griddep_wait();
+  // Programmatic dependent launch: the previous launch (the attention merge) may still be
+  // running.  Weights, scales, shared memory and TMEM never depend on it, so the producer,
+  // the A builders and the MMA issuers start at once; the epilogue / row-operation warps
+  // wait (in their own branch), then open the first GEMM's X copies (prev_done); every
+  // later X gate follows a grid barrier they pass after that.
   if (threadIdx.x == 0 && a.trace != nullptr) a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 38] = globaltimer();
 
   if (warp == 0) {
@@ -317,7 +324,8 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
           prog = true;
         }
         if (xu < xue) {
-          if (!xgate && ld_acquire_cta_shared(&xready) > xg) {
+          // the first GEMM's X is the previous launch's output: also wait for its completion
+          if (!xgate && ld_acquire_cta_shared(&xready) > xg && (xg > 0 || ld_acquire_cta_shared(&prev_done) != 0)) {
             fence_proxy_async_global();  // X was written by other CTAs with ordinary stores
             xgate = true;
             if (a.trace != nullptr) a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 25 + xg] = globaltimer();
@@ -537,6 +545,11 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
     const size_t slot_floats = static_cast<size_t>(a.ws_rows) * 128;
     int seg = -1, nbar = 0, gi = 0;
     bool ok = true;
+    griddep_wait();
+    if (e == 0) {
+      st_release_cta_shared(&prev_done, 1);  // opens the first GEMM's X copies
+      if (a.trace != nullptr) a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 66] = globaltimer();
+    }
     for (int oi = 0; oi < a.n_ops && ok; ++oi) {
       const ChainOp& op = a.ops[oi];
       if (op.kind == CH_GEMM) {

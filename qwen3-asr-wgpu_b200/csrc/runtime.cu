@@ -348,6 +348,7 @@ struct qasr_ctx {
   unsigned long long* attn_trace = nullptr;  // QASR_FLAG_TRACE: [L][sms][ATTN_TRACE_SLOTS]
   // decode chain (int8 weights, <= CHAIN_MAX_ROWS rows): partial sums and barrier counters
   bool chain_ok = false;
+  bool chain_pdl = false;  // per-layer chain launches start while the attention drains (PDL)
   float* chain_ws[4] = {};  // partial sums of the chain's QKV, o_proj, gate|up, down GEMMs
   int chain_ws_rows = 0;
   unsigned int* chain_bar = nullptr;
@@ -475,16 +476,20 @@ qasr_status run_gemm(qasr_ctx* c, const GemmLaunch& L) {
   return QASR_OK;
 }
 
-// attention_kernel and, behind it, attention_merge_kernel (rows cut into several chunks)
-cudaError_t launch_attention_pair(const AttnArgs& a, int sms, cudaStream_t st, bool pdl) {
+// attention_kernel and, behind it, attention_merge_kernel (rows cut into several chunks).
+// merge_pdl: the merge launch may start while the attention drains (its CTAs then hold
+// SMs until the attention completes); without, it starts once the attention is done,
+// which leaves every SM the attention frees to a PDL-launched successor.
+cudaError_t launch_attention_pair(const AttnArgs& a, int sms, cudaStream_t st, bool pdl, bool merge_pdl = true) {
   cudaError_t e = launch_k(attention_kernel, dim3(sms), dim3(ATTN_THREADS), attn_smem_bytes(a.rows), st, pdl, a);
   if (e != cudaSuccess) return e;
-  return launch_k(attention_merge_kernel, dim3(a.rows * a.kv.nkv), dim3(256), 0, st, pdl, a);
+  return launch_k(attention_merge_kernel, dim3(a.rows * a.kv.nkv), dim3(256), 0, st, pdl && merge_pdl, a);
 }
 
 // `early` > 0 only where the previous launch appended exactly that many positions per
 // row and wrote q, and everything else the attention reads predates it.
-qasr_status launch_attention(qasr_ctx* c, int layer, int rows, const int* rs, const int* rp, int early = 0) {
+qasr_status launch_attention(qasr_ctx* c, int layer, int rows, const int* rs, const int* rp, int early = 0,
+                             bool merge_pdl = true) {
   AttnArgs a{};
   a.q = c->q;
   a.q_ld = c->cfg.num_attention_heads * c->cfg.head_dim;
@@ -503,7 +508,7 @@ qasr_status launch_attention(qasr_ctx* c, int layer, int rows, const int* rs, co
   a.early = early;
   a.status = c->status;
   if (c->attn_trace) a.trace = c->attn_trace + static_cast<size_t>(layer) * c->num_sms * ATTN_TRACE_SLOTS;
-  CK(launch_attention_pair(a, c->num_sms, c->stream, true), "attention launch");
+  CK(launch_attention_pair(a, c->num_sms, c->stream, true, merge_pdl), "attention launch");
   return QASR_OK;
 }
 
@@ -590,7 +595,20 @@ qasr_status enqueue_decode(qasr_ctx* c, int n, uint64_t* nk) {
 }
 
 // One cooperative launch of decode_chain_kernel (one CTA per SM).
-qasr_status launch_chain(qasr_ctx* c, const ChainArgs& a, const ChainShape& sh, int n) {
+// Whether every SM holds exactly one chain CTA with `smem` bytes (the PDL launch relies
+// on it instead of the cooperative attribute's check).
+static bool chain_one_cta_per_sm(size_t smem) {
+  int blocks = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, decode_chain_kernel, CHAIN_THREADS, smem) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return blocks == 1;
+}
+
+// `pdl`: the previous launch is the attention merge, which this chain reads only after
+// griddepcontrol.wait, so it may start while the merge drains (see decode_chain_kernel).
+qasr_status launch_chain(qasr_ctx* c, const ChainArgs& a, const ChainShape& sh, int n, bool pdl = false) {
   const int hs = c->cfg.hidden_size, qd = c->cfg.num_attention_heads * c->cfg.head_dim;
   const int I = c->cfg.intermediate_size;
   CUtensorMap tx, ta, tact;
@@ -604,9 +622,20 @@ qasr_status launch_chain(qasr_ctx* c, const ChainArgs& a, const ChainShape& sh, 
   cfg.blockDim = dim3(CHAIN_THREADS);
   cfg.dynamicSmemBytes = sh.smem;
   cfg.stream = c->stream;
+  // A cooperative launch is placed as a whole, so under PDL it could not start before
+  // every SM is free.  The PDL launch is therefore a plain one: one CTA per SM (its shared
+  // memory admits no second, checked at context creation), every CTA resident once the
+  // attention's CTAs have exited (they never wait on this grid), and the grid barriers'
+  // waits are bounded in any case.
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
+  const bool use_pdl = pdl && c->chain_pdl;
+  if (use_pdl) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+  } else {
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+  }
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   g_launches.fetch_add(1, std::memory_order_relaxed);
@@ -691,7 +720,9 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
   }
   for (int l = 0; l < L; ++l) {
     // layer 0's row_pos comes from chain 0 (the launch just before it): no early start
-    qasr_status s = launch_attention(c, l, n, c->drow_slot, c->drow_pos, l > 0 ? 1 : 0);
+    // with a programmatic chain the merge launch is not programmatic, so no merge CTA holds
+    // an SM during the attention and the chain's CTAs start on the SMs the merge leaves
+    qasr_status s = launch_attention(c, l, n, c->drow_slot, c->drow_pos, l > 0 ? 1 : 0, !c->chain_pdl);
     if (s) return s;
     const LayerDev& Ld = c->layers[l];
     ChainArgs a = base;
@@ -727,10 +758,10 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
       a.ops[k++].norm_out = c->xf;
     }
     a.n_ops = k;
-    if ((s = launch_chain(c, a, sh, n))) return s;
+    if ((s = launch_chain(c, a, sh, n, true))) return s;
   }
   (void)qkv_out;
-  *nk += 1 + 3 * static_cast<uint64_t>(L);
+  *nk += 1 + 3 * static_cast<uint64_t>(L);  // chain 0, then per layer attention + merge + chain
   return enqueue_head(c, n, nullptr, c->drow_slot, c->drow_pos, c->out_tok, 0, nk, false);
 }
 
@@ -960,6 +991,9 @@ qasr_status qasr_create(const qasr_text_config* cfg, const qasr_options* opts, i
   c->chain_ok = i8 && hs <= CHAIN_MAX_HS && hs % (2 * CHAIN_EPI_THREADS) == 0 && I % 64 == 0 &&
                 !(no_chain && no_chain[0] == '1');
   if (c->chain_ok) {
+    const char* no_cpdl = std::getenv("QASR_B200_NO_CHAIN_PDL");
+    c->chain_pdl = pdl_enabled() && !(no_cpdl && no_cpdl[0] == '1') &&
+                   chain_one_cta_per_sm(chain_shape(std::min(opts->max_slots, CHAIN_MAX_ROWS)).smem);
     c->chain_ws_rows = chain_shape(std::min(opts->max_slots, CHAIN_MAX_ROWS)).n_tile;
     for (int i = 0; i < 4; ++i) {  // shapes[] order: QKV, o_proj, gate|up, down
       const ChainGemm g = chain_gemm_plan(nullptr, nullptr, false, shapes[i][0], shapes[i][1], 0, c->num_sms,

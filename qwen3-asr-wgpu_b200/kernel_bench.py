@@ -246,6 +246,10 @@ def bench_step(args, pkg, torch):
         launches.append({"start_us": round((ent - t0) / 1e3, 2), "dur_us": round((ext - ent) / 1e3, 2),
                          "entry_skew_us": round((tr[k, :, 0].max() - ent) / 1e3, 2),
                          "prologue_median_us": [round((np.median(tr[k, :, j]) - ent) / 1e3, 2) for j in (37, 38, 39)],
+                         "input_seen_min_median_us": [round((tr[k, :, 66][tr[k, :, 66] > 0].min() - ent) / 1e3, 2),
+                                                      round((np.median(tr[k, :, 66][tr[k, :, 66] > 0]) - ent) / 1e3, 2)]
+                         if (tr[k, :, 66] > 0).any() else None,
+
                          "first_unit_w_slot_a_seen_issued_us": [round((np.median(tr[k, :, j]) - ent) / 1e3, 2)
                                                                 for j in (64, 65, 72, 40, 104)],
                          "ops_done_passed_us": ops, "gemms_median_max_us": gemms,
