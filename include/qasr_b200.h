@@ -236,6 +236,9 @@ qasr_status qasr_checkpoint_weight_format(qasr_checkpoint* ck, const char* prefi
  * round-to-nearest-even, src/weights.rs:55-80; I8 dequantised with its
  * `<name without .weight>.weight_scale`, f16(f32(q) * s)); `count` = elements. */
 qasr_status qasr_checkpoint_read_f16(qasr_checkpoint* ck, const char* name, uint16_t* out, int64_t count);
+/* RawTensor::as_f32 (src/weights.rs:109-111): `name` (F16 / BF16 / F32) widened to f32
+ * exactly — biases and LayerNorm parameters of the audio tower; `count` = elements. */
+qasr_status qasr_checkpoint_read_f32(qasr_checkpoint* ck, const char* name, float* out, int64_t count);
 /* append_f16_row_le (src/weights.rs:121-146): rows `rows[0..n)` of a 2-D `name` as f16
  * into out [n][cols] (the token-embedding lookup that builds a prefill's hidden rows). */
 qasr_status qasr_checkpoint_rows_f16(qasr_checkpoint* ck, const char* name, const int32_t* rows, int n,

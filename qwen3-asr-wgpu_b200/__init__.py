@@ -8,6 +8,8 @@ include/qasr_b200.h (libqasr_b200.so, built in-tree by build.py):
   ``WgpuTextDecoder`` (``fork_capped``, ``pos``, ``set_input_token``;
   src/decoder.rs:2453, 929, 1670), ``prefill_batch`` (src/decoder.rs:3599) and
   ``BatchProjections::step`` (src/decoder.rs:3339) as ``step_batch``.
+* ``AudioEncoder`` (audio.py) is the audio tower in front of the prefill:
+  ``GpuAudioEncoder::{encode, encode_batch}`` (src/audio_encoder_gpu.rs:905-971).
 * Failures raise ``DecoderError`` carrying the library's status code and message —
   the reference's ``anyhow`` errors (src/decoder.rs:4458-4486).
 
@@ -62,7 +64,11 @@ EXPORTED_SYMBOLS = (
     "qasr_read_model_config", "qasr_checkpoint_open", "qasr_checkpoint_close",
     "qasr_checkpoint_last_error", "qasr_checkpoint_tensor_count", "qasr_checkpoint_tensor_info",
     "qasr_checkpoint_weight_format", "qasr_checkpoint_read_f16", "qasr_checkpoint_rows_f16",
-    "qasr_load_checkpoint", "qasr_batch_decode", "qasr_batch_decode_backend",
+    "qasr_load_checkpoint", "qasr_batch_decode", "qasr_batch_decode_backend", "qasr_checkpoint_read_f32",
+    # include/qasr_b200_audio.h
+    "qasr_audio_token_count", "qasr_audio_create", "qasr_audio_destroy", "qasr_audio_last_error",
+    "qasr_audio_load_weights", "qasr_audio_load_checkpoint", "qasr_audio_encode", "qasr_audio_encode_batch",
+    "qasr_audio_encode_device", "qasr_audio_sync", "qasr_audio_stream", "qasr_audio_launch_count",
 )
 
 
@@ -577,6 +583,13 @@ class Checkpoint:
         self._check(lib.qasr_checkpoint_read_f16(self._h, name.encode(), _ptr(out), out.size))
         return out
 
+    def read_f32(self, name: str) -> np.ndarray:
+        """as_f32: the tensor widened to f32 (F16 / BF16 / F32)."""
+        _, shape = self.info(name)
+        out = np.zeros(shape, np.float32)
+        self._check(lib.qasr_checkpoint_read_f32(self._h, name.encode(), _ptr(out), out.size))
+        return out
+
     def rows_f16(self, name: str, rows) -> np.ndarray:
         """append_f16_row_le for each row id: f16 bits [n, cols]."""
         _, shape = self.info(name)
@@ -682,6 +695,11 @@ def kv_page_swizzle(pool: np.ndarray) -> np.ndarray:
     d = np.arange(128)[None, :]
     col = (((d >> 3) ^ (p & 7)) << 3) | (d & 7)
     return np.take_along_axis(pool, np.broadcast_to(col, pool.shape), axis=-1)
+
+
+from .audio import (AUDIO_PRESETS, AudioEncoder, SyntheticAudioTower, audio_config,  # noqa: E402,F401
+                    conv_geometry, synthetic_mel)
+from .audio import token_count as audio_token_count  # noqa: E402,F401
 
 
 def version() -> str:

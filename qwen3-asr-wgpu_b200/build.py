@@ -29,7 +29,7 @@ CXXFLAGS = ["-O3", "-std=c++17", "-fPIC", "-march=x86-64-v3", "-fopenmp", "-Wall
 NVFLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
            "-ccbin", CXX, "-Xptxas", "-v"] + ARCH
 
-CUDA_SOURCES = ["runtime.cu"]
+CUDA_SOURCES = ["runtime.cu", "audio.cu"]
 CXX_SOURCES = ["synth.cpp", "host_helpers.cpp", "checkpoint.cpp", "batch_decode.cpp"]
 
 

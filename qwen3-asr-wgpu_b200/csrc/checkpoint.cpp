@@ -675,6 +675,19 @@ qasr_status qasr_checkpoint_read_f16(qasr_checkpoint* ck, const char* name, uint
   return QASR_OK;
 }
 
+qasr_status qasr_checkpoint_read_f32(qasr_checkpoint* ck, const char* name, float* out, int64_t count) {
+  if (!ck || !name || !out) return QASR_ERR_INVALID_ARG;
+  const Tensor* t = ck->find(name);
+  if (!t) return ck->fail(QASR_ERR_INVALID_ARG, std::string("weight not found: ") + name);
+  if (t->numel() != count)
+    return ck->fail(QASR_ERR_INVALID_ARG, std::string(name) + " has " + std::to_string(t->numel()) +
+                                              " elements, not " + std::to_string(count));
+  if (t->dtype != "F16" && t->dtype != "BF16" && t->dtype != "F32")
+    return ck->fail(QASR_ERR_INVALID_ARG, std::string(name) + ": f32 read of dtype " + t->dtype);
+  for (int64_t i = 0; i < count; ++i) out[i] = to_f32_elem(*t, i);
+  return QASR_OK;
+}
+
 qasr_status qasr_checkpoint_rows_f16(qasr_checkpoint* ck, const char* name, const int32_t* rows, int n,
                                      uint16_t* out, int64_t count) {
   if (!ck || !name || !rows || !out || n < 0) return QASR_ERR_INVALID_ARG;

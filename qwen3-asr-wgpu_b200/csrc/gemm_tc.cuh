@@ -39,6 +39,12 @@ enum EpiKind : int {
   EPI_SILU = 2,    // interleaved gate|up tiles -> f16(silu(f16 g) * f16 u) (src/cpu_decoder.rs:442-448)
   EPI_QKV = 3,     // per-head q/k RMSNorm + rotate-half RoPE; Q -> q_out, K and raw V -> paged KV
   EPI_LOGITS = 4,  // f32 logits (optional) + per-row argmax via 64-bit atomicMax keys
+  // audio tower (CpuAudioLinear::forward + the ops that follow it, src/audio_encoder.rs:117-131);
+  // `bias` may be null (no bias add)
+  EPI_BIAS_F16 = 5,      // out[r, m] = f16(acc + bias[m])
+  EPI_BIAS_GELU = 6,     // out[r, m] = f16(gelu(acc + bias[m])), gelu = 0.5 x (1 + erf(x / sqrt 2))
+  EPI_BIAS_F32 = 7,      // out32[r, m] = acc + bias[m]
+  EPI_BIAS_RESID32 = 8,  // out32[r, m] = out32[r, m] + (acc + bias[m])  (f32 residual stream)
 };
 
 constexpr int GEMM_BUILD_GROUPS = 2;  // int8 A-builder warpgroups
@@ -99,6 +105,10 @@ struct GemmArgs {
   float* logits;
   int ld_logits;
   unsigned long long* best;
+  // EPI_BIAS_*
+  const float* bias;
+  float* out32;
+  int ldo32;
   // split tiles
   float* ws;
   int* counters;
@@ -264,6 +274,28 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, EpiSmem& es, i
       }
     }
     named_bar_sync(1, 128);
+  } else if constexpr (EPI == EPI_BIAS_F16 || EPI == EPI_BIAS_GELU || EPI == EPI_BIAS_F32 ||
+                       EPI == EPI_BIAS_RESID32) {
+    const int m = mt * 128 + e;
+    const float b = a.bias != nullptr ? a.bias[m] : 0.0f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int n = nbase + j;  // warp-uniform
+      if (n < a.rows) {
+        const float y = a.bias != nullptr ? __fadd_rn(v[j], b) : v[j];
+        if constexpr (EPI == EPI_BIAS_F16) {
+          a.out[static_cast<size_t>(n) * a.ldo + m] = __float2half_rn(y);
+        } else if constexpr (EPI == EPI_BIAS_GELU) {
+          const float g = __fmul_rn(__fmul_rn(0.5f, y), __fadd_rn(1.0f, erff(__fmul_rn(y, 0.70710678118654752f))));
+          a.out[static_cast<size_t>(n) * a.ldo + m] = __float2half_rn(g);
+        } else if constexpr (EPI == EPI_BIAS_F32) {
+          a.out32[static_cast<size_t>(n) * a.ldo32 + m] = y;
+        } else {
+          float* p = a.out32 + static_cast<size_t>(n) * a.ldo32 + m;
+          *p = __fadd_rn(*p, y);
+        }
+      }
+    }
   } else if constexpr (EPI == EPI_LOGITS) {
     const uint32_t vocab_row = static_cast<uint32_t>(mt * 128 + e);
 #pragma unroll
@@ -296,7 +328,7 @@ __device__ __forceinline__ size_t weight_tile_offset(int row, int chunk16, int k
          static_cast<size_t>((c ^ (r & 7)) << 4);
 }
 
-__global__ void pack_weight_tiles_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst,
+static __global__ void pack_weight_tiles_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst,
                                          int n_out, int row_bytes) {
   const int chunks = row_bytes >> 4;
   const long long total = static_cast<long long>(n_out) * chunks;

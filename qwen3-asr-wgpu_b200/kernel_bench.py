@@ -5,6 +5,7 @@ the same way: src/bin/batch_gemv_bench.rs, src/bin/gemv_bench.rs, src/bin/attn_b
     python qwen3-asr-wgpu_b200/kernel_bench.py attention --slots 512 --lo 256 --hi 4096
     python qwen3-asr-wgpu_b200/kernel_bench.py append --slots 512 --chunk 13
     python qwen3-asr-wgpu_b200/kernel_bench.py step --slots 32 --lo 100 --hi 1500
+    python qwen3-asr-wgpu_b200/kernel_bench.py audio --model 0.6b --seconds 30
 
 Each prints one JSON line: median CUDA-event time per launch (operands evicted from L2
 by a 256 MB write between launches), algorithmic bytes and GB/s.  `attention` is
@@ -262,6 +263,74 @@ def bench_step(args, pkg, torch):
             "gaps_us": gaps[:6], "attention_layers_1plus_median": attn_median, "attention_first": attn[:2]}
 
 
+def audio_flops(pkg, cfg, n_frames):
+    """Algorithmic FLOPs of one encode: the convs over their unpadded K (9 C), conv_out, the
+    layers' projections and windowed attention (QK^T and PV), the projector."""
+    tpc, (h1, w1), (h2, w2), (h3, w3) = pkg.conv_geometry(cfg)
+    cs = 2 * cfg["n_window"]
+    chunks = -(-n_frames // cs)
+    C, d, f, o = cfg["downsample_hidden_size"], cfg["d_model"], cfg["encoder_ffn_dim"], cfg["output_dim"]
+    T = pkg.audio_token_count(cfg, n_frames)
+    conv1 = 2 * chunks * h1 * w1 * C * 9
+    gemm = 2 * chunks * (h2 * w2 + h3 * w3) * C * 9 * C + 2 * T * C * h3 * d
+    gemm += cfg["encoder_layers"] * 2 * T * (4 * d * d + 2 * d * f) + 2 * T * (d * d + d * o)
+    wlen = tpc * (max(cfg["n_window_infer"], cs) // cs)
+    lens = [min(wlen, T - s) for s in range(0, T, wlen)]
+    attn = cfg["encoder_layers"] * 4 * sum(n * n for n in lens) * d
+    return T, conv1, gemm, attn
+
+
+def bench_audio(args, pkg, torch):
+    """One encode of a clip of --seconds of audio (100 mel frames per second) through the
+    device-resident entry point, timed on the tower's stream; and the same clip through the
+    host API (mel from host memory, embeddings back to host memory) by wall clock."""
+    import time
+    cfg = pkg.audio_config(args.model)
+    tw = pkg.SyntheticAudioTower(cfg, seed=args.seed)
+    enc = pkg.AudioEncoder(cfg)
+    enc.load(tw.tensors)
+    n_frames = int(args.seconds * 100)
+    mel = pkg.synthetic_mel(cfg["num_mel_bins"], n_frames, seed=args.seed)
+    T = enc.token_count(n_frames)
+    mel_d = torch.from_numpy(mel).cuda()
+    out_d = torch.empty((T, cfg["output_dim"]), dtype=torch.float16, device="cuda")
+    st = torch.cuda.ExternalStream(enc.stream)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+    times, launches = [], 0
+    for it in range(3 + args.iters):
+        with torch.cuda.stream(st):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(st)
+            l0 = enc.launches
+            enc.encode_device(mel_d.data_ptr(), n_frames, out_d.data_ptr())
+            launches = enc.launches - l0
+            b.record(st)
+        enc.sync()
+        if it >= 3:
+            times.append(a.elapsed_time(b) * 1e-3)
+    e2e = []
+    for it in range(2 + max(3, args.iters // 4)):
+        t0 = time.perf_counter()
+        enc.encode(mel)
+        if it >= 2:
+            e2e.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    T_, conv1, gemm, attn = audio_flops(pkg, cfg, n_frames)
+    res = {"kernel": "audio_tower", "model": args.model, "seconds": args.seconds, "frames": n_frames, "tokens": T,
+           "median_ms": med * 1e3, "best_ms": min(times) * 1e3, "launches": launches,
+           "audio_s_per_s": args.seconds / med, "gemm_gflop": gemm / 1e9, "attn_gflop": attn / 1e9,
+           "conv1_gflop": conv1 / 1e9, "tflops": (gemm + attn + conv1) / med / 1e12,
+           "e2e_median_ms": statistics.median(e2e) * 1e3,
+           "e2e_bytes": mel.nbytes + T * cfg["output_dim"] * 2}
+    peaks = ROOT / "MEASURED_PEAKS.json"
+    if peaks.exists():
+        res["tensor_frac_of_measured"] = res["tflops"] / json.loads(peaks.read_text())["bf16_tflops"]
+    enc.close()
+    return res
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="what", required=True)
@@ -287,12 +356,17 @@ def main(argv=None):
     sp.add_argument("--lo", type=int, default=100)
     sp.add_argument("--hi", type=int, default=1500)
     sp.add_argument("--seed", type=int, default=5)
+    au = sub.add_parser("audio")
+    au.add_argument("--model", default="0.6b")
+    au.add_argument("--seconds", type=float, default=30.0)
+    au.add_argument("--seed", type=int, default=5)
     for p in sub.choices.values():
         p.add_argument("--iters", type=int, default=20)
     args = ap.parse_args(argv)
     import torch
     pkg = _pkg()
-    fn = {"gemm": bench_gemm, "attention": bench_attention, "append": bench_append, "step": bench_step}[args.what]
+    fn = {"gemm": bench_gemm, "attention": bench_attention, "append": bench_append, "step": bench_step,
+          "audio": bench_audio}[args.what]
     res = fn(args, pkg, torch)
     hbm = None
     peaks = ROOT / "MEASURED_PEAKS.json"
