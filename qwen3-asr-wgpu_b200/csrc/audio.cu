@@ -4,7 +4,9 @@
 // activation buffers grown to the largest request seen.  An encode is one stream of
 // launches (no host round trip inside): per round of up to AUDIO_ROUND_CHUNKS conv chunks
 // conv2d1 (CUDA cores) -> im2col -> conv2d2 GEMM -> im2col -> conv2d3 GEMM -> token packing;
-// then conv_out over all tokens, the transformer layers, ln_post and the projector.  The
+// then conv_out over all tokens, the transformer layers, ln_post and the projector.  GEMM
+// epilogues only store (bias, GELU); each residual add is fused into the LayerNorm kernel
+// that follows it (h += delta, then normalise), so no GEMM reads the residual stream.  The
 // GEMMs are gemm_tc_kernel (tcgen05, weights as UMMA M, stream-K over (tile, k-block)
 // units) launched as programmatic dependents so each streams its weights while the
 // previous kernel drains.
@@ -81,7 +83,7 @@ struct qasr_audio_ctx {
   float *lnp_w = nullptr, *lnp_b = nullptr;
   bool loaded = false;
   // activations (grown on demand)
-  Buf mel, chunks, win, act1, x2, act2, x3, act3, packed, h32, xn, qkv32, attn16, ffn16, p116, out16, ws, cnt;
+  Buf mel, chunks, win, act1, x2, act2, x3, act3, packed, h32, delta, xn, qkv32, attn16, ffn16, p116, out16, ws, cnt;
   uint32_t* status = nullptr;
   // host copies of the launch tables (they outlive an asynchronous encode's copies)
   std::vector<AudioChunk> h_chunks;
@@ -198,6 +200,11 @@ bool check_config(const qasr_audio_config& g, std::string* why) {
              g.encoder_ffn_dim, g.output_dim);
     return bad(b);
   }
+  if (g.d_model > 128 * AUDIO_LN_MAXV) {
+    snprintf(b, sizeof b, "d_model %d: this tower's LayerNorm holds rows of at most %d", g.d_model,
+             128 * AUDIO_LN_MAXV);
+    return bad(b);
+  }
   if (g.downsample_hidden_size % 8) return bad("downsample_hidden_size must be a multiple of 8");
   const int h3 = conv_len(conv_len(conv_len(g.num_mel_bins)));
   if ((g.downsample_hidden_size * h3) % 64) {
@@ -205,6 +212,11 @@ bool check_config(const qasr_audio_config& g, std::string* why) {
     return bad(b);
   }
   if (g.max_source_positions < feo(2 * g.n_window)) return bad("max_source_positions below tokens per chunk");
+  {  // the conv kernels index a round with 32-bit arithmetic
+    const long long C = g.downsample_hidden_size, w1 = conv_len(2 * g.n_window), h1 = conv_len(g.num_mel_bins);
+    const long long kv = (9 * C + 63) / 64 * 64 / 8;
+    if (AUDIO_ROUND_CHUNKS * h1 * w1 * std::max(C / 8, kv) >= (1LL << 31)) return bad("conv chunk too large");
+  }
   return true;
 }
 
@@ -228,11 +240,34 @@ cudaError_t set_gemm_attr() {
                               g_dyn_smem_max);
 }
 
+// CTA count of an audio GEMM.  With fewer tiles than SMs, each tile is cut into s
+// k-segments (grid = tiles * s): s = 1 needs no split fixup, a larger s streams fewer units
+// per CTA but adds the last CTA's pass over s partials.  Measured per CTA (B200, f16,
+// 128-row tiles): ~4 us of set-up and first loads, ~0.6 us per (16 KB W + 16 KB X) unit,
+// ~2.5 us per partial of a split tile; the cheapest s wins.  With at least as many tiles
+// as SMs the default stream-K split applies (a few boundary tiles per CTA).
+int audio_grid(int n_out, int k, int rows, int sms) {
+  const GemmShape d = gemm_shape(n_out, k, false, rows, sms);
+  if (d.tiles >= sms) return 0;
+  int best = 1;
+  double best_t = 1e30;
+  for (int sp = 1; sp <= 8 && d.tiles * sp <= sms; ++sp) {
+    const double units = static_cast<double>(d.kblocks) / sp;
+    const double t = 4.0 + 0.6 * units + (sp > 1 ? 2.5 * sp : 0.0);
+    if (t < best_t) {
+      best_t = t;
+      best = sp;
+    }
+  }
+  return d.tiles * best;
+}
+
 // One GEMM: out = epilogue(X [rows, L.k] . W^T + bias).  The split workspace must already
 // hold the plan (reserve_gemm).
 qasr_status gemm(qasr_audio_ctx* c, const ALin& L, const __half* X, int rows, int epi, __half* out16, int ldo,
                  float* out32, int ldo32) {
-  const GemmShape s = gemm_shape(L.n_out, L.k, false, rows, c->num_sms);
+  const GemmShape s =
+      gemm_shape(L.n_out, L.k, false, rows, c->num_sms, audio_grid(L.n_out, L.k, rows, c->num_sms));
   if (2ull * static_cast<unsigned long long>(s.units) * static_cast<unsigned long long>(s.grid) >= (1ull << 32))
     return afail(c, QASR_ERR_CAPACITY, "GEMM %d x %d over %d rows: too many units", L.n_out, L.k, rows);
   if (s.ws_floats * sizeof(float) > c->ws.bytes || static_cast<size_t>(s.tiles) * sizeof(int) > c->cnt.bytes)
@@ -275,9 +310,6 @@ qasr_status gemm(qasr_audio_ctx* c, const ALin& L, const __half* X, int rows, in
     case EPI_BIAS_F32:
       e = launch_k(gemm_tc_kernel<false, EPI_BIAS_F32>, grid, block, s.smem, c->stream, true, tmx, a);
       break;
-    case EPI_BIAS_RESID32:
-      e = launch_k(gemm_tc_kernel<false, EPI_BIAS_RESID32>, grid, block, s.smem, c->stream, true, tmx, a);
-      break;
     default:
       break;
   }
@@ -291,7 +323,8 @@ qasr_status gemm(qasr_audio_ctx* c, const ALin& L, const __half* X, int rows, in
 qasr_status reserve_gemm(qasr_audio_ctx* c, const std::vector<std::pair<const ALin*, int>>& plan) {
   size_t wsf = 64, tiles = 1;
   for (auto& pr : plan) {
-    const GemmShape s = gemm_shape(pr.first->n_out, pr.first->k, false, pr.second, c->num_sms);
+    const GemmShape s = gemm_shape(pr.first->n_out, pr.first->k, false, pr.second, c->num_sms,
+                                   audio_grid(pr.first->n_out, pr.first->k, pr.second, c->num_sms));
     wsf = std::max(wsf, s.ws_floats);
     tiles = std::max(tiles, static_cast<size_t>(s.tiles));
   }
@@ -351,6 +384,7 @@ qasr_status run_tower(qasr_audio_ctx* c, const float* mel_dev, std::vector<Utt>&
       (s = grow(c, c->act3, 2 * R * p3 * c->ldc, "conv3 activations")) ||
       (s = grow(c, c->packed, 2ull * T * c->cf, "conv_out operand")) ||
       (s = grow(c, c->h32, 4ull * T * dm, "residual stream")) ||
+      (s = grow(c, c->delta, 4ull * T * dm, "block outputs")) ||
       (s = grow(c, c->xn, 2ull * T * dm, "normed rows")) ||
       (s = grow(c, c->qkv32, 4ull * T * 3 * dm, "q|k|v")) ||
       (s = grow(c, c->attn16, 2ull * T * dm, "attention rows")) ||
@@ -385,61 +419,70 @@ qasr_status run_tower(qasr_audio_ctx* c, const float* mel_dev, std::vector<Utt>&
   for (int r0 = 0; r0 < n_chunks; r0 += R) {
     const int n = std::min(R, n_chunks - r0);
     const AudioChunk* ch = P<AudioChunk>(c->chunks) + r0;
-    audio_conv1_kernel<<<grid_for(static_cast<long long>(n) * p1 * (c->C / 8)), 256,
-                         static_cast<size_t>(c->C) * 10 * sizeof(float), c->stream>>>(
-        mel_dev, ch, n, g.num_mel_bins, c->h1, c->w1, c->c1_w, c->c1_b, c->C, P<__half>(c->act1), c->ldc);
-    audio_im2col_kernel<<<grid_for(static_cast<long long>(n) * p2 * (c->kconv / 8)), 256, 0, c->stream>>>(
-        P<__half>(c->act1), n, c->h1, c->w1, c->C, c->ldc, c->h2, c->w2, P<__half>(c->x2), c->kconv);
+    ACK(launch_k(audio_conv1_kernel,
+                 dim3(grid_for(static_cast<long long>(n) * c->h1 * ((c->w1 + AUDIO_C1_POS - 1) / AUDIO_C1_POS) *
+                               (c->C / 8))),
+                 dim3(256), 0, c->stream, true, mel_dev, ch, n, g.num_mel_bins, c->h1, c->w1,
+                 static_cast<const float*>(c->c1_w), static_cast<const float*>(c->c1_b), c->C, P<__half>(c->act1),
+                 c->ldc),
+        "conv1 launch");
+    ACK(launch_k(audio_im2col_kernel, dim3(grid_for(static_cast<long long>(n) * p2 * (c->kconv / 8))), dim3(256), 0,
+                 c->stream, true, static_cast<const __half*>(P<__half>(c->act1)), n, c->h1, c->w1, c->C, c->ldc,
+                 c->h2, c->w2, P<__half>(c->x2), c->kconv),
+        "im2col launch");
     c->launches += 2;
-    ACK(cudaGetLastError(), "conv1 / im2col launch");
     if ((s = gemm(c, c->c2, P<__half>(c->x2), static_cast<int>(n * p2), EPI_BIAS_GELU, P<__half>(c->act2), c->ldc,
                   nullptr, 0)))
       return s;
-    audio_im2col_kernel<<<grid_for(static_cast<long long>(n) * p3 * (c->kconv / 8)), 256, 0, c->stream>>>(
-        P<__half>(c->act2), n, c->h2, c->w2, c->C, c->ldc, c->h3, c->w3, P<__half>(c->x3), c->kconv);
+    ACK(launch_k(audio_im2col_kernel, dim3(grid_for(static_cast<long long>(n) * p3 * (c->kconv / 8))), dim3(256), 0,
+                 c->stream, true, static_cast<const __half*>(P<__half>(c->act2)), n, c->h2, c->w2, c->C, c->ldc,
+                 c->h3, c->w3, P<__half>(c->x3), c->kconv),
+        "im2col launch");
     c->launches++;
-    ACK(cudaGetLastError(), "im2col launch");
     if ((s = gemm(c, c->c3, P<__half>(c->x3), static_cast<int>(n * p3), EPI_BIAS_GELU, P<__half>(c->act3), c->ldc,
                   nullptr, 0)))
       return s;
-    audio_pack_kernel<<<dim3(std::max(1, (c->tpc * std::max(c->C, dm) + 255) / 256), n), 256, 0, c->stream>>>(
-        P<__half>(c->act3), ch, n, c->h3, c->w3, c->C, c->ldc, P<__half>(c->packed), P<float>(c->h32), c->pe, dm);
+    ACK(launch_k(audio_pack_kernel, dim3(std::max(1, (c->tpc * std::max(c->C, dm) + 255) / 256), n), dim3(256), 0,
+                 c->stream, true, static_cast<const __half*>(P<__half>(c->act3)), ch, n, c->h3, c->w3, c->C, c->ldc,
+                 P<__half>(c->packed), P<float>(c->h32), static_cast<const float*>(c->pe), dm),
+        "pack launch");
     c->launches++;
-    ACK(cudaGetLastError(), "pack launch");
   }
-  // conv_out + positions: h = pe + (packed . W^T + b)
-  if ((s = gemm(c, c->co, P<__half>(c->packed), T, EPI_BIAS_RESID32, nullptr, 0, P<float>(c->h32), dm))) return s;
+  // conv_out: delta = packed . W^T + b; the first residual add makes h = pe + delta
+  if ((s = gemm(c, c->co, P<__half>(c->packed), T, EPI_BIAS_F32, nullptr, 0, P<float>(c->delta), dm))) return s;
 
   // ---- transformer layers (CpuAudioLayer::forward, src/audio_encoder.rs:614-630)
   const int ln_grid = (T * 32 + 255) / 256;
   const float scale = 1.0f / std::sqrt(static_cast<float>(c->hd));
+  const int qblocks = (c->wlen + AUDIO_ATTN_QB - 1) / AUDIO_ATTN_QB;
   for (const ALayer& L : c->layers) {
-    audio_layernorm_kernel<<<ln_grid, 256, 0, c->stream>>>(P<float>(c->h32), T, dm, L.ln1_w, L.ln1_b,
-                                                           AUDIO_LN_EPS, P<__half>(c->xn));
+    ACK(launch_k(audio_residual_layernorm_kernel, dim3(ln_grid), dim3(256), 0, c->stream, true, P<float>(c->h32),
+                 static_cast<const float*>(P<float>(c->delta)), T, dm, static_cast<const float*>(L.ln1_w),
+                 static_cast<const float*>(L.ln1_b), AUDIO_LN_EPS, P<__half>(c->xn)),
+        "layernorm launch");
     c->launches++;
-    ACK(cudaGetLastError(), "layernorm launch");
     if ((s = gemm(c, L.qkv, P<__half>(c->xn), T, EPI_BIAS_F32, nullptr, 0, P<float>(c->qkv32), 3 * dm))) return s;
-    if (c->attn_kv_smem)
-      audio_window_attention_kernel<true><<<dim3(n_win, c->nh), AUDIO_ATTN_THREADS, c->attn_smem, c->stream>>>(
-          P<float>(c->qkv32), P<int>(c->win), dm, c->hd, scale, c->wlen, P<__half>(c->attn16));
-    else
-      audio_window_attention_kernel<false><<<dim3(n_win, c->nh), AUDIO_ATTN_THREADS, c->attn_smem, c->stream>>>(
-          P<float>(c->qkv32), P<int>(c->win), dm, c->hd, scale, c->wlen, P<__half>(c->attn16));
+    ACK(launch_k(c->attn_kv_smem ? audio_window_attention_kernel<true> : audio_window_attention_kernel<false>,
+                 dim3(n_win, c->nh, qblocks), dim3(AUDIO_ATTN_THREADS), c->attn_smem, c->stream, true,
+                 static_cast<const float*>(P<float>(c->qkv32)), static_cast<const int*>(P<int>(c->win)), dm, c->hd,
+                 scale, c->wlen, P<__half>(c->attn16)),
+        "window attention launch");
     c->launches++;
-    ACK(cudaGetLastError(), "window attention launch");
-    if ((s = gemm(c, L.o, P<__half>(c->attn16), T, EPI_BIAS_RESID32, nullptr, 0, P<float>(c->h32), dm))) return s;
-    audio_layernorm_kernel<<<ln_grid, 256, 0, c->stream>>>(P<float>(c->h32), T, dm, L.ln2_w, L.ln2_b,
-                                                           AUDIO_LN_EPS, P<__half>(c->xn));
+    if ((s = gemm(c, L.o, P<__half>(c->attn16), T, EPI_BIAS_F32, nullptr, 0, P<float>(c->delta), dm))) return s;
+    ACK(launch_k(audio_residual_layernorm_kernel, dim3(ln_grid), dim3(256), 0, c->stream, true, P<float>(c->h32),
+                 static_cast<const float*>(P<float>(c->delta)), T, dm, static_cast<const float*>(L.ln2_w),
+                 static_cast<const float*>(L.ln2_b), AUDIO_LN_EPS, P<__half>(c->xn)),
+        "layernorm launch");
     c->launches++;
-    ACK(cudaGetLastError(), "layernorm launch");
     if ((s = gemm(c, L.fc1, P<__half>(c->xn), T, EPI_BIAS_GELU, P<__half>(c->ffn16), c->ffn, nullptr, 0))) return s;
-    if ((s = gemm(c, L.fc2, P<__half>(c->ffn16), T, EPI_BIAS_RESID32, nullptr, 0, P<float>(c->h32), dm))) return s;
+    if ((s = gemm(c, L.fc2, P<__half>(c->ffn16), T, EPI_BIAS_F32, nullptr, 0, P<float>(c->delta), dm))) return s;
   }
   // ---- ln_post, proj1 + GELU, proj2 (src/audio_encoder.rs:750-755)
-  audio_layernorm_kernel<<<ln_grid, 256, 0, c->stream>>>(P<float>(c->h32), T, dm, c->lnp_w, c->lnp_b,
-                                                         AUDIO_LN_EPS, P<__half>(c->xn));
+  ACK(launch_k(audio_residual_layernorm_kernel, dim3(ln_grid), dim3(256), 0, c->stream, true, P<float>(c->h32),
+               static_cast<const float*>(P<float>(c->delta)), T, dm, static_cast<const float*>(c->lnp_w),
+               static_cast<const float*>(c->lnp_b), AUDIO_LN_EPS, P<__half>(c->xn)),
+      "layernorm launch");
   c->launches++;
-  ACK(cudaGetLastError(), "layernorm launch");
   if ((s = gemm(c, c->p1, P<__half>(c->xn), T, EPI_BIAS_GELU, P<__half>(c->p116), dm, nullptr, 0))) return s;
   return gemm(c, c->p2, P<__half>(c->p116), T, EPI_BIAS_F16, out, c->out_dim, nullptr, 0);
 }
@@ -483,7 +526,6 @@ qasr_status qasr_audio_create(const qasr_audio_config* cfg, int device, qasr_aud
   cudaError_t ce = set_gemm_attr<EPI_BIAS_F16>();
   if (ce == cudaSuccess) ce = set_gemm_attr<EPI_BIAS_GELU>();
   if (ce == cudaSuccess) ce = set_gemm_attr<EPI_BIAS_F32>();
-  if (ce == cudaSuccess) ce = set_gemm_attr<EPI_BIAS_RESID32>();
   if (ce != cudaSuccess) return fail_out(QASR_ERR_DEVICE, std::string("GEMM attributes: ") + cudaGetErrorString(ce));
 
   auto* c = new qasr_audio_ctx();
@@ -542,7 +584,7 @@ void qasr_audio_destroy(qasr_audio_ctx* c) {
   cudaSetDevice(c->device);
   if (c->stream) cudaStreamSynchronize(c->stream);
   for (void* p : c->wallocs) cudaFree(p);
-  for (Buf* b : {&c->mel, &c->chunks, &c->win, &c->act1, &c->x2, &c->act2, &c->x3, &c->act3, &c->packed, &c->h32,
+  for (Buf* b : {&c->mel, &c->chunks, &c->win, &c->act1, &c->x2, &c->act2, &c->x3, &c->act3, &c->packed, &c->h32, &c->delta,
                  &c->xn, &c->qkv32, &c->attn16, &c->ffn16, &c->p116, &c->out16, &c->ws, &c->cnt})
     if (b->p) cudaFree(b->p);
   if (c->status) cudaFree(c->status);

@@ -8,8 +8,9 @@
 //   audio_conv1_kernel      conv2d1 (1 input channel, 9 taps) + bias + GELU, f32 CUDA cores
 //   audio_im2col_kernel     3x3 / stride 2 / pad 1 operand of conv2d2 and conv2d3
 //   audio_pack_kernel       conv3 output -> conv_out operand rows (valid tokens only) and the
-//                           sinusoidal position rows the conv_out epilogue adds onto
-//   audio_layernorm_kernel  LayerNorm (mean, variance, eps 1e-5) f32 -> f16 GEMM operand
+//                           sinusoidal position rows the conv_out output is added onto
+//   audio_residual_layernorm_kernel  h += delta (a block's output), then LayerNorm
+//                           (mean, variance, eps 1e-5) f32 -> f16 GEMM operand
 //   audio_window_attention_kernel  bidirectional attention inside token windows
 //
 // Layouts in HBM (one round of conv chunks at a time; tokens of every chunk packed):
@@ -22,7 +23,28 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include "device_common.cuh"
+#include "gemm_tc.cuh"  // griddep_wait / griddep_launch_dependents
+
 namespace qasr {
+
+// Every kernel here is launched as a programmatic dependent of the kernel before it: it may
+// become resident while that kernel drains, waits (griddepcontrol.wait) before reading
+// anything, and then lets the next launch (a GEMM that streams its weights before its own
+// wait) be scheduled.  The dependent grid starts only after every CTA of this one has
+// issued the trigger, i.e. is resident, so no kernel ever waits for resources held by a
+// kernel that waits on it.
+__device__ __forceinline__ void audio_pdl_entry() {
+  griddep_wait();
+  griddep_launch_dependents();
+}
+
+// 16-byte global -> shared copy that bypasses the registers (cp.async, L2 only): a thread
+// issues all of its copies before waiting for any.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // gelu as the reference: 0.5 x (1 + erf(x / sqrt 2)) in f32 (src/audio_encoder.rs:177-179)
 __device__ __forceinline__ float audio_gelu(float y) {
@@ -41,52 +63,68 @@ struct AudioChunk {
 };
 
 // conv2d1 + bias + GELU over the chunks [0, n) of the current round: out[chunk][ho][wo][c].
-// One thread computes 8 channels of one output position; the 9 taps are summed in
-// (kh, kw) order in f32.  x beyond the chunk's valid frames or outside the mel bins is 0
-// (the chunk buffer's zero fill and the conv padding, src/audio_encoder.rs:185-225).
-__global__ void __launch_bounds__(256) audio_conv1_kernel(const float* __restrict__ mel,
+// One thread computes 8 channels at AUDIO_C1_POS consecutive output columns of one output
+// row, holding the 8 x 9 weights in registers; the 9 taps are summed in (kh, kw) order in
+// f32.  x beyond the chunk's valid frames or outside the mel bins is 0 (the chunk buffer's
+// zero fill and the conv padding, src/audio_encoder.rs:185-225).  Index arithmetic is 32-bit
+// (a round holds < 2^31 outputs; the host checks): a 64-bit division is a long software
+// sequence.
+constexpr int AUDIO_C1_POS = 4;
+__global__ void __launch_bounds__(256, 2) audio_conv1_kernel(const float* __restrict__ mel,
                                                           const AudioChunk* __restrict__ chunks, int n,
                                                           int n_mels, int h1, int w1,
                                                           const float* __restrict__ w /*[C][9]*/,
                                                           const float* __restrict__ bias, int C,
                                                           __half* __restrict__ out, int ldc) {
-  extern __shared__ float c1_smem[];
-  float* sw = c1_smem;           // [C][9]
-  float* sb = c1_smem + C * 9;   // [C]
-  for (int i = threadIdx.x; i < C * 9; i += blockDim.x) sw[i] = w[i];
-  for (int i = threadIdx.x; i < C; i += blockDim.x) sb[i] = bias[i];
-  __syncthreads();
-  const int groups = C >> 3;
-  const long long total = static_cast<long long>(n) * h1 * w1 * groups;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+  audio_pdl_entry();
+  const unsigned groups = static_cast<unsigned>(C) >> 3;
+  const unsigned wq = (static_cast<unsigned>(w1) + AUDIO_C1_POS - 1) / AUDIO_C1_POS;  // column quads per row
+  const unsigned total = static_cast<unsigned>(n) * h1 * wq * groups;
+  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
     const int g = static_cast<int>(i % groups);
-    const long long pos = i / groups;
-    const int wo = static_cast<int>(pos % w1);
-    const int ho = static_cast<int>((pos / w1) % h1);
-    const int ch = static_cast<int>(pos / (static_cast<long long>(w1) * h1));
+    const unsigned rest = i / groups;
+    const int wo0 = static_cast<int>(rest % wq) * AUDIO_C1_POS;
+    const unsigned row = rest / wq;  // chunk * h1 + ho
+    const int ho = static_cast<int>(row % static_cast<unsigned>(h1));
+    const int ch = static_cast<int>(row / static_cast<unsigned>(h1));
     const AudioChunk k = chunks[ch];
-    float x[9];
-#pragma unroll
-    for (int kh = 0; kh < 3; ++kh) {
-#pragma unroll
-      for (int kw = 0; kw < 3; ++kw) {
-        const int mb = ho * 2 + kh - 1, fr = wo * 2 + kw - 1;
-        x[kh * 3 + kw] = (mb >= 0 && mb < n_mels && fr >= 0 && fr < k.valid)
-                             ? mel[k.mel_off + static_cast<long long>(mb) * k.n_frames + k.frame0 + fr]
-                             : 0.0f;
-      }
-    }
-    alignas(16) __half o[8];
+    float wr[8][9], br[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const int c = g * 8 + j;
-      float acc = 0.0f;
 #pragma unroll
-      for (int t = 0; t < 9; ++t) acc = __fadd_rn(acc, __fmul_rn(sw[c * 9 + t], x[t]));
-      o[j] = __float2half_rn(audio_gelu(__fadd_rn(acc, sb[c])));
+      for (int t = 0; t < 9; ++t) wr[j][t] = __ldg(w + (g * 8 + j) * 9 + t);
+      br[j] = __ldg(bias + g * 8 + j);
     }
-    *reinterpret_cast<uint4*>(out + pos * ldc + g * 8) = *reinterpret_cast<const uint4*>(o);
+    // the 3 mel rows x (2 * AUDIO_C1_POS + 1) frames this strip reads
+    float x[3][2 * AUDIO_C1_POS + 1];
+#pragma unroll
+    for (int kh = 0; kh < 3; ++kh) {
+      const int mb = ho * 2 + kh - 1;
+#pragma unroll
+      for (int f = 0; f < 2 * AUDIO_C1_POS + 1; ++f) {
+        const int fr = wo0 * 2 - 1 + f;
+        x[kh][f] = (mb >= 0 && mb < n_mels && fr >= 0 && fr < k.valid)
+                       ? __ldg(mel + k.mel_off + static_cast<size_t>(mb) * k.n_frames + k.frame0 + fr)
+                       : 0.0f;
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < AUDIO_C1_POS; ++q) {
+      const int wo = wo0 + q;
+      if (wo >= w1) break;
+      alignas(16) __half o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int kh = 0; kh < 3; ++kh)
+#pragma unroll
+          for (int kw = 0; kw < 3; ++kw) acc = __fadd_rn(acc, __fmul_rn(wr[j][kh * 3 + kw], x[kh][2 * q + kw]));
+        o[j] = __float2half_rn(audio_gelu(__fadd_rn(acc, br[j])));
+      }
+      *reinterpret_cast<uint4*>(out + (static_cast<size_t>(row) * w1 + wo) * ldc + g * 8) =
+          *reinterpret_cast<const uint4*>(o);
+    }
   }
 }
 
@@ -96,15 +134,15 @@ __global__ void __launch_bounds__(256) audio_conv1_kernel(const float* __restric
 __global__ void __launch_bounds__(256) audio_im2col_kernel(const __half* __restrict__ act, int n, int h, int w,
                                                            int C, int ldc, int ho_n, int wo_n,
                                                            __half* __restrict__ X, int kpad) {
-  const int vrow = kpad >> 3;
-  const long long total = static_cast<long long>(n) * ho_n * wo_n * vrow;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+  audio_pdl_entry();
+  const unsigned vrow = static_cast<unsigned>(kpad) >> 3;
+  const unsigned total = static_cast<unsigned>(n) * ho_n * wo_n * vrow;  // < 2^31 (host-checked)
+  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
     const int v = static_cast<int>(i % vrow);
-    const long long pos = i / vrow;
-    const int wo = static_cast<int>(pos % wo_n);
-    const int ho = static_cast<int>((pos / wo_n) % ho_n);
-    const int ch = static_cast<int>(pos / (static_cast<long long>(wo_n) * ho_n));
+    const unsigned pos = i / vrow;
+    const int wo = static_cast<int>(pos % static_cast<unsigned>(wo_n));
+    const int ho = static_cast<int>((pos / static_cast<unsigned>(wo_n)) % static_cast<unsigned>(ho_n));
+    const int ch = static_cast<int>(pos / (static_cast<unsigned>(wo_n) * ho_n));
     const int k0 = v * 8;
     uint4 val = make_uint4(0u, 0u, 0u, 0u);
     if (k0 < 9 * C) {
@@ -113,18 +151,19 @@ __global__ void __launch_bounds__(256) audio_im2col_kernel(const __half* __restr
       if (ih >= 0 && ih < h && iw >= 0 && iw < w)
         val = *reinterpret_cast<const uint4*>(act + ((static_cast<long long>(ch) * h + ih) * w + iw) * ldc + c0);
     }
-    *reinterpret_cast<uint4*>(X + pos * kpad + k0) = val;
+    *reinterpret_cast<uint4*>(X + static_cast<size_t>(pos) * kpad + k0) = val;
   }
 }
 
 // conv3 output act[chunk][f][t][ldc] -> the conv_out operand rows of the chunk's valid tokens,
 // packed[tok][c * F + f] (the permute of src/audio_encoder.rs:290-305, and the packing of
-// :736-744), and h[tok][:] = pe[t][:] (the conv_out epilogue then adds the projection:
-// pe + (acc + bias) == (acc + bias) + pe, as the reference orders it).
+// :736-744), and h[tok][:] = pe[t][:] (the first residual add then adds the conv_out
+// projection: pe + (acc + bias) == (acc + bias) + pe, as the reference orders it).
 __global__ void __launch_bounds__(256) audio_pack_kernel(const __half* __restrict__ act, const AudioChunk* __restrict__ chunks,
                                                          int n, int F, int T, int C, int ldc,
                                                          __half* __restrict__ packed, float* __restrict__ h,
                                                          const float* __restrict__ pe, int dm) {
+  audio_pdl_entry();
   const int ch = blockIdx.y;
   if (ch >= n) return;
   const AudioChunk k = chunks[ch];
@@ -141,122 +180,224 @@ __global__ void __launch_bounds__(256) audio_pack_kernel(const __half* __restric
   }
 }
 
-// LayerNorm over d (src/audio_encoder.rs:152-172): mean, then the mean of squared
-// deviations, inv_std = 1 / sqrt(var + eps); o = (x - mean) * inv_std * w + b.  One warp per
-// row; f32 math with IEEE-rounded steps, the output rounded once to f16 (a GEMM operand).
-__global__ void __launch_bounds__(256) audio_layernorm_kernel(const float* __restrict__ x, int rows, int d,
-                                                              const float* __restrict__ w,
-                                                              const float* __restrict__ b, float eps,
-                                                              __half* __restrict__ out) {
+// Residual add + LayerNorm (CpuAudioLayer::forward's `x += block(x)` then the next
+// CpuAudioLayerNorm::forward, src/audio_encoder.rs:614-630, 152-172): when `delta` is given
+// the row becomes h = h + delta (stored back: the f32 residual stream); then mean, the mean
+// of squared deviations, inv_std = 1 / sqrt(var + eps), o = (h - mean) * inv_std * w + b.
+// One warp per row, the row held in registers (lane l: float4 vectors l, l + 32, ...; every
+// load in flight at once); f32 math with IEEE-rounded steps, the output rounded once to f16
+// (a GEMM operand).  d is a multiple of 4 and at most 128 * AUDIO_LN_MAXV.
+constexpr int AUDIO_LN_MAXV = 10;
+__global__ void __launch_bounds__(256) audio_residual_layernorm_kernel(float* __restrict__ x,
+                                                                       const float* __restrict__ delta, int rows,
+                                                                       int d, const float* __restrict__ w,
+                                                                       const float* __restrict__ b, float eps,
+                                                                       __half* __restrict__ out) {
+  audio_pdl_entry();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= rows) return;
-  const float* xr = x + static_cast<long long>(warp) * d;
+  const int nv = d >> 2;
+  float4* xr = reinterpret_cast<float4*>(x + static_cast<size_t>(warp) * d);
+  float4 v[AUDIO_LN_MAXV];
+#pragma unroll
+  for (int k = 0; k < AUDIO_LN_MAXV; ++k)
+    v[k] = lane + 32 * k < nv ? xr[lane + 32 * k] : make_float4(0.f, 0.f, 0.f, 0.f);
+  if (delta != nullptr) {
+    const float4* dr = reinterpret_cast<const float4*>(delta + static_cast<size_t>(warp) * d);
+    float4 dv[AUDIO_LN_MAXV];
+#pragma unroll
+    for (int k = 0; k < AUDIO_LN_MAXV; ++k)
+      dv[k] = lane + 32 * k < nv ? dr[lane + 32 * k] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < AUDIO_LN_MAXV; ++k) {
+      if (lane + 32 * k < nv) {
+        v[k] = make_float4(__fadd_rn(v[k].x, dv[k].x), __fadd_rn(v[k].y, dv[k].y), __fadd_rn(v[k].z, dv[k].z),
+                           __fadd_rn(v[k].w, dv[k].w));
+        xr[lane + 32 * k] = v[k];
+      }
+    }
+  }
   float s = 0.0f;
-  for (int j = lane; j < d; j += 32) s = __fadd_rn(s, xr[j]);
+#pragma unroll
+  for (int k = 0; k < AUDIO_LN_MAXV; ++k)
+    s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, v[k].x), v[k].y), v[k].z), v[k].w);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
   const float mean = __fdiv_rn(s, static_cast<float>(d));
-  float v = 0.0f;
-  for (int j = lane; j < d; j += 32) {
-    const float dv = __fsub_rn(xr[j], mean);
-    v = __fadd_rn(v, __fmul_rn(dv, dv));
+  float q = 0.0f;
+#pragma unroll
+  for (int k = 0; k < AUDIO_LN_MAXV; ++k) {
+    if (lane + 32 * k < nv) {
+      const float a0 = __fsub_rn(v[k].x, mean), a1 = __fsub_rn(v[k].y, mean), a2 = __fsub_rn(v[k].z, mean),
+                  a3 = __fsub_rn(v[k].w, mean);
+      q = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(q, __fmul_rn(a0, a0)), __fmul_rn(a1, a1)), __fmul_rn(a2, a2)),
+                    __fmul_rn(a3, a3));
+    }
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
-  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(v, static_cast<float>(d)), eps)));
-  __half* orow = out + static_cast<long long>(warp) * d;
-  for (int j = lane; j < d; j += 32)
-    orow[j] = __float2half_rn(__fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xr[j], mean), inv), w[j]), b[j]));
+  for (int o = 16; o > 0; o >>= 1) q = __fadd_rn(q, __shfl_xor_sync(0xffffffffu, q, o));
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(q, static_cast<float>(d)), eps)));
+  __half2* orow = reinterpret_cast<__half2*>(out + static_cast<size_t>(warp) * d);
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  const float4* b4 = reinterpret_cast<const float4*>(b);
+#pragma unroll
+  for (int k = 0; k < AUDIO_LN_MAXV; ++k) {
+    const int c = lane + 32 * k;
+    if (c < nv) {
+      const float4 ww = w4[c], bb = b4[c];
+      auto f = [&](float xv, float wv, float bv) {
+        return __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xv, mean), inv), wv), bv);
+      };
+      orow[2 * c] = __floats2half2_rn(f(v[k].x, ww.x, bb.x), f(v[k].y, ww.y, bb.y));
+      orow[2 * c + 1] = __floats2half2_rn(f(v[k].z, ww.z, bb.z), f(v[k].w, ww.w, bb.w));
+    }
+  }
 }
 
 // Attention inside token windows (attention_window, src/audio_encoder.rs:519-566): window
-// `blockIdx.x` = rows [win[2i], win[2i] + win[2i+1]), head `blockIdx.y`.  q|k|v come from
-// qkv [tokens][3 dm] f32 (head h at columns h*hd, dm + h*hd, 2 dm + h*hd).  Per query row:
+// `blockIdx.x` = rows [win[2i], win[2i] + win[2i+1]), head `blockIdx.y`, query rows
+// [AUDIO_ATTN_QB * blockIdx.z, +AUDIO_ATTN_QB) of the window.  q|k|v come from qkv
+// [tokens][3 dm] f32 (head h at columns h*hd, dm + h*hd, 2 dm + h*hd).  Per query row:
 // s_j = (q . k_j) * scale (the dot summed over dims in order, one rounding per step, like
 // the reference), softmax with the row max, p_j = exp(s_j - max), inv = 1 / sum p,
 // out = sum_j (p_j * inv) v_j summed over keys in order; out is rounded to f16 (the
-// out_proj operand).  K and V of the window sit in shared memory (row stride hd + 1:
-// conflict-free column reads) when they fit, else they are read from global memory.
+// out_proj operand).  The CTA's q rows and, when they fit, the window's K (rows padded to
+// hd + 4 floats: lane j reads key j's 16-byte vectors without bank conflicts) and V come
+// into shared memory with cp.async, every copy in flight at once; otherwise K and V are
+// read from global memory.  A warp takes two query rows at a time and a lane four keys at
+// a time, so each K / V read feeds several independent accumulation chains.
 constexpr int AUDIO_ATTN_THREADS = 256;
 constexpr int AUDIO_ATTN_WARPS = AUDIO_ATTN_THREADS / 32;
 constexpr int AUDIO_ATTN_MAX_HD = 128;
+constexpr int AUDIO_ATTN_QB = 16;  // query rows per CTA (two per warp)
 
 __host__ __device__ constexpr size_t audio_attn_smem_floats(int wlen, int hd, bool kv_in_smem) {
-  return (kv_in_smem ? static_cast<size_t>(2) * wlen * (hd + 1) : 0) +
-         static_cast<size_t>(AUDIO_ATTN_WARPS) * (wlen + hd);
+  return (kv_in_smem ? static_cast<size_t>(wlen) * (2 * hd + 4) : 0) + static_cast<size_t>(AUDIO_ATTN_QB) * hd +
+         static_cast<size_t>(AUDIO_ATTN_WARPS) * 2 * wlen;
 }
 
 template <bool KV_SMEM>
 __global__ void __launch_bounds__(AUDIO_ATTN_THREADS) audio_window_attention_kernel(
     const float* __restrict__ qkv, const int* __restrict__ win, int dm, int hd, float scale,
     int wmax, __half* __restrict__ out) {
-  extern __shared__ float at_smem[];
+  audio_pdl_entry();
+  extern __shared__ __align__(16) float at_smem[];
   const int start = win[2 * blockIdx.x], len = win[2 * blockIdx.x + 1];
+  const int r0 = blockIdx.z * AUDIO_ATTN_QB;
+  if (r0 >= len) return;
+  const int r1 = min(len, r0 + AUDIO_ATTN_QB);
   const int h = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long long ld = 3LL * dm;
-  const int ks = KV_SMEM ? hd + 1 : static_cast<int>(ld);  // row stride of K / V
-  const float* K;
-  const float* V;
-  float* pbase = at_smem + (KV_SMEM ? static_cast<size_t>(2) * wmax * (hd + 1) : 0);
+  const size_t ld = 3 * static_cast<size_t>(dm);
+  const int v4 = hd >> 2;  // 16-byte vectors per head row
+  const float* qkv_rows = qkv + static_cast<size_t>(start) * ld + h * hd;  // row r of the window: + r * ld
+  float* sk = at_smem;                                                      // [wmax][hd + 4]
+  float* sv = sk + (KV_SMEM ? static_cast<size_t>(wmax) * (hd + 4) : 0);   // [wmax][hd]
+  float* sq = sv + (KV_SMEM ? static_cast<size_t>(wmax) * hd : 0);         // [QB][hd]
+  float* p0 = sq + AUDIO_ATTN_QB * hd + static_cast<size_t>(warp) * 2 * wmax;  // [len] probabilities, row a
+  float* p1 = p0 + wmax;                                                        // row b
   if constexpr (KV_SMEM) {
-    float* sk = at_smem;
-    float* sv = at_smem + static_cast<size_t>(wmax) * (hd + 1);
-    for (int i = threadIdx.x; i < len * hd; i += blockDim.x) {
-      const int r = i / hd, d = i - r * hd;
-      const float* row = qkv + (start + r) * ld + h * hd + d;
-      sk[r * (hd + 1) + d] = row[dm];
-      sv[r * (hd + 1) + d] = row[2 * dm];
+    for (int i = threadIdx.x; i < len * v4; i += blockDim.x) {
+      const int r = i / v4, c = (i - r * v4) * 4;
+      const float* row = qkv_rows + r * ld + c;
+      cp_async16(sk + r * (hd + 4) + c, row + dm);
+      cp_async16(sv + r * hd + c, row + 2 * dm);
     }
-    __syncthreads();
-    K = sk;
-    V = sv;
-  } else {
-    K = qkv + start * ld + dm + h * hd;
-    V = qkv + start * ld + 2 * dm + h * hd;
   }
-  float* p = pbase + static_cast<size_t>(warp) * (wmax + hd);  // [len] probabilities
-  float* qs = p + wmax;                                         // [hd] this row's q
-  for (int r = warp; r < len; r += AUDIO_ATTN_WARPS) {
-    const float* qrow = qkv + (start + r) * ld + h * hd;
-    for (int d = lane; d < hd; d += 32) qs[d] = qrow[d];
-    __syncwarp();
-    float mx = -INFINITY;
-    for (int j = lane; j < len; j += 32) {
-      const float* kr = K + static_cast<long long>(j) * ks;
-      float dot = 0.0f;
-      for (int d = 0; d < hd; ++d) dot = __fadd_rn(dot, __fmul_rn(qs[d], kr[d]));
-      const float sc = __fmul_rn(dot, scale);
-      p[j] = sc;
-      mx = fmaxf(mx, sc);
+  for (int i = threadIdx.x; i < (r1 - r0) * v4; i += blockDim.x) {
+    const int r = i / v4, c = (i - r * v4) * 4;
+    cp_async16(sq + r * hd + c, qkv_rows + (r0 + r) * ld + c);
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  const float* K = KV_SMEM ? sk : qkv_rows + dm;
+  const float* V = KV_SMEM ? sv : qkv_rows + 2 * dm;
+  const size_t ks = KV_SMEM ? static_cast<size_t>(hd + 4) : ld;
+  const size_t vs = KV_SMEM ? static_cast<size_t>(hd) : ld;
+  for (int ra = r0 + 2 * warp; ra < r1; ra += 2 * AUDIO_ATTN_WARPS) {
+    const bool two = ra + 1 < r1;  // row b = ra + 1 (or a repeat of row a, discarded)
+    const float4* qa = reinterpret_cast<const float4*>(sq + (ra - r0) * hd);
+    const float4* qb = two ? qa + v4 : qa;
+    float mxa = -INFINITY, mxb = -INFINITY;
+    for (int j0 = 0; j0 < len; j0 += 128) {
+      const float4* kp[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int j = j0 + lane + 32 * t;
+        kp[t] = reinterpret_cast<const float4*>(K + static_cast<size_t>(j < len ? j : 0) * ks);
+      }
+      float da[4] = {0.f, 0.f, 0.f, 0.f}, db[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int c = 0; c < v4; ++c) {
+        const float4 x = qa[c], y = qb[c];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const float4 kv = kp[t][c];
+          da[t] = __fadd_rn(da[t], __fmul_rn(x.x, kv.x));
+          db[t] = __fadd_rn(db[t], __fmul_rn(y.x, kv.x));
+          da[t] = __fadd_rn(da[t], __fmul_rn(x.y, kv.y));
+          db[t] = __fadd_rn(db[t], __fmul_rn(y.y, kv.y));
+          da[t] = __fadd_rn(da[t], __fmul_rn(x.z, kv.z));
+          db[t] = __fadd_rn(db[t], __fmul_rn(y.z, kv.z));
+          da[t] = __fadd_rn(da[t], __fmul_rn(x.w, kv.w));
+          db[t] = __fadd_rn(db[t], __fmul_rn(y.w, kv.w));
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int j = j0 + lane + 32 * t;
+        if (j < len) {
+          const float sa = __fmul_rn(da[t], scale), sb = __fmul_rn(db[t], scale);
+          p0[j] = sa;
+          p1[j] = sb;
+          mxa = fmaxf(mxa, sa);
+          mxb = fmaxf(mxb, sb);
+        }
+      }
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float sum = 0.0f;
+    for (int o = 16; o > 0; o >>= 1) {
+      mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, o));
+      mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, o));
+    }
+    float suma = 0.0f, sumb = 0.0f;
     for (int j = lane; j < len; j += 32) {
-      const float e = expf(__fsub_rn(p[j], mx));
-      p[j] = e;
-      sum = __fadd_rn(sum, e);
+      const float ea = expf(__fsub_rn(p0[j], mxa)), eb = expf(__fsub_rn(p1[j], mxb));
+      p0[j] = ea;
+      p1[j] = eb;
+      suma = __fadd_rn(suma, ea);
+      sumb = __fadd_rn(sumb, eb);
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
-    const float inv = __fdiv_rn(1.0f, sum);
+    for (int o = 16; o > 0; o >>= 1) {
+      suma = __fadd_rn(suma, __shfl_xor_sync(0xffffffffu, suma, o));
+      sumb = __fadd_rn(sumb, __shfl_xor_sync(0xffffffffu, sumb, o));
+    }
+    const float inva = __fdiv_rn(1.0f, suma), invb = __fdiv_rn(1.0f, sumb);
     __syncwarp();
-    float acc[AUDIO_ATTN_MAX_HD / 32];
+    float acca[AUDIO_ATTN_MAX_HD / 32], accb[AUDIO_ATTN_MAX_HD / 32];
 #pragma unroll
-    for (int i = 0; i < AUDIO_ATTN_MAX_HD / 32; ++i) acc[i] = 0.0f;
+    for (int i = 0; i < AUDIO_ATTN_MAX_HD / 32; ++i) acca[i] = accb[i] = 0.0f;
     for (int j = 0; j < len; ++j) {
-      const float wj = __fmul_rn(p[j], inv);
-      const float* vr = V + static_cast<long long>(j) * ks;
+      const float wa = __fmul_rn(p0[j], inva), wb = __fmul_rn(p1[j], invb);
+      const float* vr = V + j * vs;
 #pragma unroll
-      for (int i = 0; i < AUDIO_ATTN_MAX_HD / 32; ++i)
-        if (lane + 32 * i < hd) acc[i] = __fadd_rn(acc[i], __fmul_rn(wj, vr[lane + 32 * i]));
+      for (int i = 0; i < AUDIO_ATTN_MAX_HD / 32; ++i) {
+        if (lane + 32 * i < hd) {
+          const float vv = vr[lane + 32 * i];
+          acca[i] = __fadd_rn(acca[i], __fmul_rn(wa, vv));
+          accb[i] = __fadd_rn(accb[i], __fmul_rn(wb, vv));
+        }
+      }
     }
-    __half* orow = out + static_cast<long long>(start + r) * dm + h * hd;
+    __half* oa = out + static_cast<size_t>(start + ra) * dm + h * hd;
 #pragma unroll
-    for (int i = 0; i < AUDIO_ATTN_MAX_HD / 32; ++i)
-      if (lane + 32 * i < hd) orow[lane + 32 * i] = __float2half_rn(acc[i]);
+    for (int i = 0; i < AUDIO_ATTN_MAX_HD / 32; ++i) {
+      if (lane + 32 * i < hd) {
+        oa[lane + 32 * i] = __float2half_rn(acca[i]);
+        if (two) oa[dm + lane + 32 * i] = __float2half_rn(accb[i]);
+      }
+    }
     __syncwarp();
   }
 }

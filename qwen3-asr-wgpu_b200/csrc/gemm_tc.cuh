@@ -44,7 +44,6 @@ enum EpiKind : int {
   EPI_BIAS_F16 = 5,      // out[r, m] = f16(acc + bias[m])
   EPI_BIAS_GELU = 6,     // out[r, m] = f16(gelu(acc + bias[m])), gelu = 0.5 x (1 + erf(x / sqrt 2))
   EPI_BIAS_F32 = 7,      // out32[r, m] = acc + bias[m]
-  EPI_BIAS_RESID32 = 8,  // out32[r, m] = out32[r, m] + (acc + bias[m])  (f32 residual stream)
 };
 
 constexpr int GEMM_BUILD_GROUPS = 2;  // int8 A-builder warpgroups
@@ -189,13 +188,19 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, EpiSmem& es, i
       if (n < a.rows) a.out[static_cast<size_t>(n) * a.ldo + mt * 128 + e] = __float2half_rn(v[j]);
     }
   } else if constexpr (EPI == EPI_RESID) {
+    // all 16 residual reads in flight before the first write (a read after a write to the
+    // same array would otherwise wait for it)
+    __half old[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       const int n = nbase + j;
-      if (n < a.rows) {
-        __half* p = a.out + static_cast<size_t>(n) * a.ldo + mt * 128 + e;
-        *p = __float2half_rn(__fadd_rn(__half2float(*p), v[j]));
-      }
+      old[j] = n < a.rows ? a.out[static_cast<size_t>(n) * a.ldo + mt * 128 + e] : __float2half_rn(0.0f);
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int n = nbase + j;
+      if (n < a.rows)
+        a.out[static_cast<size_t>(n) * a.ldo + mt * 128 + e] = __float2half_rn(__fadd_rn(__half2float(old[j]), v[j]));
     }
   } else if constexpr (EPI == EPI_SILU) {
     // tile mt: rows [0,64) = gate[mt*64 + i], rows [64,128) = up[mt*64 + i]
@@ -274,8 +279,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, EpiSmem& es, i
       }
     }
     named_bar_sync(1, 128);
-  } else if constexpr (EPI == EPI_BIAS_F16 || EPI == EPI_BIAS_GELU || EPI == EPI_BIAS_F32 ||
-                       EPI == EPI_BIAS_RESID32) {
+  } else if constexpr (EPI == EPI_BIAS_F16 || EPI == EPI_BIAS_GELU || EPI == EPI_BIAS_F32) {
     const int m = mt * 128 + e;
     const float b = a.bias != nullptr ? a.bias[m] : 0.0f;
 #pragma unroll
@@ -288,11 +292,8 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, EpiSmem& es, i
         } else if constexpr (EPI == EPI_BIAS_GELU) {
           const float g = __fmul_rn(__fmul_rn(0.5f, y), __fadd_rn(1.0f, erff(__fmul_rn(y, 0.70710678118654752f))));
           a.out[static_cast<size_t>(n) * a.ldo + m] = __float2half_rn(g);
-        } else if constexpr (EPI == EPI_BIAS_F32) {
-          a.out32[static_cast<size_t>(n) * a.ldo32 + m] = y;
         } else {
-          float* p = a.out32 + static_cast<size_t>(n) * a.ldo32 + m;
-          *p = __fadd_rn(*p, y);
+          a.out32[static_cast<size_t>(n) * a.ldo32 + m] = y;
         }
       }
     }
@@ -719,34 +720,29 @@ __global__ void __launch_bounds__(gemm_threads(INT8), 1)
             float4 acc[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-            // SEGU segments per round: SEGU * 4 independent 16-byte loads in flight
+            // SEGU segments per round, SEGU * 4 independent 16-byte loads in flight (a short
+            // last round loads only its segments); partials are added in segment order
             constexpr int SEGU = INT8 ? 2 : 4;  // the int8 CTA has more threads: fewer registers
-            int sg = 0;
-            for (; sg + SEGU <= nseg; sg += SEGU) {
+            for (int sg = 0; sg < nseg; sg += SEGU) {
               float4 p[SEGU][4];
 #pragma unroll
               for (int q = 0; q < SEGU; ++q)
 #pragma unroll
                 for (int j = 0; j < 4; ++j)
-                  p[q][j] = __ldcg(reinterpret_cast<const float4*>(rowp + (sg + q) * tile_elems + c0 + 4 * j));
+                  p[q][j] = sg + q < nseg
+                                ? __ldcg(reinterpret_cast<const float4*>(rowp + (sg + q) * tile_elems + c0 + 4 * j))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-              for (int q = 0; q < SEGU; ++q)
+              for (int q = 0; q < SEGU; ++q) {
+                if (sg + q < nseg) {
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                  acc[j].x += p[q][j].x;
-                  acc[j].y += p[q][j].y;
-                  acc[j].z += p[q][j].z;
-                  acc[j].w += p[q][j].w;
+                  for (int j = 0; j < 4; ++j) {
+                    acc[j].x += p[q][j].x;
+                    acc[j].y += p[q][j].y;
+                    acc[j].z += p[q][j].z;
+                    acc[j].w += p[q][j].w;
+                  }
                 }
-            }
-            for (; sg < nseg; ++sg) {
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const float4 p = __ldcg(reinterpret_cast<const float4*>(rowp + sg * tile_elems + c0 + 4 * j));
-                acc[j].x += p.x;
-                acc[j].y += p.y;
-                acc[j].z += p.z;
-                acc[j].w += p.w;
               }
             }
             float v[16];

@@ -117,7 +117,8 @@ struct GemmShape {
   size_t smem, ws_floats;
 };
 
-inline GemmShape gemm_shape(int n_out, int k, bool int8, int rows, int num_sms) {
+// grid_override > 0 fixes the CTA count (at most num_sms); otherwise at least 4 units per CTA.
+inline GemmShape gemm_shape(int n_out, int k, bool int8, int rows, int num_sms, int grid_override = 0) {
   GemmShape s{};
   s.n_tile = rows <= GEMM_MAX_NTILE ? std::max(16, (rows + 15) / 16 * 16) : GEMM_MAX_NTILE;
   s.n_tiles = (rows + s.n_tile - 1) / s.n_tile;
@@ -127,7 +128,8 @@ inline GemmShape gemm_shape(int n_out, int k, bool int8, int rows, int num_sms) 
   s.units = s.tiles * s.kblocks;
   // at least 4 units per CTA: a CTA that streams less than ~64 KB of weights spends
   // more on its pipeline fill and split fixup than on the bytes
-  s.grid = std::max(1, std::min(num_sms, s.units / 4));
+  s.grid = grid_override > 0 ? std::min(grid_override, std::min(num_sms, s.units))
+                              : std::max(1, std::min(num_sms, s.units / 4));
   const int atoms = int8 ? 2 : 1;
   const int stage = 16384 + atoms * s.n_tile * 128;
   const int dyn = g_dyn_smem_max > 0 ? g_dyn_smem_max : 200 * 1024;
