@@ -105,6 +105,13 @@ qasr_status qasr_audio_encode_batch(qasr_audio_ctx* ctx, int32_t n, const float*
  * failures. */
 qasr_status qasr_audio_encode_device(qasr_audio_ctx* ctx, const float* mel_dev, int32_t n_mels,
                                      int32_t n_frames, uint16_t* out_dev, int32_t* n_tokens);
+/* encode_batch for device-resident mels: mels_dev[i] f32 [n_mels][n_frames[i]] on the
+ * context's device; out_dev f16 receives every utterance's rows back to back (utterance i
+ * starts after the rows of 0..i-1); n_tokens (optional, host) receives each utterance's
+ * row count.  Enqueued on the context's stream like qasr_audio_encode_device. */
+qasr_status qasr_audio_encode_batch_device(qasr_audio_ctx* ctx, int32_t n, const float* const* mels_dev,
+                                           const int32_t* n_frames, int32_t n_mels, uint16_t* out_dev,
+                                           int32_t* n_tokens);
 qasr_status qasr_audio_sync(qasr_audio_ctx* ctx);
 void* qasr_audio_stream(qasr_audio_ctx* ctx);
 /* Kernel launches issued by the audio tower so far (all of them this library's own). */

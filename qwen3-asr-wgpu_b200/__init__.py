@@ -68,7 +68,7 @@ EXPORTED_SYMBOLS = (
     # include/qasr_b200_audio.h
     "qasr_audio_token_count", "qasr_audio_create", "qasr_audio_destroy", "qasr_audio_last_error",
     "qasr_audio_load_weights", "qasr_audio_load_checkpoint", "qasr_audio_encode", "qasr_audio_encode_batch",
-    "qasr_audio_encode_device", "qasr_audio_sync", "qasr_audio_stream", "qasr_audio_launch_count",
+    "qasr_audio_encode_device", "qasr_audio_encode_batch_device", "qasr_audio_sync", "qasr_audio_stream", "qasr_audio_launch_count",
 )
 
 

@@ -73,6 +73,7 @@ def _bind():
     lib.qasr_audio_encode.argtypes = [P, P, I32, I32, P, I32, ctypes.POINTER(I32)]
     lib.qasr_audio_encode_batch.argtypes = [P, I32, P, P, I32, P]
     lib.qasr_audio_encode_device.argtypes = [P, P, I32, I32, P, ctypes.POINTER(I32)]
+    lib.qasr_audio_encode_batch_device.argtypes = [P, I32, P, P, I32, P, P]
     lib.qasr_audio_sync.argtypes = [P]
     lib.qasr_audio_stream.argtypes = [P]
     lib.qasr_audio_stream.restype = P
@@ -284,6 +285,16 @@ class AudioEncoder:
         self._check(lib.qasr_audio_encode_device(self._h, ctypes.c_void_p(mel_ptr), self.cfg["num_mel_bins"],
                                                  int(n_frames), ctypes.c_void_p(out_ptr), ctypes.byref(n)))
         return n.value
+
+    def encode_batch_device(self, mel_ptrs, n_frames, out_ptr: int):
+        """Device-resident encode_batch, enqueued on ``self.stream``: the utterances' rows land
+        back to back at ``out_ptr``; returns each utterance's token count."""
+        mp = (ctypes.c_void_p * len(mel_ptrs))(*mel_ptrs)
+        nf = np.ascontiguousarray(n_frames, dtype=np.int32)
+        nt = np.zeros(len(mel_ptrs), np.int32)
+        self._check(lib.qasr_audio_encode_batch_device(self._h, len(mel_ptrs), mp, _ptr(nf),
+                                                       self.cfg["num_mel_bins"], ctypes.c_void_p(out_ptr), _ptr(nt)))
+        return nt.tolist()
 
     def sync(self):
         self._check(lib.qasr_audio_sync(self._h))

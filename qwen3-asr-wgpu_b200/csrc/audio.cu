@@ -205,7 +205,8 @@ bool check_config(const qasr_audio_config& g, std::string* why) {
              128 * AUDIO_LN_MAXV);
     return bad(b);
   }
-  if (g.downsample_hidden_size % 8) return bad("downsample_hidden_size must be a multiple of 8");
+  if (g.downsample_hidden_size % 8 || g.downsample_hidden_size > 2048)
+    return bad("downsample_hidden_size must be a multiple of 8, at most 2048");
   const int h3 = conv_len(conv_len(conv_len(g.num_mel_bins)));
   if ((g.downsample_hidden_size * h3) % 64) {
     snprintf(b, sizeof b, "conv_out width %d x %d is not a multiple of 64", g.downsample_hidden_size, h3);
@@ -334,15 +335,15 @@ qasr_status reserve_gemm(qasr_audio_ctx* c, const std::vector<std::pair<const AL
 }
 
 struct Utt {
-  const float* mel;  // host or device
+  const float* mel;  // the caller's (host or device) mel
   int n_frames;
-  size_t mel_off;    // element offset in the mel buffer
+  const float* mel_dev;  // the same mel on the device
   int tok0, ntok;
 };
 
-// The whole tower over `utts` (mel already on the device at `mel_dev` + mel_off) into
-// out [tokens][out_dim] f16 on the device.  Enqueue only.
-qasr_status run_tower(qasr_audio_ctx* c, const float* mel_dev, std::vector<Utt>& utts, __half* out) {
+// The whole tower over `utts` (each mel already on the device at `mel_dev`) into
+// out [tokens][out_dim] f16 on the device, the utterances' rows back to back.  Enqueue only.
+qasr_status run_tower(qasr_audio_ctx* c, std::vector<Utt>& utts, __half* out) {
   const qasr_audio_config& g = c->cfg;
   c->h_chunks.clear();
   c->h_win.clear();
@@ -353,7 +354,7 @@ qasr_status run_tower(qasr_audio_ctx* c, const float* mel_dev, std::vector<Utt>&
     u.tok0 = tokens;
     for (int i = 0; i < n_chunks; ++i) {
       AudioChunk k{};
-      k.mel_off = static_cast<int>(u.mel_off);
+      k.mel = u.mel_dev;
       k.n_frames = u.n_frames;
       k.frame0 = i * c->cs;
       k.valid = i < nfull ? c->cs : tail;
@@ -419,10 +420,12 @@ qasr_status run_tower(qasr_audio_ctx* c, const float* mel_dev, std::vector<Utt>&
   for (int r0 = 0; r0 < n_chunks; r0 += R) {
     const int n = std::min(R, n_chunks - r0);
     const AudioChunk* ch = P<AudioChunk>(c->chunks) + r0;
+    const int c1_block = audio_conv1_block(c->C / 8);
+    const long long c1_items = static_cast<long long>(n) * c->h1 * ((c->w1 + AUDIO_C1_POS - 1) / AUDIO_C1_POS);
     ACK(launch_k(audio_conv1_kernel,
-                 dim3(grid_for(static_cast<long long>(n) * c->h1 * ((c->w1 + AUDIO_C1_POS - 1) / AUDIO_C1_POS) *
-                               (c->C / 8))),
-                 dim3(256), 0, c->stream, true, mel_dev, ch, n, g.num_mel_bins, c->h1, c->w1,
+                 dim3(static_cast<unsigned>(std::min<long long>(
+                     std::max<long long>(1, c1_items / (c1_block / (c->C / 8)) + 1), 8LL * sms))),
+                 dim3(c1_block), 0, c->stream, true, ch, n, g.num_mel_bins, c->h1, c->w1,
                  static_cast<const float*>(c->c1_w), static_cast<const float*>(c->c1_b), c->C, P<__half>(c->act1),
                  c->ldc),
         "conv1 launch");
@@ -763,9 +766,29 @@ qasr_status qasr_audio_encode_device(qasr_audio_ctx* c, const float* mel_dev, in
   if (n_mels != c->cfg.num_mel_bins)
     return afail(c, QASR_ERR_INVALID_ARG, "mel bins %d != %d", n_mels, c->cfg.num_mel_bins);
   if (n_frames <= 0) return afail(c, QASR_ERR_INVALID_ARG, "empty mel");
-  std::vector<Utt> utts{{mel_dev, n_frames, 0, 0, 0}};
-  if ((s = run_tower(c, mel_dev, utts, reinterpret_cast<__half*>(out_dev)))) return s;
+  std::vector<Utt> utts{{mel_dev, n_frames, mel_dev, 0, 0}};
+  if ((s = run_tower(c, utts, reinterpret_cast<__half*>(out_dev)))) return s;
   if (n_tokens) *n_tokens = utts[0].ntok;
+  return QASR_OK;
+}
+
+qasr_status qasr_audio_encode_batch_device(qasr_audio_ctx* c, int32_t n, const float* const* mels_dev,
+                                           const int32_t* n_frames, int32_t n_mels, uint16_t* out_dev,
+                                           int32_t* n_tokens) {
+  if (!c || n <= 0 || !mels_dev || !n_frames || !out_dev) return QASR_ERR_INVALID_ARG;
+  qasr_status s = begin(c);
+  if (s) return s;
+  if (n_mels != c->cfg.num_mel_bins)
+    return afail(c, QASR_ERR_INVALID_ARG, "mel bins %d != %d", n_mels, c->cfg.num_mel_bins);
+  std::vector<Utt> utts(static_cast<size_t>(n));
+  for (int i = 0; i < n; ++i) {
+    if (!mels_dev[i]) return afail(c, QASR_ERR_INVALID_ARG, "utterance %d: null buffer", i);
+    if (n_frames[i] <= 0) return afail(c, QASR_ERR_INVALID_ARG, "utterance %d: empty mel", i);
+    utts[static_cast<size_t>(i)] = Utt{mels_dev[i], n_frames[i], mels_dev[i], 0, 0};
+  }
+  if ((s = run_tower(c, utts, reinterpret_cast<__half*>(out_dev)))) return s;
+  if (n_tokens)
+    for (int i = 0; i < n; ++i) n_tokens[i] = utts[static_cast<size_t>(i)].ntok;
   return QASR_OK;
 }
 
@@ -789,19 +812,22 @@ qasr_status qasr_audio_encode_batch(qasr_audio_ctx* c, int32_t n, const float* c
   for (int i = 0; i < n; ++i) {
     if (!mels[i] || !outs[i]) return afail(c, QASR_ERR_INVALID_ARG, "utterance %d: null buffer", i);
     if (n_frames[i] <= 0) return afail(c, QASR_ERR_INVALID_ARG, "utterance %d: empty mel", i);
-    utts[static_cast<size_t>(i)] = Utt{mels[i], n_frames[i], off, 0, 0};
+    utts[static_cast<size_t>(i)] = Utt{mels[i], n_frames[i], nullptr, 0, 0};
     off += static_cast<size_t>(n_mels) * n_frames[i];
     tokens += qasr_audio_token_count(&c->cfg, n_frames[i]);
   }
-  if (off > static_cast<size_t>(INT32_MAX)) return afail(c, QASR_ERR_CAPACITY, "mel input too long");
   if ((s = grow(c, c->mel, off * sizeof(float), "mel input")) ||
       (s = grow(c, c->out16, 2ull * tokens * c->out_dim, "embeddings")))
     return s;
-  for (const Utt& u : utts)
-    ACK(cudaMemcpyAsync(P<float>(c->mel) + u.mel_off, u.mel, sizeof(float) * n_mels * u.n_frames,
-                        cudaMemcpyHostToDevice, c->stream),
+  off = 0;
+  for (Utt& u : utts) {
+    u.mel_dev = P<float>(c->mel) + off;
+    ACK(cudaMemcpyAsync(P<float>(c->mel) + off, u.mel, sizeof(float) * n_mels * u.n_frames, cudaMemcpyHostToDevice,
+                        c->stream),
         "mel upload");
-  if ((s = run_tower(c, P<float>(c->mel), utts, P<__half>(c->out16)))) return s;
+    off += static_cast<size_t>(n_mels) * u.n_frames;
+  }
+  if ((s = run_tower(c, utts, P<__half>(c->out16)))) return s;
   for (int i = 0; i < n; ++i) {
     const Utt& u = utts[static_cast<size_t>(i)];
     ACK(cudaMemcpyAsync(outs[i], P<uint16_t>(c->out16) + static_cast<size_t>(u.tok0) * c->out_dim,

@@ -54,7 +54,7 @@ __device__ __forceinline__ float audio_gelu(float y) {
 // One conv chunk: n_window * 2 mel frames of one utterance (the tail chunk zero-padded),
 // src/audio_encoder.rs:702-735.
 struct AudioChunk {
-  int mel_off;   // element offset of the utterance's mel [n_mels][n_frames] in the mel buffer
+  const float* mel;  // the utterance's mel [n_mels][n_frames]
   int n_frames;  // the utterance's frame count (row length of its mel)
   int frame0;    // first frame of the chunk
   int valid;     // frames of the chunk that exist (cs, or the tail)
@@ -63,39 +63,41 @@ struct AudioChunk {
 };
 
 // conv2d1 + bias + GELU over the chunks [0, n) of the current round: out[chunk][ho][wo][c].
-// One thread computes 8 channels at AUDIO_C1_POS consecutive output columns of one output
-// row, holding the 8 x 9 weights in registers; the 9 taps are summed in (kh, kw) order in
-// f32.  x beyond the chunk's valid frames or outside the mel bins is 0 (the chunk buffer's
-// zero fill and the conv padding, src/audio_encoder.rs:185-225).  Index arithmetic is 32-bit
-// (a round holds < 2^31 outputs; the host checks): a 64-bit division is a long software
-// sequence.
-constexpr int AUDIO_C1_POS = 4;
-__global__ void __launch_bounds__(256, 2) audio_conv1_kernel(const float* __restrict__ mel,
-                                                          const AudioChunk* __restrict__ chunks, int n,
-                                                          int n_mels, int h1, int w1,
-                                                          const float* __restrict__ w /*[C][9]*/,
-                                                          const float* __restrict__ bias, int C,
-                                                          __half* __restrict__ out, int ldc) {
+// A thread owns one group of 8 channels for its whole grid-stride loop (the block is a
+// multiple of the group count, so the group is fixed per thread) and holds those 8 x 9
+// weights in registers, loaded once; each item is AUDIO_C1_POS consecutive output columns of
+// one output row.  The 9 taps are summed in (kh, kw) order in f32.  x beyond the chunk's
+// valid frames or outside the mel bins is 0 (the chunk buffer's zero fill and the conv
+// padding, src/audio_encoder.rs:185-225).  Index arithmetic is 32-bit (a round holds
+// < 2^31 outputs; the host checks): a 64-bit division is a long software sequence.
+constexpr int AUDIO_C1_POS = 2;
+__host__ __device__ constexpr int audio_conv1_block(int groups) { return groups * (256 / groups); }
+__global__ void __launch_bounds__(256, 2) audio_conv1_kernel(const AudioChunk* __restrict__ chunks, int n,
+                                                             int n_mels, int h1, int w1,
+                                                             const float* __restrict__ w /*[C][9]*/,
+                                                             const float* __restrict__ bias, int C,
+                                                             __half* __restrict__ out, int ldc) {
   audio_pdl_entry();
   const unsigned groups = static_cast<unsigned>(C) >> 3;
-  const unsigned wq = (static_cast<unsigned>(w1) + AUDIO_C1_POS - 1) / AUDIO_C1_POS;  // column quads per row
-  const unsigned total = static_cast<unsigned>(n) * h1 * wq * groups;
-  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
-    const int g = static_cast<int>(i % groups);
-    const unsigned rest = i / groups;
-    const int wo0 = static_cast<int>(rest % wq) * AUDIO_C1_POS;
-    const unsigned row = rest / wq;  // chunk * h1 + ho
+  const unsigned per_block = blockDim.x / groups;  // items of one group in flight per block
+  if (threadIdx.x >= per_block * groups) return;
+  const int g = static_cast<int>(threadIdx.x % groups);
+  float wr[8][9], br[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+#pragma unroll
+    for (int t = 0; t < 9; ++t) wr[j][t] = __ldg(w + (g * 8 + j) * 9 + t);
+    br[j] = __ldg(bias + g * 8 + j);
+  }
+  const unsigned wq = (static_cast<unsigned>(w1) + AUDIO_C1_POS - 1) / AUDIO_C1_POS;  // column groups per row
+  const unsigned items = static_cast<unsigned>(n) * h1 * wq;
+  for (unsigned it = blockIdx.x * per_block + threadIdx.x / groups; it < items; it += gridDim.x * per_block) {
+    const int wo0 = static_cast<int>(it % wq) * AUDIO_C1_POS;
+    const unsigned row = it / wq;  // chunk * h1 + ho
     const int ho = static_cast<int>(row % static_cast<unsigned>(h1));
     const int ch = static_cast<int>(row / static_cast<unsigned>(h1));
     const AudioChunk k = chunks[ch];
-    float wr[8][9], br[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-#pragma unroll
-      for (int t = 0; t < 9; ++t) wr[j][t] = __ldg(w + (g * 8 + j) * 9 + t);
-      br[j] = __ldg(bias + g * 8 + j);
-    }
-    // the 3 mel rows x (2 * AUDIO_C1_POS + 1) frames this strip reads
+    // the 3 mel rows x (2 * AUDIO_C1_POS + 1) frames this item reads
     float x[3][2 * AUDIO_C1_POS + 1];
 #pragma unroll
     for (int kh = 0; kh < 3; ++kh) {
@@ -104,26 +106,27 @@ __global__ void __launch_bounds__(256, 2) audio_conv1_kernel(const float* __rest
       for (int f = 0; f < 2 * AUDIO_C1_POS + 1; ++f) {
         const int fr = wo0 * 2 - 1 + f;
         x[kh][f] = (mb >= 0 && mb < n_mels && fr >= 0 && fr < k.valid)
-                       ? __ldg(mel + k.mel_off + static_cast<size_t>(mb) * k.n_frames + k.frame0 + fr)
+                       ? __ldg(k.mel + static_cast<size_t>(mb) * k.n_frames + k.frame0 + fr)
                        : 0.0f;
       }
     }
 #pragma unroll
     for (int q = 0; q < AUDIO_C1_POS; ++q) {
       const int wo = wo0 + q;
-      if (wo >= w1) break;
-      alignas(16) __half o[8];
+      if (wo < w1) {
+        alignas(16) __half o[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float acc = 0.0f;
+        for (int j = 0; j < 8; ++j) {
+          float acc = 0.0f;
 #pragma unroll
-        for (int kh = 0; kh < 3; ++kh)
+          for (int kh = 0; kh < 3; ++kh)
 #pragma unroll
-          for (int kw = 0; kw < 3; ++kw) acc = __fadd_rn(acc, __fmul_rn(wr[j][kh * 3 + kw], x[kh][2 * q + kw]));
-        o[j] = __float2half_rn(audio_gelu(__fadd_rn(acc, br[j])));
+            for (int kw = 0; kw < 3; ++kw) acc = __fadd_rn(acc, __fmul_rn(wr[j][kh * 3 + kw], x[kh][2 * q + kw]));
+          o[j] = __float2half_rn(audio_gelu(__fadd_rn(acc, br[j])));
+        }
+        *reinterpret_cast<uint4*>(out + (static_cast<size_t>(row) * w1 + wo) * ldc + g * 8) =
+            *reinterpret_cast<const uint4*>(o);
       }
-      *reinterpret_cast<uint4*>(out + (static_cast<size_t>(row) * w1 + wo) * ldc + g * 8) =
-          *reinterpret_cast<const uint4*>(o);
     }
   }
 }
@@ -259,10 +262,11 @@ __global__ void __launch_bounds__(256) audio_residual_layernorm_kernel(float* __
 // `blockIdx.x` = rows [win[2i], win[2i] + win[2i+1]), head `blockIdx.y`, query rows
 // [AUDIO_ATTN_QB * blockIdx.z, +AUDIO_ATTN_QB) of the window.  q|k|v come from qkv
 // [tokens][3 dm] f32 (head h at columns h*hd, dm + h*hd, 2 dm + h*hd).  Per query row:
-// s_j = (q . k_j) * scale (the dot summed over dims in order, one rounding per step, like
-// the reference), softmax with the row max, p_j = exp(s_j - max), inv = 1 / sum p,
-// out = sum_j (p_j * inv) v_j summed over keys in order; out is rounded to f16 (the
-// out_proj operand).  The CTA's q rows and, when they fit, the window's K (rows padded to
+// s_j = (q . k_j) * scale (the dot summed over dims in order, like
+// the reference, but each step a fused multiply-add, so a dot can differ from the
+// reference's in the last bit), softmax with the row max, p_j = exp(s_j - max),
+// inv = 1 / sum p, out = sum_j (p_j * inv) v_j summed over keys in order (fused
+// multiply-adds); out is rounded to f16 (the out_proj operand).  The CTA's q rows and, when they fit, the window's K (rows padded to
 // hd + 4 floats: lane j reads key j's 16-byte vectors without bank conflicts) and V come
 // into shared memory with cp.async, every copy in flight at once; otherwise K and V are
 // read from global memory.  A warp takes two query rows at a time and a lane four keys at
@@ -333,14 +337,14 @@ __global__ void __launch_bounds__(AUDIO_ATTN_THREADS) audio_window_attention_ker
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
           const float4 kv = kp[t][c];
-          da[t] = __fadd_rn(da[t], __fmul_rn(x.x, kv.x));
-          db[t] = __fadd_rn(db[t], __fmul_rn(y.x, kv.x));
-          da[t] = __fadd_rn(da[t], __fmul_rn(x.y, kv.y));
-          db[t] = __fadd_rn(db[t], __fmul_rn(y.y, kv.y));
-          da[t] = __fadd_rn(da[t], __fmul_rn(x.z, kv.z));
-          db[t] = __fadd_rn(db[t], __fmul_rn(y.z, kv.z));
-          da[t] = __fadd_rn(da[t], __fmul_rn(x.w, kv.w));
-          db[t] = __fadd_rn(db[t], __fmul_rn(y.w, kv.w));
+          da[t] = __fmaf_rn(x.x, kv.x, da[t]);
+          db[t] = __fmaf_rn(y.x, kv.x, db[t]);
+          da[t] = __fmaf_rn(x.y, kv.y, da[t]);
+          db[t] = __fmaf_rn(y.y, kv.y, db[t]);
+          da[t] = __fmaf_rn(x.z, kv.z, da[t]);
+          db[t] = __fmaf_rn(y.z, kv.z, db[t]);
+          da[t] = __fmaf_rn(x.w, kv.w, da[t]);
+          db[t] = __fmaf_rn(y.w, kv.w, db[t]);
         }
       }
 #pragma unroll
@@ -375,27 +379,32 @@ __global__ void __launch_bounds__(AUDIO_ATTN_THREADS) audio_window_attention_ker
     }
     const float inva = __fdiv_rn(1.0f, suma), invb = __fdiv_rn(1.0f, sumb);
     __syncwarp();
-    float acca[AUDIO_ATTN_MAX_HD / 32], accb[AUDIO_ATTN_MAX_HD / 32];
+    // lane owns dims 2 lane + 64 i, +1 (hd is a multiple of 32: a lane's pair exists or not)
+    float2 acca[AUDIO_ATTN_MAX_HD / 64], accb[AUDIO_ATTN_MAX_HD / 64];
 #pragma unroll
-    for (int i = 0; i < AUDIO_ATTN_MAX_HD / 32; ++i) acca[i] = accb[i] = 0.0f;
+    for (int i = 0; i < AUDIO_ATTN_MAX_HD / 64; ++i) acca[i] = accb[i] = make_float2(0.f, 0.f);
     for (int j = 0; j < len; ++j) {
       const float wa = __fmul_rn(p0[j], inva), wb = __fmul_rn(p1[j], invb);
       const float* vr = V + j * vs;
 #pragma unroll
-      for (int i = 0; i < AUDIO_ATTN_MAX_HD / 32; ++i) {
-        if (lane + 32 * i < hd) {
-          const float vv = vr[lane + 32 * i];
-          acca[i] = __fadd_rn(acca[i], __fmul_rn(wa, vv));
-          accb[i] = __fadd_rn(accb[i], __fmul_rn(wb, vv));
+      for (int i = 0; i < AUDIO_ATTN_MAX_HD / 64; ++i) {
+        const int d = 2 * lane + 64 * i;
+        if (d < hd) {
+          const float2 vv = *reinterpret_cast<const float2*>(vr + d);
+          acca[i].x = __fmaf_rn(wa, vv.x, acca[i].x);
+          acca[i].y = __fmaf_rn(wa, vv.y, acca[i].y);
+          accb[i].x = __fmaf_rn(wb, vv.x, accb[i].x);
+          accb[i].y = __fmaf_rn(wb, vv.y, accb[i].y);
         }
       }
     }
     __half* oa = out + static_cast<size_t>(start + ra) * dm + h * hd;
 #pragma unroll
-    for (int i = 0; i < AUDIO_ATTN_MAX_HD / 32; ++i) {
-      if (lane + 32 * i < hd) {
-        oa[lane + 32 * i] = __float2half_rn(acca[i]);
-        if (two) oa[dm + lane + 32 * i] = __float2half_rn(accb[i]);
+    for (int i = 0; i < AUDIO_ATTN_MAX_HD / 64; ++i) {
+      const int d = 2 * lane + 64 * i;
+      if (d < hd) {
+        *reinterpret_cast<__half2*>(oa + d) = __floats2half2_rn(acca[i].x, acca[i].y);
+        if (two) *reinterpret_cast<__half2*>(oa + dm + d) = __floats2half2_rn(accb[i].x, accb[i].y);
       }
     }
     __syncwarp();

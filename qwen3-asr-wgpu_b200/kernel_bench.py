@@ -293,7 +293,9 @@ def bench_audio(args, pkg, torch):
     mel = pkg.synthetic_mel(cfg["num_mel_bins"], n_frames, seed=args.seed)
     T = enc.token_count(n_frames)
     mel_d = torch.from_numpy(mel).cuda()
-    out_d = torch.empty((T, cfg["output_dim"]), dtype=torch.float16, device="cuda")
+    out_d = torch.empty((T * args.batch, cfg["output_dim"]), dtype=torch.float16, device="cuda")
+    mels_b = [torch.from_numpy(pkg.synthetic_mel(cfg["num_mel_bins"], n_frames, seed=args.seed, index=i)).cuda()
+              for i in range(args.batch)] if args.batch > 1 else None
     st = torch.cuda.ExternalStream(enc.stream)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
     torch.cuda.synchronize()
@@ -304,23 +306,28 @@ def bench_audio(args, pkg, torch):
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(st)
             l0 = enc.launches
-            enc.encode_device(mel_d.data_ptr(), n_frames, out_d.data_ptr())
+            if mels_b is None:
+                enc.encode_device(mel_d.data_ptr(), n_frames, out_d.data_ptr())
+            else:
+                enc.encode_batch_device([m.data_ptr() for m in mels_b], [n_frames] * args.batch, out_d.data_ptr())
             launches = enc.launches - l0
             b.record(st)
         enc.sync()
         if it >= 3:
             times.append(a.elapsed_time(b) * 1e-3)
     e2e = []
-    for it in range(2 + args.e2e_iters if args.e2e_iters > 0 else 0):
+    for it in range(2 + args.e2e_iters if args.e2e_iters > 0 and args.batch == 1 else 0):
         t0 = time.perf_counter()
         enc.encode(mel)
         if it >= 2:
             e2e.append(time.perf_counter() - t0)
     med = statistics.median(times)
     T_, conv1, gemm, attn = audio_flops(pkg, cfg, n_frames)
-    res = {"kernel": "audio_tower", "model": args.model, "seconds": args.seconds, "frames": n_frames, "tokens": T,
-           "median_ms": med * 1e3, "best_ms": min(times) * 1e3, "launches": launches,
-           "audio_s_per_s": args.seconds / med, "gemm_gflop": gemm / 1e9, "attn_gflop": attn / 1e9,
+    B = args.batch
+    conv1, gemm, attn = conv1 * B, gemm * B, attn * B
+    res = {"kernel": "audio_tower", "model": args.model, "seconds": args.seconds, "batch": B, "frames": n_frames,
+           "tokens": T * B, "median_ms": med * 1e3, "best_ms": min(times) * 1e3, "launches": launches,
+           "audio_s_per_s": B * args.seconds / med, "gemm_gflop": gemm / 1e9, "attn_gflop": attn / 1e9,
            "conv1_gflop": conv1 / 1e9, "tflops": (gemm + attn + conv1) / med / 1e12,
            "e2e_median_ms": statistics.median(e2e) * 1e3 if e2e else None,
            "e2e_bytes": mel.nbytes + T * cfg["output_dim"] * 2}
@@ -361,6 +368,7 @@ def main(argv=None):
     au.add_argument("--seconds", type=float, default=30.0)
     au.add_argument("--seed", type=int, default=5)
     au.add_argument("--e2e-iters", type=int, default=5)
+    au.add_argument("--batch", type=int, default=1, help="clips per encode (encode_batch_device)")
     for p in sub.choices.values():
         p.add_argument("--iters", type=int, default=20)
     args = ap.parse_args(argv)

@@ -88,6 +88,26 @@ def test_batch_equals_lone_encodes(qasr, cuda_device):
     enc.close()
 
 
+def test_device_batch_equals_host_batch(qasr, cuda_device):
+    """qasr_audio_encode_batch_device (device mels, rows back to back) computes exactly what
+    qasr_audio_encode_batch computes from host memory."""
+    import torch
+    cfg = qasr.audio_config("0.6b", encoder_layers=1)
+    _, enc = _tower(qasr, cfg, seed=23)
+    frames = (330, 1200, 64)
+    mels = [qasr.synthetic_mel(128, n, seed=60 + i) for i, n in enumerate(frames)]
+    host = enc.encode_batch(mels)
+    mels_d = [torch.from_numpy(m).cuda() for m in mels]
+    total = sum(h.shape[0] for h in host)
+    out_d = torch.zeros((total, 1024), dtype=torch.float16, device="cuda")
+    torch.cuda.synchronize()
+    counts = enc.encode_batch_device([m.data_ptr() for m in mels_d], frames, out_d.data_ptr())
+    enc.sync()
+    assert counts == [h.shape[0] for h in host]
+    np.testing.assert_array_equal(out_d.cpu().numpy().view(np.uint16), np.concatenate(host).view(np.uint16))
+    enc.close()
+
+
 def test_repeat_encode_is_bit_identical(qasr, cuda_device):
     cfg = qasr.audio_config("0.6b", encoder_layers=1)
     _, enc = _tower(qasr, cfg)
