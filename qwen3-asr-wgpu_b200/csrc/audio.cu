@@ -20,6 +20,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <deque>
 #include <string>
@@ -75,6 +76,8 @@ struct qasr_audio_ctx {
   int C = 0, ldc = 0, kconv = 0, cf = 0, dm = 0, hd = 0, nh = 0, ffn = 0, out_dim = 0, wlen = 0;
   bool attn_kv_smem = false;
   size_t attn_smem = 0;
+  bool attn_tc = false;  // tensor-core attention (windows <= 128 tokens, head dim 64 or 128)
+  size_t attn_tc_smem = 0;
   // weights
   std::vector<void*> wallocs;
   float *c1_w = nullptr, *c1_b = nullptr, *pe = nullptr;
@@ -248,7 +251,7 @@ cudaError_t set_gemm_attr() {
 // ~2.5 us per partial of a split tile; the cheapest s wins.  With at least as many tiles
 // as SMs the default stream-K split applies (a few boundary tiles per CTA).
 int audio_grid(int n_out, int k, int rows, int sms) {
-  const GemmShape d = gemm_shape(n_out, k, false, rows, sms);
+  const GemmShape d = gemm_shape(n_out, k, false, rows, sms, 0, true);
   if (d.tiles >= sms) return 0;
   int best = 1;
   double best_t = 1e30;
@@ -268,7 +271,7 @@ int audio_grid(int n_out, int k, int rows, int sms) {
 qasr_status gemm(qasr_audio_ctx* c, const ALin& L, const __half* X, int rows, int epi, __half* out16, int ldo,
                  float* out32, int ldo32) {
   const GemmShape s =
-      gemm_shape(L.n_out, L.k, false, rows, c->num_sms, audio_grid(L.n_out, L.k, rows, c->num_sms));
+      gemm_shape(L.n_out, L.k, false, rows, c->num_sms, audio_grid(L.n_out, L.k, rows, c->num_sms), true);
   if (2ull * static_cast<unsigned long long>(s.units) * static_cast<unsigned long long>(s.grid) >= (1ull << 32))
     return afail(c, QASR_ERR_CAPACITY, "GEMM %d x %d over %d rows: too many units", L.n_out, L.k, rows);
   if (s.ws_floats * sizeof(float) > c->ws.bytes || static_cast<size_t>(s.tiles) * sizeof(int) > c->cnt.bytes)
@@ -325,7 +328,7 @@ qasr_status reserve_gemm(qasr_audio_ctx* c, const std::vector<std::pair<const AL
   size_t wsf = 64, tiles = 1;
   for (auto& pr : plan) {
     const GemmShape s = gemm_shape(pr.first->n_out, pr.first->k, false, pr.second, c->num_sms,
-                                   audio_grid(pr.first->n_out, pr.first->k, pr.second, c->num_sms));
+                                   audio_grid(pr.first->n_out, pr.first->k, pr.second, c->num_sms), true);
     wsf = std::max(wsf, s.ws_floats);
     tiles = std::max(tiles, static_cast<size_t>(s.tiles));
   }
@@ -465,11 +468,19 @@ qasr_status run_tower(qasr_audio_ctx* c, std::vector<Utt>& utts, __half* out) {
         "layernorm launch");
     c->launches++;
     if ((s = gemm(c, L.qkv, P<__half>(c->xn), T, EPI_BIAS_F32, nullptr, 0, P<float>(c->qkv32), 3 * dm))) return s;
-    ACK(launch_k(c->attn_kv_smem ? audio_window_attention_kernel<true> : audio_window_attention_kernel<false>,
-                 dim3(n_win, c->nh, qblocks), dim3(AUDIO_ATTN_THREADS), c->attn_smem, c->stream, true,
-                 static_cast<const float*>(P<float>(c->qkv32)), static_cast<const int*>(P<int>(c->win)), dm, c->hd,
-                 scale, c->wlen, P<__half>(c->attn16)),
-        "window attention launch");
+    if (c->attn_tc)
+      ACK(launch_k(c->hd == 64 ? audio_window_attention_tc_kernel<64> : audio_window_attention_tc_kernel<128>,
+                   dim3(n_win, c->nh, (c->wlen + AUDIO_TCATT_QROWS - 1) / AUDIO_TCATT_QROWS),
+                   dim3(AUDIO_TCATT_WARPS * 32), c->attn_tc_smem, c->stream, true,
+                   static_cast<const float*>(P<float>(c->qkv32)), static_cast<const int*>(P<int>(c->win)), dm, scale,
+                   c->wlen, P<__half>(c->attn16)),
+          "window attention launch");
+    else
+      ACK(launch_k(c->attn_kv_smem ? audio_window_attention_kernel<true> : audio_window_attention_kernel<false>,
+                   dim3(n_win, c->nh, qblocks), dim3(AUDIO_ATTN_THREADS), c->attn_smem, c->stream, true,
+                   static_cast<const float*>(P<float>(c->qkv32)), static_cast<const int*>(P<int>(c->win)), dm,
+                   c->hd, scale, c->wlen, P<__half>(c->attn16)),
+          "window attention launch");
     c->launches++;
     if ((s = gemm(c, L.o, P<__half>(c->attn16), T, EPI_BIAS_F32, nullptr, 0, P<float>(c->delta), dm))) return s;
     ACK(launch_k(audio_residual_layernorm_kernel, dim3(ln_grid), dim3(256), 0, c->stream, true, P<float>(c->h32),
@@ -559,6 +570,9 @@ qasr_status qasr_audio_create(const qasr_audio_config* cfg, int device, qasr_aud
   const size_t smem_kv = audio_attn_smem_floats(c->wlen, c->hd, true) * sizeof(float);
   c->attn_kv_smem = smem_kv <= 200 * 1024;
   c->attn_smem = audio_attn_smem_floats(c->wlen, c->hd, c->attn_kv_smem) * sizeof(float);
+  c->attn_tc_smem = audio_tcatt_smem_floats(c->wlen, c->hd) * sizeof(float);
+  c->attn_tc = c->wlen <= AUDIO_TCATT_MAXW && (c->hd == 64 || c->hd == 128) && c->attn_tc_smem <= 200 * 1024 &&
+               !(std::getenv("QASR_B200_AUDIO_F32_ATTN") && std::getenv("QASR_B200_AUDIO_F32_ATTN")[0] == '1');
   if (c->attn_smem > 200 * 1024) {
     delete c;
     return fail_out(QASR_ERR_INVALID_ARG, "attention window of " + std::to_string(g.n_window_infer) +
@@ -573,6 +587,10 @@ qasr_status qasr_audio_create(const qasr_audio_config* cfg, int device, qasr_aud
                            static_cast<int>(c->attn_smem)) != cudaSuccess ||
       cudaFuncSetAttribute(audio_window_attention_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(c->attn_smem)) != cudaSuccess ||
+      (c->attn_tc && cudaFuncSetAttribute(c->hd == 64 ? audio_window_attention_tc_kernel<64>
+                                                      : audio_window_attention_tc_kernel<128>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(c->attn_tc_smem)) != cudaSuccess) ||
       cudaMalloc(&c->status, 2 * sizeof(uint32_t)) != cudaSuccess ||
       cudaMemset(c->status, 0, 2 * sizeof(uint32_t)) != cudaSuccess) {
     qasr_audio_destroy(c);

@@ -11,7 +11,9 @@
 //                           sinusoidal position rows the conv_out output is added onto
 //   audio_residual_layernorm_kernel  h += delta (a block's output), then LayerNorm
 //                           (mean, variance, eps 1e-5) f32 -> f16 GEMM operand
-//   audio_window_attention_kernel  bidirectional attention inside token windows
+//   audio_window_attention_tc_kernel  bidirectional attention inside token windows on the
+//                           tensor cores (mma.sync, TF32); audio_window_attention_kernel, the
+//                           CUDA-core f32 form, for windows longer than 128 tokens
 //
 // Layouts in HBM (one round of conv chunks at a time; tokens of every chunk packed):
 //   mel       f32 [n_mels][n_frames] per utterance (the reference's mel-bin-major input)
@@ -408,6 +410,179 @@ __global__ void __launch_bounds__(AUDIO_ATTN_THREADS) audio_window_attention_ker
       }
     }
     __syncwarp();
+  }
+}
+
+// Attention inside a window on the tensor cores (mma.sync m16n8k8, TF32 operands, f32
+// accumulate) for windows of at most AUDIO_TCATT_MAXW tokens: CTA = (window, head); q, K and
+// V of the window come into shared memory by cp.async (rows past the window zero-filled);
+// CTA z of a (window, head) takes query rows [64 z, 64 z + 64), a warp 16 of them: S = Q K^T (16 x len, registers), scaled, exact
+// softmax per row in f32 (row max, exp(s - max), sum, inv = 1 / sum, p * inv — the
+// reference's steps, src/audio_encoder.rs:519-566), P through shared memory, O = P V; O is
+// rounded to f16 (the out_proj operand).  q, k, p and v are rounded to TF32 (10-bit
+// mantissa) for the products: a numpy emulation puts the tower's output within 7.2e-4 of
+// the f32 oracle either way.  Row strides (hd + 4 for q / K / P, hd + 8 for V) make every
+// fragment read conflict-free.
+constexpr int AUDIO_TCATT_MAXW = 128;
+constexpr int AUDIO_TCATT_WARPS = 4;
+constexpr int AUDIO_TCATT_QROWS = 16 * AUDIO_TCATT_WARPS;  // query rows per CTA
+
+__host__ __device__ constexpr size_t audio_tcatt_smem_floats(int wlen, int hd) {
+  return static_cast<size_t>(((wlen + 15) / 16) * 16) * (2 * hd + 12) +
+         static_cast<size_t>(AUDIO_TCATT_QROWS) * (hd + 4) +
+         static_cast<size_t>(AUDIO_TCATT_WARPS) * 16 * (((wlen + 7) / 8) * 8 + 4);
+}
+
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+__device__ __forceinline__ void mma_tf32(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+template <int HD>
+__global__ void __launch_bounds__(AUDIO_TCATT_WARPS * 32) audio_window_attention_tc_kernel(
+    const float* __restrict__ qkv, const int* __restrict__ win, int dm, float scale, int wmax,
+    __half* __restrict__ out) {
+  audio_pdl_entry();
+  extern __shared__ __align__(16) float tc_smem[];
+  constexpr int QS = HD + 4, KS = HD + 4, VS = HD + 8;
+  const int start = win[2 * blockIdx.x], len = win[2 * blockIdx.x + 1];
+  const int h = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int q0 = blockIdx.z * AUDIO_TCATT_QROWS;  // this CTA's first query row
+  if (q0 >= len) return;
+  const int rows16 = ((wmax + 15) / 16) * 16;  // padded window rows in shared memory
+  const int ntiles = (len + 7) >> 3;           // key tiles of 8
+  const int ps = ((wmax + 7) / 8) * 8 + 4;     // P row stride
+  float* sk = tc_smem;                         // [rows16][KS]
+  float* sv = sk + static_cast<size_t>(rows16) * KS;                  // [rows16][VS]
+  float* sq = sv + static_cast<size_t>(rows16) * VS;                  // [QROWS][QS]
+  float* sp = sq + static_cast<size_t>(AUDIO_TCATT_QROWS) * QS + static_cast<size_t>(warp) * 16 * ps;  // [16][ps]
+  const size_t ld = 3 * static_cast<size_t>(dm);
+  const float* base = qkv + static_cast<size_t>(start) * ld + h * HD;
+  constexpr int V4 = HD / 4;
+  const int lpad = ((len + 7) / 8) * 8;  // key rows that fragments touch
+  for (int i = threadIdx.x; i < lpad * V4; i += blockDim.x) {
+    const int r = i / V4, c = (i - r * V4) * 4;
+    if (r < len) {
+      const float* row = base + r * ld + c;
+      cp_async16(sk + r * KS + c, row + dm);
+      cp_async16(sv + r * VS + c, row + 2 * dm);
+    } else {  // padding rows: zeros (a zero V row times a zero probability stays 0)
+      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+      *reinterpret_cast<float4*>(sk + r * KS + c) = z;
+      *reinterpret_cast<float4*>(sv + r * VS + c) = z;
+    }
+  }
+  for (int i = threadIdx.x; i < AUDIO_TCATT_QROWS * V4; i += blockDim.x) {
+    const int r = i / V4, c = (i - r * V4) * 4;
+    if (q0 + r < len)
+      cp_async16(sq + r * QS + c, base + (q0 + r) * ld + c);
+    else
+      *reinterpret_cast<float4*>(sq + r * QS + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  {
+    const int mt = warp;  // query rows q0 + 16 mt ...
+    if (q0 + mt * 16 >= len) return;
+    const float* qa = sq + (mt * 16 + g) * QS;
+    float sacc[AUDIO_TCATT_MAXW / 8][4];
+#pragma unroll
+    for (int nt = 0; nt < AUDIO_TCATT_MAXW / 8; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < HD / 8; ++kk) {
+      const uint32_t a0 = to_tf32(qa[kk * 8 + t]), a1 = to_tf32(qa[8 * QS + kk * 8 + t]);
+      const uint32_t a2 = to_tf32(qa[kk * 8 + t + 4]), a3 = to_tf32(qa[8 * QS + kk * 8 + t + 4]);
+#pragma unroll
+      for (int nt = 0; nt < AUDIO_TCATT_MAXW / 8; ++nt) {
+        if (nt < ntiles) {
+          const float* kb = sk + (nt * 8 + g) * KS + kk * 8;
+          mma_tf32(sacc[nt], a0, a1, a2, a3, to_tf32(kb[t]), to_tf32(kb[t + 4]));
+        }
+      }
+    }
+    // exact softmax of rows g (elements 0, 1) and g + 8 (2, 3); columns >= len masked
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < AUDIO_TCATT_MAXW / 8; ++nt) {
+      if (nt < ntiles) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int col = nt * 8 + 2 * t + (e & 1);
+          sacc[nt][e] = col < len ? __fmul_rn(sacc[nt][e], scale) : -INFINITY;
+        }
+        mx0 = fmaxf(mx0, fmaxf(sacc[nt][0], sacc[nt][1]));
+        mx1 = fmaxf(mx1, fmaxf(sacc[nt][2], sacc[nt][3]));
+      }
+    }
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+    }
+    float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < AUDIO_TCATT_MAXW / 8; ++nt) {
+      if (nt < ntiles) {
+        sacc[nt][0] = expf(__fsub_rn(sacc[nt][0], mx0));
+        sacc[nt][1] = expf(__fsub_rn(sacc[nt][1], mx0));
+        sacc[nt][2] = expf(__fsub_rn(sacc[nt][2], mx1));
+        sacc[nt][3] = expf(__fsub_rn(sacc[nt][3], mx1));
+        sum0 = __fadd_rn(__fadd_rn(sum0, sacc[nt][0]), sacc[nt][1]);
+        sum1 = __fadd_rn(__fadd_rn(sum1, sacc[nt][2]), sacc[nt][3]);
+      }
+    }
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+      sum0 = __fadd_rn(sum0, __shfl_xor_sync(0xffffffffu, sum0, o));
+      sum1 = __fadd_rn(sum1, __shfl_xor_sync(0xffffffffu, sum1, o));
+    }
+    const float inv0 = __fdiv_rn(1.0f, sum0), inv1 = __fdiv_rn(1.0f, sum1);
+#pragma unroll
+    for (int nt = 0; nt < AUDIO_TCATT_MAXW / 8; ++nt) {
+      if (nt < ntiles) {
+        float* p0 = sp + g * ps + nt * 8 + 2 * t;
+        p0[0] = __fmul_rn(sacc[nt][0], inv0);
+        p0[1] = __fmul_rn(sacc[nt][1], inv0);
+        p0[8 * ps] = __fmul_rn(sacc[nt][2], inv1);
+        p0[8 * ps + 1] = __fmul_rn(sacc[nt][3], inv1);
+      }
+    }
+    __syncwarp();
+    float oacc[HD / 8][4];
+#pragma unroll
+    for (int nd = 0; nd < HD / 8; ++nd) oacc[nd][0] = oacc[nd][1] = oacc[nd][2] = oacc[nd][3] = 0.f;
+    for (int kk = 0; kk < ntiles; ++kk) {
+      const float* pa = sp + g * ps + kk * 8;
+      const uint32_t a0 = to_tf32(pa[t]), a1 = to_tf32(pa[8 * ps + t]);
+      const uint32_t a2 = to_tf32(pa[t + 4]), a3 = to_tf32(pa[8 * ps + t + 4]);
+      const float* vb = sv + (kk * 8 + t) * VS + g;
+#pragma unroll
+      for (int nd = 0; nd < HD / 8; ++nd)
+        mma_tf32(oacc[nd], a0, a1, a2, a3, to_tf32(vb[nd * 8]), to_tf32(vb[4 * VS + nd * 8]));
+    }
+    const int r0 = q0 + mt * 16 + g;
+#pragma unroll
+    for (int nd = 0; nd < HD / 8; ++nd) {
+      const int col = h * HD + nd * 8 + 2 * t;
+      if (r0 < len)
+        *reinterpret_cast<__half2*>(out + static_cast<size_t>(start + r0) * dm + col) =
+            __floats2half2_rn(oacc[nd][0], oacc[nd][1]);
+      if (r0 + 8 < len)
+        *reinterpret_cast<__half2*>(out + static_cast<size_t>(start + r0 + 8) * dm + col) =
+            __floats2half2_rn(oacc[nd][2], oacc[nd][3]);
+    }
   }
 }
 

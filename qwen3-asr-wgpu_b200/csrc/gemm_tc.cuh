@@ -53,6 +53,7 @@ __host__ __device__ constexpr int gemm_threads(bool int8) {
 constexpr int GEMM_MAX_STAGES = 12;
 constexpr int GEMM_A_STAGES = 8;  // upper bound; the kernel fits what TMEM allows
 constexpr int GEMM_MAX_NTILE = 128;
+constexpr int GEMM_WIDE_NTILE = 256;  // f16 only: 2 x 256 accumulator columns fill the TMEM
 constexpr uint32_t GEMM_TMEM_COLS = 512;
 
 struct KvLayout {

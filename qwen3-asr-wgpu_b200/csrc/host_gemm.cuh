@@ -118,9 +118,17 @@ struct GemmShape {
 };
 
 // grid_override > 0 fixes the CTA count (at most num_sms); otherwise at least 4 units per CTA.
-inline GemmShape gemm_shape(int n_out, int k, bool int8, int rows, int num_sms, int grid_override = 0) {
+// wide: f16 weights over many rows may take 256-row activation tiles (UMMA N = 256): a
+// unit then moves 16 KB of weights + 32 KB of activations for 4 MFLOP instead of 16 + 16 KB
+// for 2 MFLOP, which raises the per-SM load ceiling; used only when the 256-row tiles still
+// give every SM a tile (otherwise the narrower tiles spread the work better).
+inline GemmShape gemm_shape(int n_out, int k, bool int8, int rows, int num_sms, int grid_override = 0,
+                            bool wide = false) {
   GemmShape s{};
   s.n_tile = rows <= GEMM_MAX_NTILE ? std::max(16, (rows + 15) / 16 * 16) : GEMM_MAX_NTILE;
+  if (wide && !int8 && rows >= GEMM_WIDE_NTILE &&
+      (n_out / 128) * ((rows + GEMM_WIDE_NTILE - 1) / GEMM_WIDE_NTILE) >= num_sms)
+    s.n_tile = GEMM_WIDE_NTILE;
   s.n_tiles = (rows + s.n_tile - 1) / s.n_tile;
   const int ke = int8 ? 128 : 64;
   s.kblocks = k / ke;

@@ -50,9 +50,12 @@ def test_conv_stem_and_projector_match_oracle(qasr, cuda_device, frames):
     enc.close()
 
 
-def test_two_layers_two_conv_rounds_match_oracle(qasr, cuda_device):
+@pytest.mark.parametrize("attn", ["tensor-core", "f32"])
+def test_two_layers_two_conv_rounds_match_oracle(qasr, cuda_device, monkeypatch, attn):
     """3333 frames: 34 conv chunks (two rounds of the conv stem), 436 tokens in windows of
-    104 with a short last one."""
+    104 with a short last one; both window-attention kernels (TF32 tensor cores, and the
+    f32 CUDA-core form used for windows over 128 tokens)."""
+    monkeypatch.setenv("QASR_B200_AUDIO_F32_ATTN", "1" if attn == "f32" else "0")
     cfg = qasr.audio_config("0.6b", encoder_layers=2)
     tw, enc = _tower(qasr, cfg, seed=3)
     mel = qasr.synthetic_mel(128, 3333, seed=5)
