@@ -244,34 +244,54 @@ cudaError_t set_gemm_attr() {
                               g_dyn_smem_max);
 }
 
-// CTA count of an audio GEMM.  With fewer tiles than SMs, each tile is cut into s
-// k-segments (grid = tiles * s): s = 1 needs no split fixup, a larger s streams fewer units
-// per CTA but adds the last CTA's pass over s partials.  Measured per CTA (B200, f16,
-// 128-row tiles): ~4 us of set-up and first loads, ~0.6 us per (16 KB W + 16 KB X) unit,
-// ~2.5 us per partial of a split tile; the cheapest s wins.  With at least as many tiles
-// as SMs the default stream-K split applies (a few boundary tiles per CTA).
-int audio_grid(int n_out, int k, int rows, int sms) {
-  const GemmShape d = gemm_shape(n_out, k, false, rows, sms, 0, true);
-  if (d.tiles >= sms) return 0;
-  int best = 1;
+// Plan of an audio GEMM: CTA count and activation-tile width.  With fewer tiles than SMs,
+// each tile is cut into s k-segments (grid = tiles * s): s = 1 needs no split fixup, a
+// larger s streams fewer units per CTA but adds the last CTA's pass over s partials.
+// Measured per CTA (B200, f16, 128-row tiles): ~4 us of set-up and first loads, ~0.6 us per
+// (16 KB W + 16 KB X) unit (the SM's load rate; a unit of narrower tiles costs in
+// proportion to its bytes), ~2.5 us per partial of a split tile (in proportion to its
+// size).  64-row tiles double the tile count of a GEMM over a few hundred rows.  With at
+// least as many tiles as SMs the default stream-K split applies.  The cheapest plan wins.
+struct AudioPlan {
+  int grid = 0;    // 0: the default stream-K grid
+  int n_tile = 0;  // 0: the default width
+};
+
+AudioPlan audio_plan(int n_out, int k, int rows, int sms) {
+  static const bool narrow_ok = !(std::getenv("QASR_B200_AUDIO_NT64") && std::getenv("QASR_B200_AUDIO_NT64")[0] == '0');
+  AudioPlan best;
   double best_t = 1e30;
-  for (int sp = 1; sp <= 8 && d.tiles * sp <= sms; ++sp) {
-    const double units = static_cast<double>(d.kblocks) / sp;
-    const double t = 4.0 + 0.6 * units + (sp > 1 ? 2.5 * sp : 0.0);
-    if (t < best_t) {
-      best_t = t;
-      best = sp;
+  for (int nt : {0, 64}) {
+    if (nt == 64 && (!narrow_ok || rows <= 64)) continue;
+    const GemmShape d = gemm_shape(n_out, k, false, rows, sms, 0, true, nt);
+    if (nt == 64 && d.n_tile != 64) continue;
+    const double unit = 0.6 * (16384.0 + 128.0 * d.n_tile) / 32768.0;
+    const double part = 2.5 * d.n_tile / 128.0;
+    if (d.tiles >= sms) {
+      const double t = 4.0 + unit * std::ceil(static_cast<double>(d.units) / sms) + part;
+      if (t < best_t) {
+        best_t = t;
+        best = AudioPlan{0, nt};
+      }
+      continue;
+    }
+    for (int sp = 1; sp <= 8 && d.tiles * sp <= sms; ++sp) {
+      const double t = 4.0 + unit * static_cast<double>(d.kblocks) / sp + (sp > 1 ? part * sp : 0.0);
+      if (t < best_t) {
+        best_t = t;
+        best = AudioPlan{d.tiles * sp, nt};
+      }
     }
   }
-  return d.tiles * best;
+  return best;
 }
 
 // One GEMM: out = epilogue(X [rows, L.k] . W^T + bias).  The split workspace must already
 // hold the plan (reserve_gemm).
 qasr_status gemm(qasr_audio_ctx* c, const ALin& L, const __half* X, int rows, int epi, __half* out16, int ldo,
                  float* out32, int ldo32) {
-  const GemmShape s =
-      gemm_shape(L.n_out, L.k, false, rows, c->num_sms, audio_grid(L.n_out, L.k, rows, c->num_sms), true);
+  const AudioPlan pl = audio_plan(L.n_out, L.k, rows, c->num_sms);
+  const GemmShape s = gemm_shape(L.n_out, L.k, false, rows, c->num_sms, pl.grid, true, pl.n_tile);
   if (2ull * static_cast<unsigned long long>(s.units) * static_cast<unsigned long long>(s.grid) >= (1ull << 32))
     return afail(c, QASR_ERR_CAPACITY, "GEMM %d x %d over %d rows: too many units", L.n_out, L.k, rows);
   if (s.ws_floats * sizeof(float) > c->ws.bytes || static_cast<size_t>(s.tiles) * sizeof(int) > c->cnt.bytes)
@@ -327,8 +347,9 @@ qasr_status gemm(qasr_audio_ctx* c, const ALin& L, const __half* X, int rows, in
 qasr_status reserve_gemm(qasr_audio_ctx* c, const std::vector<std::pair<const ALin*, int>>& plan) {
   size_t wsf = 64, tiles = 1;
   for (auto& pr : plan) {
-    const GemmShape s = gemm_shape(pr.first->n_out, pr.first->k, false, pr.second, c->num_sms,
-                                   audio_grid(pr.first->n_out, pr.first->k, pr.second, c->num_sms), true);
+    const AudioPlan pl = audio_plan(pr.first->n_out, pr.first->k, pr.second, c->num_sms);
+    const GemmShape s =
+        gemm_shape(pr.first->n_out, pr.first->k, false, pr.second, c->num_sms, pl.grid, true, pl.n_tile);
     wsf = std::max(wsf, s.ws_floats);
     tiles = std::max(tiles, static_cast<size_t>(s.tiles));
   }

@@ -122,11 +122,14 @@ struct GemmShape {
 // unit then moves 16 KB of weights + 32 KB of activations for 4 MFLOP instead of 16 + 16 KB
 // for 2 MFLOP, which raises the per-SM load ceiling; used only when the 256-row tiles still
 // give every SM a tile (otherwise the narrower tiles spread the work better).
+// n_tile_override > 0 (a multiple of 16, at most 128, below the default) narrows the
+// activation tiles: more tiles for a GEMM over few rows.
 inline GemmShape gemm_shape(int n_out, int k, bool int8, int rows, int num_sms, int grid_override = 0,
-                            bool wide = false) {
+                            bool wide = false, int n_tile_override = 0) {
   GemmShape s{};
   s.n_tile = rows <= GEMM_MAX_NTILE ? std::max(16, (rows + 15) / 16 * 16) : GEMM_MAX_NTILE;
-  if (wide && !int8 && rows >= GEMM_WIDE_NTILE &&
+  if (n_tile_override > 0 && n_tile_override < s.n_tile) s.n_tile = n_tile_override;
+  if (wide && !int8 && n_tile_override <= 0 && rows >= GEMM_WIDE_NTILE &&
       (n_out / 128) * ((rows + GEMM_WIDE_NTILE - 1) / GEMM_WIDE_NTILE) >= num_sms)
     s.n_tile = GEMM_WIDE_NTILE;
   s.n_tiles = (rows + s.n_tile - 1) / s.n_tile;
