@@ -154,3 +154,61 @@ def test_synthetic_tower_names_and_shapes(qasr):
     assert t["layers.0.fc1.weight"].shape == (3584, 896)
     assert t["proj2.weight"].shape == (1024, 896)
     assert t["layers.0.self_attn_layer_norm.bias"].dtype == np.float32
+
+
+def test_oracle_conv_stem_matches_torch_conv2d(qasr):
+    """An independent formula check: torch's conv2d (stride 2, padding 1) + GELU(erf) per level,
+    the permute to [t][c * F + f] written out as loops, conv_out and the positions —
+    the same numbers as the oracle's im2col restatement."""
+    import torch
+    import torch.nn.functional as F
+    cfg = qasr.audio_config("0.6b", encoder_layers=0, downsample_hidden_size=32, d_model=128, output_dim=128)
+    t = qasr.SyntheticAudioTower(cfg, seed=3).tensors
+    mel = qasr.synthetic_mel(128, 230, seed=4)
+    chunked, toks = at.chunk_mel(mel, 100)
+    x = torch.from_numpy(chunked).double()
+    for k in (1, 2, 3):
+        w = torch.from_numpy(t[f"conv2d{k}.weight"].view(np.float16).astype(np.float64))
+        b = torch.from_numpy(t[f"conv2d{k}.bias"].astype(np.float64))
+        x = F.gelu(F.conv2d(x, w, b, stride=2, padding=1))
+    n, c, f, tt = x.shape
+    perm = torch.zeros((n, tt, c * f), dtype=torch.float64)
+    for ic in range(c):
+        for ff in range(f):
+            perm[:, :, ic * f + ff] = x[:, ic, ff, :]
+    wco = torch.from_numpy(t["conv_out.weight"].view(np.float16).astype(np.float64))
+    co = perm @ wco.T + torch.from_numpy(at.sinusoid_pe(1500, 128)[:tt].astype(np.float64))
+    want = torch.cat([co[i, :v] for i, v in enumerate(toks)]).numpy()
+    got = at.conv_stem(t, cfg, mel)
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4)
+
+
+def test_oracle_window_attention_matches_torch_sdpa():
+    """Block-diagonal masked scaled_dot_product_attention (float64) = the oracle's windows."""
+    import torch
+    import torch.nn.functional as F
+    rng = np.random.default_rng(8)
+    s, nh, hd, ws = 50, 2, 64, 13
+    q, k, v = (rng.standard_normal((s, nh * hd)).astype(np.float32) for _ in range(3))
+    win = np.arange(s) // ws
+    mask = torch.from_numpy(win[:, None] == win[None, :])
+    th = lambda a: torch.from_numpy(a.astype(np.float64)).view(s, nh, hd).transpose(0, 1)  # noqa: E731
+    o = F.scaled_dot_product_attention(th(q), th(k), th(v), attn_mask=mask)
+    want = o.transpose(0, 1).reshape(s, nh * hd).numpy()
+    np.testing.assert_allclose(at.window_attention(q, k, v, nh, ws), want, rtol=1e-4, atol=1e-5)
+
+
+def test_audio_config_rejected_before_any_device_use(qasr):
+    """The geometry checks of GpuAudioEncoder::load (src/audio_encoder_gpu.rs:606-700) run
+    before the library looks for a device, with the reference's kind of message."""
+    import ctypes
+    from importlib import import_module
+    audio = import_module("qasr_b200.audio")
+    for over, needle in [(dict(d_model=900), "divisible"), (dict(encoder_attention_heads=56), "head dim"),
+                         (dict(encoder_ffn_dim=1000), "multiples of 128"),
+                         (dict(downsample_hidden_size=100), "multiple of 8")]:
+        cfg = audio._cfg_struct(qasr.audio_config("0.6b", **over))
+        err = ctypes.create_string_buffer(256)
+        h = ctypes.c_void_p()
+        st = qasr.lib.qasr_audio_create(ctypes.byref(cfg), 0, ctypes.byref(h), err, 256)
+        assert st == 1 and needle in err.value.decode(), (over, st, err.value)
