@@ -65,6 +65,18 @@ def test_two_layers_two_conv_rounds_match_oracle(qasr, cuda_device, monkeypatch,
     enc.close()
 
 
+@pytest.mark.parametrize("window_infer", [400, 1600])
+def test_other_window_lengths_match_oracle(qasr, cuda_device, window_infer):
+    """n_window_infer 400 -> windows of 52 tokens (tensor-core kernel, partial key tiles);
+    1600 -> 208 tokens, past the tensor-core kernel's 128 (the f32 kernel is chosen)."""
+    cfg = qasr.audio_config("0.6b", encoder_layers=1, n_window_infer=window_infer)
+    tw, enc = _tower(qasr, cfg, seed=19)
+    mel = qasr.synthetic_mel(128, 1234, seed=20)
+    got = enc.encode(mel)
+    _check(at.encode(tw.tensors, cfg, mel), got)
+    enc.close()
+
+
 @pytest.mark.parametrize("preset,frames", [("0.6b", 1000), ("1.7b", 760)])
 def test_full_tower_matches_oracle(qasr, cuda_device, preset, frames):
     cfg = qasr.audio_config(preset)
