@@ -196,3 +196,45 @@ def test_errors_are_status_codes(qasr, cuda_device):
     enc.encode(mel)
     assert enc.launches > before  # every launch is one of this library's kernels
     enc.close()
+
+
+def test_audio_rows_feed_the_decoder_prefill(qasr, cuda_device):
+    """The ASR composition: mel -> audio tower -> prefix (9 text embedding rows, the audio
+    rows, 5 text rows; src/prompt.rs:46-60) -> decoder prefill -> greedy steps.  The decoder
+    sees the same f16 prefix as the CPU oracle decoder (teacher-forced); logits within the
+    f16 tolerance and greedy ids equal at 4 of 5 positions at least (a near-tie may flip
+    one)."""
+    from oracle.oracle import OracleModel, OracleSeq
+    acfg = qasr.audio_config("0.6b", encoder_layers=2)
+    _, enc = _tower(qasr, acfg, seed=51)
+    audio = enc.encode(qasr.synthetic_mel(128, 300, seed=52)).view(np.uint16)
+    enc.close()
+    cfg = qasr.text_config("0.6b", num_hidden_layers=2, vocab_size=8192)
+    assert cfg["hidden_size"] == acfg["output_dim"]
+    model = qasr.SyntheticModel(cfg, seed=53)
+    ids = np.arange(14, dtype=np.int64) * 37 % 8000
+    prefix = np.concatenate([model.embed[ids[:9]], audio, model.embed[ids[9:]]]).astype(np.uint16)
+    dec = qasr.TextDecoder(cfg, max_slots=1, max_seq=256, keep_logits=True)
+    dec.load_model(model)
+    om = OracleModel(cfg)
+    om.load_model(model, int8=False)
+    cos, sin = qasr.build_rope_tables(256)
+    dec.set_rope_tables(cos, sin)
+    om.set_rope_tables(cos, sin)
+    slot = dec.fork_capped(128)
+    tok = dec.prefill(slot, prefix)
+    seq = OracleSeq(om, 256)
+    otok, olog = seq.prefill(prefix, want_logits=True)
+    worst = float(np.max(np.abs(dec.read_logits(1)[0] - olog)))
+    same = [tok == otok]
+    for _ in range(4):
+        dec.set_input_token(slot, otok)
+        tok = dec.step(slot)
+        glog = dec.read_logits(1)[0]
+        otok, olog = seq.step(want_logits=True)
+        worst = max(worst, float(np.max(np.abs(glog - olog))))
+        same.append(tok == otok)
+    dec.close()
+    om.close()
+    assert worst <= 2e-2, worst
+    assert sum(same) >= 4, same
