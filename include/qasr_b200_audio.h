@@ -67,6 +67,12 @@ typedef struct {
 
 typedef struct qasr_audio_ctx qasr_audio_ctx;
 
+/* AsrConfig::from_file for the tower (src/config.rs:142-173): `{model_dir}/config.json`'s
+ * thinker_config.audio_config (or the HF layout's top-level audio_config), absent fields
+ * taking AudioEncoderConfig's defaults (src/config.rs:54-64).  err (optional) receives a
+ * message on failure. */
+qasr_status qasr_read_audio_config(const char* model_dir, qasr_audio_config* out, char* err, int errlen);
+
 /* Token rows a mel of n_frames frames produces: full chunks give feo(2 n_window) rows,
  * the tail chunk feo(tail) (feo = three (l - 1) / 2 + 1 halvings, src/audio_encoder.rs:634-637). */
 int32_t qasr_audio_token_count(const qasr_audio_config* cfg, int32_t n_frames);

@@ -66,7 +66,7 @@ EXPORTED_SYMBOLS = (
     "qasr_checkpoint_weight_format", "qasr_checkpoint_read_f16", "qasr_checkpoint_rows_f16",
     "qasr_load_checkpoint", "qasr_batch_decode", "qasr_batch_decode_backend", "qasr_checkpoint_read_f32",
     # include/qasr_b200_audio.h
-    "qasr_audio_token_count", "qasr_audio_create", "qasr_audio_destroy", "qasr_audio_last_error",
+    "qasr_read_audio_config", "qasr_audio_token_count", "qasr_audio_create", "qasr_audio_destroy", "qasr_audio_last_error",
     "qasr_audio_load_weights", "qasr_audio_load_checkpoint", "qasr_audio_encode", "qasr_audio_encode_batch",
     "qasr_audio_encode_device", "qasr_audio_encode_batch_device", "qasr_audio_sync", "qasr_audio_stream", "qasr_audio_launch_count",
 )
@@ -698,7 +698,7 @@ def kv_page_swizzle(pool: np.ndarray) -> np.ndarray:
 
 
 from .audio import (AUDIO_PRESETS, AudioEncoder, SyntheticAudioTower, audio_config,  # noqa: E402,F401
-                    conv_geometry, synthetic_mel)
+                    conv_geometry, read_audio_config, synthetic_mel)
 from .audio import token_count as audio_token_count  # noqa: E402,F401
 
 

@@ -80,6 +80,7 @@ def _bind():
     lib.qasr_audio_launch_count.argtypes = [P]
     lib.qasr_audio_launch_count.restype = ctypes.c_uint64
     lib.qasr_checkpoint_read_f32.argtypes = [P, ctypes.c_char_p, P, ctypes.c_int64]
+    lib.qasr_read_audio_config.argtypes = [ctypes.c_char_p, ctypes.POINTER(AudioConfig), ctypes.c_char_p, I]
 
 
 _bind()
@@ -93,6 +94,16 @@ def token_count(cfg: dict, n_frames: int) -> int:
     """Rows a mel of n_frames frames produces (feo per chunk, src/audio_encoder.rs:634-637)."""
     c = _cfg_struct(cfg)
     return int(lib.qasr_audio_token_count(ctypes.byref(c), int(n_frames)))
+
+
+def read_audio_config(model_dir: str) -> dict:
+    """The tower's AudioEncoderConfig from `{model_dir}/config.json` (qasr_read_audio_config)."""
+    c = AudioConfig()
+    err = ctypes.create_string_buffer(512)
+    st = lib.qasr_read_audio_config(str(model_dir).encode(), ctypes.byref(c), err, 512)
+    if st != QASR_OK:
+        raise DecoderError(st, err.value.decode())
+    return {n: int(getattr(c, n)) for n, _ in AudioConfig._fields_}
 
 
 def conv_geometry(cfg: dict):

@@ -28,6 +28,7 @@
 #include "ctx_internal.h"
 #include "f16_host.h"
 #include "qasr_b200.h"
+#include "qasr_b200_audio.h"
 
 namespace {
 
@@ -608,6 +609,71 @@ qasr_status qasr_read_model_config(const char* model_dir, qasr_model_config* out
     if (const JValue* x = rs->get("interleaved"); x && x->kind == JValue::Bool) il = il || x->b;
     c.mrope_interleaved = il ? 1 : 0;
   }
+  *out = c;
+  return QASR_OK;
+}
+
+qasr_status qasr_read_audio_config(const char* model_dir, qasr_audio_config* out, char* err, int errlen) {
+  if (!model_dir || !out) {
+    set_err(err, errlen, "null argument");
+    return QASR_ERR_INVALID_ARG;
+  }
+  const std::string path = std::string(model_dir) + "/config.json";
+  std::string text;
+  if (!read_file(path, &text)) {
+    set_err(err, errlen, "read " + path);
+    return QASR_ERR_INVALID_ARG;
+  }
+  JValue j;
+  std::string jerr;
+  if (!JParser(text.data(), text.size()).parse(&j, &jerr)) {
+    set_err(err, errlen, path + ": " + jerr);
+    return QASR_ERR_INVALID_ARG;
+  }
+  // AsrConfig::from_json_str (src/config.rs:148-173): thinker_config.audio_config, or the
+  // HF layout's top-level audio_config
+  const JValue* ac = nullptr;
+  if (const JValue* th = j.get("thinker_config")) {
+    ac = th->get("audio_config");
+    if (!ac || ac->kind != JValue::Obj) {
+      set_err(err, errlen, path + ": thinker_config has no audio_config");
+      return QASR_ERR_INVALID_ARG;
+    }
+  } else {
+    ac = j.get("audio_config");
+    if (!ac || ac->kind != JValue::Obj) {
+      set_err(err, errlen, path + ": missing thinker_config and audio_config");
+      return QASR_ERR_INVALID_ARG;
+    }
+  }
+  // AudioEncoderConfig and its defaults (src/config.rs:26-64)
+  const char* keys[10] = {"d_model", "encoder_layers", "encoder_attention_heads", "encoder_ffn_dim", "num_mel_bins",
+                          "downsample_hidden_size", "max_source_positions", "n_window", "n_window_infer",
+                          "output_dim"};
+  const int defs[10] = {896, 18, 14, 3584, 128, 480, 1500, 50, 800, 1024};
+  int v[10];
+  for (int k = 0; k < 10; ++k) {
+    const JValue* x = ac->get(keys[k]);
+    if (!x || x->kind == JValue::Null) {
+      v[k] = defs[k];
+    } else if (!x->is_int || x->i <= 0 || x->i > (1 << 30)) {
+      set_err(err, errlen, path + ": audio_config." + keys[k] + " is not a positive integer");
+      return QASR_ERR_INVALID_ARG;
+    } else {
+      v[k] = static_cast<int>(x->i);
+    }
+  }
+  qasr_audio_config c{};
+  c.d_model = v[0];
+  c.encoder_layers = v[1];
+  c.encoder_attention_heads = v[2];
+  c.encoder_ffn_dim = v[3];
+  c.num_mel_bins = v[4];
+  c.downsample_hidden_size = v[5];
+  c.max_source_positions = v[6];
+  c.n_window = v[7];
+  c.n_window_infer = v[8];
+  c.output_dim = v[9];
   *out = c;
   return QASR_OK;
 }

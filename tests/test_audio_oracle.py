@@ -212,3 +212,47 @@ def test_audio_config_rejected_before_any_device_use(qasr):
         h = ctypes.c_void_p()
         st = qasr.lib.qasr_audio_create(ctypes.byref(cfg), 0, ctypes.byref(h), err, 256)
         assert st == 1 and needle in err.value.decode(), (over, st, err.value)
+
+
+def _write_config(tmp_path, name, obj):
+    import json
+    d = tmp_path / name
+    d.mkdir()
+    (d / "config.json").write_text(json.dumps(obj))
+    return str(d)
+
+
+def test_read_audio_config_hf_layout(qasr, tmp_path):
+    """The reference's test_parse_hf_native_config_layout (src/config.rs:260-298), its
+    audio_config half: top-level audio_config next to text_config."""
+    d = _write_config(tmp_path, "hf", {
+        "audio_config": {"d_model": 896, "encoder_layers": 18, "encoder_attention_heads": 14,
+                         "encoder_ffn_dim": 3584, "num_mel_bins": 128, "n_window": 50, "n_window_infer": 800,
+                         "conv_chunksize": 500, "output_dim": 1024},
+        "audio_token_id": 151676,
+        "text_config": {"vocab_size": 151936, "hidden_size": 1024, "rope_parameters": {"rope_theta": 1000000}}})
+    assert qasr.read_audio_config(d) == qasr.audio_config("0.6b")
+    assert qasr.read_model_config(d)["text_config"]["hidden_size"] == 1024
+
+
+def test_read_audio_config_thinker_layout_and_defaults(qasr, tmp_path):
+    """thinker_config.audio_config; fields left out take AudioEncoderConfig's defaults
+    (src/config.rs:54-64)."""
+    d = _write_config(tmp_path, "thinker", {"thinker_config": {
+        "audio_config": {"d_model": 1024, "encoder_layers": 24, "encoder_attention_heads": 16,
+                         "encoder_ffn_dim": 4096, "output_dim": 2048},
+        "text_config": {"hidden_size": 2048}}})
+    assert qasr.read_audio_config(d) == qasr.audio_config("1.7b")
+
+
+@pytest.mark.parametrize("obj,needle", [
+    ({"text_config": {}}, "missing thinker_config and audio_config"),
+    ({"thinker_config": {"text_config": {}}}, "no audio_config"),
+    ({"audio_config": {"d_model": -4}}, "d_model is not a positive integer"),
+    ({"audio_config": {"n_window": 2.5}}, "n_window is not a positive integer"),
+])
+def test_read_audio_config_errors(qasr, tmp_path, obj, needle):
+    d = _write_config(tmp_path, "bad", obj)
+    with pytest.raises(qasr.DecoderError) as e:
+        qasr.read_audio_config(d)
+    assert e.value.status == 1 and needle in str(e.value)
