@@ -1,0 +1,52 @@
+"""The bench's algorithmic accounting, checked on the CPU against the figures the hot-path
+survey derives from the reference's shapes (per-step weight bytes of the four configs,
+114,688 KV bytes per position) and the audio tower's FLOP count against a direct
+count of its GEMM shapes."""
+import importlib.util
+
+import pytest
+
+from conftest import ROOT
+
+
+def _bench():
+    spec = importlib.util.spec_from_file_location("bench_mod", ROOT / "bench.py")
+    m = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(m)
+    return m
+
+
+@pytest.mark.parametrize("preset,int8,want", [
+    # linears (1 B int8 + 2 B f16 scale per row, or 2 B f16) + the f16 tied lm_head; the
+    # bench adds the f32 RMSNorm gains on top (28 x (2 hs + 2 x 128) + hs floats)
+    ("0.6b", False, 1_191_968_768), ("0.6b", True, 752_254_976),
+    ("1.7b", False, 3_440_902_144), ("1.7b", True, 2_032_762_880),
+])
+def test_weight_bytes_per_step(qasr, preset, int8, want):
+    b = _bench()
+    cfg = qasr.text_config(preset)
+    w, kv = b.algorithmic_bytes(cfg, [0])
+    hs = cfg["hidden_size"]
+    norms = cfg["num_hidden_layers"] * (2 * hs + 2 * cfg["head_dim"]) * 4 + hs * 4
+    if not int8:
+        # the bench counts the int8 layout; an f16 step moves 2 B per linear weight, no scales
+        L, I = cfg["num_hidden_layers"], cfg["intermediate_size"]
+        qd, kvd = cfg["num_attention_heads"] * 128, cfg["num_key_value_heads"] * 128
+        lin = (qd + 2 * kvd) * hs + hs * qd + 2 * I * hs + hs * I
+        rows = (qd + 2 * kvd) + hs + 2 * I + hs
+        w = w - L * (lin + 2 * rows) + L * 2 * lin
+    assert w - norms == want
+    # one appended position: K + V of 8 kv heads x 128 dims x 28 layers, f16 (both sizes)
+    assert kv == 114_688
+
+
+def test_audio_flops_direct_count(qasr):
+    b = _bench()
+    cfg = qasr.audio_config("0.6b")
+    T, flops = b.audio_flops(qasr, cfg, 3000)
+    assert T == 390
+    d, f, C = 896, 3584, 480
+    convs = 2 * 30 * (32 * 25 + 16 * 13) * C * 9 * C + 2 * 30 * 64 * 50 * C * 9
+    gemms = 2 * T * C * 16 * d + 18 * 2 * T * (4 * d * d + 2 * d * f) + 2 * T * (d * d + d * 1024)
+    attn = 18 * 4 * (3 * 104 * 104 + 78 * 78) * d
+    assert flops == convs + gemms + attn
