@@ -273,7 +273,7 @@ class TextDecoder:
     def _err(self) -> str:
         if not self._ctx:
             return "no context"
-        return lib.qasr_last_error(self._ctx).decode()
+        return lib.qasr_last_error(self._ctx).decode(errors="replace")
 
     def _check(self, st: int):
         if st != QASR_OK:
@@ -518,7 +518,7 @@ def read_model_config(model_dir: str) -> dict:
     err = ctypes.create_string_buffer(512)
     st = lib.qasr_read_model_config(str(model_dir).encode(), ctypes.byref(mc), err, 512)
     if st != QASR_OK:
-        raise DecoderError(st, err.value.decode())
+        raise DecoderError(st, err.value.decode(errors="replace"))
     t = mc.text
     cfg = {f: getattr(t, f) for f, _ in TextConfig._fields_}
     return {"text_config": cfg, "rope_theta": mc.rope_theta,
@@ -534,7 +534,7 @@ class Checkpoint:
         err = ctypes.create_string_buffer(512)
         st = lib.qasr_checkpoint_open(str(model_dir).encode(), ctypes.byref(h), err, 512)
         if st != QASR_OK:
-            raise DecoderError(st, err.value.decode())
+            raise DecoderError(st, err.value.decode(errors="replace"))
         self._h = h
 
     def close(self):
@@ -556,7 +556,7 @@ class Checkpoint:
 
     def _check(self, st: int):
         if st != QASR_OK:
-            raise DecoderError(st, lib.qasr_checkpoint_last_error(self._h).decode())
+            raise DecoderError(st, lib.qasr_checkpoint_last_error(self._h).decode(errors="replace"))
 
     def __len__(self) -> int:
         return int(lib.qasr_checkpoint_tensor_count(self._h))
@@ -568,7 +568,7 @@ class Checkpoint:
         nd = ctypes.c_int(0)
         self._check(lib.qasr_checkpoint_tensor_info(self._h, name.encode(), dt, 16, _ptr(shape), 8,
                                                     ctypes.byref(nd)))
-        return dt.value.decode(), tuple(int(x) for x in shape[:nd.value])
+        return dt.value.decode(errors="replace"), tuple(int(x) for x in shape[:nd.value])
 
     def weight_format(self, prefix: str | None = None) -> int:
         f = ctypes.c_int(0)
@@ -607,7 +607,7 @@ def kernel_pack_weights(device: int, stream: int, weight_format: int, w_rowmajor
                                       ctypes.c_void_p(w_rowmajor_ptr), n_out, k, ctypes.c_void_p(w_tiled_ptr),
                                       err, 512)
     if st != QASR_OK:
-        raise DecoderError(st, err.value.decode())
+        raise DecoderError(st, err.value.decode(errors="replace"))
 
 
 def kernel_gemm(device: int, stream: int, weight_format: int, w_ptr: int, scale_ptr: int | None,
@@ -618,7 +618,7 @@ def kernel_gemm(device: int, stream: int, weight_format: int, w_ptr: int, scale_
                               ctypes.c_void_p(scale_ptr or 0), n_out, k, ctypes.c_void_p(x_ptr), ldx,
                               rows, ctypes.c_void_p(out_ptr), ldo, int(accumulate), err, 512)
     if st != QASR_OK:
-        raise DecoderError(st, err.value.decode())
+        raise DecoderError(st, err.value.decode(errors="replace"))
 
 
 def kernel_gemm_traced(device: int, stream: int, weight_format: int, w_ptr: int, scale_ptr: int | None,
@@ -633,7 +633,7 @@ def kernel_gemm_traced(device: int, stream: int, weight_format: int, w_ptr: int,
                                      rows, ctypes.c_void_p(out_ptr), ldo, int(accumulate),
                                      ctypes.c_void_p(trace_ptr), ctypes.byref(grid), err, 512)
     if st != QASR_OK:
-        raise DecoderError(st, err.value.decode())
+        raise DecoderError(st, err.value.decode(errors="replace"))
     return grid.value
 
 
@@ -646,7 +646,7 @@ def kernel_attention(device: int, stream: int, q_ptr: int, q_ld: int, out_ptr: i
                                    V(page_table_ptr), max_pages, layers, nkv, layer, V(row_slot_ptr),
                                    V(row_pos_ptr), rows, err, 512)
     if st != QASR_OK:
-        raise DecoderError(st, err.value.decode())
+        raise DecoderError(st, err.value.decode(errors="replace"))
 
 
 def kernel_attention_traced(device: int, stream: int, q_ptr: int, q_ld: int, out_ptr: int, pool_ptr: int,
@@ -658,7 +658,7 @@ def kernel_attention_traced(device: int, stream: int, q_ptr: int, q_ld: int, out
                                           V(page_table_ptr), max_pages, layers, nkv, layer, V(row_slot_ptr),
                                           V(row_pos_ptr), rows, V(trace_ptr), err, 512)
     if st != QASR_OK:
-        raise DecoderError(st, err.value.decode())
+        raise DecoderError(st, err.value.decode(errors="replace"))
 
 
 def kernel_attention_noalloc(device: int, stream: int, q_ptr: int, q_ld: int, out_ptr: int, pool_ptr: int,
@@ -672,7 +672,7 @@ def kernel_attention_noalloc(device: int, stream: int, q_ptr: int, q_ld: int, ou
                                            V(page_table_ptr), max_pages, layers, nkv, layer, V(row_slot_ptr),
                                            V(row_pos_ptr), rows, err, 512)
     if st != QASR_OK:
-        raise DecoderError(st, err.value.decode())
+        raise DecoderError(st, err.value.decode(errors="replace"))
 
 
 def kernel_kv_append(device: int, stream: int, k_ptr: int, v_ptr: int, pool_ptr: int,
@@ -684,7 +684,7 @@ def kernel_kv_append(device: int, stream: int, k_ptr: int, v_ptr: int, pool_ptr:
                                    max_pages, layers, nkv, layer, V(row_slot_ptr), V(row_pos_ptr), rows,
                                    err, 512)
     if st != QASR_OK:
-        raise DecoderError(st, err.value.decode())
+        raise DecoderError(st, err.value.decode(errors="replace"))
 
 
 def kv_page_swizzle(pool: np.ndarray) -> np.ndarray:

@@ -102,7 +102,7 @@ def read_audio_config(model_dir: str) -> dict:
     err = ctypes.create_string_buffer(512)
     st = lib.qasr_read_audio_config(str(model_dir).encode(), ctypes.byref(c), err, 512)
     if st != QASR_OK:
-        raise DecoderError(st, err.value.decode())
+        raise DecoderError(st, err.value.decode(errors="replace"))
     return {n: int(getattr(c, n)) for n, _ in AudioConfig._fields_}
 
 
@@ -184,7 +184,7 @@ class AudioEncoder:
         err = ctypes.create_string_buffer(512)
         st = lib.qasr_audio_create(ctypes.byref(self._c), device, ctypes.byref(h), err, 512)
         if st != QASR_OK:
-            raise DecoderError(st, err.value.decode())
+            raise DecoderError(st, err.value.decode(errors="replace"))
         self._h = h
         self._keep = []
 
@@ -207,7 +207,7 @@ class AudioEncoder:
 
     def _check(self, st: int):
         if st != QASR_OK:
-            raise DecoderError(st, lib.qasr_audio_last_error(self._h).decode())
+            raise DecoderError(st, lib.qasr_audio_last_error(self._h).decode(errors="replace"))
 
     @property
     def stream(self) -> int:
