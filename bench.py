@@ -44,6 +44,7 @@ FALLBACK_HBM_GBS = 6650.0
 CHAIN_TRAFFIC_BYTES = 56274944 + 623360
 CHAIN_TRAFFIC_SOURCE = "ncu dram bytes of one middle launch of kernel_bench.py step --layers 2 (32 rows)"
 METRIC = "decode tokens/sec (box) 1.7B INT8 @1/2/4/8 B200; % HBM roofline"
+TRACED_STEPS = 8  # steps of the traced pass after the timed region
 
 
 def load_pkg():
@@ -117,19 +118,27 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(rows)}
 
 
-def cpu_baseline(cfg, sample_tokens=12, prefix_rows=16):
-    """The reference's CPU decoder (restated in oracle/) on this host's cores: one slot,
-    `prefix_rows` prefill, then `sample_tokens` timed decode steps (tokens/s)."""
+def cpu_baseline(cfg, int8=True, sample_tokens=12, prefix_rows=16, kv_len=800, label="cfg4"):
+    """The reference's CPU decoder (restated in oracle/) on this host's cores: one slot
+    (the reference's CPU path decodes one segment at a time, src/inference.rs:462-463),
+    a `prefix_rows`-row prefill, the position then moved to `kv_len` (the workload's mean
+    KV length: attention then runs over kv_len positions, as it would after a real
+    prefix; a real 800-row CPU prefill would take about a minute, and what attention
+    costs does not depend on the cached values), then `sample_tokens` timed greedy steps.
+    Inputs come from liboracle's copy of the generator (oracle/inputs.py): this leg loads
+    no B200 library."""
+    from oracle.inputs import SyntheticModel, build_rope_tables
     from oracle.oracle import OracleModel, OracleSeq
-    pkg = load_pkg()
-    model = pkg.SyntheticModel(cfg, seed=SEED)
+    model = SyntheticModel(cfg, seed=SEED)
     om = OracleModel(cfg)
-    om.load_model(model, int8=True)
-    cos, sin = pkg.build_rope_tables(MAX_SEQ)
+    om.load_model(model, int8=int8)
+    max_seq = max(MAX_SEQ, kv_len + sample_tokens + 8)
+    cos, sin = build_rope_tables(max_seq)
     om.set_rope_tables(cos, sin)
-    seq = OracleSeq(om, MAX_SEQ)
+    seq = OracleSeq(om, max_seq)
     hidden, _ = model.prefix(0, 0, n_text=prefix_rows, n_before=9)
     seq.prefill(hidden)
+    seq.set_pos(max(prefix_rows, kv_len))
     seq.step()  # warm-up
     t0 = time.perf_counter()
     for _ in range(sample_tokens):
@@ -138,24 +147,26 @@ def cpu_baseline(cfg, sample_tokens=12, prefix_rows=16):
     threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
     seq.close()
     om.close()
+    wdesc = "INT8 weights dequantised to f32" if int8 else "f16 weights widened to f32"
     return {"value": sample_tokens / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"1 slot, {prefix_rows}-row prefix, {sample_tokens} timed greedy steps after 1 "
-                      f"warm-up (1.7B INT8 weights dequantised to f32 as the reference CPU decoder keeps "
-                      f"them); attention is <3% of a CPU step at these lengths"}
+            "sample": f"{label}: 1 slot, {prefix_rows}-row prefill, position moved to {kv_len} (the workload's "
+                      f"mean KV length), {sample_tokens} timed greedy steps after 1 warm-up ({wdesc}, as the "
+                      f"reference CPU decoder keeps them)"}
 
 
 def run_reference(args, rank, world):
-    """--impl reference: the reference CPU decoder path (restated, oracle/) on all host cores."""
+    """--impl reference: the reference CPU decoder path (restated, oracle/) on all host cores.
+    Loads only oracle libraries (liboracle.so: the restated decoder + the input generator)."""
     if rank != 0:
         return
-    pkg = load_pkg()
-    cfg = pkg.text_config("1.7b")
+    from oracle.inputs import text_config
+    cfg = text_config("1.7b")
     sample = max(3, min(args.steps, 12))
     cb = cpu_baseline(cfg, sample_tokens=sample)
     line = {"metric": METRIC, "impl": "reference", "value": cb["value"], "unit": "tokens/s",
             "n_gpus": world, "steps": sample, "warmup": 1, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32 (int8 weights dequantised to f16)",
-            "data": "synthetic", "config": {"workload": "cfg4: Qwen3-ASR-1.7B INT8 decode, 1 slot on CPU",
+            "data": "synthetic", "config": {"workload": "cfg4: Qwen3-ASR-1.7B INT8 decode, 1 slot on CPU at KV 800",
                                             "model": "qwen3-asr-1.7b-text-decoder"},
             "cpu_baseline": cb,
             "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -357,7 +368,9 @@ def chain_timing(dec, cfg):
     nbytes = lin + 2 * rows
     t = float(np.mean(durs))
     return {"seconds": t, "bytes": nbytes, "gbs": nbytes / t / 1e9, "launches_per_step": L + 1,
-            "share_of_step": None, "timing": "in-kernel %globaltimer stamps, mean of the step's middle launches"}
+            "share_of_step": None,
+            "timing": "in-kernel %globaltimer stamps of a traced pass after the timed region (the timed steps "
+                      "run untraced), mean of the last traced step's middle launches"}
 
 
 def main():
@@ -411,11 +424,12 @@ def main():
     cfg = pkg.text_config("1.7b")
     model = pkg.SyntheticModel(cfg, seed=SEED)
     rng = np.random.default_rng(SEED + 7919 * rank)
-    # trace=True: the decode-chain launches stamp %globaltimer per operation (a few global
-    # stores per CTA and unit); the stamps of the last timed step give the chain kernel's
-    # own duration for the roofline line
+    # trace=True allocates the stamp buffers; the timed steps run with the stamps off
+    # (set_trace(False)), a separate traced pass after them gives the chain kernel's own
+    # duration for the roofline line (its %globaltimer stamps per CTA and operation)
     dec = pkg.TextDecoder(cfg, weight_format=pkg.WEIGHTS_INT8, max_slots=SLOTS_PER_GPU, max_seq=MAX_SEQ,
                           device=local, trace=True)
+    dec.set_trace(False)
     t_load = time.perf_counter()
     dec.load_model(model)
     cos, sin = pkg.build_rope_tables(MAX_SEQ)
@@ -493,7 +507,6 @@ def main():
     torch.cuda.synchronize()
     t_wall = time.perf_counter() - t_wall
     launches = pkg.launch_count() - launches0
-    chain = chain_timing(dec, cfg)
     clk = clocks.stop()
     if dist is not None:
         dist.barrier()
@@ -514,6 +527,24 @@ def main():
             kv_len[i] += 1
     t_e2e = time.perf_counter() - t_e2e - (prefill_time[0] - e2e_pf0)
 
+    # ---- traced pass (not timed for the metric): the chain kernel's own launch durations,
+    # and the step time with the stamps on beside the untraced one (their cost)
+    dec.set_trace(True)
+    traced = []
+    for it in range(3 + TRACED_STEPS):
+        refill_if_full()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        dec.step_batch(slots, read_tokens=False)
+        b.record(stream)
+        b.synchronize()
+        if it >= 3:
+            traced.append(a.elapsed_time(b) * 1e-3)
+        for i in range(SLOTS_PER_GPU):
+            kv_len[i] += 1
+    chain = chain_timing(dec, cfg)
+    dec.set_trace(False)
+
     # ---- dominant kernels, timed alone at the bench shapes
     kernels = time_kernels(pkg, torch, dec, cfg, slots, stream, kv_len)
 
@@ -529,6 +560,8 @@ def main():
         step_gbs = step_bytes / (decode_max / args.steps) / 1e9
         if chain is not None:
             chain["share_of_step"] = chain["seconds"] * chain["launches_per_step"] / (decode_max / args.steps)
+            chain["traced_step_ms"] = statistics.median(traced) * 1e3
+            chain["untraced_step_ms"] = ms_step
             kernels["decode_chain"] = chain
             dom_name = "decode_chain"  # the largest share of the step (~55-60%)
         else:

@@ -195,6 +195,19 @@ qasr_status qasr_read_trace(qasr_ctx* ctx, uint64_t* out, int cap, int* count);
  * *count receives layers * ctas * slots; at most `cap` values are written. */
 #define QASR_ATTN_TRACE_SLOTS 8
 qasr_status qasr_read_attn_trace(qasr_ctx* ctx, uint64_t* out, int cap, int* count);
+/* Switch the stamps of a QASR_FLAG_TRACE context off (0) or back on (default on): the
+ * steps recorded afterwards carry no trace stores, so a caller can time untraced steps
+ * and take a traced pass apart.  QASR_ERR_STATE without the trace buffers. */
+qasr_status qasr_set_trace(qasr_ctx* ctx, int enabled);
+
+/* Diagnostic of the device-side error path (the reference maps device failures to an
+ * Err, src/decoder.rs:4458-4486): launches one kernel on the context's stream whose two
+ * bounded waits — on an mbarrier nothing arrives at, and on a device word nothing sets,
+ * the wait forms the kernels use inside a CTA and across CTAs — give up after `wait_us`
+ * (1..2,000,000) microseconds, exactly as a stalled kernel's waits do after 2 s.  Returns
+ * what any call then returns, QASR_ERR_DEVICE_TIMEOUT with the site in
+ * qasr_last_error, and clears the status so the context stays usable.  Faults nothing. */
+qasr_status qasr_check_wait_timeout(qasr_ctx* ctx, uint32_t wait_us);
 
 /* --- checkpoints (src/weights.rs, src/config.rs) -------------------------------- */
 /* The decode path's part of a model directory's config.json (AsrConfig::from_file,

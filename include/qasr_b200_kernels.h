@@ -57,7 +57,9 @@ qasr_status qasr_kernel_gemm_traced(int device, void* stream, int weight_format,
  * 128-dim row stored swizzled: dim d of position p sits at column
  * ((d/8) ^ (p%8))*8 + d%8 (16-byte chunks permuted by the position's low 3 bits, so
  * tensor-core fragment loads from shared memory are bank-conflict free); page_table:
- * [slots][max_pages] int32; row r attends positions 0..row_pos[r] of slot row_slot[r]. */
+ * [slots][max_pages] int32; row r attends positions 0..row_pos[r] of slot row_slot[r].
+ * Only enqueues (for timing with the caller's events): a bounded device-side wait that
+ * gives up is not reported by this call; the traced and no-alloc variants report it. */
 qasr_status qasr_kernel_attention(int device, void* stream, const uint16_t* q, int q_ld,
                                   uint16_t* out, const uint16_t* kv_pool, const int* page_table,
                                   int max_pages, int layers, int nkv, int layer,
@@ -67,7 +69,8 @@ qasr_status qasr_kernel_attention(int device, void* stream, const uint16_t* q, i
 /* qasr_kernel_attention with a latency trace: if `trace` (device, SM count x 8 uint64) is
  * non-NULL each CTA records %globaltimer stamps (entry, unit table ready, first stage
  * landed, first unit merged, last stage consumed, last unit merged, producer done) and
- * the number of units it processed. */
+ * the number of units it processed.  Waits for its launches and returns
+ * QASR_ERR_DEVICE_TIMEOUT if a bounded device-side wait gave up. */
 qasr_status qasr_kernel_attention_traced(int device, void* stream, const uint16_t* q, int q_ld,
                                          uint16_t* out, const uint16_t* kv_pool,
                                          const int* page_table, int max_pages, int layers,
@@ -76,17 +79,20 @@ qasr_status qasr_kernel_attention_traced(int device, void* stream, const uint16_
                                          char* err, int errlen);
 
 /* qasr_kernel_attention without any device allocation — for callers that may not call
- * cudaMalloc: code running while a CUDA graph is being captured, hosts that hand the
- * library a fixed memory budget up front, and real-time audio paths that must not touch
- * the allocator between frames.  No counterpart in the reference (its wgpu decoder owns
- * all buffers).  The scratch is one static device array inside the library (about
- * 2 MiB, held by every GPU that loads the library until the process exits), so:
+ * cudaMalloc: hosts that hand the library a fixed memory budget up front (an embedding
+ * application that owns all device memory), and real-time audio paths that must not
+ * touch the allocator between frames (an allocation can block on the driver for
+ * milliseconds).  No counterpart in the reference (its wgpu decoder owns all buffers).
+ * The scratch is one static device array inside the library (about 2 MiB) plus an
+ * 8-byte status word, held by every GPU that loads the library until the process exits, so:
  *   - at most 64 query rows and 8 kv heads per call; larger calls fail with
  *     QASR_ERR_CAPACITY (use qasr_kernel_attention);
  *   - the first call on a device looks the array's address up
  *     (cudaGetSymbolAddress): make that first call before any stream capture;
- *   - all calls share the array: calls that overlap on the GPU (other streams, other
- *     threads) race and must be serialised by the caller.
+ *   - all calls share the array and the status word: calls that overlap on the GPU
+ *     (other streams, other threads) race and must be serialised by the caller;
+ *   - the call waits for its kernels on `stream` and reads the status word back, so a
+ *     bounded device-side wait that gave up returns QASR_ERR_DEVICE_TIMEOUT.
  * Same inputs, outputs and results as qasr_kernel_attention. */
 qasr_status qasr_kernel_attention_noalloc(int device, void* stream, const uint16_t* q, int q_ld,
                                           uint16_t* out, const uint16_t* kv_pool,

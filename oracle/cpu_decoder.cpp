@@ -467,7 +467,9 @@ int oracle_step(oracle_seq* s, int32_t* token, float* logits) {
 
 void oracle_set_last_token(oracle_seq* s, int32_t tok) { s->last_token = static_cast<uint32_t>(tok); }
 int oracle_pos(const oracle_seq* s) { return s->pos; }
-void oracle_set_pos(oracle_seq* s, int pos) { s->pos = pos; }
+void oracle_set_pos(oracle_seq* s, int pos) {
+  if (pos >= 0 && pos <= s->max_seq) s->pos = pos;  // out-of-range positions are ignored
+}
 
 int oracle_last_hidden(const oracle_seq* s, uint16_t* out, int rows) {
   if (rows > s->last_rows) return 1;

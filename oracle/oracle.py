@@ -25,7 +25,9 @@ def _stale() -> bool:
     if not LIB_PATH.exists():
         return True
     t = LIB_PATH.stat().st_mtime
-    return any(p.stat().st_mtime > t for p in (HERE / "cpu_decoder.cpp", HERE / "oracle.h"))
+    srcs = (HERE / "cpu_decoder.cpp", HERE / "oracle.h", HERE / "Makefile",
+            HERE.parent / "qwen3-asr-wgpu_b200" / "csrc" / "synth.cpp", HERE.parent / "include" / "qasr_synth.h")
+    return any(p.exists() and p.stat().st_mtime > t for p in srcs)
 
 
 def _load():
@@ -199,6 +201,11 @@ class OracleSeq:
     @property
     def pos(self) -> int:
         return lib.oracle_pos(self._s)
+
+    def set_pos(self, pos: int):
+        """Move the position (the reference decoder's `pos` field): the next step writes
+        row `pos` and attends over positions 0..pos."""
+        lib.oracle_set_pos(self._s, int(pos))
 
     def kv_rows(self, layer: int, kv_head: int, pos0: int, n: int):
         hd = self.model.cfg["head_dim"]

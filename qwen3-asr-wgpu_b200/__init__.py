@@ -53,7 +53,7 @@ EXPORTED_SYMBOLS = (
     "qasr_slot_pos", "qasr_set_slot_pos", "qasr_set_input_token", "qasr_set_input_tokens",
     "qasr_prefill", "qasr_step", "qasr_prefill_batch", "qasr_step_batch", "qasr_read_logits",
     "qasr_read_trace",
-    "qasr_read_attn_trace",
+    "qasr_read_attn_trace", "qasr_check_wait_timeout", "qasr_set_trace",
     "qasr_build_rope_tables", "qasr_build_dim_map", "qasr_dequant_i8",
     "qasr_kernel_pack_weights", "qasr_kernel_gemm", "qasr_kernel_gemm_traced", "qasr_kernel_attention",
     "qasr_kernel_attention_noalloc", "qasr_kernel_attention_traced", "qasr_kernel_kv_append",
@@ -174,6 +174,8 @@ def _load() -> ctypes.CDLL:
     lib.qasr_read_logits.argtypes = [P, P, I]
     lib.qasr_read_trace.argtypes = [P, P, I, ctypes.POINTER(I)]
     lib.qasr_read_attn_trace.argtypes = [P, P, I, ctypes.POINTER(I)]
+    lib.qasr_check_wait_timeout.argtypes = [P, ctypes.c_uint32]
+    lib.qasr_set_trace.argtypes = [P, I]
     lib.qasr_build_rope_tables.argtypes = [P, P, I, I, ctypes.c_double, P, I, I]
     lib.qasr_build_dim_map.argtypes = [P, I, I, I, P]
     lib.qasr_dequant_i8.argtypes = [P, P, I, I, P]
@@ -433,6 +435,16 @@ class TextDecoder:
         out = np.zeros((rows, self.cfg["vocab_size"]), dtype=np.float32)
         self._check(lib.qasr_read_logits(self._ctx, _ptr(out), rows))
         return out
+
+    def set_trace(self, enabled: bool):
+        """Turn the decode-chain / attention stamps of a trace=True decoder off or on
+        for the steps that follow (qasr_set_trace)."""
+        self._check(lib.qasr_set_trace(self._ctx, 1 if enabled else 0))
+
+    def check_wait_timeout(self, wait_us: int):
+        """Run the bounded-wait diagnostic (qasr_check_wait_timeout): raises the
+        DecoderError a stalled device wait produces (QASR_ERR_DEVICE_TIMEOUT)."""
+        self._check(lib.qasr_check_wait_timeout(self._ctx, int(wait_us)))
 
 
 def _batch_call(fn, first_arg, segments, width, eos, kv_step, batch_seq_cap, on_item, should_stop):

@@ -402,7 +402,13 @@ struct qasr_checkpoint {
       t.data = data + b;
       t.nbytes = static_cast<size_t>(en - b);
       const size_t es = dtype_size(t.dtype);
-      if (es != 0 && static_cast<size_t>(t.numel()) * es != t.nbytes)
+      // element count and byte size without wrap-around: a shape whose product overflows
+      // (e.g. [2^33, 2^31]) would otherwise wrap to a small count and pass the size check
+      uint64_t count = 1, bytes = 0;
+      for (int64_t d : t.shape)
+        if (__builtin_mul_overflow(count, static_cast<uint64_t>(d), &count) || count > (1ull << 62))
+          return fail(QASR_ERR_INVALID_ARG, path + ": shape of " + kv.first + " overflows");
+      if (es != 0 && (__builtin_mul_overflow(count, static_cast<uint64_t>(es), &bytes) || bytes != t.nbytes))
         return fail(QASR_ERR_INVALID_ARG, path + ": " + kv.first + " holds " + std::to_string(t.nbytes) +
                                               " bytes for " + std::to_string(t.numel()) + " x " + t.dtype);
       (*out)[kv.first] = std::move(t);

@@ -61,15 +61,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // Wait for the phase with `parity` to complete.  Returns false (after recording the
-// error) when the wait timed out or another role of the CTA already aborted.
+// error) when the wait timed out (after `limit_ns`) or another role of the CTA already
+// aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          uint32_t* status, uint32_t site) {
+                                          uint32_t* status, uint32_t site, uint64_t limit_ns = QASR_WAIT_NS) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (abort_flag != nullptr && *abort_flag) return false;
-    if (globaltimer() - t0 > QASR_WAIT_NS) {
+    if (globaltimer() - t0 > limit_ns) {
       report_error(status, DEVERR_TIMEOUT, site);
       if (abort_flag != nullptr) *abort_flag = 1;
       return false;
@@ -247,15 +248,18 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
 // ---------------------------------------------------------------- f16 helpers
 __device__ __forceinline__ float f16_round(float v) { return __half2float(__float2half_rn(v)); }
 
-// Order-preserving key of an f32 logit (NaN sorts lowest, -0 == +0) packed with the
-// complement of its index, so max(key) = largest logit, lowest index among ties — the
-// strict `>` scan of argmax (src/cpu_decoder.rs:474-482).
+// Order-preserving key of an f32 logit (-0 == +0) packed with the complement of its
+// index, so max(key) = largest logit, lowest index among ties — the strict `>` scan of
+// argmax (src/cpu_decoder.rs:474-482), NaNs included: that scan starts from index 0 and
+// compares `v > logits[best]`, so a NaN at index 0 is never replaced (the answer is 0)
+// and a NaN anywhere else is never taken.  Index 0's NaN therefore gets the largest key,
+// every other NaN the smallest.
 __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
   uint32_t u = __float_as_uint(v);
   if (v == 0.0f) u = 0u;
   uint32_t k;
   if (v != v) {
-    k = 0u;
+    k = idx == 0 ? 0xffffffffu : 0u;
   } else {
     k = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
   }

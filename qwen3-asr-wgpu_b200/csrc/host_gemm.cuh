@@ -159,7 +159,7 @@ inline GemmShape gemm_shape(int n_out, int k, bool int8, int rows, int num_sms, 
   return s;
 }
 
-// Dynamic shared memory limits and kernel attributes (once per process).
+// Dynamic shared memory limits and kernel attributes (once per device, on the current one).
 cudaError_t init_kernel_attrs(std::string* err);
 
 }  // namespace qasr

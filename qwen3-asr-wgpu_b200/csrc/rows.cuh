@@ -86,6 +86,26 @@ __global__ void finalize_rows_kernel(unsigned long long* __restrict__ best, int 
   pos[slot] = row_pos[r] + 1;
 }
 
+// The bounded-wait error path, exercised without a fault: one thread waits on an
+// mbarrier that nothing arrives on, then polls a word that nothing sets (the two wait
+// forms the kernels use: within a CTA, and on another CTA's data), each giving up after
+// `limit_ns` and recording DEVERR_TIMEOUT (first site wins) in the status word.
+__global__ void wait_timeout_probe_kernel(const unsigned int* never_set, uint64_t limit_ns, uint32_t* status) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  fence_mbar_init();
+  mbar_wait(&bar, 0, nullptr, status, 0x7f1, limit_ns);
+  const uint64_t t0 = globaltimer();
+  while (*reinterpret_cast<const volatile unsigned int*>(never_set) == 0u) {
+    if (globaltimer() - t0 > limit_ns) {
+      report_error(status, DEVERR_TIMEOUT, 0x7f2);
+      break;
+    }
+    __nanosleep(256);
+  }
+}
+
 __global__ void scatter_tokens_kernel(int* __restrict__ next_tok, const int* __restrict__ slots,
                                       const int* __restrict__ toks, int n) {
   griddep_wait();

@@ -41,15 +41,25 @@ static cudaError_t gemm_set_attr(int dyn) {
                               dyn);
 }
 
+// cudaFuncSetAttribute applies to the device current when it is called, so the set-up
+// runs once for every device a context or probe uses (with that device current).
 cudaError_t init_kernel_attrs(std::string* err) {
-  static std::once_flag once;
-  static cudaError_t result = cudaSuccess;
-  std::call_once(once, [] {
+  constexpr int kMaxDev = 64;
+  static std::once_flag once[kMaxDev];
+  static cudaError_t results[kMaxDev] = {};
+  int dev = 0;
+  cudaError_t de = cudaGetDevice(&dev);
+  if (de == cudaSuccess && (dev < 0 || dev >= kMaxDev)) de = cudaErrorInvalidDevice;
+  if (de != cudaSuccess) {
+    if (err) *err = std::string("kernel attribute setup: ") + cudaGetErrorString(de);
+    return de;
+  }
+  cudaError_t& result = results[dev];
+  std::call_once(once[dev], [&result, dev] {
     cudaFuncAttributes fa{};
     result = cudaFuncGetAttributes(&fa, gemm_tc_kernel<true, EPI_QKV>);
     if (result != cudaSuccess) return;
-    int optin = 0, dev = 0;
-    cudaGetDevice(&dev);
+    int optin = 0;
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     g_dyn_smem_max = optin - static_cast<int>(fa.sharedSizeBytes) - 256;
     const int d = g_dyn_smem_max;
@@ -230,6 +240,7 @@ struct qasr_ctx {
   int* chain_row_page = nullptr;        // [CHAIN_MAX_ROWS]
   __half* chain_row_rope = nullptr;     // [CHAIN_MAX_ROWS][256]
   unsigned long long* chain_trace = nullptr;  // QASR_FLAG_TRACE: [L + 1][sms][slots]
+  bool trace_on = false;  // stamps written by the next recorded steps (qasr_set_trace)
   uint32_t* status = nullptr;
   int* pinned_tok = nullptr;  // synchronous staging
   int* pinned_in = nullptr;   // input-token staging, reusable once ev_in completed
@@ -381,7 +392,8 @@ qasr_status launch_attention(qasr_ctx* c, int layer, int rows, const int* rs, co
   a.ws = c->attn_ws;
   a.early = early;
   a.status = c->status;
-  if (c->attn_trace) a.trace = c->attn_trace + static_cast<size_t>(layer) * c->num_sms * ATTN_TRACE_SLOTS;
+  if (c->attn_trace && c->trace_on)
+    a.trace = c->attn_trace + static_cast<size_t>(layer) * c->num_sms * ATTN_TRACE_SLOTS;
   CK(launch_attention_pair(a, c->num_sms, c->stream, true, merge_pdl), "attention launch");
   return QASR_OK;
 }
@@ -576,7 +588,7 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
   {
     ChainArgs a = base;
     a.barrier = c->chain_bar;
-    a.trace = c->chain_trace;
+    a.trace = c->trace_on ? c->chain_trace : nullptr;
     const LayerDev& L0 = c->layers[0];
     a.gemms[0] = gemm(L0.qkv, 0, 0);
     a.next_first = gemm(L0.o, 1, 1);
@@ -601,7 +613,7 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
     const LayerDev& Ld = c->layers[l];
     ChainArgs a = base;
     a.barrier = c->chain_bar + l + 1;
-    if (c->chain_trace) a.trace = c->chain_trace + static_cast<size_t>(l + 1) * sms * CHAIN_TRACE_SLOTS;
+    if (c->chain_trace && c->trace_on) a.trace = c->chain_trace + static_cast<size_t>(l + 1) * sms * CHAIN_TRACE_SLOTS;
     a.gemms[0] = gemm(Ld.o, 1, 1);
     if (l + 1 < L) a.next_first = gemm(c->layers[l + 1].o, 1, 1);
     a.gemms[1] = gemm(Ld.gu, 0, 2);
@@ -889,6 +901,7 @@ qasr_status qasr_create(const qasr_text_config* cfg, const qasr_options* opts, i
          (s = dalloc(c, &c->attn_trace, static_cast<size_t>(L) * c->num_sms * ATTN_TRACE_SLOTS,
                      "attention trace"))))
       return s;
+    c->trace_on = c->chain_trace != nullptr;
   }
   CK(cudaMallocHost(&c->pinned_tok, sizeof(int) * opts->max_slots * 2), "pinned alloc");
   CK(cudaMallocHost(&c->pinned_in, sizeof(int) * opts->max_slots * 2), "pinned alloc");
@@ -1289,6 +1302,27 @@ qasr_status qasr_read_trace(qasr_ctx* c, uint64_t* out, int cap, int* count) {
   return check_device_status(c);
 }
 
+qasr_status qasr_set_trace(qasr_ctx* c, int enabled) {
+  if (!c) return QASR_ERR_INVALID_ARG;
+  if (enabled && !c->chain_trace)
+    return fail(c, QASR_ERR_STATE, "no trace buffers: create the context with QASR_FLAG_TRACE (int8 weights)");
+  if (c->trace_on != (enabled != 0)) drop_graph(c);  // the recorded launches carry the trace pointers
+  c->trace_on = enabled != 0;
+  return QASR_OK;
+}
+
+qasr_status qasr_check_wait_timeout(qasr_ctx* c, uint32_t wait_us) {
+  if (!c) return QASR_ERR_INVALID_ARG;
+  if (wait_us == 0 || wait_us > 2000000u) return fail(c, QASR_ERR_INVALID_ARG, "wait_us must be 1..2000000");
+  CK(cudaSetDevice(c->device), "cudaSetDevice");
+  // status[2] is never written by any kernel: the "flag that nothing sets"
+  wait_timeout_probe_kernel<<<1, 32, 0, c->stream>>>(c->status + 2, static_cast<uint64_t>(wait_us) * 1000ull,
+                                                      c->status);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  CK(cudaGetLastError(), "wait probe launch");
+  return check_device_status(c);
+}
+
 qasr_status qasr_read_attn_trace(qasr_ctx* c, uint64_t* out, int cap, int* count) {
   if (!c || !out || !count || cap < 0) return QASR_ERR_INVALID_ARG;
   if (!c->attn_trace) return fail(c, QASR_ERR_STATE, "no trace: create the context with QASR_FLAG_TRACE (int8 weights)");
@@ -1384,22 +1418,18 @@ qasr_status qasr_kernel_gemm_traced(int device, void* stream, int weight_format,
   return QASR_OK;
 }
 
-qasr_status qasr_kernel_attention(int device, void* stream, const uint16_t* q, int q_ld,
-                                  uint16_t* out, const uint16_t* kv_pool, const int* page_table,
-                                  int max_pages, int layers, int nkv, int layer,
-                                  const int* row_slot, const int* row_pos, int rows, char* err,
-                                  int errlen) {
-  return qasr_kernel_attention_traced(device, stream, q, q_ld, out, kv_pool, page_table, max_pages, layers,
-                                      nkv, layer, row_slot, row_pos, rows, nullptr, err, errlen);
-}
+}  // extern "C"
 
-qasr_status qasr_kernel_attention_traced(int device, void* stream, const uint16_t* q, int q_ld,
-                                         uint16_t* out, const uint16_t* kv_pool, const int* page_table,
-                                         int max_pages, int layers, int nkv, int layer,
-                                         const int* row_slot, const int* row_pos, int rows,
-                                         unsigned long long* trace, char* err, int errlen) {
+// The attention probes.  `check`: wait for the launches and report a device-side
+// timeout or bounds error recorded in the probe's status word (the traced diagnostic);
+// without it the call only enqueues (the timed probe).
+static qasr_status attention_probe(int device, void* stream, const uint16_t* q, int q_ld, uint16_t* out,
+                                   const uint16_t* kv_pool, const int* page_table, int max_pages, int layers,
+                                   int nkv, int layer, const int* row_slot, const int* row_pos, int rows,
+                                   unsigned long long* trace, bool check, char* err, int errlen) {
   static std::mutex mu;
   static ProbeWs pws[16];
+  static uint32_t* status_words[16] = {};
   std::lock_guard<std::mutex> lock(mu);
   if (device < 0 || device >= 16 || !q || !out || !kv_pool || !page_table || !row_slot || !row_pos ||
       rows <= 0 || nkv <= 0 || q_ld != 2 * nkv * 128 || layer < 0 || layer >= layers)
@@ -1436,6 +1466,15 @@ qasr_status qasr_kernel_attention_traced(int device, void* stream, const uint16_
   a.trace = trace;
   std::string e;
   if (init_kernel_attrs(&e) != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, e);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (status_words[device] == nullptr) {
+    void* p = nullptr;
+    if (cudaMalloc(&p, 2 * sizeof(uint32_t)) != cudaSuccess) return probe_err(err, errlen, QASR_ERR_OOM, "status word");
+    status_words[device] = static_cast<uint32_t*>(p);
+  }
+  a.status = status_words[device];
+  cudaError_t ce = cudaMemsetAsync(a.status, 0, 2 * sizeof(uint32_t), st);
+  if (ce != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, cudaGetErrorString(ce));
   // one launch per ATTN_MAX_ROWS rows (the unit table of a launch lives in shared memory)
   for (int r0 = 0; r0 < rows; r0 += ATTN_MAX_ROWS) {
     AttnArgs b = a;
@@ -1444,10 +1483,41 @@ qasr_status qasr_kernel_attention_traced(int device, void* stream, const uint16_
     b.out = a.out + static_cast<size_t>(r0) * q_ld;
     b.row_slot = row_slot + r0;
     b.row_pos = row_pos + r0;
-    const cudaError_t ce = launch_attention_pair(b, sms, static_cast<cudaStream_t>(stream), false);
+    ce = launch_attention_pair(b, sms, st, false);
     if (ce != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, cudaGetErrorString(ce));
   }
+  if (!check) return QASR_OK;
+  uint32_t dev_status[2] = {0, 0};
+  ce = cudaStreamSynchronize(st);
+  if (ce == cudaSuccess) ce = cudaMemcpy(dev_status, a.status, sizeof dev_status, cudaMemcpyDeviceToHost);
+  if (ce != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, cudaGetErrorString(ce));
+  if (dev_status[0] != 0) {
+    char m[96];
+    std::snprintf(m, sizeof m, "device-side %s (code %u, site 0x%x)",
+                  dev_status[0] == DEVERR_TIMEOUT ? "wait timed out" : "check failed", dev_status[0], dev_status[1]);
+    return probe_err(err, errlen, dev_status[0] == DEVERR_TIMEOUT ? QASR_ERR_DEVICE_TIMEOUT : QASR_ERR_DEVICE, m);
+  }
   return QASR_OK;
+}
+
+extern "C" {
+
+qasr_status qasr_kernel_attention(int device, void* stream, const uint16_t* q, int q_ld,
+                                  uint16_t* out, const uint16_t* kv_pool, const int* page_table,
+                                  int max_pages, int layers, int nkv, int layer,
+                                  const int* row_slot, const int* row_pos, int rows, char* err,
+                                  int errlen) {
+  return attention_probe(device, stream, q, q_ld, out, kv_pool, page_table, max_pages, layers, nkv, layer,
+                         row_slot, row_pos, rows, nullptr, false, err, errlen);
+}
+
+qasr_status qasr_kernel_attention_traced(int device, void* stream, const uint16_t* q, int q_ld,
+                                         uint16_t* out, const uint16_t* kv_pool, const int* page_table,
+                                         int max_pages, int layers, int nkv, int layer,
+                                         const int* row_slot, const int* row_pos, int rows,
+                                         unsigned long long* trace, char* err, int errlen) {
+  return attention_probe(device, stream, q, q_ld, out, kv_pool, page_table, max_pages, layers, nkv, layer,
+                         row_slot, row_pos, rows, trace, true, err, errlen);
 }
 
 }  // extern "C"
@@ -1456,10 +1526,13 @@ qasr_status qasr_kernel_attention_traced(int device, void* stream, const uint16_
 // Attention for callers that must not allocate device memory (see
 // qasr_kernel_attention_noalloc in include/qasr_b200_kernels.h).  Its scratch — the
 // chunk partials of the split-row merge — is this file-scope array, sized for
-// NOALLOC_MAX_ROWS rows x NOALLOC_MAX_KV kv heads; nothing in it needs clearing
-// between calls (every partial a merge reads is written by the same call).  Every GPU
-// that loads the library holds it until the process exits.  In host code
-// `g_attn_noalloc_scratch` only names the symbol; the device address comes from
+// NOALLOC_MAX_ROWS rows x NOALLOC_MAX_KV kv heads; the partials need no clearing between
+// calls (every partial a merge reads is written by the same call).  Beside it, a status
+// word (first device-side error code + site) that every call clears before its launch
+// and reads back after it, so a bounded wait that gave up inside the kernels turns into
+// QASR_ERR_DEVICE_TIMEOUT instead of a silent partial result.  Every GPU that loads the
+// library holds both until the process exits.  In host code the array names are
+// host-side stand-ins for the symbols; the device addresses come from
 // cudaGetSymbolAddress, once per device.
 namespace qasr {
 constexpr int NOALLOC_MAX_ROWS = 64;
@@ -1469,11 +1542,13 @@ constexpr size_t NOALLOC_SCRATCH_BYTES = static_cast<size_t>(NOALLOC_MAX_ROWS) *
 }  // namespace qasr
 
 static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[qasr::NOALLOC_SCRATCH_BYTES];
+static __device__ __align__(8) uint32_t g_attn_noalloc_status[2];
 
 namespace {
 constexpr int kMaxDevices = 16;
 std::once_flag g_noalloc_once[kMaxDevices];
 void* g_noalloc_addr[kMaxDevices] = {};
+void* g_noalloc_status_addr[kMaxDevices] = {};
 cudaError_t g_noalloc_setup[kMaxDevices] = {};
 }  // namespace
 
@@ -1494,9 +1569,12 @@ extern "C" qasr_status qasr_kernel_attention_noalloc(int device, void* stream, c
   if (cudaSetDevice(device) != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, "cudaSetDevice");
   // set-up, once per device, with that device current: the array's device address
   std::call_once(g_noalloc_once[device], [device] {
-    g_noalloc_setup[device] = cudaGetSymbolAddress(&g_noalloc_addr[device], g_attn_noalloc_scratch);
+    cudaError_t e = cudaGetSymbolAddress(&g_noalloc_addr[device], g_attn_noalloc_scratch);
+    if (e == cudaSuccess) e = cudaGetSymbolAddress(&g_noalloc_status_addr[device], g_attn_noalloc_status);
+    g_noalloc_setup[device] = e;
   });
-  if (g_noalloc_setup[device] != cudaSuccess || g_noalloc_addr[device] == nullptr)
+  if (g_noalloc_setup[device] != cudaSuccess || g_noalloc_addr[device] == nullptr ||
+      g_noalloc_status_addr[device] == nullptr)
     return probe_err(err, errlen, QASR_ERR_DEVICE,
                      std::string("cudaGetSymbolAddress of the static attention scratch failed: ") +
                          cudaGetErrorString(g_noalloc_setup[device]));
@@ -1521,8 +1599,27 @@ extern "C" qasr_status qasr_kernel_attention_noalloc(int device, void* stream, c
   a.rows = rows;
   a.scale = 1.0f / std::sqrt(128.0f);
   a.ws = partials;
-  const cudaError_t ce = launch_attention_pair(a, sms, st, false);
+  uint32_t* status = static_cast<uint32_t*>(g_noalloc_status_addr[device]);
+  a.status = status;
+  cudaError_t ce = cudaMemsetAsync(status, 0, 2 * sizeof(uint32_t), st);
+  if (ce == cudaSuccess) ce = launch_attention_pair(a, sms, st, false);
   if (ce != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, cudaGetErrorString(ce));
+  // the call completes before it returns, so its result code covers what happened on the
+  // device: a bounded wait that gave up is reported, never an OK with partial output
+  uint32_t dev_status[2] = {0, 0};
+  ce = cudaStreamSynchronize(st);
+  if (ce == cudaSuccess) ce = cudaMemcpy(dev_status, status, sizeof dev_status, cudaMemcpyDeviceToHost);
+  if (ce != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, cudaGetErrorString(ce));
+  if (dev_status[0] == DEVERR_TIMEOUT) {
+    char m[96];
+    std::snprintf(m, sizeof m, "a device-side wait timed out (site 0x%x)", dev_status[1]);
+    return probe_err(err, errlen, QASR_ERR_DEVICE_TIMEOUT, m);
+  }
+  if (dev_status[0] != 0) {
+    char m[96];
+    std::snprintf(m, sizeof m, "device-side check failed (code %u, site 0x%x)", dev_status[0], dev_status[1]);
+    return probe_err(err, errlen, QASR_ERR_DEVICE, m);
+  }
   return QASR_OK;
 }
 

@@ -17,7 +17,13 @@ import ctypes
 
 import numpy as np
 
-from . import lib
+try:
+    from . import lib
+except ImportError:
+    # loaded by file path, outside the package (oracle/inputs.py): that loader binds `lib`
+    # to the CPU oracle's copy of the generator (the same synth.cpp), so the CPU arms of
+    # the benchmark make identical inputs without loading the B200 library
+    lib = None
 
 MODEL_PRESETS = {
     # TextDecoderConfig defaults (src/config.rs:102-110) = Qwen3-ASR-0.6B

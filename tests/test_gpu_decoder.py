@@ -3,11 +3,12 @@
 Same seeded weights and prefixes into both.  Checked per case:
 * teacher-forced logits: both sides are fed the oracle's token history; max |Δlogit|
   <= 2e-2 (f16 weights) / 5e-2 (INT8 weights), the tolerances the north star states;
-* greedy ids: every step's argmax must equal the oracle's, except at a near-tie — where
-  the oracle's own logits of the two tokens differ by no more than the measured logit
-  error (the GPU sums in a different order than the CPU, so a tie inside that error
-  can resolve either way; the reference saw the same with its own re-associations,
-  src/decoder.rs:748-767).  The agreement rate and every near-tie are reported.
+* greedy ids: every step's argmax must equal the oracle's.  Only the cases marked as
+  near-tie studies (`allow_near_ties=True`: two-layer random models, whose logits are
+  nearly flat) accept a flip, and only where the oracle's own logits of the two tokens
+  differ by no more than twice the measured logit error (the GPU sums in a different
+  order than the CPU, so a tie inside that error can resolve either way; the reference
+  saw the same with its own re-associations, src/decoder.rs:748-767).
 """
 import numpy as np
 import pytest
@@ -37,12 +38,13 @@ def _setup(qasr, oracle, cfg, int8, slots, max_seq=2048, seed=1234):
     return model, dec, om
 
 
-def _run_parity(qasr, oracle, cfg, int8, n_audio, steps, n_slots=1, check_slots=None):
+def _run_parity(qasr, oracle, cfg, int8, n_audio, steps, n_slots=1, check_slots=None, n_text=24,
+                max_seq=2048):
     from oracle.oracle import OracleSeq
     tol = INT8_TOL if int8 else F16_TOL
-    model, dec, om = _setup(qasr, oracle, cfg, int8, n_slots)
+    model, dec, om = _setup(qasr, oracle, cfg, int8, n_slots, max_seq=max_seq)
     check_slots = list(range(n_slots)) if check_slots is None else check_slots
-    prefixes = [model.prefix(s, n_audio[s % len(n_audio)])[0] for s in range(n_slots)]
+    prefixes = [model.prefix(s, n_audio[s % len(n_audio)], n_text=n_text)[0] for s in range(n_slots)]
     slots = [dec.fork_capped(p.shape[0] + steps + 8) for p in prefixes]
     first = dec.prefill_batch(slots, prefixes)
     g_logits0 = dec.read_logits(n_slots)
@@ -55,7 +57,7 @@ def _run_parity(qasr, oracle, cfg, int8, n_audio, steps, n_slots=1, check_slots=
         report.append((step, i, int(g), int(o), float(lg[o] - lg[g])))
 
     for i in check_slots:
-        seqs[i] = OracleSeq(om, 2048)
+        seqs[i] = OracleSeq(om, max_seq)
         tok, lg = seqs[i].prefill(prefixes[i], want_logits=True)
         o_tok[i] = [tok]
         worst = max(worst, float(np.max(np.abs(g_logits0[i] - lg))))
@@ -79,14 +81,18 @@ def _run_parity(qasr, oracle, cfg, int8, n_audio, steps, n_slots=1, check_slots=
     return worst, report, tol
 
 
-def _check(worst, report, tol):
+def _check(worst, report, tol, allow_near_ties=False):
+    """report rows: (step, slot, gpu id, oracle id, oracle logit gap between them)."""
     flips = [r for r in report if r[2] != r[3]]
     agree = 1.0 - len(flips) / len(report)
     print(f"teacher-forced max |dlogit| {worst:.3g}; greedy agreement {agree:.3%} "
-          f"({len(report) - len(flips)}/{len(report)}); near-ties {flips}")
+          f"({len(report) - len(flips)}/{len(report)}); flips (step, slot, gpu, oracle, gap) {flips}")
     assert worst <= tol, f"teacher-forced max |dlogit| {worst:.4g} > {tol}"
-    # a flipped id is only acceptable where the oracle itself cannot separate the two
-    # tokens by more than twice the observed logit error
+    if not allow_near_ties:
+        assert not flips, f"greedy ids differ from the oracle's: {flips}"
+        return
+    # near-tie study: a flipped id is only acceptable where the oracle itself cannot
+    # separate the two tokens by more than twice the observed logit error
     bad = [r for r in flips if r[4] > 2.0 * worst]
     assert not bad, f"greedy ids differ beyond a near-tie: {bad}"
     assert len(flips) <= max(1, len(report) // 10), f"too many near-tie flips: {flips}"
@@ -94,8 +100,11 @@ def _check(worst, report, tol):
 
 @pytest.mark.parametrize("int8", [False, True, "f32"], ids=["f16", "int8", "int8-f32scale"])
 def test_two_layer_decoder_matches_oracle(qasr, cuda_device, oracle, int8):
+    """A near-tie study: two random layers leave the logits nearly flat (an INT8 case
+    has shown one flip with an oracle gap of 0.0022)."""
     cfg = qasr.text_config("0.6b", num_hidden_layers=2)
-    _check(*_run_parity(qasr, oracle, cfg, int8, n_audio=[40, 7, 120], steps=12, n_slots=3))
+    _check(*_run_parity(qasr, oracle, cfg, int8, n_audio=[40, 7, 120], steps=12, n_slots=3),
+           allow_near_ties=True)
 
 
 @pytest.mark.parametrize("int8", [False, True], ids=["f16", "int8"])
@@ -257,14 +266,15 @@ def test_errors_are_status_codes(qasr, cuda_device):
 
 @pytest.mark.slow
 def test_config1_shape_matches_oracle(qasr, cuda_device, oracle):
-    """Config 1 shape: 0.6B f16, 28 layers, prefix 9 + 200 audio + 15 ids, greedy decode."""
+    """Config 1 shape: 0.6B f16, 28 layers, prefix 9 + 200 audio + 15 ids, 64 decode steps."""
     cfg = qasr.text_config("0.6b")
-    _check(*_run_parity(qasr, oracle, cfg, False, n_audio=[200], steps=32))
+    _check(*_run_parity(qasr, oracle, cfg, False, n_audio=[200], steps=64))
 
 
 @pytest.mark.slow
 def test_config2_shape_matches_oracle(qasr, cuda_device, oracle):
-    """Config 2 shape: 0.6B INT8, 16 slots; two slots checked against the oracle."""
+    """Config 2 shape: 0.6B INT8 (the decode-chain path), 16 slots of 9 + 390 audio + 23
+    ids, 256 decode steps; two slots checked against the oracle."""
     cfg = qasr.text_config("0.6b")
-    _check(*_run_parity(qasr, oracle, cfg, True, n_audio=[390, 250], steps=12, n_slots=16,
-                        check_slots=[0, 9]))
+    _check(*_run_parity(qasr, oracle, cfg, True, n_audio=[390], steps=256, n_slots=16, check_slots=[0, 9],
+                        n_text=32))

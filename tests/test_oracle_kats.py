@@ -165,3 +165,28 @@ def test_config_defaults(qasr):
             c["num_attention_heads"], c["num_key_value_heads"], c["head_dim"]) == \
         (151936, 1024, 3072, 28, 16, 8, 128)
     assert abs(c["rms_norm_eps"] - 1e-6) < 1e-12
+
+
+def test_oracle_side_inputs_equal_the_package_inputs(qasr):
+    """bench.py's CPU arms make their inputs with liboracle's copy of the generator
+    (oracle/inputs.py), so that they load no B200 library; the bytes must equal the ones
+    the B200 runs get from the package."""
+    from oracle import inputs
+    cfg = qasr.text_config("0.6b", num_hidden_layers=1, vocab_size=4096)
+    a, b = qasr.SyntheticModel(cfg, seed=99), inputs.SyntheticModel(cfg, seed=99)
+    np.testing.assert_array_equal(a.embed, b.embed)
+    np.testing.assert_array_equal(a.final_norm, b.final_norm)
+    for int8 in (False, True):
+        la, lb = a.layer(0, int8=int8), b.layer(0, int8=int8)
+        assert la.keys() == lb.keys()
+        for k in la:
+            np.testing.assert_array_equal(la[k], lb[k])
+    for stream in (0, 70001):
+        pa, ia = a.prefix(stream, 37)
+        pb, ib = b.prefix(stream, 37)
+        np.testing.assert_array_equal(pa, pb)
+        np.testing.assert_array_equal(ia, ib)
+    ca, sa = qasr.build_rope_tables(2048)
+    cb, sb = inputs.build_rope_tables(2048)
+    np.testing.assert_array_equal(ca, cb)
+    np.testing.assert_array_equal(sa, sb)

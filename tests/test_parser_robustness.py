@@ -80,3 +80,29 @@ def test_checkpoint_open_survives_bad_headers(qasr, tmp_path):
         except qasr.DecoderError as e:
             assert e.status in (1, 2)
     assert opened >= 1
+
+
+def _raw_safetensors(header: dict, data: bytes) -> bytes:
+    h = json.dumps(header).encode()
+    return struct.pack("<Q", len(h)) + h + data
+
+
+def test_checkpoint_rejects_shapes_whose_product_wraps(qasr, tmp_path):
+    """A shape product that overflows 64 bits (or the byte size) must be rejected when the
+    file is opened: wrapped to a small element count, it would pass the size check and
+    let a row read run past the mapped file."""
+    cases = {
+        "wraps_to_zero": {"dtype": "F16", "shape": [1 << 33, 1 << 31], "data_offsets": [0, 0]},
+        "wraps_bytes": {"dtype": "F32", "shape": [1 << 62, 4], "data_offsets": [0, 0]},
+        "huge_rows": {"dtype": "I8", "shape": [1 << 40, 1 << 30], "data_offsets": [0, 16]},
+    }
+    for k, (name, entry) in enumerate(cases.items()):
+        d = tmp_path / f"w{k}"
+        d.mkdir()
+        (d / "model.safetensors").write_bytes(_raw_safetensors({"thinker.model.norm.weight": entry}, bytes(16)))
+        try:
+            with qasr.Checkpoint(str(d)) as ck:
+                raise AssertionError(f"{name}: opened a checkpoint with {len(ck)} tensors")
+        except qasr.DecoderError as e:
+            assert e.status == 1, name
+            assert "overflow" in str(e) or "bytes" in str(e), (name, str(e))

@@ -1,10 +1,11 @@
 """The allocation-free attention entry point against the regular one.
 
-qasr_kernel_attention_noalloc serves callers that cannot call cudaMalloc (graph
-capture, fixed memory budgets, real-time audio callbacks): its scratch is a static
-device array.  This file is collected last on purpose, so a run that stops at the first
-failure has already run every other test; it must also pass alone in a fresh process,
-where its first call performs the one-time symbol lookup.
+qasr_kernel_attention_noalloc serves callers that cannot call cudaMalloc (hosts with a
+fixed memory budget, real-time audio callbacks that must not block on the allocator):
+its scratch and status word are static device arrays.  This file is collected last on
+purpose, so a run that stops at the first failure has already run every other test; it
+must also pass alone in a fresh process, where its first call performs the one-time
+symbol lookup.
 """
 import numpy as np
 import pytest
