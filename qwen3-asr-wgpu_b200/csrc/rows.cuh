@@ -68,13 +68,16 @@ __global__ void rmsnorm_rows_kernel(__half* __restrict__ out, const __half* __re
 
 // argmax_into_slot (src/shaders.rs:2907-2954) tail: decode the 64-bit max keys, reset
 // them, hand each token to its slot (next step's input, read on device) and advance
-// the slot's position past the row.
+// the slot's position past the row.  `epoch` (optional): the decode step's counter, one
+// increment per step (the decode chain derives its flags from it).
 __global__ void finalize_rows_kernel(unsigned long long* __restrict__ best, int rows,
                                      const int* __restrict__ row_slot,
                                      const int* __restrict__ row_pos, int* __restrict__ out_tok,
-                                     int* __restrict__ next_tok, int* __restrict__ pos) {
+                                     int* __restrict__ next_tok, int* __restrict__ pos,
+                                     unsigned int* __restrict__ epoch) {
   griddep_wait();
   griddep_launch_dependents();
+  if (epoch != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *epoch += 1u;
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= rows) return;
   const unsigned long long key = best[r];

@@ -123,7 +123,7 @@ static int chain_seg_cap(int kind) {
 // int8 GEMM of the chain: at least two units (32 KB of weights) per taking-part CTA, and
 // few enough taking-part CTAs that no tile is cut into more than `max_seg_cap` segments
 // (the bound of the operation that adds the partials).
-static ChainGemm chain_gemm_plan(const uint8_t* w, const void* scale, bool scale32, int n_out, int k, int xmap,
+static ChainGemm chain_gemm_plan(const uint8_t* w, const void* scale, bool scale32, int n_out, int k, int xsrc,
                                  int sms, int max_seg_cap) {
   ChainGemm g{};
   g.w = w;
@@ -140,7 +140,7 @@ static ChainGemm chain_gemm_plan(const uint8_t* w, const void* scale, bool scale
     g.max_seg = ms;
     if (ms <= max_seg_cap || g.grid == 1) break;
   }
-  g.xmap = xmap;
+  g.xsrc = xsrc;
   return g;
 }
 
@@ -233,10 +233,13 @@ struct qasr_ctx {
   // decode chain (int8 weights, <= CHAIN_MAX_ROWS rows): partial sums and barrier counters
   bool chain_ok = false;
   bool chain_pdl = false;  // per-layer chain launches start while the attention drains (PDL)
-  float* chain_ws[4] = {};  // partial sums of the chain's QKV, o_proj, gate|up, down GEMMs
+  uint64_t* chain_ws[4] = {};  // flagged partial sums of the chain's QKV, o_proj, gate|up, down GEMMs
+  size_t chain_ws_n[4] = {};
   int chain_ws_rows = 0;
-  unsigned int* chain_bar = nullptr;
-  float* chain_ss = nullptr;  // [CHAIN_MAX_ROWS][CHAIN_MAX_HS / 128]
+  uint64_t* chain_hf[CHAIN_CHANNELS] = {};  // flagged residual rows [CHAIN_MAX_ROWS][CHAIN_MAX_HS / 2]
+  uint64_t* chain_ss[CHAIN_CHANNELS] = {};  // flagged per-tile sums of squares [CHAIN_MAX_ROWS][CHAIN_MAX_HS / 128]
+  uint64_t* chain_act = nullptr;            // flagged SiLU output [CHAIN_MAX_ROWS][I / 2]
+  unsigned int* step_epoch = nullptr;       // step counter of the chain's flags (finalize increments)
   int* chain_row_page = nullptr;        // [CHAIN_MAX_ROWS]
   __half* chain_row_rope = nullptr;     // [CHAIN_MAX_ROWS][256]
   unsigned long long* chain_trace = nullptr;  // QASR_FLAG_TRACE: [L + 1][sms][slots]
@@ -245,6 +248,8 @@ struct qasr_ctx {
   int* pinned_tok = nullptr;  // synchronous staging
   int* pinned_in = nullptr;   // input-token staging, reusable once ev_in completed
   cudaEvent_t ev_in = nullptr;
+
+  std::vector<int> chain_flags_for;  // slot list the chain's flagged words were last cleared for
 
   cudaGraphExec_t graph = nullptr;
   std::vector<int> graph_slots;
@@ -442,7 +447,7 @@ qasr_status enqueue_layers(qasr_ctx* c, int rows, const int* rs, const int* rp, 
 // final norm + lm_head + argmax for `n` rows: xf[i] = norm(h[src_rows[i]]).
 qasr_status enqueue_head(qasr_ctx* c, int n, const int* src_rows, const int* slot_of,
                          const int* pos_of, int* out_tok, int logit_row0, uint64_t* nk,
-                         bool norm = true) {
+                         bool norm = true, unsigned int* epoch = nullptr) {
   const int hs = c->cfg.hidden_size;
   if (norm) {
     CK(launch_k(rmsnorm_rows_kernel, dim3(n), dim3(256), 0, c->stream, true, c->xf, (const __half*)c->h,
@@ -460,7 +465,7 @@ qasr_status enqueue_head(qasr_ctx* c, int n, const int* src_rows, const int* slo
   g.args.best = c->best;
   if ((s = run_gemm(c, g))) return s;
   CK(launch_k(finalize_rows_kernel, dim3((n + 127) / 128), dim3(128), 0, c->stream, true, c->best, n,
-              slot_of, pos_of, out_tok, c->next_tok_dev, c->pos_dev),
+              slot_of, pos_of, out_tok, c->next_tok_dev, c->pos_dev, epoch),
      "finalize launch");
   *nk += 2;
   return QASR_OK;
@@ -494,15 +499,7 @@ static bool chain_one_cta_per_sm(size_t smem) {
 
 // `pdl`: the previous launch is the attention merge, which this chain reads only after
 // griddepcontrol.wait, so it may start while the merge drains (see decode_chain_kernel).
-qasr_status launch_chain(qasr_ctx* c, const ChainArgs& a, const ChainShape& sh, int n, bool pdl = false) {
-  const int hs = c->cfg.hidden_size, qd = c->cfg.num_attention_heads * c->cfg.head_dim;
-  const int I = c->cfg.intermediate_size;
-  CUtensorMap tx, ta, tact;
-  const uint32_t box = static_cast<uint32_t>(sh.n_tile);
-  if (!make_tmap(&tx, c->x, false, hs, n, static_cast<uint64_t>(hs) * 2, 64, box, &c->err) ||
-      !make_tmap(&ta, c->attn, false, qd, n, static_cast<uint64_t>(qd) * 2, 64, box, &c->err) ||
-      !make_tmap(&tact, c->act, false, I, n, static_cast<uint64_t>(I) * 2, 64, box, &c->err))
-    return QASR_ERR_DEVICE;
+qasr_status launch_chain(qasr_ctx* c, const ChainArgs& a, const ChainShape& sh, bool pdl = false) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(c->num_sms);
   cfg.blockDim = dim3(CHAIN_THREADS);
@@ -511,8 +508,8 @@ qasr_status launch_chain(qasr_ctx* c, const ChainArgs& a, const ChainShape& sh, 
   // A cooperative launch is placed as a whole, so under PDL it could not start before
   // every SM is free.  The PDL launch is therefore a plain one: one CTA per SM (its shared
   // memory admits no second, checked at context creation), every CTA resident once the
-  // attention's CTAs have exited (they never wait on this grid), and the grid barriers'
-  // waits are bounded in any case.
+  // attention's CTAs have exited (they never wait on this grid), and every wait on
+  // another CTA's flagged words is bounded in any case.
   cudaLaunchAttribute attr[1];
   const bool use_pdl = pdl && c->chain_pdl;
   if (use_pdl) {
@@ -525,7 +522,7 @@ qasr_status launch_chain(qasr_ctx* c, const ChainArgs& a, const ChainShape& sh, 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   g_launches.fetch_add(1, std::memory_order_relaxed);
-  CK(cudaLaunchKernelEx(&cfg, decode_chain_kernel, tx, ta, tact, a), "decode chain launch");
+  CK(cudaLaunchKernelEx(&cfg, decode_chain_kernel, a), "decode chain launch");
   return QASR_OK;
 }
 
@@ -536,10 +533,7 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
   const ChainShape sh = chain_shape(n);
   const int L = c->cfg.num_hidden_layers, hs = c->cfg.hidden_size, I = c->cfg.intermediate_size;
   const int nq = c->cfg.num_attention_heads, nkv = c->cfg.num_key_value_heads;
-  const int qd = nq * c->cfg.head_dim, qkv_out = qd + 2 * nkv * 128;
   const int sms = c->num_sms;
-  CK(cudaMemsetAsync(c->chain_bar, 0, static_cast<size_t>(L + 1) * sizeof(unsigned int), c->stream),
-     "chain barrier reset");
   ChainArgs base{};
   base.rows = n;
   base.n_tile = sh.n_tile;
@@ -553,7 +547,7 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
   base.eps = c->cfg.rms_norm_eps;
   base.h = c->h;
   base.q = c->q;
-  base.act = c->act;
+  base.attn = c->attn;
   base.embed = c->embed;
   base.vocab = c->cfg.vocab_size;
   base.row_slot = c->drow_slot;
@@ -570,12 +564,22 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
   base.kv.layers = L;
   base.kv.nkv = nkv;
   base.ws_rows = c->chain_ws_rows;
-  base.ss = c->chain_ss;
+  for (int ch = 0; ch < CHAIN_CHANNELS; ++ch) {
+    base.hf[ch] = c->chain_hf[ch];
+    base.ss[ch] = c->chain_ss[ch];
+  }
+  base.actf = c->chain_act;
+  base.epoch = c->step_epoch;
   base.status = c->status;
-  auto gemm = [&](const Linear& lin, int xmap, int kind) {
-    ChainGemm g = chain_gemm_plan(static_cast<const uint8_t*>(lin.w), lin.scale, lin.scale32, lin.n_out, lin.k, xmap, sms,
-                                  chain_seg_cap(kind));
+  auto gemm = [&](const Linear& lin, int xsrc, int kind) {
+    ChainGemm g = chain_gemm_plan(static_cast<const uint8_t*>(lin.w), lin.scale, lin.scale32, lin.n_out, lin.k, xsrc,
+                                  sms, chain_seg_cap(kind));
     g.ws = c->chain_ws[kind];
+    return g;
+  };
+  auto normed = [&](ChainGemm g, int ch, const float* w) {
+    g.xch = ch;
+    g.xnorm_w = w;
     return g;
   };
   auto op = [](int kind, int g) {
@@ -584,24 +588,24 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
     o.gemm = g;
     return o;
   };
-  // chain 0: embed + input norm of layer 0, QKV GEMM, q/k norm + RoPE + K/V append
+  // chain 0: embed (channel 1), layer 0's QKV GEMM over its input norm, q/k norm + RoPE + K/V append
   {
     ChainArgs a = base;
-    a.barrier = c->chain_bar;
+    a.launch_idx = 0;
     a.trace = c->trace_on ? c->chain_trace : nullptr;
     const LayerDev& L0 = c->layers[0];
-    a.gemms[0] = gemm(L0.qkv, 0, 0);
-    a.next_first = gemm(L0.o, 1, 1);
-    a.ops[0] = op(CH_EMBED_NORM, 0);
-    a.ops[0].norm_w = L0.iln;
-    a.ops[0].norm_out = c->x;
+    a.gemms[0] = normed(gemm(L0.qkv, XS_NORM, 0), 1, L0.iln);
+    a.next_first = gemm(L0.o, XS_ATTN, 1);
+    a.ops[0] = op(CH_EMBED, 0);
+    a.ops[0].ch = 1;
     a.ops[1] = op(CH_GEMM, 0);
     a.ops[2] = op(CH_QKV, 0);
     a.ops[2].qn_w = L0.qn;
     a.ops[2].kn_w = L0.kn;
     a.ops[2].layer = 0;
+    a.ops[2].direct_meta = 1;
     a.n_ops = 3;
-    qasr_status s = launch_chain(c, a, sh, n);
+    qasr_status s = launch_chain(c, a, sh);
     if (s) return s;
   }
   for (int l = 0; l < L; ++l) {
@@ -612,43 +616,40 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
     if (s) return s;
     const LayerDev& Ld = c->layers[l];
     ChainArgs a = base;
-    a.barrier = c->chain_bar + l + 1;
+    a.launch_idx = l + 1;
     if (c->chain_trace && c->trace_on) a.trace = c->chain_trace + static_cast<size_t>(l + 1) * sms * CHAIN_TRACE_SLOTS;
-    a.gemms[0] = gemm(Ld.o, 1, 1);
-    if (l + 1 < L) a.next_first = gemm(c->layers[l + 1].o, 1, 1);
-    a.gemms[1] = gemm(Ld.gu, 0, 2);
-    a.gemms[2] = gemm(Ld.down, 2, 3);
+    a.gemms[0] = gemm(Ld.o, XS_ATTN, 1);
+    if (l + 1 < L) a.next_first = gemm(c->layers[l + 1].o, XS_ATTN, 1);
+    a.gemms[1] = normed(gemm(Ld.gu, XS_NORM, 2), 0, Ld.pln);
+    a.gemms[2] = gemm(Ld.down, XS_ACT, 3);
     int k = 0;
     a.ops[k++] = op(CH_GEMM, 0);
-    a.ops[k++] = op(CH_RESID, 0);
-    a.ops[k] = op(CH_NORM, 0);
-    a.ops[k].norm_w = Ld.pln;
-    a.ops[k++].norm_out = c->x;
+    a.ops[k] = op(CH_RESID, 0);
+    a.ops[k++].ch = 0;
     a.ops[k++] = op(CH_GEMM, 1);
     a.ops[k++] = op(CH_SILU, 1);
     a.ops[k++] = op(CH_GEMM, 2);
-    a.ops[k++] = op(CH_RESID, 2);
-    a.ops[k] = op(CH_NORM, 2);
+    a.ops[k] = op(CH_RESID, 2);
+    a.ops[k++].ch = 1;
     if (l + 1 < L) {
       const LayerDev& Ln = c->layers[l + 1];
-      a.ops[k].norm_w = Ln.iln;
-      a.ops[k++].norm_out = c->x;
-      a.gemms[3] = gemm(Ln.qkv, 0, 0);
+      a.gemms[3] = normed(gemm(Ln.qkv, XS_NORM, 0), 1, Ln.iln);
       a.ops[k++] = op(CH_GEMM, 3);
       a.ops[k] = op(CH_QKV, 3);
       a.ops[k].qn_w = Ln.qn;
       a.ops[k].kn_w = Ln.kn;
       a.ops[k++].layer = l + 1;
-    } else {
+    } else {  // the final norm: the lm_head's input rows
+      a.ops[k] = op(CH_NORM, 2);
+      a.ops[k].ch = 1;
       a.ops[k].norm_w = c->final_norm;
       a.ops[k++].norm_out = c->xf;
     }
     a.n_ops = k;
-    if ((s = launch_chain(c, a, sh, n, true))) return s;
+    if ((s = launch_chain(c, a, sh, true))) return s;
   }
-  (void)qkv_out;
   *nk += 1 + 3 * static_cast<uint64_t>(L);  // chain 0, then per layer attention + merge + chain
-  return enqueue_head(c, n, nullptr, c->drow_slot, c->drow_pos, c->out_tok, 0, nk, false);
+  return enqueue_head(c, n, nullptr, c->drow_slot, c->drow_pos, c->out_tok, 0, nk, false, c->step_epoch);
 }
 
 qasr_status ready(qasr_ctx* c) {
@@ -886,12 +887,15 @@ qasr_status qasr_create(const qasr_text_config* cfg, const qasr_options* opts, i
                                           chain_seg_cap(i));
       if (2ull * static_cast<unsigned long long>(g.units) * static_cast<unsigned long long>(g.grid) >= (1ull << 32))
         return fail(c, QASR_ERR_CAPACITY, "decode chain GEMM: too many units for 32-bit unit maps");
-      if ((s = dalloc(c, &c->chain_ws[i],
-                      static_cast<size_t>(shapes[i][0] / 128) * g.max_seg * c->chain_ws_rows * 128, "chain workspace")))
-        return s;
+      c->chain_ws_n[i] = static_cast<size_t>(shapes[i][0] / 128) * g.max_seg * c->chain_ws_rows * 128;
+      if ((s = dalloc(c, &c->chain_ws[i], c->chain_ws_n[i], "chain workspace"))) return s;
     }
-    if ((s = dalloc(c, &c->chain_bar, static_cast<size_t>(L + 1), "chain barriers")) ||
-        (s = dalloc(c, &c->chain_ss, static_cast<size_t>(CHAIN_MAX_ROWS) * CHAIN_MAX_HS / 128, "chain norms")) ||
+    for (int ch = 0; ch < CHAIN_CHANNELS; ++ch)
+      if ((s = dalloc(c, &c->chain_hf[ch], static_cast<size_t>(CHAIN_MAX_ROWS) * CHAIN_MAX_HS / 2, "chain rows")) ||
+          (s = dalloc(c, &c->chain_ss[ch], static_cast<size_t>(CHAIN_MAX_ROWS) * CHAIN_MAX_HS / 128, "chain norms")))
+        return s;
+    if ((s = dalloc(c, &c->chain_act, static_cast<size_t>(CHAIN_MAX_ROWS) * I / 2, "chain act")) ||
+        (s = dalloc(c, &c->step_epoch, 1, "step counter")) ||
         (s = dalloc(c, &c->chain_row_page, static_cast<size_t>(CHAIN_MAX_ROWS), "chain row pages")) ||
         (s = dalloc(c, &c->chain_row_rope, static_cast<size_t>(CHAIN_MAX_ROWS) * 256, "chain row rope")))
       return s;
@@ -1145,6 +1149,22 @@ qasr_status qasr_step_batch(qasr_ctx* c, const int* slots, int n, int32_t* out_t
       return fail(c, QASR_ERR_CAPACITY, "slot %d position %d beyond the rope tables", sl, S.pos);
   }
   const bool use_graph = !(c->opts.flags & QASR_FLAG_NO_GRAPH);
+  if (c->chain_ok && n <= CHAIN_MAX_ROWS && c->chain_flags_for != list) {
+    // A new row set splits the GEMMs differently, so a word the new launches read may
+    // have last been written long ago: start every flag from zero (never a live flag).
+    for (int i = 0; i < 4; ++i)
+      CK(cudaMemsetAsync(c->chain_ws[i], 0, c->chain_ws_n[i] * sizeof(uint64_t), c->stream), "flag reset");
+    for (int ch = 0; ch < CHAIN_CHANNELS; ++ch) {
+      CK(cudaMemsetAsync(c->chain_hf[ch], 0, static_cast<size_t>(CHAIN_MAX_ROWS) * CHAIN_MAX_HS / 2 * 8, c->stream),
+         "flag reset");
+      CK(cudaMemsetAsync(c->chain_ss[ch], 0, static_cast<size_t>(CHAIN_MAX_ROWS) * CHAIN_MAX_HS / 128 * 8, c->stream),
+         "flag reset");
+    }
+    CK(cudaMemsetAsync(c->chain_act, 0, static_cast<size_t>(CHAIN_MAX_ROWS) * c->cfg.intermediate_size / 2 * 8,
+                       c->stream),
+       "flag reset");
+    c->chain_flags_for = list;
+  }
   if (!use_graph || !c->graph || c->graph_slots != list) {
     drop_graph(c);
     CK(cudaMemcpyAsync(c->drow_slot, list.data(), n * sizeof(int), cudaMemcpyHostToDevice, c->stream),

@@ -52,16 +52,20 @@ def _run_parity(qasr, oracle, cfg, int8, n_audio, steps, n_slots=1, check_slots=
     o_tok = {}
     worst = 0.0
     report = []  # (step, slot, gpu token, oracle token, oracle logit gap between them)
+    per_step = []  # max |dlogit| of each step over the checked slots (step 0 = prefill)
 
     def note(step, i, g, o, lg):
         report.append((step, i, int(g), int(o), float(lg[o] - lg[g])))
 
+    step_worst = 0.0
     for i in check_slots:
         seqs[i] = OracleSeq(om, max_seq)
         tok, lg = seqs[i].prefill(prefixes[i], want_logits=True)
         o_tok[i] = [tok]
-        worst = max(worst, float(np.max(np.abs(g_logits0[i] - lg))))
+        step_worst = max(step_worst, float(np.max(np.abs(g_logits0[i] - lg))))
         note(0, i, first[i], tok, lg)
+    per_step.append(step_worst)
+    worst = step_worst
     g_tok = {i: [int(first[i])] for i in range(n_slots)}
     for _ in range(steps):
         # teacher forcing: both sides embed the oracle's previous token
@@ -71,13 +75,17 @@ def _run_parity(qasr, oracle, cfg, int8, n_audio, steps, n_slots=1, check_slots=
         lg_all = dec.read_logits(n_slots)
         for i in range(n_slots):
             g_tok[i].append(int(out[i]))
+        step_worst = 0.0
         for i in check_slots:
             tok, lg = seqs[i].step(want_logits=True)
             o_tok[i].append(tok)
-            worst = max(worst, float(np.max(np.abs(lg_all[i] - lg))))
+            step_worst = max(step_worst, float(np.max(np.abs(lg_all[i] - lg))))
             note(len(o_tok[i]) - 1, i, out[i], tok, lg)
+        per_step.append(step_worst)
+        worst = max(worst, step_worst)
     dec.close()
     om.close()
+    print("max |dlogit| per step (0 = prefill): " + " ".join(f"{w:.3g}" for w in per_step))
     return worst, report, tol
 
 

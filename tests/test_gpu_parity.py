@@ -101,7 +101,6 @@ def test_kv_growth_keeps_contents_and_freed_pages_are_reused(qasr, cuda_device, 
 
     a = dec.fork_capped(64)
     b = dec.fork_capped(64)
-    assert dec.ensure_capacity(a, 10) >= 64
     pa, pb = model.prefix(0, 20)[0], model.prefix(1, 9)[0]  # 44 and 33 rows
     sa, sb = OracleSeq(om, 512), OracleSeq(om, 512)
     g = dec.prefill_batch([a, b], [pa, pb])
@@ -159,7 +158,7 @@ def _tie_model(qasr, cfg, seed, nan_row=None):
     path.  nan_row: that row of the table holds a NaN (its logit is NaN)."""
     model = qasr.SyntheticModel(cfg, seed=seed)
     emb = model.embed.copy()
-    v = qasr.normal_f16(cfg["hidden_size"], seed, 7777, 0.0, 0.5)
+    v = qasr.synth.normal_f16(cfg["hidden_size"], seed, 7777, 0.0, 0.5)
     neg = (v.view(np.float16) * np.float16(-1)).view(np.uint16)
     emb[0:64] = v
     emb[64:128] = neg
