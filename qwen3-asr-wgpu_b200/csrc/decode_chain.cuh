@@ -60,6 +60,14 @@ constexpr int CHAIN_MAX_SEG = 12;
 constexpr int CHAIN_SILU_SEG = 4;
 constexpr int CHAIN_QKV_SEG = 8;
 constexpr int CHAIN_CHANNELS = 2;  // flagged residual rows + sums of squares: two per launch
+constexpr int CHAIN_X_BATCH = 3;   // X tiles whose loads are in flight together
+// the launch programs (the op lists the host fills ChainArgs::ops with)
+enum ChainProgram : int {
+  CHAIN_PROG_FIRST = 0,   // embed, QKV GEMM (X: input norm of layer 0), QKV op
+  CHAIN_PROG_MIDDLE = 1,  // o_proj, resid, gate|up (X: post-attention norm), SiLU, down, resid,
+                          // next layer's QKV GEMM (X: its input norm), QKV op
+  CHAIN_PROG_LAST = 2,    // as MIDDLE up to the second resid, then the final norm
+};
 
 enum ChainOpKind : int {
   CH_GEMM = 0,   // partial sums of W x over this CTA's (tile, k-block) range
@@ -110,6 +118,8 @@ struct ChainArgs {
   int n_ops;
   int rows, n_tile;
   int w_stages, a_stages;  // weight stages; unit slots (A stage in TMEM + X tile in smem)
+  int w_inflight;          // most weight copies in flight at once: an SM's loads queue behind
+                           // its bulk copies, so a deep burst would delay every X and flag read
   int n_acc;  // MMA issuer warps = accumulators per segment buffer (1 to 3)
   ChainGemm next_first;  // the next chain launch's first GEMM (w == nullptr: none): its
                          // units of this CTA are prefetched into L2 once this launch's
@@ -318,6 +328,28 @@ __device__ __forceinline__ bool chain_sum4(const uint64_t* p, size_t stride, int
   return ok;
 }
 
+// Register split among the warpgroups (setmaxnreg; the launch gives every thread 128):
+// the weight producer + MMA issuers (warps 0-3) and the int8 A builders (warps 4-7) need
+// few, the epilogue / row-operation warps (8-15) hold up to CHAIN_MAX_SEG 16-byte words in
+// flight per thread.  A spilled register would live in L2 here (the shared-memory carve-out
+// leaves the L1 almost nothing) behind the SM's weight copies, so none may spill.  Each
+// role sets its share on entry and returns to 128 before the roles rejoin; the builders'
+// and the producer's return waits for the epilogue's, which waits on nothing they do after
+// their main loops.
+constexpr int CHAIN_REGS_PRODUCER = 56, CHAIN_REGS_BUILDER = 96, CHAIN_REGS_EPI = 176;
+static_assert(128 * CHAIN_REGS_PRODUCER + 128 * CHAIN_REGS_BUILDER + CHAIN_EPI_THREADS * CHAIN_REGS_EPI <=
+                  CHAIN_THREADS * 128,
+              "the warpgroups' registers must fit in what the launch allocates (512 threads x 128)");
+static_assert(CHAIN_EPI_WARPS == 8 && CHAIN_THREADS == 512, "warpgroups 0 / 1 / 2-3 = producer+MMA / builders / epilogue");
+template <uint32_t N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 __device__ __forceinline__ void fence_proxy_async_shared() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -331,10 +363,8 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
 }
 
 // CH_RESID over this warp's (row, tile) items: h = f16(h + the GEMM's partials), the flagged
-// copy and the tile's sum of squares of the new f16 values into channel op.ch.  Its own
-// function: the partial reads hold up to CHAIN_MAX_SEG 16-byte words in flight and would
-// not fit beside the epilogue's loop state in one register allocation.
-__device__ __noinline__ void chain_resid(const ChainArgs& a, const ChainOp& op, int warp_id, int warps,
+// copy and the tile's sum of squares of the new f16 values into channel op.ch.
+__device__ __forceinline__ void chain_resid(const ChainArgs& a, const ChainOp& op, int warp_id, int warps,
                                          LLWait llw) {
   const int lane = threadIdx.x & 31;
   const size_t slot_u64 = static_cast<size_t>(a.ws_rows) * 128;
@@ -372,9 +402,8 @@ __device__ __noinline__ void chain_resid(const ChainArgs& a, const ChainOp& op, 
   }
 }
 
-// CH_QKV over this warp's (row, head) items (see the operation list above); its own
-// function for the same reason as chain_resid.
-__device__ __noinline__ void chain_qkv(const ChainArgs& a, const ChainOp& op, int warp_id, int warps, LLWait llw) {
+// CH_QKV over this warp's (row, head) items (see the operation list above).
+__device__ __forceinline__ void chain_qkv(const ChainArgs& a, const ChainOp& op, int warp_id, int warps, LLWait llw) {
   const int lane = threadIdx.x & 31;
   const size_t slot_u64 = static_cast<size_t>(a.ws_rows) * 128;
   // one warp per (row, head), lane = dims 4 lane .. +3; the rotate-half partner of
@@ -453,6 +482,7 @@ __device__ __noinline__ void chain_qkv(const ChainArgs& a, const ChainOp& op, in
   }
 }
 
+template <int PROG>
 __global__ void __launch_bounds__(CHAIN_THREADS, 1) decode_chain_kernel(const __grid_constant__ ChainArgs a) {
   constexpr int KSTEPS = 8;  // 128 k elements per unit, UMMA K = 16
   constexpr int EPI_WARP0 = 16 - CHAIN_EPI_WARPS;
@@ -517,6 +547,8 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1) decode_chain_kernel(const __
   // wait (griddepcontrol.wait in their own branch) before they read any activation.
   if (threadIdx.x == 0 && a.trace != nullptr) a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 38] = globaltimer();
 
+  if (warp < 4) {
+  regs_dec<CHAIN_REGS_PRODUCER>();
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     // One thread streams the weight units of all the launch's GEMMs (16 KB bulk copies)
@@ -533,8 +565,13 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1) decode_chain_kernel(const __
       w_advance();
       if (a.trace != nullptr) a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 39] = globaltimer();
       uint64_t t_idle = globaltimer();
+      int wlanded = 0;  // copies seen complete, in issue order
+      const int cap = a.w_inflight > 0 ? a.w_inflight : SW;
       while (wu < wue) {
-        if (mbar_test(&wfree_bar[wst], wph ^ 1u)) {
+        while (wissued - wlanded >= cap &&
+               mbar_test(&wfull_bar[wlanded % SW], static_cast<uint32_t>((wlanded / SW) & 1)))
+          ++wlanded;
+        if (wissued - wlanded < cap && mbar_test(&wfree_bar[wst], wph ^ 1u)) {
           mbar_arrive_expect_tx(&wfull_bar[wst], 16384u);
           bulk_load(smem + static_cast<size_t>(wst) * 16384, a.gemms[wg].w + static_cast<size_t>(wu) * 16384, 16384u,
                     &wfull_bar[wst]);
@@ -650,7 +687,10 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1) decode_chain_kernel(const __
       umma_commit(&done_bar);
       mbar_wait(&done_bar, 0, nullptr, a.status, 0x724);
     }
-  } else if (warp >= 4 && warp < 8) {
+  }
+  regs_inc<128>();  // back to the launch's count before the roles rejoin
+  } else if (warp < 8) {
+    regs_dec<CHAIN_REGS_BUILDER>();
     // ------------------------------------------------------------ int8 A builders
     // Each unit is published as soon as its TMEM stores land (tcgen05.wait::st is cheap);
     // the row scale of the unit's tile is loaded before the unit's barrier waits so its
@@ -722,7 +762,9 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1) decode_chain_kernel(const __
           a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 72 + i] = globaltimer();
       }
     }
-  } else if (warp >= EPI_WARP0) {
+    regs_inc<128>();
+  } else {
+    regs_inc<CHAIN_REGS_EPI>();
     // ------------------------------------------------------------ epilogue, X builds, row operations
     const int e = threadIdx.x - EPI_WARP0 * 32;  // 0 .. CHAIN_EPI_THREADS - 1
     const int we = warp - EPI_WARP0;
@@ -731,7 +773,7 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1) decode_chain_kernel(const __
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const size_t slot_u64 = static_cast<size_t>(a.ws_rows) * 128;
     const int hf_ld = CHAIN_MAX_HS / 2, ss_ld = CHAIN_MAX_HS / 128;
-    int seg = -1, gi = 0;
+    int seg = -1;
     int xs = 0;  // unit-slot cursor of the X builds (the builders and issuers walk the same units)
     uint32_t xph = 0;
     bool ok = true;
@@ -776,236 +818,311 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1) decode_chain_kernel(const __
       }
     };
 
-    // X tile of unit u of GEMM g into the next unit slot: rows n < rows from the source,
-    // zeros in the tile's padding rows; the 128-byte swizzle of the K-major UMMA operand
-    // (16-byte chunk c of row n at chunk c ^ (n % 8), two 64-column halves).
-    auto build_x = [&](const ChainGemm& g, int u) {
-      const int my = xs;
-      const uint32_t myph = xph;
-      if (++xs == a.a_stages) {
-        xs = 0;
+    // X tiles of units u0 .. u0 + cnt - 1 (cnt <= CHAIN_X_BATCH) of GEMM g into the next
+    // unit slots: rows n < rows from the source, zeros in the tiles' padding rows; the
+    // 128-byte swizzle of the K-major UMMA operand (16-byte chunk c of row n at chunk
+    // c ^ (n % 8), two 64-column halves).  All the batch's loads are issued before any is
+    // used, so the batch costs one round trip, not one per unit.
+    auto build_x = [&](const ChainGemm& g, int u0, int cnt) {
+      const int items = a.n_tile * 16;
+      // per unit, this thread's items (n, c) = (it >> 4, it & 15), it = j0 + e + 256 j, two at a time
+      uint4 raw[CHAIN_X_BATCH][2][2];  // [unit][item][word]
+      const bool flagged = g.xsrc != XS_ATTN;
+      auto src_of = [&](int n, int k0) -> const uint64_t* {
+        return g.xsrc == XS_NORM ? a.hf[g.xch] + static_cast<size_t>(n) * hf_ld + k0 / 2
+                                 : a.actf + static_cast<size_t>(n) * (a.inter / 2) + k0 / 2;
+      };
+      for (int j0 = 0; j0 < items; j0 += 2 * CHAIN_EPI_THREADS) {
+#pragma unroll
+        for (int b = 0; b < CHAIN_X_BATCH; ++b) {
+          const int kb = (u0 + b) % g.kblocks;
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int it = j0 + e + j * CHAIN_EPI_THREADS;
+            const int n = it >> 4, c = it & 15;
+            const int k0 = kb * 128 + c * 8;
+            if (b < cnt && it < items && n < a.rows) {
+              if (flagged) {
+                const uint64_t* src = src_of(n, k0);
+                raw[b][j][0] = ll_ld16(src);
+                raw[b][j][1] = ll_ld16(src + 2);
+              } else {
+                raw[b][j][0] = __ldcg(reinterpret_cast<const uint4*>(a.attn + static_cast<size_t>(n) * a.nq * 128 + k0));
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int b = 0; b < CHAIN_X_BATCH; ++b) {
+          if (b >= cnt) continue;
+          const int my = (xs + b) % a.a_stages;
+          const uint32_t myph = xph ^ ((xs + b) >= a.a_stages ? 1u : 0u);
+          if (j0 == 0 && !mbar_wait_warp(&ufree_bar[my], myph ^ 1u, &abort_flag, a.status, 0x745)) continue;
+          const int kb = (u0 + b) % g.kblocks;
+          const uint32_t dst = smem_u32(xring + static_cast<size_t>(my) * x_stage_bytes);
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int it = j0 + e + j * CHAIN_EPI_THREADS;
+            if (it >= items) continue;
+            const int n = it >> 4, c = it & 15;
+            const int k0 = kb * 128 + c * 8;
+            uint4 out = make_uint4(0u, 0u, 0u, 0u);
+            if (n < a.rows) {
+              if (!flagged) {
+                out = raw[b][j][0];
+              } else {
+                const uint64_t* src = src_of(n, k0);
+                uint4 w0 = raw[b][j][0], w1 = raw[b][j][1];
+                if (!(w0.y == flag && w0.w == flag)) w0 = ll_spin16(src, llw, 0x746);
+                if (!(w1.y == flag && w1.w == flag)) w1 = ll_spin16(src + 2, llw, 0x746);
+                if (g.xsrc == XS_ACT) {
+                  out = make_uint4(w0.x, w0.z, w1.x, w1.z);
+                } else {
+                  const float inv = inv_sh[n];
+                  const float4 wa = *reinterpret_cast<const float4*>(g.xnorm_w + k0);
+                  const float4 wb = *reinterpret_cast<const float4*>(g.xnorm_w + k0 + 4);
+                  const uint32_t hw[4] = {w0.x, w0.z, w1.x, w1.z};
+                  const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+                  uint32_t o[4];
+#pragma unroll
+                  for (int q = 0; q < 4; ++q) {
+                    const float2 hv = __half22float2(*reinterpret_cast<const __half2*>(&hw[q]));
+                    o[q] = pack_half2(__fmul_rn(__fmul_rn(hv.x, inv), wv[2 * q]),
+                                      __fmul_rn(__fmul_rn(hv.y, inv), wv[2 * q + 1]));
+                  }
+                  out = make_uint4(o[0], o[1], o[2], o[3]);
+                }
+              }
+            }
+            st_shared_v4(dst + static_cast<uint32_t>(c >> 3) * x_tile_bytes + static_cast<uint32_t>(n) * 128u +
+                             (static_cast<uint32_t>((c & 7) ^ (n & 7)) << 4),
+                         out);
+          }
+        }
+      }
+#pragma unroll
+      for (int b = 0; b < CHAIN_X_BATCH; ++b) {
+        if (b >= cnt) continue;
+        const int my = (xs + b) % a.a_stages;
+        fence_proxy_async_shared();  // the MMA reads the tile through the async proxy
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ufull_bar[my]);
+      }
+      xs += cnt;
+      if (xs >= a.a_stages) {
+        xs -= a.a_stages;
         xph ^= 1u;
       }
-      if (!mbar_wait_warp(&ufree_bar[my], myph ^ 1u, &abort_flag, a.status, 0x745)) return;
-      const int kb = u % g.kblocks;
-      const uint32_t dst = smem_u32(xring + static_cast<size_t>(my) * x_stage_bytes);
-      const int items = a.n_tile * 16;
-      bool lok = true;
-      for (int it = e; it < items; it += CHAIN_EPI_THREADS) {
-        const int n = it >> 4, c = it & 15;
-        const int k0 = kb * 128 + c * 8;
-        uint4 out = make_uint4(0u, 0u, 0u, 0u);
-        if (n < a.rows && lok) {
-          if (g.xsrc == XS_ATTN) {
-            out = __ldcg(reinterpret_cast<const uint4*>(a.attn + static_cast<size_t>(n) * a.nq * 128 + k0));
-          } else {
-            const uint64_t* src = g.xsrc == XS_NORM ? a.hf[g.xch] + static_cast<size_t>(n) * hf_ld + k0 / 2
-                                                    : a.actf + static_cast<size_t>(n) * (a.inter / 2) + k0 / 2;
-            uint4 v[2];
-            lok = ll_get16<2>(src, 2, 2, v, llw, 0x746);
-            if (g.xsrc == XS_ACT) {
-              out = make_uint4(v[0].x, v[0].z, v[1].x, v[1].z);
-            } else {
-              const float inv = inv_sh[n];
-              const float4 w0 = *reinterpret_cast<const float4*>(g.xnorm_w + k0);
-              const float4 w1 = *reinterpret_cast<const float4*>(g.xnorm_w + k0 + 4);
-              const uint32_t hw[4] = {v[0].x, v[0].z, v[1].x, v[1].z};
-              const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-              uint32_t o[4];
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const float2 hv = __half22float2(*reinterpret_cast<const __half2*>(&hw[j]));
-                o[j] = pack_half2(__fmul_rn(__fmul_rn(hv.x, inv), wv[2 * j]),
-                                  __fmul_rn(__fmul_rn(hv.y, inv), wv[2 * j + 1]));
-              }
-              out = make_uint4(o[0], o[1], o[2], o[3]);
-            }
-          }
-        }
-        st_shared_v4(dst + static_cast<uint32_t>(c >> 3) * x_tile_bytes + static_cast<uint32_t>(n) * 128u +
-                         (static_cast<uint32_t>((c & 7) ^ (n & 7)) << 4),
-                     out);
-      }
-      fence_proxy_async_shared();  // the MMA reads the tile through the async proxy
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&ufull_bar[my]);
+    };
+    // all units [x0, x1) of GEMM g, in batches
+    auto build_xs = [&](const ChainGemm& g, int x0, int x1) {
+      for (int u = x0; u < x1; u += CHAIN_X_BATCH) build_x(g, u, min(CHAIN_X_BATCH, x1 - u));
     };
 
-    for (int oi = 0; oi < a.n_ops && ok; ++oi) {
-      const ChainOp& op = a.ops[oi];
-      if (op.kind == CH_GEMM) {
-        const ChainGemm& g = a.gemms[gi];
-        int ub, ue;
-        chain_unit_range(g, blockIdx.x, ub, ue);
-        auto seg_end_of = [&](int uu) { return min(ue, (uu / g.kblocks + 1) * g.kblocks); };
-        if (ub < ue && g.xsrc == XS_NORM) {
-          compute_inv(g.xch);
-          named_bar_sync(1, CHAIN_EPI_THREADS);  // inv_sh complete
-        }
-        // X tiles of the first segment, then per segment: the next segment's X tiles, then
-        // this segment's accumulators (so the issuers always have work queued)
-        int xu = ub;
-        if (ub < ue) {
-          for (const int s0e = seg_end_of(ub); xu < s0e; ++xu) build_x(g, xu);
-          if (e == 0 && a.trace != nullptr) a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 25 + gi] = globaltimer();
-        }
-        int u = ub;
-        while (u < ue) {
-          const int T = u / g.kblocks;
-          const int seg_end = seg_end_of(u);
-          if (xu < ue)
-            for (const int ne = seg_end_of(xu); xu < ne; ++xu) build_x(g, xu);
-          ++seg;
-          const int d = seg & 1;
-          if (e == 0)
-            seg_ok = mbar_wait(&dfull_bar[d], static_cast<uint32_t>((seg >> 1) & 1), &abort_flag, a.status, 0x741)
-                         ? 1
-                         : 0;
-          named_bar_sync(1, CHAIN_EPI_THREADS);
-          const int got = seg_ok;
-          named_bar_sync(1, CHAIN_EPI_THREADS);
-          if (!got) {
-            ok = false;
-            break;
-          }
-          mbar_try_wait(&dfull_bar[d], static_cast<uint32_t>((seg >> 1) & 1));
-          tc_fence_after();
-          const int segidx = static_cast<int>(blockIdx.x) - cta_of_unit(static_cast<long long>(T) * g.kblocks,
-                                                                         g.units, g.grid);
-          uint64_t* dst = g.ws + (static_cast<size_t>(T) * g.max_seg + segidx) * slot_u64 + row;
-          const uint32_t dt = tmem_base + lane_base + static_cast<uint32_t>(d) * DCOLS;
-          const int n_used = min(NACC, seg_end - u);  // issuers that had units in the segment
-          for (int c0 = 16 * half; c0 < a.n_tile; c0 += 32) {
-            float v[16];
-            for (int q = 0; q < n_used; ++q) {
-              uint32_t r[16];
-              tmem_ld_x16(dt + static_cast<uint32_t>(q) * DSTR + static_cast<uint32_t>(c0), r);
-              tmem_wait_ld();
-#pragma unroll
-              for (int j = 0; j < 16; ++j) v[j] = q == 0 ? __uint_as_float(r[j]) : v[j] + __uint_as_float(r[j]);
-            }
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-              if (c0 + j < a.rows) ll_st8(dst + static_cast<size_t>(c0 + j) * 128, __float_as_uint(v[j]), flag);
-          }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&dfree_bar[d]);
-          u = seg_end;
-        }
-        ++gi;
-        if (!ok) break;
-      } else if (op.kind == CH_EMBED) {
-        // h[r] = embed row of the slot's input token: one warp per (row, 128-column tile),
-        // lane = 4 columns; the plain copy for the later launches, the flagged copy and the
-        // tile's sum of squares for this launch's norm
-        const int tiles = a.hs / 128;
-        for (int it = blockIdx.x * CHAIN_EPI_WARPS + we; it < a.rows * tiles; it += gridDim.x * CHAIN_EPI_WARPS) {
-          const int r = it / tiles, T = it - r * tiles;
-          const int slot = a.row_slot[r];
-          int tok = a.next_tok[slot];
-          if (tok < 0 || tok >= a.vocab) {
-            if (T == 0 && lane == 0) report_error(a.status, DEVERR_BOUNDS, 0x751);
-            tok = 0;
-          }
-          const int pos = a.pos[slot];
-          if (T == 0) {
-            if (lane == 0) {
-              a.row_pos[r] = pos;
-              a.row_page[r] = a.kv.page_table[static_cast<size_t>(slot) * a.kv.max_pages + (pos >> 6)];
-            }
-            // cos | sin rows of the position, 16 bytes per lane
-            const __half* rs = (lane < 16 ? a.rope_cos : a.rope_sin) + static_cast<size_t>(pos) * 128 + (lane & 15) * 8;
-            __stcg(reinterpret_cast<uint4*>(a.row_rope + static_cast<size_t>(r) * 256 + lane * 8),
-                   *reinterpret_cast<const uint4*>(rs));
-          }
-          const int c = T * 128 + 4 * lane;
-          const uint2 hw = *reinterpret_cast<const uint2*>(a.embed + static_cast<size_t>(tok) * a.hs + c);
-          __stcg(reinterpret_cast<uint2*>(a.h + static_cast<size_t>(r) * a.hs + c), hw);
-          ll_st16(a.hf[op.ch] + static_cast<size_t>(r) * hf_ld + c / 2, hw.x, hw.y, flag);
-          const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&hw.x));
-          const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&hw.y));
-          float sq = __fmul_rn(f01.x, f01.x);
-          sq = __fadd_rn(sq, __fmul_rn(f01.y, f01.y));
-          sq = __fadd_rn(sq, __fmul_rn(f23.x, f23.x));
-          sq = __fadd_rn(sq, __fmul_rn(f23.y, f23.y));
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-          if (lane == 0) ll_st8(a.ss[op.ch] + static_cast<size_t>(r) * ss_ld + T, __float_as_uint(sq), flag);
-        }
-      } else if (op.kind == CH_RESID) {
-        chain_resid(a, op, blockIdx.x * CHAIN_EPI_WARPS + we, gridDim.x * CHAIN_EPI_WARPS, llw);
-      } else if (op.kind == CH_NORM) {
-        // norm_out[r] = f16(h * inv * w) from channel ch (rms_norm_row,
-        // src/cpu_decoder.rs:261-272); one warp per (row, tile)
-        const int tiles = a.hs / 128;
-        for (int it = blockIdx.x * CHAIN_EPI_WARPS + we; it < a.rows * tiles; it += gridDim.x * CHAIN_EPI_WARPS) {
-          const int r = it / tiles, T = it - r * tiles;
-          bool lok = true;
-          float t = 0.f;
-          if (lane < tiles) {
-            const uint64_t* src = a.ss[op.ch] + static_cast<size_t>(r) * ss_ld + lane;
-            uint2 w = ll_ld8(src);
-            if (w.y != flag) {
-              w = ll_spin8(src, llw, 0x753);
-              lok = w.y == flag;
-            }
-            t = __uint_as_float(w.x);
-          }
-          const int c = T * 128 + 4 * lane;
-          uint4 hv[1];
-          lok = ll_get16<1>(a.hf[op.ch] + static_cast<size_t>(r) * hf_ld + c / 2, 2, 1, hv, llw, 0x754) && lok;
-          if (!__all_sync(0xffffffffu, lok)) break;
-#pragma unroll
-          for (int o = 8; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-          t = __shfl_sync(0xffffffffu, t, 0);  // lane 0's order, the same value everywhere
-          const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, static_cast<float>(a.hs)), a.eps)));
-          const float2 h01 = __half22float2(*reinterpret_cast<const __half2*>(&hv[0].x));
-          const float2 h23 = __half22float2(*reinterpret_cast<const __half2*>(&hv[0].z));
-          const float4 w = *reinterpret_cast<const float4*>(op.norm_w + c);
-          uint2 xw;
-          xw.x = pack_half2(__fmul_rn(__fmul_rn(h01.x, inv), w.x), __fmul_rn(__fmul_rn(h01.y, inv), w.y));
-          xw.y = pack_half2(__fmul_rn(__fmul_rn(h23.x, inv), w.z), __fmul_rn(__fmul_rn(h23.y, inv), w.w));
-          __stcg(reinterpret_cast<uint2*>(op.norm_out + static_cast<size_t>(r) * a.hs + c), xw);
-        }
-      } else if (op.kind == CH_SILU) {
-        // gate|up tile t: rows [0, 64) gate[64 t + i], rows [64, 128) up[64 t + i].  Work
-        // unit: 4 outputs (row r, tile t, quad c); each thread takes every (G * 256)-th one.
-        const ChainGemm& g = a.gemms[op.gemm];
-        const int tiles = g.units / g.kblocks;
-        const int total = a.rows * tiles * 16;
-        const int stride = gridDim.x * CHAIN_EPI_THREADS;
-        for (int q = blockIdx.x * CHAIN_EPI_THREADS + e; q < total; q += stride) {
-          const int c = q & 15, rt = q >> 4;
-          const int r = rt / tiles, t = rt - r * tiles;
-          const int nseg = chain_tile_segs(g, t);
-          const uint64_t* p = chain_partial(a, g, t, r, 4 * c);
-          float4 gs, us;
-          bool lok = chain_sum4<CHAIN_SILU_SEG, false>(p, slot_u64, nseg, gs, llw, 0x755);
-          lok = chain_sum4<CHAIN_SILU_SEG, false>(p + 64, slot_u64, nseg, us, llw, 0x756) && lok;
-          if (!lok) break;
-          const float gv[4] = {gs.x, gs.y, gs.z, gs.w}, uv[4] = {us.x, us.y, us.z, us.w};
-          float o[4];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float gt = f16_round(gv[j]);
-            const float silu = __fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt)));
-            o[j] = __fmul_rn(silu, f16_round(uv[j]));
-          }
-          ll_st16(a.actf + static_cast<size_t>(r) * (a.inter / 2) + (t * 64 + 4 * c) / 2, pack_half2(o[0], o[1]),
-                  pack_half2(o[2], o[3]), flag);
-        }
-      } else if (op.kind == CH_QKV) {
-        chain_qkv(a, op, blockIdx.x * CHAIN_EPI_WARPS + we, gridDim.x * CHAIN_EPI_WARPS, llw);
+    // The launch's operations as straight-line code (the program is a template parameter):
+    // each operation's set-up then lives only while it runs, and nothing is hoisted into
+    // state held across all of them.
+    auto op_gemm = [&](const ChainOp& op, int gi) {
+      (void)op;
+      const ChainGemm& g = a.gemms[gi];
+      int ub, ue;
+      chain_unit_range(g, blockIdx.x, ub, ue);
+      auto seg_end_of = [&](int uu) { return min(ue, (uu / g.kblocks + 1) * g.kblocks); };
+      if (ub < ue && g.xsrc == XS_NORM) {
+        compute_inv(g.xch);
+        named_bar_sync(1, CHAIN_EPI_THREADS);  // inv_sh complete
       }
-      // ---- between operations: a CTA-wide verdict of the epilogue warps (no grid barrier:
-      // the next operation waits for exactly the flagged words it reads)
-      if (e == 0 && a.trace != nullptr && oi < 12) a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 1 + 2 * oi] = globaltimer();
-      if (oi + 1 < a.n_ops) {
-        if (!uniform_ok()) ok = false;
-        if (e == 0 && a.trace != nullptr && oi < 12) a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 2 + 2 * oi] = globaltimer();
+      // X tiles of the first segment, then per segment: the next segment's X tiles, then
+      // this segment's accumulators (so the issuers always have work queued)
+      int xu = ub;
+      if (ub < ue) {
+        build_xs(g, xu, seg_end_of(ub));
+        xu = seg_end_of(ub);
+        if (e == 0 && a.trace != nullptr) a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 25 + gi] = globaltimer();
+      }
+      int u = ub;
+      while (u < ue) {
+        const int T = u / g.kblocks;
+        const int seg_end = seg_end_of(u);
+        if (xu < ue) {
+          const int ne = seg_end_of(xu);
+          build_xs(g, xu, ne);
+          xu = ne;
+        }
+        ++seg;
+        const int d = seg & 1;
+        if (e == 0)
+          seg_ok = mbar_wait(&dfull_bar[d], static_cast<uint32_t>((seg >> 1) & 1), &abort_flag, a.status, 0x741)
+                       ? 1
+                       : 0;
+        named_bar_sync(1, CHAIN_EPI_THREADS);
+        const int got = seg_ok;
+        named_bar_sync(1, CHAIN_EPI_THREADS);
+        if (!got) {
+          ok = false;
+          break;
+        }
+        mbar_try_wait(&dfull_bar[d], static_cast<uint32_t>((seg >> 1) & 1));
+        tc_fence_after();
+        const int segidx = static_cast<int>(blockIdx.x) - cta_of_unit(static_cast<long long>(T) * g.kblocks,
+                                                                       g.units, g.grid);
+        uint64_t* dst = g.ws + (static_cast<size_t>(T) * g.max_seg + segidx) * slot_u64 + row;
+        const uint32_t dt = tmem_base + lane_base + static_cast<uint32_t>(d) * DCOLS;
+        const int n_used = min(NACC, seg_end - u);  // issuers that had units in the segment
+        for (int c0 = 16 * half; c0 < a.n_tile; c0 += 32) {
+          float v[16];
+          for (int q = 0; q < n_used; ++q) {
+            uint32_t r[16];
+            tmem_ld_x16(dt + static_cast<uint32_t>(q) * DSTR + static_cast<uint32_t>(c0), r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = q == 0 ? __uint_as_float(r[j]) : v[j] + __uint_as_float(r[j]);
+          }
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (c0 + j < a.rows) ll_st8(dst + static_cast<size_t>(c0 + j) * 128, __float_as_uint(v[j]), flag);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&dfree_bar[d]);
+        u = seg_end;
+      }
+    };
+    auto op_embed = [&](const ChainOp& op) {
+      // h[r] = embed row of the slot's input token: one warp per (row, 128-column tile),
+      // lane = 4 columns; the plain copy for the later launches, the flagged copy and the
+      // tile's sum of squares for this launch's norm
+      const int tiles = a.hs / 128;
+      for (int it = blockIdx.x * CHAIN_EPI_WARPS + we; it < a.rows * tiles; it += gridDim.x * CHAIN_EPI_WARPS) {
+        const int r = it / tiles, T = it - r * tiles;
+        const int slot = a.row_slot[r];
+        int tok = a.next_tok[slot];
+        if (tok < 0 || tok >= a.vocab) {
+          if (T == 0 && lane == 0) report_error(a.status, DEVERR_BOUNDS, 0x751);
+          tok = 0;
+        }
+        const int pos = a.pos[slot];
+        if (T == 0) {
+          if (lane == 0) {
+            a.row_pos[r] = pos;
+            a.row_page[r] = a.kv.page_table[static_cast<size_t>(slot) * a.kv.max_pages + (pos >> 6)];
+          }
+          // cos | sin rows of the position, 16 bytes per lane
+          const __half* rs = (lane < 16 ? a.rope_cos : a.rope_sin) + static_cast<size_t>(pos) * 128 + (lane & 15) * 8;
+          __stcg(reinterpret_cast<uint4*>(a.row_rope + static_cast<size_t>(r) * 256 + lane * 8),
+                 *reinterpret_cast<const uint4*>(rs));
+        }
+        const int c = T * 128 + 4 * lane;
+        const uint2 hw = *reinterpret_cast<const uint2*>(a.embed + static_cast<size_t>(tok) * a.hs + c);
+        __stcg(reinterpret_cast<uint2*>(a.h + static_cast<size_t>(r) * a.hs + c), hw);
+        ll_st16(a.hf[op.ch] + static_cast<size_t>(r) * hf_ld + c / 2, hw.x, hw.y, flag);
+        const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&hw.x));
+        const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&hw.y));
+        float sq = __fmul_rn(f01.x, f01.x);
+        sq = __fadd_rn(sq, __fmul_rn(f01.y, f01.y));
+        sq = __fadd_rn(sq, __fmul_rn(f23.x, f23.x));
+        sq = __fadd_rn(sq, __fmul_rn(f23.y, f23.y));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        if (lane == 0) ll_st8(a.ss[op.ch] + static_cast<size_t>(r) * ss_ld + T, __float_as_uint(sq), flag);
+      }
+    };
+    auto op_norm = [&](const ChainOp& op) {
+      // norm_out[r] = f16(h * inv * w) from channel ch (rms_norm_row,
+      // src/cpu_decoder.rs:261-272); one warp per (row, tile)
+      const int tiles = a.hs / 128;
+      for (int it = blockIdx.x * CHAIN_EPI_WARPS + we; it < a.rows * tiles; it += gridDim.x * CHAIN_EPI_WARPS) {
+        const int r = it / tiles, T = it - r * tiles;
+        bool lok = true;
+        float t = 0.f;
+        if (lane < tiles) {
+          const uint64_t* src = a.ss[op.ch] + static_cast<size_t>(r) * ss_ld + lane;
+          uint2 w = ll_ld8(src);
+          if (w.y != flag) {
+            w = ll_spin8(src, llw, 0x753);
+            lok = w.y == flag;
+          }
+          t = __uint_as_float(w.x);
+        }
+        const int c = T * 128 + 4 * lane;
+        uint4 hv[1];
+        lok = ll_get16<1>(a.hf[op.ch] + static_cast<size_t>(r) * hf_ld + c / 2, 2, 1, hv, llw, 0x754) && lok;
+        if (!__all_sync(0xffffffffu, lok)) break;
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+        t = __shfl_sync(0xffffffffu, t, 0);  // lane 0's order, the same value everywhere
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, static_cast<float>(a.hs)), a.eps)));
+        const float2 h01 = __half22float2(*reinterpret_cast<const __half2*>(&hv[0].x));
+        const float2 h23 = __half22float2(*reinterpret_cast<const __half2*>(&hv[0].z));
+        const float4 w = *reinterpret_cast<const float4*>(op.norm_w + c);
+        uint2 xw;
+        xw.x = pack_half2(__fmul_rn(__fmul_rn(h01.x, inv), w.x), __fmul_rn(__fmul_rn(h01.y, inv), w.y));
+        xw.y = pack_half2(__fmul_rn(__fmul_rn(h23.x, inv), w.z), __fmul_rn(__fmul_rn(h23.y, inv), w.w));
+        __stcg(reinterpret_cast<uint2*>(op.norm_out + static_cast<size_t>(r) * a.hs + c), xw);
+      }
+    };
+    auto op_silu = [&](const ChainOp& op) {
+      // gate|up tile t: rows [0, 64) gate[64 t + i], rows [64, 128) up[64 t + i].  Work
+      // unit: 4 outputs (row r, tile t, quad c); each thread takes every (G * 256)-th one.
+      const ChainGemm& g = a.gemms[op.gemm];
+      const int tiles = g.units / g.kblocks;
+      const int total = a.rows * tiles * 16;
+      const int stride = gridDim.x * CHAIN_EPI_THREADS;
+      for (int q = blockIdx.x * CHAIN_EPI_THREADS + e; q < total; q += stride) {
+        const int c = q & 15, rt = q >> 4;
+        const int r = rt / tiles, t = rt - r * tiles;
+        const int nseg = chain_tile_segs(g, t);
+        const uint64_t* p = chain_partial(a, g, t, r, 4 * c);
+        float4 gs, us;
+        bool lok = chain_sum4<CHAIN_SILU_SEG, false>(p, slot_u64, nseg, gs, llw, 0x755);
+        lok = chain_sum4<CHAIN_SILU_SEG, false>(p + 64, slot_u64, nseg, us, llw, 0x756) && lok;
+        if (!lok) break;
+        const float gv[4] = {gs.x, gs.y, gs.z, gs.w}, uv[4] = {us.x, us.y, us.z, us.w};
+        float o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float gt = f16_round(gv[j]);
+          const float silu = __fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt)));
+          o[j] = __fmul_rn(silu, f16_round(uv[j]));
+        }
+        ll_st16(a.actf + static_cast<size_t>(r) * (a.inter / 2) + (t * 64 + 4 * c) / 2, pack_half2(o[0], o[1]),
+                pack_half2(o[2], o[3]), flag);
+      }
+    };
+    // after operation oi: a CTA-wide verdict of the epilogue warps (no grid barrier: the
+    // next operation waits for exactly the flagged words it reads)
+    auto next = [&](int oi) {
+      if (e == 0 && a.trace != nullptr) a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 1 + 2 * oi] = globaltimer();
+      if (!uniform_ok()) ok = false;
+      if (e == 0 && a.trace != nullptr) a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 2 + 2 * oi] = globaltimer();
+      return ok;
+    };
+    const int wid = blockIdx.x * CHAIN_EPI_WARPS + we, nwarps = gridDim.x * CHAIN_EPI_WARPS;
+    if constexpr (PROG == CHAIN_PROG_FIRST) {
+      // embed + layer 0's input norm -> QKV GEMM -> q/k norm + RoPE + K/V append
+      op_embed(a.ops[0]);
+      if (next(0)) op_gemm(a.ops[1], 0);
+      if (next(1)) chain_qkv(a, a.ops[2], wid, nwarps, llw);
+      if (e == 0 && a.trace != nullptr) a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 1 + 2 * 2] = globaltimer();
+    } else {
+      // o_proj -> residual -> gate|up -> SiLU -> down -> residual -> (QKV + q/k norm, RoPE,
+      // K/V append | the final norm)
+      op_gemm(a.ops[0], 0);
+      if (next(0)) chain_resid(a, a.ops[1], wid, nwarps, llw);
+      if (next(1)) op_gemm(a.ops[2], 1);
+      if (next(2)) op_silu(a.ops[3]);
+      if (next(3)) op_gemm(a.ops[4], 2);
+      if (next(4)) chain_resid(a, a.ops[5], wid, nwarps, llw);
+      if constexpr (PROG == CHAIN_PROG_MIDDLE) {
+        if (next(5)) op_gemm(a.ops[6], 3);
+        if (next(6)) chain_qkv(a, a.ops[7], wid, nwarps, llw);
+        if (e == 0 && a.trace != nullptr) a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 1 + 2 * 7] = globaltimer();
+      } else {
+        if (next(5)) op_norm(a.ops[6]);
+        if (e == 0 && a.trace != nullptr) a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 1 + 2 * 6] = globaltimer();
       }
     }
+    regs_dec<128>();
   }
 
   griddep_launch_dependents();

@@ -76,11 +76,15 @@ cudaError_t init_kernel_attrs(std::string* err) {
     e = e ? e : cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(attn_smem_bytes(ATTN_MAX_ROWS)));
     cudaFuncAttributes fc{};
-    e = e ? e : cudaFuncGetAttributes(&fc, decode_chain_kernel);
+    e = e ? e : cudaFuncGetAttributes(&fc, decode_chain_kernel<CHAIN_PROG_MIDDLE>);
     if (e == cudaSuccess) {
       g_chain_dyn_max = optin - static_cast<int>(fc.sharedSizeBytes) - 256;
-      e = cudaFuncSetAttribute(decode_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      e = cudaFuncSetAttribute(decode_chain_kernel<CHAIN_PROG_FIRST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                g_chain_dyn_max);
+      e = e ? e : cudaFuncSetAttribute(decode_chain_kernel<CHAIN_PROG_MIDDLE>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, g_chain_dyn_max);
+      e = e ? e : cudaFuncSetAttribute(decode_chain_kernel<CHAIN_PROG_LAST>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, g_chain_dyn_max);
     }
     result = e;
   });
@@ -233,6 +237,7 @@ struct qasr_ctx {
   // decode chain (int8 weights, <= CHAIN_MAX_ROWS rows): partial sums and barrier counters
   bool chain_ok = false;
   bool chain_pdl = false;  // per-layer chain launches start while the attention drains (PDL)
+  int chain_wcap = 3;      // weight copies in flight per chain CTA (QASR_B200_CHAIN_WCAP overrides)
   uint64_t* chain_ws[4] = {};  // flagged partial sums of the chain's QKV, o_proj, gate|up, down GEMMs
   size_t chain_ws_n[4] = {};
   int chain_ws_rows = 0;
@@ -490,7 +495,8 @@ qasr_status enqueue_decode(qasr_ctx* c, int n, uint64_t* nk) {
 // on it instead of the cooperative attribute's check).
 static bool chain_one_cta_per_sm(size_t smem) {
   int blocks = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, decode_chain_kernel, CHAIN_THREADS, smem) != cudaSuccess) {
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, decode_chain_kernel<CHAIN_PROG_MIDDLE>, CHAIN_THREADS,
+                                                    smem) != cudaSuccess) {
     cudaGetLastError();
     return false;
   }
@@ -499,7 +505,7 @@ static bool chain_one_cta_per_sm(size_t smem) {
 
 // `pdl`: the previous launch is the attention merge, which this chain reads only after
 // griddepcontrol.wait, so it may start while the merge drains (see decode_chain_kernel).
-qasr_status launch_chain(qasr_ctx* c, const ChainArgs& a, const ChainShape& sh, bool pdl = false) {
+qasr_status launch_chain(qasr_ctx* c, const ChainArgs& a, const ChainShape& sh, int prog, bool pdl = false) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(c->num_sms);
   cfg.blockDim = dim3(CHAIN_THREADS);
@@ -522,7 +528,11 @@ qasr_status launch_chain(qasr_ctx* c, const ChainArgs& a, const ChainShape& sh, 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   g_launches.fetch_add(1, std::memory_order_relaxed);
-  CK(cudaLaunchKernelEx(&cfg, decode_chain_kernel, a), "decode chain launch");
+  cudaError_t e = cudaErrorInvalidValue;
+  if (prog == CHAIN_PROG_FIRST) e = cudaLaunchKernelEx(&cfg, decode_chain_kernel<CHAIN_PROG_FIRST>, a);
+  else if (prog == CHAIN_PROG_MIDDLE) e = cudaLaunchKernelEx(&cfg, decode_chain_kernel<CHAIN_PROG_MIDDLE>, a);
+  else if (prog == CHAIN_PROG_LAST) e = cudaLaunchKernelEx(&cfg, decode_chain_kernel<CHAIN_PROG_LAST>, a);
+  CK(e, "decode chain launch");
   return QASR_OK;
 }
 
@@ -570,6 +580,7 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
   }
   base.actf = c->chain_act;
   base.epoch = c->step_epoch;
+  base.w_inflight = c->chain_wcap;
   base.status = c->status;
   auto gemm = [&](const Linear& lin, int xsrc, int kind) {
     ChainGemm g = chain_gemm_plan(static_cast<const uint8_t*>(lin.w), lin.scale, lin.scale32, lin.n_out, lin.k, xsrc,
@@ -605,7 +616,7 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
     a.ops[2].layer = 0;
     a.ops[2].direct_meta = 1;
     a.n_ops = 3;
-    qasr_status s = launch_chain(c, a, sh);
+    qasr_status s = launch_chain(c, a, sh, CHAIN_PROG_FIRST);
     if (s) return s;
   }
   for (int l = 0; l < L; ++l) {
@@ -646,7 +657,7 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
       a.ops[k++].norm_out = c->xf;
     }
     a.n_ops = k;
-    if ((s = launch_chain(c, a, sh, true))) return s;
+    if ((s = launch_chain(c, a, sh, l + 1 < L ? CHAIN_PROG_MIDDLE : CHAIN_PROG_LAST, true))) return s;
   }
   *nk += 1 + 3 * static_cast<uint64_t>(L);  // chain 0, then per layer attention + merge + chain
   return enqueue_head(c, n, nullptr, c->drow_slot, c->drow_pos, c->out_tok, 0, nk, false, c->step_epoch);
@@ -878,6 +889,7 @@ qasr_status qasr_create(const qasr_text_config* cfg, const qasr_options* opts, i
   c->chain_ok = i8 && hs <= CHAIN_MAX_HS && hs % (2 * CHAIN_EPI_THREADS) == 0 && I % 64 == 0 &&
                 !(no_chain && no_chain[0] == '1');
   if (c->chain_ok) {
+    if (const char* wc = std::getenv("QASR_B200_CHAIN_WCAP")) c->chain_wcap = std::max(1, std::atoi(wc));
     const char* no_cpdl = std::getenv("QASR_B200_NO_CHAIN_PDL");
     c->chain_pdl = pdl_enabled() && !(no_cpdl && no_cpdl[0] == '1') &&
                    chain_one_cta_per_sm(chain_shape(std::min(opts->max_slots, CHAIN_MAX_ROWS)).smem);
