@@ -127,7 +127,7 @@ static int chain_seg_cap(int kind) {
 // int8 GEMM of the chain: at least two units (32 KB of weights) per taking-part CTA, and
 // few enough taking-part CTAs that no tile is cut into more than `max_seg_cap` segments
 // (the bound of the operation that adds the partials).
-static ChainGemm chain_gemm_plan(const uint8_t* w, const void* scale, bool scale32, int n_out, int k, int xsrc,
+static ChainGemm chain_gemm_plan(const uint8_t* w, const void* scale, bool scale32, int n_out, int k, int xmap,
                                  int sms, int max_seg_cap) {
   ChainGemm g{};
   g.w = w;
@@ -144,7 +144,7 @@ static ChainGemm chain_gemm_plan(const uint8_t* w, const void* scale, bool scale
     g.max_seg = ms;
     if (ms <= max_seg_cap || g.grid == 1) break;
   }
-  g.xsrc = xsrc;
+  g.xmap = xmap;
   return g;
 }
 
@@ -241,9 +241,8 @@ struct qasr_ctx {
   uint64_t* chain_ws[4] = {};  // flagged partial sums of the chain's QKV, o_proj, gate|up, down GEMMs
   size_t chain_ws_n[4] = {};
   int chain_ws_rows = 0;
-  uint64_t* chain_hf[CHAIN_CHANNELS] = {};  // flagged residual rows [CHAIN_MAX_ROWS][CHAIN_MAX_HS / 2]
+  unsigned int* chain_bar = nullptr;        // grid barrier counters, one per launch of a step
   uint64_t* chain_ss[CHAIN_CHANNELS] = {};  // flagged per-tile sums of squares [CHAIN_MAX_ROWS][CHAIN_MAX_HS / 128]
-  uint64_t* chain_act = nullptr;            // flagged SiLU output [CHAIN_MAX_ROWS][I / 2]
   unsigned int* step_epoch = nullptr;       // step counter of the chain's flags (finalize increments)
   int* chain_row_page = nullptr;        // [CHAIN_MAX_ROWS]
   __half* chain_row_rope = nullptr;     // [CHAIN_MAX_ROWS][256]
@@ -505,7 +504,15 @@ static bool chain_one_cta_per_sm(size_t smem) {
 
 // `pdl`: the previous launch is the attention merge, which this chain reads only after
 // griddepcontrol.wait, so it may start while the merge drains (see decode_chain_kernel).
-qasr_status launch_chain(qasr_ctx* c, const ChainArgs& a, const ChainShape& sh, int prog, bool pdl = false) {
+qasr_status launch_chain(qasr_ctx* c, const ChainArgs& a, const ChainShape& sh, int n, int prog, bool pdl = false) {
+  const int hs = c->cfg.hidden_size, qd = c->cfg.num_attention_heads * c->cfg.head_dim;
+  const int I = c->cfg.intermediate_size;
+  CUtensorMap tx, ta, tact;
+  const uint32_t box = static_cast<uint32_t>(sh.n_tile);
+  if (!make_tmap(&tx, c->x, false, hs, n, static_cast<uint64_t>(hs) * 2, 64, box, &c->err) ||
+      !make_tmap(&ta, c->attn, false, qd, n, static_cast<uint64_t>(qd) * 2, 64, box, &c->err) ||
+      !make_tmap(&tact, c->act, false, I, n, static_cast<uint64_t>(I) * 2, 64, box, &c->err))
+    return QASR_ERR_DEVICE;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(c->num_sms);
   cfg.blockDim = dim3(CHAIN_THREADS);
@@ -514,8 +521,8 @@ qasr_status launch_chain(qasr_ctx* c, const ChainArgs& a, const ChainShape& sh, 
   // A cooperative launch is placed as a whole, so under PDL it could not start before
   // every SM is free.  The PDL launch is therefore a plain one: one CTA per SM (its shared
   // memory admits no second, checked at context creation), every CTA resident once the
-  // attention's CTAs have exited (they never wait on this grid), and every wait on
-  // another CTA's flagged words is bounded in any case.
+  // attention's CTAs have exited (they never wait on this grid), and every wait on another
+  // CTA (grid barriers, flagged words) is bounded in any case.
   cudaLaunchAttribute attr[1];
   const bool use_pdl = pdl && c->chain_pdl;
   if (use_pdl) {
@@ -529,9 +536,10 @@ qasr_status launch_chain(qasr_ctx* c, const ChainArgs& a, const ChainShape& sh, 
   cfg.numAttrs = 1;
   g_launches.fetch_add(1, std::memory_order_relaxed);
   cudaError_t e = cudaErrorInvalidValue;
-  if (prog == CHAIN_PROG_FIRST) e = cudaLaunchKernelEx(&cfg, decode_chain_kernel<CHAIN_PROG_FIRST>, a);
-  else if (prog == CHAIN_PROG_MIDDLE) e = cudaLaunchKernelEx(&cfg, decode_chain_kernel<CHAIN_PROG_MIDDLE>, a);
-  else if (prog == CHAIN_PROG_LAST) e = cudaLaunchKernelEx(&cfg, decode_chain_kernel<CHAIN_PROG_LAST>, a);
+  if (prog == CHAIN_PROG_FIRST) e = cudaLaunchKernelEx(&cfg, decode_chain_kernel<CHAIN_PROG_FIRST>, tx, ta, tact, a);
+  else if (prog == CHAIN_PROG_MIDDLE)
+    e = cudaLaunchKernelEx(&cfg, decode_chain_kernel<CHAIN_PROG_MIDDLE>, tx, ta, tact, a);
+  else if (prog == CHAIN_PROG_LAST) e = cudaLaunchKernelEx(&cfg, decode_chain_kernel<CHAIN_PROG_LAST>, tx, ta, tact, a);
   CK(e, "decode chain launch");
   return QASR_OK;
 }
@@ -543,7 +551,10 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
   const ChainShape sh = chain_shape(n);
   const int L = c->cfg.num_hidden_layers, hs = c->cfg.hidden_size, I = c->cfg.intermediate_size;
   const int nq = c->cfg.num_attention_heads, nkv = c->cfg.num_key_value_heads;
+  const int qd = nq * c->cfg.head_dim, qkv_out = qd + 2 * nkv * 128;
   const int sms = c->num_sms;
+  CK(cudaMemsetAsync(c->chain_bar, 0, static_cast<size_t>(L + 1) * sizeof(unsigned int), c->stream),
+     "chain barrier reset");
   ChainArgs base{};
   base.rows = n;
   base.n_tile = sh.n_tile;
@@ -557,7 +568,7 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
   base.eps = c->cfg.rms_norm_eps;
   base.h = c->h;
   base.q = c->q;
-  base.attn = c->attn;
+  base.act = c->act;
   base.embed = c->embed;
   base.vocab = c->cfg.vocab_size;
   base.row_slot = c->drow_slot;
@@ -574,23 +585,14 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
   base.kv.layers = L;
   base.kv.nkv = nkv;
   base.ws_rows = c->chain_ws_rows;
-  for (int ch = 0; ch < CHAIN_CHANNELS; ++ch) {
-    base.hf[ch] = c->chain_hf[ch];
-    base.ss[ch] = c->chain_ss[ch];
-  }
-  base.actf = c->chain_act;
+  for (int ch = 0; ch < CHAIN_CHANNELS; ++ch) base.ss[ch] = c->chain_ss[ch];
   base.epoch = c->step_epoch;
   base.w_inflight = c->chain_wcap;
   base.status = c->status;
-  auto gemm = [&](const Linear& lin, int xsrc, int kind) {
-    ChainGemm g = chain_gemm_plan(static_cast<const uint8_t*>(lin.w), lin.scale, lin.scale32, lin.n_out, lin.k, xsrc,
-                                  sms, chain_seg_cap(kind));
+  auto gemm = [&](const Linear& lin, int xmap, int kind) {
+    ChainGemm g = chain_gemm_plan(static_cast<const uint8_t*>(lin.w), lin.scale, lin.scale32, lin.n_out, lin.k, xmap, sms,
+                                  chain_seg_cap(kind));
     g.ws = c->chain_ws[kind];
-    return g;
-  };
-  auto normed = [&](ChainGemm g, int ch, const float* w) {
-    g.xch = ch;
-    g.xnorm_w = w;
     return g;
   };
   auto op = [](int kind, int g) {
@@ -599,24 +601,25 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
     o.gemm = g;
     return o;
   };
-  // chain 0: embed (channel 1), layer 0's QKV GEMM over its input norm, q/k norm + RoPE + K/V append
+  // chain 0: embed + input norm of layer 0, QKV GEMM, q/k norm + RoPE + K/V append
   {
     ChainArgs a = base;
+    a.barrier = c->chain_bar;
     a.launch_idx = 0;
     a.trace = c->trace_on ? c->chain_trace : nullptr;
     const LayerDev& L0 = c->layers[0];
-    a.gemms[0] = normed(gemm(L0.qkv, XS_NORM, 0), 1, L0.iln);
-    a.next_first = gemm(L0.o, XS_ATTN, 1);
-    a.ops[0] = op(CH_EMBED, 0);
-    a.ops[0].ch = 1;
+    a.gemms[0] = gemm(L0.qkv, 0, 0);
+    a.next_first = gemm(L0.o, 1, 1);
+    a.ops[0] = op(CH_EMBED_NORM, 0);
+    a.ops[0].norm_w = L0.iln;
+    a.ops[0].norm_out = c->x;
     a.ops[1] = op(CH_GEMM, 0);
     a.ops[2] = op(CH_QKV, 0);
     a.ops[2].qn_w = L0.qn;
     a.ops[2].kn_w = L0.kn;
     a.ops[2].layer = 0;
-    a.ops[2].direct_meta = 1;
     a.n_ops = 3;
-    qasr_status s = launch_chain(c, a, sh, CHAIN_PROG_FIRST);
+    qasr_status s = launch_chain(c, a, sh, n, CHAIN_PROG_FIRST);
     if (s) return s;
   }
   for (int l = 0; l < L; ++l) {
@@ -627,38 +630,46 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
     if (s) return s;
     const LayerDev& Ld = c->layers[l];
     ChainArgs a = base;
+    a.barrier = c->chain_bar + l + 1;
     a.launch_idx = l + 1;
     if (c->chain_trace && c->trace_on) a.trace = c->chain_trace + static_cast<size_t>(l + 1) * sms * CHAIN_TRACE_SLOTS;
-    a.gemms[0] = gemm(Ld.o, XS_ATTN, 1);
-    if (l + 1 < L) a.next_first = gemm(c->layers[l + 1].o, XS_ATTN, 1);
-    a.gemms[1] = normed(gemm(Ld.gu, XS_NORM, 2), 0, Ld.pln);
-    a.gemms[2] = gemm(Ld.down, XS_ACT, 3);
+    a.gemms[0] = gemm(Ld.o, 1, 1);
+    if (l + 1 < L) a.next_first = gemm(c->layers[l + 1].o, 1, 1);
+    a.gemms[1] = gemm(Ld.gu, 0, 2);
+    a.gemms[2] = gemm(Ld.down, 2, 3);
     int k = 0;
     a.ops[k++] = op(CH_GEMM, 0);
     a.ops[k] = op(CH_RESID, 0);
     a.ops[k++].ch = 0;
+    a.ops[k] = op(CH_NORM, 0);
+    a.ops[k].ch = 0;
+    a.ops[k].norm_w = Ld.pln;
+    a.ops[k++].norm_out = c->x;
     a.ops[k++] = op(CH_GEMM, 1);
     a.ops[k++] = op(CH_SILU, 1);
     a.ops[k++] = op(CH_GEMM, 2);
     a.ops[k] = op(CH_RESID, 2);
     a.ops[k++].ch = 1;
+    a.ops[k] = op(CH_NORM, 2);
+    a.ops[k].ch = 1;
     if (l + 1 < L) {
       const LayerDev& Ln = c->layers[l + 1];
-      a.gemms[3] = normed(gemm(Ln.qkv, XS_NORM, 0), 1, Ln.iln);
+      a.ops[k].norm_w = Ln.iln;
+      a.ops[k++].norm_out = c->x;
+      a.gemms[3] = gemm(Ln.qkv, 0, 0);
       a.ops[k++] = op(CH_GEMM, 3);
       a.ops[k] = op(CH_QKV, 3);
       a.ops[k].qn_w = Ln.qn;
       a.ops[k].kn_w = Ln.kn;
       a.ops[k++].layer = l + 1;
-    } else {  // the final norm: the lm_head's input rows
-      a.ops[k] = op(CH_NORM, 2);
-      a.ops[k].ch = 1;
+    } else {
       a.ops[k].norm_w = c->final_norm;
       a.ops[k++].norm_out = c->xf;
     }
     a.n_ops = k;
-    if ((s = launch_chain(c, a, sh, l + 1 < L ? CHAIN_PROG_MIDDLE : CHAIN_PROG_LAST, true))) return s;
+    if ((s = launch_chain(c, a, sh, n, l + 1 < L ? CHAIN_PROG_MIDDLE : CHAIN_PROG_LAST, true))) return s;
   }
+  (void)qkv_out;
   *nk += 1 + 3 * static_cast<uint64_t>(L);  // chain 0, then per layer attention + merge + chain
   return enqueue_head(c, n, nullptr, c->drow_slot, c->drow_pos, c->out_tok, 0, nk, false, c->step_epoch);
 }
@@ -899,14 +910,13 @@ qasr_status qasr_create(const qasr_text_config* cfg, const qasr_options* opts, i
                                           chain_seg_cap(i));
       if (2ull * static_cast<unsigned long long>(g.units) * static_cast<unsigned long long>(g.grid) >= (1ull << 32))
         return fail(c, QASR_ERR_CAPACITY, "decode chain GEMM: too many units for 32-bit unit maps");
-      c->chain_ws_n[i] = static_cast<size_t>(shapes[i][0] / 128) * g.max_seg * c->chain_ws_rows * 128;
+      c->chain_ws_n[i] = static_cast<size_t>(shapes[i][0] / 128) * g.max_seg * chain_slot_words(c->chain_ws_rows);
       if ((s = dalloc(c, &c->chain_ws[i], c->chain_ws_n[i], "chain workspace"))) return s;
     }
     for (int ch = 0; ch < CHAIN_CHANNELS; ++ch)
-      if ((s = dalloc(c, &c->chain_hf[ch], static_cast<size_t>(CHAIN_MAX_ROWS) * CHAIN_MAX_HS / 2, "chain rows")) ||
-          (s = dalloc(c, &c->chain_ss[ch], static_cast<size_t>(CHAIN_MAX_ROWS) * CHAIN_MAX_HS / 128, "chain norms")))
+      if ((s = dalloc(c, &c->chain_ss[ch], static_cast<size_t>(CHAIN_MAX_ROWS) * CHAIN_MAX_HS / 128, "chain norms")))
         return s;
-    if ((s = dalloc(c, &c->chain_act, static_cast<size_t>(CHAIN_MAX_ROWS) * I / 2, "chain act")) ||
+    if ((s = dalloc(c, &c->chain_bar, static_cast<size_t>(L + 1), "chain barriers")) ||
         (s = dalloc(c, &c->step_epoch, 1, "step counter")) ||
         (s = dalloc(c, &c->chain_row_page, static_cast<size_t>(CHAIN_MAX_ROWS), "chain row pages")) ||
         (s = dalloc(c, &c->chain_row_rope, static_cast<size_t>(CHAIN_MAX_ROWS) * 256, "chain row rope")))
@@ -1166,15 +1176,9 @@ qasr_status qasr_step_batch(qasr_ctx* c, const int* slots, int n, int32_t* out_t
     // have last been written long ago: start every flag from zero (never a live flag).
     for (int i = 0; i < 4; ++i)
       CK(cudaMemsetAsync(c->chain_ws[i], 0, c->chain_ws_n[i] * sizeof(uint64_t), c->stream), "flag reset");
-    for (int ch = 0; ch < CHAIN_CHANNELS; ++ch) {
-      CK(cudaMemsetAsync(c->chain_hf[ch], 0, static_cast<size_t>(CHAIN_MAX_ROWS) * CHAIN_MAX_HS / 2 * 8, c->stream),
-         "flag reset");
+    for (int ch = 0; ch < CHAIN_CHANNELS; ++ch)
       CK(cudaMemsetAsync(c->chain_ss[ch], 0, static_cast<size_t>(CHAIN_MAX_ROWS) * CHAIN_MAX_HS / 128 * 8, c->stream),
          "flag reset");
-    }
-    CK(cudaMemsetAsync(c->chain_act, 0, static_cast<size_t>(CHAIN_MAX_ROWS) * c->cfg.intermediate_size / 2 * 8,
-                       c->stream),
-       "flag reset");
     c->chain_flags_for = list;
   }
   if (!use_graph || !c->graph || c->graph_slots != list) {
