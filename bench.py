@@ -1,19 +1,31 @@
 """Decode throughput of the B200 Qwen3-ASR text-decoder step (BASELINE.json metric).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config 1..5]
     python bench.py --audio 0.6b|1.7b [--impl b200|reference]   (the audio tower, one JSON line)
     torchrun --nproc-per-node N bench.py --gpus N ...   (one process per GPU)
 
-Workload (per GPU): Qwen3-ASR-1.7B text decoder, INT8 weights
-(per-row symmetric, f16 scales, seeded N(0, 0.02)), 32 decode slots, KV lengths drawn
-uniform in [100, 1500]; a slot that reaches 1500 positions is refilled with a fresh
-seeded prefix (prefill time is excluded from the decode metric and reported apart).
-Slots shard across GPUs: every rank holds a weight replica and its own 32 slots, no
+Default workload (per GPU, the headline): Qwen3-ASR-1.7B text
+decoder, INT8 weights (per-row symmetric, f16 scales, seeded N(0, 0.02)), 32 decode slots,
+KV lengths drawn uniform in [100, 1500]; a slot that reaches 1500 positions is refilled
+with a fresh seeded prefix (prefill time is excluded from the decode metric and reported
+apart).  Slots shard across GPUs: every rank holds a weight replica and its own slots, no
 collective on the hot path ("scaling": "weak").
 
-A step = one decode position for all 32 slots of the rank (BatchProjections::step).
-The weights (2.03 GB) and the KV cache (~3 GB) exceed the 126 MB L2 by far, so no L2
-flush is needed between steps.  Times are CUDA events on the context's stream; the
+--config selects another BASELINE.json configuration (one line each):
+  1  0.6B f16, 1 slot, prefix 9 ids + 200 audio rows + 15 ids, 64 greedy steps per run
+  2  0.6B INT8, 16 slots, prefix 9 ids + 390 audio rows + 23 ids, 256 steps per run
+  3  1.7B f16, 64 slots, prefixes of uniform 200-800 rows, 512 steps per run
+  4  the default above
+  5  decode attention microbench: 512 slots, KV lengths uniform 256-4096, one layer of
+     16 q / 8 kv heads x 128, f16 K/V/Q ~ N(0, 1); a step appends one K/V row per slot and
+     attends over it; the 13-token streaming-append mode is reported beside it
+Configs 1-3 decode a run of steps and then roll every slot back to the end of its prefix
+(the cached prefix rows stay valid), so the KV lengths stay in the configuration's range
+for any number of timed steps.
+
+A decode step = one position for all slots of the rank (BatchProjections::step).  The
+weights and the KV cache of configs 2-5 exceed the 126 MB L2 by far; config 1 moves 1.2 GB
+per step (also far above L2).  Times are CUDA events on the context's stream; the
 whole-job value uses the max over ranks.
 """
 from __future__ import annotations
@@ -33,9 +45,6 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-SLOTS_PER_GPU = 32
-LEN_LO, LEN_HI = 100, 1500
-MAX_SEQ = 1536
 SEED = 20260101
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_HBM_GBS = 6650.0
@@ -44,7 +53,35 @@ FALLBACK_HBM_GBS = 6650.0
 CHAIN_TRAFFIC_BYTES = 56274944 + 623360
 CHAIN_TRAFFIC_SOURCE = "ncu dram bytes of one middle launch of kernel_bench.py step --layers 2 (32 rows)"
 METRIC = "decode tokens/sec (box) 1.7B INT8 @1/2/4/8 B200; % HBM roofline"
-TRACED_STEPS = 8  # steps of the traced pass after the timed region
+TRACED_STEPS = 8  # steps of the traced pass after the timed region (int8 chain configs)
+
+# model preset, weights, slots per GPU, prefix lengths, run length
+WORKLOADS = {
+    1: dict(key="cfg1", preset="0.6b", int8=False, slots=1, lens=("fixed", 224), n_text=24, run=64, max_seq=512,
+            steps=64, cpu_kv=256,
+            desc="cfg1: Qwen3-ASR-0.6B text decoder, f16 weights, 1 slot, prefix 9 ids + 200 audio rows + 15 ids, "
+                 "64 greedy steps per run"),
+    2: dict(key="cfg2", preset="0.6b", int8=True, slots=16, lens=("fixed", 422), n_text=32, run=256, max_seq=768,
+            steps=256, cpu_kv=550,
+            desc="cfg2: Qwen3-ASR-0.6B text decoder, INT8 per-row weights (f16 scales), 16 slots, prefix 9 ids + "
+                 "390 audio rows + 23 ids, 256 greedy steps per run"),
+    3: dict(key="cfg3", preset="1.7b", int8=False, slots=64, lens=("uniform", 200, 800), n_text=24, run=512,
+            max_seq=1344, steps=512, cpu_kv=756,
+            desc="cfg3: Qwen3-ASR-1.7B text decoder, f16 weights, 64 slots, prefixes uniform 200-800 rows, "
+                 "512 greedy steps per run"),
+    4: dict(key="cfg4", preset="1.7b", int8=True, slots=32, lens=("uniform", 100, 1500), n_text=24, refill_at=1500,
+            max_seq=1536, steps=768, cpu_kv=800,
+            desc="cfg4: Qwen3-ASR-1.7B text decoder, INT8 per-row weights, 32 slots/GPU, KV U(100,1500), "
+                 "refill at 1500"),
+}
+
+
+def metric_of(n):
+    if n == 4:
+        return METRIC
+    w = WORKLOADS[n]
+    return (f"decode tokens/sec {w['key']} {w['preset'].upper()} {'INT8' if w['int8'] else 'f16'} "
+            f"{w['slots']} slots/GPU; % HBM roofline")
 
 
 def load_pkg():
@@ -60,19 +97,25 @@ def peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def algorithmic_bytes(cfg, kv_lens_before):
-    """HBM bytes one decode step must move: every weight byte once (int8 linears +
-    f16 scales + f16 tied lm_head + f32 norms) + each slot's K/V rows (all layers) +
-    the appended row."""
+def weight_bytes(cfg, int8):
+    """HBM bytes of every weight one decode step reads once: the layer linears (int8 + f16
+    per-row scales, or f16), the f16 tied lm_head / embedding table, the f32 norm gains."""
     hs, I, L, V = cfg["hidden_size"], cfg["intermediate_size"], cfg["num_hidden_layers"], cfg["vocab_size"]
     qd = cfg["num_attention_heads"] * cfg["head_dim"]
     kvd = cfg["num_key_value_heads"] * cfg["head_dim"]
     lin = (qd + 2 * kvd) * hs + hs * qd + 2 * I * hs + hs * I
     rows = (qd + 2 * kvd) + hs + 2 * I + hs
-    weights = L * (lin + 2 * rows) + V * hs * 2 + L * (2 * hs + 2 * cfg["head_dim"]) * 4 + hs * 4
-    kv_row = L * 2 * kvd * 2  # bytes of one position, all layers, K and V
+    per_layer = lin + 2 * rows if int8 else 2 * lin
+    return L * per_layer + V * hs * 2 + L * (2 * hs + 2 * cfg["head_dim"]) * 4 + hs * 4
+
+
+def algorithmic_bytes(cfg, kv_lens_before, int8=True):
+    """HBM bytes one decode step must move: every weight byte once + each slot's K/V rows
+    (all layers) + the appended row."""
+    kvd = cfg["num_key_value_heads"] * cfg["head_dim"]
+    kv_row = cfg["num_hidden_layers"] * 2 * kvd * 2  # bytes of one position, all layers, K and V
     kv = sum(int(n) for n in kv_lens_before) * kv_row + len(kv_lens_before) * kv_row
-    return weights, kv
+    return weight_bytes(cfg, int8), kv
 
 
 class ClockSampler:
@@ -118,6 +161,7 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(rows)}
 
 
+
 def cpu_baseline(cfg, int8=True, sample_tokens=12, prefix_rows=16, kv_len=800, label="cfg4"):
     """The reference's CPU decoder (restated in oracle/) on this host's cores: one slot
     (the reference's CPU path decodes one segment at a time, src/inference.rs:462-463),
@@ -132,7 +176,7 @@ def cpu_baseline(cfg, int8=True, sample_tokens=12, prefix_rows=16, kv_len=800, l
     model = SyntheticModel(cfg, seed=SEED)
     om = OracleModel(cfg)
     om.load_model(model, int8=int8)
-    max_seq = max(MAX_SEQ, kv_len + sample_tokens + 8)
+    max_seq = max(512, kv_len + sample_tokens + 8)
     cos, sin = build_rope_tables(max_seq)
     om.set_rope_tables(cos, sin)
     seq = OracleSeq(om, max_seq)
@@ -154,20 +198,53 @@ def cpu_baseline(cfg, int8=True, sample_tokens=12, prefix_rows=16, kv_len=800, l
                       f"reference CPU decoder keeps them)"}
 
 
+def attention_cpu_baseline(rows=12, seed=5):
+    """cfg5 on the host: the reference CPU decoder's attention() (restated in oracle/) for
+    `rows` slots x 8 kv heads x 2 q heads of the workload's length distribution; KV bytes
+    per second counted as the f16 bytes the GPU reads (the CPU keeps them as f32)."""
+    from oracle import oracle as o
+    rng = np.random.default_rng(seed)
+    lens = rng.integers(256, 4097, size=rows)
+    t_total, nbytes = 0.0, 0
+    for n in lens:
+        k = rng.standard_normal((int(n), 128)).astype(np.float16).astype(np.float32)
+        v = rng.standard_normal((int(n), 128)).astype(np.float16).astype(np.float32)
+        q = rng.standard_normal((16, 128)).astype(np.float16).view(np.uint16)
+        t0 = time.perf_counter()
+        for h in range(16):  # 16 q heads over 8 kv heads: each kv head's rows read twice
+            o.attention_head(q[h], k, v)
+        t_total += time.perf_counter() - t0
+        nbytes += int(n) * 8 * 512
+    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    return {"value": nbytes / t_total / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"cfg5: {rows} slots of KV U(256,4096) x 8 kv heads (16 q heads), attention() of the "
+                      f"reference CPU decoder restated, one call per (slot, q head), {int(lens.sum())} positions"}
+
+
 def run_reference(args, rank, world):
     """--impl reference: the reference CPU decoder path (restated, oracle/) on all host cores.
     Loads only oracle libraries (liboracle.so: the restated decoder + the input generator)."""
     if rank != 0:
         return
+    if args.config == 5:
+        cb = attention_cpu_baseline()
+        line = {"metric": ATTN_METRIC, "impl": "reference", "value": cb["value"], "unit": "GB/s", "n_gpus": world,
+                "steps": 1, "warmup": 0, "higher_is_better": True, "scaling": "replicas only", "vs_baseline": None,
+                "dtype": "f32", "data": "synthetic", "config": {"workload": cb["sample"]}, "cpu_baseline": cb,
+                "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
     from oracle.inputs import text_config
-    cfg = text_config("1.7b")
-    sample = max(3, min(args.steps, 12))
-    cb = cpu_baseline(cfg, sample_tokens=sample)
-    line = {"metric": METRIC, "impl": "reference", "value": cb["value"], "unit": "tokens/s",
+    wl = WORKLOADS[args.config]
+    cfg = text_config(wl["preset"])
+    sample = max(3, min(args.steps if args.steps else 12, 12))
+    cb = cpu_baseline(cfg, int8=wl["int8"], sample_tokens=sample, kv_len=wl["cpu_kv"], label=wl["key"])
+    line = {"metric": metric_of(args.config), "impl": "reference", "value": cb["value"], "unit": "tokens/s",
             "n_gpus": world, "steps": sample, "warmup": 1, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32 (int8 weights dequantised to f16)",
-            "data": "synthetic", "config": {"workload": "cfg4: Qwen3-ASR-1.7B INT8 decode, 1 slot on CPU at KV 800",
-                                            "model": "qwen3-asr-1.7b-text-decoder"},
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 (" + ("int8 weights dequantised to f16" if wl["int8"] else "f16 weights") + ")",
+            "data": "synthetic", "config": {"workload": f"{wl['key']}: 1 slot on CPU at KV {wl['cpu_kv']}",
+                                            "model": f"qwen3-asr-{wl['preset']}-text-decoder"},
             "cpu_baseline": cb,
             "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -298,57 +375,6 @@ def run_audio(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
-def time_kernels(pkg, torch, dec, cfg, slots, stream, kv_lens):
-    """CUDA-event timing of the two dominant kernels at the bench's shapes, through the
-    probe entry points: paged attention over the slots' current KV and the INT8
-    gate|up GEMM (the largest weight stream)."""
-    res = {}
-    dev = torch.cuda.current_device()  # this rank's GPU (the probes take an explicit device)
-    hs, I = cfg["hidden_size"], cfg["intermediate_size"]
-    # ---- gate|up GEMM, 32 rows, int8 [2I, hs]
-    w = torch.randint(-127, 128, (2 * I, hs), dtype=torch.int8, device="cuda")
-    s = torch.full((2 * I,), 0.001, dtype=torch.float16, device="cuda")
-    x = torch.randn((len(slots), hs), dtype=torch.float16, device="cuda")
-    o = torch.empty((len(slots), 2 * I), dtype=torch.float16, device="cuda")
-    wt = torch.empty_like(w)
-    pkg.kernel_pack_weights(dev, stream.cuda_stream, pkg.WEIGHTS_INT8, w.data_ptr(), 2 * I, hs, wt.data_ptr())
-    w = wt
-    def gemm():
-        pkg.kernel_gemm(dev, stream.cuda_stream, pkg.WEIGHTS_INT8, w.data_ptr(), s.data_ptr(), 2 * I, hs,
-                        x.data_ptr(), hs, len(slots), o.data_ptr(), 2 * I)
-    # ---- attention: one layer of the 1.7B shape over the slots' lengths
-    nkv = cfg["num_key_value_heads"]
-    lens = [int(n) for n in kv_lens]
-    max_pages = max((n + 63) // 64 for n in lens)
-    pool = torch.randn((len(lens) * max_pages, 1, 2, nkv, 64, 128), dtype=torch.float16, device="cuda")
-    pt = torch.arange(len(lens) * max_pages, dtype=torch.int32, device="cuda").view(len(lens), max_pages)
-    q = torch.randn((len(lens), 2 * nkv * 128), dtype=torch.float16, device="cuda")
-    ao = torch.empty_like(q)
-    rs = torch.arange(len(lens), dtype=torch.int32, device="cuda")
-    rp = torch.tensor([n - 1 for n in lens], dtype=torch.int32, device="cuda")
-    def attn():
-        pkg.kernel_attention(dev, stream.cuda_stream, q.data_ptr(), 2 * nkv * 128, ao.data_ptr(), pool.data_ptr(),
-                             pt.data_ptr(), max_pages, 1, nkv, 0, rs.data_ptr(), rp.data_ptr(), len(lens))
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
-    for name, fn, nbytes in (("gemm_gate_up_int8", gemm, 2 * I * hs + 2 * I * 2 + len(slots) * hs * 2 * 3),
-                             ("attention_decode", attn, sum(lens) * nkv * 512 + len(lens) * 4096 * 2)):
-        times = []
-        with torch.cuda.stream(stream):
-            for it in range(13):
-                flush.zero_()  # evict the operands from L2 between launches
-                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a.record(stream)
-                fn()
-                b.record(stream)
-                b.synchronize()
-                if it >= 3:
-                    times.append(a.elapsed_time(b) * 1e-3)
-        t = statistics.median(times)
-        res[name] = {"seconds": t, "bytes": nbytes, "gbs": nbytes / t / 1e9}
-    del w, pool, flush
-    return res
-
-
 def chain_timing(dec, cfg):
     """The decode-chain kernel of the last timed step, from its in-kernel %globaltimer
     stamps: each launch's duration = last CTA exit - first CTA entry.  The middle
@@ -373,33 +399,97 @@ def chain_timing(dec, cfg):
                       "run untraced), mean of the last traced step's middle launches"}
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=768)
-    ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--e2e-steps", type=int, default=128)
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--audio", choices=["0.6b", "1.7b"], default=None,
-                    help="time the audio tower instead of the decode step (one 30 s clip per step)")
-    args = ap.parse_args()
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
 
-    if args.audio:
-        if args.steps == ap.get_default("steps"):
-            args.steps = 50
-        if args.e2e_steps == ap.get_default("e2e_steps"):
-            args.e2e_steps = 10
-        run_audio(args, rank, world)
-        return
+def time_kernels(pkg, torch, cfg, int8, rows, stream, kv_lens):
+    """CUDA-event timing of the dominant kernels at the workload's shapes, alone, through the
+    probe entry points, L2 flushed before each launch: paged attention over the slots' current
+    KV, and the layer GEMMs (int8: the gate|up GEMM, the largest weight stream; f16, whose
+    step runs one GEMM kernel per projection: all four layer GEMMs and the lm_head, their
+    times and bytes summed as one step's GEMM work)."""
+    res = {}
+    dev = torch.cuda.current_device()  # this rank's GPU (the probes take an explicit device)
+    hs, I, V = cfg["hidden_size"], cfg["intermediate_size"], cfg["vocab_size"]
+    qd = cfg["num_attention_heads"] * cfg["head_dim"]
+    kvd = cfg["num_key_value_heads"] * cfg["head_dim"]
+    fmt = pkg.WEIGHTS_INT8 if int8 else pkg.WEIGHTS_F16
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
 
-    if args.impl == "reference":
-        run_reference(args, rank, world)
-        return
+    def timed(fn, iters=10):
+        times = []
+        with torch.cuda.stream(stream):
+            for it in range(iters + 3):
+                flush.zero_()  # evict the operands from L2 between launches
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                fn()
+                b.record(stream)
+                b.synchronize()
+                if it >= 3:
+                    times.append(a.elapsed_time(b) * 1e-3)
+        return statistics.median(times)
 
+    def gemm_entry(n_out, k):
+        dt = torch.int8 if int8 else torch.float16
+        w = (torch.randint(-127, 128, (n_out, k), dtype=torch.int8, device="cuda") if int8
+             else (torch.randn((n_out, k), device="cuda") * 0.02).to(torch.float16))
+        wt = torch.empty_like(w)
+        pkg.kernel_pack_weights(dev, stream.cuda_stream, fmt, w.data_ptr(), n_out, k, wt.data_ptr())
+        s = torch.full((n_out,), 0.001, dtype=torch.float16, device="cuda") if int8 else None
+        x = torch.randn((rows, k), dtype=torch.float16, device="cuda")
+        o = torch.empty((rows, n_out), dtype=torch.float16, device="cuda")
+        torch.cuda.synchronize()
+        del w
+        fn = lambda: pkg.kernel_gemm(dev, stream.cuda_stream, fmt, wt.data_ptr(), s.data_ptr() if s is not None else None,
+                                     n_out, k, x.data_ptr(), k, rows, o.data_ptr(), n_out)
+        nbytes = n_out * k * (1 if int8 else 2) + (n_out * 2 if int8 else 0) + rows * k * 2 + rows * n_out * 2
+        t = timed(fn)
+        del wt, x, o
+        return t, nbytes, dt
+
+    if int8:
+        t, nbytes, _ = gemm_entry(2 * I, hs)
+        res["gemm_gate_up_int8"] = {"seconds": t, "bytes": nbytes, "gbs": nbytes / t / 1e9}
+    else:
+        L = cfg["num_hidden_layers"]
+        tot_t, tot_b, parts = 0.0, 0, {}
+        for name, (n_out, k) in {"qkv": (qd + 2 * kvd, hs), "o": (hs, qd), "gate_up": (2 * I, hs),
+                                 "down": (hs, I)}.items():
+            t, nbytes, _ = gemm_entry(n_out, k)
+            parts[name] = {"seconds": t, "bytes": nbytes}
+            tot_t += L * t
+            tot_b += L * nbytes
+        t, nbytes, _ = gemm_entry(V, hs)
+        parts["lm_head"] = {"seconds": t, "bytes": nbytes}
+        tot_t += t
+        tot_b += nbytes
+        res["gemm_f16_step"] = {"seconds": tot_t, "bytes": tot_b, "gbs": tot_b / tot_t / 1e9, "launches_per_step":
+                                4 * L + 1, "parts": parts,
+                                "timing": "each GEMM alone (CUDA events, L2 flushed), 28 x the four layer GEMMs + "
+                                          "the lm_head, summed"}
+    # ---- attention: one layer over the slots' current lengths
+    nkv = cfg["num_key_value_heads"]
+    lens = [int(n) for n in kv_lens]
+    max_pages = max((n + 63) // 64 for n in lens)
+    pool = torch.randn((len(lens) * max_pages, 1, 2, nkv, 64, 128), dtype=torch.float16, device="cuda")
+    pt = torch.arange(len(lens) * max_pages, dtype=torch.int32, device="cuda").view(len(lens), max_pages)
+    q = torch.randn((len(lens), 2 * nkv * 128), dtype=torch.float16, device="cuda")
+    ao = torch.empty_like(q)
+    rs = torch.arange(len(lens), dtype=torch.int32, device="cuda")
+    rp = torch.tensor([n - 1 for n in lens], dtype=torch.int32, device="cuda")
+    fn = lambda: pkg.kernel_attention(dev, stream.cuda_stream, q.data_ptr(), 2 * nkv * 128, ao.data_ptr(),
+                                      pool.data_ptr(), pt.data_ptr(), max_pages, 1, nkv, 0, rs.data_ptr(),
+                                      rp.data_ptr(), len(lens))
+    nbytes = sum(lens) * nkv * 512 + len(lens) * 4096 * 2
+    t = timed(fn)
+    res["attention_decode"] = {"seconds": t, "bytes": nbytes, "gbs": nbytes / t / 1e9}
+    del pool, flush
+    return res
+
+
+def run_decode(args, rank, world, local):
+    """Configs 1-4: the decode step through the C ABI (qasr_step_batch, one CUDA graph per
+    step), timed on the device; e2e through the same call with host token buffers."""
+    wl = WORKLOADS[args.config]
     if world > 1:
         # torchrun starts every rank with OMP_NUM_THREADS=1; the host-side work (synthetic
         # weights, quantisation) gets this rank's share of the cores instead
@@ -421,67 +511,81 @@ def main():
             ctypes.CDLL("libgomp.so.1").omp_set_num_threads(int(os.environ["OMP_NUM_THREADS"]))
         except OSError:
             pass
-    cfg = pkg.text_config("1.7b")
+    cfg = pkg.text_config(wl["preset"])
+    slots_n = wl["slots"]
+    int8 = wl["int8"]
     model = pkg.SyntheticModel(cfg, seed=SEED)
-    rng = np.random.default_rng(SEED + 7919 * rank)
-    # trace=True allocates the stamp buffers; the timed steps run with the stamps off
-    # (set_trace(False)), a separate traced pass after them gives the chain kernel's own
-    # duration for the roofline line (its %globaltimer stamps per CTA and operation)
-    dec = pkg.TextDecoder(cfg, weight_format=pkg.WEIGHTS_INT8, max_slots=SLOTS_PER_GPU, max_seq=MAX_SEQ,
-                          device=local, trace=True)
-    dec.set_trace(False)
+    rng = np.random.default_rng(SEED + 7919 * rank + 104729 * args.config)
+    # trace=True (int8: the decode-chain path) allocates the stamp buffers; the timed steps run
+    # with the stamps off, a separate traced pass after them gives the chain kernel's duration
+    dec = pkg.TextDecoder(cfg, weight_format=pkg.WEIGHTS_INT8 if int8 else pkg.WEIGHTS_F16, max_slots=slots_n,
+                          max_seq=wl["max_seq"], device=local, trace=int8)
+    if int8:
+        dec.set_trace(False)
     t_load = time.perf_counter()
     dec.load_model(model)
-    cos, sin = pkg.build_rope_tables(MAX_SEQ)
+    cos, sin = pkg.build_rope_tables(wl["max_seq"])
     dec.set_rope_tables(cos, sin)
     t_load = time.perf_counter() - t_load
     stream = torch.cuda.Stream()
     dec.set_stream(stream.cuda_stream)
 
-    refill_count = [0] * SLOTS_PER_GPU
-
+    refill_count = [0] * slots_n
     from qasr_b200 import sharding
-    global_slots = sharding.slot_range(rank, world, SLOTS_PER_GPU)
+    global_slots = sharding.slot_range(rank, world, slots_n)
 
     def make_prefix(s, length):
         stream_id = sharding.prefix_stream(global_slots[s], refill_count[s])
         refill_count[s] += 1
-        n_text = min(24, length)
+        n_text = min(wl["n_text"], length)
         hidden, _ = model.prefix(stream_id, length - n_text, n_text=n_text, n_before=min(9, n_text))
         return hidden
 
-    slots = [dec.fork_capped(MAX_SEQ) for _ in range(SLOTS_PER_GPU)]
-    lens0 = rng.integers(LEN_LO, LEN_HI + 1, size=SLOTS_PER_GPU)
+    if wl["lens"][0] == "fixed":
+        lens0 = np.full(slots_n, wl["lens"][1])
+    else:
+        lens0 = rng.integers(wl["lens"][1], wl["lens"][2] + 1, size=slots_n)
+    slots = [dec.fork_capped(wl["max_seq"]) for _ in range(slots_n)]
     t_pf = time.perf_counter()
     dec.prefill_batch(slots, [make_prefix(s, int(n)) for s, n in enumerate(lens0)])
     t_pf = time.perf_counter() - t_pf
     kv_len = [int(n) for n in lens0]
     prefill_time = [0.0]
+    refill_at = wl.get("refill_at")
 
-    def refill_if_full():
-        full = [i for i in range(SLOTS_PER_GPU) if kv_len[i] >= LEN_HI]
-        if not full:
-            return
-        new = [int(rng.integers(LEN_LO, LEN_HI)) for _ in full]
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        dec.prefill_batch([slots[i] for i in full], [make_prefix(i, n) for i, n in zip(full, new)])
-        b.record(stream)
-        b.synchronize()
-        prefill_time[0] += a.elapsed_time(b) * 1e-3
-        for i, n in zip(full, new):
-            kv_len[i] = n
+    def between_steps():
+        """cfg4: refill slots at the length cap with fresh prefixes (prefill timed apart);
+        cfgs 1-3: roll slots that finished their run back to the end of their prefix."""
+        if refill_at is not None:
+            full = [i for i in range(slots_n) if kv_len[i] >= refill_at]
+            if not full:
+                return
+            new = [int(rng.integers(wl["lens"][1], refill_at)) for _ in full]
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            dec.prefill_batch([slots[i] for i in full], [make_prefix(i, n) for i, n in zip(full, new)])
+            b.record(stream)
+            b.synchronize()
+            prefill_time[0] += a.elapsed_time(b) * 1e-3
+            for i, n in zip(full, new):
+                kv_len[i] = n
+        else:
+            for i in range(slots_n):
+                if kv_len[i] >= int(lens0[i]) + wl["run"]:
+                    dec.set_pos(slots[i], int(lens0[i]))
+                    kv_len[i] = int(lens0[i])
 
     # ---- warm-up (graph capture happens on the first step)
     for _ in range(args.warmup):
-        refill_if_full()
+        between_steps()
         dec.step_batch(slots, read_tokens=False)
-        for i in range(SLOTS_PER_GPU):
+        for i in range(slots_n):
             kv_len[i] += 1
     dec.synchronize()
 
-    # ---- timed region: exactly K steps; refills (prefill) are timed apart and excluded
-    bytes_w, _ = algorithmic_bytes(cfg, [])
+    # ---- timed region: exactly K steps; refills / roll-backs happen between the timed steps
+    steps = args.steps
+    bytes_w, _ = algorithmic_bytes(cfg, [], int8)
     kv_bytes = 0
     step_events = []
     prefill_time[0] = 0.0
@@ -491,9 +595,9 @@ def main():
     clocks = ClockSampler(local)
     launches0 = pkg.launch_count()
     t_wall = time.perf_counter()
-    for _ in range(args.steps):
-        refill_if_full()
-        _, kvb = algorithmic_bytes(cfg, kv_len)
+    for _ in range(steps):
+        between_steps()
+        _, kvb = algorithmic_bytes(cfg, kv_len, int8)
         kv_bytes += kvb
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.nvtx.range_push("decode_step")
@@ -502,7 +606,7 @@ def main():
         b.record(stream)
         torch.cuda.nvtx.range_pop()
         step_events.append((a, b))
-        for i in range(SLOTS_PER_GPU):
+        for i in range(slots_n):
             kv_len[i] += 1
     torch.cuda.synchronize()
     t_wall = time.perf_counter() - t_wall
@@ -514,78 +618,85 @@ def main():
     dec.synchronize()
 
     # ---- end to end through the C ABI with host buffers: H2D input tokens, D2H argmax
-    e2e_steps = min(args.e2e_steps, args.steps)
-    host_tokens = np.zeros(SLOTS_PER_GPU, np.int32)
+    e2e_steps = min(args.e2e_steps, steps)
+    host_tokens = np.zeros(slots_n, np.int32)
     e2e_pf0 = prefill_time[0]
     torch.cuda.synchronize()
     t_e2e = time.perf_counter()
     for _ in range(e2e_steps):
-        refill_if_full()
+        between_steps()
         dec.set_input_tokens(slots, host_tokens)
         host_tokens = dec.step_batch(slots, read_tokens=True)
-        for i in range(SLOTS_PER_GPU):
+        for i in range(slots_n):
             kv_len[i] += 1
     t_e2e = time.perf_counter() - t_e2e - (prefill_time[0] - e2e_pf0)
 
     # ---- traced pass (not timed for the metric): the chain kernel's own launch durations,
     # and the step time with the stamps on beside the untraced one (their cost)
-    dec.set_trace(True)
-    traced = []
-    for it in range(3 + TRACED_STEPS):
-        refill_if_full()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        dec.step_batch(slots, read_tokens=False)
-        b.record(stream)
-        b.synchronize()
-        if it >= 3:
-            traced.append(a.elapsed_time(b) * 1e-3)
-        for i in range(SLOTS_PER_GPU):
-            kv_len[i] += 1
-    chain = chain_timing(dec, cfg)
-    dec.set_trace(False)
+    chain, traced = None, []
+    if int8:
+        dec.set_trace(True)
+        for it in range(3 + TRACED_STEPS):
+            between_steps()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            dec.step_batch(slots, read_tokens=False)
+            b.record(stream)
+            b.synchronize()
+            if it >= 3:
+                traced.append(a.elapsed_time(b) * 1e-3)
+            for i in range(slots_n):
+                kv_len[i] += 1
+        chain = chain_timing(dec, cfg)
+        dec.set_trace(False)
 
-    # ---- dominant kernels, timed alone at the bench shapes
-    kernels = time_kernels(pkg, torch, dec, cfg, slots, stream, kv_len)
+    # ---- dominant kernels, timed alone at the workload's shapes
+    kernels = time_kernels(pkg, torch, cfg, int8, slots_n, stream, kv_len)
 
     decode_max, e2e_max, _ = sharding.max_over_ranks([decode_s, t_e2e, prefill_time[0]], dist,
                                                      device=torch.device("cuda", local))
 
     if rank == 0:
         hbm, peak_kind = peaks()
-        tokens = args.steps * SLOTS_PER_GPU * world
+        tokens = steps * slots_n * world
         value = tokens / decode_max
-        ms_step = decode_max / args.steps * 1e3
-        step_bytes = bytes_w + kv_bytes / args.steps
-        step_gbs = step_bytes / (decode_max / args.steps) / 1e9
+        ms_step = decode_max / steps * 1e3
+        step_bytes = bytes_w + kv_bytes / steps
+        step_gbs = step_bytes / (decode_max / steps) / 1e9
+        traffic, traffic_src = None, None
         if chain is not None:
-            chain["share_of_step"] = chain["seconds"] * chain["launches_per_step"] / (decode_max / args.steps)
+            chain["share_of_step"] = chain["seconds"] * chain["launches_per_step"] / (decode_max / steps)
             chain["traced_step_ms"] = statistics.median(traced) * 1e3
             chain["untraced_step_ms"] = ms_step
             kernels["decode_chain"] = chain
-            dom_name = "decode_chain"  # the largest share of the step (~55-60%)
+            dom_name = "decode_chain"  # the largest share of the int8 step
+            if args.config == 4:
+                traffic, traffic_src = CHAIN_TRAFFIC_BYTES, CHAIN_TRAFFIC_SOURCE
         else:
-            dom_name = max(kernels, key=lambda k: kernels[k]["seconds"])
+            dom_name = "gemm_f16_step"  # the f16 step's GEMM launches together
+            kernels[dom_name]["share_of_step"] = kernels[dom_name]["seconds"] / (decode_max / steps)
         dom = kernels[dom_name]
         line = {
-            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "metric": metric_of(args.config), "value": value, "unit": "tokens/s", "n_gpus": world, "steps": steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int8 weights x f16 activations, f32 accumulate", "data": "synthetic",
-            "config": {"workload": "cfg4: Qwen3-ASR-1.7B text decoder, INT8 per-row weights, 32 slots/GPU, "
-                                   "KV U(100,1500), refill at 1500",
-                       "model": "qwen3-asr-1.7b-text-decoder (random init N(0,0.02), norm gains 1)",
-                       "global_batch": SLOTS_PER_GPU * world, "seq_len": f"{LEN_LO}-{LEN_HI}",
+            "vs_baseline": None,
+            "dtype": "int8 weights x f16 activations, f32 accumulate" if int8 else "f16 weights and activations, f32 accumulate",
+            "data": "synthetic",
+            "config": {"workload": wl["desc"],
+                       "model": f"qwen3-asr-{wl['preset']}-text-decoder (random init N(0,0.02), norm gains 1)",
+                       "global_batch": slots_n * world,
+                       "seq_len": (f"{wl['lens'][1]}" if wl["lens"][0] == "fixed" else f"{wl['lens'][1]}-{wl['lens'][2]}")
+                                  + (f", refill at {refill_at}" if refill_at else f" + {wl['run']} steps per run"),
                        "parallelism": f"slot-replica dp{world}",
-                       "l2": "operands (2.0 GB weights + ~3 GB KV per step) far exceed the 126 MB L2"},
+                       "l2": f"operands ({bytes_w / 1e9:.2f} GB weights + ~{kv_bytes / steps / 1e9:.2f} GB KV per step) "
+                             f"far exceed the 126 MB L2"},
             "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": dom["gbs"], "peak": hbm,
-                         "unit": "GB/s", "frac": dom["gbs"] / hbm,
-                         "traffic": CHAIN_TRAFFIC_BYTES if dom_name == "decode_chain" else None,
-                         "traffic_source": CHAIN_TRAFFIC_SOURCE if dom_name == "decode_chain" else None,
+                         "unit": "GB/s", "frac": dom["gbs"] / hbm, "traffic": traffic, "traffic_source": traffic_src,
                          "peak_kind": peak_kind, "kernels": kernels},
             "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_gbs, "frac": step_gbs / hbm,
-                              "weights_bytes": bytes_w, "kv_bytes_per_step": kv_bytes / args.steps},
-            "e2e": {"value": e2e_steps * SLOTS_PER_GPU * world / e2e_max, "unit": "tokens/s",
-                    "h2d_bytes_per_step": SLOTS_PER_GPU * 8, "d2h_bytes_per_step": SLOTS_PER_GPU * 4,
+                              "weights_bytes": bytes_w, "kv_bytes_per_step": kv_bytes / steps},
+            "e2e": {"value": e2e_steps * slots_n * world / e2e_max, "unit": "tokens/s",
+                    "h2d_bytes_per_step": slots_n * 8, "d2h_bytes_per_step": slots_n * 4,
                     "steps": e2e_steps},
             "gpu_launches": launches,
             "clocks": clk,
@@ -596,13 +707,167 @@ def main():
         }
         if world == 1 and not args.no_cpu_baseline:
             try:
-                line["cpu_baseline"] = cpu_baseline(cfg)
+                line["cpu_baseline"] = cpu_baseline(cfg, int8=int8, kv_len=wl["cpu_kv"], label=wl["key"])
             except Exception as e:  # keep the GPU line even if the host is too small
                 line["cpu_baseline"] = {"value": None, "error": str(e)}
         print(json.dumps(line), flush=True)
     dec.close()
     if dist is not None:
         dist.destroy_process_group()
+
+
+ATTN_METRIC = "decode attention KV GB/s (cfg5: 512 slots, KV U(256,4096), 16q/8kv x 128, f16); % HBM roofline"
+
+
+def run_attention(args, rank, world, local):
+    """Config 5: GQA decode attention over 512 ragged paged caches plus the per-step K/V
+    append (qasr_kernel_kv_append + qasr_kernel_attention), one layer; and the streaming mode
+    (13 new rows per slot appended and attended causally).  A step appends at each slot's
+    length and attends over length + 1 positions; the next step overwrites the same row, so
+    every step moves the same bytes.  One GPU per process (replicas for N > 1)."""
+    import torch
+    torch.cuda.set_device(local)
+    pkg = load_pkg()
+    dev = local
+    rng = np.random.default_rng(SEED + 5 + 7919 * rank)
+    n_slots, lo, hi, nkv, chunk = 512, 256, 4096, 8, 13
+    lens = rng.integers(lo, hi + 1, size=n_slots)
+    max_pages = int((lens.max() + chunk + 63) // 64)
+    pool = torch.randn((n_slots * max_pages, 1, 2, nkv, 64, 128), dtype=torch.float16, device="cuda")
+    perm = torch.randperm(n_slots * max_pages, device="cuda", dtype=torch.int64).to(torch.int32)
+    pt = perm.view(n_slots, max_pages).contiguous()
+    stream = torch.cuda.Stream()
+    st = stream.cuda_stream
+
+    def setup(rows_per_slot):
+        rows = n_slots * rows_per_slot
+        k = torch.randn((rows, nkv * 128), dtype=torch.float16, device="cuda")
+        v = torch.randn((rows, nkv * 128), dtype=torch.float16, device="cuda")
+        q = torch.randn((rows, 2 * nkv * 128), dtype=torch.float16, device="cuda")
+        out = torch.empty_like(q)
+        slot_of = np.repeat(np.arange(n_slots, dtype=np.int32), rows_per_slot)
+        pos = (np.repeat(lens, rows_per_slot) + np.tile(np.arange(rows_per_slot), n_slots)).astype(np.int32)
+        rs = torch.tensor(slot_of, device="cuda")
+        rp = torch.tensor(pos, device="cuda")
+        read = int(sum(int(l) * rows_per_slot + rows_per_slot * (rows_per_slot + 1) // 2 for l in lens)) * nkv * 512
+
+        def run():
+            pkg.kernel_kv_append(dev, st, k.data_ptr(), v.data_ptr(), pool.data_ptr(), pt.data_ptr(), max_pages, 1,
+                                 nkv, 0, rs.data_ptr(), rp.data_ptr(), rows)
+            pkg.kernel_attention(dev, st, q.data_ptr(), 2 * nkv * 128, out.data_ptr(), pool.data_ptr(), pt.data_ptr(),
+                                 max_pages, 1, nkv, 0, rs.data_ptr(), rp.data_ptr(), rows)
+        nbytes = read + rows * nkv * 512 + rows * 2 * nkv * 128 * 2 * 2
+        return run, nbytes, q, out
+
+    def timed(run, n):
+        ev = []
+        with torch.cuda.stream(stream):
+            for it in range(args.warmup + n):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                run()
+                b.record(stream)
+                if it >= args.warmup:
+                    ev.append((a, b))
+        torch.cuda.synchronize()
+        return [a.elapsed_time(b) * 1e-3 for a, b in ev]
+
+    run1, bytes1, q1, out1 = setup(1)
+    launches0 = pkg.launch_count()
+    clocks = ClockSampler(local)
+    t1 = timed(run1, args.steps)
+    clk = clocks.stop()
+    launches = (pkg.launch_count() - launches0) * args.steps // (args.warmup + args.steps)
+    tot = sum(t1)
+    # the attention kernel alone (the dominant kernel), same shapes
+    rs1 = torch.arange(n_slots, dtype=torch.int32, device="cuda")
+    rp1 = torch.tensor(lens.astype(np.int32), device="cuda")
+    attn_only = lambda: pkg.kernel_attention(dev, st, q1.data_ptr(), 2 * nkv * 128, out1.data_ptr(), pool.data_ptr(),
+                                             pt.data_ptr(), max_pages, 1, nkv, 0, rs1.data_ptr(), rp1.data_ptr(),
+                                             n_slots)
+    ta = statistics.median(timed(attn_only, 10))
+    attn_bytes = int((lens + 1).sum()) * nkv * 512 + n_slots * 2 * nkv * 128 * 2 * 2
+    # streaming mode: 13-token chunks
+    run13, bytes13, _, _ = setup(chunk)
+    t13 = timed(run13, max(3, args.steps // 4))
+    # e2e: q from pinned host memory, the output back to host memory, per step
+    q_host = q1.cpu().pin_memory()
+    o_host = torch.empty_like(q_host).pin_memory()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e2e_n = min(args.e2e_steps, args.steps)
+    with torch.cuda.stream(stream):
+        for _ in range(e2e_n):
+            q1.copy_(q_host, non_blocking=True)
+            run1()
+            o_host.copy_(out1, non_blocking=True)
+            stream.synchronize()
+    t_e2e = time.perf_counter() - t0
+    if rank == 0:
+        hbm, peak_kind = peaks()
+        gbs = bytes1 * len(t1) / tot / 1e9
+        line = {"metric": ATTN_METRIC, "value": gbs * world, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": tot / len(t1) * 1e3, "higher_is_better": True,
+                "scaling": "replicas only", "vs_baseline": None, "dtype": "f16 K/V/Q, f32 softmax and accumulate",
+                "data": "synthetic N(0,1)",
+                "config": {"workload": f"cfg5: {n_slots} slots, KV lengths U({lo},{hi}) (mean {lens.mean():.0f}), one "
+                                       f"layer 16 q / 8 kv heads x 128, per step: append one K/V row per slot + "
+                                       f"attention over length + 1",
+                           "global_batch": n_slots * world, "seq_len": f"{lo}-{hi}",
+                           "parallelism": f"replicas x{world}",
+                           "l2": f"{bytes1 / 1e9:.2f} GB of KV per step (over the 126 MB L2)"},
+                "roofline": {"bound": "hbm", "kernel": "attention_kernel (+ attention_merge_kernel)",
+                             "achieved": attn_bytes / ta / 1e9, "peak": hbm, "unit": "GB/s",
+                             "frac": attn_bytes / ta / 1e9 / hbm, "traffic": None, "peak_kind": peak_kind,
+                             "kernel_seconds": ta, "kernel_bytes": attn_bytes},
+                "streaming": {"chunk": chunk, "rows": n_slots * chunk, "ms_per_step": statistics.median(t13) * 1e3,
+                              "gbs": bytes13 / statistics.median(t13) / 1e9,
+                              "what": "13 new K/V rows per slot appended, then causal attention of the 13 rows"},
+                "e2e": {"value": bytes1 * e2e_n / t_e2e / 1e9 * world, "unit": "GB/s",
+                        "h2d_bytes_per_step": q_host.numel() * 2, "d2h_bytes_per_step": o_host.numel() * 2,
+                        "steps": e2e_n},
+                "gpu_launches": launches, "clocks": clk}
+        if world == 1 and not args.no_cpu_baseline:
+            try:
+                line["cpu_baseline"] = attention_cpu_baseline()
+            except Exception as e:
+                line["cpu_baseline"] = {"value": None, "error": str(e)}
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (default: the config's run length)")
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", type=int, default=4, choices=[1, 2, 3, 4, 5],
+                    help="BASELINE.json configuration (4, the headline, by default)")
+    ap.add_argument("--e2e-steps", type=int, default=128)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--audio", choices=["0.6b", "1.7b"], default=None,
+                    help="time the audio tower instead of the decode step (one 30 s clip per step)")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.audio:
+        if args.steps is None:
+            args.steps = 50
+        if args.e2e_steps == ap.get_default("e2e_steps"):
+            args.e2e_steps = 10
+        run_audio(args, rank, world)
+        return
+    if args.steps is None:
+        args.steps = WORKLOADS[args.config]["steps"] if args.config in WORKLOADS else 40
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if args.config == 5:
+        run_attention(args, rank, world, local)
+        return
+    run_decode(args, rank, world, local)
 
 
 if __name__ == "__main__":

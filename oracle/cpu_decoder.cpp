@@ -59,6 +59,12 @@ float to_f32(uint16_t h) {
 // buffers hold once read back with to_f32()).
 inline float r16(float v) { return to_f32(to_f16(v)); }
 
+// Summation order of every f32 dot product: 0 = the reference's (below), 1 = each
+// accumulator walks k backwards.  The second is an equally valid evaluation of the same
+// sums; tests run the oracle both ways to measure the model's own sensitivity to the
+// order of f32 additions (the floor under any GPU-vs-CPU logit difference).
+int g_sum_order = 0;
+
 // `Mat` (src/cpu_decoder.rs:11-102): row-major f32 copy of the f16 (or dequantised
 // int8) weight.
 struct Mat {
@@ -71,8 +77,8 @@ struct Mat {
     const float* w = &data[static_cast<size_t>(o) * cols];
     float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
     const int quads = cols / 4;
-    for (int q = 0; q < quads; ++q) {
-      const int k = q * 4;
+    for (int qq = 0; qq < quads; ++qq) {
+      const int k = (g_sum_order ? quads - 1 - qq : qq) * 4;
       a0 += w[k] * x[k];
       a1 += w[k + 1] * x[k + 1];
       a2 += w[k + 2] * x[k + 2];
@@ -89,8 +95,10 @@ struct Mat {
     const float* w = &data[static_cast<size_t>(o) * cols];
     float a[16] = {0};
     const int blocks = cols / 16;
-    for (int b = 0; b < blocks; ++b)
+    for (int bb = 0; bb < blocks; ++bb) {
+      const int b = g_sum_order ? blocks - 1 - bb : bb;
       for (int j = 0; j < 16; ++j) a[j] += w[b * 16 + j] * x[b * 16 + j];
+    }
     for (int j = 8; j > 0; j >>= 1)
       for (int i = 0; i < j; ++i) a[i] = a[i] + a[i + j];
     float s = a[0];
@@ -332,7 +340,10 @@ int32_t logits_argmax(oracle_seq* s, const std::vector<uint16_t>& x, int rows, f
   for (int t = 0; t < vocab; ++t) {
     const uint16_t* row = &m->embed[static_cast<size_t>(t) * hs];
     float acc = 0.0f;
-    for (int i = 0; i < hs; ++i) acc += to_f32(row[i]) * nx[i];
+    for (int ii = 0; ii < hs; ++ii) {
+      const int i = g_sum_order ? hs - 1 - ii : ii;
+      acc += to_f32(row[i]) * nx[i];
+    }
     logits[t] = acc;
   }
   int best = 0;
@@ -467,6 +478,8 @@ int oracle_step(oracle_seq* s, int32_t* token, float* logits) {
 
 void oracle_set_last_token(oracle_seq* s, int32_t tok) { s->last_token = static_cast<uint32_t>(tok); }
 int oracle_pos(const oracle_seq* s) { return s->pos; }
+void oracle_set_sum_order(int order) { g_sum_order = order ? 1 : 0; }
+
 void oracle_set_pos(oracle_seq* s, int pos) {
   if (pos >= 0 && pos <= s->max_seq) s->pos = pos;  // out-of-range positions are ignored
 }

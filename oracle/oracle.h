@@ -54,6 +54,10 @@ int oracle_step(oracle_seq* s, int32_t* token, float* logits);
 void oracle_set_last_token(oracle_seq* s, int32_t tok);
 int oracle_pos(const oracle_seq* s);
 void oracle_set_pos(oracle_seq* s, int pos);
+/* Summation order of every f32 dot product (process-wide): 0 = the reference's, 1 = each
+ * accumulator over k backwards -- the same sums in another valid order, to measure how much
+ * the model's logits move with the order of f32 additions. */
+void oracle_set_sum_order(int order);
 /* Copy the f16 hidden state rows of the last forward (rows x hidden). */
 int oracle_last_hidden(const oracle_seq* s, uint16_t* out, int rows);
 /* K / V cache rows (f16-rounded values as f32) of one layer and kv head. */

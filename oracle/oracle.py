@@ -53,6 +53,8 @@ def _load():
     lib.oracle_pos.argtypes = [P]
     lib.oracle_set_pos.argtypes = [P, I]
     lib.oracle_set_pos.restype = None
+    lib.oracle_set_sum_order.argtypes = [I]
+    lib.oracle_set_sum_order.restype = None
     lib.oracle_last_hidden.argtypes = [P, P, I]
     lib.oracle_kv_rows.argtypes = [P, I, I, I, I, P, P]
     lib.oracle_f32_to_f16.argtypes = [ctypes.c_float]
@@ -214,6 +216,12 @@ class OracleSeq:
         if lib.oracle_kv_rows(self._s, layer, kv_head, pos0, n, _p(k), _p(v)) != 0:
             raise ValueError("bad kv range")
         return k, v
+
+
+def set_sum_order(order: int):
+    """0: the reference's f32 summation order (default); 1: every dot product's k reversed
+    (process-wide; used to measure the model's own order sensitivity)."""
+    lib.oracle_set_sum_order(int(order))
 
 
 # ---- operation-level helpers -------------------------------------------------

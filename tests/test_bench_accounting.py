@@ -25,19 +25,28 @@ def _bench():
 def test_weight_bytes_per_step(qasr, preset, int8, want):
     b = _bench()
     cfg = qasr.text_config(preset)
-    w, kv = b.algorithmic_bytes(cfg, [0])
+    w, kv = b.algorithmic_bytes(cfg, [0], int8=int8)
     hs = cfg["hidden_size"]
     norms = cfg["num_hidden_layers"] * (2 * hs + 2 * cfg["head_dim"]) * 4 + hs * 4
-    if not int8:
-        # the bench counts the int8 layout; an f16 step moves 2 B per linear weight, no scales
-        L, I = cfg["num_hidden_layers"], cfg["intermediate_size"]
-        qd, kvd = cfg["num_attention_heads"] * 128, cfg["num_key_value_heads"] * 128
-        lin = (qd + 2 * kvd) * hs + hs * qd + 2 * I * hs + hs * I
-        rows = (qd + 2 * kvd) + hs + 2 * I + hs
-        w = w - L * (lin + 2 * rows) + L * 2 * lin
     assert w - norms == want
     # one appended position: K + V of 8 kv heads x 128 dims x 28 layers, f16 (both sizes)
     assert kv == 114_688
+
+
+def test_workload_table_matches_the_configs(qasr):
+    """bench.py's --config table against BASELINE.json's configs: model, weights, slots,
+    prefix lengths and run lengths."""
+    b = _bench()
+    w = b.WORKLOADS
+    assert (w[1]["preset"], w[1]["int8"], w[1]["slots"], w[1]["lens"], w[1]["run"]) == ("0.6b", False, 1, ("fixed", 224), 64)
+    assert 9 + 200 + 15 == w[1]["lens"][1] and w[1]["n_text"] == 24
+    assert (w[2]["preset"], w[2]["int8"], w[2]["slots"], w[2]["lens"], w[2]["run"]) == ("0.6b", True, 16, ("fixed", 422), 256)
+    assert 9 + 390 + 23 == w[2]["lens"][1] and w[2]["n_text"] == 32
+    assert (w[3]["preset"], w[3]["int8"], w[3]["slots"], w[3]["lens"], w[3]["run"]) == ("1.7b", False, 64, ("uniform", 200, 800), 512)
+    assert (w[4]["preset"], w[4]["int8"], w[4]["slots"], w[4]["lens"], w[4]["refill_at"]) == ("1.7b", True, 32, ("uniform", 100, 1500), 1500)
+    for n, wl in w.items():
+        longest = wl["lens"][-1] + wl.get("run", 0)
+        assert longest <= wl["max_seq"], n
 
 
 def test_audio_flops_direct_count(qasr):

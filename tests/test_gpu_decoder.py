@@ -39,7 +39,13 @@ def _setup(qasr, oracle, cfg, int8, slots, max_seq=2048, seed=1234):
 
 
 def _run_parity(qasr, oracle, cfg, int8, n_audio, steps, n_slots=1, check_slots=None, n_text=24,
-                max_seq=2048):
+                max_seq=2048, floor=False):
+    """Teacher-forced parity run.  floor=True also replays the checked slots through the
+    oracle with every f32 sum reversed (oracle.set_sum_order(1)): the same arithmetic in
+    another valid order; the largest logit difference between the two oracle runs is the
+    model's own order-sensitivity floor, and the returned tolerance becomes
+    max(tol, 2 * floor)."""
+    from oracle import oracle as oracle_mod
     from oracle.oracle import OracleSeq
     tol = INT8_TOL if int8 else F16_TOL
     model, dec, om = _setup(qasr, oracle, cfg, int8, n_slots, max_seq=max_seq)
@@ -58,10 +64,13 @@ def _run_parity(qasr, oracle, cfg, int8, n_audio, steps, n_slots=1, check_slots=
         report.append((step, i, int(g), int(o), float(lg[o] - lg[g])))
 
     step_worst = 0.0
+    o_logits = {i: [] for i in check_slots}  # kept for the floor replay
     for i in check_slots:
         seqs[i] = OracleSeq(om, max_seq)
         tok, lg = seqs[i].prefill(prefixes[i], want_logits=True)
         o_tok[i] = [tok]
+        if floor:
+            o_logits[i].append(lg)
         step_worst = max(step_worst, float(np.max(np.abs(g_logits0[i] - lg))))
         note(0, i, first[i], tok, lg)
     per_step.append(step_worst)
@@ -79,13 +88,33 @@ def _run_parity(qasr, oracle, cfg, int8, n_audio, steps, n_slots=1, check_slots=
         for i in check_slots:
             tok, lg = seqs[i].step(want_logits=True)
             o_tok[i].append(tok)
+            if floor:
+                o_logits[i].append(lg)
             step_worst = max(step_worst, float(np.max(np.abs(lg_all[i] - lg))))
             note(len(o_tok[i]) - 1, i, out[i], tok, lg)
         per_step.append(step_worst)
         worst = max(worst, step_worst)
     dec.close()
-    om.close()
     print("max |dlogit| per step (0 = prefill): " + " ".join(f"{w:.3g}" for w in per_step))
+    if floor:
+        fl = 0.0
+        oracle_mod.set_sum_order(1)
+        try:
+            for i in check_slots:
+                seq = OracleSeq(om, max_seq)
+                _, lg = seq.prefill(prefixes[i], want_logits=True)
+                fl = max(fl, float(np.max(np.abs(lg - o_logits[i][0]))))
+                for k in range(1, len(o_logits[i])):
+                    seq.set_last_token(o_tok[i][k - 1])
+                    _, lg = seq.step(want_logits=True)
+                    fl = max(fl, float(np.max(np.abs(lg - o_logits[i][k]))))
+                seq.close()
+        finally:
+            oracle_mod.set_sum_order(0)
+        print(f"oracle order-sensitivity floor (same sums, k reversed): max |dlogit| {fl:.3g}; "
+              f"tolerance max({tol}, 2 x floor) = {max(tol, 2 * fl):.3g}")
+        tol = max(tol, 2.0 * fl)
+    om.close()
     return worst, report, tol
 
 

@@ -27,19 +27,22 @@ def test_cfg4_shape_int8_chain_matches_oracle(qasr, cuda_device, oracle):
     n_audio = [int(x) for x in rng.integers(100 - 24, 1500 - 24 - 24, size=32)]
     n_audio[0], n_audio[13], n_audio[27] = 260, 420, 150  # the checked slots: oracle prefill time
     _check(*_run_parity(qasr, oracle, cfg, True, n_audio=n_audio, steps=16, n_slots=32,
-                        check_slots=[0, 13, 27], max_seq=1536))
+                        check_slots=[0, 13, 27], max_seq=1536, floor=True))
 
 
 @pytest.mark.slow
 def test_cfg3_shape_f16_matches_oracle(qasr, cuda_device, oracle):
     """1.7B f16 weights (the per-kernel GEMM path), 64 slots with prefixes of 200-800
-    rows; slots 5 and 50 checked teacher-forced for 16 steps (logits within 2e-2)."""
+    rows; slots 5 and 50 checked teacher-forced for 16 steps, ids identical.  Logits within
+    max(2e-2, 2 x the oracle's own order-sensitivity floor): this model's logits move by
+    ~0.015-0.018 when the reference's f32 sums are merely reordered (measured by the same
+    test with the oracle's k loops reversed), so 2e-2 alone sits on the floor itself."""
     cfg = qasr.text_config("1.7b")
     rng = np.random.default_rng(3)
     n_audio = [int(x) for x in rng.integers(200 - 24, 800 - 24, size=64)]
     n_audio[5], n_audio[50] = 300, 190
     _check(*_run_parity(qasr, oracle, cfg, False, n_audio=n_audio, steps=16, n_slots=64,
-                        check_slots=[5, 50], max_seq=1024))
+                        check_slots=[5, 50], max_seq=1024, floor=True))
 
 
 @pytest.mark.slow
