@@ -159,6 +159,16 @@ inline GemmShape gemm_shape(int n_out, int k, bool int8, int rows, int num_sms, 
   return s;
 }
 
+// TMEM columns one gemm_tc_kernel CTA addresses: two accumulator buffers of the tile's
+// width rounded to 32, and for int8 weights at least one 64-column dequantised A stage.
+// Every tcgen05 access must stay inside the GEMM_TMEM_COLS the CTA allocates; a plan
+// that would not is refused on the host (plan_gemm) rather than run.
+inline bool gemm_tmem_fits(const GemmShape& s, bool int8) {
+  const int dcols = (s.n_tile + 31) / 32 * 32;
+  const int a_cols = int8 ? 64 : 0;  // at least one A stage
+  return 2 * dcols + a_cols <= static_cast<int>(GEMM_TMEM_COLS);
+}
+
 // Dynamic shared memory limits and kernel attributes (once per device, on the current one).
 cudaError_t init_kernel_attrs(std::string* err);
 

@@ -111,6 +111,10 @@ static ChainShape chain_shape(int rows) {
   const int dcols = dstr * s.n_acc;
   // unit slots: one 64-column A stage in TMEM and one X tile in shared memory each
   s.a_stages = std::min(CHAIN_MAX_A_STAGES, (static_cast<int>(GEMM_TMEM_COLS) - 2 * dcols) / 64);
+  // the accumulators (2 x n_acc x dstr) and at least one A stage must fit the 512 TMEM
+  // columns the CTA allocates: n_acc falls as the tile widens (at most 128 rows: 2 x 128 +
+  // 4 x 64 = 512)
+  static_assert(2 * CHAIN_MAX_ROWS + 64 <= static_cast<int>(GEMM_TMEM_COLS), "chain TMEM budget");
   const int xstage = 2 * s.n_tile * 128;
   const int dyn = g_chain_dyn_max > 0 ? g_chain_dyn_max : 200 * 1024;
   s.w_stages = std::min(CHAIN_MAX_W_STAGES, (dyn - 1024 - s.a_stages * xstage) / 16384);
@@ -327,6 +331,9 @@ qasr_status plan_gemm(qasr_ctx* c, const Linear& lin, const __half* X, int ldx, 
   if (s.ws_floats > c->gemm_ws_floats || static_cast<size_t>(s.tiles) > c->gemm_cnt_n)
     return fail(c, QASR_ERR_CAPACITY, "GEMM workspace too small for %d x %d over %d rows",
                 lin.n_out, lin.k, rows);
+  if (!gemm_tmem_fits(s, lin.int8))
+    return fail(c, QASR_ERR_CAPACITY, "GEMM %d x %d over %d rows: %d-column tiles need more TMEM than a CTA holds",
+                lin.n_out, lin.k, rows, s.n_tile);
   if (!make_tmap(&L->tmx, X, false, static_cast<uint64_t>(lin.k), static_cast<uint64_t>(rows),
                  static_cast<uint64_t>(ldx) * 2, 64, static_cast<uint32_t>(s.n_tile), &c->err))
     return QASR_ERR_DEVICE;
