@@ -50,7 +50,7 @@ PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_HBM_GBS = 6650.0
 # dram__bytes_read.sum + dram__bytes_write.sum of one middle decode_chain_kernel launch,
 # from an ncu capture of `kernel_bench.py step --layers 2` (same per-layer shapes, 32 rows)
-CHAIN_TRAFFIC_BYTES = 56274944 + 623360
+CHAIN_TRAFFIC_BYTES = 55376384 + 1674496
 CHAIN_TRAFFIC_SOURCE = "ncu dram bytes of one middle launch of kernel_bench.py step --layers 2 (32 rows)"
 METRIC = "decode tokens/sec (box) 1.7B INT8 @1/2/4/8 B200; % HBM roofline"
 TRACED_STEPS = 8  # steps of the traced pass after the timed region (int8 chain configs)
