@@ -190,6 +190,11 @@ __device__ __forceinline__ unsigned int ld_relaxed_gpu(const unsigned int* p) {
   asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ unsigned int ld_acquire_gpu(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 __device__ __forceinline__ int ld_acquire_cta_shared(const int* p) {
   int v;
   asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
@@ -322,6 +327,59 @@ __device__ __forceinline__ bool chain_sum4(const uint64_t* p, size_t stride, int
         acc.w += __uint_as_float(v[2 * s + 1].z);
       }
   }
+  return ok;
+}
+
+// SiLU's read of a gate|up tile: the gate partials of 4 columns (two words at p) and the
+// up partials (two words at p + 64) of `nseg` segments, every word polled together.
+__device__ __forceinline__ bool chain_sum_gate_up(const uint64_t* p, size_t stride, int nseg, float4& gs, float4& us,
+                                                  const LLWait& w, uint32_t site) {
+  constexpr int S = CHAIN_SILU_SEG;
+  uint4 v[4 * S];  // segment s: v[4 s + 0..1] gate, v[4 s + 2..3] up
+  auto addr = [&](int k) { return p + (k >> 2) * stride + ((k & 2) ? 64 : 0) + (k & 1) * 2; };
+  auto ready = [&](const uint4& x) { return x.y == w.flag && x.w == w.flag; };
+#pragma unroll
+  for (int k = 0; k < 4 * S; ++k)
+    if ((k >> 2) < nseg) v[k] = ll_ld16(addr(k));
+  uint64_t t0 = 0;
+  bool ok = true;
+  while (true) {
+    bool all = true;
+#pragma unroll
+    for (int k = 0; k < 4 * S; ++k)
+      if ((k >> 2) < nseg) all = all && ready(v[k]);
+    if (all) break;
+    if (*w.abort_flag) {
+      ok = false;
+      break;
+    }
+    const uint64_t now = globaltimer();
+    if (t0 == 0) {
+      t0 = now;
+    } else if (now - t0 > QASR_WAIT_NS) {
+      report_error(w.status, DEVERR_TIMEOUT, site);
+      *w.abort_flag = 1;
+      ok = false;
+      break;
+    }
+#pragma unroll
+    for (int k = 0; k < 4 * S; ++k)
+      if ((k >> 2) < nseg && !ready(v[k])) v[k] = ll_ld16(addr(k));
+  }
+  gs = make_float4(0.f, 0.f, 0.f, 0.f);
+  us = gs;
+#pragma unroll
+  for (int s = 0; s < S; ++s)
+    if (s < nseg) {
+      gs.x += __uint_as_float(v[4 * s].x);
+      gs.y += __uint_as_float(v[4 * s].z);
+      gs.z += __uint_as_float(v[4 * s + 1].x);
+      gs.w += __uint_as_float(v[4 * s + 1].z);
+      us.x += __uint_as_float(v[4 * s + 2].x);
+      us.y += __uint_as_float(v[4 * s + 2].z);
+      us.z += __uint_as_float(v[4 * s + 3].x);
+      us.w += __uint_as_float(v[4 * s + 3].z);
+    }
   return ok;
 }
 
@@ -605,9 +663,7 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
     }
   } else if (warp >= 4 && warp < 8) {
     // ------------------------------------------------------------ int8 A builders
-    // Each unit is published as soon as its TMEM stores land (tcgen05.wait::st is cheap);
-    // the row scale of the unit's tile is loaded before the unit's barrier waits so its
-    // latency overlaps them.
+    // Each unit is published as soon as its TMEM stores land (tcgen05.wait::st is cheap).
     const int t = (threadIdx.x - 128) & 127;  // row of the tile == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     int st = 0, ast = 0, i = 0;  // W stage, unit slot
@@ -617,6 +673,17 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
       const ChainGemm& g = a.gemms[gi];
       int ub, ue;
       chain_unit_range(g, blockIdx.x, ub, ue);
+      const bool f32s = g.scale32 != 0;
+      // the rows' scales of a tile: loaded one unit ahead of the tile's first unit, so the
+      // load's latency never stands between two units
+      auto load_scale = [&](int tile, __half& s16, float& s32) {
+        const int srow = tile * 128 + t;
+        s32 = f32s ? static_cast<const float*>(g.scale)[srow] : 1.0f;
+        s16 = f32s ? __float2half_rn(1.0f) : static_cast<const __half*>(g.scale)[srow];
+      };
+      __half sc = __float2half_rn(1.0f), nsc = sc;
+      float sc32 = 1.0f, nsc32 = 1.0f;
+      if (ub < ue) load_scale(ub / g.kblocks, sc, sc32);
       for (int u = ub; u < ue; ++u, ++i) {
         const int my_st = st, my_ast = ast;
         const uint32_t my_ph = ph, my_aph = aph;
@@ -628,10 +695,8 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
           ast = 0;
           aph ^= 1u;
         }
-        const bool f32s = g.scale32 != 0;
-        const int srow = (u / g.kblocks) * 128 + t;
-        const float sc32 = f32s ? static_cast<const float*>(g.scale)[srow] : 1.0f;
-        const __half sc = f32s ? __float2half_rn(1.0f) : static_cast<const __half*>(g.scale)[srow];
+        const bool next_tile = u + 1 < ue && (u + 1) % g.kblocks == 0;
+        if (next_tile) load_scale((u + 1) / g.kblocks, nsc, nsc32);
         if (!mbar_wait_warp(&wfull_bar[my_st], my_ph, &abort_flag, a.status, 0x731)) {
           ok = false;
           break;
@@ -653,16 +718,22 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&wfree_bar[my_st]);  // the W stage is read: refill it
         const uint32_t taddr = tmem_base + lane_base + A_COLS0 + static_cast<uint32_t>(my_ast) * 64u;
-        // one body per scale width: the choice is made once per unit, not per word
+        // one body per scale width: the choice is made once per unit, not per word.  Two
+        // 32-column stores per row: a tcgen05 instruction costs its warp ~130 cycles to
+        // issue whatever its width (measured on B200)
         auto build_row = [&](auto f32tag) {
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const uint32_t w4[4] = {chunk[c].x, chunk[c].y, chunk[c].z, chunk[c].w};
-            uint32_t outw[8];
+          for (int h = 0; h < 2; ++h) {
+            uint32_t outw[32];
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-              dequant_i8x4<decltype(f32tag)::value>(w4[q], sc2, sc32, outw[2 * q], outw[2 * q + 1]);
-            tmem_st_x8(taddr + static_cast<uint32_t>(c) * 8u, reinterpret_cast<const uint32_t(&)[8]>(outw));
+            for (int c = 0; c < 4; ++c) {
+              const uint4 ch = chunk[4 * h + c];
+              const uint32_t w4[4] = {ch.x, ch.y, ch.z, ch.w};
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+                dequant_i8x4<decltype(f32tag)::value>(w4[q], sc2, sc32, outw[8 * c + 2 * q], outw[8 * c + 2 * q + 1]);
+            }
+            tmem_st_x32(taddr + static_cast<uint32_t>(h) * 32u, outw);
           }
         };
         if (f32s) build_row(std::true_type{});
@@ -673,6 +744,10 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
         if (lane == 0) mbar_arrive(&ufull_bar[my_ast]);
         if (i < 24 && warp == 4 && lane == 0 && a.trace != nullptr)
           a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 72 + i] = globaltimer();
+        if (next_tile) {
+          sc = nsc;
+          sc32 = nsc32;
+        }
       }
     }
   } else if (warp >= EPI_WARP0) {
@@ -748,7 +823,10 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
 
     // grid barrier after operation oi (before a GEMM whose X tiles the producer copies with
     // TMA): release this CTA's writes (the group's, ordered by the named barrier), arrive,
-    // poll with relaxed loads, one acquire fence, then open GEMM next_gemm's X copies
+    // poll with acquire loads, then open GEMM next_gemm's X copies.  (Measured on B200: a
+    // release, or a fence.acq_rel, waits until every bulk copy the SM has in flight has
+    // landed, ~1.3 us while the weight ring streams; an acquire load costs what a relaxed
+    // load does, so the poll carries the acquire and no fence follows it.)
     auto grid_barrier = [&](int oi, int next_gemm) {
       named_bar_sync(1, CHAIN_EPI_THREADS);
       if (e == 0) {
@@ -756,9 +834,9 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
         ++nbar;
         asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.barrier) : "memory");
         const unsigned int target = static_cast<unsigned int>(nbar) * gridDim.x;
-        if (ld_relaxed_gpu(a.barrier) < target) {
+        if (ld_acquire_gpu(a.barrier) < target) {
           const uint64_t t0 = globaltimer();
-          while (ld_relaxed_gpu(a.barrier) < target) {
+          while (ld_acquire_gpu(a.barrier) < target) {
             if (abort_flag || globaltimer() - t0 > QASR_WAIT_NS) {
               if (!abort_flag) report_error(a.status, DEVERR_TIMEOUT, 0x761);
               abort_flag = 1;
@@ -766,7 +844,6 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
             }
           }
         }
-        asm volatile("fence.acq_rel.gpu;" ::: "memory");
         bar_ok = abort_flag ? 0 : 1;
         if (a.trace != nullptr) a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 2 + 2 * oi] = globaltimer();
         st_release_cta_shared(&xready, next_gemm + 1);
@@ -923,10 +1000,9 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
         const int r = rt / tiles, t = rt - r * tiles;
         const int nseg = chain_tile_segs(g, t);
         const uint64_t* p = chain_partial(a, g, t, r, 4 * c);
+        // per segment: the gate words (at p) and the up words (at p + 64), all polled together
         float4 gs, us;
-        bool lok = chain_sum4<CHAIN_SILU_SEG>(p, slot_u64, nseg, gs, llw, 0x755);
-        lok = chain_sum4<CHAIN_SILU_SEG>(p + 64, slot_u64, nseg, us, llw, 0x756) && lok;
-        if (!lok) break;
+        if (!chain_sum_gate_up(p, slot_u64, nseg, gs, us, llw, 0x755)) break;
         const float gv[4] = {gs.x, gs.y, gs.z, gs.w}, uv[4] = {us.x, us.y, us.z, us.w};
         float o[4];
 #pragma unroll
