@@ -534,8 +534,9 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
             const int kb = xu % g.kblocks;
             uint8_t* dst = xring + static_cast<size_t>(xst) * x_stage_bytes;
             mbar_arrive_expect_tx(&ufull_bar[xst], x_stage_bytes);
-            tma_load_2d(dst, tm, &ufull_bar[xst], kb * 128, 0);
-            tma_load_2d(dst + x_tile_bytes, tm, &ufull_bar[xst], kb * 128 + 64, 0);
+            // both 64-column halves in one copy (the map views X as {64, rows, K / 64}):
+            // the producer's copies queue behind the weight copies, so each one counts
+            tma_load_3d(dst, tm, &ufull_bar[xst], 0, 0, 2 * kb);
             ++xissued;
             if (++xst == SU) {
               xst = 0;

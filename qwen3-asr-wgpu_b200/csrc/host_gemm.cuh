@@ -59,6 +59,27 @@ inline bool make_tmap(CUtensorMap* m, const void* base, bool bytes1, uint64_t in
   return true;
 }
 
+// 2-D row-major tensor [outer, inner] viewed as 3-D {64, outer, inner / 64}: one box of
+// {64, box_outer, box_chunks} lands as box_chunks consecutive 128-byte swizzled [box_outer][64]
+// tiles, the layout two 2-D boxes at consecutive 64-column offsets would give.
+inline bool make_tmap_chunks(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                             uint32_t box_outer, uint32_t box_chunks, std::string* err) {
+  EncodeTiledFn fn = encode_fn(err);
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {64, outer, inner / 64};
+  const cuuint64_t strides[2] = {row_bytes, 128};
+  const cuuint32_t box[3] = {64, box_outer, box_chunks};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    if (err) *err = "cuTensorMapEncodeTiled (chunked view) failed (code " + std::to_string(static_cast<int>(r)) + ")";
+    return false;
+  }
+  return true;
+}
+
 // ----------------------------------------------------------------------------- GEMM plan
 struct Linear {
   void* w = nullptr;        // device, tiled layout (weight_tile_offset)

@@ -516,9 +516,9 @@ qasr_status launch_chain(qasr_ctx* c, const ChainArgs& a, const ChainShape& sh, 
   const int I = c->cfg.intermediate_size;
   CUtensorMap tx, ta, tact;
   const uint32_t box = static_cast<uint32_t>(sh.n_tile);
-  if (!make_tmap(&tx, c->x, false, hs, n, static_cast<uint64_t>(hs) * 2, 64, box, &c->err) ||
-      !make_tmap(&ta, c->attn, false, qd, n, static_cast<uint64_t>(qd) * 2, 64, box, &c->err) ||
-      !make_tmap(&tact, c->act, false, I, n, static_cast<uint64_t>(I) * 2, 64, box, &c->err))
+  if (!make_tmap_chunks(&tx, c->x, hs, n, static_cast<uint64_t>(hs) * 2, box, 2, &c->err) ||
+      !make_tmap_chunks(&ta, c->attn, qd, n, static_cast<uint64_t>(qd) * 2, box, 2, &c->err) ||
+      !make_tmap_chunks(&tact, c->act, I, n, static_cast<uint64_t>(I) * 2, box, 2, &c->err))
     return QASR_ERR_DEVICE;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(c->num_sms);
