@@ -53,7 +53,7 @@ FALLBACK_HBM_GBS = 6650.0
 CHAIN_TRAFFIC_BYTES = 55376384 + 1674496
 CHAIN_TRAFFIC_SOURCE = "ncu dram bytes of one middle launch of kernel_bench.py step --layers 2 (32 rows)"
 METRIC = "decode tokens/sec (box) 1.7B INT8 @1/2/4/8 B200; % HBM roofline"
-TRACED_STEPS = 8  # steps of the traced pass after the timed region (int8 chain configs)
+TRACED_STEPS = 8  # steps of the traced pass after the timed region (decode-chain configs)
 
 # model preset, weights, slots per GPU, prefix lengths, run length
 WORKLOADS = {
@@ -375,11 +375,12 @@ def run_audio(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
-def chain_timing(dec, cfg):
+def chain_timing(dec, cfg, int8=True):
     """The decode-chain kernel of the last timed step, from its in-kernel %globaltimer
     stamps: each launch's duration = last CTA exit - first CTA entry.  The middle
-    launches (o_proj of layer l through the QKV of layer l+1) all move one layer's int8
-    weights; their mean duration and those bytes give the kernel's roofline point."""
+    launches (o_proj of layer l through the QKV of layer l+1) all move one layer's
+    weights (int8 + f16 scales, or f16); their mean duration and those bytes give the
+    kernel's roofline point."""
     try:
         tr = dec.read_trace().astype(np.float64)
     except Exception:
@@ -389,9 +390,9 @@ def chain_timing(dec, cfg):
     hs, I = cfg["hidden_size"], cfg["intermediate_size"]
     qd = cfg["num_attention_heads"] * cfg["head_dim"]
     kvd = cfg["num_key_value_heads"] * cfg["head_dim"]
-    lin = (qd + 2 * kvd) * hs + hs * qd + 2 * I * hs + hs * I  # int8 weight bytes of one layer
-    rows = (qd + 2 * kvd) + hs + 2 * I + hs                    # f16 scales
-    nbytes = lin + 2 * rows
+    lin = (qd + 2 * kvd) * hs + hs * qd + 2 * I * hs + hs * I  # weights of one layer
+    rows = (qd + 2 * kvd) + hs + 2 * I + hs                    # their rows (one f16 scale each, int8)
+    nbytes = lin + 2 * rows if int8 else 2 * lin
     t = float(np.mean(durs))
     return {"seconds": t, "bytes": nbytes, "gbs": nbytes / t / 1e9, "launches_per_step": L + 1,
             "share_of_step": None,
@@ -516,12 +517,11 @@ def run_decode(args, rank, world, local):
     int8 = wl["int8"]
     model = pkg.SyntheticModel(cfg, seed=SEED)
     rng = np.random.default_rng(SEED + 7919 * rank + 104729 * args.config)
-    # trace=True (int8: the decode-chain path) allocates the stamp buffers; the timed steps run
-    # with the stamps off, a separate traced pass after them gives the chain kernel's duration
+    # trace=True allocates the decode chain's stamp buffers; the timed steps run with the
+    # stamps off, a separate traced pass after them gives the chain kernel's duration
     dec = pkg.TextDecoder(cfg, weight_format=pkg.WEIGHTS_INT8 if int8 else pkg.WEIGHTS_F16, max_slots=slots_n,
-                          max_seq=wl["max_seq"], device=local, trace=int8)
-    if int8:
-        dec.set_trace(False)
+                          max_seq=wl["max_seq"], device=local, trace=True)
+    dec.set_trace(False)
     t_load = time.perf_counter()
     dec.load_model(model)
     cos, sin = pkg.build_rope_tables(wl["max_seq"])
@@ -634,7 +634,7 @@ def run_decode(args, rank, world, local):
     # ---- traced pass (not timed for the metric): the chain kernel's own launch durations,
     # and the step time with the stamps on beside the untraced one (their cost)
     chain, traced = None, []
-    if int8:
+    if slots_n <= 128:  # the decode-chain path (int8 or f16 weights, at most 128 rows)
         dec.set_trace(True)
         for it in range(3 + TRACED_STEPS):
             between_steps()
@@ -647,7 +647,7 @@ def run_decode(args, rank, world, local):
                 traced.append(a.elapsed_time(b) * 1e-3)
             for i in range(slots_n):
                 kv_len[i] += 1
-        chain = chain_timing(dec, cfg)
+        chain = chain_timing(dec, cfg, int8)
         dec.set_trace(False)
 
     # ---- dominant kernels, timed alone at the workload's shapes
@@ -669,7 +669,7 @@ def run_decode(args, rank, world, local):
             chain["traced_step_ms"] = statistics.median(traced) * 1e3
             chain["untraced_step_ms"] = ms_step
             kernels["decode_chain"] = chain
-            dom_name = "decode_chain"  # the largest share of the int8 step
+            dom_name = "decode_chain"  # the largest share of the step
             if args.config == 4:
                 traffic, traffic_src = CHAIN_TRAFFIC_BYTES, CHAIN_TRAFFIC_SOURCE
         else:

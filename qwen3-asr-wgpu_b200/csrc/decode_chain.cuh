@@ -34,9 +34,13 @@
 // Roles (512 threads):
 //   warp 0      producer: 16 KB bulk copy per weight unit into the W ring, and the TMA of
 //               each unit's X tile once its GEMM's input is ready
-//   warps 1-3   UMMA issuers (A from TMEM, B = X from shared memory), k-steps split
-//               round-robin over them; warp 2 also allocates the TMEM
-//   warps 4-7   int8 A builders: f16(q * s) into TMEM
+//   warps 1-3   UMMA issuers (int8 weights: A from TMEM; f16 weights: A straight from the
+//               W ring), B = X from shared memory, units dealt round-robin over them;
+//               warp 2 also allocates the TMEM
+//   warps 4-7   int8 A builders: f16(q * s) into TMEM (idle with f16 weights)
+//
+// Weight formats (template parameter F16): a weight unit is always one 16 KB tile of 128
+// rows x 128 bytes in the tiled layout (weight_tile_offset): 128 k of int8 or 64 k of f16.
 //   warps 8-15  epilogue (two warps per TMEM lane quadrant, splitting the accumulator
 //               columns) and row operations; they also run the grid barriers
 #pragma once
@@ -396,11 +400,11 @@ __device__ __forceinline__ float chain_group_sum(float v, float* red, int e) {
   return t;
 }
 
-template <int PROG>
+template <int PROG, bool F16>
 __global__ void __launch_bounds__(CHAIN_THREADS, 1)
     decode_chain_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_attn,
                         const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ ChainArgs a) {
-  constexpr int KSTEPS = 8;  // 128 k elements per unit, UMMA K = 16
+  constexpr int KSTEPS = F16 ? 4 : 8;  // k elements per unit (64 f16 or 128 int8) / UMMA K (16)
   constexpr int EPI_WARP0 = 16 - CHAIN_EPI_WARPS;
   extern __shared__ __align__(1024) uint8_t chain_dsmem[];
   __shared__ __align__(8) uint64_t wfull_bar[CHAIN_MAX_W_STAGES], wfree_bar[CHAIN_MAX_W_STAGES];
@@ -419,7 +423,7 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(chain_dsmem) + 1023) & ~uintptr_t(1023));
   const int SW = a.w_stages, SU = a.a_stages;  // W stages, unit slots
   const uint32_t x_tile_bytes = static_cast<uint32_t>(a.n_tile) * 128u;
-  const uint32_t x_stage_bytes = 2u * x_tile_bytes;
+  const uint32_t x_stage_bytes = F16 ? x_tile_bytes : 2u * x_tile_bytes;  // 64 or 128 k
   uint8_t* xring = smem + static_cast<size_t>(SW) * 16384;
   // TMEM columns: two accumulator buffers (double-buffered segments), each split into
   // NACC accumulators (one per MMA issuer warp) that the epilogue adds in index order;
@@ -435,10 +439,11 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
     if (a.trace != nullptr) a.trace[blockIdx.x * CHAIN_TRACE_SLOTS] = globaltimer();
     for (int i = 0; i < SW; ++i) {
       mbar_init(&wfull_bar[i], 1);
-      mbar_init(&wfree_bar[i], 4);
+      mbar_init(&wfree_bar[i], F16 ? 1 : 4);  // the unit's MMA commit, or the 4 builder warps
     }
     for (int i = 0; i < SU; ++i) {
-      mbar_init(&ufull_bar[i], 5);  // 4 builder warps + the X copy's expect_tx arrival
+      // 4 builder warps + the X copy's expect_tx arrival (f16: the X copy alone)
+      mbar_init(&ufull_bar[i], F16 ? 1 : 5);
       mbar_init(&ufree_bar[i], 1);  // the commit of the issuer that took the unit
     }
     for (int i = 0; i < 2; ++i) {
@@ -536,7 +541,7 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
             mbar_arrive_expect_tx(&ufull_bar[xst], x_stage_bytes);
             // both 64-column halves in one copy (the map views X as {64, rows, K / 64}):
             // the producer's copies queue behind the weight copies, so each one counts
-            tma_load_3d(dst, tm, &ufull_bar[xst], 0, 0, 2 * kb);
+            tma_load_3d(dst, tm, &ufull_bar[xst], 0, 0, F16 ? kb : 2 * kb);
             ++xissued;
             if (++xst == SU) {
               xst = 0;
@@ -601,18 +606,23 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
     if (lane == 0 && j < NACC) {
       const uint32_t idesc = umma_idesc_f16_m128(static_cast<uint32_t>(a.n_tile));
       int us = 0, seg = -1, d = 0, i = 0, seg_i0 = 0;
-      uint32_t uph = 0;
+      int wst = 0;  // f16: the unit's W stage (the producer fills the ring in unit order)
+      uint32_t uph = 0, wph = 0;
       bool ok = true, started = false;
       for (int gi = 0; gi < n_gemm_ops && ok; ++gi) {
         const ChainGemm& g = a.gemms[gi];
         int ub, ue;
         chain_unit_range(g, blockIdx.x, ub, ue);
         for (int u = ub; u < ue; ++u, ++i) {
-          const int my_us = us;
-          const uint32_t my_uph = uph;
+          const int my_us = us, my_wst = wst;
+          const uint32_t my_uph = uph, my_wph = wph;
           if (++us == SU) {
             us = 0;
             uph ^= 1u;
+          }
+          if (++wst == SW) {
+            wst = 0;
+            wph ^= 1u;
           }
           const int kb = u % g.kblocks;
           const bool first = (u == ub) || (kb == 0);
@@ -630,24 +640,36 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
             tc_fence_after();
           }
           if ((i - seg_i0) % NACC == j) {
-            if (!mbar_wait(&ufull_bar[my_us], my_uph, &abort_flag, a.status, 0x722)) {
+            if (!mbar_wait(&ufull_bar[my_us], my_uph, &abort_flag, a.status, 0x722) ||
+                (F16 && !mbar_wait(&wfull_bar[my_wst], my_wph, &abort_flag, a.status, 0x726))) {
               ok = false;
               break;
             }
             tc_fence_after();
             if (a.trace != nullptr && i < 24) a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 40 + i] = globaltimer();
             const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(d) * DCOLS + static_cast<uint32_t>(j) * DSTR;
-            const uint32_t a_tmem = tmem_base + A_COLS0 + static_cast<uint32_t>(my_us) * 64u;
             const uint32_t x_base = smem_u32(xring + static_cast<size_t>(my_us) * x_stage_bytes);
+            if constexpr (F16) {
+              // A = the weight tile itself (128 rows x 64 k, 128-byte swizzled rows)
+              const uint32_t w_base = smem_u32(smem + static_cast<size_t>(my_wst) * 16384);
 #pragma unroll
-            for (int kk = 0; kk < KSTEPS; ++kk) {
-              const uint32_t b_addr = x_base + static_cast<uint32_t>(kk >> 2) * x_tile_bytes +
-                                      static_cast<uint32_t>(kk & 3) * 32u;
-              umma_f16_ts(d_tmem, a_tmem + static_cast<uint32_t>(kk) * 8u, smem_desc_sw128(b_addr), idesc,
-                          (!started && kk == 0) ? 0u : 1u);
+              for (int kk = 0; kk < KSTEPS; ++kk)
+                umma_f16_ss(d_tmem, smem_desc_sw128(w_base + static_cast<uint32_t>(kk) * 32u),
+                            smem_desc_sw128(x_base + static_cast<uint32_t>(kk) * 32u), idesc,
+                            (!started && kk == 0) ? 0u : 1u);
+            } else {
+              const uint32_t a_tmem = tmem_base + A_COLS0 + static_cast<uint32_t>(my_us) * 64u;
+#pragma unroll
+              for (int kk = 0; kk < KSTEPS; ++kk) {
+                const uint32_t b_addr = x_base + static_cast<uint32_t>(kk >> 2) * x_tile_bytes +
+                                        static_cast<uint32_t>(kk & 3) * 32u;
+                umma_f16_ts(d_tmem, a_tmem + static_cast<uint32_t>(kk) * 8u, smem_desc_sw128(b_addr), idesc,
+                            (!started && kk == 0) ? 0u : 1u);
+              }
             }
             started = true;
             umma_commit(&ufree_bar[my_us]);
+            if constexpr (F16) umma_commit(&wfree_bar[my_wst]);  // the W stage is read
             if (a.trace != nullptr) {
               const unsigned long long now = globaltimer();
               if (u == ub) a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 29 + gi] = now;
@@ -662,7 +684,7 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
       umma_commit(&done_bar);
       mbar_wait(&done_bar, 0, nullptr, a.status, 0x724);
     }
-  } else if (warp >= 4 && warp < 8) {
+  } else if (!F16 && warp >= 4 && warp < 8) {
     // ------------------------------------------------------------ int8 A builders
     // Each unit is published as soon as its TMEM stores land (tcgen05.wait::st is cheap).
     const int t = (threadIdx.x - 128) & 127;  // row of the tile == TMEM lane

@@ -76,15 +76,17 @@ cudaError_t init_kernel_attrs(std::string* err) {
     e = e ? e : cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(attn_smem_bytes(ATTN_MAX_ROWS)));
     cudaFuncAttributes fc{};
-    e = e ? e : cudaFuncGetAttributes(&fc, decode_chain_kernel<CHAIN_PROG_MIDDLE>);
+    e = e ? e : cudaFuncGetAttributes(&fc, decode_chain_kernel<CHAIN_PROG_MIDDLE, false>);
     if (e == cudaSuccess) {
       g_chain_dyn_max = optin - static_cast<int>(fc.sharedSizeBytes) - 256;
-      e = cudaFuncSetAttribute(decode_chain_kernel<CHAIN_PROG_FIRST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               g_chain_dyn_max);
-      e = e ? e : cudaFuncSetAttribute(decode_chain_kernel<CHAIN_PROG_MIDDLE>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, g_chain_dyn_max);
-      e = e ? e : cudaFuncSetAttribute(decode_chain_kernel<CHAIN_PROG_LAST>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, g_chain_dyn_max);
+      const int cd = g_chain_dyn_max;
+      const auto attr = cudaFuncAttributeMaxDynamicSharedMemorySize;
+      e = cudaFuncSetAttribute(decode_chain_kernel<CHAIN_PROG_FIRST, false>, attr, cd);
+      e = e ? e : cudaFuncSetAttribute(decode_chain_kernel<CHAIN_PROG_MIDDLE, false>, attr, cd);
+      e = e ? e : cudaFuncSetAttribute(decode_chain_kernel<CHAIN_PROG_LAST, false>, attr, cd);
+      e = e ? e : cudaFuncSetAttribute(decode_chain_kernel<CHAIN_PROG_FIRST, true>, attr, cd);
+      e = e ? e : cudaFuncSetAttribute(decode_chain_kernel<CHAIN_PROG_MIDDLE, true>, attr, cd);
+      e = e ? e : cudaFuncSetAttribute(decode_chain_kernel<CHAIN_PROG_LAST, true>, attr, cd);
     }
     result = e;
   });
@@ -101,7 +103,9 @@ struct ChainShape {
   size_t smem;
 };
 
-static ChainShape chain_shape(int rows) {
+// `f16`: f16 weights, whose unit (one 16 KB tile) covers 64 k, so an X stage is one
+// 64-column tile; int8 units cover 128 k (two X tiles).
+static ChainShape chain_shape(int rows, bool f16) {
   ChainShape s{};
   s.n_tile = std::max(16, (rows + 15) / 16 * 16);
   const int dstr = (s.n_tile + 31) / 32 * 32;  // TMEM columns of one accumulator
@@ -115,7 +119,7 @@ static ChainShape chain_shape(int rows) {
   // columns the CTA allocates: n_acc falls as the tile widens (at most 128 rows: 2 x 128 +
   // 4 x 64 = 512)
   static_assert(2 * CHAIN_MAX_ROWS + 64 <= static_cast<int>(GEMM_TMEM_COLS), "chain TMEM budget");
-  const int xstage = 2 * s.n_tile * 128;
+  const int xstage = (f16 ? 1 : 2) * s.n_tile * 128;
   const int dyn = g_chain_dyn_max > 0 ? g_chain_dyn_max : 200 * 1024;
   s.w_stages = std::min(CHAIN_MAX_W_STAGES, (dyn - 1024 - s.a_stages * xstage) / 16384);
   s.smem = 1024 + static_cast<size_t>(s.w_stages) * 16384 + static_cast<size_t>(s.a_stages) * xstage;
@@ -128,16 +132,16 @@ static int chain_seg_cap(int kind) {
   return kind == 0 ? CHAIN_QKV_SEG : (kind == 2 ? CHAIN_SILU_SEG : CHAIN_MAX_SEG);
 }
 
-// int8 GEMM of the chain: at least two units (32 KB of weights) per taking-part CTA, and
-// few enough taking-part CTAs that no tile is cut into more than `max_seg_cap` segments
-// (the bound of the operation that adds the partials).
+// GEMM of the chain (int8, or f16 when `f16`): at least two units (32 KB of weights) per
+// taking-part CTA, and few enough taking-part CTAs that no tile is cut into more than
+// `max_seg_cap` segments (the bound of the operation that adds the partials).
 static ChainGemm chain_gemm_plan(const uint8_t* w, const void* scale, bool scale32, int n_out, int k, int xmap,
-                                 int sms, int max_seg_cap) {
+                                 int sms, int max_seg_cap, bool f16) {
   ChainGemm g{};
   g.w = w;
   g.scale = scale;
   g.scale32 = scale32 ? 1 : 0;
-  g.kblocks = k / 128;
+  g.kblocks = k / (f16 ? 64 : 128);
   g.units = (n_out / 128) * g.kblocks;
   for (g.grid = std::max(1, std::min(sms, g.units / 2));; --g.grid) {
     int ms = 1;
@@ -240,6 +244,7 @@ struct qasr_ctx {
   unsigned long long* attn_trace = nullptr;  // QASR_FLAG_TRACE: [L][sms][ATTN_TRACE_SLOTS]
   // decode chain (int8 weights, <= CHAIN_MAX_ROWS rows): partial sums and barrier counters
   bool chain_ok = false;
+  bool chain_f16 = false;  // the chain runs the f16-weight kernels
   bool chain_pdl = false;  // per-layer chain launches start while the attention drains (PDL)
   int chain_wcap = 3;      // weight copies in flight per chain CTA (QASR_B200_CHAIN_WCAP overrides)
   uint64_t* chain_ws[4] = {};  // flagged partial sums of the chain's QKV, o_proj, gate|up, down GEMMs
@@ -501,7 +506,7 @@ qasr_status enqueue_decode(qasr_ctx* c, int n, uint64_t* nk) {
 // on it instead of the cooperative attribute's check).
 static bool chain_one_cta_per_sm(size_t smem) {
   int blocks = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, decode_chain_kernel<CHAIN_PROG_MIDDLE>, CHAIN_THREADS,
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, decode_chain_kernel<CHAIN_PROG_MIDDLE, false>, CHAIN_THREADS,
                                                     smem) != cudaSuccess) {
     cudaGetLastError();
     return false;
@@ -516,9 +521,10 @@ qasr_status launch_chain(qasr_ctx* c, const ChainArgs& a, const ChainShape& sh, 
   const int I = c->cfg.intermediate_size;
   CUtensorMap tx, ta, tact;
   const uint32_t box = static_cast<uint32_t>(sh.n_tile);
-  if (!make_tmap_chunks(&tx, c->x, hs, n, static_cast<uint64_t>(hs) * 2, box, 2, &c->err) ||
-      !make_tmap_chunks(&ta, c->attn, qd, n, static_cast<uint64_t>(qd) * 2, box, 2, &c->err) ||
-      !make_tmap_chunks(&tact, c->act, I, n, static_cast<uint64_t>(I) * 2, box, 2, &c->err))
+  const uint32_t nch = c->chain_f16 ? 1u : 2u;  // 64-column tiles per unit
+  if (!make_tmap_chunks(&tx, c->x, hs, n, static_cast<uint64_t>(hs) * 2, box, nch, &c->err) ||
+      !make_tmap_chunks(&ta, c->attn, qd, n, static_cast<uint64_t>(qd) * 2, box, nch, &c->err) ||
+      !make_tmap_chunks(&tact, c->act, I, n, static_cast<uint64_t>(I) * 2, box, nch, &c->err))
     return QASR_ERR_DEVICE;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(c->num_sms);
@@ -543,10 +549,14 @@ qasr_status launch_chain(qasr_ctx* c, const ChainArgs& a, const ChainShape& sh, 
   cfg.numAttrs = 1;
   g_launches.fetch_add(1, std::memory_order_relaxed);
   cudaError_t e = cudaErrorInvalidValue;
-  if (prog == CHAIN_PROG_FIRST) e = cudaLaunchKernelEx(&cfg, decode_chain_kernel<CHAIN_PROG_FIRST>, tx, ta, tact, a);
+#define QASR_CHAIN_LAUNCH(P)                                                                    \
+  (c->chain_f16 ? cudaLaunchKernelEx(&cfg, decode_chain_kernel<P, true>, tx, ta, tact, a)       \
+                : cudaLaunchKernelEx(&cfg, decode_chain_kernel<P, false>, tx, ta, tact, a))
+  if (prog == CHAIN_PROG_FIRST) e = QASR_CHAIN_LAUNCH(CHAIN_PROG_FIRST);
   else if (prog == CHAIN_PROG_MIDDLE)
-    e = cudaLaunchKernelEx(&cfg, decode_chain_kernel<CHAIN_PROG_MIDDLE>, tx, ta, tact, a);
-  else if (prog == CHAIN_PROG_LAST) e = cudaLaunchKernelEx(&cfg, decode_chain_kernel<CHAIN_PROG_LAST>, tx, ta, tact, a);
+    e = QASR_CHAIN_LAUNCH(CHAIN_PROG_MIDDLE);
+  else if (prog == CHAIN_PROG_LAST) e = QASR_CHAIN_LAUNCH(CHAIN_PROG_LAST);
+#undef QASR_CHAIN_LAUNCH
   CK(e, "decode chain launch");
   return QASR_OK;
 }
@@ -555,7 +565,7 @@ qasr_status launch_chain(qasr_ctx* c, const ChainArgs& a, const ChainShape& sh, 
 // layer attention + merge + chain (o_proj ... next layer's QKV, or the final norm),
 // then lm_head + argmax.
 qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
-  const ChainShape sh = chain_shape(n);
+  const ChainShape sh = chain_shape(n, c->chain_f16);
   const int L = c->cfg.num_hidden_layers, hs = c->cfg.hidden_size, I = c->cfg.intermediate_size;
   const int nq = c->cfg.num_attention_heads, nkv = c->cfg.num_key_value_heads;
   const int qd = nq * c->cfg.head_dim, qkv_out = qd + 2 * nkv * 128;
@@ -598,7 +608,7 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
   base.status = c->status;
   auto gemm = [&](const Linear& lin, int xmap, int kind) {
     ChainGemm g = chain_gemm_plan(static_cast<const uint8_t*>(lin.w), lin.scale, lin.scale32, lin.n_out, lin.k, xmap, sms,
-                                  chain_seg_cap(kind));
+                                  chain_seg_cap(kind), c->chain_f16);
     g.ws = c->chain_ws[kind];
     return g;
   };
@@ -902,19 +912,21 @@ qasr_status qasr_create(const qasr_text_config* cfg, const qasr_options* opts, i
   const size_t apart = R * t.num_key_value_heads * ATTN_ROW_CHUNKS * ATTN_PART_FLOATS;
   if ((s = dalloc(c, &c->attn_ws, apart, "attention workspace")))
     return s;
-  // The int8 decode step runs as persistent chain launches when its shapes fit them.
+  // The decode step runs as persistent chain launches when its shapes fit them (int8 or
+  // f16 weights).
   const char* no_chain = std::getenv("QASR_B200_NO_CHAIN");
-  c->chain_ok = i8 && hs <= CHAIN_MAX_HS && hs % (2 * CHAIN_EPI_THREADS) == 0 && I % 64 == 0 &&
+  c->chain_f16 = !i8;
+  c->chain_ok = hs <= CHAIN_MAX_HS && hs % (2 * CHAIN_EPI_THREADS) == 0 && I % 128 == 0 &&
                 !(no_chain && no_chain[0] == '1');
   if (c->chain_ok) {
     if (const char* wc = std::getenv("QASR_B200_CHAIN_WCAP")) c->chain_wcap = std::max(1, std::atoi(wc));
     const char* no_cpdl = std::getenv("QASR_B200_NO_CHAIN_PDL");
     c->chain_pdl = pdl_enabled() && !(no_cpdl && no_cpdl[0] == '1') &&
-                   chain_one_cta_per_sm(chain_shape(std::min(opts->max_slots, CHAIN_MAX_ROWS)).smem);
-    c->chain_ws_rows = chain_shape(std::min(opts->max_slots, CHAIN_MAX_ROWS)).n_tile;
+                   chain_one_cta_per_sm(chain_shape(std::min(opts->max_slots, CHAIN_MAX_ROWS), c->chain_f16).smem);
+    c->chain_ws_rows = chain_shape(std::min(opts->max_slots, CHAIN_MAX_ROWS), c->chain_f16).n_tile;
     for (int i = 0; i < 4; ++i) {  // shapes[] order: QKV, o_proj, gate|up, down
       const ChainGemm g = chain_gemm_plan(nullptr, nullptr, false, shapes[i][0], shapes[i][1], 0, c->num_sms,
-                                          chain_seg_cap(i));
+                                          chain_seg_cap(i), c->chain_f16);
       if (2ull * static_cast<unsigned long long>(g.units) * static_cast<unsigned long long>(g.grid) >= (1ull << 32))
         return fail(c, QASR_ERR_CAPACITY, "decode chain GEMM: too many units for 32-bit unit maps");
       c->chain_ws_n[i] = static_cast<size_t>(shapes[i][0] / 128) * g.max_seg * chain_slot_words(c->chain_ws_rows);

@@ -39,16 +39,17 @@ def _setup(qasr, oracle, cfg, int8, slots, max_seq=2048, seed=1234):
 
 
 def _run_parity(qasr, oracle, cfg, int8, n_audio, steps, n_slots=1, check_slots=None, n_text=24,
-                max_seq=2048, floor=False):
-    """Teacher-forced parity run.  floor=True also replays the checked slots through the
-    oracle with every f32 sum reversed (oracle.set_sum_order(1)): the same arithmetic in
-    another valid order; the largest logit difference between the two oracle runs is the
-    model's own order-sensitivity floor, and the returned tolerance becomes
-    max(tol, 2 * floor)."""
+                max_seq=2048, floor=False, seed=1234):
+    """Teacher-forced parity run; returns (worst |dlogit|, report, tolerance, floor).
+    floor=True also replays the checked slots through the oracle with every f32 sum
+    reversed (oracle.set_sum_order(1)): the same arithmetic in another valid order; the
+    largest logit difference between the two oracle runs is the model's own
+    order-sensitivity floor, and the returned tolerance becomes max(tol, 2 * floor)
+    (floor 0.0 when not measured)."""
     from oracle import oracle as oracle_mod
     from oracle.oracle import OracleSeq
     tol = INT8_TOL if int8 else F16_TOL
-    model, dec, om = _setup(qasr, oracle, cfg, int8, n_slots, max_seq=max_seq)
+    model, dec, om = _setup(qasr, oracle, cfg, int8, n_slots, max_seq=max_seq, seed=seed)
     check_slots = list(range(n_slots)) if check_slots is None else check_slots
     prefixes = [model.prefix(s, n_audio[s % len(n_audio)], n_text=n_text)[0] for s in range(n_slots)]
     slots = [dec.fork_capped(p.shape[0] + steps + 8) for p in prefixes]
@@ -96,8 +97,8 @@ def _run_parity(qasr, oracle, cfg, int8, n_audio, steps, n_slots=1, check_slots=
         worst = max(worst, step_worst)
     dec.close()
     print("max |dlogit| per step (0 = prefill): " + " ".join(f"{w:.3g}" for w in per_step))
+    fl = 0.0
     if floor:
-        fl = 0.0
         oracle_mod.set_sum_order(1)
         try:
             for i in check_slots:
@@ -115,18 +116,23 @@ def _run_parity(qasr, oracle, cfg, int8, n_audio, steps, n_slots=1, check_slots=
               f"tolerance max({tol}, 2 x floor) = {max(tol, 2 * fl):.3g}")
         tol = max(tol, 2.0 * fl)
     om.close()
-    return worst, report, tol
+    return worst, report, tol, fl
 
 
-def _check(worst, report, tol, allow_near_ties=False):
-    """report rows: (step, slot, gpu id, oracle id, oracle logit gap between them)."""
+def _check(worst, report, tol, floor=0.0, allow_near_ties=False):
+    """report rows: (step, slot, gpu id, oracle id, oracle logit gap between them).
+    Greedy ids must be identical, except where the oracle's own gap between the two ids
+    is below its measured order-sensitivity floor (`floor`: the reference itself, with its
+    sums merely reordered, cannot separate them there) — and, for the near-tie studies,
+    within twice the observed logit error."""
     flips = [r for r in report if r[2] != r[3]]
     agree = 1.0 - len(flips) / len(report)
     print(f"teacher-forced max |dlogit| {worst:.3g}; greedy agreement {agree:.3%} "
           f"({len(report) - len(flips)}/{len(report)}); flips (step, slot, gpu, oracle, gap) {flips}")
     assert worst <= tol, f"teacher-forced max |dlogit| {worst:.4g} > {tol}"
     if not allow_near_ties:
-        assert not flips, f"greedy ids differ from the oracle's: {flips}"
+        bad = [r for r in flips if r[4] > floor]
+        assert not bad, f"greedy ids differ from the oracle's (oracle floor {floor:.3g}): {bad}"
         return
     # near-tie study: a flipped id is only acceptable where the oracle itself cannot
     # separate the two tokens by more than twice the observed logit error
@@ -250,18 +256,19 @@ def test_graph_replay_equals_eager(qasr, cuda_device, int8):
     assert runs[0] == runs[1]
 
 
-def test_decode_chain_matches_per_kernel_path(qasr, cuda_device, monkeypatch):
+@pytest.mark.parametrize("int8", [True, False], ids=["int8", "f16"])
+def test_decode_chain_matches_per_kernel_path(qasr, cuda_device, monkeypatch, int8):
     """The persistent decode-chain launches and the per-kernel launches compute the same
-    step (they differ only in f32 summation order): logits within the INT8 tolerance of
-    each other over 1.7B-shaped layers with 20 slots."""
+    step (they differ only in f32 summation order): logits within the weights' tolerance
+    of each other over 1.7B-shaped layers with 20 slots, int8 or f16 weights."""
     cfg = qasr.text_config("1.7b", num_hidden_layers=3)
     model = qasr.SyntheticModel(cfg, seed=31)
     cos, sin = qasr.build_rope_tables(512)
     logits, toks = [], []
     for no_chain in ("0", "1"):
         monkeypatch.setenv("QASR_B200_NO_CHAIN", no_chain)
-        dec = qasr.TextDecoder(cfg, weight_format=qasr.WEIGHTS_INT8, max_slots=20, max_seq=512,
-                               keep_logits=True)
+        dec = qasr.TextDecoder(cfg, weight_format=qasr.WEIGHTS_INT8 if int8 else qasr.WEIGHTS_F16, max_slots=20,
+                               max_seq=512, keep_logits=True)
         dec.load_model(model)
         dec.set_rope_tables(cos, sin)
         slots = [dec.fork_capped(400) for _ in range(20)]
@@ -276,7 +283,7 @@ def test_decode_chain_matches_per_kernel_path(qasr, cuda_device, monkeypatch):
         dec.close()
     err = float(np.max(np.abs(logits[0] - logits[1])))
     print(f"chain vs per-kernel: max |dlogit| {err:.3g}, ids equal {np.mean(toks[0] == toks[1]):.3f}")
-    assert err <= INT8_TOL
+    assert err <= (INT8_TOL if int8 else F16_TOL)
     assert np.mean(toks[0] == toks[1]) >= 0.9
 
 
@@ -303,9 +310,12 @@ def test_errors_are_status_codes(qasr, cuda_device):
 
 @pytest.mark.slow
 def test_config1_shape_matches_oracle(qasr, cuda_device, oracle):
-    """Config 1 shape: 0.6B f16, 28 layers, prefix 9 + 200 audio + 15 ids, 64 decode steps."""
+    """Config 1 shape: 0.6B f16, 28 layers, prefix 9 + 200 audio + 15 ids, 64 decode steps.
+    This seed's step 1 has an oracle top-2 margin of 0.00049, ten times below the model's
+    own order-sensitivity floor (~0.005, measured here): a flip is accepted there and only
+    there."""
     cfg = qasr.text_config("0.6b")
-    _check(*_run_parity(qasr, oracle, cfg, False, n_audio=[200], steps=64))
+    _check(*_run_parity(qasr, oracle, cfg, False, n_audio=[200], steps=64, floor=True))
 
 
 @pytest.mark.slow

@@ -4,7 +4,8 @@ B200 against the CPU oracle (the restated CpuTextDecoder, src/cpu_decoder.rs).
 
 * cfg4 shape: Qwen3-ASR-1.7B, INT8 weights, 28 layers, 32 slots with KV lengths of a few
   hundred to ~1500 — the decode-chain path bench.py measures; three slots checked.
-* cfg3 shape: 1.7B, f16 weights, 28 layers, 64 slots — the per-kernel path; two checked.
+* cfg3 shape: 1.7B, f16 weights, 28 layers, 64 slots — the decode chain's f16 kernels;
+  two checked.
 * cfg1 free-running: 0.6B f16, 28 layers, one slot, 224-row prefix, 64 greedy steps with
   no teacher forcing: the id streams must be identical (the reference's own identity
   design, src/bin/batch_step_bench.rs:60-170).
@@ -15,6 +16,8 @@ import pytest
 from test_gpu_decoder import F16_TOL, INT8_TOL, _check, _run_parity, _setup
 
 pytestmark = pytest.mark.gpu
+
+CFG1_FREE_SEED = 2024  # weights seed of the free-running cfg1 case (well-conditioned, see its test)
 
 
 @pytest.mark.slow
@@ -32,7 +35,7 @@ def test_cfg4_shape_int8_chain_matches_oracle(qasr, cuda_device, oracle):
 
 @pytest.mark.slow
 def test_cfg3_shape_f16_matches_oracle(qasr, cuda_device, oracle):
-    """1.7B f16 weights (the per-kernel GEMM path), 64 slots with prefixes of 200-800
+    """1.7B f16 weights (the decode chain's f16 kernels), 64 slots with prefixes of 200-800
     rows; slots 5 and 50 checked teacher-forced for 16 steps, ids identical.  Logits within
     max(2e-2, 2 x the oracle's own order-sensitivity floor): this model's logits move by
     ~0.015-0.018 when the reference's f32 sums are merely reordered (measured by the same
@@ -50,10 +53,13 @@ def test_cfg1_free_running_greedy_is_identical(qasr, cuda_device, oracle):
     """Config 1: 0.6B f16, 28 layers, prefix 9 ids + 200 audio rows + 15 ids, then 64
     greedy steps where each side feeds back its own argmax.  The two id streams must be
     identical; on a mismatch the first divergent step and the oracle's top-2 margin there
-    are reported."""
+    are reported.  Weights seed CFG1_FREE_SEED: every step's oracle top-2 margin is >= 0.042
+    (asserted), so the streams are determined by the reference's arithmetic and not by
+    its summation order (the default seed has a step with margin 0.00049, below the
+    order-sensitivity floor, where any valid reordering may pick either token)."""
     from oracle.oracle import OracleSeq
     cfg = qasr.text_config("0.6b")
-    model, dec, om = _setup(qasr, oracle, cfg, False, 1, max_seq=512)
+    model, dec, om = _setup(qasr, oracle, cfg, False, 1, max_seq=512, seed=CFG1_FREE_SEED)
     hidden, _ = model.prefix(0, 200)
     assert hidden.shape[0] == 224
     slot = dec.fork_capped(hidden.shape[0] + 64 + 8)
@@ -74,6 +80,9 @@ def test_cfg1_free_running_greedy_is_identical(qasr, cuda_device, oracle):
     diff = [i for i in range(len(o_ids)) if g_ids[i] != o_ids[i]]
     print(f"free-running cfg1: {len(o_ids) - len(diff)}/{len(o_ids)} ids identical; smallest oracle "
           f"top-2 margin {min(margins):.4g}")
+    # the case is well-conditioned: every step's margin is far above the f16 logit error
+    # (~0.006) and the model's order-sensitivity floor (~0.005), so identity is defined
+    assert min(margins) > 0.02, f"ill-conditioned case: smallest oracle top-2 margin {min(margins):.4g}"
     if diff:
         i = diff[0]
         raise AssertionError(f"first divergence at step {i}: gpu {g_ids[i]} vs oracle {o_ids[i]} "
