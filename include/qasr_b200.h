@@ -84,7 +84,7 @@ typedef struct {
 #define QASR_FLAG_KEEP_LOGITS 1u
 /* Replay batched decode steps through a CUDA graph (default on). */
 #define QASR_FLAG_NO_GRAPH 2u
-/* Record per-CTA %globaltimer stamps inside the int8 decode-chain launches of each step
+/* Record per-CTA %globaltimer stamps inside the decode-chain launches of each step
  * (read with qasr_read_trace; a diagnostic like the reference's QWEN3_ASR_PROFILE
  * timings, src/decoder.rs:84-96). */
 #define QASR_FLAG_TRACE 4u
@@ -329,6 +329,35 @@ qasr_status qasr_batch_decode(qasr_ctx* ctx, const qasr_segment* segs, int n, co
 qasr_status qasr_batch_decode_backend(const qasr_decode_backend* backend, const qasr_segment* segs, int n,
                                       const qasr_batch_options* opts, const qasr_batch_events* events,
                                       qasr_item_result* results);
+
+/* --- streaming session rounds (src/stream.rs:338-403) --------------------------- */
+/* The decoder-facing part of one round of the reference's streaming loop.  A session
+ * wraps one allocated slot.  Each round the caller passes the round's full prefill rows
+ * (f16 [rows, hidden_size]: prompt embeddings, audio rows, fed-back text); with kv_reuse
+ * the session prefills only the rows after the longest prefix unchanged since the
+ * previous round (common_rows, src/stream.rs:366-376: those cached KV rows are what a
+ * re-prefill would recompute; at most rows - 1 are reused), grows the slot to rows +
+ * budget + 8 (src/stream.rs:343-349, QASR_ERR_CAPACITY past max_seq), then decodes greedily
+ * until one of `eos` or `budget` tokens (src/stream.rs:380-395), and returns the tokens with
+ * same-token runs longer than max_run dropped (suppress_runs, src/stream.rs:403; the run
+ * may continue the fed-back text `prev_tokens`).  The reference's constants: budget 32
+ * (CHUNK_MAX_NEW) on a non-final round, max_run 12 (MAX_REPEAT_RUN), eos {151643, 151645}.
+ * Text assembly, rollback and the tokenizer stay with the caller. */
+typedef struct qasr_session qasr_session;
+qasr_status qasr_session_create(qasr_ctx* ctx, int slot, int kv_reuse, qasr_session** out);
+void qasr_session_destroy(qasr_session* session);
+/* tokens: room for `budget`; reused_rows: rows taken from the previous round's KV. */
+qasr_status qasr_session_round(qasr_session* session, const uint16_t* hidden, int rows, int budget,
+                               const int32_t* eos, int n_eos, const uint32_t* prev_tokens, int n_prev,
+                               int max_run, int32_t* tokens, int* n_tokens, int* dropped, int* hit_eos,
+                               int* reused_rows);
+/* common_rows (src/stream.rs:666-676): how many whole row_bytes rows a and b share at
+ * their start. */
+size_t qasr_common_rows(const void* a, size_t a_bytes, const void* b, size_t b_bytes, size_t row_bytes);
+/* suppress_runs (src/stream.rs:702-737): kept tokens into out (room for n_next), count in
+ * *n_out; returns the number dropped, -1 on a bad argument.  Host only. */
+int qasr_suppress_runs(const uint32_t* prev, int n_prev, const uint32_t* next, int n_next, int max_run,
+                       uint32_t* out, int* n_out);
 
 /* --- host helpers of the reference's loader ------------------------------------ */
 /* compute_mrope_cos_sin + text_positions (src/mrope.rs:46-80) rounded to f16 the

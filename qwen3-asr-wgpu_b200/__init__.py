@@ -65,11 +65,72 @@ EXPORTED_SYMBOLS = (
     "qasr_checkpoint_last_error", "qasr_checkpoint_tensor_count", "qasr_checkpoint_tensor_info",
     "qasr_checkpoint_weight_format", "qasr_checkpoint_read_f16", "qasr_checkpoint_rows_f16",
     "qasr_load_checkpoint", "qasr_batch_decode", "qasr_batch_decode_backend", "qasr_checkpoint_read_f32",
+    "qasr_session_create", "qasr_session_destroy", "qasr_session_round", "qasr_common_rows", "qasr_suppress_runs",
     # include/qasr_b200_audio.h
     "qasr_read_audio_config", "qasr_audio_token_count", "qasr_audio_create", "qasr_audio_destroy", "qasr_audio_last_error",
     "qasr_audio_load_weights", "qasr_audio_load_checkpoint", "qasr_audio_encode", "qasr_audio_encode_batch",
     "qasr_audio_encode_device", "qasr_audio_encode_batch_device", "qasr_audio_sync", "qasr_audio_stream", "qasr_audio_launch_count",
 )
+
+
+# streaming-round constants of the reference (src/stream.rs:47, 53)
+CHUNK_MAX_NEW, MAX_REPEAT_RUN = 32, 12
+
+
+def common_rows(a: np.ndarray, b: np.ndarray, row_bytes: int) -> int:
+    """common_rows (src/stream.rs:666-676) over the raw bytes of a and b."""
+    a = np.ascontiguousarray(a)
+    b = np.ascontiguousarray(b)
+    return int(lib.qasr_common_rows(_ptr(a), a.nbytes, _ptr(b), b.nbytes, row_bytes))
+
+
+def suppress_runs(prev, new, max_run: int):
+    """suppress_runs (src/stream.rs:702-737): (kept tokens, number dropped)."""
+    p = np.ascontiguousarray(prev, dtype=np.uint32)
+    n = np.ascontiguousarray(new, dtype=np.uint32)
+    out = np.zeros(max(1, n.size), np.uint32)
+    k = ctypes.c_int()
+    d = lib.qasr_suppress_runs(_ptr(p) if p.size else None, p.size, _ptr(n) if n.size else None, n.size, max_run,
+                               _ptr(out), ctypes.byref(k))
+    if d < 0:
+        raise ValueError("bad arguments")
+    return [int(x) for x in out[:k.value]], int(d)
+
+
+class Session:
+    """One slot's streaming rounds (qasr_session_round): prefill the round's rows after the
+    prefix unchanged since the last round, greedy-decode to an end id or the budget."""
+
+    def __init__(self, dec: "TextDecoder", slot: int, kv_reuse: bool = True):
+        self._dec = dec
+        h = ctypes.c_void_p()
+        dec._check(lib.qasr_session_create(dec._ctx, slot, 1 if kv_reuse else 0, ctypes.byref(h)))
+        self._h = h
+
+    def round(self, hidden: np.ndarray, budget: int = CHUNK_MAX_NEW, eos=(ENDOFTEXT_TOKEN_ID, IM_END_TOKEN_ID),
+              prev_tokens=(), max_run: int = MAX_REPEAT_RUN):
+        """Returns (tokens, dropped, hit_eos, reused_rows)."""
+        hidden = np.ascontiguousarray(hidden, dtype=np.uint16)
+        e = np.ascontiguousarray(eos, dtype=np.int32)
+        pv = np.ascontiguousarray(prev_tokens, dtype=np.uint32)
+        out = np.zeros(budget, np.int32)
+        n, d, he, ru = ctypes.c_int(), ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        self._dec._check(lib.qasr_session_round(self._h, _ptr(hidden), hidden.shape[0], budget,
+                                                _ptr(e) if e.size else None, e.size, _ptr(pv) if pv.size else None,
+                                                pv.size, max_run, _ptr(out), ctypes.byref(n), ctypes.byref(d),
+                                                ctypes.byref(he), ctypes.byref(ru)))
+        return [int(x) for x in out[:n.value]], d.value, bool(he.value), ru.value
+
+    def close(self):
+        if self._h:
+            lib.qasr_session_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class DecoderError(RuntimeError):
@@ -173,6 +234,14 @@ def _load() -> ctypes.CDLL:
     lib.qasr_step_batch.argtypes = [P, P, I, P]
     lib.qasr_read_logits.argtypes = [P, P, I]
     lib.qasr_read_trace.argtypes = [P, P, I, ctypes.POINTER(I)]
+    lib.qasr_session_create.argtypes = [P, I, I, ctypes.POINTER(P)]
+    lib.qasr_session_destroy.argtypes = [P]
+    lib.qasr_session_destroy.restype = None
+    lib.qasr_session_round.argtypes = [P, P, I, I, P, I, P, I, I, P, ctypes.POINTER(I), ctypes.POINTER(I),
+                                       ctypes.POINTER(I), ctypes.POINTER(I)]
+    lib.qasr_common_rows.argtypes = [P, ctypes.c_size_t, P, ctypes.c_size_t, ctypes.c_size_t]
+    lib.qasr_common_rows.restype = ctypes.c_size_t
+    lib.qasr_suppress_runs.argtypes = [P, I, P, I, I, P, ctypes.POINTER(I)]
     lib.qasr_read_attn_trace.argtypes = [P, P, I, ctypes.POINTER(I)]
     lib.qasr_check_wait_timeout.argtypes = [P, ctypes.c_uint32]
     lib.qasr_set_trace.argtypes = [P, I]
@@ -370,6 +439,10 @@ class TextDecoder:
 
     def set_pos(self, slot: int, pos: int):
         self._check(lib.qasr_set_slot_pos(self._ctx, slot, pos))
+
+    def session(self, slot: int, kv_reuse: bool = True) -> "Session":
+        """A streaming session over `slot` (qasr_session_create)."""
+        return Session(self, slot, kv_reuse)
 
     def set_input_token(self, slot: int, token: int):
         self._check(lib.qasr_set_input_token(self._ctx, slot, int(token)))
@@ -723,7 +796,8 @@ __all__ = [
     "build_rope_tables", "dim_map", "kernel_pack_weights", "kernel_gemm", "kernel_attention_noalloc", "kernel_attention", "kernel_kv_append",
     "launch_count", "version", "WEIGHTS_F16", "WEIGHTS_INT8", "WEIGHTS_INT8_F32", "EXPORTED_SYMBOLS", "lib",
     "Checkpoint", "read_model_config", "ModelConfig", "batch_decode_backend", "STOP_EOS", "STOP_MAX_TOKENS",
-    "ENDOFTEXT_TOKEN_ID", "IM_END_TOKEN_ID",
+    "ENDOFTEXT_TOKEN_ID", "IM_END_TOKEN_ID", "Session", "common_rows", "suppress_runs", "CHUNK_MAX_NEW",
+    "MAX_REPEAT_RUN",
     "f16_bits_to_f32", "f32_to_f16_bits", "PAGE_POSITIONS", "kv_page_swizzle", "FLAG_TRACE",
     "TRACE_SLOTS",
 ]

@@ -30,7 +30,7 @@ NVFLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-rela
            "-ccbin", CXX, "-Xptxas", "-v"] + ARCH
 
 CUDA_SOURCES = ["runtime.cu", "audio.cu"]
-CXX_SOURCES = ["synth.cpp", "host_helpers.cpp", "checkpoint.cpp", "batch_decode.cpp"]
+CXX_SOURCES = ["synth.cpp", "host_helpers.cpp", "checkpoint.cpp", "batch_decode.cpp", "session.cpp"]
 
 
 def _sources_digest() -> str:

@@ -1347,7 +1347,7 @@ qasr_status qasr_read_logits(qasr_ctx* c, float* out, int rows) {
 
 qasr_status qasr_read_trace(qasr_ctx* c, uint64_t* out, int cap, int* count) {
   if (!c || !out || !count || cap < 0) return QASR_ERR_INVALID_ARG;
-  if (!c->chain_trace) return fail(c, QASR_ERR_STATE, "no trace: create the context with QASR_FLAG_TRACE (int8 weights)");
+  if (!c->chain_trace) return fail(c, QASR_ERR_STATE, "no trace: create the context with QASR_FLAG_TRACE (decode-chain steps)");
   const size_t n = static_cast<size_t>(c->cfg.num_hidden_layers + 1) * c->num_sms * CHAIN_TRACE_SLOTS;
   *count = static_cast<int>(n);
   CK(cudaSetDevice(c->device), "cudaSetDevice");
@@ -1360,7 +1360,7 @@ qasr_status qasr_read_trace(qasr_ctx* c, uint64_t* out, int cap, int* count) {
 qasr_status qasr_set_trace(qasr_ctx* c, int enabled) {
   if (!c) return QASR_ERR_INVALID_ARG;
   if (enabled && !c->chain_trace)
-    return fail(c, QASR_ERR_STATE, "no trace buffers: create the context with QASR_FLAG_TRACE (int8 weights)");
+    return fail(c, QASR_ERR_STATE, "no trace buffers: create the context with QASR_FLAG_TRACE (decode-chain steps)");
   if (c->trace_on != (enabled != 0)) drop_graph(c);  // the recorded launches carry the trace pointers
   c->trace_on = enabled != 0;
   return QASR_OK;
@@ -1380,7 +1380,7 @@ qasr_status qasr_check_wait_timeout(qasr_ctx* c, uint32_t wait_us) {
 
 qasr_status qasr_read_attn_trace(qasr_ctx* c, uint64_t* out, int cap, int* count) {
   if (!c || !out || !count || cap < 0) return QASR_ERR_INVALID_ARG;
-  if (!c->attn_trace) return fail(c, QASR_ERR_STATE, "no trace: create the context with QASR_FLAG_TRACE (int8 weights)");
+  if (!c->attn_trace) return fail(c, QASR_ERR_STATE, "no trace: create the context with QASR_FLAG_TRACE (decode-chain steps)");
   const size_t n = static_cast<size_t>(c->cfg.num_hidden_layers) * c->num_sms * ATTN_TRACE_SLOTS;
   *count = static_cast<int>(n);
   CK(cudaSetDevice(c->device), "cudaSetDevice");
