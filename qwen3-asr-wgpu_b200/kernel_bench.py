@@ -175,14 +175,14 @@ def bench_append(args, pkg, torch):
 
 
 def bench_step(args, pkg, torch):
-    """Timeline of one int8 decode step (cfg4 shape) from the decode-chain trace: per
+    """Timeline of one decode step (cfg4 shape by default) from the decode-chain trace: per
     chain launch its duration, per operation the time (after the launch's first CTA
     entry) at which the last CTA finished it and at which the barrier after it opened,
     and the gap between launches (attention + merge + launch overhead)."""
     cfg = pkg.text_config(args.model, num_hidden_layers=args.layers)
     model = pkg.SyntheticModel(cfg, seed=args.seed)
-    dec = pkg.TextDecoder(cfg, weight_format=pkg.WEIGHTS_INT8, max_slots=args.slots, max_seq=args.hi + 64,
-                          trace=True)
+    dec = pkg.TextDecoder(cfg, weight_format=pkg.WEIGHTS_INT8 if args.fmt == "int8" else pkg.WEIGHTS_F16,
+                          max_slots=args.slots, max_seq=args.hi + 64, trace=True)
     dec.load_model(model)
     cos, sin = pkg.build_rope_tables(args.hi + 64)
     dec.set_rope_tables(cos, sin)
@@ -363,6 +363,7 @@ def main(argv=None):
     sp.add_argument("--lo", type=int, default=100)
     sp.add_argument("--hi", type=int, default=1500)
     sp.add_argument("--seed", type=int, default=5)
+    sp.add_argument("--fmt", choices=["f16", "int8"], default="int8")
     au = sub.add_parser("audio")
     au.add_argument("--model", default="0.6b")
     au.add_argument("--seconds", type=float, default=30.0)
