@@ -949,12 +949,13 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
       const int tiles = a.hs / 128;
       for (int it = wid; it < a.rows * tiles; it += nwarps) {
         const int r = it / tiles, T = it - r * tiles;
+        // the residual's load is issued before the poll, so its round trip overlaps it
+        __half* hp = a.h + static_cast<size_t>(r) * a.hs + T * 128 + 4 * lane;
+        const uint2 hw = __ldcg(reinterpret_cast<const uint2*>(hp));
         float4 acc;
         const bool lok = chain_sum4<CHAIN_MAX_SEG>(chain_partial(a, g, T, r, 4 * lane), slot_u64,
                                                    chain_tile_segs(g, T), acc, llw, 0x752);
         if (!__all_sync(0xffffffffu, lok)) break;
-        __half* hp = a.h + static_cast<size_t>(r) * a.hs + T * 128 + 4 * lane;
-        const uint2 hw = __ldcg(reinterpret_cast<const uint2*>(hp));
         const float2 h01 = __half22float2(*reinterpret_cast<const __half2*>(&hw.x));
         const float2 h23 = __half22float2(*reinterpret_cast<const __half2*>(&hw.y));
         const __half2 n01 = __floats2half2_rn(__fadd_rn(h01.x, acc.x), __fadd_rn(h01.y, acc.y));
@@ -981,6 +982,11 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
       const int tiles = a.hs / 128;
       for (int it = wid; it < a.rows * tiles; it += nwarps) {
         const int r = it / tiles, T = it - r * tiles;
+        // this warp's h tile (it wrote it in the residual add) and the gains, loaded before
+        // the poll so their round trips overlap it
+        const int c = T * 128 + 4 * lane;
+        const uint2 hw = __ldcg(reinterpret_cast<const uint2*>(a.h + static_cast<size_t>(r) * a.hs + c));
+        const float4 w = *reinterpret_cast<const float4*>(op.norm_w + c);
         bool lok = true;
         float t = 0.f;
         if (lane < tiles) {
@@ -997,11 +1003,8 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
         for (int o = 8; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
         t = __shfl_sync(0xffffffffu, t, 0);  // lane 0's order, the same value everywhere
         const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, static_cast<float>(a.hs)), a.eps)));
-        const int c = T * 128 + 4 * lane;
-        const uint2 hw = __ldcg(reinterpret_cast<const uint2*>(a.h + static_cast<size_t>(r) * a.hs + c));
         const float2 h01 = __half22float2(*reinterpret_cast<const __half2*>(&hw.x));
         const float2 h23 = __half22float2(*reinterpret_cast<const __half2*>(&hw.y));
-        const float4 w = *reinterpret_cast<const float4*>(op.norm_w + c);
         const __half2 x01 = __floats2half2_rn(__fmul_rn(__fmul_rn(h01.x, inv), w.x), __fmul_rn(__fmul_rn(h01.y, inv), w.y));
         const __half2 x23 = __floats2half2_rn(__fmul_rn(__fmul_rn(h23.x, inv), w.z), __fmul_rn(__fmul_rn(h23.y, inv), w.w));
         uint2 xw;
@@ -1054,6 +1057,8 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
         const int page = __ldcg(a.row_page + r);
         const uint2 cw = __ldcg(reinterpret_cast<const uint2*>(a.row_rope + static_cast<size_t>(r) * 256 + d0));
         const uint2 sw = __ldcg(reinterpret_cast<const uint2*>(a.row_rope + static_cast<size_t>(r) * 256 + 128 + d0));
+        const float4 w = t < a.nq + a.nkv ? *reinterpret_cast<const float4*>((t < a.nq ? op.qn_w : op.kn_w) + d0)
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
         float4 acc;
         const bool lok = chain_sum4<CHAIN_QKV_SEG>(chain_partial(a, g, t, r, 4 * lane), slot_u64,
                                                    chain_tile_segs(g, t), acc, llw, 0x757);
@@ -1082,7 +1087,6 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
         ss = __shfl_sync(0xffffffffu, ss, 0);
         const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 128.0f), a.eps)));
-        const float4 w = *reinterpret_cast<const float4*>((t < a.nq ? op.qn_w : op.kn_w) + d0);
         const float wv[4] = {w.x, w.y, w.z, w.w};
         float xn[4], xp[4];
 #pragma unroll
