@@ -39,8 +39,9 @@
 //               warp 2 also allocates the TMEM
 //   warps 4-7   int8 A builders: f16(q * s) into TMEM (idle with f16 weights)
 //
-// Weight formats (template parameter F16): a weight unit is always one 16 KB tile of 128
-// rows x 128 bytes in the tiled layout (weight_tile_offset): 128 k of int8 or 64 k of f16.
+// Weight formats (template parameter F16): a unit is 128 output rows x 128 k, its weights
+// one 16 KB tile of the tiled layout (weight_tile_offset) in int8, two consecutive tiles
+// (64 k each) in f16; either way its activation tile is 128 k.
 //   warps 8-15  epilogue (two warps per TMEM lane quadrant, splitting the accumulator
 //               columns) and row operations; they also run the grid barriers
 #pragma once
@@ -404,7 +405,8 @@ template <int PROG, bool F16>
 __global__ void __launch_bounds__(CHAIN_THREADS, 1)
     decode_chain_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_attn,
                         const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ ChainArgs a) {
-  constexpr int KSTEPS = F16 ? 4 : 8;  // k elements per unit (64 f16 or 128 int8) / UMMA K (16)
+  constexpr int KSTEPS = 8;            // 128 k elements per unit, UMMA K = 16
+  constexpr int WPU = F16 ? 2 : 1;     // 16 KB weight tiles (W stages) per unit
   constexpr int EPI_WARP0 = 16 - CHAIN_EPI_WARPS;
   extern __shared__ __align__(1024) uint8_t chain_dsmem[];
   __shared__ __align__(8) uint64_t wfull_bar[CHAIN_MAX_W_STAGES], wfree_bar[CHAIN_MAX_W_STAGES];
@@ -423,7 +425,7 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(chain_dsmem) + 1023) & ~uintptr_t(1023));
   const int SW = a.w_stages, SU = a.a_stages;  // W stages, unit slots
   const uint32_t x_tile_bytes = static_cast<uint32_t>(a.n_tile) * 128u;
-  const uint32_t x_stage_bytes = F16 ? x_tile_bytes : 2u * x_tile_bytes;  // 64 or 128 k
+  const uint32_t x_stage_bytes = 2u * x_tile_bytes;
   uint8_t* xring = smem + static_cast<size_t>(SW) * 16384;
   // TMEM columns: two accumulator buffers (double-buffered segments), each split into
   // NACC accumulators (one per MMA issuer warp) that the epilogue adds in index order;
@@ -487,10 +489,12 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
       int xg = -1, xu = 0, xue = 0, xst = 0, xissued = 0;
       uint32_t wph = 0, xph = 0;
       bool xgate = false;
-      auto w_advance = [&]() {
+      auto w_advance = [&]() {  // wu, wue count weight tiles (WPU per unit)
         while (wu >= wue && wg + 1 < n_gemm_ops) {
           ++wg;
           chain_unit_range(a.gemms[wg], blockIdx.x, wu, wue);
+          wu *= WPU;
+          wue *= WPU;
         }
       };
       auto x_advance = [&]() {
@@ -541,7 +545,7 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
             mbar_arrive_expect_tx(&ufull_bar[xst], x_stage_bytes);
             // both 64-column halves in one copy (the map views X as {64, rows, K / 64}):
             // the producer's copies queue behind the weight copies, so each one counts
-            tma_load_3d(dst, tm, &ufull_bar[xst], 0, 0, F16 ? kb : 2 * kb);
+            tma_load_3d(dst, tm, &ufull_bar[xst], 0, 0, 2 * kb);
             ++xissued;
             if (++xst == SU) {
               xst = 0;
@@ -606,24 +610,23 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
     if (lane == 0 && j < NACC) {
       const uint32_t idesc = umma_idesc_f16_m128(static_cast<uint32_t>(a.n_tile));
       int us = 0, seg = -1, d = 0, i = 0, seg_i0 = 0;
-      int wst = 0;  // f16: the unit's W stage (the producer fills the ring in unit order)
-      uint32_t uph = 0, wph = 0;
+      uint32_t uph = 0;
       bool ok = true, started = false;
       for (int gi = 0; gi < n_gemm_ops && ok; ++gi) {
         const ChainGemm& g = a.gemms[gi];
         int ub, ue;
         chain_unit_range(g, blockIdx.x, ub, ue);
         for (int u = ub; u < ue; ++u, ++i) {
-          const int my_us = us, my_wst = wst;
-          const uint32_t my_uph = uph, my_wph = wph;
+          const int my_us = us;
+          const uint32_t my_uph = uph;
           if (++us == SU) {
             us = 0;
             uph ^= 1u;
           }
-          if (++wst == SW) {
-            wst = 0;
-            wph ^= 1u;
-          }
+          // f16: the unit's two W stages (the producer fills the ring tile by tile in unit order)
+          const int wt0 = 2 * i, wt1 = 2 * i + 1;
+          const int ws0 = wt0 % SW, ws1 = wt1 % SW;
+          const uint32_t wp0 = static_cast<uint32_t>((wt0 / SW) & 1), wp1 = static_cast<uint32_t>((wt1 / SW) & 1);
           const int kb = u % g.kblocks;
           const bool first = (u == ub) || (kb == 0);
           const bool last = (u == ue - 1) || (kb == g.kblocks - 1);
@@ -641,7 +644,8 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
           }
           if ((i - seg_i0) % NACC == j) {
             if (!mbar_wait(&ufull_bar[my_us], my_uph, &abort_flag, a.status, 0x722) ||
-                (F16 && !mbar_wait(&wfull_bar[my_wst], my_wph, &abort_flag, a.status, 0x726))) {
+                (F16 && (!mbar_wait(&wfull_bar[ws0], wp0, &abort_flag, a.status, 0x726) ||
+                         !mbar_wait(&wfull_bar[ws1], wp1, &abort_flag, a.status, 0x727)))) {
               ok = false;
               break;
             }
@@ -650,13 +654,16 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
             const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(d) * DCOLS + static_cast<uint32_t>(j) * DSTR;
             const uint32_t x_base = smem_u32(xring + static_cast<size_t>(my_us) * x_stage_bytes);
             if constexpr (F16) {
-              // A = the weight tile itself (128 rows x 64 k, 128-byte swizzled rows)
-              const uint32_t w_base = smem_u32(smem + static_cast<size_t>(my_wst) * 16384);
+              // A = the weight tiles themselves (128 rows x 64 k each, 128-byte swizzled rows)
+              const uint32_t w0 = smem_u32(smem + static_cast<size_t>(ws0) * 16384);
+              const uint32_t w1 = smem_u32(smem + static_cast<size_t>(ws1) * 16384);
 #pragma unroll
-              for (int kk = 0; kk < KSTEPS; ++kk)
-                umma_f16_ss(d_tmem, smem_desc_sw128(w_base + static_cast<uint32_t>(kk) * 32u),
-                            smem_desc_sw128(x_base + static_cast<uint32_t>(kk) * 32u), idesc,
-                            (!started && kk == 0) ? 0u : 1u);
+              for (int kk = 0; kk < KSTEPS; ++kk) {
+                const uint32_t b_addr = x_base + static_cast<uint32_t>(kk >> 2) * x_tile_bytes +
+                                        static_cast<uint32_t>(kk & 3) * 32u;
+                umma_f16_ss(d_tmem, smem_desc_sw128((kk < 4 ? w0 : w1) + static_cast<uint32_t>(kk & 3) * 32u),
+                            smem_desc_sw128(b_addr), idesc, (!started && kk == 0) ? 0u : 1u);
+              }
             } else {
               const uint32_t a_tmem = tmem_base + A_COLS0 + static_cast<uint32_t>(my_us) * 64u;
 #pragma unroll
@@ -669,7 +676,10 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 1)
             }
             started = true;
             umma_commit(&ufree_bar[my_us]);
-            if constexpr (F16) umma_commit(&wfree_bar[my_wst]);  // the W stage is read
+            if constexpr (F16) {  // the W stages are read
+              umma_commit(&wfree_bar[ws0]);
+              umma_commit(&wfree_bar[ws1]);
+            }
             if (a.trace != nullptr) {
               const unsigned long long now = globaltimer();
               if (u == ub) a.trace[blockIdx.x * CHAIN_TRACE_SLOTS + 29 + gi] = now;

@@ -103,9 +103,7 @@ struct ChainShape {
   size_t smem;
 };
 
-// `f16`: f16 weights, whose unit (one 16 KB tile) covers 64 k, so an X stage is one
-// 64-column tile; int8 units cover 128 k (two X tiles).
-static ChainShape chain_shape(int rows, bool f16) {
+static ChainShape chain_shape(int rows) {
   ChainShape s{};
   s.n_tile = std::max(16, (rows + 15) / 16 * 16);
   const int dstr = (s.n_tile + 31) / 32 * 32;  // TMEM columns of one accumulator
@@ -119,7 +117,7 @@ static ChainShape chain_shape(int rows, bool f16) {
   // columns the CTA allocates: n_acc falls as the tile widens (at most 128 rows: 2 x 128 +
   // 4 x 64 = 512)
   static_assert(2 * CHAIN_MAX_ROWS + 64 <= static_cast<int>(GEMM_TMEM_COLS), "chain TMEM budget");
-  const int xstage = (f16 ? 1 : 2) * s.n_tile * 128;
+  const int xstage = 2 * s.n_tile * 128;
   const int dyn = g_chain_dyn_max > 0 ? g_chain_dyn_max : 200 * 1024;
   s.w_stages = std::min(CHAIN_MAX_W_STAGES, (dyn - 1024 - s.a_stages * xstage) / 16384);
   s.smem = 1024 + static_cast<size_t>(s.w_stages) * 16384 + static_cast<size_t>(s.a_stages) * xstage;
@@ -132,16 +130,16 @@ static int chain_seg_cap(int kind) {
   return kind == 0 ? CHAIN_QKV_SEG : (kind == 2 ? CHAIN_SILU_SEG : CHAIN_MAX_SEG);
 }
 
-// GEMM of the chain (int8, or f16 when `f16`): at least two units (32 KB of weights) per
+// GEMM of the chain (units of 128 rows x 128 k; int8 or f16): at least two units per
 // taking-part CTA, and few enough taking-part CTAs that no tile is cut into more than
 // `max_seg_cap` segments (the bound of the operation that adds the partials).
 static ChainGemm chain_gemm_plan(const uint8_t* w, const void* scale, bool scale32, int n_out, int k, int xmap,
-                                 int sms, int max_seg_cap, bool f16) {
+                                 int sms, int max_seg_cap) {
   ChainGemm g{};
   g.w = w;
   g.scale = scale;
   g.scale32 = scale32 ? 1 : 0;
-  g.kblocks = k / (f16 ? 64 : 128);
+  g.kblocks = k / 128;
   g.units = (n_out / 128) * g.kblocks;
   for (g.grid = std::max(1, std::min(sms, g.units / 2));; --g.grid) {
     int ms = 1;
@@ -521,7 +519,7 @@ qasr_status launch_chain(qasr_ctx* c, const ChainArgs& a, const ChainShape& sh, 
   const int I = c->cfg.intermediate_size;
   CUtensorMap tx, ta, tact;
   const uint32_t box = static_cast<uint32_t>(sh.n_tile);
-  const uint32_t nch = c->chain_f16 ? 1u : 2u;  // 64-column tiles per unit
+  const uint32_t nch = 2;  // 64-column tiles per unit (128 k)
   if (!make_tmap_chunks(&tx, c->x, hs, n, static_cast<uint64_t>(hs) * 2, box, nch, &c->err) ||
       !make_tmap_chunks(&ta, c->attn, qd, n, static_cast<uint64_t>(qd) * 2, box, nch, &c->err) ||
       !make_tmap_chunks(&tact, c->act, I, n, static_cast<uint64_t>(I) * 2, box, nch, &c->err))
@@ -565,7 +563,7 @@ qasr_status launch_chain(qasr_ctx* c, const ChainArgs& a, const ChainShape& sh, 
 // layer attention + merge + chain (o_proj ... next layer's QKV, or the final norm),
 // then lm_head + argmax.
 qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
-  const ChainShape sh = chain_shape(n, c->chain_f16);
+  const ChainShape sh = chain_shape(n);
   const int L = c->cfg.num_hidden_layers, hs = c->cfg.hidden_size, I = c->cfg.intermediate_size;
   const int nq = c->cfg.num_attention_heads, nkv = c->cfg.num_key_value_heads;
   const int qd = nq * c->cfg.head_dim, qkv_out = qd + 2 * nkv * 128;
@@ -608,7 +606,7 @@ qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
   base.status = c->status;
   auto gemm = [&](const Linear& lin, int xmap, int kind) {
     ChainGemm g = chain_gemm_plan(static_cast<const uint8_t*>(lin.w), lin.scale, lin.scale32, lin.n_out, lin.k, xmap, sms,
-                                  chain_seg_cap(kind), c->chain_f16);
+                                  chain_seg_cap(kind));
     g.ws = c->chain_ws[kind];
     return g;
   };
@@ -926,11 +924,11 @@ qasr_status qasr_create(const qasr_text_config* cfg, const qasr_options* opts, i
     if (const char* wc = std::getenv("QASR_B200_CHAIN_WCAP")) c->chain_wcap = std::max(1, std::atoi(wc));
     const char* no_cpdl = std::getenv("QASR_B200_NO_CHAIN_PDL");
     c->chain_pdl = pdl_enabled() && !(no_cpdl && no_cpdl[0] == '1') &&
-                   chain_one_cta_per_sm(chain_shape(std::min(opts->max_slots, CHAIN_MAX_ROWS), c->chain_f16).smem);
-    c->chain_ws_rows = chain_shape(std::min(opts->max_slots, CHAIN_MAX_ROWS), c->chain_f16).n_tile;
+                   chain_one_cta_per_sm(chain_shape(std::min(opts->max_slots, CHAIN_MAX_ROWS)).smem);
+    c->chain_ws_rows = chain_shape(std::min(opts->max_slots, CHAIN_MAX_ROWS)).n_tile;
     for (int i = 0; i < 4; ++i) {  // shapes[] order: QKV, o_proj, gate|up, down
       const ChainGemm g = chain_gemm_plan(nullptr, nullptr, false, shapes[i][0], shapes[i][1], 0, c->num_sms,
-                                          chain_seg_cap(i), c->chain_f16);
+                                          chain_seg_cap(i));
       if (2ull * static_cast<unsigned long long>(g.units) * static_cast<unsigned long long>(g.grid) >= (1ull << 32))
         return fail(c, QASR_ERR_CAPACITY, "decode chain GEMM: too many units for 32-bit unit maps");
       c->chain_ws_n[i] = static_cast<size_t>(shapes[i][0] / 128) * g.max_seg * chain_slot_words(c->chain_ws_rows);
