@@ -559,7 +559,7 @@ qasr_status launch_chain(qasr_ctx* c, const ChainArgs& a, const ChainShape& sh, 
   return QASR_OK;
 }
 
-// The int8 decode step as 1 + 3 L + 2 launches: chain (embed, norm, QKV 0), then per
+// The decode step (int8 or f16 weights) as 1 + 3 L + 2 launches: chain (embed, norm, QKV 0), then per
 // layer attention + merge + chain (o_proj ... next layer's QKV, or the final norm),
 // then lm_head + argmax.
 qasr_status enqueue_decode_chain(qasr_ctx* c, int n, uint64_t* nk) {
