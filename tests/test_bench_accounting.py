@@ -59,3 +59,27 @@ def test_audio_flops_direct_count(qasr):
     gemms = 2 * T * C * 16 * d + 18 * 2 * T * (4 * d * d + 2 * d * f) + 2 * T * (d * d + d * 1024)
     attn = 18 * 4 * (3 * 104 * 104 + 78 * 78) * d
     assert flops == convs + gemms + attn
+
+
+@pytest.mark.parametrize("int8", [True, False], ids=["int8", "f16"])
+def test_chain_roofline_bytes(qasr, int8):
+    """The decode chain's roofline point: one layer's weights per middle launch (int8 +
+    f16 scales: 50,372,608 B at 1.7B; f16: twice the linears), its duration from the
+    trace's first entry to last exit (a fake trace of 3 launches x 2 CTAs x 128 slots)."""
+    import numpy as np
+    b = _bench()
+    cfg = qasr.text_config("1.7b", num_hidden_layers=2)
+
+    class FakeDec:
+        def read_trace(self):
+            t = np.zeros((3, 2, 128), np.uint64)
+            t[:, :, 0] = 1000
+            t[:, :, -1] = 1000 + 45_000  # 45 us per launch
+            return t
+
+    r = b.chain_timing(FakeDec(), cfg, int8)
+    lin = 4096 * 2048 + 2048 * 2048 + 12288 * 2048 + 2048 * 6144
+    want = 50_372_608 if int8 else 2 * lin
+    assert r["bytes"] == want
+    assert r["seconds"] == pytest.approx(45e-6)
+    assert r["launches_per_step"] == 3
