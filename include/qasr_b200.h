@@ -342,7 +342,9 @@ qasr_status qasr_batch_decode_backend(const qasr_decode_backend* backend, const 
  * same-token runs longer than max_run dropped (suppress_runs, src/stream.rs:403; the run
  * may continue the fed-back text `prev_tokens`).  The reference's constants: budget 32
  * (CHUNK_MAX_NEW) on a non-final round, max_run 12 (MAX_REPEAT_RUN), eos {151643, 151645}.
- * Text assembly, rollback and the tokenizer stay with the caller. */
+ * Text assembly, rollback and the tokenizer stay with the caller.  Between rounds the
+ * slot belongs to the session: prefilling, stepping, rolling back or freeing it through
+ * other calls voids the reuse, which assumes its cached rows are the previous round's. */
 typedef struct qasr_session qasr_session;
 qasr_status qasr_session_create(qasr_ctx* ctx, int slot, int kv_reuse, qasr_session** out);
 void qasr_session_destroy(qasr_session* session);

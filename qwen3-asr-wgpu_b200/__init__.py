@@ -110,7 +110,7 @@ class Session:
     def round(self, hidden: np.ndarray, budget: int = CHUNK_MAX_NEW, eos=(ENDOFTEXT_TOKEN_ID, IM_END_TOKEN_ID),
               prev_tokens=(), max_run: int = MAX_REPEAT_RUN):
         """Returns (tokens, dropped, hit_eos, reused_rows)."""
-        hidden = np.ascontiguousarray(hidden, dtype=np.uint16)
+        hidden = _rows(hidden, self._dec.cfg["hidden_size"])
         e = np.ascontiguousarray(eos, dtype=np.int32)
         pv = np.ascontiguousarray(prev_tokens, dtype=np.uint32)
         out = np.zeros(budget, np.int32)
@@ -304,6 +304,19 @@ from .synth import (MODEL_PRESETS, SyntheticModel, build_rope_tables, dim_map,  
                     f16_bits_to_f32, f32_to_f16_bits, text_config)
 
 
+def _rows(hidden, width: int) -> np.ndarray:
+    """Prefill rows as the library reads them: C-contiguous f16 bits [rows, width] (uint16;
+    an f16 array is taken bit for bit).  The C ABI reads rows x width values behind the
+    pointer, so any other shape is refused here rather than read past."""
+    h = np.asarray(hidden)
+    if h.dtype == np.float16:
+        h = h.view(np.uint16)
+    h = np.ascontiguousarray(h, dtype=np.uint16)
+    if h.ndim != 2 or h.shape[1] != width:
+        raise ValueError(f"hidden rows must be [rows, {width}] f16 bits, got shape {h.shape}")
+    return h
+
+
 def _ptr(a: np.ndarray | None):
     if a is None:
         return None
@@ -397,8 +410,8 @@ class TextDecoder:
     def batch_decode(self, segments, *, width: int, eos=(ENDOFTEXT_TOKEN_ID, IM_END_TOKEN_ID),
                      kv_step: int = 256, batch_seq_cap: int = 4096, on_item=None, should_stop=None):
         """qasr_batch_decode: [(hidden, max_new_tokens)] -> [{status, stop, tokens}]."""
-        return _batch_call(lib.qasr_batch_decode, self._ctx, segments, width, eos, kv_step, batch_seq_cap,
-                           on_item, should_stop)
+        return _batch_call(lib.qasr_batch_decode, self._ctx, self.cfg["hidden_size"], segments, width, eos, kv_step,
+                           batch_seq_cap, on_item, should_stop)
 
     def load_checkpoint(self, ck: "Checkpoint", prefix: str | None = None):
         """Every decoder weight of an opened checkpoint (qasr_load_checkpoint)."""
@@ -455,7 +468,7 @@ class TextDecoder:
     # ---------------------------------------------------------------- hot path
     def prefill(self, slot: int, hidden: np.ndarray, kv_start: int = 0) -> int:
         """TextBackend::prefill: hidden is [s, hidden] f16 bits (uint16)."""
-        h = np.ascontiguousarray(hidden, dtype=np.uint16)
+        h = _rows(hidden, self.cfg["hidden_size"])
         tok = ctypes.c_int32()
         self._check(lib.qasr_prefill(self._ctx, slot, _ptr(h), h.shape[0], kv_start, ctypes.byref(tok)))
         return tok.value
@@ -467,8 +480,9 @@ class TextDecoder:
 
     def prefill_batch(self, slots, hiddens, kv_starts=None) -> np.ndarray:
         slots_a = np.ascontiguousarray(slots, dtype=np.int32)
-        lens = np.array([h.shape[0] for h in hiddens], dtype=np.int32)
-        hid = np.ascontiguousarray(np.concatenate(hiddens, axis=0), dtype=np.uint16)
+        rows = [_rows(h, self.cfg["hidden_size"]) for h in hiddens]
+        lens = np.array([h.shape[0] for h in rows], dtype=np.int32)
+        hid = np.ascontiguousarray(np.concatenate(rows, axis=0))
         ks = None if kv_starts is None else np.ascontiguousarray(kv_starts, dtype=np.int32)
         out = np.zeros(len(slots_a), dtype=np.int32)
         self._check(lib.qasr_prefill_batch(self._ctx, _ptr(slots_a), len(slots_a), _ptr(hid), _ptr(lens),
@@ -520,12 +534,12 @@ class TextDecoder:
         self._check(lib.qasr_check_wait_timeout(self._ctx, int(wait_us)))
 
 
-def _batch_call(fn, first_arg, segments, width, eos, kv_step, batch_seq_cap, on_item, should_stop):
+def _batch_call(fn, first_arg, hidden_size, segments, width, eos, kv_step, batch_seq_cap, on_item, should_stop):
     """Shared driver of qasr_batch_decode(_backend): segments = [(hidden f16 bits
     [len, hidden], max_new_tokens)]; returns per segment {status, stop, tokens} and calls
     on_item(index, result) in completion order."""
     n = len(segments)
-    keep = [np.ascontiguousarray(h, dtype=np.uint16) for h, _ in segments]
+    keep = [_rows(h, hidden_size) for h, _ in segments]
     segs = (Segment * max(n, 1))()
     res = (ItemResult * max(n, 1))()
     bufs = []
@@ -592,8 +606,8 @@ def batch_decode_backend(backend, segments, *, width: int, eos=(ENDOFTEXT_TOKEN_
 
     be = DecodeBackend(None, backend.hidden_size, BE_FORK(wrap(fork)), BE_FREE(wrap(free)),
                        BE_PREFILL(wrap(prefill)), BE_STEP(wrap(step)))
-    return _batch_call(lib.qasr_batch_decode_backend, ctypes.byref(be), segments, width, eos, kv_step,
-                       batch_seq_cap, on_item, should_stop)
+    return _batch_call(lib.qasr_batch_decode_backend, ctypes.byref(be), backend.hidden_size, segments, width, eos,
+                       kv_step, batch_seq_cap, on_item, should_stop)
 
 
 def read_model_config(model_dir: str) -> dict:

@@ -112,6 +112,10 @@ qasr_status qasr_session_round(qasr_session* s, const uint16_t* hidden, int rows
     reuse = std::min(qasr_common_rows(s->prev.data(), s->prev.size() * sizeof(uint16_t), hidden,
                                       static_cast<size_t>(rows) * row_bytes, row_bytes),
                      static_cast<size_t>(rows - 1));
+  // from here on the slot's rows past `reuse` are rewritten: until this round's prefill
+  // has succeeded, only the first `reuse` rows of `prev` still describe its cache (a round
+  // that fails part-way cannot leave a longer reusable prefix behind)
+  if (s->kv_reuse) s->prev.resize(reuse * static_cast<size_t>(s->hidden_size));
   int32_t tok = 0;
   const int r = static_cast<int>(reuse);
   if (qasr_status st = qasr_prefill(s->ctx, s->slot, hidden + reuse * s->hidden_size, rows - r, r, &tok)) return st;

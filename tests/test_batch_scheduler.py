@@ -249,3 +249,18 @@ def test_random_workloads_match_the_restated_control_flow(qasr):
         check(res, want)
         assert sorted(seen) == list(range(n)), (case, seen)
         assert not fake.live, case  # every slot freed
+
+
+def test_rows_of_the_wrong_width_are_refused_before_the_library_reads_them(qasr):
+    """The C ABI reads len x hidden_size values behind each segment's pointer, so the
+    Python mirror refuses rows of another shape instead of letting it read past them; f16
+    arrays are taken bit for bit."""
+    scripts = [[5, 6]]
+    with pytest.raises(ValueError, match=r"\[rows, 4\]"):
+        qasr.batch_decode_backend(Fake(scripts), [(np.zeros((3, HS + 1), np.uint16), 2)], width=1)
+    with pytest.raises(ValueError, match=r"\[rows, 4\]"):
+        qasr.batch_decode_backend(Fake(scripts), [(np.zeros(3 * HS, np.uint16), 2)], width=1)
+    # segment 1's marker as the f16 whose bits are 1 (a value cast would make it 0)
+    rows = [h if i == 0 else h.view(np.float16) for i, (h, _) in enumerate(segs([3, 3], [2, 2]))]
+    res = qasr.batch_decode_backend(Fake([[5, 6], [8, 9]]), [(h, 2) for h in rows], width=1)
+    assert [r["tokens"] for r in res] == [[5, 6], [8, 9]]
