@@ -348,6 +348,9 @@ qasr_status qasr_batch_decode_backend(const qasr_decode_backend* backend, const 
 typedef struct qasr_session qasr_session;
 qasr_status qasr_session_create(qasr_ctx* ctx, int slot, int kv_reuse, qasr_session** out);
 void qasr_session_destroy(qasr_session* session);
+/* Forget the previous round's rows, so the next round prefills all of its rows: the
+ * stream's recovery step (reanchor, src/stream.rs:593-607) clears them the same way. */
+void qasr_session_reset(qasr_session* session);
 /* tokens: room for `budget`; reused_rows: rows taken from the previous round's KV. */
 qasr_status qasr_session_round(qasr_session* session, const uint16_t* hidden, int rows, int budget,
                                const int32_t* eos, int n_eos, const uint32_t* prev_tokens, int n_prev,

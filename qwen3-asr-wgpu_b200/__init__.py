@@ -65,7 +65,7 @@ EXPORTED_SYMBOLS = (
     "qasr_checkpoint_last_error", "qasr_checkpoint_tensor_count", "qasr_checkpoint_tensor_info",
     "qasr_checkpoint_weight_format", "qasr_checkpoint_read_f16", "qasr_checkpoint_rows_f16",
     "qasr_load_checkpoint", "qasr_batch_decode", "qasr_batch_decode_backend", "qasr_checkpoint_read_f32",
-    "qasr_session_create", "qasr_session_destroy", "qasr_session_round", "qasr_common_rows", "qasr_suppress_runs",
+    "qasr_session_create", "qasr_session_destroy", "qasr_session_reset", "qasr_session_round", "qasr_common_rows", "qasr_suppress_runs",
     # include/qasr_b200_audio.h
     "qasr_read_audio_config", "qasr_audio_token_count", "qasr_audio_create", "qasr_audio_destroy", "qasr_audio_last_error",
     "qasr_audio_load_weights", "qasr_audio_load_checkpoint", "qasr_audio_encode", "qasr_audio_encode_batch",
@@ -120,6 +120,12 @@ class Session:
                                                 pv.size, max_run, _ptr(out), ctypes.byref(n), ctypes.byref(d),
                                                 ctypes.byref(he), ctypes.byref(ru)))
         return [int(x) for x in out[:n.value]], d.value, bool(he.value), ru.value
+
+    def reset(self):
+        """Forget the previous round's rows (qasr_session_reset): the next round prefills
+        all of its rows."""
+        if self._h:
+            lib.qasr_session_reset(self._h)
 
     def close(self):
         if self._h:
@@ -237,6 +243,8 @@ def _load() -> ctypes.CDLL:
     lib.qasr_session_create.argtypes = [P, I, I, ctypes.POINTER(P)]
     lib.qasr_session_destroy.argtypes = [P]
     lib.qasr_session_destroy.restype = None
+    lib.qasr_session_reset.argtypes = [P]
+    lib.qasr_session_reset.restype = None
     lib.qasr_session_round.argtypes = [P, P, I, I, P, I, P, I, I, P, ctypes.POINTER(I), ctypes.POINTER(I),
                                        ctypes.POINTER(I), ctypes.POINTER(I)]
     lib.qasr_common_rows.argtypes = [P, ctypes.c_size_t, P, ctypes.c_size_t, ctypes.c_size_t]

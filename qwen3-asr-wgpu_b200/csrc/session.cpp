@@ -90,6 +90,12 @@ qasr_status qasr_session_create(qasr_ctx* ctx, int slot, int kv_reuse, qasr_sess
 
 void qasr_session_destroy(qasr_session* s) { delete s; }
 
+// The stream's recovery step forgets the previous round's rows (src/stream.rs:605), so
+// the next round prefills all of its rows.
+void qasr_session_reset(qasr_session* s) {
+  if (s) s->prev.clear();
+}
+
 qasr_status qasr_session_round(qasr_session* s, const uint16_t* hidden, int rows, int budget, const int32_t* eos,
                                int n_eos, const uint32_t* prev_tokens, int n_prev, int max_run, int32_t* tokens,
                                int* n_tokens, int* dropped, int* hit_eos, int* reused_rows) {
@@ -99,7 +105,7 @@ qasr_status qasr_session_round(qasr_session* s, const uint16_t* hidden, int rows
   *n_tokens = *dropped = *hit_eos = *reused_rows = 0;
   const size_t row_bytes = static_cast<size_t>(s->hidden_size) * sizeof(uint16_t);
   // the round must fit the decoder (src/stream.rs:343-348), then the slot grows to it
-  if (rows + budget + 8 > qasr_max_seq(s->ctx))
+  if (static_cast<long long>(rows) + budget + 8 > qasr_max_seq(s->ctx))
     return qasr::ctx_fail(s->ctx, QASR_ERR_CAPACITY,
                           "live seq " + std::to_string(rows) + " + max_new " + std::to_string(budget) +
                               " exceeds decoder max_seq " + std::to_string(qasr_max_seq(s->ctx)));

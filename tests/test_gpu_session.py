@@ -44,6 +44,10 @@ def test_session_rounds_reuse_the_unchanged_prefix(qasr, cuda_device, oracle):
     assert reused == 150
     assert (toks, dropped, hit) == (kept2, dropped2, False)
     assert dropped2 > 0  # the repeated id ran past the cap of 12
+    # after a reset (the stream's reanchor) the same rows are prefilled whole
+    sa.reset()
+    toks, dropped, hit, reused = sa.round(p2, budget=16, eos=())
+    assert (toks, dropped, hit, reused) == (kept2, dropped2, False, 0)
 
     b = dec.fork_capped(64)
     sb = dec.session(b, kv_reuse=False)
