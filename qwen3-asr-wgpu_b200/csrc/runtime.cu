@@ -1099,7 +1099,8 @@ qasr_status qasr_ensure_capacity(qasr_ctx* c, int slot, int need, int* cap) {
   if (s) return s;
   CK(cudaSetDevice(c->device), "cudaSetDevice");
   // grow-only and stepped like KV_STEP (src/decoder.rs:1604-1661); contents are kept
-  const int target = std::min(c->opts.max_seq, (need + 255) / 256 * 256);
+  const long long stepped = (static_cast<long long>(need) + 255) / 256 * 256;  // no int wrap near INT_MAX
+  const int target = static_cast<int>(std::min<long long>(c->opts.max_seq, stepped));
   if ((s = grow_slot(c, slot, std::max(target, need)))) return s;
   if (cap) *cap = c->slots[slot].cap;
   return QASR_OK;
@@ -1262,10 +1263,10 @@ qasr_status qasr_prefill_batch(qasr_ctx* c, const int* slots, int n, const uint1
     if ((s = check_slot(c, slots[i]))) return s;
     const int ks = kv_starts ? kv_starts[i] : 0;
     if (lens[i] <= 0 || ks < 0) return fail(c, QASR_ERR_INVALID_ARG, "segment %d: bad length/start", i);
-    if (ks + lens[i] > c->opts.max_seq)
-      return fail(c, QASR_ERR_CAPACITY, "prefill needs %d positions, max_seq is %d", ks + lens[i],
-                  c->opts.max_seq);
-    if (ks + lens[i] > c->rope_positions)
+    const long long end = static_cast<long long>(ks) + lens[i];  // no int wrap past max_seq
+    if (end > c->opts.max_seq)
+      return fail(c, QASR_ERR_CAPACITY, "prefill needs %lld positions, max_seq is %d", end, c->opts.max_seq);
+    if (end > c->rope_positions)
       return fail(c, QASR_ERR_CAPACITY, "prefill beyond the rope tables");
     if ((s = grow_slot(c, slots[i], ks + lens[i]))) return s;
     seen.push_back(slots[i]);

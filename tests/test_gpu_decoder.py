@@ -301,6 +301,12 @@ def test_errors_are_status_codes(qasr, cuda_device):
     with pytest.raises(qasr.DecoderError) as e:
         dec.prefill(s, model.prefix(0, 200)[0])  # 224 rows > max_seq 128
     assert e.value.status == 3
+    with pytest.raises(qasr.DecoderError) as e:  # a start whose end would wrap a 32-bit int
+        dec.prefill(s, model.prefix(0, 8)[0], kv_start=2**31 - 8)
+    assert e.value.status == 3
+    with pytest.raises(qasr.DecoderError) as e:
+        dec.ensure_capacity(s, 2**31 - 1)
+    assert e.value.status == 3
     with pytest.raises(qasr.DecoderError):
         dec.fork_capped(64)  # only one slot
     with pytest.raises(qasr.DecoderError):
