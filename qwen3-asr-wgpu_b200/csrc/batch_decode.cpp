@@ -13,7 +13,7 @@
 
 namespace {
 
-int round_up(long long x, int m) { return static_cast<int>((x + m - 1) / m * m); }
+long long round_up(long long x, int m) { return (x + m - 1) / m * m; }
 
 struct Run {
   const qasr_decode_backend* be;
@@ -25,7 +25,10 @@ struct Run {
 
   bool is_eos(int32_t t) const { return t == o->eos[0] || t == o->eos[1]; }
   bool should_stop() const { return ev && ev->should_stop && ev->should_stop(ev->user) != 0; }
-  int cap_of(int i) const { return round_up(static_cast<long long>(segs[i].len) + segs[i].max_new_tokens + 8, o->kv_step); }
+  // KV positions a segment needs, in 64-bit (len + max_new near INT_MAX must not wrap)
+  long long cap_of(int i) const {
+    return round_up(static_cast<long long>(segs[i].len) + segs[i].max_new_tokens + 8, o->kv_step);
+  }
 
   // Outcomes::done: the first result of an item is final and reported at once
   void done(int i, int status, int stop, const std::vector<int32_t>& toks) {
@@ -44,7 +47,9 @@ struct Run {
   int decode_one(int i, std::vector<int32_t>* toks, int* stop) {
     const qasr_segment& g = segs[i];
     int slot = -1;
-    int st = be->fork_capped(be->user, cap_of(i), &slot);
+    // a cap past INT32_MAX is asked as INT32_MAX: the backend clamps it to its max_seq
+    // and the prefill or a step then reports the shortfall
+    int st = be->fork_capped(be->user, static_cast<int>(std::min<long long>(cap_of(i), INT32_MAX)), &slot);
     if (st) return st;
     int32_t tok = 0;
     st = be->prefill_batch(be->user, &slot, 1, g.hidden, &g.len, &tok);
@@ -84,8 +89,8 @@ struct Run {
   // run_batch_attempt (src/inference.rs:2110-2227)
   Attempt attempt(const std::vector<int>& run, int width) {
     const int nslots = std::min<int>(width, static_cast<int>(run.size()));
-    int cap = o->kv_step;
-    for (int i : run) cap = std::max(cap, cap_of(i));
+    int cap = o->kv_step;  // the run's segments all fit batch_seq_cap, an int
+    for (int i : run) cap = std::max(cap, static_cast<int>(cap_of(i)));
     std::vector<int> slot_id;
     auto release = [&]() {
       for (int s : slot_id) be->slot_free(be->user, s);

@@ -264,3 +264,43 @@ def test_rows_of_the_wrong_width_are_refused_before_the_library_reads_them(qasr)
     rows = [h if i == 0 else h.view(np.float16) for i, (h, _) in enumerate(segs([3, 3], [2, 2]))]
     res = qasr.batch_decode_backend(Fake([[5, 6], [8, 9]]), [(h, 2) for h in rows], width=1)
     assert [r["tokens"] for r in res] == [[5, 6], [8, 9]]
+
+
+def test_capacity_of_a_huge_budget_does_not_wrap(qasr):
+    """len + max_new near INT32_MAX: the capacity the scheduler asks for is computed in
+    64 bits, so the segment goes to the single-sequence path (past batch_seq_cap) and its
+    slot is asked for INT32_MAX positions, not a wrapped negative count.  The call is made
+    directly with a small token buffer: the scripted decoder ends on an eos id after two
+    tokens, so no more are written."""
+    import ctypes
+    fake = Fake([[5, 6, EOS[0]]])
+    h = segs([3], [1])[0][0]
+    seg = (qasr.Segment * 1)()
+    seg[0].hidden, seg[0].len, seg[0].max_new_tokens = h.ctypes.data, 3, 2**31 - 1
+    toks = (ctypes.c_int32 * 8)()
+    res = (qasr.ItemResult * 1)()
+    res[0].tokens = toks
+
+    def fork(user, cap, slot_p):
+        slot_p[0] = fake.fork_capped(cap)
+        return 0
+
+    def prefill(user, slots_p, n, hidden_p, lens_p, first_p):
+        flat = np.ctypeslib.as_array(hidden_p, shape=(lens_p[0] * HS,)).reshape(-1, HS)
+        first_p[0] = fake.prefill_batch([slots_p[0]], [flat])[0]
+        return 0
+
+    def step(user, slots_p, n, out_p):
+        out_p[0] = fake.step_batch([slots_p[0]])[0]
+        return 0
+
+    cbs = (qasr.BE_FORK(fork), qasr.BE_FREE(lambda user, s: fake.slot_free(s) or 0),
+           qasr.BE_PREFILL(prefill), qasr.BE_STEP(step))
+    be = qasr.DecodeBackend(None, HS, *cbs)
+    ev = qasr.BatchEvents(None, qasr.ON_ITEM(lambda user, i, r: None), qasr.SHOULD_STOP(lambda user: 0))
+    opts = qasr.BatchOptions(4, (ctypes.c_int32 * 2)(*EOS), 256, 4096)
+    st = qasr.lib.qasr_batch_decode_backend(ctypes.byref(be), seg, 1, ctypes.byref(opts), ctypes.byref(ev), res)
+    assert st == 0
+    assert fake.forks == [2**31 - 1]
+    assert (res[0].status, res[0].stop_reason, [toks[k] for k in range(res[0].n_tokens)]) == \
+        (0, qasr.STOP_EOS, [5, 6])
