@@ -33,7 +33,9 @@ qasr_status qasr_kernel_pack_weights(int device, void* stream, int weight_format
  * out[r, m] = f16(f32(out[r, m]) + sum_k ...)         (accumulate != 0)
  * W: [n_out, k] f16 (weight_format QASR_WEIGHTS_F16) or int8 + a per-row scale, f16
  * (QASR_WEIGHTS_INT8) or f32 (QASR_WEIGHTS_INT8_F32), value f16(f32(q) * s), in the
- * layout qasr_kernel_pack_weights produces.  n_out % 128 == 0; k % 128 == 0.
+ * layout qasr_kernel_pack_weights produces.  n_out % 128 == 0; k % 128 == 0; x is
+ * [rows, ldx] and out [rows, ldo] f16 with ldx >= k, ldo >= n_out (ldx * 2 a multiple of
+ * 16 bytes, the activation copy's stride).
  * Replaces gemv / gemv_w8 / gemv_batch_slots / prefill_gemm(_w8)
  * (src/shaders.rs:273-889, 2995-3082). */
 qasr_status qasr_kernel_gemm(int device, void* stream, int weight_format, const void* w,
@@ -58,6 +60,8 @@ qasr_status qasr_kernel_gemm_traced(int device, void* stream, int weight_format,
  * ((d/8) ^ (p%8))*8 + d%8 (16-byte chunks permuted by the position's low 3 bits, so
  * tensor-core fragment loads from shared memory are bank-conflict free); page_table:
  * [slots][max_pages] int32; row r attends positions 0..row_pos[r] of slot row_slot[r].
+ * The device arrays are taken as given (the call checks only its scalar arguments):
+ * row_pos[r] < max_pages * 64, and every page id the rows reach lies in kv_pool.
  * Only enqueues (for timing with the caller's events): a bounded device-side wait that
  * gives up is not reported by this call; the traced and no-alloc variants report it. */
 qasr_status qasr_kernel_attention(int device, void* stream, const uint16_t* q, int q_ld,

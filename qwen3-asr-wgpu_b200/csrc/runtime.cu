@@ -1416,7 +1416,8 @@ qasr_status qasr_kernel_gemm_traced(int device, void* stream, int weight_format,
   static ProbeWs pws[16];
   std::lock_guard<std::mutex> lock(mu);
   std::string e;
-  if (device < 0 || device >= 16 || !w || !x || !out || rows <= 0 || n_out % 128 || k % 128 ||
+  if (device < 0 || device >= 16 || !w || !x || !out || rows <= 0 || n_out <= 0 || k <= 0 || n_out % 128 ||
+      k % 128 || ldx < k || ldo < n_out ||
       (weight_format != QASR_WEIGHTS_F16 && weight_format != QASR_WEIGHTS_INT8 &&
        weight_format != QASR_WEIGHTS_INT8_F32) ||
       (weight_format != QASR_WEIGHTS_F16 && !scale))
@@ -1490,7 +1491,7 @@ static qasr_status attention_probe(int device, void* stream, const uint16_t* q, 
   static uint32_t* status_words[16] = {};
   std::lock_guard<std::mutex> lock(mu);
   if (device < 0 || device >= 16 || !q || !out || !kv_pool || !page_table || !row_slot || !row_pos ||
-      rows <= 0 || nkv <= 0 || q_ld != 2 * nkv * 128 || layer < 0 || layer >= layers)
+      rows <= 0 || nkv <= 0 || q_ld != 2 * nkv * 128 || layer < 0 || layer >= layers || max_pages <= 0)
     return probe_err(err, errlen, QASR_ERR_INVALID_ARG, "bad attention probe arguments");
   if (cudaSetDevice(device) != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, "cudaSetDevice");
   const int max_chunks = ATTN_ROW_CHUNKS;
@@ -1617,7 +1618,8 @@ extern "C" qasr_status qasr_kernel_attention_noalloc(int device, void* stream, c
                                                      const int* row_pos, int rows, char* err,
                                                      int errlen) {
   if (device < 0 || device >= kMaxDevices || !q || !out || !kv_pool || !page_table || !row_slot ||
-      !row_pos || rows <= 0 || nkv <= 0 || q_ld != 2 * nkv * 128 || layer < 0 || layer >= layers)
+      !row_pos || rows <= 0 || nkv <= 0 || q_ld != 2 * nkv * 128 || layer < 0 || layer >= layers ||
+      max_pages <= 0)
     return probe_err(err, errlen, QASR_ERR_INVALID_ARG, "bad attention arguments");
   if (rows > NOALLOC_MAX_ROWS || nkv > NOALLOC_MAX_KV)
     return probe_err(err, errlen, QASR_ERR_CAPACITY,
@@ -1716,7 +1718,7 @@ extern "C" qasr_status qasr_kernel_kv_append(int device, void* stream, const uin
                                              int nkv, int layer, const int* row_slot,
                                              const int* row_pos, int rows, char* err, int errlen) {
   if (!k || !v || !kv_pool || !page_table || !row_slot || !row_pos || rows <= 0 || nkv <= 0 ||
-      layer < 0 || layer >= layers)
+      layer < 0 || layer >= layers || max_pages <= 0)
     return probe_err(err, errlen, QASR_ERR_INVALID_ARG, "bad kv append arguments");
   if (cudaSetDevice(device) != cudaSuccess) return probe_err(err, errlen, QASR_ERR_DEVICE, "cudaSetDevice");
   KvLayout kv{reinterpret_cast<__half*>(kv_pool), page_table, max_pages, layers, nkv};
