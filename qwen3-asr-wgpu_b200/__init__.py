@@ -325,6 +325,32 @@ def _rows(hidden, width: int) -> np.ndarray:
     return h
 
 
+def _sized(name: str, a, count: int, itemsize: int) -> np.ndarray:
+    """A host array the C ABI reads as `count` values of `itemsize` bytes: any other size is
+    refused here rather than read past."""
+    a = np.ascontiguousarray(a)
+    if a.size != count or a.itemsize != itemsize:
+        raise ValueError(f"{name}: {a.size} values of {a.itemsize} bytes, needs {count} of {itemsize}")
+    return a
+
+
+def layer_sizes(cfg: dict, weight_format: int) -> dict:
+    """Values and bytes per value of each qasr_layer_weights field (qasr_load_layer) for a
+    text config and weight format: [out, in] linears, per-row scales, norm gains."""
+    hs, inter, hd = cfg["hidden_size"], cfg["intermediate_size"], cfg["head_dim"]
+    qd, kvd = cfg["num_attention_heads"] * hd, cfg["num_key_value_heads"] * hd
+    dims = {"q": (qd, hs), "k": (kvd, hs), "v": (kvd, hs), "o": (hs, qd), "gate": (inter, hs),
+            "up": (inter, hs), "down": (hs, inter)}
+    wb = 2 if weight_format == WEIGHTS_F16 else 1
+    sb = 4 if weight_format == WEIGHTS_INT8_F32 else 2
+    out = {}
+    for p, (n, k) in dims.items():
+        out[f"{p}_proj"] = (n * k, wb)
+        out[f"{p}_scale"] = (n, sb)
+    out.update(input_layernorm=(hs, 2), post_attention_layernorm=(hs, 2), q_norm=(hd, 2), k_norm=(hd, 2))
+    return out
+
+
 def _ptr(a: np.ndarray | None):
     if a is None:
         return None
@@ -396,7 +422,11 @@ class TextDecoder:
 
     # ---------------------------------------------------------------- loading
     def load_embed(self, embed: np.ndarray, final_norm: np.ndarray):
+        hs = self.cfg["hidden_size"]
+        embed = _sized("embed", embed, self.cfg["vocab_size"] * hs, 2)
+        final_norm = _sized("final_norm", final_norm, hs, 2)
         self._check(lib.qasr_load_embed(self._ctx, _ptr(embed), _ptr(final_norm)))
+
 
     def load_layer(self, layer: int, w: dict):
         """w: HF-named arrays (q_proj ... down_proj, *_scale for INT8, norms).  Scales are
@@ -404,13 +434,16 @@ class TextDecoder:
         lw = LayerWeights()
         keep = []
         want = {WEIGHTS_INT8: np.uint16, WEIGHTS_INT8_F32: np.float32}.get(self.weight_format)
+        sizes = layer_sizes(self.cfg, self.weight_format)
         for name, _ in LayerWeights._fields_:
             a = w.get(name)
             if a is not None:
-                if name.endswith("_scale") and want is not None and np.asarray(a).dtype != want:
+                if name.endswith("_scale") and want is None:
+                    continue  # f16 weights: the library ignores the scale fields
+                if name.endswith("_scale") and np.asarray(a).dtype != want:
                     raise ValueError(f"{name}: {np.asarray(a).dtype} scales for weight format "
                                      f"{self.weight_format} (needs {np.dtype(want).name})")
-                a = np.ascontiguousarray(a)
+                a = _sized(name, a, *sizes[name])
                 keep.append(a)
                 setattr(lw, name, a.ctypes.data)
         self._check(lib.qasr_load_layer(self._ctx, layer, ctypes.byref(lw)))
@@ -432,7 +465,10 @@ class TextDecoder:
                                                scale_f32=self.weight_format == WEIGHTS_INT8_F32))
 
     def set_rope_tables(self, cos: np.ndarray, sin: np.ndarray):
-        positions = cos.shape[0]
+        """f16 bits [positions, head_dim] each (qasr_build_rope_tables)."""
+        positions = int(np.shape(cos)[0])
+        n = positions * self.cfg["head_dim"]
+        cos, sin = _sized("cos", cos, n, 2), _sized("sin", sin, n, 2)
         self._check(lib.qasr_set_rope_tables(self._ctx, _ptr(cos), _ptr(sin), positions))
 
     @property

@@ -68,3 +68,24 @@ def test_kv_page_swizzle_is_an_involution(qasr):
     for p, d in [(0, 0), (1, 0), (7, 127), (9, 13), (63, 64)]:
         col = (((d // 8) ^ (p % 8)) * 8) + d % 8
         assert sw[1, 0, 1, 2, p, col] == pool[1, 0, 1, 2, p, d]
+
+
+@pytest.mark.parametrize("preset", ["0.6b", "1.7b"])
+@pytest.mark.parametrize("fmt", ["f16", "int8", "int8_f32"])
+def test_layer_sizes_match_the_loader_inputs(qasr, preset, fmt):
+    """qasr_load_layer reads each field as `count` values of `itemsize` bytes; the Python
+    mirror refuses arrays of another size (layer_sizes).  The synthetic layers the tests and
+    the bench load — and the rope tables — have exactly those sizes in every format."""
+    cfg = qasr.text_config(preset, num_hidden_layers=1, vocab_size=1024)
+    wf = {"f16": qasr.WEIGHTS_F16, "int8": qasr.WEIGHTS_INT8, "int8_f32": qasr.WEIGHTS_INT8_F32}[fmt]
+    sizes = qasr.layer_sizes(cfg, wf)
+    layer = qasr.SyntheticModel(cfg, seed=3).layer(0, int8=fmt != "f16", scale_f32=fmt == "int8_f32")
+    for name, a in layer.items():
+        if name.endswith("_scale") and fmt == "f16":
+            continue
+        assert (a.size, a.itemsize) == sizes[name], name
+    assert {n for n in sizes if fmt != "f16" or not n.endswith("_scale")} == set(layer)
+    with pytest.raises(ValueError, match="q_proj"):
+        qasr._sized("q_proj", layer["q_proj"][:-1], *sizes["q_proj"])
+    cos, sin = qasr.build_rope_tables(64)
+    assert cos.shape == sin.shape == (64, cfg["head_dim"]) and cos.itemsize == 2
