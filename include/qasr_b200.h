@@ -344,7 +344,8 @@ qasr_status qasr_batch_decode_backend(const qasr_decode_backend* backend, const 
  * (CHUNK_MAX_NEW) on a non-final round, max_run 12 (MAX_REPEAT_RUN), eos {151643, 151645}.
  * Text assembly, rollback and the tokenizer stay with the caller.  Between rounds the
  * slot belongs to the session: prefilling, stepping, rolling back or freeing it through
- * other calls voids the reuse, which assumes its cached rows are the previous round's. */
+ * other calls voids the reuse, which assumes its cached rows are the previous round's.
+ * A session borrows its context: destroy it before the context. */
 typedef struct qasr_session qasr_session;
 qasr_status qasr_session_create(qasr_ctx* ctx, int slot, int kv_reuse, qasr_session** out);
 void qasr_session_destroy(qasr_session* session);

@@ -110,6 +110,8 @@ class Session:
     def round(self, hidden: np.ndarray, budget: int = CHUNK_MAX_NEW, eos=(ENDOFTEXT_TOKEN_ID, IM_END_TOKEN_ID),
               prev_tokens=(), max_run: int = MAX_REPEAT_RUN):
         """Returns (tokens, dropped, hit_eos, reused_rows)."""
+        if not self._h or not self._dec._ctx:
+            raise DecoderError(7, "session or its decoder is closed")  # QASR_ERR_STATE
         hidden = _rows(hidden, self._dec.cfg["hidden_size"])
         e = np.ascontiguousarray(eos, dtype=np.int32)
         pv = np.ascontiguousarray(prev_tokens, dtype=np.uint32)

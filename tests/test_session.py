@@ -42,3 +42,22 @@ def test_suppress_prev_run_counted_back_up_to_the_cap(qasr):
     assert qasr.suppress_runs([5] * 30, [5, 6], 12) == ([6], 1)
     assert qasr.suppress_runs([1, 5, 5], [5] * 12, 12) == ([5] * 10, 2)
     assert qasr.suppress_runs([], [], 12) == ([], 0)
+
+
+def test_a_round_on_a_closed_decoder_is_refused_on_the_host(qasr):
+    """A session borrows its decoder's context: once the decoder is closed the mirror
+    refuses the round (QASR_ERR_STATE) instead of handing the library a freed context.
+    A stand-in decoder with a closed (null) context is enough, no GPU."""
+    import ctypes
+    import pytest
+
+    class Closed:
+        _ctx = ctypes.c_void_p()
+        cfg = {"hidden_size": 4}
+
+    s = object.__new__(qasr.Session)
+    s._dec, s._h = Closed(), ctypes.c_void_p(1)  # never passed to the library
+    with pytest.raises(qasr.DecoderError) as e:
+        s.round(np.zeros((2, 4), np.uint16))
+    assert e.value.status == 7
+    s._h = None
