@@ -843,7 +843,7 @@ def kv_page_swizzle(pool: np.ndarray) -> np.ndarray:
 
 
 from .audio import (AUDIO_PRESETS, AudioEncoder, SyntheticAudioTower, audio_config,  # noqa: E402,F401
-                    conv_geometry, read_audio_config, synthetic_mel)
+                    audio_weight_sizes, conv_geometry, read_audio_config, synthetic_mel)
 from .audio import token_count as audio_token_count  # noqa: E402,F401
 
 

@@ -116,6 +116,27 @@ def conv_geometry(cfg: dict):
     return w3, (h1, w1), (h2, w2), (h3, w3)
 
 
+def audio_weight_sizes(cfg: dict) -> dict:
+    """Values each tower weight holds, by checkpoint name: qasr_audio_load_weights reads that
+    many behind each pointer (f16 matrices, f32 biases and LayerNorm parameters)."""
+    d, C, ffn, out = cfg["d_model"], cfg["downsample_hidden_size"], cfg["encoder_ffn_dim"], cfg["output_dim"]
+    h3 = conv_geometry(cfg)[3][0]
+    n = {"conv2d1.weight": C * 9, "conv2d1.bias": C, "conv2d2.weight": C * C * 9, "conv2d2.bias": C,
+         "conv2d3.weight": C * C * 9, "conv2d3.bias": C, "conv_out.weight": d * C * h3, "conv_out.bias": d,
+         "ln_post.weight": d, "ln_post.bias": d, "proj1.weight": d * d, "proj1.bias": d,
+         "proj2.weight": out * d, "proj2.bias": out}
+    for i in range(cfg["encoder_layers"]):
+        p = f"layers.{i}."
+        for lin in ("q_proj", "k_proj", "v_proj", "out_proj"):
+            n[p + f"self_attn.{lin}.weight"] = d * d
+            n[p + f"self_attn.{lin}.bias"] = d
+        for ln in ("self_attn_layer_norm", "final_layer_norm"):
+            n[p + ln + ".weight"] = d
+            n[p + ln + ".bias"] = d
+        n.update({p + "fc1.weight": ffn * d, p + "fc1.bias": ffn, p + "fc2.weight": d * ffn, p + "fc2.bias": d})
+    return n
+
+
 class SyntheticAudioTower:
     """Seeded tower weights with the checkpoint's names and shapes (f16 matrices as uint16
     bits, f32 biases and LayerNorm parameters).  conv_out and k_proj carry no bias, as in
@@ -223,6 +244,7 @@ class AudioEncoder:
     def load(self, tensors: dict):
         """Weights by checkpoint name (relative to the tower's prefix)."""
         keep = []
+        sizes = audio_weight_sizes(self.cfg)
 
         def arr(name, dtype, required=True):
             a = tensors.get(name)
@@ -230,7 +252,12 @@ class AudioEncoder:
                 if required:
                     raise KeyError(name)
                 return None
+            a = np.asarray(a)
+            if dtype == np.uint16 and a.dtype == np.float16:
+                a = a.view(np.uint16)  # f16 matrices travel as their bits
             a = np.ascontiguousarray(a, dtype=dtype)
+            if a.size != sizes[name]:
+                raise ValueError(f"{name}: {a.size} values, the tower reads {sizes[name]}")
             keep.append(a)
             return _ptr(a)
 
@@ -282,6 +309,9 @@ class AudioEncoder:
     def encode_batch(self, mels) -> list:
         """Several utterances, one transformer pass (GpuAudioEncoder::encode_batch)."""
         mels = [np.ascontiguousarray(m, dtype=np.float32) for m in mels]
+        for i, m in enumerate(mels):  # the library reads num_mel_bins x n_frames behind each
+            if m.ndim != 2 or m.shape[0] != self.cfg["num_mel_bins"]:
+                raise ValueError(f"mel {i}: shape {m.shape}, needs [{self.cfg['num_mel_bins']}, n_frames]")
         outs = [np.zeros((max(1, self.token_count(m.shape[1])), self.cfg["output_dim"]), np.float16) for m in mels]
         mp = (ctypes.c_void_p * len(mels))(*[m.ctypes.data for m in mels])
         op = (ctypes.c_void_p * len(mels))(*[o.ctypes.data for o in outs])

@@ -256,3 +256,17 @@ def test_read_audio_config_errors(qasr, tmp_path, obj, needle):
     with pytest.raises(qasr.DecoderError) as e:
         qasr.read_audio_config(d)
     assert e.value.status == 1 and needle in str(e.value)
+
+
+@pytest.mark.parametrize("preset", ["0.6b", "1.7b"])
+def test_tower_weight_sizes_match_the_synthetic_tower(qasr, preset):
+    """AudioEncoder.load refuses a weight whose size is not what qasr_audio_load_weights
+    reads (audio_weight_sizes); the synthetic tower the tests and the bench load has
+    exactly those sizes (its k_proj carries no bias, as in the checkpoints)."""
+    cfg = qasr.audio_config(preset, encoder_layers=2)
+    sizes = qasr.audio_weight_sizes(cfg)
+    t = qasr.SyntheticAudioTower(cfg, seed=5).tensors
+    assert set(t) <= set(sizes)
+    assert set(sizes) - set(t) == {f"layers.{i}.self_attn.k_proj.bias" for i in range(2)} | {"conv_out.bias"}
+    for name, a in t.items():
+        assert a.size == sizes[name], name
