@@ -165,6 +165,8 @@ def test_failed_attempt_keeps_finished_items(qasr):
 
 
 def test_should_stop_cancels_the_unfinished(qasr):
+    """Outcomes (src/inference.rs:2727-2736): stopping charges the remaining items
+    QASR_ERR_CANCELLED and keeps the finished ones."""
     scripts = [[1, EOS[0]], [2] * 20, [3] * 20]
     polls = {"n": 0}
 
@@ -247,6 +249,7 @@ def test_random_workloads_match_the_restated_control_flow(qasr):
                                         on_item=lambda i, r: seen.append(i))
         want = _py_scheduler(scripts, lens, max_new, width, max_live, cap)
         check(res, want)
+        # each item reported exactly once (src/inference.rs:2715-2724)
         assert sorted(seen) == list(range(n)), (case, seen)
         assert not fake.live, case  # every slot freed
 
@@ -304,3 +307,44 @@ def test_capacity_of_a_huge_budget_does_not_wrap(qasr):
     assert fake.forks == [2**31 - 1]
     assert (res[0].status, res[0].stop_reason, [toks[k] for k in range(res[0].n_tokens)]) == \
         (0, qasr.STOP_EOS, [5, 6])
+
+
+class FailPrefill(Fake):
+    """The scripted decoder, with the prefill of one segment failing with its own status."""
+
+    def __init__(self, scripts, bad_seg, status=1, **kw):
+        super().__init__(scripts, **kw)
+        self.bad_seg, self.status = bad_seg, status
+
+    def prefill_batch(self, slots, hiddens):
+        from qasr_b200 import DecoderError
+        if any(int(h[0, 0]) == self.bad_seg for h in hiddens):
+            raise DecoderError(self.status, "unsupported input")
+        return super().prefill_batch(slots, hiddens)
+
+
+def test_one_failure_does_not_drop_the_others(qasr):
+    """Outcomes (src/inference.rs:2681-2700): the failing item keeps its own error, the
+    items around it their results, each reported once in order."""
+    scripts = [[1, 2, EOS[0]], [3, 4, EOS[0]], [5, EOS[1]]]
+    seen = []
+    fake = FailPrefill(scripts, bad_seg=1)
+    res = qasr.batch_decode_backend(fake, segs([4, 4, 4], [5, 5, 5]), width=1,
+                                    on_item=lambda i, r: seen.append((i, r["status"] == 0)))
+    assert [r["status"] for r in res] == [0, 1, 0]
+    assert res[0]["tokens"] == [1, 2] and res[2]["tokens"] == [5]
+    assert res[1]["tokens"] == []
+    assert seen == [(0, True), (1, False), (2, True)]
+    assert not fake.live  # the failed item's slot is freed too
+
+
+def test_an_unfinished_item_is_reported_as_not_decoded_last(qasr):
+    """Outcomes::finish (src/inference.rs:2703-2712): an item the batch never finished is
+    an error (QASR_ERR_NOT_DECODED), reported after the finished ones.  A batched segment
+    whose first token is an eos id is such an item."""
+    scripts = [[7, 8, EOS[0]], [EOS[0]]]
+    seen = []
+    res = qasr.batch_decode_backend(Fake(scripts), segs([5, 4], [4, 4]), width=2,
+                                    on_item=lambda i, r: seen.append((i, r["status"])))
+    assert [r["status"] for r in res] == [0, 8]
+    assert seen == [(0, 0), (1, 8)]
