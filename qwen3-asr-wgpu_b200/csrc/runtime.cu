@@ -839,6 +839,12 @@ qasr_status qasr_create(const qasr_text_config* cfg, const qasr_options* opts, i
     return bad("weight_format must be QASR_WEIGHTS_F16, QASR_WEIGHTS_INT8 or QASR_WEIGHTS_INT8_F32");
   if (opts->max_slots <= 0 || opts->max_slots > 4096 || opts->max_seq <= 0)
     return bad("max_slots must be 1..4096 and max_seq positive");
+  {  // page-table entries and page ids are 32-bit: their counts, in 64-bit, must fit
+    const long long mp = (static_cast<long long>(opts->max_seq) + QASR_PAGE_POSITIONS - 1) / QASR_PAGE_POSITIONS;
+    const long long table = static_cast<long long>(opts->max_slots) * mp;
+    if (opts->kv_pages < 0 || table > INT32_MAX)
+      return bad("max_slots x max_seq / 64 pages must fit 32-bit page indices; kv_pages must not be negative");
+  }
   if (c->opts.max_prefill_rows <= 0) c->opts.max_prefill_rows = 2048;
   c->opts.max_prefill_rows = std::min(c->opts.max_prefill_rows, ATTN_MAX_ROWS);
   *out = c;

@@ -57,6 +57,11 @@ def test_create_rejects_bad_options(qasr):
     with pytest.raises(qasr.DecoderError) as e:
         qasr.TextDecoder(cfg, max_slots=0)
     assert "max_slots" in str(e.value)
+    # 64 slots x (2^31 - 1) positions: 2^31 page-table entries, refused before any
+    # allocation instead of wrapping the 32-bit page count
+    with pytest.raises(qasr.DecoderError) as e:
+        qasr.TextDecoder(cfg, max_slots=64, max_seq=2**31 - 1)
+    assert e.value.status == 1 and "32-bit page indices" in str(e.value)
 
 
 def test_kv_page_swizzle_is_an_involution(qasr):
