@@ -26,6 +26,7 @@
 #include <string>
 #include <vector>
 
+#include "abi_guard.h"
 #include "audio_kernels.cuh"
 #include "f16_host.h"
 #include "gemm_tc.cuh"
@@ -732,7 +733,7 @@ qasr_status qasr_audio_load_weights(qasr_audio_ctx* c, const qasr_audio_weights*
   return QASR_OK;
 }
 
-qasr_status qasr_audio_load_checkpoint(qasr_audio_ctx* c, qasr_checkpoint* ck, const char* prefix_c) {
+static qasr_status audio_load_checkpoint_body(qasr_audio_ctx* c, qasr_checkpoint* ck, const char* prefix_c) {
   if (!c || !ck) return QASR_ERR_INVALID_ARG;
   const std::string pre = std::string(prefix_c ? prefix_c : "thinker.audio_tower") + ".";
   const qasr_audio_config& g = c->cfg;
@@ -838,8 +839,8 @@ qasr_status qasr_audio_sync(qasr_audio_ctx* c) {
   return check_device_status(c);
 }
 
-qasr_status qasr_audio_encode_batch(qasr_audio_ctx* c, int32_t n, const float* const* mels,
-                                    const int32_t* n_frames, int32_t n_mels, uint16_t* const* outs) {
+static qasr_status audio_encode_batch_body(qasr_audio_ctx* c, int32_t n, const float* const* mels,
+                                          const int32_t* n_frames, int32_t n_mels, uint16_t* const* outs) {
   if (!c || n <= 0 || !mels || !n_frames || !outs) return QASR_ERR_INVALID_ARG;
   qasr_status s = begin(c);
   if (s) return s;
@@ -874,6 +875,19 @@ qasr_status qasr_audio_encode_batch(qasr_audio_ctx* c, int32_t n, const float* c
         "embedding read");
   }
   return check_device_status(c);
+}
+
+// Behind the guard that keeps C++ exceptions (a failed host allocation, most of all)
+// inside the library: the two entry points whose host buffers follow the input.
+qasr_status qasr_audio_load_checkpoint(qasr_audio_ctx* c, qasr_checkpoint* ck, const char* prefix_c) {
+  return qasr::guard([&] { return audio_load_checkpoint_body(c, ck, prefix_c); },
+                     [&](qasr_status s, const std::string& m) { return c ? afail(c, s, "%s", m.c_str()) : s; });
+}
+
+qasr_status qasr_audio_encode_batch(qasr_audio_ctx* c, int32_t n, const float* const* mels,
+                                    const int32_t* n_frames, int32_t n_mels, uint16_t* const* outs) {
+  return qasr::guard([&] { return audio_encode_batch_body(c, n, mels, n_frames, n_mels, outs); },
+                     [&](qasr_status s, const std::string& m) { return c ? afail(c, s, "%s", m.c_str()) : s; });
 }
 
 qasr_status qasr_audio_encode(qasr_audio_ctx* c, const float* mel, int32_t n_mels, int32_t n_frames, uint16_t* out,

@@ -8,6 +8,7 @@
 #include <cstring>
 #include <vector>
 
+#include "abi_guard.h"
 #include "ctx_internal.h"
 #include "qasr_b200.h"
 
@@ -217,9 +218,9 @@ struct CtxBackend {
 
 extern "C" {
 
-qasr_status qasr_batch_decode_backend(const qasr_decode_backend* be, const qasr_segment* segs, int n,
-                                      const qasr_batch_options* opts, const qasr_batch_events* events,
-                                      qasr_item_result* results) {
+static qasr_status batch_decode_body(const qasr_decode_backend* be, const qasr_segment* segs, int n,
+                                     const qasr_batch_options* opts, const qasr_batch_events* events,
+                                     qasr_item_result* results) {
   if (!be || !be->fork_capped || !be->slot_free || !be->prefill_batch || !be->step_batch || be->hidden_size <= 0 ||
       !opts || n < 0 || (n > 0 && (!segs || !results)) || opts->kv_step <= 0 || opts->batch_seq_cap <= 0)
     return QASR_ERR_INVALID_ARG;
@@ -260,6 +261,14 @@ qasr_status qasr_batch_decode_backend(const qasr_decode_backend* be, const qasr_
   for (int i = 0; i < n; ++i)  // Outcomes::finish: the rest were not decoded
     if (!r.emitted[static_cast<size_t>(i)]) r.done(i, QASR_ERR_NOT_DECODED, QASR_STOP_MAX_TOKENS, {});
   return QASR_OK;
+}
+
+qasr_status qasr_batch_decode_backend(const qasr_decode_backend* be, const qasr_segment* segs, int n,
+                                      const qasr_batch_options* opts, const qasr_batch_events* events,
+                                      qasr_item_result* results) {
+  // no context to hold a message here: the status alone reports a host failure
+  return qasr::guard([&] { return batch_decode_body(be, segs, n, opts, events, results); },
+                     [](qasr_status s, const std::string&) { return s; });
 }
 
 qasr_status qasr_batch_decode(qasr_ctx* ctx, const qasr_segment* segs, int n, const qasr_batch_options* opts,

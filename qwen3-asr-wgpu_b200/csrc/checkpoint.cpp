@@ -20,11 +20,13 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <memory>
 #include <string>
 #include <unordered_map>
 #include <utility>
 #include <vector>
 
+#include "abi_guard.h"
 #include "ctx_internal.h"
 #include "f16_host.h"
 #include "qasr_b200.h"
@@ -530,7 +532,7 @@ struct qasr_checkpoint {
 
 extern "C" {
 
-qasr_status qasr_read_model_config(const char* model_dir, qasr_model_config* out, char* err, int errlen) {
+static qasr_status read_model_config_body(const char* model_dir, qasr_model_config* out, char* err, int errlen) {
   if (!model_dir || !out) {
     set_err(err, errlen, "null argument");
     return QASR_ERR_INVALID_ARG;
@@ -619,7 +621,7 @@ qasr_status qasr_read_model_config(const char* model_dir, qasr_model_config* out
   return QASR_OK;
 }
 
-qasr_status qasr_read_audio_config(const char* model_dir, qasr_audio_config* out, char* err, int errlen) {
+static qasr_status read_audio_config_body(const char* model_dir, qasr_audio_config* out, char* err, int errlen) {
   if (!model_dir || !out) {
     set_err(err, errlen, "null argument");
     return QASR_ERR_INVALID_ARG;
@@ -684,13 +686,13 @@ qasr_status qasr_read_audio_config(const char* model_dir, qasr_audio_config* out
   return QASR_OK;
 }
 
-qasr_status qasr_checkpoint_open(const char* model_dir, qasr_checkpoint** out, char* err, int errlen) {
+static qasr_status checkpoint_open_body(const char* model_dir, qasr_checkpoint** out, char* err, int errlen) {
   if (!model_dir || !out) {
     set_err(err, errlen, "null argument");
     return QASR_ERR_INVALID_ARG;
   }
   *out = nullptr;
-  qasr_checkpoint* ck = new (std::nothrow) qasr_checkpoint();
+  std::unique_ptr<qasr_checkpoint> ck(new (std::nothrow) qasr_checkpoint());  // freed on every early exit
   if (!ck) {
     set_err(err, errlen, "out of host memory");
     return QASR_ERR_OOM;
@@ -698,10 +700,9 @@ qasr_status qasr_checkpoint_open(const char* model_dir, qasr_checkpoint** out, c
   const qasr_status s = ck->open_dir(model_dir);
   if (s) {
     set_err(err, errlen, ck->err);
-    delete ck;
     return s;
   }
-  *out = ck;
+  *out = ck.release();
   return QASR_OK;
 }
 
@@ -733,7 +734,7 @@ qasr_status qasr_checkpoint_weight_format(qasr_checkpoint* ck, const char* prefi
   return QASR_OK;
 }
 
-qasr_status qasr_checkpoint_read_f16(qasr_checkpoint* ck, const char* name, uint16_t* out, int64_t count) {
+static qasr_status checkpoint_read_f16_body(qasr_checkpoint* ck, const char* name, uint16_t* out, int64_t count) {
   if (!ck || !name || !out) return QASR_ERR_INVALID_ARG;
   const Tensor* t = ck->find(name);
   if (!t) return ck->fail(QASR_ERR_INVALID_ARG, std::string("weight not found: ") + name);
@@ -785,7 +786,7 @@ qasr_status qasr_checkpoint_rows_f16(qasr_checkpoint* ck, const char* name, cons
   return QASR_OK;
 }
 
-qasr_status qasr_load_checkpoint(qasr_ctx* ctx, qasr_checkpoint* ck, const char* prefix_c) {
+static qasr_status load_checkpoint_body(qasr_ctx* ctx, qasr_checkpoint* ck, const char* prefix_c) {
   if (!ctx || !ck) return QASR_ERR_INVALID_ARG;
   qasr_text_config cfg{};
   int fmt = 0;
@@ -871,6 +872,33 @@ qasr_status qasr_load_checkpoint(qasr_ctx* ctx, qasr_checkpoint* ck, const char*
     if ((s = qasr_load_layer(ctx, l, &w))) return s;
   }
   return QASR_OK;
+}
+
+// The entry points above whose host buffers follow a file's contents, behind the guard
+// that keeps C++ exceptions (a failed host allocation, most of all) inside the library.
+qasr_status qasr_read_model_config(const char* model_dir, qasr_model_config* out, char* err, int errlen) {
+  return qasr::guard([&] { return read_model_config_body(model_dir, out, err, errlen); },
+                     [&](qasr_status s, const std::string& m) { set_err(err, errlen, m); return s; });
+}
+
+qasr_status qasr_read_audio_config(const char* model_dir, qasr_audio_config* out, char* err, int errlen) {
+  return qasr::guard([&] { return read_audio_config_body(model_dir, out, err, errlen); },
+                     [&](qasr_status s, const std::string& m) { set_err(err, errlen, m); return s; });
+}
+
+qasr_status qasr_checkpoint_open(const char* model_dir, qasr_checkpoint** out, char* err, int errlen) {
+  return qasr::guard([&] { return checkpoint_open_body(model_dir, out, err, errlen); },
+                     [&](qasr_status s, const std::string& m) { set_err(err, errlen, m); return s; });
+}
+
+qasr_status qasr_checkpoint_read_f16(qasr_checkpoint* ck, const char* name, uint16_t* out, int64_t count) {
+  return qasr::guard([&] { return checkpoint_read_f16_body(ck, name, out, count); },
+                     [&](qasr_status s, const std::string& m) { return ck ? ck->fail(s, m) : s; });
+}
+
+qasr_status qasr_load_checkpoint(qasr_ctx* ctx, qasr_checkpoint* ck, const char* prefix_c) {
+  return qasr::guard([&] { return load_checkpoint_body(ctx, ck, prefix_c); },
+                     [&](qasr_status s, const std::string& m) { return qasr::ctx_fail(ctx, s, "checkpoint: " + m); });
 }
 
 }  // extern "C"

@@ -26,6 +26,7 @@
 #include "gemm_tc.cuh"
 #include "host_gemm.cuh"
 #include "qasr_b200.h"
+#include "abi_guard.h"
 #include "ctx_internal.h"
 #include "qasr_b200_kernels.h"
 #include "rows.cuh"
@@ -814,8 +815,8 @@ const char* qasr_last_error(const qasr_ctx* ctx) { return ctx ? ctx->err.c_str()
 
 uint64_t qasr_kernel_launch_count(void) { return g_launches.load(); }
 
-qasr_status qasr_create(const qasr_text_config* cfg, const qasr_options* opts, int device,
-                        qasr_ctx** out) {
+static qasr_status create_body(const qasr_text_config* cfg, const qasr_options* opts, int device,
+                               qasr_ctx** out) {
   if (!cfg || !opts || !out) return QASR_ERR_INVALID_ARG;
   *out = nullptr;
   auto* c = new qasr_ctx();
@@ -960,6 +961,13 @@ qasr_status qasr_create(const qasr_text_config* cfg, const qasr_options* opts, i
   CK(cudaMallocHost(&c->pinned_in, sizeof(int) * opts->max_slots * 2), "pinned alloc");
   CK(cudaEventCreateWithFlags(&c->ev_in, cudaEventDisableTiming), "event create");
   return QASR_OK;
+}
+
+qasr_status qasr_create(const qasr_text_config* cfg, const qasr_options* opts, int device,
+                        qasr_ctx** out) {
+  // a failure after the context exists is reported on it (the caller reads, then destroys)
+  return qasr::guard([&] { return create_body(cfg, opts, device, out); },
+                     [&](qasr_status s, const std::string& m) { return out && *out ? qasr::ctx_fail(*out, s, m) : s; });
 }
 
 void qasr_destroy(qasr_ctx* c) {
@@ -1255,8 +1263,8 @@ qasr_status qasr_step(qasr_ctx* c, int slot, int32_t* token) {
   return qasr_step_batch(c, &slot, 1, token);
 }
 
-qasr_status qasr_prefill_batch(qasr_ctx* c, const int* slots, int n, const uint16_t* hidden,
-                               const int* lens, const int* kv_starts, int32_t* first_tokens) {
+static qasr_status prefill_batch_body(qasr_ctx* c, const int* slots, int n, const uint16_t* hidden,
+                                      const int* lens, const int* kv_starts, int32_t* first_tokens) {
   if (!c || !slots || !hidden || !lens || n <= 0 || !first_tokens)
     return fail(c, QASR_ERR_INVALID_ARG, "bad prefill arguments");
   qasr_status s = ready(c);
@@ -1333,6 +1341,12 @@ qasr_status qasr_prefill_batch(qasr_ctx* c, const int* slots, int n, const uint1
   for (int i = 0; i < n; ++i) c->slots[slots[i]].pos = (kv_starts ? kv_starts[i] : 0) + lens[i];
   c->last_logit_rows = n;
   return QASR_OK;
+}
+
+qasr_status qasr_prefill_batch(qasr_ctx* c, const int* slots, int n, const uint16_t* hidden,
+                               const int* lens, const int* kv_starts, int32_t* first_tokens) {
+  return qasr::guard([&] { return prefill_batch_body(c, slots, n, hidden, lens, kv_starts, first_tokens); },
+                     [&](qasr_status s, const std::string& m) { return qasr::ctx_fail(c, s, m); });
 }
 
 qasr_status qasr_prefill(qasr_ctx* c, int slot, const uint16_t* hidden, int s, int kv_start,

@@ -12,6 +12,7 @@
 #include <string>
 #include <vector>
 
+#include "abi_guard.h"
 #include "ctx_internal.h"
 #include "qasr_b200.h"
 
@@ -96,9 +97,10 @@ void qasr_session_reset(qasr_session* s) {
   if (s) s->prev.clear();
 }
 
-qasr_status qasr_session_round(qasr_session* s, const uint16_t* hidden, int rows, int budget, const int32_t* eos,
-                               int n_eos, const uint32_t* prev_tokens, int n_prev, int max_run, int32_t* tokens,
-                               int* n_tokens, int* dropped, int* hit_eos, int* reused_rows) {
+static qasr_status session_round_body(qasr_session* s, const uint16_t* hidden, int rows, int budget,
+                                      const int32_t* eos, int n_eos, const uint32_t* prev_tokens, int n_prev,
+                                      int max_run, int32_t* tokens, int* n_tokens, int* dropped, int* hit_eos,
+                                      int* reused_rows) {
   if (!s || !hidden || rows <= 0 || budget <= 0 || (n_eos > 0 && !eos) || n_eos < 0 || max_run <= 0 || !tokens ||
       !n_tokens || !dropped || !hit_eos || !reused_rows || n_prev < 0 || (n_prev > 0 && !prev_tokens))
     return QASR_ERR_INVALID_ARG;
@@ -148,6 +150,20 @@ qasr_status qasr_session_round(qasr_session* s, const uint16_t* hidden, int rows
   for (int i = 0; i < kept; ++i) tokens[i] = static_cast<int32_t>(out[i]);
   *n_tokens = kept;
   return QASR_OK;
+}
+
+qasr_status qasr_session_round(qasr_session* s, const uint16_t* hidden, int rows, int budget, const int32_t* eos,
+                               int n_eos, const uint32_t* prev_tokens, int n_prev, int max_run, int32_t* tokens,
+                               int* n_tokens, int* dropped, int* hit_eos, int* reused_rows) {
+  return qasr::guard(
+      [&] {
+        return session_round_body(s, hidden, rows, budget, eos, n_eos, prev_tokens, n_prev, max_run, tokens,
+                                  n_tokens, dropped, hit_eos, reused_rows);
+      },
+      [&](qasr_status st, const std::string& m) {
+        if (s && s->kv_reuse) s->prev.clear();  // a round cut short leaves no reusable prefix
+        return s ? qasr::ctx_fail(s->ctx, st, m) : st;
+      });
 }
 
 }  // extern "C"
