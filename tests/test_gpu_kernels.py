@@ -134,6 +134,33 @@ def test_int8_f32_scale_dequant_bit_exact(qasr, cuda_device, oracle):
     np.testing.assert_array_equal(got, deq[:, cols].T)
 
 
+def test_w8_gemv_probe_bar(qasr, cuda_device, oracle):
+    """The reference's W8 GEMV probe (src/bin/w8_probe.rs:41-117) on the B200: its LCG
+    inputs (seed 0xDEB) with f32 row scales (QASR_WEIGHTS_INT8_F32) through the GEMM at
+    one row; worst relative error against the probe's f64 reference below 2e-3.  The GEMM
+    tiles 128 output rows, so the probe's 64 rows are followed by 64 zero rows."""
+    import torch
+    from w8_probe_inputs import K, REL_BAR, ROWS, probe_inputs, probe_reference, worst_rel
+    q, scale, x = probe_inputs()
+    n_out = 128
+    qp = np.zeros((n_out, K), np.int8)
+    qp[:ROWS] = q
+    sp = np.zeros(n_out, np.float32)
+    sp[:ROWS] = scale
+    qd = _pack(qasr, torch, qasr.WEIGHTS_INT8_F32, _dev(qp, torch), n_out, K)
+    sd, xd = _dev(sp, torch), _dev(x.reshape(1, K), torch)
+    out = torch.zeros((1, n_out), dtype=torch.int16, device="cuda")
+    qasr.kernel_gemm(0, 0, qasr.WEIGHTS_INT8_F32, qd.data_ptr(), sd.data_ptr(), n_out, K, xd.data_ptr(), K,
+                     1, out.data_ptr(), n_out, False)
+    torch.cuda.synchronize()
+    res = out.cpu().numpy().view(np.uint16)
+    got = res[0, :ROWS].view(np.float16).astype(np.float64)
+    assert not res[0, ROWS:].any()  # the zero rows stay zero
+    worst = worst_rel(got, probe_reference(oracle.dequant_i8(q, scale), x))
+    print(f"w8 probe on the B200 GEMM: worst rel {worst:.2e}")
+    assert worst < REL_BAR
+
+
 def _attention_case(qasr, torch, oracle, lens, seed, nkv=8, layers=2, layer=1):
     from qasr_b200 import synth
     rows = len(lens)

@@ -190,3 +190,19 @@ def test_oracle_side_inputs_equal_the_package_inputs(qasr):
     cb, sb = inputs.build_rope_tables(2048)
     np.testing.assert_array_equal(ca, cb)
     np.testing.assert_array_equal(sa, sb)
+
+
+def test_w8_gemv_probe_bar(oracle):
+    """The reference's W8 GEMV probe (src/bin/w8_probe.rs:41-117): its LCG inputs
+    (seed 0xDEB, int8 weights, f32 row scales, f16 activations), host dequant, then the
+    decode GEMV; worst relative error against the f64 reference below 2e-3.  Here the
+    oracle's 4-accumulator decode dot (src/cpu_decoder.rs:64-101) meets the probe's bar;
+    tests/test_gpu_kernels.py holds the B200 GEMM to it."""
+    from w8_probe_inputs import REL_BAR, probe_inputs, probe_reference, worst_rel
+    q, scale, x = probe_inputs()
+    assert q.min() == -128 and q.max() == 127  # the probe's draw covers the whole byte
+    wd = oracle.dequant_i8(q, scale)
+    got = oracle.gemv_f16(wd, x).view(np.float16).astype(np.float64)
+    worst = worst_rel(got, probe_reference(wd, x))
+    print(f"w8 probe inputs, oracle decode GEMV: worst rel {worst:.2e}")
+    assert worst < REL_BAR
